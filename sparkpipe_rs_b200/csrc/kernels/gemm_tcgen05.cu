@@ -1,0 +1,509 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+//   D[m, n] = sum_k A[m, k] * B[n, k]        (both operands K-major, fp32 accumulate)
+//
+// One kernel template covers every GEMM-shaped op of the MLA-MoE model:
+//   * MODE_DENSE   — persistent CTAs walk (m, n, batch) tiles; the TMEM
+//                    accumulator is double buffered so the epilogue of tile i
+//                    overlaps the main loop of tile i+1. Batched GEMMs (the
+//                    per-head MLA absorb products) offset A rows, A/B K columns
+//                    and D per batch index.
+//   * MODE_SPLITK  — decode-shaped GEMMs (few tokens, weight-bandwidth bound):
+//                    the K loop of one tile is split over the CTAs of a
+//                    thread-block cluster; partial accumulators are reduced
+//                    through distributed shared memory (no global workspace).
+//   * MODE_GROUPED — MoE expert GEMMs: group g (an expert) owns A rows
+//                    [g*M, g*M+M) and a device-side range of B rows (its sorted
+//                    tokens); tile counts come from device memory, so the launch
+//                    is CUDA-graph safe.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer + TMEM
+// owner, warps 2..5 = epilogue (TMEM lane quarter = warp % 4).
+// Operand tiles are 128-byte swizzled (64 bf16 of K per row); BLOCK_M = 128.
+//
+// The reference declares these products only as cuBLASLt "linear plans"
+// (crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_resident_decode_stage.h:599-622)
+// and the fused MoE entry points (same header :1046-1058); the math is written
+// here from scratch.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace sp {
+
+enum { MODE_DENSE = 0, MODE_SPLITK = 1, MODE_GROUPED = 2 };
+
+struct GemmKParams {
+  int M, N, K;
+  int batch;
+  int a_row0, a_batch_rows, a_k0, a_batch_k;
+  int b_row0, b_batch_rows, b_k0, b_batch_k;
+  void* D;
+  long long ldd;
+  long long d_batch_stride;
+  int trans_out;
+  int out_f32;
+  int m_tiles, n_tiles, num_tiles;
+  int splits;
+  const int* grp_rows;   // [G+1]
+  const int* grp_tiles;  // [G+1]
+  int num_groups;
+  int a_evict_first;
+  int* err;
+};
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int RED_LD = BN + 4;  // fp32 row pitch of the split-K reduce buffer
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+struct TileInfo {
+  int a_row, a_k, b_row, b_k;
+  int m_base, n_base;  // output coordinates of the tile origin
+  int m_valid, n_valid;
+  long long d_off;
+};
+
+template <int BN, int MODE>
+SP_DEVI bool get_tile(const GemmKParams& p, int t, TileInfo& ti) {
+  if (MODE == MODE_GROUPED) {
+    const int mt = t % p.m_tiles;
+    const int q = t / p.m_tiles;
+    // group = last g with grp_tiles[g] <= q
+    int lo = 0, hi = p.num_groups;  // grp_tiles[lo] <= q < grp_tiles[hi]
+    while (hi - lo > 1) {
+      int mid = (lo + hi) >> 1;
+      if (__ldg(p.grp_tiles + mid) <= q) lo = mid; else hi = mid;
+    }
+    const int g = lo;
+    const int nt = q - __ldg(p.grp_tiles + g);
+    const int r0 = __ldg(p.grp_rows + g);
+    const int r1 = __ldg(p.grp_rows + g + 1);
+    ti.a_row = p.a_row0 + g * p.a_batch_rows + mt * BM;
+    ti.a_k = p.a_k0;
+    ti.b_row = r0 + nt * BN;
+    ti.b_k = p.b_k0;
+    ti.m_base = mt * BM;
+    ti.n_base = ti.b_row;
+    ti.m_valid = min(BM, p.M - mt * BM);
+    ti.n_valid = min(BN, r1 - ti.b_row);
+    ti.d_off = 0;
+    return ti.n_valid > 0;
+  } else {
+    const int mt = t % p.m_tiles;
+    const int r = t / p.m_tiles;
+    const int nt = r % p.n_tiles;
+    const int z = r / p.n_tiles;
+    ti.a_row = p.a_row0 + z * p.a_batch_rows + mt * BM;
+    ti.a_k = p.a_k0 + z * p.a_batch_k;
+    ti.b_row = p.b_row0 + z * p.b_batch_rows + nt * BN;
+    ti.b_k = p.b_k0 + z * p.b_batch_k;
+    ti.m_base = mt * BM;
+    ti.n_base = nt * BN;
+    ti.m_valid = min(BM, p.M - mt * BM);
+    ti.n_valid = min(BN, p.N - nt * BN);
+    ti.d_off = (long long)z * p.d_batch_stride;
+    return true;
+  }
+}
+
+template <int BN>
+SP_DEVI void store_chunk(const GemmKParams& p, const TileInfo& ti, int m, int c0, const float (&v)[16]) {
+  if (m >= ti.m_valid) return;
+  const long long mg = ti.m_base + m;
+  if (p.out_f32) {
+    float* D = reinterpret_cast<float*>(p.D) + ti.d_off;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = c0 + j;
+      if (n < ti.n_valid) {
+        const long long ng = ti.n_base + n;
+        if (p.trans_out) D[ng * p.ldd + mg] = v[j];
+        else D[mg * p.ldd + ng] = v[j];
+      }
+    }
+    return;
+  }
+  __nv_bfloat16* D = reinterpret_cast<__nv_bfloat16*>(p.D) + ti.d_off;
+  if (p.trans_out) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = c0 + j;
+      if (n < ti.n_valid) D[(long long)(ti.n_base + n) * p.ldd + mg] = __float2bfloat16_rn(v[j]);
+    }
+  } else {
+    __nv_bfloat16* dst = D + mg * p.ldd + ti.n_base + c0;
+    if (c0 + 16 <= ti.n_valid && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+      st_bf16x8(dst, v);
+      st_bf16x8(dst + 8, v + 8);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (c0 + j < ti.n_valid) dst[j] = __float2bfloat16_rn(v[j]);
+    }
+  }
+}
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmKParams p) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* s_ntiles = s_err + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    *s_err = 0;
+    int nt = p.num_tiles;
+    if (MODE == MODE_GROUPED) nt = p.m_tiles * __ldg(p.grp_tiles + p.num_groups);
+    *s_ntiles = nt;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc<C::TMEM_COLS>(tmem_slot);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = *s_ntiles;
+
+  // Split-K: one tile per cluster; this CTA owns a slice of the K blocks.
+  int kb_begin = 0, kb_end = (p.K + BK - 1) / BK;
+  int tile_first = blockIdx.x, tile_step = gridDim.x;
+  uint32_t crank = 0;
+  if (MODE == MODE_SPLITK) {
+    crank = cluster_ctarank();
+    const int total_kb = kb_end;
+    kb_begin = (int)((long long)total_kb * crank / p.splits);
+    kb_end = (int)((long long)total_kb * (crank + 1) / p.splits);
+    tile_first = blockIdx.x / p.splits;
+    tile_step = 1 << 30;  // exactly one tile
+  }
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_a = p.a_evict_first ? policy_evict_first() : policy_evict_last();
+      int it = 0;
+      bool ok = true;
+      for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
+        TileInfo ti;
+        if (!get_tile<BN, MODE>(p, t, ti)) continue;
+        for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, s_err, p.err, kErrWaitTimeoutProducer)) { ok = false; break; }
+          uint8_t* sa = smem + s * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          tma_load_2d_hint(sa, &tmA, &full[s], ti.a_k + kb * BK, ti.a_row, pol_a);
+          tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], ti.b_k + kb * BK, ti.b_row);
+        }
+      }
+      if (!ok) {
+        // Let loads already in flight land before the CTA releases its memory.
+        for (int j = 0; j < C::STAGES && j < it; ++j) {
+          const int i2 = it - 1 - j;
+          mbar_wait(&full[i2 % C::STAGES], (i2 / C::STAGES) & 1, s_err, nullptr, 0);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int it = 0, tc = 0;
+      bool ok = true;
+      for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
+        TileInfo ti;
+        if (!get_tile<BN, MODE>(p, t, ti)) continue;
+        const int buf = tc & 1;
+        const uint32_t tph = (tc >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tph ^ 1, s_err, p.err, kErrWaitTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, s_err, p.err, kErrWaitTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint64_t adesc = sdesc_kmajor_sw128(sa);
+          const uint64_t bdesc = sdesc_kmajor_sw128(sa + C::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // +32 bytes of K per step -> +2 in the encoded start address
+            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[buf]);
+        ++tc;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter of this warp
+    const int m = q * 32 + lane;
+    const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
+    if (MODE != MODE_SPLITK) {
+      int tc = 0;
+      for (int t = tile_first; t < num_tiles; t += tile_step) {
+        TileInfo ti;
+        if (!get_tile<BN, MODE>(p, t, ti)) continue;
+        const int buf = tc & 1;
+        const uint32_t tph = (tc >> 1) & 1;
+        if (!mbar_wait(&tfull[buf], tph, s_err, p.err, kErrWaitTimeoutEpilogue)) break;
+        tc_fence_after();
+        for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
+          float v[16];
+          tmem_ld16(lane_addr + buf * BN + c0, v);
+          store_chunk<BN>(p, ti, m, c0, v);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[buf]);
+        ++tc;
+      }
+    } else {
+      // Split-K: park this CTA's fp32 partial tile in shared memory.
+      float* red = reinterpret_cast<float*>(smem);
+      if (mbar_wait(&tfull[0], 0, s_err, p.err, kErrWaitTimeoutEpilogue)) {
+        tc_fence_after();
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(lane_addr + c0, v);
+          float4* dst = reinterpret_cast<float4*>(red + m * C::RED_LD + c0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        tc_fence_before();
+      }
+    }
+  }
+
+  if (MODE == MODE_SPLITK) {
+    // Cluster-wide reduction of the partial tiles through DSMEM. Every thread of
+    // every CTA in the cluster takes both cluster barriers, error or not.
+    cluster_sync();
+    TileInfo ti;
+    get_tile<BN, MODE>(p, tile_first, ti);
+    const int rows = BM / p.splits;
+    const int r0 = crank * rows;
+    const uint32_t red_addr = smem_u32(smem);
+    const int n4 = BN / 4;
+    if (*s_err == 0) {
+      for (int idx = threadIdx.x; idx < rows * n4; idx += blockDim.x) {
+        int mm, nn;
+        if (p.trans_out) { mm = r0 + idx % rows; nn = (idx / rows) * 4; }
+        else { mm = r0 + idx / n4; nn = (idx % n4) * 4; }
+        if (mm >= ti.m_valid || nn >= ti.n_valid) continue;
+        const uint32_t off = uint32_t((mm * C::RED_LD + nn) * 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < p.splits; ++s) {
+          const float4 v = ld_dsmem_f32x4(mapa_shared(red_addr + off, s));
+          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+        const long long mg = ti.m_base + mm;
+        for (int j = 0; j < 4; ++j) {
+          if (nn + j >= ti.n_valid) break;
+          const long long ng = ti.n_base + nn + j;
+          const long long di = p.trans_out ? ng * p.ldd + mg : mg * p.ldd + ng;
+          if (p.out_f32) reinterpret_cast<float*>(p.D)[ti.d_off + di] = a4[j];
+          else reinterpret_cast<__nv_bfloat16*>(p.D)[ti.d_off + di] = __float2bfloat16_rn(a4[j]);
+        }
+      }
+    }
+    cluster_sync();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<C::TMEM_COLS>(tmem_base);
+  }
+}
+
+// ======================================================================= host
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !ptr)
+      throw std::runtime_error("sparkpipe: cannot resolve cuTensorMapEncodeTiled");
+    fn = reinterpret_cast<PFN_encodeTiled>(ptr);
+  }
+  return fn;
+}
+
+// 2-D K-major tensor map: `rows` x `cols` elements, row pitch `ld` elements, box
+// (box_cols x box_rows), 128-byte swizzle, zero fill outside the tensor.
+void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, long long rows,
+                  long long cols, long long ld, int box_rows, int box_cols) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) throw std::runtime_error("tensor map base not 16B aligned");
+  if ((ld * elem_bytes) % 16 != 0) throw std::runtime_error("tensor map row pitch not a multiple of 16 bytes");
+  cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)(ld * elem_bytes)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = get_encode_fn()(map, dt, 2, const_cast<void*>(ptr), gdim, gstride, box, estride,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+template <int BN, int MODE>
+static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
+  using C = GemmCfg<BN>;
+  CUtensorMap ta, tb;
+  make_tmap_2d(&ta, g.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.a_rows, g.a_cols, g.lda, BM, BK);
+  make_tmap_2d(&tb, g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.b_rows, g.b_cols, g.ldb, BN, BK);
+  auto kern = gemm_bf16_kernel<BN, MODE>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (MODE == MODE_SPLITK) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attrs[1];
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = g.stream;
+  if (MODE == MODE_SPLITK) {
+    if (C::STAGES * C::STAGE_BYTES < BM * C::RED_LD * 4) throw std::runtime_error("split-K reduce buffer too big");
+    cfg.gridDim = dim3(p.num_tiles * p.splits, 1, 1);
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = p.splits;
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 1;
+  } else {
+    int grid = MODE == MODE_GROUPED ? g.num_sms : std::min(p.num_tiles, g.num_sms);
+    if (grid < 1) grid = 1;
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.numAttrs = 0;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("gemm launch failed: ") + cudaGetErrorString(e));
+}
+
+template <int MODE>
+static void dispatch_bn(int bn, const GemmLaunch& g, GemmKParams& p) {
+  switch (bn) {
+    case 16: launch_gemm<16, MODE>(g, p); break;
+    case 32: launch_gemm<32, MODE>(g, p); break;
+    case 64: launch_gemm<64, MODE>(g, p); break;
+    case 128: launch_gemm<128, MODE>(g, p); break;
+    case 256: launch_gemm<256, MODE>(g, p); break;
+    default: throw std::runtime_error("unsupported BLOCK_N");
+  }
+}
+
+static int pick_bn(int n) {
+  if (n <= 16) return 16;
+  if (n <= 32) return 32;
+  if (n <= 64) return 64;
+  if (n <= 128) return 128;
+  return 256;
+}
+
+static void check_k_window(long long cols, int k0, int batch_k, int K, int batch) {
+  const long long kmax = (long long)k0 + (long long)batch_k * (batch - 1) + K;
+  if (kmax > cols) throw std::runtime_error("gemm: K window exceeds operand columns");
+  const bool partial = (k0 != 0) || (batch_k != 0) || (K != cols);
+  if (partial && (K % BK) != 0)
+    throw std::runtime_error("gemm: a K window inside a wider operand needs K % 64 == 0");
+}
+
+void gemm_bf16(const GemmLaunch& g) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return;
+  if (g.K % 8 != 0) throw std::runtime_error("gemm: K must be a multiple of 8");
+  check_k_window(g.a_cols, g.a_k0, g.a_batch_k, g.K, g.grouped ? 1 : g.batch);
+  check_k_window(g.b_cols, g.b_k0, g.b_batch_k, g.K, g.grouped ? 1 : g.batch);
+  GemmKParams p = {};
+  p.M = g.M; p.N = g.N; p.K = g.K;
+  p.batch = g.batch;
+  p.a_row0 = g.a_row0; p.a_batch_rows = g.a_batch_rows; p.a_k0 = g.a_k0; p.a_batch_k = g.a_batch_k;
+  p.b_row0 = g.b_row0; p.b_batch_rows = g.b_batch_rows; p.b_k0 = g.b_k0; p.b_batch_k = g.b_batch_k;
+  p.D = g.D; p.ldd = g.ldd; p.d_batch_stride = g.d_batch_stride;
+  p.trans_out = g.trans_out; p.out_f32 = g.out_f32;
+  p.err = g.err;
+  p.a_evict_first = g.a_evict_first;
+  p.m_tiles = (g.M + BM - 1) / BM;
+  if (g.grouped) {
+    const int bn = g.block_n > 0 ? g.block_n : 32;
+    p.n_tiles = 0;
+    p.num_tiles = 0;
+    p.grp_rows = g.grp_rows;
+    p.grp_tiles = g.grp_tiles;
+    p.num_groups = g.num_groups;
+    dispatch_bn<MODE_GROUPED>(bn, g, p);
+    return;
+  }
+  const int bn = g.block_n > 0 ? g.block_n : pick_bn(g.N);
+  p.n_tiles = (g.N + bn - 1) / bn;
+  p.num_tiles = p.m_tiles * p.n_tiles * g.batch;
+  int splits = g.splits;
+  const int kbs = (g.K + BK - 1) / BK;
+  if (splits <= 0) {
+    // Auto: split K over a cluster when the tile grid leaves most SMs idle.
+    splits = 1;
+    while (splits < 8 && p.num_tiles * splits * 2 <= g.num_sms && kbs / (splits * 2) >= 4) splits *= 2;
+  }
+  if (splits > 1 && bn > 128) splits = 1;  // reduce buffer must fit the stage memory
+  p.splits = splits;
+  if (splits > 1) dispatch_bn<MODE_SPLITK>(bn, g, p);
+  else dispatch_bn<MODE_DENSE>(bn, g, p);
+}
+
+}  // namespace sp

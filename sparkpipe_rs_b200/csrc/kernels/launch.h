@@ -1,0 +1,123 @@
+// Host-side launch interfaces of the sm_100a kernels. Plain C++ (no torch
+// headers) so the .cu translation units compile quickly; ops.cpp binds these
+// to torch tensors.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sp {
+
+// D[m, n] = sum_k A[m, k] * B[n, k]; see gemm_tcgen05.cu for the modes.
+struct GemmLaunch {
+  const void* A = nullptr;
+  long long a_rows = 0, a_cols = 0, lda = 0;  // 2-D view of A as stored (elements)
+  const void* B = nullptr;
+  long long b_rows = 0, b_cols = 0, ldb = 0;
+  void* D = nullptr;
+  long long ldd = 0, d_batch_stride = 0;
+  int M = 0, N = 0, K = 0, batch = 1;
+  int a_row0 = 0, a_batch_rows = 0, a_k0 = 0, a_batch_k = 0;
+  int b_row0 = 0, b_batch_rows = 0, b_k0 = 0, b_batch_k = 0;
+  int trans_out = 0;  // 1: write D^T, i.e. element (m, n) to D[n * ldd + m]
+  int out_f32 = 0;
+  int splits = 0;     // split-K cluster size; 0 = automatic, 1 = off
+  int block_n = 0;    // 0 = automatic
+  int grouped = 0;
+  const int* grp_rows = nullptr;   // [num_groups + 1] B-row prefix offsets
+  const int* grp_tiles = nullptr;  // [num_groups + 1] n-tile prefix counts (for block_n)
+  int num_groups = 0;
+  int a_evict_first = 0;
+  int* err = nullptr;
+  int num_sms = 148;
+  cudaStream_t stream = 0;
+};
+void gemm_bf16(const GemmLaunch& g);
+void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, long long rows,
+                  long long cols, long long ld, int box_rows, int box_cols);
+
+// ---- normalisation / rotary / KV cache (norm_rope.cu)
+// residual (optional, in/out) += x; out = rmsnorm(residual or x) * w.
+void add_rmsnorm(const void* x, long long ldx, void* residual, const void* w, void* out, long long ldo, int rows,
+                 int hidden, float eps, cudaStream_t s);
+// kv: [T, kv_lora + rope] rows (pitch ldkv). Writes norm(latent)|rope(k_pe) into
+// cache rows slot_mapping[t] (pitch kv_lora+rope) and, if latent_out != null,
+// the same row into latent_out (pitch ldl).
+void mla_kv_write(const void* kv, long long ldkv, const void* norm_w, const int* positions, const float* cos_sin,
+                  const int* slot_mapping, void* cache, void* latent_out, long long ldl, int T, int kv_lora, int rope,
+                  float eps, cudaStream_t s);
+// In-place-capable RoPE on q: src[t, h, rope_off : rope_off+rope] -> dst[t, h, dst_off : dst_off+rope]
+void rope_q(const void* src, long long src_tok, long long src_head, int src_off, void* dst, long long dst_tok,
+            long long dst_head, int dst_off, const int* positions, const float* cos_sin, int T, int H, int rope,
+            cudaStream_t s);
+// fp8 e4m3 activation quantisation with one fp32 scale per 128-element block.
+void quant_fp8_block(const void* x, long long ldx, void* q, float* scales, int rows, int cols, cudaStream_t s);
+
+// ---- MLA decode attention (mla_decode.cu)
+struct MlaDecodeLaunch {
+  const void* q = nullptr;        // [B, H, kv_lora + rope] bf16
+  const void* cache = nullptr;    // [num_slots, kv_lora + rope] bf16 (one layer)
+  long long num_slots = 0;
+  const int* block_table = nullptr;  // [B, max_blocks]
+  int max_blocks = 0;
+  const int* context_lens = nullptr; // [B]
+  void* out = nullptr;            // [B, H, kv_lora] bf16
+  float* o_part = nullptr;        // [B, splits, H, kv_lora] fp32 scratch
+  float* lse_part = nullptr;      // [B, splits, H] fp32 scratch
+  int B = 0, H = 0, kv_lora = 512, rope = 64, block_size = 64;
+  int splits = 1;
+  float scale = 1.f;
+  int* err = nullptr;
+  cudaStream_t stream = 0;
+};
+void mla_decode(const MlaDecodeLaunch& l);
+
+// ---- prefill attention (prefill_attn.cu)
+struct PrefillAttnLaunch {
+  const void* q = nullptr;  long long q_tok = 0, q_head = 0;      // [Tq, H, dn + dr]
+  const void* k = nullptr;  long long k_tok = 0, k_head = 0;      // nope part [Tk, H, dn]
+  const void* kpe = nullptr; long long kpe_tok = 0;               // rope part [Tk, dr] shared by heads
+  const void* v = nullptr;  long long v_tok = 0, v_head = 0;      // [Tk, H, dv]
+  void* o = nullptr;        long long o_tok = 0, o_head = 0;      // [Tq, H, dv]
+  const int* cu_q = nullptr; const int* cu_k = nullptr;           // [B + 1]
+  int B = 0, H = 0, max_q = 0;
+  int dn = 128, dr = 64, dv = 128;
+  float scale = 1.f;
+  int causal = 1;
+  cudaStream_t stream = 0;
+};
+void prefill_attention(const PrefillAttnLaunch& l);
+
+// ---- MoE routing (moe.cu)
+// scoring: 0 = softmax, 1 = sigmoid (+bias for selection). Weights are renormalised
+// over the selected experts when renorm != 0, then multiplied by `scaling`.
+void moe_topk(const float* logits, const float* bias, int* topk_ids, float* topk_w, int T, int E, int k, int scoring,
+              int renorm, float scaling, int n_group, int topk_group, cudaStream_t s);
+// Builds the expert-sorted row layout: counts -> grp_rows [E+1], grp_tiles [E+1]
+// (n-tiles of width block_n), sorted_tok [T*k] (source token of each sorted row),
+// inv_pos [T*k] (sorted row of pair (t, j)). `work` is E ints of scratch.
+void moe_align(const int* topk_ids, int T, int k, int E, int block_n, int* grp_rows, int* grp_tiles,
+               int* sorted_tok, int* inv_pos, int* work, cudaStream_t s);
+void gather_rows(const void* x, long long ldx, const int* idx, void* out, long long ldo, int rows, int cols,
+                 cudaStream_t s);
+void silu_mul(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s);
+// out[t] = sum_j w[t, j] * y[inv_pos[t*k + j]] (+ add[t] if add != null)
+void moe_combine(const void* y, long long ldy, const int* inv_pos, const float* topk_w, const void* add,
+                 long long ld_add, void* out, long long ldo, int T, int k, int H, cudaStream_t s);
+
+// ---- sampling / embedding / speculative verify (sampling.cu)
+void embedding(const void* table, long long ld, const int* ids, void* out, long long ldo, int T, int H,
+               cudaStream_t s);
+// temperature <= 0 -> greedy argmax; else Gumbel-max sampling seeded by (seed, offset, row).
+void sample_tokens(const void* logits, long long ldl, int T, int V, float temperature, unsigned long long seed,
+                   unsigned long long offset, int* out_ids, float* out_logit, cudaStream_t s);
+// Greedy speculative verification over a chain of L drafts per row.
+// target: [B, L+1] argmax tokens of the verifier; draft: [B, L].
+// forced_accept_p > 0 replaces the token comparison by a seeded Bernoulli(p).
+void spec_verify(const int* draft, const int* target, int B, int L, float forced_accept_p, unsigned long long seed,
+                 unsigned long long offset, int* accepted, int* committed, cudaStream_t s);
+
+void decode_advance(const int* out_ids, int* ids, int* pos, int* ctx, int* slots, const int* block_table,
+                    int max_blocks, int B, int block_size, cudaStream_t s);
+
+}  // namespace sp

@@ -1,0 +1,337 @@
+// MLA paged latent-KV decode attention (absorbed form), sm_100a.
+//
+// For each sequence b and head h:  o[b,h,:] = softmax(scale * q[b,h,:] . K^T) V
+// where K = cache rows [latent (kv_lora) | rope key (rope)] of the sequence's
+// paged blocks and V = the latent part of the same rows. All heads of a head
+// group share every KV byte, so one CTA streams each 64-token block once (TMA,
+// 128-byte swizzled sub-tiles, double buffered) and all of its warps consume it.
+//
+// Split-KV: a sequence's blocks are divided over `splits` CTAs; each writes a
+// normalised partial output and its log-sum-exp, and a combine kernel merges
+// them. With splits == 1 the kernel writes the bf16 output directly.
+//
+// Reference: PHASE_MLA_ATTENTION with ABSORBED_LATENT mode and block tables in
+// crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_resident_decode_stage.h:445-460,
+// 563-568 and the pipeline-slot buffers :815-867.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "launch.h"
+#include "mma_sync.cuh"
+
+namespace sp {
+
+using bf16 = __nv_bfloat16;
+
+struct MlaKParams {
+  const int* block_table;
+  int max_blocks;
+  const int* context_lens;
+  bf16* out;
+  float* o_part;
+  float* lse_part;
+  int B, H, splits;
+  float scale_log2;
+  int* err;
+};
+
+constexpr int MLA_DIM = 576;     // kv_lora 512 + rope 64
+constexpr int MLA_LAT = 512;
+constexpr int MLA_CHUNKS = 9;    // 64-element (128-byte) column chunks
+constexpr int MLA_BLK = 64;      // tokens per cache block
+constexpr int KV_STAGE_BYTES = MLA_CHUNKS * MLA_BLK * 128;
+
+template <int HG>
+struct MlaCfg {
+  static constexpr int WARPS = 4 * (HG / 16);
+  static constexpr int Q_BYTES = MLA_CHUNKS * HG * 128;
+  static constexpr int P_PITCH = 72;  // bf16 elements per P row (64 + 8 pad)
+  static constexpr int OFF_KV = (Q_BYTES + 1023) / 1024 * 1024;
+  static constexpr int OFF_P = OFF_KV + 2 * KV_STAGE_BYTES;
+  static constexpr int OFF_STAT = OFF_P + HG * P_PITCH * 2;
+  static constexpr int OFF_BAR = OFF_STAT + 2 * 4 * HG * 4;
+  static constexpr int SMEM = OFF_BAR + 64 + 1024;
+};
+
+template <int HG>
+__global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
+    mla_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+                      const MlaKParams p) {
+  using C = MlaCfg<HG>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sKV = smem_u32(smem + C::OFF_KV);
+  bf16* sP = reinterpret_cast<bf16*>(smem + C::OFF_P);
+  float* sMax = reinterpret_cast<float*>(smem + C::OFF_STAT);  // [4][HG]
+  float* sSum = sMax + 4 * HG;                                  // [4][HG]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* qbar = full + 2;
+  volatile int* s_err = reinterpret_cast<volatile int*>(qbar + 1);
+
+  const int b = blockIdx.x;
+  const int split = blockIdx.y;
+  const int hg = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = warp >> 2, j = warp & 3;
+
+  const int ctx = p.context_lens[b];
+  const int nblk = (ctx + MLA_BLK - 1) / MLA_BLK;
+  const int per = (nblk + p.splits - 1) / p.splits;
+  const int kb0 = min(nblk, split * per);
+  const int kb1 = min(nblk, kb0 + per);
+  const int nb = kb1 - kb0;
+  const int* bt = p.block_table + (long long)b * p.max_blocks;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    mbar_init(qbar, 1);
+    *s_err = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+
+  auto issue_block = [&](int i) {  // thread 0 only
+    const int s = i & 1;
+    const int pb = bt[kb0 + i];
+    uint64_t* bar = &full[s];
+    mbar_arrive_expect_tx(bar, KV_STAGE_BYTES);
+    uint8_t* dst = smem + C::OFF_KV + s * KV_STAGE_BYTES;
+#pragma unroll 1
+    for (int c = 0; c < MLA_CHUNKS; ++c) tma_load_2d(dst + c * MLA_BLK * 128, &tmKV, bar, c * 64, pb * MLA_BLK);
+  };
+  int issued = 0;
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmKV);
+    mbar_arrive_expect_tx(qbar, C::Q_BYTES);
+    for (int c = 0; c < MLA_CHUNKS; ++c) tma_load_2d(smem + c * HG * 128, &tmQ, qbar, c * 64, b * p.H + hg * HG);
+    for (; issued < 2 && issued < nb; ++issued) issue_block(issued);
+  }
+
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+  const int r_lo = lane >> 2;           // fragment rows r_lo and r_lo + 8
+  const int qrow = mt * 16;
+
+  bool ok = mbar_wait(qbar, 0, s_err, p.err, kErrWaitTimeoutMma);
+  ok = __syncthreads_and(ok);
+  for (int i = 0; ok && i < nb; ++i) {
+    const int s = i & 1;
+    bool got = mbar_wait(&full[s], (i >> 1) & 1, s_err, p.err, kErrWaitTimeoutMma);
+    if (!__syncthreads_and(got)) { ok = false; break; }
+    const uint32_t kvb = sKV + s * KV_STAGE_BYTES;
+
+    // ---- S = Q K^T for 16 heads x 16 tokens of this warp
+    float sc[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll 4
+    for (int kk = 0; kk < MLA_DIM / 16; ++kk) {
+      const int c = kk >> 2;
+      const int cc = (kk & 3) * 16;
+      uint32_t a[4], bb[4];
+      ldsm_x4(a, swz128(sQ + c * HG * 128, qrow + (lane & 15), cc + (lane >> 4) * 8));
+      ldsm_x4(bb, swz128(kvb + c * MLA_BLK * 128, j * 16 + (lane & 7) + (lane >> 4) * 8, cc + ((lane >> 3) & 1) * 8));
+      mma16816(sc[0], a, bb[0], bb[1]);
+      mma16816(sc[1], a, bb[2], bb[3]);
+    }
+    // ---- scale, mask, row max
+    const int tok0 = (kb0 + i) * MLA_BLK + j * 16;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = tok0 + n * 8 + (lane & 3) * 2 + (e & 1);
+        float v = sc[n][e] * p.scale_log2;
+        if (tok >= ctx) v = -INFINITY;
+        sc[n][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+    }
+    if ((lane & 3) == 0) {
+      sMax[j * HG + qrow + r_lo] = mx[0];
+      sMax[j * HG + qrow + r_lo + 8] = mx[1];
+    }
+    __syncthreads();
+    float alpha[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = qrow + r_lo + h * 8;
+      float mn = m_run[h];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) mn = fmaxf(mn, sMax[jj * HG + row]);
+      alpha[h] = (m_run[h] == -INFINITY) ? 0.f : exp2f(m_run[h] - mn);
+      m_run[h] = mn;
+      l_run[h] *= alpha[h];
+    }
+    // ---- P = exp2(S - m), stored bf16 for the PV product
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      float pv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mrow = m_run[e >> 1];
+        pv[e] = (sc[n][e] == -INFINITY) ? 0.f : exp2f(sc[n][e] - mrow);
+        l_run[e >> 1] += pv[e];
+      }
+      const int col = j * 16 + n * 8 + (lane & 3) * 2;
+      *reinterpret_cast<uint32_t*>(sP + (qrow + r_lo) * C::P_PITCH + col) = pack_bf16(pv[0], pv[1]);
+      *reinterpret_cast<uint32_t*>(sP + (qrow + r_lo + 8) * C::P_PITCH + col) = pack_bf16(pv[2], pv[3]);
+    }
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= alpha[0]; o[n][1] *= alpha[0];
+      o[n][2] *= alpha[1]; o[n][3] *= alpha[1];
+    }
+    __syncthreads();
+    // ---- O[16 heads, 128 dims of slice j] += P[16, 64] V[64, 128]
+    const uint32_t sPa = smem_u32(sP);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t a[4];
+      ldsm_x4(a, sPa + ((qrow + (lane & 15)) * C::P_PITCH + kk * 16 + (lane >> 4) * 8) * 2);
+      const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        const int dim = j * 128 + np * 16 + (lane >> 4) * 8;
+        uint32_t bb[4];
+        ldsm_x4_t(bb, swz128(kvb + (dim >> 6) * MLA_BLK * 128, tok, dim & 63));
+        mma16816(o[2 * np], a, bb[0], bb[1]);
+        mma16816(o[2 * np + 1], a, bb[2], bb[3]);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && issued < nb) { issue_block(issued); ++issued; }
+  }
+
+  if (!ok) {
+    // Drain loads still in flight before the CTA's shared memory is released.
+    if (threadIdx.x == 0) {
+      for (int i2 = max(0, issued - 2); i2 < issued; ++i2) mbar_wait(&full[i2 & 1], (i2 >> 1) & 1, s_err, nullptr, 0);
+    }
+    return;
+  }
+
+  // ---- final row sums across the 4 warps of this head tile
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+  }
+  if ((lane & 3) == 0) {
+    sSum[j * HG + qrow + r_lo] = l_run[0];
+    sSum[j * HG + qrow + r_lo + 8] = l_run[1];
+  }
+  __syncthreads();
+  float inv[2], lse[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = qrow + r_lo + h * 8;
+    float l = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) l += sSum[jj * HG + row];
+    inv[h] = l > 0.f ? 1.f / l : 0.f;
+    lse[h] = l > 0.f ? m_run[h] + __log2f(l) : -INFINITY;
+  }
+  const int head0 = hg * HG + qrow + r_lo;
+  if (p.splits == 1) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      bf16* orow = p.out + ((long long)b * p.H + head0 + h * 8) * MLA_LAT + j * 128 + (lane & 3) * 2;
+#pragma unroll
+      for (int n = 0; n < 16; ++n)
+        *reinterpret_cast<uint32_t*>(orow + n * 8) = pack_bf16(o[n][2 * h] * inv[h], o[n][2 * h + 1] * inv[h]);
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const long long rowi = ((long long)b * p.splits + split) * p.H + head0 + h * 8;
+      float* orow = p.o_part + rowi * MLA_LAT + j * 128 + (lane & 3) * 2;
+#pragma unroll
+      for (int n = 0; n < 16; ++n)
+        *reinterpret_cast<float2*>(orow + n * 8) = make_float2(o[n][2 * h] * inv[h], o[n][2 * h + 1] * inv[h]);
+      if (j == 0 && (lane & 3) == 0) p.lse_part[rowi] = lse[h];
+    }
+  }
+}
+
+__global__ void mla_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ lse,
+                                   bf16* __restrict__ out, int H, int S) {
+  const int b = blockIdx.x / H, h = blockIdx.x % H;
+  float M = -INFINITY;
+  for (int s = 0; s < S; ++s) M = fmaxf(M, lse[((long long)b * S + s) * H + h]);
+  float wsum = 0.f;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int d = threadIdx.x * 4;
+  for (int s = 0; s < S; ++s) {
+    const float l = lse[((long long)b * S + s) * H + h];
+    const float w = (l == -INFINITY) ? 0.f : exp2f(l - M);
+    wsum += w;
+    if (w > 0.f) {
+      const float4 v = *reinterpret_cast<const float4*>(o_part + (((long long)b * S + s) * H + h) * MLA_LAT + d);
+      acc[0] += w * v.x; acc[1] += w * v.y; acc[2] += w * v.z; acc[3] += w * v.w;
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  bf16* orow = out + ((long long)b * H + h) * MLA_LAT + d;
+  *reinterpret_cast<uint32_t*>(orow) = pack_bf16(acc[0] * inv, acc[1] * inv);
+  *reinterpret_cast<uint32_t*>(orow + 2) = pack_bf16(acc[2] * inv, acc[3] * inv);
+}
+
+template <int HG>
+static void launch_mla(const MlaDecodeLaunch& l) {
+  using C = MlaCfg<HG>;
+  CUtensorMap tq, tkv;
+  make_tmap_2d(&tq, l.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (long long)l.B * l.H, MLA_DIM, MLA_DIM, HG, 64);
+  make_tmap_2d(&tkv, l.cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.num_slots, MLA_DIM, MLA_DIM, MLA_BLK, 64);
+  auto kern = mla_decode_kernel<HG>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    attr = true;
+  }
+  MlaKParams p;
+  p.block_table = l.block_table;
+  p.max_blocks = l.max_blocks;
+  p.context_lens = l.context_lens;
+  p.out = (bf16*)l.out;
+  p.o_part = l.o_part;
+  p.lse_part = l.lse_part;
+  p.B = l.B;
+  p.H = l.H;
+  p.splits = l.splits;
+  p.scale_log2 = l.scale * 1.4426950408889634f;
+  p.err = l.err;
+  dim3 grid(l.B, l.splits, l.H / HG);
+  kern<<<grid, C::WARPS * 32, C::SMEM, l.stream>>>(tq, tkv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("mla_decode launch: ") + cudaGetErrorString(e));
+  if (l.splits > 1) {
+    mla_combine_kernel<<<l.B * l.H, MLA_LAT / 4, 0, l.stream>>>(l.o_part, l.lse_part, (bf16*)l.out, l.H, l.splits);
+  }
+}
+
+void mla_decode(const MlaDecodeLaunch& l) {
+  if (l.B <= 0) return;
+  if (l.kv_lora != MLA_LAT || l.rope != 64 || l.block_size != MLA_BLK)
+    throw std::runtime_error("mla_decode: supports kv_lora 512, rope 64, 64-token blocks");
+  if (l.splits > 1 && (!l.o_part || !l.lse_part)) throw std::runtime_error("mla_decode: split-KV needs scratch");
+  if (l.H % 32 == 0) launch_mla<32>(l);
+  else if (l.H % 16 == 0) launch_mla<16>(l);
+  else throw std::runtime_error("mla_decode: heads must be a multiple of 16");
+}
+
+}  // namespace sp

@@ -1,0 +1,252 @@
+// Mixture-of-experts routing and token layout kernels, sm_100a.
+//
+//  * moe_topk     — router scores (softmax, or sigmoid with a selection bias as in
+//                   the noaux_tc routers), top-k selection, optional renormalisation
+//                   and the routed scaling factor. One warp per token.
+//  * moe_align    — expert histogram -> per-expert row offsets and n-tile prefix
+//                   counts (the device-side tile schedule of the grouped GEMM) ->
+//                   scatter of (token, slot) pairs into expert-sorted rows.
+//  * gather_rows / silu_mul / moe_combine — row gather into the sorted layout,
+//                   SwiGLU activation, and the top-k weighted scatter-add back.
+//
+// Reference: FAST_MOE_ROUTER fields (moe_router_weight_bf16, score bias, routed
+// scaling factor, norm_topk_prob, topk ids/weights) of the resident decode stage
+// node context, crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_resident_decode_stage.h:869-1010,
+// and the fused top-k reduce of the FP8 MoE entry point (:321-342, :1053).
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace sp {
+
+using bf16 = __nv_bfloat16;
+
+constexpr int TOPK_MAX_PER_LANE = 16;  // E <= 512
+
+__global__ void moe_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                                int* __restrict__ ids, float* __restrict__ wts, int T, int E, int k, int scoring,
+                                int renorm, float scaling) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float* row = logits + (long long)t * E;
+  float score[TOPK_MAX_PER_LANE], sel[TOPK_MAX_PER_LANE];
+  const int per = (E + 31) / 32;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+    const int e = lane + i * 32;
+    score[i] = (i < per && e < E) ? row[e] : -INFINITY;
+    mx = fmaxf(mx, score[i]);
+  }
+  if (scoring == 0) {
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      score[i] = (score[i] == -INFINITY) ? 0.f : __expf(score[i] - mx);
+      sum += score[i];
+    }
+    sum = warp_sum(sum);
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      const int e = lane + i * 32;
+      score[i] *= inv;
+      sel[i] = (i < per && e < E) ? score[i] : -INFINITY;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      const int e = lane + i * 32;
+      const bool valid = i < per && e < E;
+      score[i] = valid ? 1.f / (1.f + __expf(-score[i])) : 0.f;
+      sel[i] = valid ? score[i] + (bias ? bias[e] : 0.f) : -INFINITY;
+    }
+  }
+  float wsum = 0.f;
+  float my_w = 0.f;
+  int my_id = 0;
+  for (int j = 0; j < k; ++j) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      const int e = lane + i * 32;
+      if (sel[i] > best) { best = sel[i]; bi = e; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    // owner lane publishes the routing weight of the chosen expert
+    float w = 0.f;
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      if (lane + i * 32 == bi) { w = score[i]; sel[i] = -INFINITY; }
+    }
+    w = warp_sum(w);  // only the owner contributed
+    wsum += w;
+    if (lane == j) { my_w = w; my_id = bi; }
+  }
+  const float norm = (renorm && wsum > 0.f) ? 1.f / wsum : 1.f;
+  if (lane < k) {
+    ids[(long long)t * k + lane] = my_id;
+    wts[(long long)t * k + lane] = my_w * norm * scaling;
+  }
+}
+
+void moe_topk(const float* logits, const float* bias, int* topk_ids, float* topk_w, int T, int E, int k, int scoring,
+              int renorm, float scaling, int n_group, int topk_group, cudaStream_t s) {
+  if (T <= 0) return;
+  if (E > 32 * TOPK_MAX_PER_LANE) throw std::runtime_error("moe_topk: at most 512 experts");
+  if (k > 32) throw std::runtime_error("moe_topk: k <= 32");
+  if (n_group > 1 && topk_group < n_group) throw std::runtime_error("moe_topk: group-limited routing not supported");
+  const int warps = 8;
+  moe_topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, s>>>(logits, bias, topk_ids, topk_w, T, E, k, scoring,
+                                                                  renorm, scaling);
+}
+
+__global__ void moe_count_kernel(const int* __restrict__ ids, int n, int* __restrict__ counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) atomicAdd(&counts[ids[i]], 1);
+}
+
+// One warp: exclusive prefix over E experts of counts and of ceil(count / bn).
+__global__ void moe_scan_kernel(int* __restrict__ counts, int E, int bn, int* __restrict__ grp_rows,
+                                int* __restrict__ grp_tiles) {
+  const int lane = threadIdx.x;
+  const int per = (E + 31) / 32;
+  const int e0 = lane * per;
+  int rs = 0, ts = 0;
+  for (int i = 0; i < per; ++i) {
+    const int e = e0 + i;
+    if (e < E) { const int c = counts[e]; rs += c; ts += (c + bn - 1) / bn; }
+  }
+  int ri = rs, ti = ts;  // inclusive scan across lanes
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(0xffffffffu, ri, o);
+    const int b = __shfl_up_sync(0xffffffffu, ti, o);
+    if (lane >= o) { ri += a; ti += b; }
+  }
+  int r = ri - rs, tt = ti - ts;  // exclusive base of this lane
+  for (int i = 0; i < per; ++i) {
+    const int e = e0 + i;
+    if (e < E) {
+      const int c = counts[e];
+      grp_rows[e] = r;
+      grp_tiles[e] = tt;
+      counts[e] = r;  // becomes the scatter cursor
+      r += c;
+      tt += (c + bn - 1) / bn;
+    }
+  }
+  if (lane == 31) { grp_rows[E] = ri; grp_tiles[E] = ti; }
+}
+
+__global__ void moe_scatter_kernel(const int* __restrict__ ids, int n, int k, int* __restrict__ cursor,
+                                   int* __restrict__ sorted_tok, int* __restrict__ inv_pos) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int pos = atomicAdd(&cursor[ids[i]], 1);
+  sorted_tok[pos] = i / k;
+  inv_pos[i] = pos;
+}
+
+void moe_align(const int* topk_ids, int T, int k, int E, int block_n, int* grp_rows, int* grp_tiles, int* sorted_tok,
+               int* inv_pos, int* work, cudaStream_t s) {
+  const int n = T * k;
+  cudaMemsetAsync(work, 0, sizeof(int) * E, s);
+  if (n > 0) moe_count_kernel<<<(n + 255) / 256, 256, 0, s>>>(topk_ids, n, work);
+  moe_scan_kernel<<<1, 32, 0, s>>>(work, E, block_n, grp_rows, grp_tiles);
+  if (n > 0) moe_scatter_kernel<<<(n + 255) / 256, 256, 0, s>>>(topk_ids, n, k, work, sorted_tok, inv_pos);
+}
+
+__global__ void gather_rows_kernel(const bf16* __restrict__ x, long long ldx, const int* __restrict__ idx,
+                                   bf16* __restrict__ out, long long ldo, int rows, int cols) {
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const uint4* src = reinterpret_cast<const uint4*>(x + (long long)idx[r] * ldx);
+  uint4* dst = reinterpret_cast<uint4*>(out + (long long)r * ldo);
+  for (int c = lane; c < cols / 8; c += 32) dst[c] = src[c];
+}
+
+void gather_rows(const void* x, long long ldx, const int* idx, void* out, long long ldo, int rows, int cols,
+                 cudaStream_t s) {
+  if (rows <= 0) return;
+  if (cols % 8 || ldx % 8 || ldo % 8) throw std::runtime_error("gather_rows: 16-byte rows required");
+  const int warps = 8;
+  gather_rows_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, s>>>((const bf16*)x, ldx, idx, (bf16*)out, ldo,
+                                                                        rows, cols);
+}
+
+__global__ void silu_mul_kernel(const bf16* __restrict__ h, long long ldh, bf16* __restrict__ out, long long ldo,
+                                int rows, int F) {
+  const int per_row = F / 8;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)rows * per_row) return;
+  const int r = i / per_row, c = (i % per_row) * 8;
+  float g[8], u[8];
+  ld_bf16x8(h + r * ldh + c, g);
+  ld_bf16x8(h + r * ldh + F + c, u);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) g[j] = g[j] / (1.f + __expf(-g[j])) * u[j];
+  st_bf16x8(out + r * ldo + c, g);
+}
+
+void silu_mul(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s) {
+  if (rows <= 0) return;
+  if (F % 8 || ldh % 8 || ldo % 8) throw std::runtime_error("silu_mul: 16-byte rows required");
+  const long long n = (long long)rows * (F / 8);
+  silu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const bf16*)h, ldh, (bf16*)out, ldo, rows, F);
+}
+
+__global__ void moe_combine_kernel(const bf16* __restrict__ y, long long ldy, const int* __restrict__ inv_pos,
+                                   const float* __restrict__ w, const bf16* __restrict__ add, long long lda,
+                                   bf16* __restrict__ out, long long ldo, int T, int k, int H) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  int pos[32];
+  float wt[32];
+  for (int j = 0; j < k; ++j) {
+    pos[j] = inv_pos[t * k + j];
+    wt[j] = w[t * k + j];
+  }
+  for (int c = lane * 8; c < H; c += 256) {
+    float acc[8];
+    if (add) ld_bf16x8(add + (long long)t * lda + c, acc);
+    else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    }
+    for (int j = 0; j < k; ++j) {
+      float v[8];
+      ld_bf16x8(y + (long long)pos[j] * ldy + c, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += wt[j] * v[e];
+    }
+    st_bf16x8(out + (long long)t * ldo + c, acc);
+  }
+}
+
+void moe_combine(const void* y, long long ldy, const int* inv_pos, const float* topk_w, const void* add,
+                 long long ld_add, void* out, long long ldo, int T, int k, int H, cudaStream_t s) {
+  if (T <= 0) return;
+  if (k > 32) throw std::runtime_error("moe_combine: k <= 32");
+  if (H % 8) throw std::runtime_error("moe_combine: hidden % 8");
+  const int warps = 8;
+  moe_combine_kernel<<<(T + warps - 1) / warps, warps * 32, 0, s>>>((const bf16*)y, ldy, inv_pos, topk_w,
+                                                                     (const bf16*)add, ld_add, (bf16*)out, ldo, T, k,
+                                                                     H);
+}
+
+}  // namespace sp

@@ -1,0 +1,313 @@
+// torch bindings of the sm_100a kernels. Every op launches on the current CUDA
+// stream (so it can be captured into a CUDA graph) and checks the device, dtype
+// and contiguity assumptions of its kernel before launching.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "launch.h"
+
+namespace {
+
+using torch::Tensor;
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bf16")
+#define CHECK_I32(x) TORCH_CHECK((x).scalar_type() == at::kInt, #x " must be int32")
+#define CHECK_F32(x) TORCH_CHECK((x).scalar_type() == at::kFloat, #x " must be fp32")
+#define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+
+// Per-device status word written by kernels on a bounded-wait timeout.
+std::mutex g_mu;
+std::unordered_map<int, int*> g_err;
+std::unordered_map<int, int> g_sms;
+
+int* err_word() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_err.find(dev);
+  if (it != g_err.end()) return it->second;
+  int* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, sizeof(int)) == cudaSuccess, "cannot allocate the kernel status word");
+  TORCH_CHECK(cudaMemset(p, 0, sizeof(int)) == cudaSuccess, "cannot clear the kernel status word");
+  g_err[dev] = p;
+  return p;
+}
+
+int num_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_sms.find(dev);
+  if (it != g_sms.end()) return it->second;
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  g_sms[dev] = n;
+  return n;
+}
+
+int status_word() {
+  int* p = err_word();
+  int v = 0;
+  TORCH_CHECK(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess, "status read failed");
+  return v;
+}
+
+void clear_status() {
+  int* p = err_word();
+  TORCH_CHECK(cudaMemset(p, 0, sizeof(int)) == cudaSuccess, "status clear failed");
+}
+
+void gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, int64_t a_cols, int64_t lda,
+          int64_t b_rows, int64_t b_cols, int64_t ldb, int64_t ldd, int64_t d_batch_stride, int64_t M, int64_t N,
+          int64_t K, int64_t batch, int64_t a_row0, int64_t a_batch_rows, int64_t a_k0, int64_t a_batch_k,
+          int64_t b_row0, int64_t b_batch_rows, int64_t b_k0, int64_t b_batch_k, int64_t trans_out, int64_t splits,
+          int64_t block_n, const c10::optional<Tensor>& grp_rows, const c10::optional<Tensor>& grp_tiles,
+          int64_t num_groups, int64_t a_evict_first) {
+  CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D);
+  CHECK_BF16(A); CHECK_BF16(B);
+  TORCH_CHECK(D.scalar_type() == at::kBFloat16 || D.scalar_type() == at::kFloat, "D must be bf16 or fp32");
+  const c10::cuda::CUDAGuard guard(A.device());
+  sp::GemmLaunch g;
+  g.A = A.data_ptr(); g.a_rows = a_rows; g.a_cols = a_cols; g.lda = lda;
+  g.B = B.data_ptr(); g.b_rows = b_rows; g.b_cols = b_cols; g.ldb = ldb;
+  g.D = D.data_ptr(); g.ldd = ldd; g.d_batch_stride = d_batch_stride;
+  g.M = (int)M; g.N = (int)N; g.K = (int)K; g.batch = (int)batch;
+  g.a_row0 = (int)a_row0; g.a_batch_rows = (int)a_batch_rows; g.a_k0 = (int)a_k0; g.a_batch_k = (int)a_batch_k;
+  g.b_row0 = (int)b_row0; g.b_batch_rows = (int)b_batch_rows; g.b_k0 = (int)b_k0; g.b_batch_k = (int)b_batch_k;
+  g.trans_out = (int)trans_out;
+  g.out_f32 = D.scalar_type() == at::kFloat ? 1 : 0;
+  g.splits = (int)splits;
+  g.block_n = (int)block_n;
+  if (grp_rows.has_value()) {
+    TORCH_CHECK(grp_tiles.has_value(), "grouped GEMM needs grp_tiles");
+    CHECK_I32(*grp_rows); CHECK_I32(*grp_tiles);
+    g.grouped = 1;
+    g.grp_rows = grp_rows->data_ptr<int>();
+    g.grp_tiles = grp_tiles->data_ptr<int>();
+    g.num_groups = (int)num_groups;
+  }
+  g.a_evict_first = (int)a_evict_first;
+  g.err = err_word();
+  g.num_sms = num_sms();
+  g.stream = stream();
+  sp::gemm_bf16(g);
+}
+
+void add_rmsnorm(const Tensor& x, const c10::optional<Tensor>& residual, const Tensor& w, const Tensor& out,
+                 double eps) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_BF16(out);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "add_rmsnorm: 2-D row-major");
+  const c10::cuda::CUDAGuard guard(x.device());
+  void* r = nullptr;
+  if (residual.has_value()) {
+    CHECK_BF16(*residual); CHECK_CONTIG(*residual);
+    r = residual->data_ptr();
+  }
+  sp::add_rmsnorm(x.data_ptr(), x.stride(0), r, w.data_ptr(), out.data_ptr(), out.stride(0), (int)x.size(0),
+                  (int)x.size(1), (float)eps, stream());
+}
+
+void mla_kv_write(const Tensor& kv, const Tensor& norm_w, const Tensor& positions, const Tensor& cos_sin,
+                  const c10::optional<Tensor>& slot_mapping, const Tensor& cache,
+                  const c10::optional<Tensor>& latent_out, int64_t kv_lora, int64_t rope, double eps) {
+  CHECK_CUDA(kv); CHECK_BF16(kv); CHECK_BF16(norm_w); CHECK_I32(positions); CHECK_F32(cos_sin);
+  TORCH_CHECK(kv.stride(1) == 1, "kv rows must be contiguous");
+  const c10::cuda::CUDAGuard guard(kv.device());
+  const int* slots = nullptr;
+  if (slot_mapping.has_value()) { CHECK_I32(*slot_mapping); slots = slot_mapping->data_ptr<int>(); }
+  void* lat = nullptr;
+  long long ldl = 0;
+  if (latent_out.has_value()) { CHECK_BF16(*latent_out); lat = latent_out->data_ptr(); ldl = latent_out->stride(0); }
+  sp::mla_kv_write(kv.data_ptr(), kv.stride(0), norm_w.data_ptr(), positions.data_ptr<int>(),
+                   cos_sin.data_ptr<float>(), slots, cache.data_ptr(), lat, ldl, (int)kv.size(0), (int)kv_lora,
+                   (int)rope, (float)eps, stream());
+}
+
+void rope_q(const Tensor& src, int64_t src_off, const Tensor& dst, int64_t dst_off, const Tensor& positions,
+            const Tensor& cos_sin, int64_t rope) {
+  // src/dst: [T, H, *] with unit innermost stride
+  CHECK_CUDA(src); CHECK_BF16(src); CHECK_BF16(dst); CHECK_I32(positions); CHECK_F32(cos_sin);
+  TORCH_CHECK(src.dim() == 3 && dst.dim() == 3 && src.stride(2) == 1 && dst.stride(2) == 1, "rope_q: [T, H, D]");
+  const c10::cuda::CUDAGuard guard(src.device());
+  sp::rope_q(src.data_ptr(), src.stride(0), src.stride(1), (int)src_off, dst.data_ptr(), dst.stride(0),
+             dst.stride(1), (int)dst_off, positions.data_ptr<int>(), cos_sin.data_ptr<float>(), (int)src.size(0),
+             (int)src.size(1), (int)rope, stream());
+}
+
+void quant_fp8_block(const Tensor& x, const Tensor& q, const Tensor& scales) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_F32(scales);
+  TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn, "q must be float8_e4m3fn");
+  CHECK_CONTIG(q); CHECK_CONTIG(scales);
+  const c10::cuda::CUDAGuard guard(x.device());
+  sp::quant_fp8_block(x.data_ptr(), x.stride(0), q.data_ptr(), scales.data_ptr<float>(), (int)x.size(0),
+                      (int)x.size(1), stream());
+}
+
+void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table, const Tensor& context_lens,
+                const Tensor& out, const c10::optional<Tensor>& o_part, const c10::optional<Tensor>& lse_part,
+                int64_t splits, double scale) {
+  CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(cache); CHECK_I32(block_table); CHECK_I32(context_lens); CHECK_BF16(out);
+  CHECK_CONTIG(q); CHECK_CONTIG(block_table); CHECK_CONTIG(out);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 576, "q: [B, H, 576]");
+  TORCH_CHECK(cache.size(-1) == 576 && cache.stride(-1) == 1, "cache rows of 576");
+  const c10::cuda::CUDAGuard guard(q.device());
+  sp::MlaDecodeLaunch l;
+  l.q = q.data_ptr();
+  l.cache = cache.data_ptr();
+  l.num_slots = cache.numel() / 576;
+  l.block_table = block_table.data_ptr<int>();
+  l.max_blocks = (int)block_table.size(1);
+  l.context_lens = context_lens.data_ptr<int>();
+  l.out = out.data_ptr();
+  if (o_part.has_value()) { CHECK_F32(*o_part); l.o_part = o_part->data_ptr<float>(); }
+  if (lse_part.has_value()) { CHECK_F32(*lse_part); l.lse_part = lse_part->data_ptr<float>(); }
+  l.B = (int)q.size(0);
+  l.H = (int)q.size(1);
+  l.splits = (int)splits;
+  l.scale = (float)scale;
+  l.err = err_word();
+  l.stream = stream();
+  sp::mla_decode(l);
+}
+
+void prefill_attention(const Tensor& q, const Tensor& k, const Tensor& kpe, const Tensor& v, const Tensor& o,
+                       const Tensor& cu_q, const Tensor& cu_k, int64_t max_q, double scale, bool causal) {
+  // q [Tq, H, 192], k [Tk, H, >=128] (nope part at offset 0), kpe [Tk, 64], v [Tk, H, 128], o [Tq, H, 128]
+  CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(kpe); CHECK_BF16(v); CHECK_BF16(o);
+  CHECK_I32(cu_q); CHECK_I32(cu_k);
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.dim() == 3 && o.dim() == 3 && kpe.dim() == 2, "prefill shapes");
+  TORCH_CHECK(q.stride(2) == 1 && k.stride(2) == 1 && v.stride(2) == 1 && o.stride(2) == 1 && kpe.stride(1) == 1,
+              "prefill: unit innermost stride");
+  const c10::cuda::CUDAGuard guard(q.device());
+  sp::PrefillAttnLaunch l;
+  l.q = q.data_ptr(); l.q_tok = q.stride(0); l.q_head = q.stride(1);
+  l.k = k.data_ptr(); l.k_tok = k.stride(0); l.k_head = k.stride(1);
+  l.kpe = kpe.data_ptr(); l.kpe_tok = kpe.stride(0);
+  l.v = v.data_ptr(); l.v_tok = v.stride(0); l.v_head = v.stride(1);
+  l.o = o.data_ptr(); l.o_tok = o.stride(0); l.o_head = o.stride(1);
+  l.cu_q = cu_q.data_ptr<int>(); l.cu_k = cu_k.data_ptr<int>();
+  l.B = (int)cu_q.size(0) - 1;
+  l.H = (int)q.size(1);
+  l.max_q = (int)max_q;
+  l.scale = (float)scale;
+  l.causal = causal ? 1 : 0;
+  l.stream = stream();
+  sp::prefill_attention(l);
+}
+
+void moe_topk(const Tensor& logits, const c10::optional<Tensor>& bias, const Tensor& ids, const Tensor& w,
+              int64_t scoring, bool renorm, double scaling) {
+  CHECK_CUDA(logits); CHECK_F32(logits); CHECK_CONTIG(logits); CHECK_I32(ids); CHECK_F32(w);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const float* b = nullptr;
+  if (bias.has_value()) { CHECK_F32(*bias); b = bias->data_ptr<float>(); }
+  sp::moe_topk(logits.data_ptr<float>(), b, ids.data_ptr<int>(), w.data_ptr<float>(), (int)logits.size(0),
+               (int)logits.size(1), (int)ids.size(1), (int)scoring, renorm ? 1 : 0, (float)scaling, 1, 1, stream());
+}
+
+void moe_align(const Tensor& topk_ids, int64_t num_experts, int64_t block_n, const Tensor& grp_rows,
+               const Tensor& grp_tiles, const Tensor& sorted_tok, const Tensor& inv_pos, const Tensor& work) {
+  CHECK_CUDA(topk_ids); CHECK_I32(topk_ids); CHECK_CONTIG(topk_ids);
+  CHECK_I32(grp_rows); CHECK_I32(grp_tiles); CHECK_I32(sorted_tok); CHECK_I32(inv_pos); CHECK_I32(work);
+  const c10::cuda::CUDAGuard guard(topk_ids.device());
+  sp::moe_align(topk_ids.data_ptr<int>(), (int)topk_ids.size(0), (int)topk_ids.size(1), (int)num_experts,
+                (int)block_n, grp_rows.data_ptr<int>(), grp_tiles.data_ptr<int>(), sorted_tok.data_ptr<int>(),
+                inv_pos.data_ptr<int>(), work.data_ptr<int>(), stream());
+}
+
+void gather_rows(const Tensor& x, const Tensor& idx, const Tensor& out) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(out); CHECK_I32(idx);
+  const c10::cuda::CUDAGuard guard(x.device());
+  sp::gather_rows(x.data_ptr(), x.stride(0), idx.data_ptr<int>(), out.data_ptr(), out.stride(0), (int)idx.size(0),
+                  (int)x.size(1), stream());
+}
+
+void silu_mul(const Tensor& h, const Tensor& out) {
+  CHECK_CUDA(h); CHECK_BF16(h); CHECK_BF16(out);
+  TORCH_CHECK(h.size(1) == 2 * out.size(1), "silu_mul: h is [R, 2F], out [R, F]");
+  const c10::cuda::CUDAGuard guard(h.device());
+  sp::silu_mul(h.data_ptr(), h.stride(0), out.data_ptr(), out.stride(0), (int)out.size(0), (int)out.size(1),
+               stream());
+}
+
+void moe_combine(const Tensor& y, const Tensor& inv_pos, const Tensor& w, const c10::optional<Tensor>& add,
+                 const Tensor& out, int64_t k) {
+  CHECK_CUDA(y); CHECK_BF16(y); CHECK_I32(inv_pos); CHECK_F32(w); CHECK_BF16(out);
+  const c10::cuda::CUDAGuard guard(y.device());
+  const void* a = nullptr;
+  long long lda = 0;
+  if (add.has_value()) { CHECK_BF16(*add); a = add->data_ptr(); lda = add->stride(0); }
+  sp::moe_combine(y.data_ptr(), y.stride(0), inv_pos.data_ptr<int>(), w.data_ptr<float>(), a, lda, out.data_ptr(),
+                  out.stride(0), (int)out.size(0), (int)k, (int)out.size(1), stream());
+}
+
+void embedding(const Tensor& table, const Tensor& ids, const Tensor& out) {
+  CHECK_CUDA(table); CHECK_BF16(table); CHECK_I32(ids); CHECK_BF16(out);
+  const c10::cuda::CUDAGuard guard(table.device());
+  sp::embedding(table.data_ptr(), table.stride(0), ids.data_ptr<int>(), out.data_ptr(), out.stride(0),
+                (int)ids.size(0), (int)table.size(1), stream());
+}
+
+void sample_tokens(const Tensor& logits, double temperature, int64_t seed, int64_t offset, const Tensor& out_ids,
+                   const c10::optional<Tensor>& out_logit) {
+  CHECK_CUDA(logits); CHECK_BF16(logits); CHECK_I32(out_ids);
+  TORCH_CHECK(logits.stride(1) == 1, "logits rows must be contiguous");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  float* ol = nullptr;
+  if (out_logit.has_value()) { CHECK_F32(*out_logit); ol = out_logit->data_ptr<float>(); }
+  sp::sample_tokens(logits.data_ptr(), logits.stride(0), (int)logits.size(0), (int)logits.size(1),
+                    (float)temperature, (unsigned long long)seed, (unsigned long long)offset, out_ids.data_ptr<int>(),
+                    ol, stream());
+}
+
+void spec_verify(const Tensor& draft, const Tensor& target, double p_accept, int64_t seed, int64_t offset,
+                 const Tensor& accepted, const Tensor& committed) {
+  CHECK_CUDA(draft); CHECK_I32(draft); CHECK_I32(target); CHECK_I32(accepted); CHECK_I32(committed);
+  CHECK_CONTIG(draft); CHECK_CONTIG(target); CHECK_CONTIG(committed);
+  const c10::cuda::CUDAGuard guard(draft.device());
+  sp::spec_verify(draft.data_ptr<int>(), target.data_ptr<int>(), (int)draft.size(0), (int)draft.size(1),
+                  (float)p_accept, (unsigned long long)seed, (unsigned long long)offset, accepted.data_ptr<int>(),
+                  committed.data_ptr<int>(), stream());
+}
+
+void decode_advance(const Tensor& out_ids, const Tensor& ids, const Tensor& pos, const Tensor& ctx,
+                    const Tensor& slots, const Tensor& block_table, int64_t block_size) {
+  CHECK_CUDA(ids); CHECK_I32(out_ids); CHECK_I32(ids); CHECK_I32(pos); CHECK_I32(ctx); CHECK_I32(slots);
+  CHECK_I32(block_table); CHECK_CONTIG(block_table);
+  const c10::cuda::CUDAGuard guard(ids.device());
+  sp::decode_advance(out_ids.data_ptr<int>(), ids.data_ptr<int>(), pos.data_ptr<int>(), ctx.data_ptr<int>(),
+                     slots.data_ptr<int>(), block_table.data_ptr<int>(), (int)block_table.size(1), (int)ids.size(0),
+                     (int)block_size, stream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of the sparkpipe_rs_b200 serving engine";
+  m.def("gemm", &gemm);
+  m.def("add_rmsnorm", &add_rmsnorm);
+  m.def("mla_kv_write", &mla_kv_write);
+  m.def("rope_q", &rope_q);
+  m.def("quant_fp8_block", &quant_fp8_block);
+  m.def("mla_decode", &mla_decode);
+  m.def("prefill_attention", &prefill_attention);
+  m.def("moe_topk", &moe_topk);
+  m.def("moe_align", &moe_align);
+  m.def("gather_rows", &gather_rows);
+  m.def("silu_mul", &silu_mul);
+  m.def("moe_combine", &moe_combine);
+  m.def("embedding", &embedding);
+  m.def("sample_tokens", &sample_tokens);
+  m.def("spec_verify", &spec_verify);
+  m.def("decode_advance", &decode_advance);
+  m.def("status_word", &status_word);
+  m.def("clear_status", &clear_status);
+  m.def("num_sms", &num_sms);
+}

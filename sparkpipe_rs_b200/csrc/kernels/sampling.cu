@@ -1,0 +1,172 @@
+// Token sampling, embedding gather and speculative-decode verification, sm_100a.
+//
+//  * sample_tokens — greedy argmax (temperature <= 0) or Gumbel-max sampling
+//                    (argmax of logits / T + Gumbel noise). Noise comes from a
+//                    SplitMix64 hash (Steele, Lea & Flood, OOPSLA 2014) of
+//                    (seed, offset, row, column), so a replay with the same seed
+//                    reproduces the same tokens.
+//  * embedding     — token id -> bf16 row.
+//  * spec_verify   — accept the longest draft prefix that matches the
+//                    verifier's tokens (or, for benchmarking, a seeded
+//                    Bernoulli(p) chain), emit the committed tokens (accepted
+//                    drafts + one verifier token).
+//
+// Reference: RESTRICTED_LOGITS / FUSED_FINAL_TOKEN_TAIL and MTP_VERIFY phases
+// of crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_resident_decode_stage.h:445-460, 645-671,
+// and the accept/commit rule of crates/spark-serve/src/request_api/speculation.rs:211-254.
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace sp {
+
+using bf16 = __nv_bfloat16;
+
+SP_DEVI uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+SP_DEVI float uniform01(uint64_t seed, uint64_t a, uint64_t b, uint64_t c) {
+  const uint64_t h = splitmix64(seed ^ splitmix64(a ^ splitmix64(b ^ splitmix64(c))));
+  return ((h >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
+}
+
+__global__ void sample_kernel(const bf16* __restrict__ logits, long long ldl, int V, float temp, uint64_t seed,
+                              uint64_t offset, int* __restrict__ out_ids, float* __restrict__ out_logit) {
+  const int row = blockIdx.x;
+  const bf16* lr = logits + (long long)row * ldl;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  const float inv_t = temp > 0.f ? 1.f / temp : 0.f;
+  const bool vec = (V % 8 == 0) && (ldl % 8 == 0);
+  if (vec) {
+    for (int c = threadIdx.x * 8; c < V; c += blockDim.x * 8) {
+      float v[8];
+      ld_bf16x8(lr + c, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float s = v[e];
+        if (temp > 0.f) s = s * inv_t - __logf(-__logf(uniform01(seed, offset, row, c + e)));
+        if (s > best) { best = s; bi = c + e; }
+      }
+    }
+  } else {
+    for (int c = threadIdx.x; c < V; c += blockDim.x) {
+      float s = __bfloat162float(lr[c]);
+      if (temp > 0.f) s = s * inv_t - __logf(-__logf(uniform01(seed, offset, row, c)));
+      if (s > best) { best = s; bi = c; }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sb[w] = best; si[w] = bi; }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sb[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    if (lane == 0) {
+      out_ids[row] = bi;
+      if (out_logit) out_logit[row] = __bfloat162float(lr[bi]);
+    }
+  }
+}
+
+void sample_tokens(const void* logits, long long ldl, int T, int V, float temperature, unsigned long long seed,
+                   unsigned long long offset, int* out_ids, float* out_logit, cudaStream_t s) {
+  if (T <= 0) return;
+  sample_kernel<<<T, 1024, 0, s>>>((const bf16*)logits, ldl, V, temperature, seed, offset, out_ids, out_logit);
+}
+
+__global__ void embedding_kernel(const bf16* __restrict__ table, long long ld, const int* __restrict__ ids,
+                                 bf16* __restrict__ out, long long ldo, int T, int H) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const uint4* src = reinterpret_cast<const uint4*>(table + (long long)ids[t] * ld);
+  uint4* dst = reinterpret_cast<uint4*>(out + (long long)t * ldo);
+  for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+}
+
+void embedding(const void* table, long long ld, const int* ids, void* out, long long ldo, int T, int H,
+               cudaStream_t s) {
+  if (T <= 0) return;
+  if (H % 8 || ld % 8 || ldo % 8) throw std::runtime_error("embedding: 16-byte rows required");
+  const int warps = 8;
+  embedding_kernel<<<(T + warps - 1) / warps, warps * 32, 0, s>>>((const bf16*)table, ld, ids, (bf16*)out, ldo, T,
+                                                                   H);
+}
+
+__global__ void spec_verify_kernel(const int* __restrict__ draft, const int* __restrict__ target, int B, int L,
+                                   float p_accept, uint64_t seed, uint64_t offset, int* __restrict__ accepted,
+                                   int* __restrict__ committed) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  int a = 0;
+  for (; a < L; ++a) {
+    bool ok;
+    if (p_accept > 0.f) ok = uniform01(seed, offset, b, a) < p_accept;
+    else ok = draft[b * L + a] == target[b * (L + 1) + a];
+    if (!ok) break;
+  }
+  accepted[b] = a;
+  // committed = accepted drafts followed by the verifier's token at the first
+  // rejected position (or the bonus token after a fully accepted chain)
+  for (int i = 0; i <= L; ++i) {
+    int tok = -1;
+    if (i < a) tok = draft[b * L + i];
+    else if (i == a) tok = target[b * (L + 1) + a];
+    committed[b * (L + 1) + i] = tok;
+  }
+}
+
+void spec_verify(const int* draft, const int* target, int B, int L, float forced_accept_p, unsigned long long seed,
+                 unsigned long long offset, int* accepted, int* committed, cudaStream_t s) {
+  if (B <= 0) return;
+  spec_verify_kernel<<<(B + 127) / 128, 128, 0, s>>>(draft, target, B, L, forced_accept_p, seed, offset, accepted,
+                                                      committed);
+}
+
+// Feeds a decode step's sampled tokens back as the next step's inputs: token id,
+// position + 1, context length + 1 and the cache slot of the new position
+// (from the block table; -1 once the table is exhausted). Rows with a zero
+// context length are idle and left untouched.
+__global__ void decode_advance_kernel(const int* __restrict__ out_ids, int* __restrict__ ids, int* __restrict__ pos,
+                                      int* __restrict__ ctx, int* __restrict__ slots,
+                                      const int* __restrict__ block_table, int max_blocks, int B, int block_size) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B || ctx[b] == 0) return;
+  ids[b] = out_ids[b];
+  const int p = pos[b] + 1;
+  pos[b] = p;
+  ctx[b] = p + 1;
+  const int blk = p / block_size;
+  slots[b] = blk < max_blocks ? block_table[(long long)b * max_blocks + blk] * block_size + p % block_size : -1;
+}
+
+void decode_advance(const int* out_ids, int* ids, int* pos, int* ctx, int* slots, const int* block_table,
+                    int max_blocks, int B, int block_size, cudaStream_t s) {
+  if (B <= 0) return;
+  decode_advance_kernel<<<(B + 127) / 128, 128, 0, s>>>(out_ids, ids, pos, ctx, slots, block_table, max_blocks, B,
+                                                         block_size);
+}
+
+}  // namespace sp

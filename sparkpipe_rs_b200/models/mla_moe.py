@@ -1,0 +1,269 @@
+"""MLA-MoE decoder running on the package's sm_100a kernels.
+
+Decode uses the absorbed MLA form (queries projected into the 512-d latent
+space, attention directly over the paged latent cache); prefill uses the
+expanded form (k_nope / v re-materialised from the latent by w_kv_b) with a
+flash-attention kernel, and writes the latent cache on the way.
+
+Every GEMM-shaped op goes through the tcgen05 kernel (``ops.linear`` /
+``ops.batched_gemm`` / ``ops.grouped_gemm``); the remaining ops are the
+package's own kernels. The whole decode step is static-shape and stream
+ordered, so ``DecodeGraph`` captures it into one CUDA graph per batch size.
+
+The reference executes the same phases inside its (absent) resident decode
+stage firmware: ATTENTION_NORM -> ATTENTION_PROJECTION -> ROPE_KV_WRITE ->
+MLA_ATTENTION -> OUTPUT_PROJECTION -> POST_ATTENTION_NORM -> LOCAL_MOE ->
+RESTRICTED_LOGITS (crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_resident_decode_stage.h:445-460).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+from .config import MLAMoEConfig
+from .rope import cos_sin_table
+from .weights import derive_decode_weights, init_weights
+
+
+@dataclass
+class ForwardBatch:
+    """Device-side inputs of one forward pass (all int32 tensors on the model device)."""
+
+    mode: str                       # "prefill" | "decode"
+    token_ids: torch.Tensor         # [T]
+    positions: torch.Tensor         # [T]
+    slot_mapping: torch.Tensor      # [T] cache row of each token (-1 = do not store)
+    # decode
+    block_table: torch.Tensor | None = None   # [B, max_blocks]
+    context_lens: torch.Tensor | None = None  # [B] (including the current token)
+    decode_splits: int = 1
+    # prefill
+    cu_q: torch.Tensor | None = None          # [B + 1]
+    cu_k: torch.Tensor | None = None          # [B + 1]
+    max_q: int = 0
+    ctx_slots: torch.Tensor | None = None     # [Tk] cache rows of every context token (prefix + chunk)
+    logits_idx: torch.Tensor | None = None    # rows to compute logits for (None = all)
+
+
+class KVCache:
+    """Paged latent KV cache: [layers, num_blocks * block_size, kv_lora + rope] bf16."""
+
+    def __init__(self, cfg: MLAMoEConfig, num_blocks: int, block_size: int = 64, device="cuda",
+                 layers: int | None = None):
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+        self.num_layers = layers if layers is not None else cfg.num_layers
+        self.data = torch.zeros(self.num_layers, num_blocks * block_size, cfg.kv_cache_dim, dtype=torch.bfloat16,
+                                device=device)
+
+    def layer(self, i: int) -> torch.Tensor:
+        return self.data[i]
+
+    @property
+    def bytes(self) -> int:
+        return self.data.numel() * self.data.element_size()
+
+
+def _moe_block_n(rows: int, experts: int) -> int:
+    avg = rows / max(1, experts)
+    for bn in (16, 32, 64, 128):
+        if avg <= bn * 0.75:
+            return bn
+    return 256
+
+
+class MLAMoEModel:
+    def __init__(self, cfg: MLAMoEConfig, weights: dict[str, torch.Tensor] | None = None, device="cuda",
+                 seed: int = 0, max_positions: int | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        if weights is None:
+            weights = init_weights(cfg, seed=seed, device=self.device, dtype=torch.bfloat16)
+        self.w = {k: v.to(self.device) for k, v in weights.items()}
+        derive_decode_weights(cfg, self.w)
+        maxp = max_positions or min(cfg.max_position_embeddings, 1 << 17)
+        self.cos_sin = cos_sin_table(cfg, maxp, device=self.device)
+        self.scale = cfg.softmax_scale()
+        self.qa_dim = cfg.q_lora_rank or cfg.q_out_dim
+
+    # ------------------------------------------------------------------ pieces
+    def _q_view(self, q2d: torch.Tensor, T: int) -> torch.Tensor:
+        c = self.cfg
+        return torch.as_strided(q2d, (T, c.num_heads, c.qk_head_dim), (q2d.stride(0), c.qk_head_dim, 1))
+
+    def _project(self, i: int, xn: torch.Tensor):
+        c, w = self.cfg, self.w
+        p = f"l{i}."
+        a = ops.linear(xn, w[p + "w_qkv_a"])
+        if c.q_lora_rank:
+            qa = torch.empty(xn.shape[0], c.q_lora_rank, dtype=torch.bfloat16, device=self.device)
+            ops.add_rmsnorm(a[:, : c.q_lora_rank], None, w[p + "q_a_norm"], qa, c.rms_norm_eps)
+            q = ops.linear(qa, w[p + "w_q_b"])
+        else:
+            q = a[:, : self.qa_dim]
+        kv_a = a[:, self.qa_dim:]
+        return q, kv_a
+
+    def _attn_decode(self, i: int, xn: torch.Tensor, fb: ForwardBatch, cache: KVCache) -> torch.Tensor:
+        c, w = self.cfg, self.w
+        p = f"l{i}."
+        T = xn.shape[0]
+        nh, dn, dv, kvl = c.num_heads, c.qk_nope_head_dim, c.v_head_dim, c.kv_lora_rank
+        q, kv_a = self._project(i, xn)
+        layer_cache = cache.layer(i)
+        ops.mla_kv_write(kv_a, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache, None,
+                         kvl, c.qk_rope_head_dim, c.rms_norm_eps)
+        q_lat = torch.empty(T, nh, c.kv_cache_dim, dtype=torch.bfloat16, device=self.device)
+        # q_lat[t, h, :kvl] = q_nope[t, h] @ W_UK[h]
+        ops.batched_gemm(w[p + "w_uk_t"], q, q_lat.view(T, nh * c.kv_cache_dim), M=kvl, N=T, K=dn, batch=nh,
+                         a_batch_rows=kvl, b_k0=0, b_batch_k=c.qk_head_dim, ldd=nh * c.kv_cache_dim,
+                         d_batch_stride=c.kv_cache_dim)
+        ops.rope_q(self._q_view(q, T), dn, q_lat, kvl, fb.positions, self.cos_sin, c.qk_rope_head_dim)
+        o_lat = torch.empty(T, nh, kvl, dtype=torch.bfloat16, device=self.device)
+        ops.mla_decode(q_lat, layer_cache, fb.block_table, fb.context_lens, o_lat, fb.decode_splits, self.scale)
+        attn = torch.empty(T, nh * dv, dtype=torch.bfloat16, device=self.device)
+        # attn[t, h*dv + v] = o_lat[t, h] @ W_UV[h]^T
+        ops.batched_gemm(w[p + "w_kv_b"], o_lat.view(T, nh * kvl), attn, M=dv, N=T, K=kvl, batch=nh, a_row0=dn,
+                         a_batch_rows=dn + dv, b_batch_k=kvl, ldd=nh * dv, d_batch_stride=dv)
+        return ops.linear(attn, w[p + "w_o"])
+
+    def _attn_prefill(self, i: int, xn: torch.Tensor, fb: ForwardBatch, cache: KVCache) -> torch.Tensor:
+        c, w = self.cfg, self.w
+        p = f"l{i}."
+        T = xn.shape[0]
+        nh, dn, dv, kvl, dr = c.num_heads, c.qk_nope_head_dim, c.v_head_dim, c.kv_lora_rank, c.qk_rope_head_dim
+        q, kv_a = self._project(i, xn)
+        layer_cache = cache.layer(i)
+        lat = torch.empty(T, c.kv_cache_dim, dtype=torch.bfloat16, device=self.device)
+        ops.mla_kv_write(kv_a, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache, lat,
+                         kvl, dr, c.rms_norm_eps)
+        lat_ctx = lat if fb.ctx_slots is None else ops.gather_rows(layer_cache, fb.ctx_slots)
+        Tk = lat_ctx.shape[0]
+        kv = ops.linear(lat_ctx[:, :kvl], w[p + "w_kv_b"])              # [Tk, nh*(dn+dv)]
+        q3 = self._q_view(q, T)
+        ops.rope_q(q3, dn, q3, dn, fb.positions, self.cos_sin, dr)
+        kv3 = kv.view(Tk, nh, dn + dv)
+        o = torch.empty(T, nh, dv, dtype=torch.bfloat16, device=self.device)
+        ops.prefill_attention(q3, kv3[:, :, :dn], lat_ctx[:, kvl:], kv3[:, :, dn:], o, fb.cu_q, fb.cu_k, fb.max_q,
+                              self.scale, True)
+        return ops.linear(o.view(T, nh * dv), w[p + "w_o"])
+
+    def _mlp(self, i: int, xn: torch.Tensor) -> torch.Tensor:
+        c, w = self.cfg, self.w
+        p = f"l{i}."
+        if not c.is_moe_layer(i):
+            return ops.linear(ops.silu_mul(ops.linear(xn, w[p + "w13"])), w[p + "w2"])
+        T = xn.shape[0]
+        E, k, F = c.n_routed_experts, c.num_experts_per_tok, c.moe_intermediate_size
+        logits = ops.linear(xn, w[p + "gate"], out_dtype=torch.float32)
+        sigmoid = c.scoring_func == "sigmoid"
+        ids, wts = ops.moe_topk(logits, w[p + "gate_bias"] if sigmoid else None, k, 1 if sigmoid else 0,
+                                c.norm_topk_prob, c.routed_scaling_factor)
+        bn = _moe_block_n(T * k, E)
+        grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E, bn)
+        xs = ops.gather_rows(xn, sorted_tok)
+        h13 = torch.empty(T * k, 2 * F, dtype=torch.bfloat16, device=self.device)
+        ops.grouped_gemm(w[p + "e_w13"], xs, h13, grp_rows, grp_tiles, E, bn)
+        act = ops.silu_mul(h13)
+        y = torch.empty(T * k, c.hidden_size, dtype=torch.bfloat16, device=self.device)
+        ops.grouped_gemm(w[p + "e_w2"], act, y, grp_rows, grp_tiles, E, bn)
+        shared = None
+        if c.n_shared_experts:
+            shared = ops.linear(ops.silu_mul(ops.linear(xn, w[p + "s_w13"])), w[p + "s_w2"])
+        out = torch.empty(T, c.hidden_size, dtype=torch.bfloat16, device=self.device)
+        ops.moe_combine(y, inv_pos, wts, shared, out, k)
+        return out
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, fb: ForwardBatch, cache: KVCache, layers: range | None = None,
+                hidden_in: torch.Tensor | None = None, return_hidden: bool = False):
+        """Runs `layers` (default: all) and returns logits [n, V] (bf16) of the rows in
+        fb.logits_idx, or the residual stream when return_hidden (pipeline stages)."""
+        c, w = self.cfg, self.w
+        T = fb.token_ids.shape[0]
+        layers = layers if layers is not None else range(c.num_layers)
+        eps = c.rms_norm_eps
+        if hidden_in is None:
+            res = ops.embedding(w["embed"], fb.token_ids)
+        else:
+            res = hidden_in.clone()
+        xn = torch.empty_like(res)
+        delta = None
+        for i in layers:
+            p = f"l{i}."
+            ops.add_rmsnorm(delta if delta is not None else res, res if delta is not None else None,
+                            w[p + "in_norm"], xn, eps)
+            if fb.mode == "decode":
+                o = self._attn_decode(i, xn, fb, cache)
+            else:
+                o = self._attn_prefill(i, xn, fb, cache)
+            ops.add_rmsnorm(o, res, w[p + "post_norm"], xn, eps)
+            delta = self._mlp(i, xn)
+        if return_hidden:
+            if delta is not None:
+                res.add_(delta)
+            return res
+        if delta is not None:
+            ops.add_rmsnorm(delta, res, w["final_norm"], xn, eps)
+        else:
+            ops.add_rmsnorm(res, None, w["final_norm"], xn, eps)
+        sel = xn if fb.logits_idx is None else ops.gather_rows(xn, fb.logits_idx)
+        return ops.linear(sel, w["lm_head"])
+
+
+class DecodeGraph:
+    """One CUDA graph of a full decode step (forward + greedy/seeded sampling) for a
+    fixed batch size. Inputs are copied into static device buffers before replay."""
+
+    def __init__(self, model: MLAMoEModel, cache: KVCache, batch: int, max_blocks: int, max_context: int,
+                 temperature: float = 0.0, seed: int = 0, use_graph: bool = True, self_advance: bool = False):
+        self.model, self.cache, self.B = model, cache, batch
+        dev = model.device
+        self.ids = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.slots = torch.full((batch,), -1, dtype=torch.int32, device=dev)
+        self.block_table = torch.zeros(batch, max_blocks, dtype=torch.int32, device=dev)
+        self.ctx = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.out_ids = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.temperature, self.seed = temperature, seed
+        self.self_advance = self_advance
+        self.step_offset = torch.zeros(1, dtype=torch.int64)
+        heads = model.cfg.num_heads
+        self.fb = ForwardBatch(mode="decode", token_ids=self.ids, positions=self.pos, slot_mapping=self.slots,
+                               block_table=self.block_table, context_lens=self.ctx,
+                               decode_splits=ops.mla_decode_splits(batch, heads, max_context, ops.kernels().num_sms()))
+        self.graph = None
+        self.use_graph = use_graph
+        self._run_eager()  # warm-up (also sets kernel attributes outside capture)
+        torch.cuda.synchronize()
+        if use_graph:
+            self.graph = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(self.graph, stream=s):
+                    self._step()
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+
+    def _step(self):
+        logits = self.model.forward(self.fb, self.cache)
+        ops.sample_tokens(logits, self.temperature, self.seed, 0, out_ids=self.out_ids)
+        if self.self_advance:
+            ops.decode_advance(self.out_ids, self.ids, self.pos, self.ctx, self.slots, self.block_table,
+                               self.cache.block_size)
+
+    def _run_eager(self):
+        self._step()
+
+    def run(self):
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._run_eager()
+        return self.out_ids
+
+    def release(self):
+        self.graph = None

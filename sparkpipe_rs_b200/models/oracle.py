@@ -1,0 +1,119 @@
+"""Plain PyTorch fp32 forward of the MLA-MoE decoder: the numerics oracle.
+
+This is the reference every kernel and the engine are checked against. It uses
+the expanded (non-absorbed) MLA form, dense causal attention over the whole
+sequence and per-expert loops, in fp32, on whatever device its inputs live.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .config import MLAMoEConfig
+from .rope import apply_rope, cos_sin_table
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    x = x.float()
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+
+
+def route(cfg: MLAMoEConfig, x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor | None):
+    logits = x.float() @ gate.float().t()
+    if cfg.scoring_func == "softmax":
+        scores = logits.softmax(-1)
+        sel = scores
+    else:
+        scores = logits.sigmoid()
+        sel = scores + (bias.float() if bias is not None else 0.0)
+    ids = sel.topk(cfg.num_experts_per_tok, dim=-1).indices
+    w = scores.gather(-1, ids)
+    if cfg.norm_topk_prob:
+        w = w / w.sum(-1, keepdim=True)
+    return ids, w * cfg.routed_scaling_factor, logits
+
+
+def swiglu_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
+    h = x @ w13.float().t()
+    f = w13.shape[0] // 2
+    return (F.silu(h[..., :f]) * h[..., f:]) @ w2.float().t()
+
+
+def moe(cfg: MLAMoEConfig, W: dict, p: str, x: torch.Tensor, routing=None) -> torch.Tensor:
+    ids, w, _ = route(cfg, x, W[p + "gate"], W.get(p + "gate_bias")) if routing is None else routing
+    out = torch.zeros_like(x, dtype=torch.float32)
+    for e in range(cfg.n_routed_experts):
+        mask = ids == e
+        rows = mask.any(-1).nonzero().flatten()
+        if rows.numel() == 0:
+            continue
+        we = (w * mask).sum(-1)[rows]
+        y = swiglu_mlp(x[rows].float(), W[p + "e_w13"][e], W[p + "e_w2"][e])
+        out[rows] += we[:, None] * y
+    if cfg.n_shared_experts:
+        out += swiglu_mlp(x.float(), W[p + "s_w13"], W[p + "s_w2"])
+    return out
+
+
+def attention(cfg: MLAMoEConfig, W: dict, p: str, x: torch.Tensor, pos: torch.Tensor, table: torch.Tensor):
+    """x [S, H] of one sequence (positions pos) -> [S, H]."""
+    S = x.shape[0]
+    nh, dn, dr, dv = cfg.num_heads, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
+    kvl = cfg.kv_lora_rank
+    qa_dim = cfg.q_lora_rank or cfg.q_out_dim
+    a = x @ W[p + "w_qkv_a"].float().t()
+    if cfg.q_lora_rank:
+        q = rmsnorm(a[:, :qa_dim], W[p + "q_a_norm"], cfg.rms_norm_eps) @ W[p + "w_q_b"].float().t()
+    else:
+        q = a[:, :qa_dim]
+    kv_a = a[:, qa_dim:]
+    latent = rmsnorm(kv_a[:, :kvl], W[p + "kv_a_norm"], cfg.rms_norm_eps)
+    k_pe = apply_rope(kv_a[:, kvl:], pos, table)                     # [S, dr]
+    q = q.view(S, nh, dn + dr)
+    q_nope, q_pe = q[..., :dn], apply_rope(q[..., dn:], pos, table)
+    kv = (latent @ W[p + "w_kv_b"].float().t()).view(S, nh, dn + dv)
+    k_nope, v = kv[..., :dn], kv[..., dn:]
+    qf = torch.cat([q_nope, q_pe], -1).transpose(0, 1)                # [nh, S, dn+dr]
+    kf = torch.cat([k_nope, k_pe[:, None, :].expand(S, nh, dr)], -1).transpose(0, 1)
+    scores = (qf @ kf.transpose(1, 2)) * cfg.softmax_scale()
+    mask = torch.ones(S, S, dtype=torch.bool, device=x.device).tril()
+    scores = scores.masked_fill(~mask, float("-inf"))
+    o = scores.softmax(-1) @ v.transpose(0, 1)                        # [nh, S, dv]
+    o = o.transpose(0, 1).reshape(S, nh * dv)
+    return o @ W[p + "w_o"].float().t()
+
+
+def forward(cfg: MLAMoEConfig, W: dict, tokens: torch.Tensor, table: torch.Tensor | None = None,
+            return_hidden: bool = False):
+    """tokens [S] (one sequence) -> logits [S, V] in fp32."""
+    S = tokens.shape[0]
+    pos = torch.arange(S, device=tokens.device)
+    if table is None:
+        table = cos_sin_table(cfg, max(S, 1), device=tokens.device)
+    h = W["embed"][tokens.long()].float()
+    for i in range(cfg.num_layers):
+        p = f"l{i}."
+        h = h + attention(cfg, W, p, rmsnorm(h, W[p + "in_norm"], cfg.rms_norm_eps), pos, table)
+        x = rmsnorm(h, W[p + "post_norm"], cfg.rms_norm_eps)
+        if cfg.is_moe_layer(i):
+            h = h + moe(cfg, W, p, x)
+        else:
+            h = h + swiglu_mlp(x, W[p + "w13"], W[p + "w2"])
+    hn = rmsnorm(h, W["final_norm"], cfg.rms_norm_eps)
+    logits = hn @ W["lm_head"].float().t()
+    return (logits, h) if return_hidden else logits
+
+
+def greedy_generate(cfg: MLAMoEConfig, W: dict, prompt: torch.Tensor, new_tokens: int):
+    """Greedy decode by re-running the full forward each step (oracle for the engine).
+    Returns (generated ids [new_tokens], logits of each generated position [new_tokens, V])."""
+    seq = prompt.clone()
+    outs, logits_all = [], []
+    table = cos_sin_table(cfg, prompt.shape[0] + new_tokens + 1, device=prompt.device)
+    for _ in range(new_tokens):
+        logits = forward(cfg, W, seq, table)[-1]
+        nxt = int(logits.argmax())
+        outs.append(nxt)
+        logits_all.append(logits)
+        seq = torch.cat([seq, torch.tensor([nxt], dtype=seq.dtype, device=seq.device)])
+    return torch.tensor(outs), torch.stack(logits_all)

@@ -1,0 +1,102 @@
+"""Seeded random-init weights for the MLA-MoE decoder, in the engine's layout.
+
+Every matrix is ``[out_features, in_features]`` (K-major), which is the operand
+layout of the tcgen05 GEMM. Per layer ``i`` (prefix ``l{i}.``):
+
+  in_norm [H] · w_qkv_a [Qa + kv_lora + rope, H] (q path (LoRA-A or full q) and
+  kv_a fused into one GEMM) · q_a_norm [q_lora] · w_q_b [Hh*(dn+dr), q_lora] ·
+  kv_a_norm [kv_lora] · w_kv_b [Hh*(dn+dv), kv_lora] · w_o [H, Hh*dv] ·
+  post_norm [H] · dense: w13 [2I, H], w2 [H, I] · MoE: gate [E, H],
+  gate_bias [E] (fp32), e_w13 [E, 2F, H], e_w2 [E, H, F], s_w13 [2Fs, H], s_w2 [H, Fs]
+
+plus ``embed`` [V, H], ``final_norm`` [H] and ``lm_head`` [V, H]. ``w13`` stacks
+the gate projection rows on top of the up projection rows.
+
+Values are N(0, init_std) (norm weights 1, router bias 0), drawn per tensor from
+a generator seeded with (seed, tensor index), so any subset of layers or any
+device produces the same numbers.
+"""
+from __future__ import annotations
+
+import torch
+
+from .config import MLAMoEConfig
+
+
+def weight_shapes(cfg: MLAMoEConfig) -> dict[str, tuple]:
+    H, nh = cfg.hidden_size, cfg.num_heads
+    dn, dr, dv = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
+    qa = cfg.q_lora_rank or cfg.q_out_dim
+    shapes: dict[str, tuple] = {"embed": (cfg.vocab_size, H)}
+    for i in range(cfg.num_layers):
+        p = f"l{i}."
+        shapes[p + "in_norm"] = (H,)
+        shapes[p + "w_qkv_a"] = (qa + cfg.kv_cache_dim, H)
+        if cfg.q_lora_rank:
+            shapes[p + "q_a_norm"] = (cfg.q_lora_rank,)
+            shapes[p + "w_q_b"] = (nh * (dn + dr), cfg.q_lora_rank)
+        shapes[p + "kv_a_norm"] = (cfg.kv_lora_rank,)
+        shapes[p + "w_kv_b"] = (nh * (dn + dv), cfg.kv_lora_rank)
+        shapes[p + "w_o"] = (H, nh * dv)
+        shapes[p + "post_norm"] = (H,)
+        if cfg.is_moe_layer(i):
+            E, F = cfg.n_routed_experts, cfg.moe_intermediate_size
+            shapes[p + "gate"] = (E, H)
+            shapes[p + "gate_bias"] = (E,)
+            shapes[p + "e_w13"] = (E, 2 * F, H)
+            shapes[p + "e_w2"] = (E, H, F)
+            if cfg.n_shared_experts:
+                Fs = cfg.shared_intermediate
+                shapes[p + "s_w13"] = (2 * Fs, H)
+                shapes[p + "s_w2"] = (H, Fs)
+        else:
+            shapes[p + "w13"] = (2 * cfg.intermediate_size, H)
+            shapes[p + "w2"] = (H, cfg.intermediate_size)
+    shapes["final_norm"] = (H,)
+    shapes["lm_head"] = (cfg.vocab_size, H)
+    return shapes
+
+
+def _is_norm(name: str) -> bool:
+    return name.endswith("norm")
+
+
+def init_weights(cfg: MLAMoEConfig, seed: int = 0, device="cpu", dtype=torch.bfloat16,
+                 layers: list[int] | None = None) -> dict[str, torch.Tensor]:
+    """Random-init weights. ``layers`` restricts which decoder layers are created."""
+    shapes = weight_shapes(cfg)
+    out: dict[str, torch.Tensor] = {}
+    dev = torch.device(device)
+    for idx, (name, shape) in enumerate(shapes.items()):
+        if layers is not None and name.startswith("l"):
+            li = int(name[1:name.index(".")])
+            if li not in layers:
+                continue
+        if _is_norm(name):
+            out[name] = torch.ones(shape, dtype=dtype, device=dev)
+            continue
+        if name.endswith("gate_bias"):
+            out[name] = torch.zeros(shape, dtype=torch.float32, device=dev)
+            continue
+        g = torch.Generator(device=dev)
+        g.manual_seed((seed * 1_000_003 + idx) & 0x7FFFFFFFFFFFFFFF)
+        t = torch.empty(shape, dtype=dtype, device=dev)
+        if dtype in (torch.float32, torch.bfloat16, torch.float16):
+            t.normal_(0.0, cfg.init_std, generator=g)
+        else:
+            t.copy_(torch.empty(shape, dtype=torch.float32, device=dev).normal_(0.0, cfg.init_std, generator=g))
+        out[name] = t
+    return out
+
+
+def derive_decode_weights(cfg: MLAMoEConfig, w: dict[str, torch.Tensor]) -> None:
+    """Adds the absorbed-attention operand ``l{i}.w_uk_t`` [Hh * kv_lora, dn]:
+    per head the transpose of the k_nope rows of w_kv_b (K-major for the
+    q_nope -> latent product)."""
+    nh, dn, dv, kvl = cfg.num_heads, cfg.qk_nope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
+    for i in range(cfg.num_layers):
+        k = f"l{i}.w_kv_b"
+        if k not in w:
+            continue
+        kvb = w[k].view(nh, dn + dv, kvl)
+        w[f"l{i}.w_uk_t"] = kvb[:, :dn, :].transpose(1, 2).contiguous().view(nh * kvl, dn)

@@ -1,0 +1,261 @@
+"""Python entry points of the sm_100a kernels.
+
+Every function here launches one of the package's own CUDA kernels on the
+current stream; none falls back to a PyTorch implementation. On a machine
+without the compiled extension or without a CUDA device they raise.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import _ext
+
+__all__ = [
+    "kernels",
+    "linear",
+    "gemm",
+    "batched_gemm",
+    "grouped_gemm",
+    "add_rmsnorm",
+    "mla_kv_write",
+    "rope_q",
+    "quant_fp8_block",
+    "mla_decode",
+    "mla_decode_splits",
+    "prefill_attention",
+    "moe_topk",
+    "moe_align",
+    "gather_rows",
+    "silu_mul",
+    "moe_combine",
+    "embedding",
+    "sample_tokens",
+    "spec_verify",
+    "decode_advance",
+    "status_word",
+    "clear_status",
+    "SWAP_AB_MAX_TOKENS",
+    "launch_count",
+]
+
+# Up to this many tokens a linear layer runs "swap-AB": the weight fills the
+# 128-row MMA tile and the tokens become the N dimension (decode shapes).
+SWAP_AB_MAX_TOKENS = 256
+
+_K = None
+
+# Number of this package's kernels launched so far (host-side count of launches
+# issued through this module; a CUDA-graph replay re-runs the captured ones).
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
+
+def launch_count() -> int:
+    return LAUNCHES[0]
+
+
+def kernels():
+    global _K
+    if _K is None:
+        _K = _ext.kernels()
+    return _K
+
+
+def _rows_cols_ld(t: torch.Tensor):
+    assert t.dim() == 2 and t.stride(1) == 1, "operand must be a 2-D row-major view"
+    return t.size(0), t.size(1), t.stride(0)
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, d: torch.Tensor, *, M: int, N: int, K: int, trans_out: bool = False,
+         batch: int = 1, a_row0: int = 0, a_batch_rows: int = 0, a_k0: int = 0, a_batch_k: int = 0,
+         b_row0: int = 0, b_batch_rows: int = 0, b_k0: int = 0, b_batch_k: int = 0, ldd: int | None = None,
+         d_batch_stride: int = 0, splits: int = 0, block_n: int = 0, grp_rows=None, grp_tiles=None,
+         num_groups: int = 0, a_evict_first: bool = False) -> torch.Tensor:
+    """Raw tcgen05 GEMM: D[m, n] = sum_k A[m, k] B[n, k] (see gemm_tcgen05.cu)."""
+    ar, ac, lda = _rows_cols_ld(a)
+    br, bc, ldb = _rows_cols_ld(b)
+    if ldd is None:
+        ldd = d.stride(0)
+    kernels().gemm(a, b, d, ar, ac, lda, br, bc, ldb, ldd, d_batch_stride, M, N, K, batch, a_row0, a_batch_rows,
+                   a_k0, a_batch_k, b_row0, b_batch_rows, b_k0, b_batch_k, int(trans_out), splits, block_n,
+                   grp_rows, grp_tiles, num_groups, int(a_evict_first))
+    _count(1)
+    return d
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, out_dtype=torch.bfloat16,
+           splits: int = 0) -> torch.Tensor:
+    """y = x @ w.T for x [T, K] (row-major view) and w [O, K] (bf16)."""
+    T, K = x.shape
+    O = w.shape[0]
+    if out is None:
+        out = torch.empty(T, O, dtype=out_dtype, device=x.device)
+    if T == 0:
+        return out
+    if T <= SWAP_AB_MAX_TOKENS:
+        gemm(w, x, out, M=O, N=T, K=K, trans_out=True, splits=splits, a_evict_first=True)
+    else:
+        gemm(x, w, out, M=T, N=O, K=K, trans_out=False, splits=1)
+    return out
+
+
+def batched_gemm(a, b, d, *, M, N, K, batch, a_row0=0, a_batch_rows=0, a_k0=0, a_batch_k=0, b_row0=0,
+                 b_batch_rows=0, b_k0=0, b_batch_k=0, ldd=None, d_batch_stride=0, trans_out=True):
+    """Strided-batched GEMM, batch index z shifts A rows / K columns, B rows / K columns and D."""
+    return gemm(a, b, d, M=M, N=N, K=K, trans_out=trans_out, batch=batch, a_row0=a_row0, a_batch_rows=a_batch_rows,
+                a_k0=a_k0, a_batch_k=a_batch_k, b_row0=b_row0, b_batch_rows=b_batch_rows, b_k0=b_k0,
+                b_batch_k=b_batch_k, ldd=ldd, d_batch_stride=d_batch_stride, splits=1)
+
+
+def grouped_gemm(w: torch.Tensor, x_sorted: torch.Tensor, out: torch.Tensor, grp_rows: torch.Tensor,
+                 grp_tiles: torch.Tensor, num_groups: int, block_n: int) -> torch.Tensor:
+    """MoE expert GEMM: out[r] = W[g(r)] @ x_sorted[r] for rows r sorted by group.
+
+    w is [G, M, K] (or its [G*M, K] view), x_sorted [R, K], out [R, M].
+    """
+    if w.dim() == 3:
+        G, M, K = w.shape
+        w2 = w.view(G * M, K)
+    else:
+        w2 = w
+        M = w.shape[0] // num_groups
+        K = w.shape[1]
+    gemm(w2, x_sorted, out, M=M, N=x_sorted.shape[0], K=K, trans_out=True, a_batch_rows=M, block_n=block_n,
+         grp_rows=grp_rows, grp_tiles=grp_tiles, num_groups=num_groups, a_evict_first=True)
+    return out
+
+
+def add_rmsnorm(x, residual, w, out, eps):
+    kernels().add_rmsnorm(x, residual, w, out, float(eps))
+    _count(1)
+    return out
+
+
+def mla_kv_write(kv, norm_w, positions, cos_sin, slot_mapping, cache, latent_out, kv_lora, rope, eps):
+    kernels().mla_kv_write(kv, norm_w, positions, cos_sin, slot_mapping, cache, latent_out, kv_lora, rope, float(eps))
+    _count(1)
+
+
+def rope_q(src, src_off, dst, dst_off, positions, cos_sin, rope):
+    kernels().rope_q(src, src_off, dst, dst_off, positions, cos_sin, rope)
+    _count(1)
+
+
+def quant_fp8_block(x):
+    q = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(x.shape[0], x.shape[1] // 128, dtype=torch.float32, device=x.device)
+    kernels().quant_fp8_block(x, q, s)
+    _count(1)
+    return q, s
+
+
+def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 148) -> int:
+    """Split-KV factor: enough CTAs to cover the SMs without splits of under two blocks."""
+    groups = heads // (32 if heads % 32 == 0 else 16)
+    ctas = max(1, batch * groups)
+    want = max(1, math.ceil(num_sms / ctas))
+    blocks = max(1, math.ceil(max_context / 64))
+    return int(max(1, min(want, blocks // 2 if blocks >= 2 else 1, 16)))
+
+
+def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=None, lse_part=None):
+    B, H, _ = q.shape
+    if splits > 1 and o_part is None:
+        o_part = torch.empty(B, splits, H, 512, dtype=torch.float32, device=q.device)
+        lse_part = torch.empty(B, splits, H, dtype=torch.float32, device=q.device)
+    kernels().mla_decode(q, cache, block_table, context_lens, out, o_part, lse_part, splits, float(scale))
+    _count(1 + (1 if splits > 1 else 0))
+    return out
+
+
+def prefill_attention(q, k, kpe, v, o, cu_q, cu_k, max_q, scale, causal=True):
+    kernels().prefill_attention(q, k, kpe, v, o, cu_q, cu_k, int(max_q), float(scale), bool(causal))
+    _count(1)
+    return o
+
+
+def moe_topk(logits, bias, k, scoring, renorm, scaling):
+    T = logits.shape[0]
+    ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+    kernels().moe_topk(logits, bias, ids, w, int(scoring), bool(renorm), float(scaling))
+    _count(1)
+    return ids, w
+
+
+def moe_align(topk_ids, num_experts, block_n):
+    dev = topk_ids.device
+    n = topk_ids.numel()
+    grp_rows = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    grp_tiles = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    sorted_tok = torch.empty(n, dtype=torch.int32, device=dev)
+    inv_pos = torch.empty(n, dtype=torch.int32, device=dev)
+    work = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    kernels().moe_align(topk_ids, num_experts, block_n, grp_rows, grp_tiles, sorted_tok, inv_pos, work)
+    _count(3)
+    return grp_rows, grp_tiles, sorted_tok, inv_pos
+
+
+def gather_rows(x, idx, out=None):
+    if out is None:
+        out = torch.empty(idx.shape[0], x.shape[1], dtype=x.dtype, device=x.device)
+    kernels().gather_rows(x, idx, out)
+    _count(1)
+    return out
+
+
+def silu_mul(h, out=None):
+    if out is None:
+        out = torch.empty(h.shape[0], h.shape[1] // 2, dtype=h.dtype, device=h.device)
+    kernels().silu_mul(h, out)
+    _count(1)
+    return out
+
+
+def moe_combine(y, inv_pos, w, add, out, k):
+    kernels().moe_combine(y, inv_pos, w, add, out, int(k))
+    _count(1)
+    return out
+
+
+def embedding(table, ids, out=None):
+    if out is None:
+        out = torch.empty(ids.shape[0], table.shape[1], dtype=table.dtype, device=table.device)
+    kernels().embedding(table, ids, out)
+    _count(1)
+    return out
+
+
+def sample_tokens(logits, temperature=0.0, seed=0, offset=0, out_ids=None, out_logit=None):
+    if out_ids is None:
+        out_ids = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    kernels().sample_tokens(logits, float(temperature), int(seed), int(offset), out_ids, out_logit)
+    _count(1)
+    return out_ids
+
+
+def spec_verify(draft, target, p_accept=0.0, seed=0, offset=0):
+    B, L = draft.shape
+    accepted = torch.empty(B, dtype=torch.int32, device=draft.device)
+    committed = torch.empty(B, L + 1, dtype=torch.int32, device=draft.device)
+    kernels().spec_verify(draft, target, float(p_accept), int(seed), int(offset), accepted, committed)
+    _count(1)
+    return accepted, committed
+
+
+def decode_advance(out_ids, ids, pos, ctx, slots, block_table, block_size=64):
+    kernels().decode_advance(out_ids, ids, pos, ctx, slots, block_table, int(block_size))
+    _count(1)
+
+
+def status_word() -> int:
+    return int(kernels().status_word())
+
+
+def clear_status() -> None:
+    kernels().clear_status()

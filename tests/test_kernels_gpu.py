@@ -1,0 +1,325 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ops():
+    from sparkpipe_rs_b200 import ops
+
+    return ops
+
+
+def _close(out, ref, atol=3e-2, rtol=3e-2):
+    torch.testing.assert_close(out.float(), ref.float(), atol=atol, rtol=rtol)
+
+
+def _status_ok():
+    ops = _ops()
+    assert ops.status_word() == 0, f"kernel status word {ops.status_word()}"
+
+
+# ------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize("T,O,K", [(1, 3648, 2048), (7, 2048, 2048), (64, 2048, 1408), (64, 64, 2048),
+                                   (200, 5632, 2048), (33, 1000, 576)])
+def test_linear_swap_ab(T, O, K):
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(T * 7 + O)
+    x = torch.randn(T, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(O, K, device=DEV, generator=g) * 0.02).bfloat16()
+    out = ops.linear(x, w)
+    _close(out, x.float() @ w.float().t())
+    _status_ok()
+
+
+@pytest.mark.parametrize("splits", [1, 2, 4, 8])
+def test_linear_split_k_cluster(splits):
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(splits)
+    x = torch.randn(48, 2048, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(1000, 2048, device=DEV, generator=g) * 0.02).bfloat16()
+    out = ops.linear(x, w, splits=splits)
+    _close(out, x.float() @ w.float().t())
+    _status_ok()
+
+
+@pytest.mark.parametrize("T,O,K", [(1000, 3648, 2048), (4096, 2048, 2048), (300, 102400 // 8, 2048), (513, 4096, 512)])
+def test_linear_prefill(T, O, K):
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(T + O)
+    x = torch.randn(T, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(O, K, device=DEV, generator=g) * 0.02).bfloat16()
+    out = ops.linear(x, w)
+    _close(out, x.float() @ w.float().t())
+    _status_ok()
+
+
+def test_linear_fp32_out_and_strided_input():
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(3)
+    base = torch.randn(64, 3000, device=DEV, generator=g).bfloat16()
+    x = base[:, 128:128 + 2048]  # row pitch 3000, offset 128 elements (256 B)
+    w = (torch.randn(64, 2048, device=DEV, generator=g) * 0.02).bfloat16()
+    out = ops.linear(x, w, out_dtype=torch.float32)
+    assert out.dtype == torch.float32
+    _close(out, x.float() @ w.float().t(), atol=1e-3, rtol=1e-3)
+
+
+def test_batched_absorb_gemm():
+    """q_lat[t, h, :512] = q_nope[t, h] @ W_UK[h] and the W_UV un-absorb product."""
+    ops = _ops()
+    T, nh, dn, dr, dv, kvl = 37, 16, 128, 64, 128, 512
+    g = torch.Generator(device=DEV).manual_seed(5)
+    q = torch.randn(T, nh * (dn + dr), device=DEV, generator=g).bfloat16()
+    wkvb = (torch.randn(nh * (dn + dv), kvl, device=DEV, generator=g) * 0.02).bfloat16()
+    wuk_t = wkvb.view(nh, dn + dv, kvl)[:, :dn].transpose(1, 2).contiguous().view(nh * kvl, dn)
+    q_lat = torch.zeros(T, nh, kvl + dr, device=DEV, dtype=torch.bfloat16)
+    ops.batched_gemm(wuk_t, q, q_lat.view(T, nh * (kvl + dr)), M=kvl, N=T, K=dn, batch=nh, a_batch_rows=kvl,
+                     b_batch_k=dn + dr, ldd=nh * (kvl + dr), d_batch_stride=kvl + dr)
+    qn = q.float().view(T, nh, dn + dr)[..., :dn]
+    ref = torch.einsum("thd,hdc->thc", qn, wkvb.float().view(nh, dn + dv, kvl)[:, :dn])
+    _close(q_lat[..., :kvl], ref)
+    o_lat = torch.randn(T, nh, kvl, device=DEV, generator=g).bfloat16()
+    attn = torch.empty(T, nh * dv, device=DEV, dtype=torch.bfloat16)
+    ops.batched_gemm(wkvb, o_lat.view(T, nh * kvl), attn, M=dv, N=T, K=kvl, batch=nh, a_row0=dn,
+                     a_batch_rows=dn + dv, b_batch_k=kvl, ldd=nh * dv, d_batch_stride=dv)
+    ref2 = torch.einsum("thc,hvc->thv", o_lat.float(), wkvb.float().view(nh, dn + dv, kvl)[:, dn:]).reshape(T, -1)
+    _close(attn, ref2)
+    _status_ok()
+
+
+@pytest.mark.parametrize("T,E,k,bn", [(64, 64, 6, 16), (64, 64, 6, 32), (512, 16, 4, 64), (3000, 64, 6, 256)])
+def test_grouped_gemm_moe(T, E, k, bn):
+    ops = _ops()
+    H, F = 512, 384
+    g = torch.Generator(device=DEV).manual_seed(T + E)
+    x = torch.randn(T, H, device=DEV, generator=g).bfloat16()
+    ids = torch.stack([torch.randperm(E, device=DEV, generator=g)[:k] for _ in range(T)]).int()
+    w13 = (torch.randn(E, 2 * F, H, device=DEV, generator=g) * 0.02).bfloat16()
+    grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E, bn)
+    counts = torch.bincount(ids.flatten().long(), minlength=E)
+    assert torch.equal(grp_rows[1:].cpu() - grp_rows[:-1].cpu(), counts.int().cpu())
+    xs = ops.gather_rows(x, sorted_tok)
+    out = torch.empty(T * k, 2 * F, device=DEV, dtype=torch.bfloat16)
+    ops.grouped_gemm(w13, xs, out, grp_rows, grp_tiles, E, bn)
+    # reference: row r belongs to the expert whose row range holds it
+    rows = grp_rows.cpu().tolist()
+    ref = torch.empty_like(out, dtype=torch.float32)
+    for e in range(E):
+        r0, r1 = rows[e], rows[e + 1]
+        if r1 > r0:
+            ref[r0:r1] = xs[r0:r1].float() @ w13[e].float().t()
+    _close(out, ref)
+    # inv_pos maps (t, j) to a row holding token t
+    st = sorted_tok.cpu()
+    ip = inv_pos.cpu().view(T, k)
+    assert torch.equal(st[ip.flatten().long()].view(T, k), torch.arange(T).view(T, 1).expand(T, k).int())
+    _status_ok()
+
+
+# ------------------------------------------------------------------ norms / rope
+@pytest.mark.parametrize("rows,H", [(1, 2048), (64, 2048), (300, 7168), (17, 512)])
+def test_add_rmsnorm(rows, H):
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(rows)
+    x = torch.randn(rows, H, device=DEV, generator=g).bfloat16()
+    r = torch.randn(rows, H, device=DEV, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device=DEV, generator=g)).bfloat16()
+    r0 = r.clone()
+    out = torch.empty_like(x)
+    ops.add_rmsnorm(x, r, w, out, 1e-6)
+    s = (x.float() + r0.float()).bfloat16().float()
+    _close(r, s, atol=1e-2, rtol=1e-2)
+    ref = s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    _close(out, ref)
+    out2 = torch.empty_like(x)
+    ops.add_rmsnorm(x, None, w, out2, 1e-6)
+    ref2 = x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    _close(out2, ref2)
+
+
+def test_mla_kv_write_and_rope_q():
+    ops = _ops()
+    from sparkpipe_rs_b200.models.config import v2_lite
+    from sparkpipe_rs_b200.models.rope import apply_rope, cos_sin_table
+
+    cfg = v2_lite()
+    T, nh = 19, 16
+    g = torch.Generator(device=DEV).manual_seed(9)
+    tab = cos_sin_table(cfg, 4096, device=DEV)
+    kv = torch.randn(T, 3072 + 576, device=DEV, generator=g).bfloat16()
+    kv_a = kv[:, 3072:]
+    nw = (1 + 0.1 * torch.randn(512, device=DEV, generator=g)).bfloat16()
+    pos = torch.randint(0, 4000, (T,), device=DEV, generator=g).int()
+    slots = torch.randperm(256, device=DEV, generator=g)[:T].int()
+    slots[3] = -1
+    cache = torch.zeros(256, 576, device=DEV, dtype=torch.bfloat16)
+    lat = torch.empty(T, 576, device=DEV, dtype=torch.bfloat16)
+    ops.mla_kv_write(kv_a, nw, pos, tab, slots, cache, lat, 512, 64, 1e-6)
+    x = kv_a.float()
+    ref_lat = x[:, :512] * torch.rsqrt(x[:, :512].pow(2).mean(-1, keepdim=True) + 1e-6) * nw.float()
+    ref_pe = apply_rope(x[:, 512:], pos, tab)
+    _close(lat[:, :512], ref_lat)
+    _close(lat[:, 512:], ref_pe)
+    keep = slots >= 0
+    _close(cache[slots[keep].long()], lat[keep], atol=0, rtol=0)
+    q = torch.randn(T, nh, 192, device=DEV, generator=g).bfloat16()
+    q_lat = torch.zeros(T, nh, 576, device=DEV, dtype=torch.bfloat16)
+    ops.rope_q(q, 128, q_lat, 512, pos, tab, 64)
+    _close(q_lat[..., 512:], apply_rope(q.float()[..., 128:], pos, tab))
+
+
+def test_quant_fp8_block():
+    ops = _ops()
+    x = torch.randn(33, 1024, device=DEV).bfloat16() * 3
+    q, s = ops.quant_fp8_block(x)
+    deq = q.float().view(33, 8, 128) * s.view(33, 8, 1)
+    _close(deq.view(33, 1024), x.float(), atol=0.1, rtol=0.07)
+    amax = x.float().view(33, 8, 128).abs().amax(-1)
+    _close(s, amax / 448.0, atol=1e-6, rtol=1e-5)
+
+
+# ------------------------------------------------------------------ attention
+def _mla_ref(q, cache, bt, ctx, scale):
+    B, H, _ = q.shape
+    out = torch.empty(B, H, 512, device=q.device)
+    for b in range(B):
+        L = int(ctx[b])
+        blocks = bt[b, : (L + 63) // 64].long()
+        rows = (blocks[:, None] * 64 + torch.arange(64, device=q.device)).flatten()[:L]
+        kv = cache[rows].float()
+        s = (q[b].float() @ kv.t()) * scale
+        out[b] = s.softmax(-1) @ kv[:, :512]
+    return out
+
+
+@pytest.mark.parametrize("H,splits", [(16, 1), (16, 3), (32, 2), (64, 1), (128, 4)])
+def test_mla_decode(H, splits):
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(H + splits)
+    B, nblocks, maxb = 6, 64, 10
+    cache = torch.randn(nblocks * 64, 576, device=DEV, generator=g).bfloat16()
+    ctx = torch.tensor([1, 63, 64, 65, 300, 640][:B], device=DEV, dtype=torch.int32)
+    bt = torch.stack([torch.randperm(nblocks, device=DEV, generator=g)[:maxb] for _ in range(B)]).int()
+    q = torch.randn(B, H, 576, device=DEV, generator=g).bfloat16()
+    out = torch.empty(B, H, 512, device=DEV, dtype=torch.bfloat16)
+    scale = 1.0 / math.sqrt(192)
+    ops.mla_decode(q, cache, bt, ctx, out, splits, scale)
+    _close(out, _mla_ref(q, cache, bt, ctx, scale), atol=2e-2, rtol=2e-2)
+    _status_ok()
+
+
+def _prefill_ref(q, k, kpe, v, cu_q, cu_k, scale):
+    out = torch.empty(q.shape[0], q.shape[1], v.shape[2], device=q.device)
+    for b in range(len(cu_q) - 1):
+        q0, q1, k0, k1 = int(cu_q[b]), int(cu_q[b + 1]), int(cu_k[b]), int(cu_k[b + 1])
+        Lq, Lk = q1 - q0, k1 - k0
+        if Lq == 0:
+            continue
+        H = q.shape[1]
+        kk = torch.cat([k[k0:k1].float(), kpe[k0:k1].float()[:, None, :].expand(Lk, H, -1)], -1)
+        s = torch.einsum("qhd,khd->hqk", q[q0:q1].float(), kk) * scale
+        mask = torch.arange(Lk, device=q.device)[None, :] <= (Lk - Lq + torch.arange(Lq, device=q.device))[:, None]
+        s = s.masked_fill(~mask[None], float("-inf"))
+        out[q0:q1] = torch.einsum("hqk,khd->qhd", s.softmax(-1), v[k0:k1].float())
+    return out
+
+
+@pytest.mark.parametrize("qlens,klens", [([100, 64, 1], [100, 130, 50]), ([1024], [1024]), ([7, 200], [7, 333])])
+def test_prefill_attention(qlens, klens):
+    ops = _ops()
+    H = 4
+    g = torch.Generator(device=DEV).manual_seed(sum(qlens))
+    Tq, Tk = sum(qlens), sum(klens)
+    q = torch.randn(Tq, H, 192, device=DEV, generator=g).bfloat16()
+    kv = torch.randn(Tk, H, 256, device=DEV, generator=g).bfloat16()
+    kpe = torch.randn(Tk, 576, device=DEV, generator=g).bfloat16()[:, 512:]
+    cu_q = torch.tensor([0] + list(torch.tensor(qlens).cumsum(0)), device=DEV, dtype=torch.int32)
+    cu_k = torch.tensor([0] + list(torch.tensor(klens).cumsum(0)), device=DEV, dtype=torch.int32)
+    o = torch.empty(Tq, H, 128, device=DEV, dtype=torch.bfloat16)
+    scale = 1.0 / math.sqrt(192)
+    ops.prefill_attention(q, kv[:, :, :128], kpe, kv[:, :, 128:], o, cu_q, cu_k, max(qlens), scale)
+    ref = _prefill_ref(q, kv[:, :, :128], kpe, kv[:, :, 128:], cu_q.cpu(), cu_k.cpu(), scale)
+    _close(o, ref, atol=2e-2, rtol=2e-2)
+
+
+# ------------------------------------------------------------------ MoE routing
+@pytest.mark.parametrize("scoring,renorm,E,k", [(0, False, 64, 6), (1, True, 384, 8), (0, True, 8, 2)])
+def test_moe_topk(scoring, renorm, E, k):
+    ops = _ops()
+    T = 77
+    g = torch.Generator(device=DEV).manual_seed(E)
+    logits = torch.randn(T, E, device=DEV, generator=g)
+    bias = torch.randn(E, device=DEV, generator=g) * 0.1 if scoring == 1 else None
+    ids, w = ops.moe_topk(logits, bias, k, scoring, renorm, 2.5)
+    if scoring == 0:
+        sc = logits.softmax(-1)
+        sel = sc
+    else:
+        sc = logits.sigmoid()
+        sel = sc + bias
+    ref_ids = sel.topk(k, -1).indices
+    assert torch.equal(ids.long().sort(-1).values, ref_ids.sort(-1).values)
+    rw = sc.gather(-1, ids.long())
+    if renorm:
+        rw = rw / rw.sum(-1, keepdim=True)
+    _close(w, rw * 2.5, atol=1e-5, rtol=1e-5)
+
+
+def test_silu_mul_and_combine():
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(11)
+    h = torch.randn(50, 2 * 1408, device=DEV, generator=g).bfloat16()
+    a = ops.silu_mul(h)
+    ref = torch.nn.functional.silu(h.float()[:, :1408]) * h.float()[:, 1408:]
+    _close(a, ref)
+    T, k, H = 20, 6, 2048
+    y = torch.randn(T * k, H, device=DEV, generator=g).bfloat16()
+    inv = torch.randperm(T * k, device=DEV, generator=g).int()
+    w = torch.rand(T, k, device=DEV, generator=g)
+    add = torch.randn(T, H, device=DEV, generator=g).bfloat16()
+    out = torch.empty(T, H, device=DEV, dtype=torch.bfloat16)
+    ops.moe_combine(y, inv, w, add, out, k)
+    ref = add.float() + (w[..., None] * y.float()[inv.long()].view(T, k, H)).sum(1)
+    _close(out, ref)
+
+
+# ------------------------------------------------------------------ sampling / embedding / verify
+def test_sampling_greedy_and_seeded():
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(13)
+    logits = torch.randn(9, 102400, device=DEV, generator=g).bfloat16()
+    ids = ops.sample_tokens(logits)
+    assert torch.equal(ids.long(), logits.float().argmax(-1))
+    a = ops.sample_tokens(logits, temperature=1.0, seed=7, offset=3)
+    b = ops.sample_tokens(logits, temperature=1.0, seed=7, offset=3)
+    c = ops.sample_tokens(logits, temperature=1.0, seed=8, offset=3)
+    assert torch.equal(a, b) and not torch.equal(a, c)
+    # odd vocabulary exercises the scalar path
+    ids2 = ops.sample_tokens(logits[:, :1001].contiguous())
+    assert torch.equal(ids2.long(), logits[:, :1001].float().argmax(-1))
+
+
+def test_embedding():
+    ops = _ops()
+    table = torch.randn(1000, 2048, device=DEV).bfloat16()
+    ids = torch.tensor([0, 5, 999, 5], device=DEV, dtype=torch.int32)
+    assert torch.equal(ops.embedding(table, ids), table[ids.long()])
+
+
+def test_spec_verify():
+    ops = _ops()
+    draft = torch.tensor([[1, 2, 3], [1, 9, 3], [7, 7, 7]], device=DEV, dtype=torch.int32)
+    target = torch.tensor([[1, 2, 3, 4], [1, 2, 3, 4], [8, 0, 0, 0]], device=DEV, dtype=torch.int32)
+    acc, com = ops.spec_verify(draft, target)
+    assert acc.tolist() == [3, 1, 0]
+    assert com.tolist() == [[1, 2, 3, 4], [1, 2, -1, -1], [8, -1, -1, -1]]
+    acc2, _ = ops.spec_verify(torch.zeros(4096, 3, device=DEV, dtype=torch.int32),
+                              torch.ones(4096, 4, device=DEV, dtype=torch.int32), p_accept=0.7, seed=1)
+    # E[accepted] for a Bernoulli(0.7) chain of 3 = 0.7 + 0.49 + 0.343
+    assert abs(acc2.float().mean().item() - 1.533) < 0.08
