@@ -1,0 +1,75 @@
+"""Per-kernel device-time breakdown of one MLA-MoE decode step.
+
+Runs the kernel-backed model eagerly for a few decode steps of a batch with a
+given context length and prints, per kernel name, the summed device time per
+step (from the CUDA activity trace of torch.profiler) and its share. This is a
+diagnostic: the benchmark numbers come from CUDA-event timing without any
+profiler attached.
+
+    python -m sparkpipe_rs_b200.utils.profile_decode --batch 64 --ctx 1024
+"""
+from __future__ import annotations
+
+import argparse
+import collections
+import math
+
+import torch
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="v2_lite")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--ctx", type=int, default=1024)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = model default)")
+    args = ap.parse_args()
+
+    from sparkpipe_rs_b200.models.config import get_config
+    from sparkpipe_rs_b200.models.mla_moe import DecodeGraph, KVCache, MLAMoEModel
+
+    cfg = get_config(args.model)
+    if args.layers:
+        cfg = cfg.replace(num_layers=args.layers)
+    dev = torch.device("cuda", 0)
+    model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=args.ctx + 64)
+    B, bs = args.batch, 64
+    bps = math.ceil((args.ctx + args.steps + 8) / bs)
+    cache = KVCache(cfg, num_blocks=B * bps, block_size=bs, device=dev)
+    cache.data.normal_(0, 1)
+    bt = torch.arange(B * bps, dtype=torch.int32, device=dev).view(B, bps)
+    dg = DecodeGraph(model, cache, B, bps, args.ctx + args.steps + 8, use_graph=False, self_advance=True)
+    dg.block_table.copy_(bt)
+    dg.pos.fill_(args.ctx)
+    dg.ctx.fill_(args.ctx + 1)
+    dg.slots.copy_(bt[:, args.ctx // bs] * bs + args.ctx % bs)
+    for _ in range(2):
+        dg.run()
+    torch.cuda.synchronize()
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(args.steps):
+            dg.run()
+        torch.cuda.synchronize()
+    tot = collections.defaultdict(float)
+    cnt = collections.defaultdict(int)
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            name = ev.name.split("(")[0].split("<")[0][:60]
+            if "gemm_bf16_kernel" in ev.name:
+                name = ev.name.split("(")[0][:80]
+            tot[name] += ev.device_time_total
+            cnt[name] += 1
+    all_us = sum(tot.values()) / args.steps
+    print(f"decode step: batch {B}, context {args.ctx}, layers {cfg.num_layers}: "
+          f"{all_us / 1000:.3f} ms of kernel time per step")
+    print(f"{'kernel':80s} {'us/step':>10s} {'share':>7s} {'launches/step':>14s}")
+    for name, us in sorted(tot.items(), key=lambda kv: -kv[1]):
+        print(f"{name:80s} {us / args.steps:10.1f} {100 * us / args.steps / all_us:6.1f}% "
+              f"{cnt[name] / args.steps:14.1f}")
+
+
+if __name__ == "__main__":
+    main()

@@ -79,7 +79,8 @@ def test_prefill_then_decode_matches_oracle(q_lora):
                 ref = oracle.forward(cfg, w_ref, seq_state[b], model.cos_sin)[-1]
                 if model_logits is not None:
                     assert _cos(model_logits[b], ref) > 0.995, f"decode step {step} seq {b}"
-                assert int(out[b]) == int(ref.argmax()) or ref.topk(2).values.diff().abs().item() < 0.05
+                # greedy token agrees with the oracle unless the oracle's top logits nearly tie
+                assert ref[int(out[b])].item() >= ref.max().item() - 0.1
             cur = out.clone()
         dg.release()
     assert ops.status_word() == 0
