@@ -271,6 +271,15 @@ SP_DEVI float4 ld_dsmem_f32x4(uint32_t addr) {
   return v;
 }
 
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor in the stream
+// is still running. It must call griddep_wait() before touching memory the
+// predecessor writes (or reads, for buffers it overwrites); griddep_launch()
+// lets the next kernel in the stream start its own prologue.
+SP_DEVI void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+SP_DEVI void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- misc
 SP_DEVI float warp_sum(float v) {
 #pragma unroll

@@ -34,6 +34,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "pdl.h"
 
 namespace sp {
 
@@ -54,7 +55,8 @@ struct GemmKParams {
   const int* grp_rows;   // [G+1]
   const int* grp_tiles;  // [G+1]
   int num_groups;
-  int a_evict_first;
+  int a_evict_first;  // A is a weight operand: stream it with evict_first and prefetch it before the PDL wait
+  int swiglu;         // grouped: A rows are [64 gate | 64 up] per tile; write silu(gate) * up
   int* err;
 };
 
@@ -69,7 +71,8 @@ struct GemmCfg {
   static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int RED_LD = BN + 4;  // fp32 row pitch of the split-K reduce buffer
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int XBUF_BYTES = 64 * 17 * 4;  // SwiGLU exchange buffer (64 rows x 16 cols, padded)
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + XBUF_BYTES;
 };
 
 struct TileInfo {
@@ -177,6 +180,8 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  float* xbuf = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + 256);
+
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
       mbar_init(&full[i], 1);
@@ -187,9 +192,6 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&tempty[i], 128);
     }
     *s_err = 0;
-    int nt = p.num_tiles;
-    if (MODE == MODE_GROUPED) nt = p.m_tiles * __ldg(p.grp_tiles + p.num_groups);
-    *s_ntiles = nt;
     fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -201,8 +203,21 @@ __global__ void __launch_bounds__(192, 1)
     tmem_relinquish();
     tc_fence_before();
   }
+  // PDL: weights (A) never change while serving, so the producer may stream the
+  // first stages of A before the previous kernel has finished; everything else
+  // (B activations, outputs, device-side tile counts) waits for it.
+  const bool prefetch_a = (MODE != MODE_GROUPED) && p.a_evict_first;
+  const bool is_producer = (warp == 0 && lane == 0);
+  if (MODE == MODE_GROUPED) griddep_wait();  // the tile count lives in device memory
+  if (threadIdx.x == 0) {
+    int nt = p.num_tiles;
+    if (MODE == MODE_GROUPED) nt = p.m_tiles * __ldg(p.grp_tiles + p.num_groups);
+    *s_ntiles = nt;
+  }
   __syncthreads();
   tc_fence_after();
+  griddep_launch();
+  if (!(prefetch_a && is_producer)) griddep_wait();
   const uint32_t tmem_base = *tmem_slot;
   const int num_tiles = *s_ntiles;
 
@@ -225,14 +240,31 @@ __global__ void __launch_bounds__(192, 1)
       const uint64_t pol_a = p.a_evict_first ? policy_evict_first() : policy_evict_last();
       int it = 0;
       bool ok = true;
+      int pre = 0;  // stages whose A tile went out before the PDL wait
+      if (prefetch_a) {
+        if (tile_first < num_tiles) {
+          TileInfo t0;
+          get_tile<BN, MODE>(p, tile_first, t0);
+          pre = min(C::STAGES, kb_end - kb_begin);
+          for (int j = 0; j < pre; ++j) {
+            mbar_arrive_expect_tx(&full[j], C::STAGE_BYTES);
+            tma_load_2d_hint(smem + j * C::STAGE_BYTES, &tmA, &full[j], t0.a_k + (kb_begin + j) * BK, t0.a_row, pol_a);
+          }
+        }
+        griddep_wait();
+      }
       for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
         TileInfo ti;
         if (!get_tile<BN, MODE>(p, t, ti)) continue;
         for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, s_err, p.err, kErrWaitTimeoutProducer)) { ok = false; break; }
           uint8_t* sa = smem + s * C::STAGE_BYTES;
+          if (it < pre) {
+            tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], ti.b_k + kb * BK, ti.b_row);
+            continue;
+          }
+          if (!mbar_wait(&empty[s], ph ^ 1, s_err, p.err, kErrWaitTimeoutProducer)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
           tma_load_2d_hint(sa, &tmA, &full[s], ti.a_k + kb * BK, ti.a_row, pol_a);
           tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], ti.b_k + kb * BK, ti.b_row);
@@ -296,10 +328,36 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t tph = (tc >> 1) & 1;
         if (!mbar_wait(&tfull[buf], tph, s_err, p.err, kErrWaitTimeoutEpilogue)) break;
         tc_fence_after();
-        for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
-          float v[16];
-          tmem_ld16(lane_addr + buf * BN + c0, v);
-          store_chunk<BN>(p, ti, m, c0, v);
+        if (MODE == MODE_GROUPED && p.swiglu) {
+          // rows [0, 64) of the tile are gate features, rows [64, 128) the matching
+          // up features: exchange through shared memory, write silu(g) * u.
+          __nv_bfloat16* D = reinterpret_cast<__nv_bfloat16*>(p.D);
+          const int f = (ti.m_base >> 1) + m;
+          for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
+            float v[16];
+            tmem_ld16(lane_addr + buf * BN + c0, v);
+            if (m >= 64) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) xbuf[(m - 64) * 17 + j] = v[j];
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (m < 64 && 2 * m < ti.m_valid) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (c0 + j < ti.n_valid) {
+                  const float g = v[j], u = xbuf[m * 17 + j];
+                  D[(long long)(ti.n_base + c0 + j) * p.ldd + f] = __float2bfloat16_rn(g / (1.f + __expf(-g)) * u);
+                }
+              }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+          }
+        } else {
+          for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
+            float v[16];
+            tmem_ld16(lane_addr + buf * BN + c0, v);
+            store_chunk<BN>(p, ti, m, c0, v);
+          }
         }
         tc_fence_before();
         mbar_arrive(&tempty[buf]);
@@ -414,7 +472,7 @@ static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
     attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = g.stream;
@@ -431,7 +489,13 @@ static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
     int grid = MODE == MODE_GROUPED ? g.num_sms : std::min(p.num_tiles, g.num_sms);
     if (grid < 1) grid = 1;
     cfg.gridDim = dim3(grid, 1, 1);
+    cfg.attrs = attrs;
     cfg.numAttrs = 0;
+  }
+  if (pdl_enabled()) {
+    attrs[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs += 1;
   }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
   if (e != cudaSuccess) throw std::runtime_error(std::string("gemm launch failed: ") + cudaGetErrorString(e));
@@ -479,6 +543,9 @@ void gemm_bf16(const GemmLaunch& g) {
   p.trans_out = g.trans_out; p.out_f32 = g.out_f32;
   p.err = g.err;
   p.a_evict_first = g.a_evict_first;
+  p.swiglu = g.swiglu;
+  if (g.swiglu && (!g.grouped || !g.trans_out || g.out_f32 || g.M % 128 != 0))
+    throw std::runtime_error("gemm: fused SwiGLU needs a grouped, transposed bf16 GEMM with M % 128 == 0");
   p.m_tiles = (g.M + BM - 1) / BM;
   if (g.grouped) {
     const int bn = g.block_n > 0 ? g.block_n : 32;
@@ -501,6 +568,7 @@ void gemm_bf16(const GemmLaunch& g) {
     while (splits < 8 && p.num_tiles * splits * 2 <= g.num_sms && kbs / (splits * 2) >= 4) splits *= 2;
   }
   if (splits > 1 && bn > 128) splits = 1;  // reduce buffer must fit the stage memory
+  if (splits > kbs) splits = kbs;          // every CTA of the cluster needs at least one K block
   p.splits = splits;
   if (splits > 1) dispatch_bn<MODE_SPLITK>(bn, g, p);
   else dispatch_bn<MODE_DENSE>(bn, g, p);

@@ -28,6 +28,7 @@ struct GemmLaunch {
   const int* grp_tiles = nullptr;  // [num_groups + 1] n-tile prefix counts (for block_n)
   int num_groups = 0;
   int a_evict_first = 0;
+  int swiglu = 0;  // grouped only: fused silu(gate) * up epilogue, output [rows, M / 2]
   int* err = nullptr;
   int num_sms = 148;
   cudaStream_t stream = 0;
@@ -91,12 +92,14 @@ void prefill_attention(const PrefillAttnLaunch& l);
 // ---- MoE routing (moe.cu)
 // scoring: 0 = softmax, 1 = sigmoid (+bias for selection). Weights are renormalised
 // over the selected experts when renorm != 0, then multiplied by `scaling`.
-void moe_topk(const float* logits, const float* bias, int* topk_ids, float* topk_w, int T, int E, int k, int scoring,
-              int renorm, float scaling, int n_group, int topk_group, cudaStream_t s);
+// The last n_shared columns of topk_ids / topk_w are the shared experts E .. E+n_shared-1 (weight 1).
+void moe_topk(const float* logits, const float* bias, int* topk_ids, float* topk_w, int T, int E, int k, int n_shared,
+              int scoring, int renorm, float scaling, int n_group, int topk_group, cudaStream_t s);
 // Builds the expert-sorted row layout: counts -> grp_rows [E+1], grp_tiles [E+1]
 // (n-tiles of width block_n), sorted_tok [T*k] (source token of each sorted row),
 // inv_pos [T*k] (sorted row of pair (t, j)). `work` is E ints of scratch.
-void moe_align(const int* topk_ids, int T, int k, int E, int block_n, int* grp_rows, int* grp_tiles,
+// Returns the number of kernels launched.
+int moe_align(const int* topk_ids, int T, int k, int E, int block_n, int* grp_rows, int* grp_tiles,
                int* sorted_tok, int* inv_pos, int* work, cudaStream_t s);
 void gather_rows(const void* x, long long ldx, const int* idx, void* out, long long ldo, int rows, int cols,
                  cudaStream_t s);

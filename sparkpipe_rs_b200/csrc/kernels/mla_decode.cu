@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "pdl.h"
 #include "mma_sync.cuh"
 
 namespace sp {
@@ -61,6 +62,8 @@ template <int HG>
 __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
     mla_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       const MlaKParams p) {
+  griddep_wait();
+  griddep_launch();
   using C = MlaCfg<HG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -93,6 +96,8 @@ __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
     mbar_init(qbar, 1);
     *s_err = 0;
     fence_mbarrier_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmKV);
   }
   __syncthreads();
 
@@ -270,6 +275,8 @@ __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
 
 __global__ void mla_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ lse,
                                    bf16* __restrict__ out, int H, int S) {
+  griddep_wait();
+  griddep_launch();
   const int b = blockIdx.x / H, h = blockIdx.x % H;
   float M = -INFINITY;
   for (int s = 0; s < S; ++s) M = fmaxf(M, lse[((long long)b * S + s) * H + h]);
@@ -316,11 +323,10 @@ static void launch_mla(const MlaDecodeLaunch& l) {
   p.scale_log2 = l.scale * 1.4426950408889634f;
   p.err = l.err;
   dim3 grid(l.B, l.splits, l.H / HG);
-  kern<<<grid, C::WARPS * 32, C::SMEM, l.stream>>>(tq, tkv, p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) throw std::runtime_error(std::string("mla_decode launch: ") + cudaGetErrorString(e));
+  launch_k(kern, grid, dim3(C::WARPS * 32), C::SMEM, l.stream, tq, tkv, p);
   if (l.splits > 1) {
-    mla_combine_kernel<<<l.B * l.H, MLA_LAT / 4, 0, l.stream>>>(l.o_part, l.lse_part, (bf16*)l.out, l.H, l.splits);
+    launch_k(mla_combine_kernel, dim3(l.B * l.H), dim3(MLA_LAT / 4), 0, l.stream, (const float*)l.o_part,
+             (const float*)l.lse_part, (bf16*)l.out, l.H, l.splits);
   }
 }
 

@@ -2,10 +2,14 @@
 //
 //  * moe_topk     — router scores (softmax, or sigmoid with a selection bias as in
 //                   the noaux_tc routers), top-k selection, optional renormalisation
-//                   and the routed scaling factor. One warp per token.
+//                   and the routed scaling factor. Shared experts are appended as
+//                   always-selected experts E .. E+S-1 with weight 1, so they run
+//                   inside the same grouped GEMM as the routed experts.
 //  * moe_align    — expert histogram -> per-expert row offsets and n-tile prefix
 //                   counts (the device-side tile schedule of the grouped GEMM) ->
-//                   scatter of (token, slot) pairs into expert-sorted rows.
+//                   scatter of (token, slot) pairs into expert-sorted rows. Decode
+//                   sized problems run in one CTA (shared-memory histogram); large
+//                   ones use grid-wide atomics in three kernels.
 //  * gather_rows / silu_mul / moe_combine — row gather into the sorted layout,
 //                   SwiGLU activation, and the top-k weighted scatter-add back.
 //
@@ -20,6 +24,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "pdl.h"
 
 namespace sp {
 
@@ -28,8 +33,10 @@ using bf16 = __nv_bfloat16;
 constexpr int TOPK_MAX_PER_LANE = 16;  // E <= 512
 
 __global__ void moe_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
-                                int* __restrict__ ids, float* __restrict__ wts, int T, int E, int k, int scoring,
-                                int renorm, float scaling) {
+                                int* __restrict__ ids, float* __restrict__ wts, int T, int E, int k, int n_shared,
+                                int scoring, int renorm, float scaling) {
+  griddep_wait();
+  griddep_launch();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -85,43 +92,44 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, const float* _
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
     }
-    // owner lane publishes the routing weight of the chosen expert
     float w = 0.f;
 #pragma unroll
     for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
       if (lane + i * 32 == bi) { w = score[i]; sel[i] = -INFINITY; }
     }
-    w = warp_sum(w);  // only the owner contributed
+    w = warp_sum(w);  // only the owner lane contributed
     wsum += w;
     if (lane == j) { my_w = w; my_id = bi; }
   }
   const float norm = (renorm && wsum > 0.f) ? 1.f / wsum : 1.f;
+  const int kk = k + n_shared;
   if (lane < k) {
-    ids[(long long)t * k + lane] = my_id;
-    wts[(long long)t * k + lane] = my_w * norm * scaling;
+    ids[(long long)t * kk + lane] = my_id;
+    wts[(long long)t * kk + lane] = my_w * norm * scaling;
+  } else if (lane < kk) {
+    ids[(long long)t * kk + lane] = E + (lane - k);
+    wts[(long long)t * kk + lane] = 1.f;
   }
 }
 
-void moe_topk(const float* logits, const float* bias, int* topk_ids, float* topk_w, int T, int E, int k, int scoring,
-              int renorm, float scaling, int n_group, int topk_group, cudaStream_t s) {
+void moe_topk(const float* logits, const float* bias, int* topk_ids, float* topk_w, int T, int E, int k, int n_shared,
+              int scoring, int renorm, float scaling, int n_group, int topk_group, cudaStream_t s) {
   if (T <= 0) return;
   if (E > 32 * TOPK_MAX_PER_LANE) throw std::runtime_error("moe_topk: at most 512 experts");
-  if (k > 32) throw std::runtime_error("moe_topk: k <= 32");
+  if (k + n_shared > 32) throw std::runtime_error("moe_topk: k + shared <= 32");
   if (n_group > 1 && topk_group < n_group) throw std::runtime_error("moe_topk: group-limited routing not supported");
-  const int warps = 8;
-  moe_topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, s>>>(logits, bias, topk_ids, topk_w, T, E, k, scoring,
-                                                                  renorm, scaling);
+  const int warps = 2;
+  launch_k(moe_topk_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, s, logits, bias, topk_ids, topk_w, T,
+           E, k, n_shared, scoring, renorm, scaling);
 }
 
-__global__ void moe_count_kernel(const int* __restrict__ ids, int n, int* __restrict__ counts) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) atomicAdd(&counts[ids[i]], 1);
-}
+// ---------------------------------------------------------------- align
+constexpr int ALIGN_MAX_E = 1024;
 
-// One warp: exclusive prefix over E experts of counts and of ceil(count / bn).
-__global__ void moe_scan_kernel(int* __restrict__ counts, int E, int bn, int* __restrict__ grp_rows,
-                                int* __restrict__ grp_tiles) {
-  const int lane = threadIdx.x;
+// Exclusive scan of counts (and of their n-tile counts) by one warp; writes the
+// row / tile prefix arrays and leaves the scatter cursors in `cursor`.
+SP_DEVI void scan_counts_warp(const int* counts, int E, int bn, int* grp_rows, int* grp_tiles, int* cursor) {
+  const int lane = threadIdx.x & 31;
   const int per = (E + 31) / 32;
   const int e0 = lane * per;
   int rs = 0, ts = 0;
@@ -129,21 +137,21 @@ __global__ void moe_scan_kernel(int* __restrict__ counts, int E, int bn, int* __
     const int e = e0 + i;
     if (e < E) { const int c = counts[e]; rs += c; ts += (c + bn - 1) / bn; }
   }
-  int ri = rs, ti = ts;  // inclusive scan across lanes
+  int ri = rs, ti = ts;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int a = __shfl_up_sync(0xffffffffu, ri, o);
     const int b = __shfl_up_sync(0xffffffffu, ti, o);
     if (lane >= o) { ri += a; ti += b; }
   }
-  int r = ri - rs, tt = ti - ts;  // exclusive base of this lane
+  int r = ri - rs, tt = ti - ts;
   for (int i = 0; i < per; ++i) {
     const int e = e0 + i;
     if (e < E) {
       const int c = counts[e];
       grp_rows[e] = r;
       grp_tiles[e] = tt;
-      counts[e] = r;  // becomes the scatter cursor
+      cursor[e] = r;
       r += c;
       tt += (c + bn - 1) / bn;
     }
@@ -151,8 +159,52 @@ __global__ void moe_scan_kernel(int* __restrict__ counts, int E, int bn, int* __
   if (lane == 31) { grp_rows[E] = ri; grp_tiles[E] = ti; }
 }
 
+__global__ void __launch_bounds__(1024) moe_align_small_kernel(const int* __restrict__ ids, int n, int k, int E,
+                                                               int bn, int* __restrict__ grp_rows,
+                                                               int* __restrict__ grp_tiles,
+                                                               int* __restrict__ sorted_tok,
+                                                               int* __restrict__ inv_pos) {
+  griddep_wait();
+  griddep_launch();
+  __shared__ int cnt[ALIGN_MAX_E];
+  __shared__ int cur[ALIGN_MAX_E];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&cnt[ids[i]], 1);
+  __syncthreads();
+  if (threadIdx.x < 32) scan_counts_warp(cnt, E, bn, grp_rows, grp_tiles, cur);
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int pos = atomicAdd(&cur[ids[i]], 1);
+    sorted_tok[pos] = i / k;
+    inv_pos[i] = pos;
+  }
+}
+
+__global__ void moe_zero_kernel(int* __restrict__ p, int n) {
+  griddep_wait();
+  griddep_launch();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = 0;
+}
+
+__global__ void moe_count_kernel(const int* __restrict__ ids, int n, int* __restrict__ counts) {
+  griddep_wait();
+  griddep_launch();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) atomicAdd(&counts[ids[i]], 1);
+}
+
+__global__ void moe_scan_kernel(int* __restrict__ counts, int E, int bn, int* __restrict__ grp_rows,
+                                int* __restrict__ grp_tiles) {
+  griddep_wait();
+  griddep_launch();
+  scan_counts_warp(counts, E, bn, grp_rows, grp_tiles, counts);
+}
+
 __global__ void moe_scatter_kernel(const int* __restrict__ ids, int n, int k, int* __restrict__ cursor,
                                    int* __restrict__ sorted_tok, int* __restrict__ inv_pos) {
+  griddep_wait();
+  griddep_launch();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int pos = atomicAdd(&cursor[ids[i]], 1);
@@ -160,17 +212,28 @@ __global__ void moe_scatter_kernel(const int* __restrict__ ids, int n, int k, in
   inv_pos[i] = pos;
 }
 
-void moe_align(const int* topk_ids, int T, int k, int E, int block_n, int* grp_rows, int* grp_tiles, int* sorted_tok,
-               int* inv_pos, int* work, cudaStream_t s) {
+int moe_align(const int* topk_ids, int T, int k, int E, int block_n, int* grp_rows, int* grp_tiles, int* sorted_tok,
+              int* inv_pos, int* work, cudaStream_t s) {
   const int n = T * k;
-  cudaMemsetAsync(work, 0, sizeof(int) * E, s);
-  if (n > 0) moe_count_kernel<<<(n + 255) / 256, 256, 0, s>>>(topk_ids, n, work);
-  moe_scan_kernel<<<1, 32, 0, s>>>(work, E, block_n, grp_rows, grp_tiles);
-  if (n > 0) moe_scatter_kernel<<<(n + 255) / 256, 256, 0, s>>>(topk_ids, n, k, work, sorted_tok, inv_pos);
+  if (E > ALIGN_MAX_E) throw std::runtime_error("moe_align: at most 1024 experts");
+  if (n <= 16384) {
+    launch_k(moe_align_small_kernel, dim3(1), dim3(1024), 0, s, topk_ids, n, k, E, block_n, grp_rows, grp_tiles,
+             sorted_tok, inv_pos);
+    return 1;
+  }
+  launch_k(moe_zero_kernel, dim3(1), dim3(1024), 0, s, work, E);
+  launch_k(moe_count_kernel, dim3((n + 255) / 256), dim3(256), 0, s, (const int*)topk_ids, n, work);
+  launch_k(moe_scan_kernel, dim3(1), dim3(32), 0, s, work, E, block_n, grp_rows, grp_tiles);
+  launch_k(moe_scatter_kernel, dim3((n + 255) / 256), dim3(256), 0, s, (const int*)topk_ids, n, k, work, sorted_tok,
+           inv_pos);
+  return 4;
 }
 
+// ---------------------------------------------------------------- data movement
 __global__ void gather_rows_kernel(const bf16* __restrict__ x, long long ldx, const int* __restrict__ idx,
                                    bf16* __restrict__ out, long long ldo, int rows, int cols) {
+  griddep_wait();
+  griddep_launch();
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -183,13 +246,15 @@ void gather_rows(const void* x, long long ldx, const int* idx, void* out, long l
                  cudaStream_t s) {
   if (rows <= 0) return;
   if (cols % 8 || ldx % 8 || ldo % 8) throw std::runtime_error("gather_rows: 16-byte rows required");
-  const int warps = 8;
-  gather_rows_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, s>>>((const bf16*)x, ldx, idx, (bf16*)out, ldo,
-                                                                        rows, cols);
+  const int warps = 4;
+  launch_k(gather_rows_kernel, dim3((rows + warps - 1) / warps), dim3(warps * 32), 0, s, (const bf16*)x, ldx, idx,
+           (bf16*)out, ldo, rows, cols);
 }
 
 __global__ void silu_mul_kernel(const bf16* __restrict__ h, long long ldh, bf16* __restrict__ out, long long ldo,
                                 int rows, int F) {
+  griddep_wait();
+  griddep_launch();
   const int per_row = F / 8;
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)rows * per_row) return;
@@ -206,47 +271,52 @@ void silu_mul(const void* h, long long ldh, void* out, long long ldo, int rows, 
   if (rows <= 0) return;
   if (F % 8 || ldh % 8 || ldo % 8) throw std::runtime_error("silu_mul: 16-byte rows required");
   const long long n = (long long)rows * (F / 8);
-  silu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const bf16*)h, ldh, (bf16*)out, ldo, rows, F);
+  launch_k(silu_mul_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, (const bf16*)h, ldh, (bf16*)out, ldo,
+           rows, F);
 }
 
+constexpr int COMBINE_MAXK = 32;
+
+// One thread per 8 columns of one token: blockIdx.x = token, blockIdx.y = 1024-column chunk.
 __global__ void moe_combine_kernel(const bf16* __restrict__ y, long long ldy, const int* __restrict__ inv_pos,
                                    const float* __restrict__ w, const bf16* __restrict__ add, long long lda,
                                    bf16* __restrict__ out, long long ldo, int T, int k, int H) {
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  int pos[32];
-  float wt[32];
+  griddep_wait();
+  griddep_launch();
+  const int t = blockIdx.x;
+  __shared__ int s_pos[COMBINE_MAXK];
+  __shared__ float s_w[COMBINE_MAXK];
+  if (threadIdx.x < k) {
+    s_pos[threadIdx.x] = inv_pos[t * k + threadIdx.x];
+    s_w[threadIdx.x] = w[t * k + threadIdx.x];
+  }
+  __syncthreads();
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (c >= H) return;
+  float acc[8];
+  if (add) ld_bf16x8(add + (long long)t * lda + c, acc);
+  else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  }
   for (int j = 0; j < k; ++j) {
-    pos[j] = inv_pos[t * k + j];
-    wt[j] = w[t * k + j];
-  }
-  for (int c = lane * 8; c < H; c += 256) {
-    float acc[8];
-    if (add) ld_bf16x8(add + (long long)t * lda + c, acc);
-    else {
+    float v[8];
+    ld_bf16x8(y + (long long)s_pos[j] * ldy + c, v);
+    const float wj = s_w[j];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-    }
-    for (int j = 0; j < k; ++j) {
-      float v[8];
-      ld_bf16x8(y + (long long)pos[j] * ldy + c, v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += wt[j] * v[e];
-    }
-    st_bf16x8(out + (long long)t * ldo + c, acc);
+    for (int e = 0; e < 8; ++e) acc[e] += wj * v[e];
   }
+  st_bf16x8(out + (long long)t * ldo + c, acc);
 }
 
 void moe_combine(const void* y, long long ldy, const int* inv_pos, const float* topk_w, const void* add,
                  long long ld_add, void* out, long long ldo, int T, int k, int H, cudaStream_t s) {
   if (T <= 0) return;
-  if (k > 32) throw std::runtime_error("moe_combine: k <= 32");
+  if (k > COMBINE_MAXK) throw std::runtime_error("moe_combine: k <= 32");
   if (H % 8) throw std::runtime_error("moe_combine: hidden % 8");
-  const int warps = 8;
-  moe_combine_kernel<<<(T + warps - 1) / warps, warps * 32, 0, s>>>((const bf16*)y, ldy, inv_pos, topk_w,
-                                                                     (const bf16*)add, ld_add, (bf16*)out, ldo, T, k,
-                                                                     H);
+  const int threads = 128;
+  launch_k(moe_combine_kernel, dim3(T, (H / 8 + threads - 1) / threads), dim3(threads), 0, s, (const bf16*)y, ldy,
+           inv_pos, topk_w, (const bf16*)add, ld_add, (bf16*)out, ldo, T, k, H);
 }
 
 }  // namespace sp

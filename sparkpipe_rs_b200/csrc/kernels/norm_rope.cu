@@ -17,44 +17,59 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "pdl.h"
 
 namespace sp {
 
 using bf16 = __nv_bfloat16;
 
-__global__ void add_rmsnorm_kernel(const bf16* __restrict__ x, long long ldx, bf16* __restrict__ res,
-                                   const bf16* __restrict__ w, bf16* __restrict__ out, long long ldo, int rows, int H,
-                                   float eps) {
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+// One CTA (256 threads) per row; the row stays in registers (hidden <= 8192).
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(const bf16* __restrict__ x, long long ldx,
+                                                          bf16* __restrict__ res, const bf16* __restrict__ w,
+                                                          bf16* __restrict__ out, long long ldo, int rows, int H,
+                                                          float eps) {
+  griddep_wait();
+  griddep_launch();
+  const int row = blockIdx.x;
   const bf16* xr = x + (long long)row * ldx;
   bf16* rr = res ? res + (long long)row * H : nullptr;
+  float v[4][8];
   float ss = 0.f;
-  for (int c = lane * 8; c < H; c += 256) {
-    float v[8];
-    ld_bf16x8(xr + c, v);
-    if (rr) {
-      float r[8];
-      ld_bf16x8(rr + c, r);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j] + r[j]));
-      st_bf16x8(rr + c, v);
+  for (int i = 0; i < 4; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c < H) {
+      ld_bf16x8(xr + c, v[i]);
+      if (rr) {
+        float r[8];
+        ld_bf16x8(rr + c, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j] + r[j]));
+        st_bf16x8(rr + c, v[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
     }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
   }
+  __shared__ float part[8];
   ss = warp_sum(ss);
-  const float inv = rsqrtf(ss / H + eps);
-  const bf16* src = rr ? rr : xr;
-  bf16* orow = out + (long long)row * ldo;
-  for (int c = lane * 8; c < H; c += 256) {
-    float v[8], g[8];
-    ld_bf16x8(src + c, v);
-    ld_bf16x8(w + c, g);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = v[j] * inv * g[j];
-    st_bf16x8(orow + c, v);
+  for (int i = 0; i < 8; ++i) tot += part[i];
+  const float inv = rsqrtf(tot / H + eps);
+  bf16* orow = out + (long long)row * ldo;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c < H) {
+      float g[8];
+      ld_bf16x8(w + c, g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = v[i][j] * inv * g[j];
+      st_bf16x8(orow + c, v[i]);
+    }
   }
 }
 
@@ -62,15 +77,17 @@ void add_rmsnorm(const void* x, long long ldx, void* residual, const void* w, vo
                  int hidden, float eps, cudaStream_t s) {
   if (rows <= 0) return;
   if (hidden % 8 != 0 || ldx % 8 != 0 || ldo % 8 != 0) throw std::runtime_error("add_rmsnorm: hidden/pitch % 8");
-  const int warps = 8;
-  add_rmsnorm_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, s>>>(
-      (const bf16*)x, ldx, (bf16*)residual, (const bf16*)w, (bf16*)out, ldo, rows, hidden, eps);
+  if (hidden > 8192) throw std::runtime_error("add_rmsnorm: hidden <= 8192");
+  launch_k(add_rmsnorm_kernel, dim3(rows), dim3(256), 0, s, (const bf16*)x, ldx, (bf16*)residual, (const bf16*)w,
+           (bf16*)out, ldo, rows, hidden, eps);
 }
 
 __global__ void mla_kv_write_kernel(const bf16* __restrict__ kv, long long ldkv, const bf16* __restrict__ nw,
                                     const int* __restrict__ pos, const float* __restrict__ cs,
                                     const int* __restrict__ slots, bf16* __restrict__ cache, bf16* __restrict__ lat,
                                     long long ldl, int T, int L, int R, float eps) {
+  griddep_wait();
+  griddep_launch();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -126,14 +143,16 @@ void mla_kv_write(const void* kv, long long ldkv, const void* norm_w, const int*
   if (T <= 0) return;
   if (kv_lora % 256 != 0 || kv_lora > 1024) throw std::runtime_error("mla_kv_write: kv_lora must be 256..1024");
   const int warps = 8;
-  mla_kv_write_kernel<<<(T + warps - 1) / warps, warps * 32, 0, s>>>(
-      (const bf16*)kv, ldkv, (const bf16*)norm_w, positions, cos_sin, slot_mapping, (bf16*)cache, (bf16*)latent_out,
-      ldl, T, kv_lora, rope, eps);
+  launch_k(mla_kv_write_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, s, (const bf16*)kv, ldkv,
+           (const bf16*)norm_w, positions, cos_sin, slot_mapping, (bf16*)cache, (bf16*)latent_out, ldl, T, kv_lora,
+           rope, eps);
 }
 
 __global__ void rope_q_kernel(const bf16* src, long long st, long long sh, int so, bf16* dst, long long dt,
                               long long dh, int doff, const int* __restrict__ pos, const float* __restrict__ cs, int T,
                               int H, int R) {
+  griddep_wait();
+  griddep_launch();
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (w >= T * H) return;
@@ -156,13 +175,14 @@ void rope_q(const void* src, long long src_tok, long long src_head, int src_off,
   if (T <= 0) return;
   const int warps = 8;
   const int n = T * H;
-  rope_q_kernel<<<(n + warps - 1) / warps, warps * 32, 0, s>>>((const bf16*)src, src_tok, src_head, src_off,
-                                                                (bf16*)dst, dst_tok, dst_head, dst_off, positions,
-                                                                cos_sin, T, H, rope);
+  launch_k(rope_q_kernel, dim3((n + warps - 1) / warps), dim3(warps * 32), 0, s, (const bf16*)src, src_tok, src_head,
+           src_off, (bf16*)dst, dst_tok, dst_head, dst_off, positions, cos_sin, T, H, rope);
 }
 
 __global__ void quant_fp8_block_kernel(const bf16* __restrict__ x, long long ldx, __nv_fp8_e4m3* __restrict__ q,
                                        float* __restrict__ scales, int rows, int cols) {
+  griddep_wait();
+  griddep_launch();
   const int nb = cols / 128;
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -188,8 +208,8 @@ void quant_fp8_block(const void* x, long long ldx, void* q, float* scales, int r
   if (cols % 128 != 0) throw std::runtime_error("quant_fp8_block: cols % 128");
   const int n = rows * (cols / 128);
   const int warps = 8;
-  quant_fp8_block_kernel<<<(n + warps - 1) / warps, warps * 32, 0, s>>>((const bf16*)x, ldx, (__nv_fp8_e4m3*)q,
-                                                                         scales, rows, cols);
+  launch_k(quant_fp8_block_kernel, dim3((n + warps - 1) / warps), dim3(warps * 32), 0, s, (const bf16*)x, ldx,
+           (__nv_fp8_e4m3*)q, scales, rows, cols);
 }
 
 }  // namespace sp

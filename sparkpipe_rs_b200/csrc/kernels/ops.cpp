@@ -69,7 +69,7 @@ void gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, int
           int64_t K, int64_t batch, int64_t a_row0, int64_t a_batch_rows, int64_t a_k0, int64_t a_batch_k,
           int64_t b_row0, int64_t b_batch_rows, int64_t b_k0, int64_t b_batch_k, int64_t trans_out, int64_t splits,
           int64_t block_n, const c10::optional<Tensor>& grp_rows, const c10::optional<Tensor>& grp_tiles,
-          int64_t num_groups, int64_t a_evict_first) {
+          int64_t num_groups, int64_t a_evict_first, int64_t swiglu) {
   CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D);
   CHECK_BF16(A); CHECK_BF16(B);
   TORCH_CHECK(D.scalar_type() == at::kBFloat16 || D.scalar_type() == at::kFloat, "D must be bf16 or fp32");
@@ -94,6 +94,7 @@ void gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, int
     g.num_groups = (int)num_groups;
   }
   g.a_evict_first = (int)a_evict_first;
+  g.swiglu = (int)swiglu;
   g.err = err_word();
   g.num_sms = num_sms();
   g.stream = stream();
@@ -203,21 +204,22 @@ void prefill_attention(const Tensor& q, const Tensor& k, const Tensor& kpe, cons
 }
 
 void moe_topk(const Tensor& logits, const c10::optional<Tensor>& bias, const Tensor& ids, const Tensor& w,
-              int64_t scoring, bool renorm, double scaling) {
+              int64_t n_shared, int64_t scoring, bool renorm, double scaling) {
   CHECK_CUDA(logits); CHECK_F32(logits); CHECK_CONTIG(logits); CHECK_I32(ids); CHECK_F32(w);
   const c10::cuda::CUDAGuard guard(logits.device());
   const float* b = nullptr;
   if (bias.has_value()) { CHECK_F32(*bias); b = bias->data_ptr<float>(); }
   sp::moe_topk(logits.data_ptr<float>(), b, ids.data_ptr<int>(), w.data_ptr<float>(), (int)logits.size(0),
-               (int)logits.size(1), (int)ids.size(1), (int)scoring, renorm ? 1 : 0, (float)scaling, 1, 1, stream());
+               (int)logits.size(1), (int)(ids.size(1) - n_shared), (int)n_shared, (int)scoring, renorm ? 1 : 0,
+               (float)scaling, 1, 1, stream());
 }
 
-void moe_align(const Tensor& topk_ids, int64_t num_experts, int64_t block_n, const Tensor& grp_rows,
+int64_t moe_align(const Tensor& topk_ids, int64_t num_experts, int64_t block_n, const Tensor& grp_rows,
                const Tensor& grp_tiles, const Tensor& sorted_tok, const Tensor& inv_pos, const Tensor& work) {
   CHECK_CUDA(topk_ids); CHECK_I32(topk_ids); CHECK_CONTIG(topk_ids);
   CHECK_I32(grp_rows); CHECK_I32(grp_tiles); CHECK_I32(sorted_tok); CHECK_I32(inv_pos); CHECK_I32(work);
   const c10::cuda::CUDAGuard guard(topk_ids.device());
-  sp::moe_align(topk_ids.data_ptr<int>(), (int)topk_ids.size(0), (int)topk_ids.size(1), (int)num_experts,
+  return sp::moe_align(topk_ids.data_ptr<int>(), (int)topk_ids.size(0), (int)topk_ids.size(1), (int)num_experts,
                 (int)block_n, grp_rows.data_ptr<int>(), grp_tiles.data_ptr<int>(), sorted_tok.data_ptr<int>(),
                 inv_pos.data_ptr<int>(), work.data_ptr<int>(), stream());
 }

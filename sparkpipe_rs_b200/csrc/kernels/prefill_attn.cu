@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "pdl.h"
 #include "mma_sync.cuh"
 
 namespace sp {
@@ -49,6 +50,8 @@ SP_DEVI uint32_t chunk_addr(uint32_t base, int row, int chunk) {
 }  // namespace
 
 __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(const PrefillAttnLaunch p, float scale_log2) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t s0 = smem_u32(smem);
@@ -215,9 +218,7 @@ void prefill_attention(const PrefillAttnLaunch& l) {
     attr = true;
   }
   dim3 grid((l.max_q + QT - 1) / QT, l.H, l.B);
-  prefill_attn_kernel<<<grid, 128, SMEM, l.stream>>>(l, l.scale * 1.4426950408889634f);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) throw std::runtime_error(std::string("prefill_attention launch: ") + cudaGetErrorString(e));
+  launch_k(prefill_attn_kernel, grid, dim3(128), SMEM, l.stream, l, l.scale * 1.4426950408889634f);
 }
 
 }  // namespace sp

@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "pdl.h"
 
 namespace sp {
 
@@ -38,6 +39,8 @@ SP_DEVI float uniform01(uint64_t seed, uint64_t a, uint64_t b, uint64_t c) {
 
 __global__ void sample_kernel(const bf16* __restrict__ logits, long long ldl, int V, float temp, uint64_t seed,
                               uint64_t offset, int* __restrict__ out_ids, float* __restrict__ out_logit) {
+  griddep_wait();
+  griddep_launch();
   const int row = blockIdx.x;
   const bf16* lr = logits + (long long)row * ldl;
   float best = -INFINITY;
@@ -93,11 +96,14 @@ __global__ void sample_kernel(const bf16* __restrict__ logits, long long ldl, in
 void sample_tokens(const void* logits, long long ldl, int T, int V, float temperature, unsigned long long seed,
                    unsigned long long offset, int* out_ids, float* out_logit, cudaStream_t s) {
   if (T <= 0) return;
-  sample_kernel<<<T, 1024, 0, s>>>((const bf16*)logits, ldl, V, temperature, seed, offset, out_ids, out_logit);
+  launch_k(sample_kernel, dim3(T), dim3(1024), 0, s, (const bf16*)logits, ldl, V, temperature, (uint64_t)seed,
+           (uint64_t)offset, out_ids, out_logit);
 }
 
 __global__ void embedding_kernel(const bf16* __restrict__ table, long long ld, const int* __restrict__ ids,
                                  bf16* __restrict__ out, long long ldo, int T, int H) {
+  griddep_wait();
+  griddep_launch();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -111,13 +117,15 @@ void embedding(const void* table, long long ld, const int* ids, void* out, long 
   if (T <= 0) return;
   if (H % 8 || ld % 8 || ldo % 8) throw std::runtime_error("embedding: 16-byte rows required");
   const int warps = 8;
-  embedding_kernel<<<(T + warps - 1) / warps, warps * 32, 0, s>>>((const bf16*)table, ld, ids, (bf16*)out, ldo, T,
-                                                                   H);
+  launch_k(embedding_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, s, (const bf16*)table, ld, ids,
+           (bf16*)out, ldo, T, H);
 }
 
 __global__ void spec_verify_kernel(const int* __restrict__ draft, const int* __restrict__ target, int B, int L,
                                    float p_accept, uint64_t seed, uint64_t offset, int* __restrict__ accepted,
                                    int* __restrict__ committed) {
+  griddep_wait();
+  griddep_launch();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   int a = 0;
@@ -141,8 +149,8 @@ __global__ void spec_verify_kernel(const int* __restrict__ draft, const int* __r
 void spec_verify(const int* draft, const int* target, int B, int L, float forced_accept_p, unsigned long long seed,
                  unsigned long long offset, int* accepted, int* committed, cudaStream_t s) {
   if (B <= 0) return;
-  spec_verify_kernel<<<(B + 127) / 128, 128, 0, s>>>(draft, target, B, L, forced_accept_p, seed, offset, accepted,
-                                                      committed);
+  launch_k(spec_verify_kernel, dim3((B + 127) / 128), dim3(128), 0, s, draft, target, B, L, forced_accept_p,
+           (uint64_t)seed, (uint64_t)offset, accepted, committed);
 }
 
 // Feeds a decode step's sampled tokens back as the next step's inputs: token id,
@@ -152,6 +160,8 @@ void spec_verify(const int* draft, const int* target, int B, int L, float forced
 __global__ void decode_advance_kernel(const int* __restrict__ out_ids, int* __restrict__ ids, int* __restrict__ pos,
                                       int* __restrict__ ctx, int* __restrict__ slots,
                                       const int* __restrict__ block_table, int max_blocks, int B, int block_size) {
+  griddep_wait();
+  griddep_launch();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B || ctx[b] == 0) return;
   ids[b] = out_ids[b];
@@ -165,8 +175,8 @@ __global__ void decode_advance_kernel(const int* __restrict__ out_ids, int* __re
 void decode_advance(const int* out_ids, int* ids, int* pos, int* ctx, int* slots, const int* block_table,
                     int max_blocks, int B, int block_size, cudaStream_t s) {
   if (B <= 0) return;
-  decode_advance_kernel<<<(B + 127) / 128, 128, 0, s>>>(out_ids, ids, pos, ctx, slots, block_table, max_blocks, B,
-                                                         block_size);
+  launch_k(decode_advance_kernel, dim3((B + 127) / 128), dim3(128), 0, s, out_ids, ids, pos, ctx, slots, block_table,
+           max_blocks, B, block_size);
 }
 
 }  // namespace sp

@@ -88,8 +88,8 @@ class MLAMoEConfig:
         for i in range(L):
             total += att
             if self.is_moe_layer(i):
-                total += self.n_routed_experts * 3 * H * self.moe_intermediate_size
-                total += 3 * H * self.shared_intermediate + self.n_routed_experts * H
+                total += (self.n_routed_experts + self.n_shared_experts) * 3 * H * self.moe_intermediate_size
+                total += self.n_routed_experts * H
             else:
                 total += 3 * H * self.intermediate_size
         return total

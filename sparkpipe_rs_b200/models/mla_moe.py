@@ -83,6 +83,12 @@ class MLAMoEModel:
             weights = init_weights(cfg, seed=seed, device=self.device, dtype=torch.bfloat16)
         self.w = {k: v.to(self.device) for k, v in weights.items()}
         derive_decode_weights(cfg, self.w)
+        # routed + shared expert gate/up weights in the fused-SwiGLU tile order
+        self.fused_swiglu = cfg.moe_intermediate_size % 64 == 0
+        for i in range(cfg.num_layers):
+            k = f"l{i}.e_w13"
+            if k in self.w and self.fused_swiglu:
+                self.w[k] = ops.interleave_gate_up(self.w[k])
         maxp = max_positions or min(cfg.max_position_embeddings, 1 << 17)
         self.cos_sin = cos_sin_table(cfg, maxp, device=self.device)
         self.scale = cfg.softmax_scale()
@@ -156,24 +162,26 @@ class MLAMoEModel:
         if not c.is_moe_layer(i):
             return ops.linear(ops.silu_mul(ops.linear(xn, w[p + "w13"])), w[p + "w2"])
         T = xn.shape[0]
-        E, k, F = c.n_routed_experts, c.num_experts_per_tok, c.moe_intermediate_size
+        E, k, F, S = c.n_routed_experts, c.num_experts_per_tok, c.moe_intermediate_size, c.n_shared_experts
         logits = ops.linear(xn, w[p + "gate"], out_dtype=torch.float32)
         sigmoid = c.scoring_func == "sigmoid"
         ids, wts = ops.moe_topk(logits, w[p + "gate_bias"] if sigmoid else None, k, 1 if sigmoid else 0,
-                                c.norm_topk_prob, c.routed_scaling_factor)
-        bn = _moe_block_n(T * k, E)
-        grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E, bn)
+                                c.norm_topk_prob, c.routed_scaling_factor, n_shared=S)
+        kk = k + S
+        bn = _moe_block_n(T * kk, E + S)
+        grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E + S, bn)
         xs = ops.gather_rows(xn, sorted_tok)
-        h13 = torch.empty(T * k, 2 * F, dtype=torch.bfloat16, device=self.device)
-        ops.grouped_gemm(w[p + "e_w13"], xs, h13, grp_rows, grp_tiles, E, bn)
-        act = ops.silu_mul(h13)
-        y = torch.empty(T * k, c.hidden_size, dtype=torch.bfloat16, device=self.device)
-        ops.grouped_gemm(w[p + "e_w2"], act, y, grp_rows, grp_tiles, E, bn)
-        shared = None
-        if c.n_shared_experts:
-            shared = ops.linear(ops.silu_mul(ops.linear(xn, w[p + "s_w13"])), w[p + "s_w2"])
+        if self.fused_swiglu:
+            act = torch.empty(T * kk, F, dtype=torch.bfloat16, device=self.device)
+            ops.grouped_gemm(w[p + "e_w13"], xs, act, grp_rows, grp_tiles, E + S, bn, swiglu=True)
+        else:
+            h13 = torch.empty(T * kk, 2 * F, dtype=torch.bfloat16, device=self.device)
+            ops.grouped_gemm(w[p + "e_w13"], xs, h13, grp_rows, grp_tiles, E + S, bn)
+            act = ops.silu_mul(h13)
+        y = torch.empty(T * kk, c.hidden_size, dtype=torch.bfloat16, device=self.device)
+        ops.grouped_gemm(w[p + "e_w2"], act, y, grp_rows, grp_tiles, E + S, bn)
         out = torch.empty(T, c.hidden_size, dtype=torch.bfloat16, device=self.device)
-        ops.moe_combine(y, inv_pos, wts, shared, out, k)
+        ops.moe_combine(y, inv_pos, wts, None, out, kk)
         return out
 
     # ------------------------------------------------------------------ forward

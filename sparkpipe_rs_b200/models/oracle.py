@@ -40,9 +40,11 @@ def swiglu_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor) -> torch.Te
 
 
 def moe(cfg: MLAMoEConfig, W: dict, p: str, x: torch.Tensor, routing=None) -> torch.Tensor:
+    """Routed experts 0..E-1 (top-k) plus the shared experts E..E+S-1 on every token."""
     ids, w, _ = route(cfg, x, W[p + "gate"], W.get(p + "gate_bias")) if routing is None else routing
     out = torch.zeros_like(x, dtype=torch.float32)
-    for e in range(cfg.n_routed_experts):
+    E = cfg.n_routed_experts
+    for e in range(E):
         mask = ids == e
         rows = mask.any(-1).nonzero().flatten()
         if rows.numel() == 0:
@@ -50,8 +52,8 @@ def moe(cfg: MLAMoEConfig, W: dict, p: str, x: torch.Tensor, routing=None) -> to
         we = (w * mask).sum(-1)[rows]
         y = swiglu_mlp(x[rows].float(), W[p + "e_w13"][e], W[p + "e_w2"][e])
         out[rows] += we[:, None] * y
-    if cfg.n_shared_experts:
-        out += swiglu_mlp(x.float(), W[p + "s_w13"], W[p + "s_w2"])
+    for s in range(cfg.n_shared_experts):
+        out += swiglu_mlp(x.float(), W[p + "e_w13"][E + s], W[p + "e_w2"][E + s])
     return out
 
 

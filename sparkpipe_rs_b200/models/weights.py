@@ -7,10 +7,13 @@ layout of the tcgen05 GEMM. Per layer ``i`` (prefix ``l{i}.``):
   kv_a fused into one GEMM) · q_a_norm [q_lora] · w_q_b [Hh*(dn+dr), q_lora] ·
   kv_a_norm [kv_lora] · w_kv_b [Hh*(dn+dv), kv_lora] · w_o [H, Hh*dv] ·
   post_norm [H] · dense: w13 [2I, H], w2 [H, I] · MoE: gate [E, H],
-  gate_bias [E] (fp32), e_w13 [E, 2F, H], e_w2 [E, H, F], s_w13 [2Fs, H], s_w2 [H, Fs]
+  gate_bias [E] (fp32), e_w13 [E + S, 2F, H], e_w2 [E + S, H, F]
 
 plus ``embed`` [V, H], ``final_norm`` [H] and ``lm_head`` [V, H]. ``w13`` stacks
-the gate projection rows on top of the up projection rows.
+the gate projection rows on top of the up projection rows. Experts E .. E+S-1
+are the S shared experts (each of width F; together they are the shared MLP of
+width S*F, which decomposes exactly into per-expert SwiGLU blocks), so routed
+and shared experts run in one grouped GEMM.
 
 Values are N(0, init_std) (norm weights 1, router bias 0), drawn per tensor from
 a generator seeded with (seed, tensor index), so any subset of layers or any
@@ -43,12 +46,9 @@ def weight_shapes(cfg: MLAMoEConfig) -> dict[str, tuple]:
             E, F = cfg.n_routed_experts, cfg.moe_intermediate_size
             shapes[p + "gate"] = (E, H)
             shapes[p + "gate_bias"] = (E,)
-            shapes[p + "e_w13"] = (E, 2 * F, H)
-            shapes[p + "e_w2"] = (E, H, F)
-            if cfg.n_shared_experts:
-                Fs = cfg.shared_intermediate
-                shapes[p + "s_w13"] = (2 * Fs, H)
-                shapes[p + "s_w2"] = (H, Fs)
+            S = cfg.n_shared_experts
+            shapes[p + "e_w13"] = (E + S, 2 * F, H)
+            shapes[p + "e_w2"] = (E + S, H, F)
         else:
             shapes[p + "w13"] = (2 * cfg.intermediate_size, H)
             shapes[p + "w2"] = (H, cfg.intermediate_size)

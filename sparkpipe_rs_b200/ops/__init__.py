@@ -18,6 +18,7 @@ __all__ = [
     "gemm",
     "batched_gemm",
     "grouped_gemm",
+    "interleave_gate_up",
     "add_rmsnorm",
     "mla_kv_write",
     "rope_q",
@@ -75,7 +76,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, d: torch.Tensor, *, M: int, N: int, K
          batch: int = 1, a_row0: int = 0, a_batch_rows: int = 0, a_k0: int = 0, a_batch_k: int = 0,
          b_row0: int = 0, b_batch_rows: int = 0, b_k0: int = 0, b_batch_k: int = 0, ldd: int | None = None,
          d_batch_stride: int = 0, splits: int = 0, block_n: int = 0, grp_rows=None, grp_tiles=None,
-         num_groups: int = 0, a_evict_first: bool = False) -> torch.Tensor:
+         num_groups: int = 0, a_evict_first: bool = False, swiglu: bool = False) -> torch.Tensor:
     """Raw tcgen05 GEMM: D[m, n] = sum_k A[m, k] B[n, k] (see gemm_tcgen05.cu)."""
     ar, ac, lda = _rows_cols_ld(a)
     br, bc, ldb = _rows_cols_ld(b)
@@ -83,7 +84,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, d: torch.Tensor, *, M: int, N: int, K
         ldd = d.stride(0)
     kernels().gemm(a, b, d, ar, ac, lda, br, bc, ldb, ldd, d_batch_stride, M, N, K, batch, a_row0, a_batch_rows,
                    a_k0, a_batch_k, b_row0, b_batch_rows, b_k0, b_batch_k, int(trans_out), splits, block_n,
-                   grp_rows, grp_tiles, num_groups, int(a_evict_first))
+                   grp_rows, grp_tiles, num_groups, int(a_evict_first), int(swiglu))
     _count(1)
     return d
 
@@ -113,10 +114,12 @@ def batched_gemm(a, b, d, *, M, N, K, batch, a_row0=0, a_batch_rows=0, a_k0=0, a
 
 
 def grouped_gemm(w: torch.Tensor, x_sorted: torch.Tensor, out: torch.Tensor, grp_rows: torch.Tensor,
-                 grp_tiles: torch.Tensor, num_groups: int, block_n: int) -> torch.Tensor:
+                 grp_tiles: torch.Tensor, num_groups: int, block_n: int, swiglu: bool = False) -> torch.Tensor:
     """MoE expert GEMM: out[r] = W[g(r)] @ x_sorted[r] for rows r sorted by group.
 
-    w is [G, M, K] (or its [G*M, K] view), x_sorted [R, K], out [R, M].
+    w is [G, M, K] (or its [G*M, K] view), x_sorted [R, K], out [R, M]. With
+    swiglu, w holds per 128-row tile 64 gate rows then the 64 matching up rows
+    (see ``interleave_gate_up``) and out [R, M/2] receives silu(gate) * up.
     """
     if w.dim() == 3:
         G, M, K = w.shape
@@ -126,8 +129,17 @@ def grouped_gemm(w: torch.Tensor, x_sorted: torch.Tensor, out: torch.Tensor, grp
         M = w.shape[0] // num_groups
         K = w.shape[1]
     gemm(w2, x_sorted, out, M=M, N=x_sorted.shape[0], K=K, trans_out=True, a_batch_rows=M, block_n=block_n,
-         grp_rows=grp_rows, grp_tiles=grp_tiles, num_groups=num_groups, a_evict_first=True)
+         grp_rows=grp_rows, grp_tiles=grp_tiles, num_groups=num_groups, a_evict_first=True, swiglu=swiglu)
     return out
+
+
+def interleave_gate_up(w13: torch.Tensor) -> torch.Tensor:
+    """[..., 2F, K] stacked [gate; up] -> per 128-row tile [64 gate rows; 64 up rows] (F % 64 == 0)."""
+    *lead, two_f, K = w13.shape
+    F = two_f // 2
+    assert F % 64 == 0, "fused SwiGLU needs the FFN width to be a multiple of 64"
+    v = w13.reshape(*lead, 2, F // 64, 64, K).transpose(-4, -3)
+    return v.reshape(*lead, two_f, K).contiguous()
 
 
 def add_rmsnorm(x, residual, w, out, eps):
@@ -179,11 +191,12 @@ def prefill_attention(q, k, kpe, v, o, cu_q, cu_k, max_q, scale, causal=True):
     return o
 
 
-def moe_topk(logits, bias, k, scoring, renorm, scaling):
+def moe_topk(logits, bias, k, scoring, renorm, scaling, n_shared=0):
+    """Top-k routing; the last n_shared columns are the shared experts E.. (weight 1)."""
     T = logits.shape[0]
-    ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
-    w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
-    kernels().moe_topk(logits, bias, ids, w, int(scoring), bool(renorm), float(scaling))
+    ids = torch.empty(T, k + n_shared, dtype=torch.int32, device=logits.device)
+    w = torch.empty(T, k + n_shared, dtype=torch.float32, device=logits.device)
+    kernels().moe_topk(logits, bias, ids, w, int(n_shared), int(scoring), bool(renorm), float(scaling))
     _count(1)
     return ids, w
 
@@ -196,8 +209,7 @@ def moe_align(topk_ids, num_experts, block_n):
     sorted_tok = torch.empty(n, dtype=torch.int32, device=dev)
     inv_pos = torch.empty(n, dtype=torch.int32, device=dev)
     work = torch.empty(num_experts, dtype=torch.int32, device=dev)
-    kernels().moe_align(topk_ids, num_experts, block_n, grp_rows, grp_tiles, sorted_tok, inv_pos, work)
-    _count(3)
+    _count(kernels().moe_align(topk_ids, num_experts, block_n, grp_rows, grp_tiles, sorted_tok, inv_pos, work))
     return grp_rows, grp_tiles, sorted_tok, inv_pos
 
 

@@ -24,6 +24,7 @@ def main():
     ap.add_argument("--ctx", type=int, default=1024)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = model default)")
+    ap.add_argument("--no-trace", action="store_true", help="run the steps without the profiler (for ncu)")
     args = ap.parse_args()
 
     from sparkpipe_rs_b200.models.config import get_config
@@ -47,6 +48,12 @@ def main():
     for _ in range(2):
         dg.run()
     torch.cuda.synchronize()
+    if args.no_trace:
+        for _ in range(args.steps):
+            dg.run()
+        torch.cuda.synchronize()
+        print("ran", args.steps, "decode steps")
+        return
     from torch.profiler import ProfilerActivity, profile
 
     with profile(activities=[ProfilerActivity.CUDA]) as prof:

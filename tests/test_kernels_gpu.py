@@ -122,6 +122,29 @@ def test_grouped_gemm_moe(T, E, k, bn):
     _status_ok()
 
 
+@pytest.mark.parametrize("T,E,k,bn", [(64, 66, 8, 16), (700, 18, 5, 128)])
+def test_grouped_gemm_fused_swiglu(T, E, k, bn):
+    ops = _ops()
+    H, F = 512, 192
+    g = torch.Generator(device=DEV).manual_seed(T * 3 + E)
+    x = torch.randn(T, H, device=DEV, generator=g).bfloat16()
+    ids = torch.stack([torch.randperm(E, device=DEV, generator=g)[:k] for _ in range(T)]).int()
+    w13 = (torch.randn(E, 2 * F, H, device=DEV, generator=g) * 0.05).bfloat16()
+    grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E, bn)
+    xs = ops.gather_rows(x, sorted_tok)
+    act = torch.empty(T * k, F, device=DEV, dtype=torch.bfloat16)
+    ops.grouped_gemm(ops.interleave_gate_up(w13), xs, act, grp_rows, grp_tiles, E, bn, swiglu=True)
+    rows = grp_rows.cpu().tolist()
+    ref = torch.empty(T * k, F, device=DEV)
+    for e in range(E):
+        r0, r1 = rows[e], rows[e + 1]
+        if r1 > r0:
+            h = xs[r0:r1].float() @ w13[e].float().t()
+            ref[r0:r1] = torch.nn.functional.silu(h[:, :F]) * h[:, F:]
+    _close(act, ref)
+    _status_ok()
+
+
 # ------------------------------------------------------------------ norms / rope
 @pytest.mark.parametrize("rows,H", [(1, 2048), (64, 2048), (300, 7168), (17, 512)])
 def test_add_rmsnorm(rows, H):
@@ -256,7 +279,10 @@ def test_moe_topk(scoring, renorm, E, k):
     g = torch.Generator(device=DEV).manual_seed(E)
     logits = torch.randn(T, E, device=DEV, generator=g)
     bias = torch.randn(E, device=DEV, generator=g) * 0.1 if scoring == 1 else None
-    ids, w = ops.moe_topk(logits, bias, k, scoring, renorm, 2.5)
+    ids, w = ops.moe_topk(logits, bias, k, scoring, renorm, 2.5, n_shared=2)
+    assert torch.equal(ids[:, k:].cpu(), torch.tensor([[E, E + 1]] * T, dtype=torch.int32))
+    assert torch.equal(w[:, k:].cpu(), torch.ones(T, 2))
+    ids, w = ids[:, :k].contiguous(), w[:, :k].contiguous()
     if scoring == 0:
         sc = logits.softmax(-1)
         sel = sc
