@@ -1,0 +1,174 @@
+// Continuous-batching scheduler of the serving engine.
+//
+// Owns every request's slot state and its KV blocks (through the prefix
+// cache), and turns the live set into one step plan per engine iteration:
+// either a prefill step (chunked, prefix-cache aware, several prompts packed
+// into one variable-length batch) or a decode step (all ready sequences, padded
+// to a CUDA-graph batch bucket). The plan carries every host array the GPU
+// step needs (token ids, positions, cache slots, cu_seqlens, block tables,
+// context lengths), laid out for one pinned host->device copy each.
+//
+// Slot states and configuration / decision flag names follow the reference's
+// request API and scheduler (crates/spark-serve/src/request_api/slot.rs:9-248,
+// crates/spark-sched/src/scheduler.rs:73-170); the policy (prefill-first with
+// an interleave cap, chunked prefill under a token budget, recompute preemption
+// when KV blocks run out) is this engine's own single-box design.
+#pragma once
+
+#include <cstdint>
+#include <deque>
+#include <memory>
+#include <unordered_map>
+#include <vector>
+
+#include "common.h"
+#include "prefix_cache.h"
+
+namespace spc {
+
+enum class SlotState : uint32_t {
+  Free = 0,
+  QueuedPrefill = 1,
+  RunningPrefill = 2,
+  ReadyDecode = 3,
+  RunningDecode = 4,
+  Completed = 5,
+  Cancelled = 6,
+  WaitingPrefixCohort = 7,
+  ReadySpeculativeVerify = 8,
+  RunningSpeculativeVerify = 9,
+};
+
+// configuration flags
+constexpr uint32_t kSchedChunkedPrefill = 0x01;
+constexpr uint32_t kSchedPrefixCache = 0x02;
+constexpr uint32_t kSchedCudaGraphPadding = 0x04;
+constexpr uint32_t kSchedPrefillDecodeInterleave = 0x08;
+constexpr uint32_t kSchedKvCacheRequired = 0x10;
+constexpr uint32_t kSchedCrossSequencePrefixReuse = 0x40;
+constexpr uint32_t kSchedDefaultFlags = kSchedChunkedPrefill | kSchedPrefixCache | kSchedCudaGraphPadding |
+                                        kSchedPrefillDecodeInterleave | kSchedKvCacheRequired |
+                                        kSchedCrossSequencePrefixReuse;
+// decision flags
+constexpr uint32_t kDecisionPrefillChunk = 0x001;
+constexpr uint32_t kDecisionPrefillFinalChunk = 0x002;
+constexpr uint32_t kDecisionPrefixCacheUsed = 0x004;
+constexpr uint32_t kDecisionCudaGraphPadding = 0x008;
+constexpr uint32_t kDecisionDecodeStep = 0x010;
+constexpr uint32_t kDecisionPrefillStep = 0x020;
+constexpr uint32_t kDecisionPreempted = 0x800;
+
+// finish reasons
+enum class FinishReason : uint32_t { None = 0, Length = 1, Stop = 2, Cancelled = 3, ContextLimit = 4, Error = 5 };
+
+struct SchedulerConfig {
+  uint32_t max_batch = 64;            // concurrently decoding sequences
+  uint32_t max_prefill_tokens = 16384;  // token budget of one prefill step
+  uint32_t max_prefill_seqs = 256;
+  uint32_t block_tokens = 64;
+  uint32_t num_blocks = 1024;
+  uint32_t max_model_len = 8192;
+  uint32_t max_sequences = 4096;      // admitted + queued
+  uint32_t flags = kSchedDefaultFlags;
+  uint32_t max_consecutive_prefills = 4;  // interleave cap while decodes wait
+  std::vector<uint32_t> decode_buckets = {1, 2, 4, 8, 16, 32, 64, 128, 256};
+};
+
+struct RequestSpec {
+  uint64_t id = 0;
+  std::vector<uint32_t> prompt;
+  uint32_t max_new_tokens = 16;
+  uint32_t priority = 1000000;        // higher runs first; ties by arrival
+  std::vector<uint32_t> stop_token_ids;
+  bool ignore_eos = false;
+};
+
+struct StepPlan {
+  enum Kind : uint32_t { None = 0, Prefill = 1, Decode = 2 };
+  uint32_t kind = None;
+  uint32_t flags = 0;
+  uint32_t num_seqs = 0;      // real sequences
+  uint32_t padded_seqs = 0;   // decode: CUDA-graph bucket size
+  uint32_t num_tokens = 0;
+  uint64_t step_index = 0;
+  std::vector<uint64_t> seq_ids;
+  std::vector<int32_t> token_ids, positions, slot_mapping;
+  // prefill
+  std::vector<int32_t> cu_q, cu_k, ctx_slots, logits_idx, chunk_lens;
+  std::vector<uint8_t> emits_token;
+  uint32_t max_q = 0;
+  bool has_prefix = false;    // some sequence attends to previously cached tokens
+  uint32_t cached_prefix_tokens = 0;
+  // decode
+  std::vector<int32_t> block_table, context_lens;
+  uint32_t max_blocks = 0;
+  uint32_t max_context = 0;
+};
+
+struct SchedEvent {
+  enum Kind : uint32_t { Token = 1, Finished = 2, Preempted = 3, PrefillProgress = 4 };
+  uint32_t kind;
+  uint64_t id;
+  int32_t token;
+  uint32_t reason;  // FinishReason for Finished
+  uint32_t value;   // computed prompt tokens for PrefillProgress, generated count for Token
+};
+
+struct SchedulerStats {
+  uint64_t steps = 0, prefill_steps = 0, decode_steps = 0, preemptions = 0;
+  uint64_t prefill_tokens = 0, decode_tokens = 0, cached_prompt_tokens = 0;
+  uint64_t admitted = 0, finished = 0, cancelled = 0, rejected = 0;
+};
+
+class Scheduler {
+ public:
+  explicit Scheduler(const SchedulerConfig& cfg);
+  void add_request(const RequestSpec& spec);
+  StepPlan schedule();
+  std::vector<SchedEvent> complete(const StepPlan& plan, const int32_t* sampled, uint32_t n_sampled);
+  bool cancel(uint64_t id);  // false when unknown / already finished
+  void fail_step(const StepPlan& plan);  // a dispatched step failed: cancel its sequences
+
+  bool has_work() const { return !waiting_.empty() || running_count_ > 0; }
+  uint32_t waiting_count() const { return (uint32_t)waiting_.size(); }
+  uint32_t running_count() const { return running_count_; }
+  SlotState state(uint64_t id) const;
+  std::vector<uint32_t> output_tokens(uint64_t id) const;
+  uint32_t bucket_for(uint32_t n) const;
+  const SchedulerConfig& config() const { return cfg_; }
+  const SchedulerStats& stats() const { return stats_; }
+  const PrefixCache& prefix_cache() const { return *cache_; }
+  uint32_t max_blocks_per_seq() const { return max_blocks_; }
+
+ private:
+  struct Req {
+    RequestSpec spec;
+    std::vector<uint32_t> tokens;  // prompt + generated
+    uint32_t prompt_len = 0;       // may grow on preemption (recompute the generated tail)
+    uint32_t computed = 0;         // tokens with KV in the cache
+    uint32_t generated = 0;
+    SlotState state = SlotState::QueuedPrefill;
+    bool reserved = false;
+    uint64_t arrival = 0;
+    FinishReason reason = FinishReason::None;
+  };
+  StepPlan build_prefill();
+  StepPlan build_decode();
+  void preempt_one(uint64_t keep);
+  void finish(Req& r, uint64_t id, FinishReason why, std::vector<SchedEvent>& ev);
+  int32_t slot_of(const Req& r, uint64_t id, uint32_t pos) const;
+
+  SchedulerConfig cfg_;
+  std::unique_ptr<PrefixCache> cache_;
+  std::unordered_map<uint64_t, Req> reqs_;
+  std::deque<uint64_t> waiting_;   // queued for (more) prefill, in admission order
+  std::vector<uint64_t> running_;  // ready to decode, in admission order
+  uint32_t running_count_ = 0;
+  uint32_t consecutive_prefills_ = 0;
+  uint32_t max_blocks_;
+  uint64_t arrival_clock_ = 0;
+  uint64_t step_clock_ = 0;
+  SchedulerStats stats_;
+};
+
+}  // namespace spc

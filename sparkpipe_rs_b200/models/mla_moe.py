@@ -51,12 +51,14 @@ class KVCache:
     """Paged latent KV cache: [layers, num_blocks * block_size, kv_lora + rope] bf16."""
 
     def __init__(self, cfg: MLAMoEConfig, num_blocks: int, block_size: int = 64, device="cuda",
-                 layers: int | None = None):
+                 layers: int | None = None, dtype: torch.dtype | None = None):
         self.block_size = block_size
         self.num_blocks = num_blocks
         self.num_layers = layers if layers is not None else cfg.num_layers
-        self.data = torch.zeros(self.num_layers, num_blocks * block_size, cfg.kv_cache_dim, dtype=torch.bfloat16,
-                                device=device)
+        dev = torch.device(device)
+        if dtype is None:
+            dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
+        self.data = torch.zeros(self.num_layers, num_blocks * block_size, cfg.kv_cache_dim, dtype=dtype, device=dev)
 
     def layer(self, i: int) -> torch.Tensor:
         return self.data[i]
@@ -93,6 +95,7 @@ class MLAMoEModel:
         self.cos_sin = cos_sin_table(cfg, maxp, device=self.device)
         self.scale = cfg.softmax_scale()
         self.qa_dim = cfg.q_lora_rank or cfg.q_out_dim
+        self._layer_offset = 0
 
     # ------------------------------------------------------------------ pieces
     def _q_view(self, q2d: torch.Tensor, T: int) -> torch.Tensor:
@@ -118,7 +121,7 @@ class MLAMoEModel:
         T = xn.shape[0]
         nh, dn, dv, kvl = c.num_heads, c.qk_nope_head_dim, c.v_head_dim, c.kv_lora_rank
         q, kv_a = self._project(i, xn)
-        layer_cache = cache.layer(i)
+        layer_cache = cache.layer(i - self._layer_offset)
         ops.mla_kv_write(kv_a, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache, None,
                          kvl, c.qk_rope_head_dim, c.rms_norm_eps)
         q_lat = torch.empty(T, nh, c.kv_cache_dim, dtype=torch.bfloat16, device=self.device)
@@ -141,7 +144,7 @@ class MLAMoEModel:
         T = xn.shape[0]
         nh, dn, dv, kvl, dr = c.num_heads, c.qk_nope_head_dim, c.v_head_dim, c.kv_lora_rank, c.qk_rope_head_dim
         q, kv_a = self._project(i, xn)
-        layer_cache = cache.layer(i)
+        layer_cache = cache.layer(i - self._layer_offset)
         lat = torch.empty(T, c.kv_cache_dim, dtype=torch.bfloat16, device=self.device)
         ops.mla_kv_write(kv_a, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache, lat,
                          kvl, dr, c.rms_norm_eps)
@@ -186,9 +189,11 @@ class MLAMoEModel:
 
     # ------------------------------------------------------------------ forward
     def forward(self, fb: ForwardBatch, cache: KVCache, layers: range | None = None,
-                hidden_in: torch.Tensor | None = None, return_hidden: bool = False):
+                hidden_in: torch.Tensor | None = None, return_hidden: bool = False, layer_offset: int = 0):
         """Runs `layers` (default: all) and returns logits [n, V] (bf16) of the rows in
-        fb.logits_idx, or the residual stream when return_hidden (pipeline stages)."""
+        fb.logits_idx, or the residual stream when return_hidden (pipeline stages).
+        Model layer i uses cache layer i - layer_offset (a stage caches only its layers)."""
+        self._layer_offset = layer_offset
         c, w = self.cfg, self.w
         T = fb.token_ids.shape[0]
         layers = layers if layers is not None else range(c.num_layers)
