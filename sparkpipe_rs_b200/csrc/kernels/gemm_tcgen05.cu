@@ -9,9 +9,14 @@
 //                    per-head MLA absorb products) offset A rows, A/B K columns
 //                    and D per batch index.
 //   * MODE_SPLITK  — decode-shaped GEMMs (few tokens, weight-bandwidth bound):
-//                    the K loop of one tile is split over the CTAs of a
-//                    thread-block cluster; partial accumulators are reduced
-//                    through distributed shared memory (no global workspace).
+//                    the K loop of one tile is split over `splits` independent
+//                    CTAs with a short (4-stage) pipeline, so two fit per SM and
+//                    the next kernel's CTAs can start early under PDL. Every CTA
+//                    adds its fp32 partial into a per-tile accumulator with
+//                    red.global.add (the reduction happens in L2, in parallel);
+//                    the CTA that arrives last at the tile's counter converts
+//                    the tile to the output and zeroes accumulator and counter
+//                    for the next launch.
 //   * MODE_GROUPED — MoE expert GEMMs: group g (an expert) owns A rows
 //                    [g*M, g*M+M) and a device-side range of B rows (its sorted
 //                    tokens); tile counts come from device memory, so the launch
@@ -57,20 +62,22 @@ struct GemmKParams {
   int num_groups;
   int a_evict_first;  // A is a weight operand: stream it with evict_first and prefetch it before the PDL wait
   int swiglu;         // grouped: A rows are [64 gate | 64 up] per tile; write silu(gate) * up
+  float* ws;          // split-K accumulators [tiles][BN][128] fp32 (zero between launches)
+  int* counters;      // split-K per-tile arrival counters (zero between launches)
   int* err;
 };
 
 constexpr int BM = 128;
 constexpr int BK = 64;
 
-template <int BN>
+template <int BN, int MODE>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+  // split-K CTAs own only a few K blocks: a short pipeline keeps two CTAs per SM
+  static constexpr int STAGES = MODE == MODE_SPLITK ? 4 : (BN >= 256 ? 4 : (BN >= 128 ? 6 : 8));
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int RED_LD = BN + 4;  // fp32 row pitch of the split-K reduce buffer
   static constexpr int XBUF_BYTES = 64 * 17 * 4;  // SwiGLU exchange buffer (64 rows x 16 cols, padded)
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + XBUF_BYTES;
 };
@@ -166,7 +173,7 @@ template <int BN, int MODE>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const GemmKParams p) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, MODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
@@ -176,6 +183,7 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* s_ntiles = s_err + 1;
+  volatile int* s_last = s_ntiles + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -221,15 +229,15 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int num_tiles = *s_ntiles;
 
-  // Split-K: one tile per cluster; this CTA owns a slice of the K blocks.
+  // Split-K: CTA (tile, ks) owns K-block slice ks of exactly one tile.
   int kb_begin = 0, kb_end = (p.K + BK - 1) / BK;
   int tile_first = blockIdx.x, tile_step = gridDim.x;
-  uint32_t crank = 0;
+  int ks = 0;
   if (MODE == MODE_SPLITK) {
-    crank = cluster_ctarank();
+    ks = blockIdx.x % p.splits;
     const int total_kb = kb_end;
-    kb_begin = (int)((long long)total_kb * crank / p.splits);
-    kb_end = (int)((long long)total_kb * (crank + 1) / p.splits);
+    kb_begin = (int)((long long)total_kb * ks / p.splits);
+    kb_end = (int)((long long)total_kb * (ks + 1) / p.splits);
     tile_first = blockIdx.x / p.splits;
     tile_step = 1 << 30;  // exactly one tile
   }
@@ -364,56 +372,55 @@ __global__ void __launch_bounds__(192, 1)
         ++tc;
       }
     } else {
-      // Split-K: park this CTA's fp32 partial tile in shared memory.
-      float* red = reinterpret_cast<float*>(smem);
-      if (mbar_wait(&tfull[0], 0, s_err, p.err, kErrWaitTimeoutEpilogue)) {
+      // Split-K: add this CTA's fp32 partial into the tile accumulator (column
+      // major: the 32 lanes of a warp hit 128 contiguous bytes per column).
+      const int tile = tile_first;
+      float* acc = p.ws + (size_t)tile * BN * BM;
+      TileInfo ti;
+      get_tile<BN, MODE>(p, tile, ti);
+      const bool ok = mbar_wait(&tfull[0], 0, s_err, p.err, kErrWaitTimeoutEpilogue);
+      if (ok) {
         tc_fence_after();
-        for (int c0 = 0; c0 < BN; c0 += 16) {
+        for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
           float v[16];
           tmem_ld16(lane_addr + c0, v);
-          float4* dst = reinterpret_cast<float4*>(red + m * C::RED_LD + c0);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          for (int j = 0; j < 16; ++j) atomicAdd(acc + (c0 + j) * BM + m, v[j]);
         }
         tc_fence_before();
       }
-    }
-  }
-
-  if (MODE == MODE_SPLITK) {
-    // Cluster-wide reduction of the partial tiles through DSMEM. Every thread of
-    // every CTA in the cluster takes both cluster barriers, error or not.
-    cluster_sync();
-    TileInfo ti;
-    get_tile<BN, MODE>(p, tile_first, ti);
-    const int rows = BM / p.splits;
-    const int r0 = crank * rows;
-    const uint32_t red_addr = smem_u32(smem);
-    const int n4 = BN / 4;
-    if (*s_err == 0) {
-      for (int idx = threadIdx.x; idx < rows * n4; idx += blockDim.x) {
-        int mm, nn;
-        if (p.trans_out) { mm = r0 + idx % rows; nn = (idx / rows) * 4; }
-        else { mm = r0 + idx / n4; nn = (idx % n4) * 4; }
-        if (mm >= ti.m_valid || nn >= ti.n_valid) continue;
-        const uint32_t off = uint32_t((mm * C::RED_LD + nn) * 4);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int s = 0; s < p.splits; ++s) {
-          const float4 v = ld_dsmem_f32x4(mapa_shared(red_addr + off, s));
-          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (warp == 2 && lane == 0) {
+        int last = 0;
+        if (ok && *s_err == 0) last = atomicAdd(p.counters + tile, 1) == p.splits - 1;
+        *s_last = last;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*s_last) {
+        __threadfence();
+        const int t = threadIdx.x - 64;  // 0..127
+        for (int it = t; it < BN * (BM / 4); it += 128) {
+          const int c = it / (BM / 4), m4 = (it % (BM / 4)) * 4;
+          if (c >= ti.n_valid) continue;
+          float4* ap = reinterpret_cast<float4*>(acc + c * BM + m4);
+          const float4 v = __ldcg(ap);
+          __stcg(ap, make_float4(0.f, 0.f, 0.f, 0.f));
+          const float vv[4] = {v.x, v.y, v.z, v.w};
+          const long long ng = ti.n_base + c;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (m4 + j >= ti.m_valid) break;
+            const long long mg = ti.m_base + m4 + j;
+            const long long di = p.trans_out ? ng * p.ldd + mg : mg * p.ldd + ng;
+            if (p.out_f32) reinterpret_cast<float*>(p.D)[ti.d_off + di] = vv[j];
+            else reinterpret_cast<__nv_bfloat16*>(p.D)[ti.d_off + di] = __float2bfloat16_rn(vv[j]);
+          }
         }
-        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-        const long long mg = ti.m_base + mm;
-        for (int j = 0; j < 4; ++j) {
-          if (nn + j >= ti.n_valid) break;
-          const long long ng = ti.n_base + nn + j;
-          const long long di = p.trans_out ? ng * p.ldd + mg : mg * p.ldd + ng;
-          if (p.out_f32) reinterpret_cast<float*>(p.D)[ti.d_off + di] = a4[j];
-          else reinterpret_cast<__nv_bfloat16*>(p.D)[ti.d_off + di] = __float2bfloat16_rn(a4[j]);
-        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (warp == 2 && lane == 0) p.counters[tile] = 0;  // ready for the next launch
       }
     }
-    cluster_sync();
   }
 
   __syncthreads();
@@ -460,7 +467,7 @@ void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int
 
 template <int BN, int MODE>
 static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, MODE>;
   CUtensorMap ta, tb;
   make_tmap_2d(&ta, g.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.a_rows, g.a_cols, g.lda, BM, BK);
   make_tmap_2d(&tb, g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.b_rows, g.b_cols, g.ldb, BN, BK);
@@ -468,7 +475,6 @@ static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (MODE == MODE_SPLITK) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -477,14 +483,9 @@ static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = g.stream;
   if (MODE == MODE_SPLITK) {
-    if (C::STAGES * C::STAGE_BYTES < BM * C::RED_LD * 4) throw std::runtime_error("split-K reduce buffer too big");
     cfg.gridDim = dim3(p.num_tiles * p.splits, 1, 1);
-    attrs[0].id = cudaLaunchAttributeClusterDimension;
-    attrs[0].val.clusterDim.x = p.splits;
-    attrs[0].val.clusterDim.y = 1;
-    attrs[0].val.clusterDim.z = 1;
     cfg.attrs = attrs;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 0;
   } else {
     int grid = MODE == MODE_GROUPED ? g.num_sms : std::min(p.num_tiles, g.num_sms);
     if (grid < 1) grid = 1;
@@ -563,12 +564,16 @@ void gemm_bf16(const GemmLaunch& g) {
   int splits = g.splits;
   const int kbs = (g.K + BK - 1) / BK;
   if (splits <= 0) {
-    // Auto: split K over a cluster when the tile grid leaves most SMs idle.
+    // Auto: split K when the tile grid leaves SMs idle; two split CTAs fit per SM.
     splits = 1;
-    while (splits < 8 && p.num_tiles * splits * 2 <= g.num_sms && kbs / (splits * 2) >= 4) splits *= 2;
+    while (splits < 8 && p.num_tiles * splits * 2 <= 2 * g.num_sms && kbs / (splits * 2) >= 2) splits *= 2;
   }
-  if (splits > 1 && bn > 128) splits = 1;  // reduce buffer must fit the stage memory
-  if (splits > kbs) splits = kbs;          // every CTA of the cluster needs at least one K block
+  if (splits > kbs) splits = kbs;  // every split CTA needs at least one K block
+  if (splits > 1 && (!g.ws || !g.counters || (long long)p.num_tiles * bn * BM > g.ws_floats ||
+                     p.num_tiles > g.num_counters))
+    splits = 1;  // workspace too small: run unsplit
+  p.ws = g.ws;
+  p.counters = g.counters;
   p.splits = splits;
   if (splits > 1) dispatch_bn<MODE_SPLITK>(bn, g, p);
   else dispatch_bn<MODE_DENSE>(bn, g, p);

@@ -29,6 +29,10 @@ struct GemmLaunch {
   int num_groups = 0;
   int a_evict_first = 0;
   int swiglu = 0;  // grouped only: fused silu(gate) * up epilogue, output [rows, M / 2]
+  float* ws = nullptr;        // split-K partial workspace (fp32)
+  long long ws_floats = 0;
+  int* counters = nullptr;    // split-K per-tile counters, all zero between launches
+  int num_counters = 0;
   int* err = nullptr;
   int num_sms = 148;
   cudaStream_t stream = 0;

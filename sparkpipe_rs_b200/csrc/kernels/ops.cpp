@@ -27,6 +27,32 @@ std::mutex g_mu;
 std::unordered_map<int, int*> g_err;
 std::unordered_map<int, int> g_sms;
 
+// Per-device split-K workspace: fp32 tile accumulators and per-tile arrival
+// counters (both start at zero; each split-K launch leaves them at zero again,
+// so split-K GEMMs must be stream-ordered on a device, which PDL preserves).
+constexpr long long kSplitWsFloats = 8ll << 20;  // 32 MiB
+constexpr int kSplitCounters = 1 << 16;
+struct SplitWs {
+  float* ws = nullptr;
+  int* counters = nullptr;
+};
+std::unordered_map<int, SplitWs> g_split;
+
+SplitWs split_ws() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_split.find(dev);
+  if (it != g_split.end()) return it->second;
+  SplitWs w;
+  TORCH_CHECK(cudaMalloc(&w.ws, sizeof(float) * kSplitWsFloats) == cudaSuccess, "split-K workspace allocation");
+  TORCH_CHECK(cudaMalloc(&w.counters, sizeof(int) * kSplitCounters) == cudaSuccess, "split-K counter allocation");
+  TORCH_CHECK(cudaMemset(w.counters, 0, sizeof(int) * kSplitCounters) == cudaSuccess, "split-K counter clear");
+  TORCH_CHECK(cudaMemset(w.ws, 0, sizeof(float) * kSplitWsFloats) == cudaSuccess, "split-K accumulator clear");
+  g_split[dev] = w;
+  return w;
+}
+
 int* err_word() {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -95,6 +121,13 @@ void gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, int
   }
   g.a_evict_first = (int)a_evict_first;
   g.swiglu = (int)swiglu;
+  if (!grp_rows.has_value() && splits != 1) {
+    const SplitWs w = split_ws();
+    g.ws = w.ws;
+    g.ws_floats = kSplitWsFloats;
+    g.counters = w.counters;
+    g.num_counters = kSplitCounters;
+  }
   g.err = err_word();
   g.num_sms = num_sms();
   g.stream = stream();
