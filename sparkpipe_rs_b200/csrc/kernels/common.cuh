@@ -5,11 +5,13 @@
 // mbarriers with *bounded* waits, tcgen05 MMA / TMEM allocation / TMEM loads,
 // and thread-block-cluster shared-memory access (DSMEM).
 //
-// Bounded waits: every spin on an mbarrier gives up after kWaitBudgetNs of
-// %globaltimer time (or as soon as another role of the same CTA has flagged an
-// error in shared memory), records an error code and returns false. Callers
-// then skip the remaining work, still free their TMEM and return, so a lost
-// signal ends the kernel with a status word instead of hanging the GPU.
+// Bounded waits: every spin on an mbarrier gives up after kWaitBudgetCycles of
+// the SM-local clock64 counter (about two seconds; or as soon as another role of
+// the same CTA has flagged an error in shared memory), records an error code
+// and returns false. Callers then skip the remaining work, still free their
+// TMEM and return, so a lost signal ends the kernel with a status word instead
+// of hanging the GPU. (clock64 rather than %globaltimer: the global timer is a
+// slow register read, and waits sit on every pipeline stage's critical path.)
 #pragma once
 
 #include <cuda.h>
@@ -31,7 +33,7 @@ enum : int {
   kErrBadIndex = 5,
 };
 
-constexpr unsigned long long kWaitBudgetNs = 2000000000ull;  // 2 s
+constexpr long long kWaitBudgetCycles = 4000000000ll;  // ~2 s at 2 GHz
 
 SP_DEVI uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -77,13 +79,13 @@ SP_DEVI bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // global status word `gerr`) with `code` when the time budget runs out.
 SP_DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* cta_err, int* gerr, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const long long t0 = clock64();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*cta_err != 0) return false;
-    if (globaltimer() - t0 > kWaitBudgetNs) {
+    if (clock64() - t0 > kWaitBudgetCycles) {
       *cta_err = code;
       if (gerr) atomicCAS(gerr, 0, code);
       return false;

@@ -62,7 +62,7 @@ struct GemmKParams {
   int num_groups;
   int a_evict_first;  // A is a weight operand: stream it with evict_first and prefetch it before the PDL wait
   int swiglu;         // grouped: A rows are [64 gate | 64 up] per tile; write silu(gate) * up
-  float* ws;          // split-K accumulators [tiles][BN][128] fp32 (zero between launches)
+  float* ws;          // split-K accumulators [tiles][128][BN] fp32 (zero between launches)
   int* counters;      // split-K per-tile arrival counters (zero between launches)
   int* err;
 };
@@ -372,8 +372,8 @@ __global__ void __launch_bounds__(192, 1)
         ++tc;
       }
     } else {
-      // Split-K: add this CTA's fp32 partial into the tile accumulator (column
-      // major: the 32 lanes of a warp hit 128 contiguous bytes per column).
+      // Split-K: add this CTA's fp32 partial into the tile accumulator
+      // ([128 rows][BN] row major) with 16-byte vector atomics.
       const int tile = tile_first;
       float* acc = p.ws + (size_t)tile * BN * BM;
       TileInfo ti;
@@ -384,8 +384,9 @@ __global__ void __launch_bounds__(192, 1)
         for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
           float v[16];
           tmem_ld16(lane_addr + c0, v);
+          float4* dst = reinterpret_cast<float4*>(acc + m * BN + c0);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) atomicAdd(acc + (c0 + j) * BM + m, v[j]);
+          for (int j = 0; j < 4; ++j) atomicAdd(dst + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
         }
         tc_fence_before();
       }
@@ -400,18 +401,18 @@ __global__ void __launch_bounds__(192, 1)
       if (*s_last) {
         __threadfence();
         const int t = threadIdx.x - 64;  // 0..127
-        for (int it = t; it < BN * (BM / 4); it += 128) {
-          const int c = it / (BM / 4), m4 = (it % (BM / 4)) * 4;
-          if (c >= ti.n_valid) continue;
-          float4* ap = reinterpret_cast<float4*>(acc + c * BM + m4);
+        for (int it = t; it < BM * (BN / 4); it += 128) {
+          const int mm = it % BM, c4 = (it / BM) * 4;
+          if (c4 >= ti.n_valid || mm >= ti.m_valid) continue;
+          float4* ap = reinterpret_cast<float4*>(acc + mm * BN + c4);
           const float4 v = __ldcg(ap);
           __stcg(ap, make_float4(0.f, 0.f, 0.f, 0.f));
           const float vv[4] = {v.x, v.y, v.z, v.w};
-          const long long ng = ti.n_base + c;
+          const long long mg = ti.m_base + mm;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            if (m4 + j >= ti.m_valid) break;
-            const long long mg = ti.m_base + m4 + j;
+            if (c4 + j >= ti.n_valid) break;
+            const long long ng = ti.n_base + c4 + j;
             const long long di = p.trans_out ? ng * p.ldd + mg : mg * p.ldd + ng;
             if (p.out_f32) reinterpret_cast<float*>(p.D)[ti.d_off + di] = vv[j];
             else reinterpret_cast<__nv_bfloat16*>(p.D)[ti.d_off + di] = __float2bfloat16_rn(vv[j]);
@@ -475,6 +476,7 @@ static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};

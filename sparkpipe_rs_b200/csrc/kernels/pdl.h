@@ -6,8 +6,10 @@
 #include <cuda_runtime.h>
 
 #include <cstdlib>
+#include <mutex>
 #include <stdexcept>
 #include <string>
+#include <unordered_set>
 
 namespace sp {
 
@@ -20,8 +22,18 @@ inline bool pdl_enabled() {
   return on == 1;
 }
 
+// Every kernel asks for the maximum shared-memory carveout, so consecutive
+// kernels of a decode step never force an SM to reconfigure L1 / shared memory.
+inline void prefer_max_smem_carveout(const void* kern) {
+  static std::mutex mu;
+  static std::unordered_set<const void*> done;
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.insert(kern).second) cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+}
+
 template <typename... KArgs, typename... Args>
 inline void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  prefer_max_smem_carveout(reinterpret_cast<const void*>(kern));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
