@@ -11,12 +11,12 @@
 //   * MODE_SPLITK  — decode-shaped GEMMs (few tokens, weight-bandwidth bound):
 //                    the K loop of one tile is split over `splits` independent
 //                    CTAs with a short (4-stage) pipeline, so two fit per SM and
-//                    the next kernel's CTAs can start early under PDL. Every CTA
-//                    adds its fp32 partial into a per-tile accumulator with
-//                    red.global.add (the reduction happens in L2, in parallel);
-//                    the CTA that arrives last at the tile's counter converts
-//                    the tile to the output and zeroes accumulator and counter
-//                    for the next launch.
+//                    the next kernel's CTAs can start early under PDL. (One SM's
+//                    TMA stream tops out near 55 GB/s on these 128-byte rows, so
+//                    an HBM-bound GEMM needs >100 SMs streaming at once.) Each
+//                    CTA stores its fp32 partial with plain coalesced stores into
+//                    a workspace slab; a wide split_reduce kernel sums the slabs
+//                    into the output.
 //   * MODE_GROUPED — MoE expert GEMMs: group g (an expert) owns A rows
 //                    [g*M, g*M+M) and a device-side range of B rows (its sorted
 //                    tokens); tile counts come from device memory, so the launch
@@ -62,8 +62,8 @@ struct GemmKParams {
   int num_groups;
   int a_evict_first;  // A is a weight operand: stream it with evict_first and prefetch it before the PDL wait
   int swiglu;         // grouped: A rows are [64 gate | 64 up] per tile; write silu(gate) * up
-  float* ws;          // split-K accumulators [tiles][128][BN] fp32 (zero between launches)
-  int* counters;      // split-K per-tile arrival counters (zero between launches)
+  float* ws;          // split-K partial slabs: [splits][N][M] (trans_out) or [splits][M][N], fp32
+  long long split_stride;
   int* err;
 };
 
@@ -372,54 +372,23 @@ __global__ void __launch_bounds__(192, 1)
         ++tc;
       }
     } else {
-      // Split-K: add this CTA's fp32 partial into the tile accumulator
-      // ([128 rows][BN] row major) with 16-byte vector atomics.
-      const int tile = tile_first;
-      float* acc = p.ws + (size_t)tile * BN * BM;
+      // Split-K: this CTA's fp32 partial goes to its own slab of the workspace,
+      // in the output's (n, m) coordinates with a dense pitch.
       TileInfo ti;
-      get_tile<BN, MODE>(p, tile, ti);
-      const bool ok = mbar_wait(&tfull[0], 0, s_err, p.err, kErrWaitTimeoutEpilogue);
-      if (ok) {
+      get_tile<BN, MODE>(p, tile_first, ti);
+      GemmKParams q = p;
+      q.D = p.ws + (size_t)ks * p.split_stride;
+      q.out_f32 = 1;
+      q.ldd = p.trans_out ? p.M : p.N;
+      ti.d_off = 0;
+      if (mbar_wait(&tfull[0], 0, s_err, p.err, kErrWaitTimeoutEpilogue)) {
         tc_fence_after();
         for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
           float v[16];
           tmem_ld16(lane_addr + c0, v);
-          float4* dst = reinterpret_cast<float4*>(acc + m * BN + c0);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) atomicAdd(dst + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+          store_chunk<BN>(q, ti, m, c0, v);
         }
         tc_fence_before();
-      }
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (warp == 2 && lane == 0) {
-        int last = 0;
-        if (ok && *s_err == 0) last = atomicAdd(p.counters + tile, 1) == p.splits - 1;
-        *s_last = last;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (*s_last) {
-        __threadfence();
-        const int t = threadIdx.x - 64;  // 0..127
-        for (int it = t; it < BM * (BN / 4); it += 128) {
-          const int mm = it % BM, c4 = (it / BM) * 4;
-          if (c4 >= ti.n_valid || mm >= ti.m_valid) continue;
-          float4* ap = reinterpret_cast<float4*>(acc + mm * BN + c4);
-          const float4 v = __ldcg(ap);
-          __stcg(ap, make_float4(0.f, 0.f, 0.f, 0.f));
-          const float vv[4] = {v.x, v.y, v.z, v.w};
-          const long long mg = ti.m_base + mm;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (c4 + j >= ti.n_valid) break;
-            const long long ng = ti.n_base + c4 + j;
-            const long long di = p.trans_out ? ng * p.ldd + mg : mg * p.ldd + ng;
-            if (p.out_f32) reinterpret_cast<float*>(p.D)[ti.d_off + di] = vv[j];
-            else reinterpret_cast<__nv_bfloat16*>(p.D)[ti.d_off + di] = __float2bfloat16_rn(vv[j]);
-          }
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (warp == 2 && lane == 0) p.counters[tile] = 0;  // ready for the next launch
       }
     }
   }
@@ -428,6 +397,32 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<C::TMEM_COLS>(tmem_base);
+  }
+}
+
+// Sums the split-K slabs: out[r, c] = sum_s ws[s][r][c] for a [rows, cols]
+// dense slab layout; output pitch ldo (elements), bf16 or fp32.
+__global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restrict__ ws, long long stride,
+                                                           int splits, int rows, int cols, void* __restrict__ out,
+                                                           long long ldo, int out_f32) {
+  griddep_wait();
+  griddep_launch();
+  const int c4 = cols / 4;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)rows * c4) return;
+  const int r = int(i / c4), c = int(i % c4) * 4;
+  const float* src = ws + (long long)r * cols + c;
+  float4 acc = __ldcg(reinterpret_cast<const float4*>(src));
+  for (int s = 1; s < splits; ++s) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(src + s * stride));
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  if (out_f32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (long long)r * ldo + c) = acc;
+  } else {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + (long long)r * ldo + c;
+    *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(acc.x, acc.y);
+    *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z, acc.w);
   }
 }
 
@@ -532,8 +527,8 @@ static void check_k_window(long long cols, int k0, int batch_k, int K, int batch
     throw std::runtime_error("gemm: a K window inside a wider operand needs K % 64 == 0");
 }
 
-void gemm_bf16(const GemmLaunch& g) {
-  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return;
+int gemm_bf16(const GemmLaunch& g) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return 0;
   if (g.K % 8 != 0) throw std::runtime_error("gemm: K must be a multiple of 8");
   check_k_window(g.a_cols, g.a_k0, g.a_batch_k, g.K, g.grouped ? 1 : g.batch);
   check_k_window(g.b_cols, g.b_k0, g.b_batch_k, g.K, g.grouped ? 1 : g.batch);
@@ -558,7 +553,7 @@ void gemm_bf16(const GemmLaunch& g) {
     p.grp_tiles = g.grp_tiles;
     p.num_groups = g.num_groups;
     dispatch_bn<MODE_GROUPED>(bn, g, p);
-    return;
+    return 1;
   }
   const int bn = g.block_n > 0 ? g.block_n : pick_bn(g.N);
   p.n_tiles = (g.N + bn - 1) / bn;
@@ -566,19 +561,31 @@ void gemm_bf16(const GemmLaunch& g) {
   int splits = g.splits;
   const int kbs = (g.K + BK - 1) / BK;
   if (splits <= 0) {
-    // Auto: split K when the tile grid leaves SMs idle; two split CTAs fit per SM.
+    // Auto: split K until the grid covers the SMs (two split CTAs fit per SM).
     splits = 1;
     while (splits < 8 && p.num_tiles * splits * 2 <= 2 * g.num_sms && kbs / (splits * 2) >= 2) splits *= 2;
   }
   if (splits > kbs) splits = kbs;  // every split CTA needs at least one K block
-  if (splits > 1 && (!g.ws || !g.counters || (long long)p.num_tiles * bn * BM > g.ws_floats ||
-                     p.num_tiles > g.num_counters))
-    splits = 1;  // workspace too small: run unsplit
+  const long long slab = (long long)g.M * g.N;
+  // the slab reduction needs dense, 4-aligned rows and a workspace that fits
+  const int out_cols = g.trans_out ? g.M : g.N;
+  if (splits > 1 && (!g.ws || g.batch != 1 || slab * splits > g.ws_floats || out_cols % 4 != 0 ||
+                     g.ldd % 4 != 0 || (reinterpret_cast<uintptr_t>(g.D) & 15) != 0))
+    splits = 1;
   p.ws = g.ws;
-  p.counters = g.counters;
+  p.split_stride = slab;
   p.splits = splits;
-  if (splits > 1) dispatch_bn<MODE_SPLITK>(bn, g, p);
-  else dispatch_bn<MODE_DENSE>(bn, g, p);
+  if (splits > 1) {
+    dispatch_bn<MODE_SPLITK>(bn, g, p);
+    const int rows = g.trans_out ? g.N : g.M;
+    const int cols = g.trans_out ? g.M : g.N;
+    const long long n = (long long)rows * (cols / 4);
+    launch_k(split_reduce_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, g.stream, (const float*)g.ws,
+             slab, splits, rows, cols, g.D, g.ldd, g.out_f32);
+    return 2;
+  }
+  dispatch_bn<MODE_DENSE>(bn, g, p);
+  return 1;
 }
 
 }  // namespace sp

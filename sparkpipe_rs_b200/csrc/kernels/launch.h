@@ -29,15 +29,13 @@ struct GemmLaunch {
   int num_groups = 0;
   int a_evict_first = 0;
   int swiglu = 0;  // grouped only: fused silu(gate) * up epilogue, output [rows, M / 2]
-  float* ws = nullptr;        // split-K partial workspace (fp32)
+  float* ws = nullptr;        // split-K partial workspace (fp32 slabs)
   long long ws_floats = 0;
-  int* counters = nullptr;    // split-K per-tile counters, all zero between launches
-  int num_counters = 0;
   int* err = nullptr;
   int num_sms = 148;
   cudaStream_t stream = 0;
 };
-void gemm_bf16(const GemmLaunch& g);
+int gemm_bf16(const GemmLaunch& g);  // returns the number of kernels launched
 void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, long long rows,
                   long long cols, long long ld, int box_rows, int box_cols);
 

@@ -27,28 +27,20 @@ std::mutex g_mu;
 std::unordered_map<int, int*> g_err;
 std::unordered_map<int, int> g_sms;
 
-// Per-device split-K workspace: fp32 tile accumulators and per-tile arrival
-// counters (both start at zero; each split-K launch leaves them at zero again,
-// so split-K GEMMs must be stream-ordered on a device, which PDL preserves).
+// Per-device split-K workspace: the fp32 partial slabs of one split GEMM. Split
+// GEMMs on a device must be stream-ordered (PDL keeps that order: a kernel
+// writes its slabs only after its predecessor has finished).
 constexpr long long kSplitWsFloats = 8ll << 20;  // 32 MiB
-constexpr int kSplitCounters = 1 << 16;
-struct SplitWs {
-  float* ws = nullptr;
-  int* counters = nullptr;
-};
-std::unordered_map<int, SplitWs> g_split;
+std::unordered_map<int, float*> g_split;
 
-SplitWs split_ws() {
+float* split_ws() {
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lk(g_mu);
   auto it = g_split.find(dev);
   if (it != g_split.end()) return it->second;
-  SplitWs w;
-  TORCH_CHECK(cudaMalloc(&w.ws, sizeof(float) * kSplitWsFloats) == cudaSuccess, "split-K workspace allocation");
-  TORCH_CHECK(cudaMalloc(&w.counters, sizeof(int) * kSplitCounters) == cudaSuccess, "split-K counter allocation");
-  TORCH_CHECK(cudaMemset(w.counters, 0, sizeof(int) * kSplitCounters) == cudaSuccess, "split-K counter clear");
-  TORCH_CHECK(cudaMemset(w.ws, 0, sizeof(float) * kSplitWsFloats) == cudaSuccess, "split-K accumulator clear");
+  float* w = nullptr;
+  TORCH_CHECK(cudaMalloc(&w, sizeof(float) * kSplitWsFloats) == cudaSuccess, "split-K workspace allocation");
   g_split[dev] = w;
   return w;
 }
@@ -90,7 +82,7 @@ void clear_status() {
   TORCH_CHECK(cudaMemset(p, 0, sizeof(int)) == cudaSuccess, "status clear failed");
 }
 
-void gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, int64_t a_cols, int64_t lda,
+int64_t gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, int64_t a_cols, int64_t lda,
           int64_t b_rows, int64_t b_cols, int64_t ldb, int64_t ldd, int64_t d_batch_stride, int64_t M, int64_t N,
           int64_t K, int64_t batch, int64_t a_row0, int64_t a_batch_rows, int64_t a_k0, int64_t a_batch_k,
           int64_t b_row0, int64_t b_batch_rows, int64_t b_k0, int64_t b_batch_k, int64_t trans_out, int64_t splits,
@@ -122,16 +114,13 @@ void gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, int
   g.a_evict_first = (int)a_evict_first;
   g.swiglu = (int)swiglu;
   if (!grp_rows.has_value() && splits != 1) {
-    const SplitWs w = split_ws();
-    g.ws = w.ws;
+    g.ws = split_ws();
     g.ws_floats = kSplitWsFloats;
-    g.counters = w.counters;
-    g.num_counters = kSplitCounters;
   }
   g.err = err_word();
   g.num_sms = num_sms();
   g.stream = stream();
-  sp::gemm_bf16(g);
+  return sp::gemm_bf16(g);
 }
 
 void add_rmsnorm(const Tensor& x, const c10::optional<Tensor>& residual, const Tensor& w, const Tensor& out,

@@ -82,10 +82,9 @@ def gemm(a: torch.Tensor, b: torch.Tensor, d: torch.Tensor, *, M: int, N: int, K
     br, bc, ldb = _rows_cols_ld(b)
     if ldd is None:
         ldd = d.stride(0)
-    kernels().gemm(a, b, d, ar, ac, lda, br, bc, ldb, ldd, d_batch_stride, M, N, K, batch, a_row0, a_batch_rows,
-                   a_k0, a_batch_k, b_row0, b_batch_rows, b_k0, b_batch_k, int(trans_out), splits, block_n,
-                   grp_rows, grp_tiles, num_groups, int(a_evict_first), int(swiglu))
-    _count(1)
+    _count(kernels().gemm(a, b, d, ar, ac, lda, br, bc, ldb, ldd, d_batch_stride, M, N, K, batch, a_row0,
+                          a_batch_rows, a_k0, a_batch_k, b_row0, b_batch_rows, b_k0, b_batch_k, int(trans_out),
+                          splits, block_n, grp_rows, grp_tiles, num_groups, int(a_evict_first), int(swiglu)))
     return d
 
 
