@@ -570,13 +570,14 @@ int gemm_bf16(const GemmLaunch& g) {
   // the slab reduction needs dense, 4-aligned rows and a workspace that fits
   const int out_cols = g.trans_out ? g.M : g.N;
   if (splits > 1 && (!g.ws || g.batch != 1 || slab * splits > g.ws_floats || out_cols % 4 != 0 ||
-                     g.ldd % 4 != 0 || (reinterpret_cast<uintptr_t>(g.D) & 15) != 0))
+                     (!g.slab_out && (g.ldd % 4 != 0 || (reinterpret_cast<uintptr_t>(g.D) & 15) != 0))))
     splits = 1;
   p.ws = g.ws;
   p.split_stride = slab;
   p.splits = splits;
   if (splits > 1) {
     dispatch_bn<MODE_SPLITK>(bn, g, p);
+    if (g.slab_out) return -splits;  // the caller's next kernel sums the slabs itself
     const int rows = g.trans_out ? g.N : g.M;
     const int cols = g.trans_out ? g.M : g.N;
     const long long n = (long long)rows * (cols / 4);

@@ -31,11 +31,14 @@ struct GemmLaunch {
   int swiglu = 0;  // grouped only: fused silu(gate) * up epilogue, output [rows, M / 2]
   float* ws = nullptr;        // split-K partial workspace (fp32 slabs)
   long long ws_floats = 0;
+  int slab_out = 0;           // split-K: leave the partial slabs (dense [rows][cols] fp32) for the consumer
   int* err = nullptr;
   int num_sms = 148;
   cudaStream_t stream = 0;
 };
-int gemm_bf16(const GemmLaunch& g);  // returns the number of kernels launched
+// Returns the number of kernels launched, or -splits when the result was left as
+// `splits` fp32 slabs in g.ws (slab_out requested and K was split).
+int gemm_bf16(const GemmLaunch& g);
 void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, long long rows,
                   long long cols, long long ld, int box_rows, int box_cols);
 
@@ -43,6 +46,16 @@ void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int
 // residual (optional, in/out) += x; out = rmsnorm(residual or x) * w.
 void add_rmsnorm(const void* x, long long ldx, void* residual, const void* w, void* out, long long ldo, int rows,
                  int hidden, float eps, cudaStream_t s);
+// residual += sum of `splits` fp32 slabs ([rows, hidden] each, `stride` apart); out = rmsnorm(residual) * w
+void slab_add_rmsnorm(const float* slab, long long stride, int splits, void* residual, const void* w, void* out,
+                      long long ldo, int rows, int hidden, float eps, cudaStream_t s);
+// Decode prologue of MLA attention from the q/kv projection row (bf16 `src` with pitch lds, or fp32 split-K
+// slabs with row length row_len): cache <- [rmsnorm(latent), rope(k_pe)], q_nope_out [T, H, dn] <- q_nope,
+// q_lat[t, h, kv_lora:] <- rope(q_pe).
+void mla_decode_prep(const float* slab, long long stride, int splits, const void* src, long long lds,
+                     const void* norm_w, const int* positions, const float* cos_sin, const int* slot_mapping,
+                     void* cache, void* q_nope_out, void* q_lat, int T, int H, int dn, int dr, int kv_lora,
+                     int q_off, int kv_off, int row_len, float eps, cudaStream_t s);
 // kv: [T, kv_lora + rope] rows (pitch ldkv). Writes norm(latent)|rope(k_pe) into
 // cache rows slot_mapping[t] (pitch kv_lora+rope) and, if latent_out != null,
 // the same row into latent_out (pitch ldl).
@@ -95,8 +108,13 @@ void prefill_attention(const PrefillAttnLaunch& l);
 // scoring: 0 = softmax, 1 = sigmoid (+bias for selection). Weights are renormalised
 // over the selected experts when renorm != 0, then multiplied by `scaling`.
 // The last n_shared columns of topk_ids / topk_w are the shared experts E .. E+n_shared-1 (weight 1).
-void moe_topk(const float* logits, const float* bias, int* topk_ids, float* topk_w, int T, int E, int k, int n_shared,
-              int scoring, int renorm, float scaling, int n_group, int topk_group, cudaStream_t s);
+// `logits` may be split-K slabs: the logits are sum_s logits[s * slab_stride + ...] over `splits`.
+void moe_topk(const float* logits, long long slab_stride, int splits, const float* bias, int* topk_ids, float* topk_w,
+              int T, int E, int k, int n_shared, int scoring, int renorm, float scaling, int n_group, int topk_group,
+              cudaStream_t s);
+// res[t] += sum_j w[t, j] * y[inv_pos[t*k + j]]; out[t] = rmsnorm(res[t]) * gamma
+void combine_add_rmsnorm(const void* y, long long ldy, const int* inv_pos, const float* topk_w, void* residual,
+                         const void* gamma, void* out, long long ldo, int T, int k, int H, float eps, cudaStream_t s);
 // Builds the expert-sorted row layout: counts -> grp_rows [E+1], grp_tiles [E+1]
 // (n-tiles of width block_n), sorted_tok [T*k] (source token of each sorted row),
 // inv_pos [T*k] (sorted row of pair (t, j)). `work` is E ints of scratch.

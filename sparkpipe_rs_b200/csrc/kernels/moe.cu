@@ -32,9 +32,9 @@ using bf16 = __nv_bfloat16;
 
 constexpr int TOPK_MAX_PER_LANE = 16;  // E <= 512
 
-__global__ void moe_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
-                                int* __restrict__ ids, float* __restrict__ wts, int T, int E, int k, int n_shared,
-                                int scoring, int renorm, float scaling) {
+__global__ void moe_topk_kernel(const float* __restrict__ logits, long long slab_stride, int splits,
+                                const float* __restrict__ bias, int* __restrict__ ids, float* __restrict__ wts, int T,
+                                int E, int k, int n_shared, int scoring, int renorm, float scaling) {
   griddep_wait();
   griddep_launch();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -47,7 +47,13 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, const float* _
 #pragma unroll
   for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
     const int e = lane + i * 32;
-    score[i] = (i < per && e < E) ? row[e] : -INFINITY;
+    if (i < per && e < E) {
+      float x = __ldcg(row + e);
+      for (int s2 = 1; s2 < splits; ++s2) x += __ldcg(row + s2 * slab_stride + e);  // split-K slabs
+      score[i] = x;
+    } else {
+      score[i] = -INFINITY;
+    }
     mx = fmaxf(mx, score[i]);
   }
   if (scoring == 0) {
@@ -112,15 +118,16 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, const float* _
   }
 }
 
-void moe_topk(const float* logits, const float* bias, int* topk_ids, float* topk_w, int T, int E, int k, int n_shared,
-              int scoring, int renorm, float scaling, int n_group, int topk_group, cudaStream_t s) {
+void moe_topk(const float* logits, long long slab_stride, int splits, const float* bias, int* topk_ids, float* topk_w,
+              int T, int E, int k, int n_shared, int scoring, int renorm, float scaling, int n_group, int topk_group,
+              cudaStream_t s) {
   if (T <= 0) return;
   if (E > 32 * TOPK_MAX_PER_LANE) throw std::runtime_error("moe_topk: at most 512 experts");
   if (k + n_shared > 32) throw std::runtime_error("moe_topk: k + shared <= 32");
   if (n_group > 1 && topk_group < n_group) throw std::runtime_error("moe_topk: group-limited routing not supported");
   const int warps = 2;
-  launch_k(moe_topk_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, s, logits, bias, topk_ids, topk_w, T,
-           E, k, n_shared, scoring, renorm, scaling);
+  launch_k(moe_topk_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, s, logits, slab_stride,
+           splits < 1 ? 1 : splits, bias, topk_ids, topk_w, T, E, k, n_shared, scoring, renorm, scaling);
 }
 
 // ---------------------------------------------------------------- align
@@ -317,6 +324,77 @@ void moe_combine(const void* y, long long ldy, const int* inv_pos, const float* 
   const int threads = 128;
   launch_k(moe_combine_kernel, dim3(T, (H / 8 + threads - 1) / threads), dim3(threads), 0, s, (const bf16*)y, ldy,
            inv_pos, topk_w, (const bf16*)add, ld_add, (bf16*)out, ldo, T, k, H);
+}
+
+// MoE combine fused with the next residual add + RMSNorm: one CTA per token,
+//   res[t] += sum_j w[t, j] * y[inv_pos[t, j]];  out[t] = rmsnorm(res[t]) * gamma
+__global__ void __launch_bounds__(256) combine_add_rmsnorm_kernel(
+    const bf16* __restrict__ y, long long ldy, const int* __restrict__ inv_pos, const float* __restrict__ w,
+    bf16* __restrict__ res, const bf16* __restrict__ gamma, bf16* __restrict__ out, long long ldo, int k, int H,
+    float eps) {
+  griddep_wait();
+  griddep_launch();
+  const int t = blockIdx.x;
+  __shared__ int s_pos[COMBINE_MAXK];
+  __shared__ float s_w[COMBINE_MAXK];
+  __shared__ float part[8];
+  if (threadIdx.x < k) {
+    s_pos[threadIdx.x] = inv_pos[t * k + threadIdx.x];
+    s_w[threadIdx.x] = w[t * k + threadIdx.x];
+  }
+  __syncthreads();
+  bf16* rr = res + (long long)t * H;
+  float v[4][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c < H) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < k; ++j) {
+        float yv[8];
+        ld_bf16x8(y + (long long)s_pos[j] * ldy + c, yv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += s_w[j] * yv[e];
+      }
+      float r[8];
+      ld_bf16x8(rr + c, r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        v[i][e] = __bfloat162float(__float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(acc[e])) + r[e]));
+      st_bf16x8(rr + c, v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += part[i];
+  const float inv = rsqrtf(tot / H + eps);
+  bf16* orow = out + (long long)t * ldo;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c < H) {
+      float g[8];
+      ld_bf16x8(gamma + c, g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = v[i][e] * inv * g[e];
+      st_bf16x8(orow + c, v[i]);
+    }
+  }
+}
+
+void combine_add_rmsnorm(const void* y, long long ldy, const int* inv_pos, const float* topk_w, void* residual,
+                         const void* gamma, void* out, long long ldo, int T, int k, int H, float eps, cudaStream_t s) {
+  if (T <= 0) return;
+  if (k > COMBINE_MAXK) throw std::runtime_error("combine_add_rmsnorm: k <= 32");
+  if (H % 8 || H > 8192) throw std::runtime_error("combine_add_rmsnorm: hidden % 8, <= 8192");
+  launch_k(combine_add_rmsnorm_kernel, dim3(T), dim3(256), 0, s, (const bf16*)y, ldy, inv_pos, topk_w,
+           (bf16*)residual, (const bf16*)gamma, (bf16*)out, ldo, k, H, eps);
 }
 
 }  // namespace sp

@@ -82,6 +82,150 @@ void add_rmsnorm(const void* x, long long ldx, void* residual, const void* w, vo
            (bf16*)out, ldo, rows, hidden, eps);
 }
 
+// Residual add + RMSNorm whose input is the sum of `splits` fp32 split-K slabs
+// (x[t] = sum_s slab[s][t]): the split reduction of the producing GEMM fused
+// into its consumer. One CTA (256 threads) per row, hidden <= 8192.
+__global__ void __launch_bounds__(256) slab_add_rmsnorm_kernel(const float* __restrict__ slab, long long stride,
+                                                               int splits, bf16* __restrict__ res,
+                                                               const bf16* __restrict__ w, bf16* __restrict__ out,
+                                                               long long ldo, int H, float eps) {
+  griddep_wait();
+  griddep_launch();
+  const int row = blockIdx.x;
+  bf16* rr = res + (long long)row * H;
+  float v[4][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c < H) {
+      const float* src = slab + (long long)row * H + c;
+      float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+      float4 b = __ldcg(reinterpret_cast<const float4*>(src + 4));
+      for (int s2 = 1; s2 < splits; ++s2) {
+        const float4 a2 = __ldcg(reinterpret_cast<const float4*>(src + s2 * stride));
+        const float4 b2 = __ldcg(reinterpret_cast<const float4*>(src + s2 * stride + 4));
+        a.x += a2.x; a.y += a2.y; a.z += a2.z; a.w += a2.w;
+        b.x += b2.x; b.y += b2.y; b.z += b2.z; b.w += b2.w;
+      }
+      // the GEMM output is rounded to bf16 before the residual add, as in the unfused path
+      const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      float r[8];
+      ld_bf16x8(rr + c, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[i][j] = __bfloat162float(__float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(x[j])) + r[j]));
+      st_bf16x8(rr + c, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  __shared__ float part[8];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += part[i];
+  const float inv = rsqrtf(tot / H + eps);
+  bf16* orow = out + (long long)row * ldo;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c < H) {
+      float g[8];
+      ld_bf16x8(w + c, g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = v[i][j] * inv * g[j];
+      st_bf16x8(orow + c, v[i]);
+    }
+  }
+}
+
+void slab_add_rmsnorm(const float* slab, long long stride, int splits, void* residual, const void* w, void* out,
+                      long long ldo, int rows, int hidden, float eps, cudaStream_t s) {
+  if (rows <= 0) return;
+  if (hidden % 8 != 0 || hidden > 8192) throw std::runtime_error("slab_add_rmsnorm: hidden % 8, <= 8192");
+  launch_k(slab_add_rmsnorm_kernel, dim3(rows), dim3(256), 0, s, slab, stride, splits, (bf16*)residual,
+           (const bf16*)w, (bf16*)out, ldo, hidden, eps);
+}
+
+// Decode prologue of MLA attention, one CTA (8 warps) per token. The token's
+// q/kv projection row is either bf16 (`src`) or the sum of fp32 split-K slabs.
+//   warp 0        : latent RMSNorm + RoPE on the rope key -> paged cache slot
+//   all warps     : per head, q_nope -> q_nope_out[t, h, :] (bf16, compact) and
+//                   RoPE(q_pe) -> q_lat[t, h, kv_lora:]
+__global__ void __launch_bounds__(256) mla_decode_prep_kernel(
+    const float* __restrict__ slab, long long stride, int splits, const bf16* __restrict__ src, long long lds,
+    const bf16* __restrict__ nw, const int* __restrict__ pos, const float* __restrict__ cs,
+    const int* __restrict__ slots, bf16* __restrict__ cache, bf16* __restrict__ q_nope_out,
+    bf16* __restrict__ q_lat, int H, int dn, int dr, int L, int qoff, int kvoff, int row_len, float eps) {
+  griddep_wait();
+  griddep_launch();
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto val = [&](int c) -> float {
+    if (slab) {
+      const float* p = slab + (long long)t * row_len + c;
+      float a = __ldcg(p);
+      for (int s2 = 1; s2 < splits; ++s2) a += __ldcg(p + s2 * stride);
+      return __bfloat162float(__float2bfloat16_rn(a));
+    }
+    return __bfloat162float(src[(long long)t * lds + c]);
+  };
+  const int p = pos[t];
+  const float* cp = cs + (long long)p * dr;
+  const int W = L + dr;
+  if (warp == 0) {
+    float v[32];
+    float ss = 0.f;
+    const int per = L / 32;  // <= 32
+    for (int i = 0; i < per; ++i) {
+      v[i] = val(kvoff + lane + i * 32);
+      ss += v[i] * v[i];
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / L + eps);
+    const int slot = slots[t];
+    if (slot >= 0) {
+      bf16* crow = cache + (long long)slot * W;
+      for (int i = 0; i < per; ++i) {
+        const int c = lane + i * 32;
+        crow[c] = __float2bfloat16_rn(v[i] * inv * __bfloat162float(nw[c]));
+      }
+      for (int i = lane; i < dr / 2; i += 32) {
+        const float x0 = val(kvoff + L + 2 * i), x1 = val(kvoff + L + 2 * i + 1);
+        const float c = cp[i], sn = cp[dr / 2 + i];
+        crow[L + 2 * i] = __float2bfloat16_rn(x0 * c - x1 * sn);
+        crow[L + 2 * i + 1] = __float2bfloat16_rn(x0 * sn + x1 * c);
+      }
+    }
+  }
+  for (int h = warp; h < H; h += 8) {
+    const int base = qoff + h * (dn + dr);
+    bf16* qn = q_nope_out + ((long long)t * H + h) * dn;
+    for (int c = lane; c < dn; c += 32) qn[c] = __float2bfloat16_rn(val(base + c));
+    bf16* ql = q_lat + ((long long)t * H + h) * W + L;
+    for (int i = lane; i < dr / 2; i += 32) {
+      const float x0 = val(base + dn + 2 * i), x1 = val(base + dn + 2 * i + 1);
+      const float c = cp[i], sn = cp[dr / 2 + i];
+      ql[2 * i] = __float2bfloat16_rn(x0 * c - x1 * sn);
+      ql[2 * i + 1] = __float2bfloat16_rn(x0 * sn + x1 * c);
+    }
+  }
+}
+
+void mla_decode_prep(const float* slab, long long stride, int splits, const void* src, long long lds,
+                     const void* norm_w, const int* positions, const float* cos_sin, const int* slot_mapping,
+                     void* cache, void* q_nope_out, void* q_lat, int T, int H, int dn, int dr, int kv_lora,
+                     int q_off, int kv_off, int row_len, float eps, cudaStream_t s) {
+  if (T <= 0) return;
+  if (kv_lora % 32 != 0 || kv_lora > 1024) throw std::runtime_error("mla_decode_prep: kv_lora % 32, <= 1024");
+  launch_k(mla_decode_prep_kernel, dim3(T), dim3(256), 0, s, slab, stride, splits, (const bf16*)src, lds,
+           (const bf16*)norm_w, positions, cos_sin, slot_mapping, (bf16*)cache, (bf16*)q_nope_out, (bf16*)q_lat, H,
+           dn, dr, kv_lora, q_off, kv_off, row_len, eps);
+}
+
 __global__ void mla_kv_write_kernel(const bf16* __restrict__ kv, long long ldkv, const bf16* __restrict__ nw,
                                     const int* __restrict__ pos, const float* __restrict__ cs,
                                     const int* __restrict__ slots, bf16* __restrict__ cache, bf16* __restrict__ lat,

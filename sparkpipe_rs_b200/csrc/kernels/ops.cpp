@@ -87,7 +87,7 @@ int64_t gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, 
           int64_t K, int64_t batch, int64_t a_row0, int64_t a_batch_rows, int64_t a_k0, int64_t a_batch_k,
           int64_t b_row0, int64_t b_batch_rows, int64_t b_k0, int64_t b_batch_k, int64_t trans_out, int64_t splits,
           int64_t block_n, const c10::optional<Tensor>& grp_rows, const c10::optional<Tensor>& grp_tiles,
-          int64_t num_groups, int64_t a_evict_first, int64_t swiglu) {
+          int64_t num_groups, int64_t a_evict_first, int64_t swiglu, int64_t slab_out) {
   CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D);
   CHECK_BF16(A); CHECK_BF16(B);
   TORCH_CHECK(D.scalar_type() == at::kBFloat16 || D.scalar_type() == at::kFloat, "D must be bf16 or fp32");
@@ -117,6 +117,7 @@ int64_t gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, 
     g.ws = split_ws();
     g.ws_floats = kSplitWsFloats;
   }
+  g.slab_out = (int)slab_out;
   g.err = err_word();
   g.num_sms = num_sms();
   g.stream = stream();
@@ -226,14 +227,63 @@ void prefill_attention(const Tensor& q, const Tensor& k, const Tensor& kpe, cons
 }
 
 void moe_topk(const Tensor& logits, const c10::optional<Tensor>& bias, const Tensor& ids, const Tensor& w,
-              int64_t n_shared, int64_t scoring, bool renorm, double scaling) {
+              int64_t n_shared, int64_t scoring, bool renorm, double scaling, int64_t T, int64_t E,
+              int64_t slab_stride, int64_t splits) {
+  // logits: [T, E] fp32, or the split-K workspace holding `splits` [T, E] slabs slab_stride apart
   CHECK_CUDA(logits); CHECK_F32(logits); CHECK_CONTIG(logits); CHECK_I32(ids); CHECK_F32(w);
   const c10::cuda::CUDAGuard guard(logits.device());
   const float* b = nullptr;
   if (bias.has_value()) { CHECK_F32(*bias); b = bias->data_ptr<float>(); }
-  sp::moe_topk(logits.data_ptr<float>(), b, ids.data_ptr<int>(), w.data_ptr<float>(), (int)logits.size(0),
-               (int)logits.size(1), (int)(ids.size(1) - n_shared), (int)n_shared, (int)scoring, renorm ? 1 : 0,
-               (float)scaling, 1, 1, stream());
+  sp::moe_topk(logits.data_ptr<float>(), slab_stride, (int)splits, b, ids.data_ptr<int>(), w.data_ptr<float>(), (int)T,
+               (int)E, (int)(ids.size(1) - n_shared), (int)n_shared, (int)scoring, renorm ? 1 : 0, (float)scaling, 1,
+               1, stream());
+}
+
+void slab_add_rmsnorm(const Tensor& slabs, int64_t stride, int64_t splits, const Tensor& residual, const Tensor& w,
+                      const Tensor& out, double eps) {
+  CHECK_CUDA(slabs); CHECK_F32(slabs); CHECK_BF16(residual); CHECK_CONTIG(residual); CHECK_BF16(w); CHECK_BF16(out);
+  const c10::cuda::CUDAGuard guard(slabs.device());
+  sp::slab_add_rmsnorm(slabs.data_ptr<float>(), stride, (int)splits, residual.data_ptr(), w.data_ptr(),
+                       out.data_ptr(), out.stride(0), (int)residual.size(0), (int)residual.size(1), (float)eps,
+                       stream());
+}
+
+void mla_decode_prep(const c10::optional<Tensor>& slabs, int64_t stride, int64_t splits,
+                     const c10::optional<Tensor>& src, const Tensor& norm_w, const Tensor& positions,
+                     const Tensor& cos_sin, const Tensor& slot_mapping, const Tensor& cache, const Tensor& q_nope_out,
+                     const Tensor& q_lat, int64_t T, int64_t dn, int64_t q_off, int64_t kv_off, int64_t row_len,
+                     double eps) {
+  CHECK_I32(positions); CHECK_F32(cos_sin); CHECK_I32(slot_mapping); CHECK_BF16(cache); CHECK_BF16(q_nope_out);
+  CHECK_BF16(q_lat); CHECK_CONTIG(q_nope_out); CHECK_CONTIG(q_lat);
+  const c10::cuda::CUDAGuard guard(q_lat.device());
+  const float* sl = nullptr;
+  const void* sr = nullptr;
+  long long lds = 0;
+  if (slabs.has_value()) { CHECK_F32(*slabs); sl = slabs->data_ptr<float>(); }
+  if (src.has_value()) { CHECK_BF16(*src); TORCH_CHECK(src->stride(1) == 1, "src rows"); sr = src->data_ptr(); lds = src->stride(0); }
+  TORCH_CHECK((sl != nullptr) != (sr != nullptr), "mla_decode_prep: exactly one of slabs / src");
+  const int H = (int)q_lat.size(1), W = (int)q_lat.size(2);
+  const int kvl = (int)norm_w.size(0);
+  sp::mla_decode_prep(sl, stride, (int)splits, sr, lds, norm_w.data_ptr(), positions.data_ptr<int>(),
+                      cos_sin.data_ptr<float>(), slot_mapping.data_ptr<int>(), cache.data_ptr(), q_nope_out.data_ptr(),
+                      q_lat.data_ptr(), (int)T, H, (int)dn, W - kvl, kvl, (int)q_off, (int)kv_off, (int)row_len,
+                      (float)eps, stream());
+}
+
+void combine_add_rmsnorm(const Tensor& y, const Tensor& inv_pos, const Tensor& w, const Tensor& residual,
+                         const Tensor& gamma, const Tensor& out, int64_t k, double eps) {
+  CHECK_CUDA(y); CHECK_BF16(y); CHECK_I32(inv_pos); CHECK_F32(w); CHECK_BF16(residual); CHECK_CONTIG(residual);
+  CHECK_BF16(gamma); CHECK_BF16(out);
+  const c10::cuda::CUDAGuard guard(y.device());
+  sp::combine_add_rmsnorm(y.data_ptr(), y.stride(0), inv_pos.data_ptr<int>(), w.data_ptr<float>(), residual.data_ptr(),
+                          gamma.data_ptr(), out.data_ptr(), out.stride(0), (int)residual.size(0), (int)k,
+                          (int)residual.size(1), (float)eps, stream());
+}
+
+Tensor split_workspace() {
+  float* w = split_ws();
+  auto opts = torch::TensorOptions().dtype(torch::kFloat32).device(torch::kCUDA, c10::cuda::current_device());
+  return torch::from_blob(w, {kSplitWsFloats}, opts);
 }
 
 int64_t moe_align(const Tensor& topk_ids, int64_t num_experts, int64_t block_n, const Tensor& grp_rows,
@@ -331,6 +381,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample_tokens", &sample_tokens);
   m.def("spec_verify", &spec_verify);
   m.def("decode_advance", &decode_advance);
+  m.def("slab_add_rmsnorm", &slab_add_rmsnorm);
+  m.def("mla_decode_prep", &mla_decode_prep);
+  m.def("combine_add_rmsnorm", &combine_add_rmsnorm);
+  m.def("split_workspace", &split_workspace);
   m.def("status_word", &status_word);
   m.def("clear_status", &clear_status);
   m.def("num_sms", &num_sms);

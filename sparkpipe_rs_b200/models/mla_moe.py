@@ -115,28 +115,39 @@ class MLAMoEModel:
         kv_a = a[:, self.qa_dim:]
         return q, kv_a
 
-    def _attn_decode(self, i: int, xn: torch.Tensor, fb: ForwardBatch, cache: KVCache) -> torch.Tensor:
+    def _attn_decode(self, i: int, xn: torch.Tensor, fb: ForwardBatch, cache: KVCache):
+        """Absorbed-MLA decode attention; returns the o_proj result as ``ops.Slabs`` or a tensor."""
         c, w = self.cfg, self.w
         p = f"l{i}."
         T = xn.shape[0]
         nh, dn, dv, kvl = c.num_heads, c.qk_nope_head_dim, c.v_head_dim, c.kv_lora_rank
-        q, kv_a = self._project(i, xn)
         layer_cache = cache.layer(i - self._layer_offset)
-        ops.mla_kv_write(kv_a, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache, None,
-                         kvl, c.qk_rope_head_dim, c.rms_norm_eps)
         q_lat = torch.empty(T, nh, c.kv_cache_dim, dtype=torch.bfloat16, device=self.device)
+        if c.q_lora_rank:
+            q, kv_a = self._project(i, xn)
+            ops.mla_kv_write(kv_a, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache,
+                             None, kvl, c.qk_rope_head_dim, c.rms_norm_eps)
+            ops.rope_q(self._q_view(q, T), dn, q_lat, kvl, fb.positions, self.cos_sin, c.qk_rope_head_dim)
+            q_src, q_batch_k = q, c.qk_head_dim
+        else:
+            # one kernel: split-K reduction of the q/kv projection, latent norm + RoPE
+            # + cache write, query RoPE and the compact q_nope operand
+            qkv = ops.linear_slabs(xn, w[p + "w_qkv_a"])
+            q_src = torch.empty(T, nh * dn, dtype=torch.bfloat16, device=self.device)
+            ops.mla_decode_prep(qkv, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache,
+                                q_src, q_lat, dn, 0, self.qa_dim, c.rms_norm_eps)
+            q_batch_k = dn
         # q_lat[t, h, :kvl] = q_nope[t, h] @ W_UK[h]
-        ops.batched_gemm(w[p + "w_uk_t"], q, q_lat.view(T, nh * c.kv_cache_dim), M=kvl, N=T, K=dn, batch=nh,
-                         a_batch_rows=kvl, b_k0=0, b_batch_k=c.qk_head_dim, ldd=nh * c.kv_cache_dim,
+        ops.batched_gemm(w[p + "w_uk_t"], q_src, q_lat.view(T, nh * c.kv_cache_dim), M=kvl, N=T, K=dn, batch=nh,
+                         a_batch_rows=kvl, b_k0=0, b_batch_k=q_batch_k, ldd=nh * c.kv_cache_dim,
                          d_batch_stride=c.kv_cache_dim)
-        ops.rope_q(self._q_view(q, T), dn, q_lat, kvl, fb.positions, self.cos_sin, c.qk_rope_head_dim)
         o_lat = torch.empty(T, nh, kvl, dtype=torch.bfloat16, device=self.device)
         ops.mla_decode(q_lat, layer_cache, fb.block_table, fb.context_lens, o_lat, fb.decode_splits, self.scale)
         attn = torch.empty(T, nh * dv, dtype=torch.bfloat16, device=self.device)
         # attn[t, h*dv + v] = o_lat[t, h] @ W_UV[h]^T
         ops.batched_gemm(w[p + "w_kv_b"], o_lat.view(T, nh * kvl), attn, M=dv, N=T, K=kvl, batch=nh, a_row0=dn,
                          a_batch_rows=dn + dv, b_batch_k=kvl, ldd=nh * dv, d_batch_stride=dv)
-        return ops.linear(attn, w[p + "w_o"])
+        return ops.linear_slabs(attn, w[p + "w_o"])
 
     def _attn_prefill(self, i: int, xn: torch.Tensor, fb: ForwardBatch, cache: KVCache) -> torch.Tensor:
         c, w = self.cfg, self.w
@@ -166,7 +177,7 @@ class MLAMoEModel:
             return ops.linear(ops.silu_mul(ops.linear(xn, w[p + "w13"])), w[p + "w2"])
         T = xn.shape[0]
         E, k, F, S = c.n_routed_experts, c.num_experts_per_tok, c.moe_intermediate_size, c.n_shared_experts
-        logits = ops.linear(xn, w[p + "gate"], out_dtype=torch.float32)
+        logits = ops.linear_slabs(xn, w[p + "gate"], out_dtype=torch.float32)
         sigmoid = c.scoring_func == "sigmoid"
         ids, wts = ops.moe_topk(logits, w[p + "gate_bias"] if sigmoid else None, k, 1 if sigmoid else 0,
                                 c.norm_topk_prob, c.routed_scaling_factor, n_shared=S)
@@ -183,9 +194,20 @@ class MLAMoEModel:
             act = ops.silu_mul(h13)
         y = torch.empty(T * kk, c.hidden_size, dtype=torch.bfloat16, device=self.device)
         ops.grouped_gemm(w[p + "e_w2"], act, y, grp_rows, grp_tiles, E + S, bn)
-        out = torch.empty(T, c.hidden_size, dtype=torch.bfloat16, device=self.device)
-        ops.moe_combine(y, inv_pos, wts, None, out, kk)
-        return out
+        # the weighted combine is fused into the next residual add + RMSNorm
+        return ("combine", y, inv_pos, wts, kk)
+
+    def _residual_norm(self, pending, res: torch.Tensor, gamma: torch.Tensor, xn: torch.Tensor):
+        """res += pending (if any); xn = rmsnorm(res) * gamma. `pending` is None, a
+        bf16 tensor, split-K ``ops.Slabs`` or a deferred MoE combine."""
+        eps = self.cfg.rms_norm_eps
+        if pending is None:
+            ops.add_rmsnorm(res, None, gamma, xn, eps)
+        elif isinstance(pending, tuple):
+            _, y, inv_pos, wts, kk = pending
+            ops.combine_add_rmsnorm(y, inv_pos, wts, res, gamma, xn, kk, eps)
+        else:
+            ops.slab_add_rmsnorm(pending, res, gamma, xn, eps)
 
     # ------------------------------------------------------------------ forward
     def forward(self, fb: ForwardBatch, cache: KVCache, layers: range | None = None,
@@ -203,25 +225,21 @@ class MLAMoEModel:
         else:
             res = hidden_in.clone()
         xn = torch.empty_like(res)
-        delta = None
+        pending = None
         for i in layers:
             p = f"l{i}."
-            ops.add_rmsnorm(delta if delta is not None else res, res if delta is not None else None,
-                            w[p + "in_norm"], xn, eps)
+            self._residual_norm(pending, res, w[p + "in_norm"], xn)
             if fb.mode == "decode":
                 o = self._attn_decode(i, xn, fb, cache)
             else:
                 o = self._attn_prefill(i, xn, fb, cache)
-            ops.add_rmsnorm(o, res, w[p + "post_norm"], xn, eps)
-            delta = self._mlp(i, xn)
+            self._residual_norm(o, res, w[p + "post_norm"], xn)
+            pending = self._mlp(i, xn)
         if return_hidden:
-            if delta is not None:
-                res.add_(delta)
+            if pending is not None:
+                self._residual_norm(pending, res, w["final_norm"], xn)
             return res
-        if delta is not None:
-            ops.add_rmsnorm(delta, res, w["final_norm"], xn, eps)
-        else:
-            ops.add_rmsnorm(res, None, w["final_norm"], xn, eps)
+        self._residual_norm(pending, res, w["final_norm"], xn)
         sel = xn if fb.logits_idx is None else ops.gather_rows(xn, fb.logits_idx)
         return ops.linear(sel, w["lm_head"])
 

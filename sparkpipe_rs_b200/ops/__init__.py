@@ -35,6 +35,11 @@ __all__ = [
     "sample_tokens",
     "spec_verify",
     "decode_advance",
+    "linear_slabs",
+    "Slabs",
+    "slab_add_rmsnorm",
+    "mla_decode_prep",
+    "combine_add_rmsnorm",
     "status_word",
     "clear_status",
     "SWAP_AB_MAX_TOKENS",
@@ -76,16 +81,60 @@ def gemm(a: torch.Tensor, b: torch.Tensor, d: torch.Tensor, *, M: int, N: int, K
          batch: int = 1, a_row0: int = 0, a_batch_rows: int = 0, a_k0: int = 0, a_batch_k: int = 0,
          b_row0: int = 0, b_batch_rows: int = 0, b_k0: int = 0, b_batch_k: int = 0, ldd: int | None = None,
          d_batch_stride: int = 0, splits: int = 0, block_n: int = 0, grp_rows=None, grp_tiles=None,
-         num_groups: int = 0, a_evict_first: bool = False, swiglu: bool = False) -> torch.Tensor:
-    """Raw tcgen05 GEMM: D[m, n] = sum_k A[m, k] B[n, k] (see gemm_tcgen05.cu)."""
+         num_groups: int = 0, a_evict_first: bool = False, swiglu: bool = False, slab_out: bool = False):
+    """Raw tcgen05 GEMM: D[m, n] = sum_k A[m, k] B[n, k] (see gemm_tcgen05.cu).
+
+    Returns D, or with ``slab_out`` and a split K, ``-splits``: the result then
+    is the sum of `splits` fp32 slabs in the split workspace (dense, D's
+    orientation), to be consumed by a slab-aware kernel."""
     ar, ac, lda = _rows_cols_ld(a)
     br, bc, ldb = _rows_cols_ld(b)
     if ldd is None:
         ldd = d.stride(0)
-    _count(kernels().gemm(a, b, d, ar, ac, lda, br, bc, ldb, ldd, d_batch_stride, M, N, K, batch, a_row0,
-                          a_batch_rows, a_k0, a_batch_k, b_row0, b_batch_rows, b_k0, b_batch_k, int(trans_out),
-                          splits, block_n, grp_rows, grp_tiles, num_groups, int(a_evict_first), int(swiglu)))
+    r = kernels().gemm(a, b, d, ar, ac, lda, br, bc, ldb, ldd, d_batch_stride, M, N, K, batch, a_row0,
+                       a_batch_rows, a_k0, a_batch_k, b_row0, b_batch_rows, b_k0, b_batch_k, int(trans_out),
+                       splits, block_n, grp_rows, grp_tiles, num_groups, int(a_evict_first), int(swiglu),
+                       int(slab_out))
+    if r < 0:
+        _count(1)
+        return r
+    _count(r)
     return d
+
+
+_WS = {}
+
+
+def split_workspace() -> torch.Tensor:
+    """The device's split-K partial workspace (fp32, owned by the kernel library)."""
+    dev = torch.cuda.current_device()
+    if dev not in _WS:
+        _WS[dev] = kernels().split_workspace()
+    return _WS[dev]
+
+
+class Slabs:
+    """A linear layer's result left as `splits` fp32 slabs [rows, cols] in the split workspace."""
+
+    def __init__(self, splits: int, rows: int, cols: int):
+        self.splits, self.rows, self.cols = splits, rows, cols
+        self.stride = rows * cols
+        self.ws = split_workspace()
+
+
+def linear_slabs(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, out_dtype=torch.bfloat16):
+    """Decode-shaped y = x @ w.T that may leave its split-K partial sums for the
+    consumer: returns ``Slabs`` (fused consumers sum them) or the output tensor."""
+    T, K = x.shape
+    O = w.shape[0]
+    if out is None:
+        out = torch.empty(T, O, dtype=out_dtype, device=x.device)
+    if T > SWAP_AB_MAX_TOKENS:
+        return linear(x, w, out=out)
+    r = gemm(w, x, out, M=O, N=T, K=K, trans_out=True, a_evict_first=True, slab_out=True)
+    if isinstance(r, int):
+        return Slabs(-r, T, O)
+    return out
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, out_dtype=torch.bfloat16,
@@ -191,11 +240,18 @@ def prefill_attention(q, k, kpe, v, o, cu_q, cu_k, max_q, scale, causal=True):
 
 
 def moe_topk(logits, bias, k, scoring, renorm, scaling, n_shared=0):
-    """Top-k routing; the last n_shared columns are the shared experts E.. (weight 1)."""
-    T = logits.shape[0]
-    ids = torch.empty(T, k + n_shared, dtype=torch.int32, device=logits.device)
-    w = torch.empty(T, k + n_shared, dtype=torch.float32, device=logits.device)
-    kernels().moe_topk(logits, bias, ids, w, int(n_shared), int(scoring), bool(renorm), float(scaling))
+    """Top-k routing; the last n_shared columns are the shared experts E.. (weight 1).
+    ``logits`` is a [T, E] fp32 tensor or router ``Slabs``."""
+    if isinstance(logits, Slabs):
+        T, E, dev = logits.rows, logits.cols, logits.ws.device
+        src, stride, splits = logits.ws, logits.stride, logits.splits
+    else:
+        T, E, dev = logits.shape[0], logits.shape[1], logits.device
+        src, stride, splits = logits, 0, 1
+    ids = torch.empty(T, k + n_shared, dtype=torch.int32, device=dev)
+    w = torch.empty(T, k + n_shared, dtype=torch.float32, device=dev)
+    kernels().moe_topk(src, bias, ids, w, int(n_shared), int(scoring), bool(renorm), float(scaling), T, E, stride,
+                       splits)
     _count(1)
     return ids, w
 
@@ -262,6 +318,33 @@ def spec_verify(draft, target, p_accept=0.0, seed=0, offset=0):
 def decode_advance(out_ids, ids, pos, ctx, slots, block_table, block_size=64):
     kernels().decode_advance(out_ids, ids, pos, ctx, slots, block_table, int(block_size))
     _count(1)
+
+
+def slab_add_rmsnorm(x, residual, w, out, eps):
+    """residual += x; out = rmsnorm(residual) * w, where x is ``Slabs`` or a bf16 tensor."""
+    if isinstance(x, Slabs):
+        kernels().slab_add_rmsnorm(x.ws, x.stride, x.splits, residual, w, out, float(eps))
+        _count(1)
+        return out
+    return add_rmsnorm(x, residual, w, out, eps)
+
+
+def mla_decode_prep(qkv, norm_w, positions, cos_sin, slot_mapping, cache, q_nope_out, q_lat, dn, q_off, kv_off,
+                    eps):
+    """Decode prologue of MLA attention from the fused q/kv projection (``Slabs`` or bf16 [T, Qa + kv])."""
+    if isinstance(qkv, Slabs):
+        kernels().mla_decode_prep(qkv.ws, qkv.stride, qkv.splits, None, norm_w, positions, cos_sin, slot_mapping,
+                                  cache, q_nope_out, q_lat, qkv.rows, dn, q_off, kv_off, qkv.cols, float(eps))
+    else:
+        kernels().mla_decode_prep(None, 0, 1, qkv, norm_w, positions, cos_sin, slot_mapping, cache, q_nope_out,
+                                  q_lat, qkv.shape[0], dn, q_off, kv_off, qkv.shape[1], float(eps))
+    _count(1)
+
+
+def combine_add_rmsnorm(y, inv_pos, w, residual, gamma, out, k, eps):
+    kernels().combine_add_rmsnorm(y, inv_pos, w, residual, gamma, out, int(k), float(eps))
+    _count(1)
+    return out
 
 
 def status_word() -> int:

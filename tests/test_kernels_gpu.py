@@ -349,3 +349,73 @@ def test_spec_verify():
                               torch.ones(4096, 4, device=DEV, dtype=torch.int32), p_accept=0.7, seed=1)
     # E[accepted] for a Bernoulli(0.7) chain of 3 = 0.7 + 0.49 + 0.343
     assert abs(acc2.float().mean().item() - 1.533) < 0.08
+
+
+# ------------------------------------------------------------------ fused decode kernels
+def test_linear_slabs_and_slab_add_rmsnorm():
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(21)
+    x = torch.randn(64, 2048, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(2048, 2048, device=DEV, generator=g) * 0.02).bfloat16()
+    res = torch.randn(64, 2048, device=DEV, generator=g).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(2048, device=DEV, generator=g)).bfloat16()
+    r0 = res.clone()
+    out = torch.empty_like(res)
+    sl = ops.linear_slabs(x, w)
+    assert isinstance(sl, ops.Slabs) and sl.splits > 1
+    ops.slab_add_rmsnorm(sl, res, gamma, out, 1e-6)
+    y = (x.float() @ w.float().t()).bfloat16().float()
+    s = (y + r0.float()).bfloat16().float()
+    _close(res, s, atol=3e-2, rtol=3e-2)
+    _close(out, s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-6) * gamma.float())
+    # router logits left as slabs feed the top-k kernel directly
+    gate = (torch.randn(64, 2048, device=DEV, generator=g) * 0.02).bfloat16()
+    lg = ops.linear_slabs(x, gate, out_dtype=torch.float32)
+    ids, wts = ops.moe_topk(lg, None, 6, 0, False, 1.0, n_shared=2)
+    ref = (x.float() @ gate.float().t()).softmax(-1)
+    assert torch.equal(ids[:, :6].long().sort(-1).values, ref.topk(6, -1).indices.sort(-1).values)
+
+
+def test_mla_decode_prep_matches_unfused_ops():
+    ops = _ops()
+    from sparkpipe_rs_b200.models.config import v2_lite
+    from sparkpipe_rs_b200.models.rope import cos_sin_table
+
+    cfg = v2_lite()
+    T, nh = 40, 16
+    g = torch.Generator(device=DEV).manual_seed(31)
+    tab = cos_sin_table(cfg, 2048, device=DEV)
+    qkv = torch.randn(T, 3072 + 576, device=DEV, generator=g).bfloat16()
+    nw = (1 + 0.1 * torch.randn(512, device=DEV, generator=g)).bfloat16()
+    pos = torch.randint(0, 2000, (T,), device=DEV, generator=g).int()
+    slots = torch.randperm(512, device=DEV, generator=g)[:T].int()
+    c1 = torch.zeros(512, 576, device=DEV, dtype=torch.bfloat16)
+    c2 = torch.zeros_like(c1)
+    qn = torch.empty(T, nh * 128, device=DEV, dtype=torch.bfloat16)
+    ql1 = torch.zeros(T, nh, 576, device=DEV, dtype=torch.bfloat16)
+    ql2 = torch.zeros_like(ql1)
+    ops.mla_decode_prep(qkv, nw, pos, tab, slots, c1, qn, ql1, 128, 0, 3072, 1e-6)
+    ops.mla_kv_write(qkv[:, 3072:], nw, pos, tab, slots, c2, None, 512, 64, 1e-6)
+    q3 = qkv[:, :3072].reshape(T, nh, 192)
+    ops.rope_q(q3, 128, ql2, 512, pos, tab, 64)
+    _close(c1, c2, atol=2e-2, rtol=2e-2)
+    _close(ql1[..., 512:], ql2[..., 512:], atol=2e-2, rtol=2e-2)
+    assert torch.equal(qn.view(T, nh, 128), q3[..., :128])
+
+
+def test_combine_add_rmsnorm_matches_unfused():
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(41)
+    T, k, H = 64, 8, 2048
+    y = torch.randn(T * k, H, device=DEV, generator=g).bfloat16()
+    inv = torch.randperm(T * k, device=DEV, generator=g).int()
+    w = torch.rand(T, k, device=DEV, generator=g)
+    res = torch.randn(T, H, device=DEV, generator=g).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(H, device=DEV, generator=g)).bfloat16()
+    r1, r2 = res.clone(), res.clone()
+    o1, o2, comb = torch.empty_like(res), torch.empty_like(res), torch.empty_like(res)
+    ops.combine_add_rmsnorm(y, inv, w, r1, gamma, o1, k, 1e-6)
+    ops.moe_combine(y, inv, w, None, comb, k)
+    ops.add_rmsnorm(comb, r2, gamma, o2, 1e-6)
+    _close(r1, r2, atol=2e-2, rtol=2e-2)
+    _close(o1, o2)
