@@ -49,6 +49,7 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, long long slab
     const int e = lane + i * 32;
     if (i < per && e < E) {
       float x = __ldcg(row + e);
+#pragma unroll 8
       for (int s2 = 1; s2 < splits; ++s2) x += __ldcg(row + s2 * slab_stride + e);  // split-K slabs
       score[i] = x;
     } else {
@@ -125,7 +126,7 @@ void moe_topk(const float* logits, long long slab_stride, int splits, const floa
   if (E > 32 * TOPK_MAX_PER_LANE) throw std::runtime_error("moe_topk: at most 512 experts");
   if (k + n_shared > 32) throw std::runtime_error("moe_topk: k + shared <= 32");
   if (n_group > 1 && topk_group < n_group) throw std::runtime_error("moe_topk: group-limited routing not supported");
-  const int warps = 2;
+  const int warps = 1;
   launch_k(moe_topk_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, s, logits, slab_stride,
            splits < 1 ? 1 : splits, bias, topk_ids, topk_w, T, E, k, n_shared, scoring, renorm, scaling);
 }

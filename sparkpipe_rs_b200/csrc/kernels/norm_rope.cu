@@ -150,67 +150,111 @@ void slab_add_rmsnorm(const float* slab, long long stride, int splits, void* res
            (const bf16*)w, (bf16*)out, ldo, hidden, eps);
 }
 
-// Decode prologue of MLA attention, one CTA (8 warps) per token. The token's
-// q/kv projection row is either bf16 (`src`) or the sum of fp32 split-K slabs.
-//   warp 0        : latent RMSNorm + RoPE on the rope key -> paged cache slot
-//   all warps     : per head, q_nope -> q_nope_out[t, h, :] (bf16, compact) and
-//                   RoPE(q_pe) -> q_lat[t, h, kv_lora:]
-__global__ void __launch_bounds__(256) mla_decode_prep_kernel(
-    const float* __restrict__ slab, long long stride, int splits, const bf16* __restrict__ src, long long lds,
-    const bf16* __restrict__ nw, const int* __restrict__ pos, const float* __restrict__ cs,
+// Decode prologue of MLA attention. The token's q/kv projection row is either
+// bf16 (`src`) or the sum of fp32 split-K slabs. Grid (T, 1 + ceil(H / 4)),
+// 128 threads, every thread handles 4 consecutive columns (float4 slab loads,
+// the split loop unrolled so the loads overlap):
+//   blockIdx.y == 0 : latent RMSNorm + RoPE on the rope key -> paged cache slot
+//   blockIdx.y >= 1 : 4 heads: q_nope -> q_nope_out[t, h, :] (bf16, compact),
+//                     RoPE(q_pe) -> q_lat[t, h, kv_lora:]
+struct PrepSrc {
+  const float* slab;
+  long long stride;
+  int splits;
+  const bf16* src;
+  long long lds;
+  int row_len;
+};
+
+SP_DEVI float4 prep_load4(const PrepSrc& s, int t, int c) {
+  if (s.slab) {
+    const float* p = s.slab + (long long)t * s.row_len + c;
+    float4 a = __ldcg(reinterpret_cast<const float4*>(p));
+#pragma unroll 8
+    for (int k = 1; k < s.splits; ++k) {
+      const float4 b = __ldcg(reinterpret_cast<const float4*>(p + k * s.stride));
+      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    // the unfused path rounds the GEMM output to bf16: keep the same numerics
+    a.x = __bfloat162float(__float2bfloat16_rn(a.x));
+    a.y = __bfloat162float(__float2bfloat16_rn(a.y));
+    a.z = __bfloat162float(__float2bfloat16_rn(a.z));
+    a.w = __bfloat162float(__float2bfloat16_rn(a.w));
+    return a;
+  }
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(s.src + (long long)t * s.lds + c);
+  const float2 u = __bfloat1622float2(h[0]), v = __bfloat1622float2(h[1]);
+  return make_float4(u.x, u.y, v.x, v.y);
+}
+
+SP_DEVI void rope_store4(const float4& x, const float* cp, int half, int i0, bf16* dst) {
+  // elements (2*i0, 2*i0+1) and (2*i0+2, 2*i0+3) form two rotation pairs
+  const float c0 = cp[i0], s0 = cp[half + i0], c1 = cp[i0 + 1], s1 = cp[half + i0 + 1];
+  __nv_bfloat162 a = __floats2bfloat162_rn(x.x * c0 - x.y * s0, x.x * s0 + x.y * c0);
+  __nv_bfloat162 b = __floats2bfloat162_rn(x.z * c1 - x.w * s1, x.z * s1 + x.w * c1);
+  reinterpret_cast<__nv_bfloat162*>(dst)[0] = a;
+  reinterpret_cast<__nv_bfloat162*>(dst)[1] = b;
+}
+
+__global__ void __launch_bounds__(128) mla_decode_prep_kernel(
+    PrepSrc src, const bf16* __restrict__ nw, const int* __restrict__ pos, const float* __restrict__ cs,
     const int* __restrict__ slots, bf16* __restrict__ cache, bf16* __restrict__ q_nope_out,
-    bf16* __restrict__ q_lat, int H, int dn, int dr, int L, int qoff, int kvoff, int row_len, float eps) {
+    bf16* __restrict__ q_lat, int H, int dn, int dr, int L, int qoff, int kvoff, float eps) {
   griddep_wait();
   griddep_launch();
   const int t = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  auto val = [&](int c) -> float {
-    if (slab) {
-      const float* p = slab + (long long)t * row_len + c;
-      float a = __ldcg(p);
-      for (int s2 = 1; s2 < splits; ++s2) a += __ldcg(p + s2 * stride);
-      return __bfloat162float(__float2bfloat16_rn(a));
-    }
-    return __bfloat162float(src[(long long)t * lds + c]);
-  };
-  const int p = pos[t];
-  const float* cp = cs + (long long)p * dr;
+  const int tid = threadIdx.x;
+  const float* cp = cs + (long long)pos[t] * dr;
   const int W = L + dr;
-  if (warp == 0) {
-    float v[32];
+  if (blockIdx.y == 0) {
+    __shared__ float part[4];
+    float4 v[2];
     float ss = 0.f;
-    const int per = L / 32;  // <= 32
-    for (int i = 0; i < per; ++i) {
-      v[i] = val(kvoff + lane + i * 32);
-      ss += v[i] * v[i];
+    const int nv = L / 4;  // float4 columns of the latent (<= 256)
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c4 = tid + i * 128;
+      if (c4 < nv) {
+        v[i] = prep_load4(src, t, kvoff + c4 * 4);
+        ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+      }
     }
     ss = warp_sum(ss);
-    const float inv = rsqrtf(ss / L + eps);
+    if ((tid & 31) == 0) part[tid >> 5] = ss;
+    __syncthreads();
+    const float inv = rsqrtf((part[0] + part[1] + part[2] + part[3]) / L + eps);
     const int slot = slots[t];
-    if (slot >= 0) {
-      bf16* crow = cache + (long long)slot * W;
-      for (int i = 0; i < per; ++i) {
-        const int c = lane + i * 32;
-        crow[c] = __float2bfloat16_rn(v[i] * inv * __bfloat162float(nw[c]));
-      }
-      for (int i = lane; i < dr / 2; i += 32) {
-        const float x0 = val(kvoff + L + 2 * i), x1 = val(kvoff + L + 2 * i + 1);
-        const float c = cp[i], sn = cp[dr / 2 + i];
-        crow[L + 2 * i] = __float2bfloat16_rn(x0 * c - x1 * sn);
-        crow[L + 2 * i + 1] = __float2bfloat16_rn(x0 * sn + x1 * c);
+    if (slot < 0) return;
+    bf16* crow = cache + (long long)slot * W;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c4 = tid + i * 128;
+      if (c4 < nv) {
+        const int c = c4 * 4;
+        const float g0 = __bfloat162float(nw[c]), g1 = __bfloat162float(nw[c + 1]);
+        const float g2 = __bfloat162float(nw[c + 2]), g3 = __bfloat162float(nw[c + 3]);
+        reinterpret_cast<__nv_bfloat162*>(crow + c)[0] = __floats2bfloat162_rn(v[i].x * inv * g0, v[i].y * inv * g1);
+        reinterpret_cast<__nv_bfloat162*>(crow + c)[1] = __floats2bfloat162_rn(v[i].z * inv * g2, v[i].w * inv * g3);
       }
     }
+    if (tid < dr / 4) rope_store4(prep_load4(src, t, kvoff + L + tid * 4), cp, dr / 2, tid * 2, crow + L + tid * 4);
+    return;
   }
-  for (int h = warp; h < H; h += 8) {
-    const int base = qoff + h * (dn + dr);
-    bf16* qn = q_nope_out + ((long long)t * H + h) * dn;
-    for (int c = lane; c < dn; c += 32) qn[c] = __float2bfloat16_rn(val(base + c));
-    bf16* ql = q_lat + ((long long)t * H + h) * W + L;
-    for (int i = lane; i < dr / 2; i += 32) {
-      const float x0 = val(base + dn + 2 * i), x1 = val(base + dn + 2 * i + 1);
-      const float c = cp[i], sn = cp[dr / 2 + i];
-      ql[2 * i] = __float2bfloat16_rn(x0 * c - x1 * sn);
-      ql[2 * i + 1] = __float2bfloat16_rn(x0 * sn + x1 * c);
+  // 4 heads per CTA: (dn + dr) / 4 float4 columns per head
+  const int per_head = (dn + dr) / 4;
+  const int h0 = (blockIdx.y - 1) * 4;
+  for (int j = tid; j < 4 * per_head; j += 128) {
+    const int h = h0 + j / per_head;
+    if (h >= H) break;
+    const int c = (j % per_head) * 4;
+    const float4 x = prep_load4(src, t, qoff + h * (dn + dr) + c);
+    if (c < dn) {
+      bf16* qn = q_nope_out + ((long long)t * H + h) * dn + c;
+      reinterpret_cast<__nv_bfloat162*>(qn)[0] = __floats2bfloat162_rn(x.x, x.y);
+      reinterpret_cast<__nv_bfloat162*>(qn)[1] = __floats2bfloat162_rn(x.z, x.w);
+    } else {
+      const int r = c - dn;
+      rope_store4(x, cp, dr / 2, r / 2, q_lat + ((long long)t * H + h) * W + L + r);
     }
   }
 }
@@ -220,10 +264,14 @@ void mla_decode_prep(const float* slab, long long stride, int splits, const void
                      void* cache, void* q_nope_out, void* q_lat, int T, int H, int dn, int dr, int kv_lora,
                      int q_off, int kv_off, int row_len, float eps, cudaStream_t s) {
   if (T <= 0) return;
-  if (kv_lora % 32 != 0 || kv_lora > 1024) throw std::runtime_error("mla_decode_prep: kv_lora % 32, <= 1024");
-  launch_k(mla_decode_prep_kernel, dim3(T), dim3(256), 0, s, slab, stride, splits, (const bf16*)src, lds,
-           (const bf16*)norm_w, positions, cos_sin, slot_mapping, (bf16*)cache, (bf16*)q_nope_out, (bf16*)q_lat, H,
-           dn, dr, kv_lora, q_off, kv_off, row_len, eps);
+  if (kv_lora % 4 || kv_lora > 1024 || dn % 4 || dr % 4 || dr > 512 || q_off % 4 || kv_off % 4 || row_len % 4)
+    throw std::runtime_error("mla_decode_prep: 4-aligned dims, kv_lora <= 1024 required");
+  if (!slab && (lds % 4 || (reinterpret_cast<uintptr_t>(src) & 7)))
+    throw std::runtime_error("mla_decode_prep: bf16 source rows must be 8-byte aligned");
+  PrepSrc ps{slab, stride, splits < 1 ? 1 : splits, (const bf16*)src, lds, row_len};
+  launch_k(mla_decode_prep_kernel, dim3(T, 1 + (H + 3) / 4), dim3(128), 0, s, ps, (const bf16*)norm_w, positions,
+           cos_sin, slot_mapping, (bf16*)cache, (bf16*)q_nope_out, (bf16*)q_lat, H, dn, dr, kv_lora, q_off, kv_off,
+           eps);
 }
 
 __global__ void mla_kv_write_kernel(const bf16* __restrict__ kv, long long ldkv, const bf16* __restrict__ nw,
