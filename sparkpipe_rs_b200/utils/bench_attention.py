@@ -1,0 +1,53 @@
+"""Micro-benchmark of the MLA paged decode attention kernel.
+
+Captures `iters` launches (attention + split-KV combine) into a CUDA graph and
+times the replay with CUDA events: device time per call, achieved KV-cache
+bandwidth against the bytes that must be read (context x 576 x 2 bytes per
+sequence). Sweeps the split-KV factor.
+
+    python -m sparkpipe_rs_b200.utils.bench_attention --batch 64 --heads 16 --ctx 1024 --splits 1,2,3,4,6,8
+"""
+from __future__ import annotations
+
+import argparse
+import math
+
+import torch
+
+from .bench_gemm import time_fn
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--ctx", type=int, default=1024)
+    ap.add_argument("--splits", default="0,1,2,3,4,5,6,8")
+    ap.add_argument("--iters", type=int, default=50)
+    args = ap.parse_args()
+    from sparkpipe_rs_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    B, H, L = args.batch, args.heads, args.ctx
+    bpseq = math.ceil(L / 64)
+    # several cache copies so consecutive launches stream from HBM, not L2
+    n_caches = max(1, min(8, (1 << 30) // (B * bpseq * 64 * 576 * 2)))
+    caches = [torch.randn(B * bpseq * 64, 576, device=dev).bfloat16() for _ in range(n_caches)]
+    bt = torch.randperm(B * bpseq, device=dev).int().view(B, bpseq)
+    ctx = torch.full((B,), L, device=dev, dtype=torch.int32)
+    q = torch.randn(B, H, 576, device=dev).bfloat16()
+    out = torch.empty(B, H, 512, device=dev, dtype=torch.bfloat16)
+    nbytes = B * L * 576 * 2
+    scale = 1 / math.sqrt(192)
+    for sp in [int(s) for s in args.splits.split(",")]:
+        splits = sp or ops.mla_decode_splits(B, H, L, ops.kernels().num_sms())
+        o_part = torch.empty(B, splits, H, 512, device=dev, dtype=torch.float32)
+        lse = torch.empty(B, splits, H, device=dev, dtype=torch.float32)
+        us = time_fn(lambda i: ops.mla_decode(q, caches[i % n_caches], bt, ctx, out, splits, scale, o_part, lse),
+                     args.iters)
+        print(f"mla_decode B={B} H={H} ctx={L} splits={splits}{' (auto)' if sp == 0 else ''}: {us:8.2f} us  "
+              f"{nbytes / us / 1e6:6.2f} TB/s of KV")
+
+
+if __name__ == "__main__":
+    main()
