@@ -6,6 +6,11 @@
 // group share every KV byte, so one CTA streams each 64-token block once (TMA,
 // 128-byte swizzled sub-tiles, double buffered) and all of its warps consume it.
 //
+// Warp layout: NJ warps per 16-head tile. For each 64-token block a warp
+// computes the scores of 64/NJ tokens and the output of 512/NJ latent dims, so
+// NJ = 8 halves the serial mma.sync work per warp; measured on 16-head
+// decode (B=64, ctx 1024) it was 6% slower than NJ = 4, so both widths use 4.
+//
 // Split-KV: a sequence's blocks are divided over `splits` CTAs; each writes a
 // normalised partial output and its log-sum-exp, and a combine kernel merges
 // them. With splits == 1 the kernel writes the bf16 output directly.
@@ -46,32 +51,36 @@ constexpr int MLA_CHUNKS = 9;    // 64-element (128-byte) column chunks
 constexpr int MLA_BLK = 64;      // tokens per cache block
 constexpr int KV_STAGE_BYTES = MLA_CHUNKS * MLA_BLK * 128;
 
-template <int HG>
+template <int HG, int NJ>
 struct MlaCfg {
-  static constexpr int WARPS = 4 * (HG / 16);
+  static constexpr int WARPS = NJ * (HG / 16);
+  static constexpr int TOKW = MLA_BLK / NJ;   // tokens per warp in S = Q K^T
+  static constexpr int NT = TOKW / 8;         // n8 tiles per warp in S
+  static constexpr int DIMW = MLA_LAT / NJ;   // latent dims per warp in O = P V
+  static constexpr int NP = DIMW / 16;        // n8-tile pairs per warp in O
   static constexpr int Q_BYTES = MLA_CHUNKS * HG * 128;
   static constexpr int P_PITCH = 72;  // bf16 elements per P row (64 + 8 pad)
   static constexpr int OFF_KV = (Q_BYTES + 1023) / 1024 * 1024;
   static constexpr int OFF_P = OFF_KV + 2 * KV_STAGE_BYTES;
   static constexpr int OFF_STAT = OFF_P + HG * P_PITCH * 2;
-  static constexpr int OFF_BAR = OFF_STAT + 2 * 4 * HG * 4;
+  static constexpr int OFF_BAR = OFF_STAT + 2 * NJ * HG * 4;
   static constexpr int SMEM = OFF_BAR + 64 + 1024;
 };
 
-template <int HG>
-__global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
+template <int HG, int NJ>
+__global__ void __launch_bounds__(MlaCfg<HG, NJ>::WARPS * 32, 1)
     mla_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       const MlaKParams p) {
   griddep_wait();
   griddep_launch();
-  using C = MlaCfg<HG>;
+  using C = MlaCfg<HG, NJ>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sQ = smem_u32(smem);
   const uint32_t sKV = smem_u32(smem + C::OFF_KV);
   bf16* sP = reinterpret_cast<bf16*>(smem + C::OFF_P);
-  float* sMax = reinterpret_cast<float*>(smem + C::OFF_STAT);  // [4][HG]
-  float* sSum = sMax + 4 * HG;                                  // [4][HG]
+  float* sMax = reinterpret_cast<float*>(smem + C::OFF_STAT);  // [NJ][HG]
+  float* sSum = sMax + NJ * HG;                                 // [NJ][HG]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* qbar = full + 2;
   volatile int* s_err = reinterpret_cast<volatile int*>(qbar + 1);
@@ -80,7 +89,7 @@ __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
   const int split = blockIdx.y;
   const int hg = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mt = warp >> 2, j = warp & 3;
+  const int mt = warp / NJ, j = warp % NJ;
 
   const int ctx = p.context_lens[b];
   const int nblk = (ctx + MLA_BLK - 1) / MLA_BLK;
@@ -118,9 +127,9 @@ __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
     for (; issued < 2 && issued < nb; ++issued) issue_block(issued);
   }
 
-  float o[16][4];
+  float o[2 * C::NP][4];
 #pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  for (int n = 0; n < 2 * C::NP; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_run[2] = {0.f, 0.f};
   const int r_lo = lane >> 2;           // fragment rows r_lo and r_lo + 8
@@ -134,25 +143,32 @@ __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
     if (!__syncthreads_and(got)) { ok = false; break; }
     const uint32_t kvb = sKV + s * KV_STAGE_BYTES;
 
-    // ---- S = Q K^T for 16 heads x 16 tokens of this warp
-    float sc[2][4];
+    // ---- S = Q K^T for 16 heads x TOKW tokens of this warp
+    float sc[C::NT][4];
 #pragma unroll
-    for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+    for (int n = 0; n < C::NT; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
 #pragma unroll 4
     for (int kk = 0; kk < MLA_DIM / 16; ++kk) {
       const int c = kk >> 2;
       const int cc = (kk & 3) * 16;
-      uint32_t a[4], bb[4];
+      uint32_t a[4];
       ldsm_x4(a, swz128(sQ + c * HG * 128, qrow + (lane & 15), cc + (lane >> 4) * 8));
-      ldsm_x4(bb, swz128(kvb + c * MLA_BLK * 128, j * 16 + (lane & 7) + (lane >> 4) * 8, cc + ((lane >> 3) & 1) * 8));
-      mma16816(sc[0], a, bb[0], bb[1]);
-      mma16816(sc[1], a, bb[2], bb[3]);
+      if constexpr (C::NT == 2) {
+        uint32_t bb[4];
+        ldsm_x4(bb, swz128(kvb + c * MLA_BLK * 128, j * 16 + (lane & 7) + (lane >> 4) * 8, cc + ((lane >> 3) & 1) * 8));
+        mma16816(sc[0], a, bb[0], bb[1]);
+        mma16816(sc[1], a, bb[2], bb[3]);
+      } else {
+        uint32_t bb[2];
+        ldsm_x2(bb, swz128(kvb + c * MLA_BLK * 128, j * 8 + (lane & 7), cc + ((lane >> 3) & 1) * 8));
+        mma16816(sc[0], a, bb[0], bb[1]);
+      }
     }
     // ---- scale, mask, row max
-    const int tok0 = (kb0 + i) * MLA_BLK + j * 16;
+    const int tok0 = (kb0 + i) * MLA_BLK + j * C::TOKW;
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int n = 0; n < 2; ++n)
+    for (int n = 0; n < C::NT; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int tok = tok0 + n * 8 + (lane & 3) * 2 + (e & 1);
@@ -177,14 +193,14 @@ __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
       const int row = qrow + r_lo + h * 8;
       float mn = m_run[h];
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) mn = fmaxf(mn, sMax[jj * HG + row]);
+      for (int jj = 0; jj < NJ; ++jj) mn = fmaxf(mn, sMax[jj * HG + row]);
       alpha[h] = (m_run[h] == -INFINITY) ? 0.f : exp2f(m_run[h] - mn);
       m_run[h] = mn;
       l_run[h] *= alpha[h];
     }
     // ---- P = exp2(S - m), stored bf16 for the PV product
 #pragma unroll
-    for (int n = 0; n < 2; ++n) {
+    for (int n = 0; n < C::NT; ++n) {
       float pv[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -192,17 +208,17 @@ __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
         pv[e] = (sc[n][e] == -INFINITY) ? 0.f : exp2f(sc[n][e] - mrow);
         l_run[e >> 1] += pv[e];
       }
-      const int col = j * 16 + n * 8 + (lane & 3) * 2;
+      const int col = j * C::TOKW + n * 8 + (lane & 3) * 2;
       *reinterpret_cast<uint32_t*>(sP + (qrow + r_lo) * C::P_PITCH + col) = pack_bf16(pv[0], pv[1]);
       *reinterpret_cast<uint32_t*>(sP + (qrow + r_lo + 8) * C::P_PITCH + col) = pack_bf16(pv[2], pv[3]);
     }
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
+    for (int n = 0; n < 2 * C::NP; ++n) {
       o[n][0] *= alpha[0]; o[n][1] *= alpha[0];
       o[n][2] *= alpha[1]; o[n][3] *= alpha[1];
     }
     __syncthreads();
-    // ---- O[16 heads, 128 dims of slice j] += P[16, 64] V[64, 128]
+    // ---- O[16 heads, DIMW dims of slice j] += P[16, 64] V[64, DIMW]
     const uint32_t sPa = smem_u32(sP);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
@@ -210,8 +226,8 @@ __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
       ldsm_x4(a, sPa + ((qrow + (lane & 15)) * C::P_PITCH + kk * 16 + (lane >> 4) * 8) * 2);
       const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
-      for (int np = 0; np < 8; ++np) {
-        const int dim = j * 128 + np * 16 + (lane >> 4) * 8;
+      for (int np = 0; np < C::NP; ++np) {
+        const int dim = j * C::DIMW + np * 16 + (lane >> 4) * 8;
         uint32_t bb[4];
         ldsm_x4_t(bb, swz128(kvb + (dim >> 6) * MLA_BLK * 128, tok, dim & 63));
         mma16816(o[2 * np], a, bb[0], bb[1]);
@@ -247,7 +263,7 @@ __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
     const int row = qrow + r_lo + h * 8;
     float l = 0.f;
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) l += sSum[jj * HG + row];
+    for (int jj = 0; jj < NJ; ++jj) l += sSum[jj * HG + row];
     inv[h] = l > 0.f ? 1.f / l : 0.f;
     lse[h] = l > 0.f ? m_run[h] + __log2f(l) : -INFINITY;
   }
@@ -255,18 +271,18 @@ __global__ void __launch_bounds__(MlaCfg<HG>::WARPS * 32, 1)
   if (p.splits == 1) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      bf16* orow = p.out + ((long long)b * p.H + head0 + h * 8) * MLA_LAT + j * 128 + (lane & 3) * 2;
+      bf16* orow = p.out + ((long long)b * p.H + head0 + h * 8) * MLA_LAT + j * C::DIMW + (lane & 3) * 2;
 #pragma unroll
-      for (int n = 0; n < 16; ++n)
+      for (int n = 0; n < 2 * C::NP; ++n)
         *reinterpret_cast<uint32_t*>(orow + n * 8) = pack_bf16(o[n][2 * h] * inv[h], o[n][2 * h + 1] * inv[h]);
     }
   } else {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const long long rowi = ((long long)b * p.splits + split) * p.H + head0 + h * 8;
-      float* orow = p.o_part + rowi * MLA_LAT + j * 128 + (lane & 3) * 2;
+      float* orow = p.o_part + rowi * MLA_LAT + j * C::DIMW + (lane & 3) * 2;
 #pragma unroll
-      for (int n = 0; n < 16; ++n)
+      for (int n = 0; n < 2 * C::NP; ++n)
         *reinterpret_cast<float2*>(orow + n * 8) = make_float2(o[n][2 * h] * inv[h], o[n][2 * h + 1] * inv[h]);
       if (j == 0 && (lane & 3) == 0) p.lse_part[rowi] = lse[h];
     }
@@ -298,13 +314,13 @@ __global__ void mla_combine_kernel(const float* __restrict__ o_part, const float
   *reinterpret_cast<uint32_t*>(orow + 2) = pack_bf16(acc[2] * inv, acc[3] * inv);
 }
 
-template <int HG>
+template <int HG, int NJ>
 static void launch_mla(const MlaDecodeLaunch& l) {
-  using C = MlaCfg<HG>;
+  using C = MlaCfg<HG, NJ>;
   CUtensorMap tq, tkv;
   make_tmap_2d(&tq, l.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (long long)l.B * l.H, MLA_DIM, MLA_DIM, HG, 64);
   make_tmap_2d(&tkv, l.cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.num_slots, MLA_DIM, MLA_DIM, MLA_BLK, 64);
-  auto kern = mla_decode_kernel<HG>;
+  auto kern = mla_decode_kernel<HG, NJ>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
@@ -335,8 +351,8 @@ void mla_decode(const MlaDecodeLaunch& l) {
   if (l.kv_lora != MLA_LAT || l.rope != 64 || l.block_size != MLA_BLK)
     throw std::runtime_error("mla_decode: supports kv_lora 512, rope 64, 64-token blocks");
   if (l.splits > 1 && (!l.o_part || !l.lse_part)) throw std::runtime_error("mla_decode: split-KV needs scratch");
-  if (l.H % 32 == 0) launch_mla<32>(l);
-  else if (l.H % 16 == 0) launch_mla<16>(l);
+  if (l.H % 32 == 0) launch_mla<32, 4>(l);
+  else if (l.H % 16 == 0) launch_mla<16, 4>(l);
   else throw std::runtime_error("mla_decode: heads must be a multiple of 16");
 }
 

@@ -215,10 +215,12 @@ def quant_fp8_block(x):
 
 
 def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 148) -> int:
-    """Split-KV factor: enough CTAs to cover the SMs without splits of under two blocks."""
+    """Split-KV factor: the most CTAs that still fit one wave on the SMs, without
+    splits of under two blocks (a second partial wave costs more than it hides:
+    B=64, 16 heads, ctx 1024 measured 27 us at 2 splits, 34 us at 3)."""
     groups = heads // (32 if heads % 32 == 0 else 16)
     ctas = max(1, batch * groups)
-    want = max(1, math.ceil(num_sms / ctas))
+    want = max(1, num_sms // ctas)
     blocks = max(1, math.ceil(max_context / 64))
     return int(max(1, min(want, blocks // 2 if blocks >= 2 else 1, 16)))
 
