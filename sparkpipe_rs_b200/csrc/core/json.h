@@ -29,6 +29,7 @@ class Json {
   bool is_string() const { return type_ == Type::String; }
   bool is_number() const { return type_ == Type::Number; }
   bool is_bool() const { return type_ == Type::Bool; }
+  bool is_integer() const { return type_ == Type::Number && is_int_; }  // integral literal
 
   const std::string& str() const;
   double num() const;

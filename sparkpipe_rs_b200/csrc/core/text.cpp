@@ -374,50 +374,80 @@ int64_t Tokenizer::token_to_id(const std::string& token) const {
 bool Tokenizer::is_special(uint32_t id) const { return id < special_mask_.size() && special_mask_[id]; }
 
 // ------------------------------------------------------------------ chat templates
+namespace {
+const char* kDsBos = "<\xef\xbd\x9c" "begin\xe2\x96\x81of\xe2\x96\x81sentence\xef\xbd\x9c>";
+const char* kDsEos = "<\xef\xbd\x9c" "end\xe2\x96\x81of\xe2\x96\x81sentence\xef\xbd\x9c>";
+const char* kDsUser = "<\xef\xbd\x9cUser\xef\xbd\x9c>";
+const char* kDsAssistant = "<\xef\xbd\x9c" "Assistant\xef\xbd\x9c>";
+const char* kDsTool = "<\xef\xbd\x9ctool\xe2\x96\x81output\xef\xbd\x9c>";
+}  // namespace
+
+ChatWriter::ChatWriter(const std::string& style, size_t capacity) : cap_(capacity) {
+  if (style == "glm") glm_ = true;
+  else if (style == "deepseek") glm_ = false;
+  else fail(Status::InvalidArgument, "chat: unknown template style " + style);
+}
+
+void ChatWriter::append(const std::string& s) {
+  if (out_.size() + s.size() > cap_) fail(Status::CapacityExceeded, "chat: rendered prompt exceeds capacity");
+  out_ += s;
+}
+
+void ChatWriter::begin(const std::string& effort, uint32_t flags) {
+  if (flags & ~(kChatAddGenerationPrompt | kChatEnableThinking)) fail(Status::InvalidArgument, "chat: unknown flags");
+  if (!glm_) { append(kDsBos); return; }
+  append("[gMASK]<sop>");
+  if (flags & kChatEnableThinking) {
+    append("<|system|>Reasoning Effort: ");
+    append((effort == "high" || effort == "High") ? "High" : "Max");
+  }
+}
+
+void ChatWriter::begin_message(const std::string& role) {
+  if (glm_) {
+    if (role == "system") append("<|system|>");
+    else if (role == "user") append("<|user|>");
+    else if (role == "assistant") { append("<|assistant|>"); append("<think></think>"); }
+    else if (role == "tool") { append("<|observation|>"); append("<tool_response>"); }
+    else fail(Status::InvalidArgument, "chat: unknown role " + role);
+  } else {
+    if (role == "system") {}
+    else if (role == "user") append(kDsUser);
+    else if (role == "assistant") append(kDsAssistant);
+    else if (role == "tool") append(kDsTool);
+    else fail(Status::InvalidArgument, "chat: unknown role " + role);
+  }
+}
+
+void ChatWriter::end_message(const std::string& role) {
+  if (glm_) {
+    if (role == "tool") append("</tool_response>");
+  } else if (role == "assistant") {
+    append(kDsEos);
+  }
+}
+
+void ChatWriter::finish(uint32_t flags) {
+  if (!(flags & kChatAddGenerationPrompt)) return;
+  if (glm_) {
+    append("<|assistant|>");
+    append((flags & kChatEnableThinking) ? "<think>" : "<think></think>");
+  } else {
+    append(kDsAssistant);
+  }
+}
+
 std::string render_chat(const std::vector<ChatMessage>& msgs, const std::string& style, uint32_t flags,
                         const std::string& effort, size_t capacity) {
-  if (flags & ~(kChatAddGenerationPrompt | kChatEnableThinking)) fail(Status::InvalidArgument, "chat: unknown flags");
-  std::string o;
-  auto add = [&](const std::string& s) {
-    if (o.size() + s.size() > capacity) fail(Status::CapacityExceeded, "chat: rendered prompt exceeds capacity");
-    o += s;
-  };
-  if (style == "glm") {
-    add("[gMASK]<sop>");
-    if (flags & kChatEnableThinking) {
-      add("<|system|>Reasoning Effort: ");
-      add((effort == "high" || effort == "High") ? "High" : "Max");
-    }
-    for (const auto& m : msgs) {
-      if (m.role == "system") add("<|system|>");
-      else if (m.role == "user") add("<|user|>");
-      else if (m.role == "assistant") { add("<|assistant|>"); add("<think></think>"); }
-      else if (m.role == "tool") { add("<|observation|>"); add("<tool_response>"); }
-      else fail(Status::InvalidArgument, "chat: unknown role " + m.role);
-      add(m.content);
-      if (m.role == "tool") add("</tool_response>");
-    }
-    if (flags & kChatAddGenerationPrompt) {
-      add("<|assistant|>");
-      add((flags & kChatEnableThinking) ? "<think>" : "<think></think>");
-    }
-  } else if (style == "deepseek") {
-    add("<\xef\xbd\x9c" "begin\xe2\x96\x81of\xe2\x96\x81sentence\xef\xbd\x9c>");
-    for (const auto& m : msgs) {
-      if (m.role == "system") add(m.content);
-      else if (m.role == "user") { add("<\xef\xbd\x9cUser\xef\xbd\x9c>"); add(m.content); }
-      else if (m.role == "assistant") {
-        add("<\xef\xbd\x9c" "Assistant\xef\xbd\x9c>");
-        add(m.content);
-        add("<\xef\xbd\x9c" "end\xe2\x96\x81of\xe2\x96\x81sentence\xef\xbd\x9c>");
-      } else if (m.role == "tool") { add("<\xef\xbd\x9ctool\xe2\x96\x81output\xef\xbd\x9c>"); add(m.content); }
-      else fail(Status::InvalidArgument, "chat: unknown role " + m.role);
-    }
-    if (flags & kChatAddGenerationPrompt) add("<\xef\xbd\x9c" "Assistant\xef\xbd\x9c>");
-  } else {
-    fail(Status::InvalidArgument, "chat: unknown template style " + style);
+  ChatWriter w(style, capacity);
+  w.begin(effort, flags);
+  for (const auto& m : msgs) {
+    w.begin_message(m.role);
+    w.append(m.content);
+    w.end_message(m.role);
   }
-  return o;
+  w.finish(flags);
+  return w.text();
 }
 
 }  // namespace spc

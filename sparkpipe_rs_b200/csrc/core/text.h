@@ -86,6 +86,29 @@ struct ChatMessage {
 };
 constexpr uint32_t kChatAddGenerationPrompt = 0x1;
 constexpr uint32_t kChatEnableThinking = 0x2;
+
+// Incremental template writer: begin, then per message begin_message / append
+// (any number of pieces: text parts, folded file attachments) / end_message,
+// free text between messages, finish. Every append is checked against the
+// byte capacity (CapacityExceeded). Reference: ChatTemplateWriter
+// (crates/spark-text/src/chat_template.rs:76-215).
+class ChatWriter {
+ public:
+  ChatWriter(const std::string& style, size_t capacity);
+  void begin(const std::string& reasoning_effort, uint32_t flags);
+  void begin_message(const std::string& role);
+  void end_message(const std::string& role);
+  void append(const std::string& s);
+  void finish(uint32_t flags);
+  const std::string& text() const { return out_; }
+  size_t capacity() const { return cap_; }
+
+ private:
+  bool glm_;
+  size_t cap_;
+  std::string out_;
+};
+
 std::string render_chat(const std::vector<ChatMessage>& messages, const std::string& style, uint32_t flags,
                         const std::string& reasoning_effort, size_t capacity);
 
