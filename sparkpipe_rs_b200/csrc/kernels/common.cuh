@@ -1,7 +1,7 @@
 // Shared device helpers for the sm_100a kernels of this package.
 //
 // Everything here is a thin inline-PTX wrapper around Blackwell features:
-// TMA tensor copies (cp.async.bulk.tensor, never with .multicast::cluster),
+// TMA tensor copies (cp.async.bulk.tensor, each CTA loading its own tiles),
 // mbarriers with *bounded* waits, tcgen05 MMA / TMEM allocation / TMEM loads,
 // and thread-block-cluster shared-memory access (DSMEM).
 //
