@@ -143,4 +143,26 @@ void spec_verify(const int* draft, const int* target, int B, int L, float forced
 void decode_advance(const int* out_ids, int* ids, int* pos, int* ctx, int* slots, const int* block_table,
                     int max_blocks, int B, int block_size, cudaStream_t s);
 
+// ---- expert-parallel dispatch / combine over peer memory (ep.cu)
+constexpr int EP_MAX_RANKS = 8;
+constexpr int EP_MAX_KK = 16;
+// Every rank's EP buffer (mapped into this process) plus the byte offsets of
+// its regions; identical on all ranks except `rank`.
+struct EpArgs {
+  unsigned long long base[EP_MAX_RANKS];
+  long long off_recv_flag, off_comb_flag, off_recv_count, off_recv_meta, off_recv_x, off_comb_x, off_scratch;
+  int world, rank, cap, H, kk, n_routed, experts_per_rank, n_shared, moe_layers;
+};
+constexpr int EP_ARGS_WORDS = EP_MAX_RANKS + 7 + 9;
+void ep_dispatch(const void* x, int64_t ldx, const int* ids, int T, const EpArgs& a, const int64_t* epoch, int layer,
+                 cudaStream_t s);
+void ep_recv_align(const EpArgs& a, const int64_t* epoch, int layer, int bn, int* grp_rows, int* grp_tiles,
+                   int* src_row, int* comb_dst, long long budget, int* err, cudaStream_t s);
+void ep_gather(const EpArgs& a, const int64_t* epoch, int layer, const int* total, const int* src_row, void* xs,
+               int num_sms, cudaStream_t s);
+void ep_combine_send(const void* y, const int* total, const int* comb_dst, const EpArgs& a, const int64_t* epoch,
+                     int layer, int num_sms, cudaStream_t s);
+void ep_wait_combine(const EpArgs& a, const int64_t* epoch, int layer, long long budget, int* err, cudaStream_t s);
+void ep_advance(int64_t* epoch, cudaStream_t s);
+
 }  // namespace sp

@@ -5,6 +5,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -361,6 +362,111 @@ void decode_advance(const Tensor& out_ids, const Tensor& ids, const Tensor& pos,
                      (int)block_size, stream());
 }
 
+// ---------------------------------------------------------------- expert parallel
+// One cudaMalloc per rank holds every EP region; its IPC handle is exchanged
+// over the process group and each peer maps it (cudaIpcOpenMemHandle), so the
+// kernels address all ranks' buffers directly.
+Tensor ep_alloc(int64_t nbytes, int64_t device) {
+  const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, nbytes) == cudaSuccess, "ep: buffer allocation failed");
+  TORCH_CHECK(cudaMemset(p, 0, nbytes) == cudaSuccess, "ep: buffer clear failed");
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device);
+  return torch::from_blob(p, {nbytes}, [](void* q) { cudaFree(q); }, opts);
+}
+
+py::bytes ep_ipc_handle(const Tensor& buf) {
+  CHECK_CUDA(buf);
+  const c10::cuda::CUDAGuard guard(buf.device());
+  cudaIpcMemHandle_t h;
+  TORCH_CHECK(cudaIpcGetMemHandle(&h, buf.data_ptr()) == cudaSuccess, "ep: cudaIpcGetMemHandle failed");
+  return py::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+
+int64_t ep_ipc_open(const std::string& handle, int64_t device) {
+  TORCH_CHECK(handle.size() == sizeof(cudaIpcMemHandle_t), "ep: bad IPC handle size");
+  const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  TORCH_CHECK(e == cudaSuccess, "ep: cudaIpcOpenMemHandle failed: ", cudaGetErrorString(e));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ep_ipc_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
+
+sp::EpArgs ep_args(const std::vector<int64_t>& v) {
+  TORCH_CHECK((int)v.size() == sp::EP_ARGS_WORDS, "ep: argument vector must hold ", sp::EP_ARGS_WORDS, " words");
+  sp::EpArgs a{};
+  int i = 0;
+  for (int r = 0; r < sp::EP_MAX_RANKS; ++r) a.base[r] = (unsigned long long)v[i++];
+  a.off_recv_flag = v[i++]; a.off_comb_flag = v[i++]; a.off_recv_count = v[i++]; a.off_recv_meta = v[i++];
+  a.off_recv_x = v[i++]; a.off_comb_x = v[i++]; a.off_scratch = v[i++];
+  a.world = (int)v[i++]; a.rank = (int)v[i++]; a.cap = (int)v[i++]; a.H = (int)v[i++]; a.kk = (int)v[i++];
+  a.n_routed = (int)v[i++]; a.experts_per_rank = (int)v[i++]; a.n_shared = (int)v[i++]; a.moe_layers = (int)v[i++];
+  for (int r = 0; r < a.world; ++r) TORCH_CHECK(a.base[r] != 0 && a.base[r] % 256 == 0, "ep: bad rank base pointer");
+  return a;
+}
+
+void ep_dispatch(const Tensor& x, const Tensor& ids, const std::vector<int64_t>& args, const Tensor& epoch,
+                 int64_t layer) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_I32(ids); CHECK_CONTIG(ids);
+  TORCH_CHECK(x.stride(1) == 1 && x.stride(0) % 8 == 0, "ep: x rows must be contiguous and 16-byte aligned");
+  TORCH_CHECK(epoch.scalar_type() == at::kLong, "ep: epoch must be int64");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const sp::EpArgs a = ep_args(args);
+  TORCH_CHECK(x.size(1) == a.H && ids.numel() == x.size(0) * a.kk, "ep: shape mismatch");
+  sp::ep_dispatch(x.data_ptr(), x.stride(0), ids.data_ptr<int>(), (int)x.size(0), a, epoch.data_ptr<int64_t>(),
+                  (int)layer, stream());
+}
+
+void ep_recv_align(const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, int64_t bn,
+                   const Tensor& grp_rows, const Tensor& grp_tiles, const Tensor& src_row, const Tensor& comb_dst,
+                   int64_t budget_cycles) {
+  CHECK_I32(grp_rows); CHECK_I32(grp_tiles); CHECK_I32(src_row); CHECK_I32(comb_dst);
+  const c10::cuda::CUDAGuard guard(grp_rows.device());
+  const sp::EpArgs a = ep_args(args);
+  TORCH_CHECK(grp_rows.numel() >= a.experts_per_rank + a.n_shared + 1, "ep: grp_rows too small");
+  TORCH_CHECK(src_row.numel() >= (int64_t)a.world * a.cap * std::min(a.kk, a.experts_per_rank + a.n_shared),
+              "ep: pair buffers too small");
+  sp::ep_recv_align(a, epoch.data_ptr<int64_t>(), (int)layer, (int)bn, grp_rows.data_ptr<int>(),
+                    grp_tiles.data_ptr<int>(), src_row.data_ptr<int>(), comb_dst.data_ptr<int>(), budget_cycles,
+                    err_word(), stream());
+}
+
+void ep_gather(const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, const Tensor& total,
+               const Tensor& src_row, const Tensor& xs) {
+  CHECK_BF16(xs); CHECK_CONTIG(xs); CHECK_I32(src_row); CHECK_I32(total);
+  const c10::cuda::CUDAGuard guard(xs.device());
+  const sp::EpArgs a = ep_args(args);
+  TORCH_CHECK(xs.size(1) == a.H, "ep: xs width");
+  sp::ep_gather(a, epoch.data_ptr<int64_t>(), (int)layer, total.data_ptr<int>(), src_row.data_ptr<int>(),
+                xs.data_ptr(), num_sms(), stream());
+}
+
+void ep_combine_send(const Tensor& y, const Tensor& total, const Tensor& comb_dst, const std::vector<int64_t>& args,
+                     const Tensor& epoch, int64_t layer) {
+  CHECK_BF16(y); CHECK_CONTIG(y); CHECK_I32(total); CHECK_I32(comb_dst);
+  const c10::cuda::CUDAGuard guard(y.device());
+  const sp::EpArgs a = ep_args(args);
+  TORCH_CHECK(y.size(1) == a.H, "ep: y width");
+  sp::ep_combine_send(y.data_ptr(), total.data_ptr<int>(), comb_dst.data_ptr<int>(), a, epoch.data_ptr<int64_t>(),
+                      (int)layer, num_sms(), stream());
+}
+
+void ep_wait_combine(const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, int64_t budget_cycles) {
+  const c10::cuda::CUDAGuard guard(epoch.device());
+  const sp::EpArgs a = ep_args(args);
+  sp::ep_wait_combine(a, epoch.data_ptr<int64_t>(), (int)layer, budget_cycles, err_word(), stream());
+}
+
+void ep_advance(const Tensor& epoch) {
+  TORCH_CHECK(epoch.scalar_type() == at::kLong && epoch.is_cuda(), "ep: epoch must be a CUDA int64 tensor");
+  const c10::cuda::CUDAGuard guard(epoch.device());
+  sp::ep_advance(epoch.data_ptr<int64_t>(), stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -388,4 +494,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_word", &status_word);
   m.def("clear_status", &clear_status);
   m.def("num_sms", &num_sms);
+  m.def("ep_alloc", &ep_alloc);
+  m.def("ep_ipc_handle", &ep_ipc_handle);
+  m.def("ep_ipc_open", &ep_ipc_open);
+  m.def("ep_ipc_close", &ep_ipc_close);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_recv_align", &ep_recv_align);
+  m.def("ep_gather", &ep_gather);
+  m.def("ep_combine_send", &ep_combine_send);
+  m.def("ep_wait_combine", &ep_wait_combine);
+  m.def("ep_advance", &ep_advance);
+  m.attr("EP_ARGS_WORDS") = sp::EP_ARGS_WORDS;
+  m.attr("EP_MAX_RANKS") = sp::EP_MAX_RANKS;
 }

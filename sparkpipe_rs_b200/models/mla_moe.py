@@ -78,11 +78,16 @@ def _moe_block_n(rows: int, experts: int) -> int:
 
 class MLAMoEModel:
     def __init__(self, cfg: MLAMoEConfig, weights: dict[str, torch.Tensor] | None = None, device="cuda",
-                 seed: int = 0, max_positions: int | None = None):
+                 seed: int = 0, max_positions: int | None = None, ep=None):
+        """``ep``: an ``ExpertParallel`` rank; the model then holds only that
+        rank's routed experts (plus the shared ones) and runs its MoE layers
+        through the peer-memory expert all-to-all."""
         self.cfg = cfg
         self.device = torch.device(device)
+        self.ep = ep
         if weights is None:
-            weights = init_weights(cfg, seed=seed, device=self.device, dtype=torch.bfloat16)
+            weights = init_weights(cfg, seed=seed, device=self.device, dtype=torch.bfloat16,
+                                   experts=ep.local_expert_range() if ep is not None else None)
         self.w = {k: v.to(self.device) for k, v in weights.items()}
         derive_decode_weights(cfg, self.w)
         # routed + shared expert gate/up weights in the fused-SwiGLU tile order
@@ -182,6 +187,9 @@ class MLAMoEModel:
         ids, wts = ops.moe_topk(logits, w[p + "gate_bias"] if sigmoid else None, k, 1 if sigmoid else 0,
                                 c.norm_topk_prob, c.routed_scaling_factor, n_shared=S)
         kk = k + S
+        if self.ep is not None:
+            bn = _moe_block_n(T * kk, self.ep.n_local)
+            return self.ep.moe(i, xn, ids, wts, w[p + "e_w13"], w[p + "e_w2"], bn, self.fused_swiglu)
         bn = _moe_block_n(T * kk, E + S)
         grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E + S, bn)
         xs = ops.gather_rows(xn, sorted_tok)
@@ -238,8 +246,12 @@ class MLAMoEModel:
         if return_hidden:
             if pending is not None:
                 self._residual_norm(pending, res, w["final_norm"], xn)
+            if self.ep is not None:
+                self.ep.end_step()
             return res
         self._residual_norm(pending, res, w["final_norm"], xn)
+        if self.ep is not None:
+            self.ep.end_step()
         sel = xn if fb.logits_idx is None else ops.gather_rows(xn, fb.logits_idx)
         return ops.linear(sel, w["lm_head"])
 

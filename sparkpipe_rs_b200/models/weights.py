@@ -62,8 +62,11 @@ def _is_norm(name: str) -> bool:
 
 
 def init_weights(cfg: MLAMoEConfig, seed: int = 0, device="cpu", dtype=torch.bfloat16,
-                 layers: list[int] | None = None) -> dict[str, torch.Tensor]:
-    """Random-init weights. ``layers`` restricts which decoder layers are created."""
+                 layers: list[int] | None = None, experts: tuple[int, int] | None = None) -> dict[str, torch.Tensor]:
+    """Random-init weights. ``layers`` restricts which decoder layers are created;
+    ``experts`` = (lo, hi) keeps only routed experts lo..hi-1 (plus every shared
+    expert) of the expert tensors, as one expert-parallel rank holds them. The
+    kept rows are bit-identical to the same rows of the full tensors."""
     shapes = weight_shapes(cfg)
     out: dict[str, torch.Tensor] = {}
     dev = torch.device(device)
@@ -85,6 +88,9 @@ def init_weights(cfg: MLAMoEConfig, seed: int = 0, device="cpu", dtype=torch.bfl
             t.normal_(0.0, cfg.init_std, generator=g)
         else:
             t.copy_(torch.empty(shape, dtype=torch.float32, device=dev).normal_(0.0, cfg.init_std, generator=g))
+        if experts is not None and (name.endswith("e_w13") or name.endswith("e_w2")):
+            lo, hi = experts
+            t = torch.cat([t[lo:hi], t[cfg.n_routed_experts:]]).contiguous()
         out[name] = t
     return out
 

@@ -1,0 +1,183 @@
+"""Expert parallelism: routed experts split over the ranks of one box, with the
+token all-to-all done by fused peer-memory kernels (``csrc/kernels/ep.cu``).
+
+Attention stays data-parallel (every rank decodes its own requests); rank r
+holds routed experts [r*El, (r+1)*El) plus all shared experts. Per MoE layer:
+
+    dispatch -> recv/align -> gather -> grouped GEMM (gate/up + SwiGLU) ->
+    grouped GEMM (down) -> combine-send -> combine-wait
+
+and the weighted sum of the returned rows is fused into the next residual add
++ RMSNorm, exactly like the single-GPU path. All of it is stream-ordered device
+work (CUDA-graph capturable): the layer epoch lives in device memory and is
+advanced once per forward by ``end_step``.
+
+Buffers: one ``cudaMalloc`` per rank, mapped by every peer through CUDA IPC.
+Two parity halves (per MoE layer index) make back-to-back layers race-free.
+
+``ExpertParallel.emulated(W, ...)`` builds W ranks inside one process on one
+GPU (peer pointers are the other local buffers); driving the phases
+rank-by-rank in phase order exercises every kernel without any kernel waiting
+on a concurrently running one.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _ext, ops
+
+DEFAULT_BUDGET_CYCLES = 20_000_000_000  # ~10 s at 2 GHz: far above any healthy wait
+
+
+def _align(x: int, a: int = 256) -> int:
+    return (x + a - 1) // a * a
+
+
+def ep_layout(world: int, cap: int, hidden: int, kk: int) -> dict:
+    """Byte offsets of the EP regions inside one rank's buffer."""
+    off = {}
+    pos = 0
+
+    def region(name, nbytes):
+        nonlocal pos
+        off[name] = pos
+        pos = _align(pos + nbytes)
+
+    max_ranks = 8
+    region("recv_flag", 2 * max_ranks * 8)
+    region("comb_flag", 2 * max_ranks * 8)
+    region("recv_count", 2 * max_ranks * 4)
+    region("scratch", 64 * 4)
+    region("recv_meta", 2 * world * cap * (2 + 2 * kk) * 4)
+    region("recv_x", 2 * world * cap * hidden * 2)
+    region("comb_x", 2 * cap * kk * hidden * 2)
+    off["total"] = pos
+    return off
+
+
+class ExpertParallel:
+    def __init__(self, cfg, rank: int, world: int, cap_tokens: int, device, group=None,
+                 budget_cycles: int = DEFAULT_BUDGET_CYCLES):
+        assert cfg.n_routed_experts % world == 0, "routed experts must split evenly over the ranks"
+        assert 1 <= world <= 8
+        self.cfg, self.rank, self.world, self.cap = cfg, rank, world, cap_tokens
+        self.device = torch.device(device)
+        self.budget = int(budget_cycles)
+        self.kk = cfg.num_experts_per_tok + cfg.n_shared_experts
+        self.El = cfg.n_routed_experts // world
+        self.n_local = self.El + cfg.n_shared_experts
+        self.H = cfg.hidden_size
+        self.moe_layers = [i for i in range(cfg.num_layers) if cfg.is_moe_layer(i)]
+        self.moe_index = {layer: j for j, layer in enumerate(self.moe_layers)}
+        # even layer count per step -> MoE layer j always uses buffer parity j & 1
+        self.layers_per_step = len(self.moe_layers) + (len(self.moe_layers) & 1)
+        self.layout = ep_layout(world, cap_tokens, self.H, self.kk)
+        K = _ext.kernels()
+        self.K = K
+        self.buf = K.ep_alloc(self.layout["total"], self.device.index or 0)
+        self._opened: list[int] = []
+        self.bases = [0] * 8
+        self.bases[rank] = self.buf.data_ptr()
+        if group is not None:
+            import torch.distributed as dist
+            handles = [None] * world
+            dist.all_gather_object(handles, K.ep_ipc_handle(self.buf), group=group)
+            for r in range(world):
+                if r != rank:
+                    p = K.ep_ipc_open(handles[r], self.device.index or 0)
+                    self._opened.append(p)
+                    self.bases[r] = p
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=self.device)
+        dev = self.device
+        max_pairs = world * cap_tokens * min(self.kk, self.n_local)
+        self.grp_rows = torch.zeros(self.n_local + 1, dtype=torch.int32, device=dev)
+        self.grp_tiles = torch.zeros(self.n_local + 1, dtype=torch.int32, device=dev)
+        self.src_row = torch.zeros(max_pairs, dtype=torch.int32, device=dev)
+        self.comb_dst = torch.zeros(max_pairs, dtype=torch.int32, device=dev)
+        self.xs = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
+        F = cfg.moe_intermediate_size
+        self.act = torch.zeros(max_pairs, F, dtype=torch.bfloat16, device=dev)
+        self.y = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
+        self.ident = torch.arange(cap_tokens * self.kk, dtype=torch.int32, device=dev)
+        o = self.layout["comb_x"]
+        n = 2 * cap_tokens * self.kk * self.H * 2
+        self.comb = self.buf[o:o + n].view(torch.bfloat16).view(2, cap_tokens * self.kk, self.H)
+
+    @classmethod
+    def emulated(cls, cfg, world: int, cap_tokens: int, device, budget_cycles: int = DEFAULT_BUDGET_CYCLES):
+        ranks = [cls(cfg, r, world, cap_tokens, device, budget_cycles=budget_cycles) for r in range(world)]
+        bases = [r.buf.data_ptr() for r in ranks] + [0] * (8 - world)
+        for r in ranks:
+            r.bases = list(bases)
+        return ranks
+
+    def close(self):
+        for p in self._opened:
+            self.K.ep_ipc_close(p)
+        self._opened.clear()
+
+    # ------------------------------------------------------------------ args
+    def args(self) -> list[int]:
+        L = self.layout
+        c = self.cfg
+        return (list(self.bases) + [L["recv_flag"], L["comb_flag"], L["recv_count"], L["recv_meta"], L["recv_x"],
+                                    L["comb_x"], L["scratch"]] +
+                [self.world, self.rank, self.cap, self.H, self.kk, c.n_routed_experts, self.El,
+                 c.n_shared_experts, self.layers_per_step])
+
+    def local_expert_range(self) -> tuple[int, int]:
+        return self.rank * self.El, (self.rank + 1) * self.El
+
+    # ------------------------------------------------------------------ phases
+    def dispatch(self, layer: int, xn: torch.Tensor, ids: torch.Tensor):
+        self.K.ep_dispatch(xn, ids, self.args(), self.epoch, self.moe_index[layer])
+        ops._count(1)
+
+    def receive(self, layer: int, bn: int):
+        j = self.moe_index[layer]
+        self.K.ep_recv_align(self.args(), self.epoch, j, bn, self.grp_rows, self.grp_tiles, self.src_row,
+                             self.comb_dst, self.budget)
+        self.K.ep_gather(self.args(), self.epoch, j, self.grp_rows[self.n_local:], self.src_row, self.xs)
+        ops._count(2)
+
+    def experts(self, w13: torch.Tensor, w2: torch.Tensor, bn: int, fused_swiglu: bool = True):
+        if fused_swiglu:
+            ops.grouped_gemm(w13, self.xs, self.act, self.grp_rows, self.grp_tiles, self.n_local, bn, swiglu=True)
+        else:
+            h13 = torch.empty(self.xs.shape[0], 2 * self.act.shape[1], dtype=torch.bfloat16, device=self.device)
+            ops.grouped_gemm(w13, self.xs, h13, self.grp_rows, self.grp_tiles, self.n_local, bn)
+            ops.silu_mul(h13, out=self.act)
+        ops.grouped_gemm(w2, self.act, self.y, self.grp_rows, self.grp_tiles, self.n_local, bn)
+
+    def combine_send(self, layer: int):
+        self.K.ep_combine_send(self.y, self.grp_rows[self.n_local:], self.comb_dst, self.args(), self.epoch,
+                               self.moe_index[layer])
+        ops._count(1)
+
+    def combine_wait(self, layer: int, T: int, wts: torch.Tensor):
+        j = self.moe_index[layer]
+        self.K.ep_wait_combine(self.args(), self.epoch, j, self.budget)
+        ops._count(1)
+        return ("combine", self.comb[j & 1], self.ident[: T * self.kk], wts, self.kk)
+
+    def end_step(self):
+        self.K.ep_advance(self.epoch)
+        ops._count(1)
+
+    # ------------------------------------------------------------------ one layer
+    def moe(self, layer: int, xn: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, w13: torch.Tensor,
+            w2: torch.Tensor, bn: int, fused_swiglu: bool = True):
+        """Runs one MoE layer for this rank's tokens; returns the deferred combine."""
+        if xn.shape[0] > self.cap:
+            raise ValueError(f"expert parallel: {xn.shape[0]} tokens exceed the buffer capacity {self.cap}")
+        self.dispatch(layer, xn, ids)
+        self.receive(layer, bn)
+        self.experts(w13, w2, bn, fused_swiglu)
+        self.combine_send(layer)
+        return self.combine_wait(layer, xn.shape[0], wts)
+
+
+def block_n_for(tokens_per_rank: int, kk: int, n_local: int) -> int:
+    """Tile width of the expert GEMM from the expected rows per local expert."""
+    from ..models.mla_moe import _moe_block_n
+    return _moe_block_n(tokens_per_rank * kk, n_local)

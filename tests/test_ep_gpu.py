@@ -1,0 +1,190 @@
+"""Expert-parallel MoE over peer memory (csrc/kernels/ep.cu).
+
+* emulated ranks on one GPU: W ExpertParallel ranks in one process, driven
+  phase by phase (every rank's dispatch, then every rank's receive, ...), so no
+  kernel waits on a kernel that has not finished; the combined output of every
+  rank must equal the single-GPU MoE path bit for bit;
+* the bounded wait: a flag that nothing sets ends the receive with the peer
+  timeout status, an empty expert schedule and a usable context;
+* two real ranks on two GPUs (skipped with fewer GPUs): the expert-parallel
+  model's logits equal the single-GPU model's.
+"""
+import os
+import socket
+
+import pytest
+import torch
+
+from sparkpipe_rs_b200 import ops
+from sparkpipe_rs_b200.models.config import tiny, v2_lite
+from sparkpipe_rs_b200.models.mla_moe import _moe_block_n
+from sparkpipe_rs_b200.models.weights import init_weights
+from sparkpipe_rs_b200.parallel.expert_parallel import ExpertParallel
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg():
+    return tiny().replace(num_layers=3, hidden_size=512, n_routed_experts=16, num_experts_per_tok=4,
+                          n_shared_experts=1, moe_intermediate_size=128, scoring_func="sigmoid",
+                          norm_topk_prob=True, routed_scaling_factor=2.5)
+
+
+def _model_cfg():
+    # MLA dims the GPU attention kernels support (kv_lora 512), small everything else
+    return v2_lite().replace(name="small-mla-moe", num_layers=4, hidden_size=1024, n_routed_experts=16,
+                             num_experts_per_tok=4, moe_intermediate_size=256, intermediate_size=2048,
+                             n_shared_experts=1, vocab_size=4096, first_k_dense_replace=1, init_std=0.05)
+
+
+def _local_moe(cfg, xn, w13, w2, ids, wts, res, gamma, eps):
+    E, S = cfg.n_routed_experts, cfg.n_shared_experts
+    kk = cfg.num_experts_per_tok + S
+    T = xn.shape[0]
+    bn = _moe_block_n(T * kk, E + S)
+    grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E + S, bn)
+    xs = ops.gather_rows(xn, sorted_tok)
+    act = torch.empty(T * kk, cfg.moe_intermediate_size, dtype=torch.bfloat16, device=xn.device)
+    ops.grouped_gemm(w13, xs, act, grp_rows, grp_tiles, E + S, bn, swiglu=True)
+    y = torch.empty(T * kk, cfg.hidden_size, dtype=torch.bfloat16, device=xn.device)
+    ops.grouped_gemm(w2, act, y, grp_rows, grp_tiles, E + S, bn)
+    out = torch.empty_like(xn)
+    ops.combine_add_rmsnorm(y, inv_pos, wts, res, gamma, out, kk, eps)
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_emulated_ranks_match_single_gpu(world):
+    torch.manual_seed(0)
+    dev = torch.device("cuda")
+    cfg = _cfg()
+    E, S, H = cfg.n_routed_experts, cfg.n_shared_experts, cfg.hidden_size
+    kk = cfg.num_experts_per_tok + S
+    full = init_weights(cfg, seed=3, device=dev)
+    for k in list(full):
+        if k.endswith("e_w13"):
+            full[k] = ops.interleave_gate_up(full[k])
+    ranks = ExpertParallel.emulated(cfg, world, cap_tokens=48, device=dev)
+    El = E // world
+    local = [{k: torch.cat([v[r * El:(r + 1) * El], v[E:]]).contiguous() for k, v in full.items()
+              if k.endswith("e_w13") or k.endswith("e_w2")} for r in range(world)]
+    tokens = [7, 0, 48, 21][:world]
+    gamma = torch.rand(H, device=dev, dtype=torch.bfloat16) + 0.5
+    ops.clear_status()
+    for step in range(2):
+        for layer in ranks[0].moe_layers:
+            p = f"l{layer}."
+            xs, ids, wts, res = [], [], [], []
+            for r in range(world):
+                x = (torch.randn(tokens[r], H, device=dev) * 0.5).to(torch.bfloat16)
+                logits = (x.float() @ full[p + "gate"].float().t()).contiguous()
+                bias = torch.randn(E, device=dev) * 0.1
+                i, w_ = ops.moe_topk(logits, bias, cfg.num_experts_per_tok, 1, True, 2.5, n_shared=S)
+                xs.append(x); ids.append(i); wts.append(w_)
+                res.append((torch.randn(tokens[r], H, device=dev)).to(torch.bfloat16))
+            bn = _moe_block_n(max(tokens) * kk, ranks[0].n_local)
+            for r in range(world):
+                ranks[r].dispatch(layer, xs[r], ids[r])
+            for r in range(world):
+                ranks[r].receive(layer, bn)
+            for r in range(world):
+                ranks[r].experts(local[r][p + "e_w13"], local[r][p + "e_w2"], bn)
+            for r in range(world):
+                ranks[r].combine_send(layer)
+            for r in range(world):
+                if tokens[r] == 0:
+                    ranks[r].combine_wait(layer, 0, wts[r])
+                    continue
+                pend = ranks[r].combine_wait(layer, tokens[r], wts[r])
+                res_ep = res[r].clone()
+                out_ep = torch.empty_like(xs[r])
+                ops.combine_add_rmsnorm(pend[1], pend[2], pend[3], res_ep, gamma, out_ep, kk, cfg.rms_norm_eps)
+                res_ref = res[r].clone()
+                out_ref = _local_moe(cfg, xs[r], full[p + "e_w13"], full[p + "e_w2"], ids[r], wts[r], res_ref,
+                                     gamma, cfg.rms_norm_eps)
+                torch.cuda.synchronize()
+                assert ops.status_word() == 0
+                assert torch.equal(res_ep, res_ref), (step, layer, r, (res_ep.float() - res_ref.float()).abs().max())
+                assert torch.equal(out_ep, out_ref)
+        for r in ranks:
+            r.end_step()
+    torch.cuda.synchronize()
+    assert ops.status_word() == 0
+
+
+def test_receive_wait_times_out_with_status():
+    dev = torch.device("cuda")
+    cfg = _cfg()
+    ranks = ExpertParallel.emulated(cfg, 2, cap_tokens=8, device=dev, budget_cycles=2_000_000)  # ~1 ms
+    ops.clear_status()
+    x = torch.randn(4, cfg.hidden_size, device=dev).to(torch.bfloat16)
+    ids = torch.zeros(4, ranks[0].kk, dtype=torch.int32, device=dev)
+    layer = ranks[0].moe_layers[0]
+    ranks[0].dispatch(layer, x, ids)  # rank 1 never dispatches: its flag stays unset
+    ranks[0].grp_rows.fill_(7)
+    ranks[0].receive(layer, 16)
+    torch.cuda.synchronize()
+    assert ops.status_word() == 4  # peer wait timeout
+    assert int(ranks[0].grp_rows.sum()) == 0  # empty schedule: downstream kernels do nothing
+    ops.clear_status()
+    torch.cuda.synchronize()
+    assert ops.status_word() == 0
+    y = torch.ones(4, device=dev) + 1  # the context is still usable
+    assert float(y.sum()) == 8.0
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _two_rank_worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    from sparkpipe_rs_b200.models.mla_moe import ForwardBatch, KVCache, MLAMoEModel
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        cfg = _model_cfg()
+        ep = ExpertParallel(cfg, rank, world, cap_tokens=64, device=dev, group=dist.group.WORLD)
+        m_ep = MLAMoEModel(cfg, seed=5, device=dev, ep=ep)
+        m_ref = MLAMoEModel(cfg, seed=5, device=dev)
+        T = 12 + 5 * rank
+        g = torch.Generator().manual_seed(rank)
+        ids = torch.randint(0, cfg.vocab_size, (T,), generator=g).to(torch.int32).to(dev)
+        pos = torch.arange(T, dtype=torch.int32, device=dev)
+        outs = []
+        for m in (m_ep, m_ref):
+            cache = KVCache(cfg, num_blocks=4, block_size=64, device=dev)
+            cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+            fb = ForwardBatch(mode="prefill", token_ids=ids, positions=pos, slot_mapping=pos.clone(), cu_q=cu,
+                              cu_k=cu, max_q=T)
+            dist.barrier()
+            outs.append(m.forward(fb, cache).float())
+            torch.cuda.synchronize()
+        ok = torch.equal(outs[0], outs[1])
+        q.put((rank, ok, float((outs[0] - outs[1]).abs().max()), ops.status_word()))
+        dist.barrier()
+        ep.close()
+        dist.destroy_process_group()
+    except Exception as e:  # report, never hang the parent
+        q.put((rank, False, repr(e), -1))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_expert_parallel_model_matches_single_gpu():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_two_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, ok, diff, status in sorted(results, key=lambda r: r[0]):
+        assert ok and status == 0, (rank, diff, status)
