@@ -43,14 +43,18 @@ def parse_args():
     ap.add_argument("--output", type=int, default=256)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--parallel", default="auto", choices=["auto", "dp", "ep"],
+                    help="N>1: dp = replicated model per GPU; ep = data-parallel attention + experts split "
+                         "over the GPUs (auto: ep when the experts divide evenly)")
+    ap.add_argument("--prefill-chunk", type=int, default=8192, help="max tokens per prefill forward")
     return ap.parse_args()
 
 
 def reference_arm(args):
     print(json.dumps({
         "impl": "reference",
-        "unavailable": "the reference (awdemos/sparkpipe-rs) is a Rust host-side orchestration plane with no GPU "
-                       "code in-tree (kernels live in an absent C/CUDA tree) and no Rust toolchain exists here",
+        "unavailable": "the reference is a Rust Cargo workspace: pip reports it is not installable (no setup.py or "
+                       "pyproject.toml), this image has no Rust toolchain, and its GPU kernels are not in its tree",
         "metric": METRIC, "n_gpus": args.gpus,
     }))
 
@@ -75,13 +79,24 @@ def main():
     from sparkpipe_rs_b200 import ops
     from sparkpipe_rs_b200.models.config import get_config
     from sparkpipe_rs_b200.models.mla_moe import DecodeGraph, ForwardBatch, KVCache, MLAMoEModel
+    from sparkpipe_rs_b200.parallel.expert_parallel import ExpertParallel
     from sparkpipe_rs_b200.utils.clocks import ClockSampler
 
     cfg = get_config(args.model)
     B, P = args.batch, args.prompt
     bs = 64
+    par = args.parallel
+    if par == "auto":
+        par = "ep" if world > 1 and cfg.n_routed_experts % world == 0 else "dp"
+    seqs_per_chunk = max(1, min(B, args.prefill_chunk // P))
+    ep = None
+    if par == "ep" and world > 1:
+        ep = ExpertParallel(cfg, rank, world, max(B, seqs_per_chunk * P), dev, group=dist.group.WORLD)
     torch.manual_seed(1234 + rank)
-    model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=P + args.output + args.warmup + args.steps + 64)
+    model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=P + args.output + args.warmup + args.steps + 64,
+                        ep=ep)
+    weight_gb = sum(t.numel() * t.element_size() for t in model.w.values()) / 1e9
+    parallelism = f"dp{world}-ep{world}" if ep is not None else f"dp{world}"
 
     # ------------------------------------------------------------ device-timed decode
     total_ctx = P + args.warmup + args.steps + 2
@@ -90,15 +105,19 @@ def main():
     block_table = torch.arange(B * bps, dtype=torch.int32, device=dev).view(B, bps)
     g = torch.Generator(device="cpu").manual_seed(rank)
     prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=g, dtype=torch.int32)
-    ids = prompts.flatten().to(dev)
-    pos = torch.arange(P, dtype=torch.int32, device=dev).repeat(B)
     slots = (block_table[:, :, None] * bs + torch.arange(bs, device=dev, dtype=torch.int32)).view(B, -1)[:, :P]
-    cu = torch.arange(0, (B + 1) * P, P, dtype=torch.int32, device=dev)
-    fb = ForwardBatch(mode="prefill", token_ids=ids, positions=pos, slot_mapping=slots.flatten().contiguous(),
-                      cu_q=cu, cu_k=cu, max_q=P, logits_idx=(cu[1:] - 1).contiguous())
-    logits = model.forward(fb, cache)
-    first = ops.sample_tokens(logits)
-    del logits, fb
+    first = torch.empty(B, dtype=torch.int32, device=dev)
+    for b0 in range(0, B, seqs_per_chunk):  # prefill in chunks of whole prompts
+        nb = min(seqs_per_chunk, B - b0)
+        ids = prompts[b0:b0 + nb].flatten().to(dev)
+        pos = torch.arange(P, dtype=torch.int32, device=dev).repeat(nb)
+        cu = torch.arange(0, (nb + 1) * P, P, dtype=torch.int32, device=dev)
+        fb = ForwardBatch(mode="prefill", token_ids=ids, positions=pos,
+                          slot_mapping=slots[b0:b0 + nb].flatten().contiguous(), cu_q=cu, cu_k=cu, max_q=P,
+                          logits_idx=(cu[1:] - 1).contiguous())
+        logits = model.forward(fb, cache)
+        first[b0:b0 + nb] = ops.sample_tokens(logits)
+        del logits, fb
     torch.cuda.synchronize()
 
     graph = DecodeGraph(model, cache, B, bps, total_ctx, use_graph=not args.no_graph, self_advance=True)
@@ -151,6 +170,7 @@ def main():
 
         engine = LLMEngine(cfg, EngineConfig(max_batch=B, block_size=bs, max_model_len=P + args.output + 64,
                                              num_blocks=B * math.ceil((P + args.output + 64) / bs) + 64,
+                                             max_prefill_tokens=seqs_per_chunk * P,
                                              use_cuda_graph=not args.no_graph),
                            model=model, device=dev)
         prompts_l = [p.tolist() for p in prompts]
@@ -193,8 +213,8 @@ def main():
                 "seq_len": P,
                 "output_len": args.output,
                 "kv_block": bs,
-                "parallelism": f"dp{world}",
-                "l2": "inputs larger than L2: each decode step streams ~30 GB of weights",
+                "parallelism": parallelism,
+                "l2": f"inputs larger than L2: each decode step streams {weight_gb:.1f} GB of weights per GPU",
             },
             "clocks": clk.summary(),
             "gpu_launches": per_step_launches * args.steps,
@@ -206,6 +226,8 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        if ep is not None:
+            ep.close()
         dist.destroy_process_group()
     return 0
 

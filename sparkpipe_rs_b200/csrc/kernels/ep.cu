@@ -4,32 +4,39 @@
 // experts are split evenly over the W ranks (rank r owns experts
 // [r*El, (r+1)*El)), shared experts are replicated and run locally. Every rank
 // maps every peer's EP buffer (CUDA IPC), so the kernels below move data with
-// plain 16-byte loads / stores to peer addresses; there are no copy engines,
-// no NCCL calls and no host synchronisation in the per-layer path.
+// plain loads / stores to peer addresses; there are no copy engines, no NCCL
+// calls and no host synchronisation in the per-layer path.
 //
-// Per MoE layer (epoch e = step * moe_layers + layer, buffer parity e & 1):
-//   ep_dispatch     one CTA per local token: for each distinct destination rank
-//                   of its top-k experts, reserve a row in that rank's receive
-//                   region for this source, store the hidden row and its
-//                   (token, local expert, k-slot) list there. The last CTA
-//                   publishes the per-destination row counts and raises each
-//                   destination's flag (release, system scope).
-//   ep_recv_align   one CTA: waits (bounded) for all W flags, builds the
-//                   expert-sorted pair list of everything received, the
-//                   grouped-GEMM tile schedule and the combine destinations.
-//   ep_gather       copies received rows into expert-sorted order (local HBM).
-//   grouped GEMMs   (gemm_tcgen05.cu) gate/up with fused SwiGLU, then down.
-//   ep_combine_send stores each output row straight into its source rank's
-//                   combine buffer at (token, k-slot); the last CTA raises the
-//                   combine flag on every rank.
-//   ep_wait         waits (bounded) for all W combine flags; the weighted sum is
-//                   fused into the next residual add + RMSNorm (moe.cu).
+// Transport: every word that crosses to a peer is a 64-bit store of
+// (payload:32 | tag:32) with tag = low 32 bits of (epoch + 1). A reader polls
+// the word itself until the tag matches, so a 64-bit single-copy-atomic store
+// is both the data and its own arrival flag: no system-scope fences, no flag
+// words, no ordering between words. (A system-scope fence costs microseconds
+// on this machine; a layer needs several of them otherwise.) Rows therefore
+// travel at twice their size, which is irrelevant at decode batch sizes.
+//
+// Per MoE layer (epoch e = step * layers_per_step + layer, buffer parity e & 1):
+//   ep_dispatch            grid (destination, 8-token chunk): stores each token
+//                          routed to that destination once (row + (token, local
+//                          expert, k-slot) list) into the chunk's own slots of
+//                          this source's region there, plus the chunk's row
+//                          count (and, for chunk 0, the chunk count).
+//   ep_recv_align          one CTA: reads every source's counts and lists and
+//                          builds the expert-sorted pair list, the grouped-GEMM
+//                          tile schedule and the combine destinations.
+//   ep_gather              received rows -> expert-sorted bf16 rows (local HBM).
+//   grouped GEMMs          (gemm_tcgen05.cu) gate/up with fused SwiGLU, then down.
+//   ep_combine_send        grid (destination, 16): each output row goes straight
+//                          into its source rank's combine slot (token, k-slot).
+//   ep_combine_add_rmsnorm the source sums its k slots per token (router
+//                          weights), adds the residual and applies the next
+//                          RMSNorm, reading the slots as they arrive.
 //
 // Why two buffers suffice: rank A dispatches layer e+2 only after it consumed
-// the combine of layer e+1, which rank B sent only after gathering layer e+1
-// (and so layer e). Every wait is bounded (clock64 budget); on a timeout the
-// kernel records kErrWaitTimeoutPeer in the status word, empties its outputs
-// and returns, so the context stays usable and the host raises.
+// the combine of layer e+1, which rank B sent only after it received layer e+1
+// (and so layer e) completely. Every poll is bounded (clock64 budget); on a
+// timeout the kernel records kErrWaitTimeoutPeer in the status word, empties
+// its outputs and returns, so the context stays usable and the host raises.
 //
 // Reference: the fused-MoE and expert-queue seams of the reference
 // (crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_resident_decode_stage.h:321-342,
@@ -42,116 +49,162 @@
 namespace sp {
 
 using bf16 = __nv_bfloat16;
+using u64 = unsigned long long;
 
 namespace {
-SP_DEVI void st_release_sys(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+SP_DEVI u64 ll_word(uint32_t payload, uint32_t tag) { return (u64(tag) << 32) | payload; }
+SP_DEVI void st_ll(u64* p, u64 w) { asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory"); }
+SP_DEVI void st_ll2(u64* p, u64 a, u64 b) {  // two independent 64-bit elements (each single-copy atomic)
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
-SP_DEVI uint64_t ld_acquire_sys(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+SP_DEVI u64 ld_ll(const u64* p) {
+  u64 v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-SP_DEVI uint8_t* rank_base(const EpArgs& a, int r) { return reinterpret_cast<uint8_t*>(a.base[r]); }
-SP_DEVI uint64_t* recv_flag(const EpArgs& a, int r, int buf, int src) {
-  return reinterpret_cast<uint64_t*>(rank_base(a, r) + a.off_recv_flag) + buf * EP_MAX_RANKS + src;
+SP_DEVI void ld_ll2(const u64* p, u64& a, u64& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
-SP_DEVI uint64_t* comb_flag(const EpArgs& a, int r, int buf, int src) {
-  return reinterpret_cast<uint64_t*>(rank_base(a, r) + a.off_comb_flag) + buf * EP_MAX_RANKS + src;
-}
-SP_DEVI int* recv_count(const EpArgs& a, int r, int buf, int src) {
-  return reinterpret_cast<int*>(rank_base(a, r) + a.off_recv_count) + buf * EP_MAX_RANKS + src;
-}
-SP_DEVI int* recv_meta(const EpArgs& a, int r, int buf, int src, int row) {
-  const int mi = 2 + 2 * a.kk;
-  return reinterpret_cast<int*>(rank_base(a, r) + a.off_recv_meta) +
-         ((int64_t(buf) * a.world + src) * a.cap + row) * mi;
-}
-SP_DEVI bf16* recv_row(const EpArgs& a, int r, int buf, int src, int row) {
-  return reinterpret_cast<bf16*>(rank_base(a, r) + a.off_recv_x) + ((int64_t(buf) * a.world + src) * a.cap + row) * a.H;
-}
-SP_DEVI bf16* comb_row(const EpArgs& a, int r, int buf, int slot) {
-  return reinterpret_cast<bf16*>(rank_base(a, r) + a.off_comb_x) + (int64_t(buf) * a.cap * a.kk + slot) * a.H;
-}
-SP_DEVI int* local_scratch(const EpArgs& a) { return reinterpret_cast<int*>(rank_base(a, a.rank) + a.off_scratch); }
+SP_DEVI uint32_t tag_of(u64 w) { return uint32_t(w >> 32); }
 
-// 16-byte vector copy of one hidden row (H % 8 == 0), spread over the CTA
-SP_DEVI void copy_row(bf16* dst, const bf16* src, int H) {
-  const int4* s = reinterpret_cast<const int4*>(src);
-  int4* d = reinterpret_cast<int4*>(dst);
-  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) d[c] = __ldcg(s + c);  // L2: rows written by peers
-}
+// Every poll is bounded twice: by its own clock64 budget, and by the device
+// status word: once any poll of the device has given up (status set), every
+// other poll gives up at its next check, so a kernel whose peer is gone ends
+// after one budget, not one budget per word.
+SP_DEVI bool poll_abort(const int* gerr) { return *reinterpret_cast<const volatile int*>(gerr) != 0; }
 
-SP_DEVI bool wait_flags(const uint64_t* flags, int n, uint64_t want, long long budget) {
-  // thread i < n waits for flag i; returns false on timeout for any
-  bool ok = true;
-  if (threadIdx.x < n) {
+// Bounded poll of one word; returns its payload (0 and ok = false on timeout).
+SP_DEVI uint32_t poll_ll(const u64* p, uint32_t tag, long long budget, bool& ok, int* gerr) {
+  u64 w = ld_ll(p);
+  if (tag_of(w) == tag) return uint32_t(w);
+  const long long t0 = clock64();
+  for (unsigned it = 1;; ++it) {
+    w = ld_ll(p);
+    if (tag_of(w) == tag) return uint32_t(w);
+    if (clock64() - t0 > budget) { atomicCAS(gerr, 0, kErrWaitTimeoutPeer); ok = false; return 0; }
+    if ((it & 255) == 0 && poll_abort(gerr)) { ok = false; return 0; }
+  }
+}
+// Bounded poll of four consecutive words (8 bf16); false on timeout.
+SP_DEVI bool poll_ll4(const u64* p, uint32_t tag, long long budget, uint32_t (&v)[4], int* gerr) {
+  u64 w0, w1, w2, w3;
+  ld_ll2(p, w0, w1);
+  ld_ll2(p + 2, w2, w3);
+  if (tag_of(w0) != tag || tag_of(w1) != tag || tag_of(w2) != tag || tag_of(w3) != tag) {
     const long long t0 = clock64();
-    while (ld_acquire_sys(flags + threadIdx.x) != want) {
-      if (clock64() - t0 > budget) { ok = false; break; }
-      __nanosleep(64);
+    for (unsigned it = 1;; ++it) {
+      ld_ll2(p, w0, w1);
+      ld_ll2(p + 2, w2, w3);
+      if (tag_of(w0) == tag && tag_of(w1) == tag && tag_of(w2) == tag && tag_of(w3) == tag) break;
+      if (clock64() - t0 > budget) { atomicCAS(gerr, 0, kErrWaitTimeoutPeer); return false; }
+      if ((it & 255) == 0 && poll_abort(gerr)) return false;
     }
   }
-  return __syncthreads_and(ok);
+  v[0] = uint32_t(w0); v[1] = uint32_t(w1); v[2] = uint32_t(w2); v[3] = uint32_t(w3);
+  return true;
+}
+
+SP_DEVI uint8_t* rank_base(const EpArgs& a, int r) { return reinterpret_cast<uint8_t*>(a.base[r]); }
+// (rows in chunk c of source src) on rank r
+SP_DEVI u64* ctrl_word(const EpArgs& a, int r, int buf, int src, int c) {
+  return reinterpret_cast<u64*>(rank_base(a, r) + a.off_ctrl) + (int64_t(buf) * EP_MAX_RANKS + src) * a.max_chunks + c;
+}
+// (chunks the source sent this epoch) on rank r
+SP_DEVI u64* nch_word(const EpArgs& a, int r, int buf, int src) {
+  return reinterpret_cast<u64*>(rank_base(a, r) + a.off_nch) + buf * EP_MAX_RANKS + src;
+}
+SP_DEVI u64* meta_words(const EpArgs& a, int r, int buf, int src, int row) {
+  return reinterpret_cast<u64*>(rank_base(a, r) + a.off_meta) +
+         ((int64_t(buf) * a.world + src) * a.cap + row) * (2 + 2 * a.kk);
+}
+SP_DEVI u64* row_words(const EpArgs& a, int r, int buf, int src, int row) {
+  return reinterpret_cast<u64*>(rank_base(a, r) + a.off_rows) + ((int64_t(buf) * a.world + src) * a.cap + row) * (a.H / 2);
+}
+SP_DEVI u64* comb_words(const EpArgs& a, int r, int buf, int slot) {
+  return reinterpret_cast<u64*>(rank_base(a, r) + a.off_comb) + (int64_t(buf) * a.cap * a.kk + slot) * (a.H / 2);
+}
+
+SP_DEVI uint32_t epoch_tag(const int64_t* epoch_ptr, const EpArgs& a, int layer, int* buf) {
+  const u64 e = u64(*epoch_ptr) * a.moe_layers + layer;
+  *buf = int(e & 1);
+  return uint32_t(e + 1);
+}
+
+// One warp sends one bf16 row as tagged words: lane handles 8 columns (16 B in,
+// 4 words = 32 B out) per step; all of a lane's loads are issued before its
+// stores so the row costs one load latency, not one per step.
+constexpr int EP_ROW_STEPS = 8;  // 16-byte steps per lane held in registers per pass (2048 columns)
+SP_DEVI void warp_send_row(u64* dst, const bf16* src, int H, uint32_t tag) {
+  const int lane = threadIdx.x & 31;
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+  const int n = H / 8;
+  for (int c0 = 0; c0 < n; c0 += 32 * EP_ROW_STEPS) {
+    uint4 v[EP_ROW_STEPS];
+#pragma unroll
+    for (int u = 0; u < EP_ROW_STEPS; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < n) v[u] = __ldcg(s + c);
+    }
+#pragma unroll
+    for (int u = 0; u < EP_ROW_STEPS; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < n) {
+        st_ll2(dst + 4 * c, ll_word(v[u].x, tag), ll_word(v[u].y, tag));
+        st_ll2(dst + 4 * c + 2, ll_word(v[u].z, tag), ll_word(v[u].w, tag));
+      }
+    }
+  }
 }
 }  // namespace
 
-// scratch ints: [0, W) per-destination row cursors, [W] dispatch ticket, [W+1] combine ticket
+// grid (W destinations, C chunks of EP_CHUNK_TOKENS tokens), 256 threads
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(const bf16* __restrict__ x, int64_t ldx,
                                                           const int* __restrict__ ids, int T, EpArgs a,
                                                           const int64_t* __restrict__ epoch_ptr, int layer) {
   griddep_wait();
   griddep_launch();
-  const uint64_t e = uint64_t(*epoch_ptr) * a.moe_layers + layer;
-  const int buf = int(e & 1);
-  int* scr = local_scratch(a);
-  __shared__ int s_dest[EP_MAX_KK], s_pos[EP_MAX_KK], s_nd;
-  const int t = blockIdx.x;
-  if (t < T) {
-    if (threadIdx.x == 0) {
-      int nd = 0;
-      int dest_of[EP_MAX_KK], le_of[EP_MAX_KK];
+  int buf;
+  const uint32_t tag = epoch_tag(epoch_ptr, a, layer, &buf);
+  const int d = blockIdx.x, c = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int s_tok[EP_CHUNK_TOKENS], s_n;
+  if (warp == 0) {
+    const int t = c * EP_CHUNK_TOKENS + lane;
+    int n = 0;
+    int le[EP_MAX_KK], jj[EP_MAX_KK];
+    if (lane < EP_CHUNK_TOKENS && t < T) {
       for (int j = 0; j < a.kk; ++j) {
         const int id = ids[t * a.kk + j];
-        int d, le;
-        if (id >= a.n_routed) { d = a.rank; le = a.experts_per_rank + (id - a.n_routed); }  // shared: local
-        else { d = id / a.experts_per_rank; le = id - d * a.experts_per_rank; }
-        dest_of[j] = d;
-        le_of[j] = le;
-        bool seen = false;
-        for (int q = 0; q < nd; ++q) seen |= s_dest[q] == d;
-        if (!seen) s_dest[nd++] = d;
+        const int dd = id >= a.n_routed ? a.rank : id / a.experts_per_rank;
+        if (dd == d) {
+          le[n] = id >= a.n_routed ? a.experts_per_rank + (id - a.n_routed) : id - dd * a.experts_per_rank;
+          jj[n] = j;
+          ++n;
+        }
       }
-      for (int q = 0; q < nd; ++q) {
-        const int d = s_dest[q];
-        const int pos = atomicAdd(&scr[d], 1);
-        s_pos[q] = pos;
-        int* m = recv_meta(a, d, buf, a.rank, pos);
-        int n = 0;
-        for (int j = 0; j < a.kk; ++j)
-          if (dest_of[j] == d) { m[2 + n] = le_of[j]; m[2 + a.kk + n] = j; ++n; }
-        m[0] = t;
-        m[1] = n;
-      }
-      s_nd = nd;
     }
-    __syncthreads();
-    for (int q = 0; q < s_nd; ++q) copy_row(recv_row(a, s_dest[q], buf, a.rank, s_pos[q]), x + int64_t(t) * ldx, a.H);
+    const unsigned mask = __ballot_sync(0xffffffffu, n > 0);
+    if (n > 0) {
+      const int pos = __popc(mask & ((1u << lane) - 1));
+      u64* m = meta_words(a, d, buf, a.rank, c * EP_CHUNK_TOKENS + pos);
+      st_ll(m, ll_word(uint32_t(t), tag));
+      st_ll(m + 1, ll_word(uint32_t(n), tag));
+      for (int q = 0; q < n; ++q) {
+        st_ll(m + 2 + q, ll_word(uint32_t(le[q]), tag));
+        st_ll(m + 2 + a.kk + q, ll_word(uint32_t(jj[q]), tag));
+      }
+      s_tok[pos] = t;
+    }
+    if (lane == 0) {
+      s_n = __popc(mask);
+      st_ll(ctrl_word(a, d, buf, a.rank, c), ll_word(uint32_t(__popc(mask)), tag));
+      if (c == 0) st_ll(nch_word(a, d, buf, a.rank), ll_word(gridDim.y, tag));
+    }
   }
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int ticket = atomicAdd(&scr[a.world], 1);
-    if (ticket == int(gridDim.x) - 1) {
-      __threadfence();
-      for (int d = 0; d < a.world; ++d) {
-        *recv_count(a, d, buf, a.rank) = atomicExch(&scr[d], 0);
-      }
-      __threadfence_system();
-      for (int d = 0; d < a.world; ++d) st_release_sys(recv_flag(a, d, buf, a.rank), e + 1);
-      scr[a.world] = 0;
-    }
-  }
+  const int n = s_n;
+  for (int i = warp; i < n; i += blockDim.x / 32)
+    warp_send_row(row_words(a, d, buf, a.rank, c * EP_CHUNK_TOKENS + i), x + int64_t(s_tok[i]) * ldx, a.H, tag);
 }
 
 constexpr int EP_ALIGN_MAX_E = 1024;
@@ -194,90 +247,222 @@ __global__ void __launch_bounds__(1024) ep_recv_align_kernel(EpArgs a, const int
                                                              int* __restrict__ gerr) {
   griddep_wait();
   griddep_launch();
-  const uint64_t e = uint64_t(*epoch_ptr) * a.moe_layers + layer;
-  const int buf = int(e & 1);
+  int buf;
+  const uint32_t tag = epoch_tag(epoch_ptr, a, layer, &buf);
   const int El = a.experts_per_rank + a.n_shared;
-  __shared__ int cnt[EP_ALIGN_MAX_E], cur[EP_ALIGN_MAX_E], rows[EP_MAX_RANKS];
-  const bool ok = wait_flags(recv_flag(a, a.rank, buf, 0), a.world, e + 1, budget);
-  if (!ok) {
+  __shared__ int cnt[EP_ALIGN_MAX_E], cur[EP_ALIGN_MAX_E], nch[EP_MAX_RANKS], s_rows;
+  extern __shared__ int s_count[];  // [world][max_chunks] rows per (source, chunk)
+  bool ok = true;
+  if (threadIdx.x < a.world) {
+    const int v = int(poll_ll(nch_word(a, a.rank, buf, threadIdx.x), tag, budget, ok, gerr));
+    nch[threadIdx.x] = v < 1 ? 1 : (v > a.max_chunks ? a.max_chunks : v);
+  }
+  if (__syncthreads_and(ok)) {
+    for (int i = threadIdx.x; i < a.world * a.max_chunks && ok; i += blockDim.x) {
+      const int s = i / a.max_chunks, c = i % a.max_chunks;
+      s_count[i] = c < nch[s] ? int(poll_ll(ctrl_word(a, a.rank, buf, s, c), tag, budget, ok, gerr)) : 0;
+    }
+    for (int i = threadIdx.x; i < El; i += blockDim.x) cnt[i] = 0;
+    if (threadIdx.x == 0) {
+      int m = 0;
+      for (int s = 0; s < a.world; ++s) m = nch[s] > m ? nch[s] : m;
+      s_rows = m * EP_CHUNK_TOKENS;  // row slots to scan per source
+    }
+  }
+  ok = __syncthreads_and(ok);
+  const int rows = ok ? s_rows : 0, total = a.world * rows;
+  // pass 1: histogram of local experts over every received (row, entry), all sources at once
+  for (int i = threadIdx.x; i < total && ok; i += blockDim.x) {
+    const int s = i / rows, r = i % rows;
+    if (r % EP_CHUNK_TOKENS >= s_count[s * a.max_chunks + r / EP_CHUNK_TOKENS]) continue;
+    const u64* m = meta_words(a, a.rank, buf, s, r);
+    // one batch of loads for the row's whole list, then the (rare) late words
+    u64 w[2 + EP_MAX_KK];
+#pragma unroll
+    for (int q = 0; q < 2 + EP_MAX_KK; ++q)
+      if (q < 2 + a.kk) w[q] = ld_ll(m + q);
+    const int n = tag_of(w[1]) == tag ? int(uint32_t(w[1])) : int(poll_ll(m + 1, tag, budget, ok, gerr));
+#pragma unroll
+    for (int q = 0; q < EP_MAX_KK; ++q) {
+      if (q >= n || !ok) break;
+      const int le = tag_of(w[2 + q]) == tag ? int(uint32_t(w[2 + q])) : int(poll_ll(m + 2 + q, tag, budget, ok, gerr));
+      if (ok && le < El) atomicAdd(&cnt[le], 1);
+    }
+  }
+  if (!__syncthreads_and(ok)) {
     for (int i = threadIdx.x; i <= El; i += blockDim.x) grp_rows[i] = grp_tiles[i] = 0;
     if (threadIdx.x == 0) atomicCAS(gerr, 0, kErrWaitTimeoutPeer);
     return;
   }
-  for (int i = threadIdx.x; i < El; i += blockDim.x) cnt[i] = 0;
-  if (threadIdx.x < a.world) rows[threadIdx.x] = __ldcg(recv_count(a, a.rank, buf, threadIdx.x));
-  __syncthreads();
-  const int mi = 2 + 2 * a.kk;
-  for (int s = 0; s < a.world; ++s) {
-    const int* m0 = recv_meta(a, a.rank, buf, s, 0);
-    for (int r = threadIdx.x; r < rows[s]; r += blockDim.x) {
-      const int* m = m0 + r * mi;
-      const int n = __ldcg(m + 1);
-      for (int q = 0; q < n; ++q) atomicAdd(&cnt[__ldcg(m + 2 + q)], 1);
-    }
-  }
-  __syncthreads();
   if (threadIdx.x < 32) ep_scan(cnt, El, bn, grp_rows, grp_tiles, cur);
   __syncthreads();
-  for (int s = 0; s < a.world; ++s) {
-    const int* m0 = recv_meta(a, a.rank, buf, s, 0);
-    for (int r = threadIdx.x; r < rows[s]; r += blockDim.x) {
-      const int* m = m0 + r * mi;
-      const int n = __ldcg(m + 1), tok = __ldcg(m);
-      for (int q = 0; q < n; ++q) {
-        const int p = atomicAdd(&cur[__ldcg(m + 2 + q)], 1);
-        src_row[p] = s * a.cap + r;
-        comb_dst[p] = (s << 20) | (tok * a.kk + __ldcg(m + 2 + a.kk + q));
+  // pass 2: every word has arrived (pass 1 saw them); scatter to expert-sorted positions
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int s = i / rows, r = i % rows;
+    if (r % EP_CHUNK_TOKENS >= s_count[s * a.max_chunks + r / EP_CHUNK_TOKENS]) continue;
+    const u64* m = meta_words(a, a.rank, buf, s, r);
+    bool ok2 = true;
+    const int tok = int(poll_ll(m, tag, budget, ok2, gerr)), n = int(uint32_t(ld_ll(m + 1)));
+    for (int q = 0; q < n; ++q) {
+      const int le = int(uint32_t(ld_ll(m + 2 + q)));
+      if (le >= El) continue;
+      const int p = atomicAdd(&cur[le], 1);
+      src_row[p] = s * a.cap + r;
+      comb_dst[p] = (s << 20) | (tok * a.kk + int(poll_ll(m + 2 + a.kk + q, tag, budget, ok2, gerr)));
+    }
+    if (!ok2) atomicCAS(gerr, 0, kErrWaitTimeoutPeer);
+  }
+}
+
+// received rows (tagged words) -> expert-sorted bf16 rows; one warp per row
+__global__ void __launch_bounds__(256) ep_gather_kernel(EpArgs a, const int64_t* __restrict__ epoch_ptr, int layer,
+                                                        const int* __restrict__ total, const int* __restrict__ src_row,
+                                                        bf16* __restrict__ xs, long long budget,
+                                                        int* __restrict__ gerr) {
+  griddep_wait();
+  griddep_launch();
+  int buf;
+  const uint32_t tag = epoch_tag(epoch_ptr, a, layer, &buf);
+  const int n = *total;
+  const u64* base = row_words(a, a.rank, buf, 0, 0);
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x / 32);
+  bool ok = true;
+  const int nc = a.H / 8;
+  for (int p = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); p < n && ok; p += warps) {
+    const u64* src = base + int64_t(src_row[p]) * (a.H / 2);
+    uint4* dst = reinterpret_cast<uint4*>(xs + int64_t(p) * a.H);
+    for (int c0 = 0; c0 < nc && ok; c0 += 32 * EP_ROW_STEPS) {
+      u64 w[EP_ROW_STEPS][4];
+      // issue every load of this pass first, then check tags (re-poll only the late ones)
+#pragma unroll
+      for (int u = 0; u < EP_ROW_STEPS; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < nc) {
+          ld_ll2(src + 4 * c, w[u][0], w[u][1]);
+          ld_ll2(src + 4 * c + 2, w[u][2], w[u][3]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < EP_ROW_STEPS; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c >= nc) continue;
+        uint32_t v[4];
+        if (tag_of(w[u][0]) == tag && tag_of(w[u][1]) == tag && tag_of(w[u][2]) == tag && tag_of(w[u][3]) == tag) {
+          v[0] = uint32_t(w[u][0]); v[1] = uint32_t(w[u][1]); v[2] = uint32_t(w[u][2]); v[3] = uint32_t(w[u][3]);
+        } else if (!poll_ll4(src + 4 * c, tag, budget, v, gerr)) {
+          ok = false;
+          break;
+        }
+        dst[c] = make_uint4(v[0], v[1], v[2], v[3]);
       }
     }
   }
+  if (!ok) atomicCAS(gerr, 0, kErrWaitTimeoutPeer);
 }
 
-__global__ void __launch_bounds__(256) ep_gather_kernel(EpArgs a, const int64_t* __restrict__ epoch_ptr, int layer,
-                                                        const int* __restrict__ total, const int* __restrict__ src_row,
-                                                        bf16* __restrict__ xs) {
-  griddep_wait();
-  griddep_launch();
-  const uint64_t e = uint64_t(*epoch_ptr) * a.moe_layers + layer;
-  const int buf = int(e & 1);
-  const int n = *total;
-  const bf16* base = recv_row(a, a.rank, buf, 0, 0);
-  for (int p = blockIdx.x; p < n; p += gridDim.x) copy_row(xs + int64_t(p) * a.H, base + int64_t(src_row[p]) * a.H, a.H);
-}
-
+// grid (W destinations, EP_COMBINE_CTAS): output rows whose source is rank d go
+// straight into d's combine slots as tagged words
 __global__ void __launch_bounds__(256) ep_combine_send_kernel(const bf16* __restrict__ y, const int* __restrict__ total,
                                                               const int* __restrict__ comb_dst, EpArgs a,
                                                               const int64_t* __restrict__ epoch_ptr, int layer) {
   griddep_wait();
   griddep_launch();
-  const uint64_t e = uint64_t(*epoch_ptr) * a.moe_layers + layer;
-  const int buf = int(e & 1);
+  int buf;
+  const uint32_t tag = epoch_tag(epoch_ptr, a, layer, &buf);
+  const int d = blockIdx.x, c = blockIdx.y;
   const int n = *total;
-  for (int p = blockIdx.x; p < n; p += gridDim.x) {
-    const int d = comb_dst[p];
-    copy_row(comb_row(a, d >> 20, buf, d & 0xFFFFF), y + int64_t(p) * a.H, a.H);
-  }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int* scr = local_scratch(a);
-    const int ticket = atomicAdd(&scr[a.world + 1], 1);
-    if (ticket == int(gridDim.x) - 1) {
-      __threadfence_system();
-      for (int d = 0; d < a.world; ++d) st_release_sys(comb_flag(a, d, buf, a.rank), e + 1);
-      scr[a.world + 1] = 0;
-    }
+  const int wpc = blockDim.x / 32;
+  for (int p = c * wpc + (threadIdx.x >> 5); p < n; p += EP_COMBINE_CTAS * wpc) {
+    const int dst = comb_dst[p];
+    if ((dst >> 20) == d) warp_send_row(comb_words(a, d, buf, dst & 0xFFFFF), y + int64_t(p) * a.H, a.H, tag);
   }
 }
 
-__global__ void __launch_bounds__(32) ep_wait_combine_kernel(EpArgs a, const int64_t* __restrict__ epoch_ptr,
-                                                             int layer, long long budget, int* __restrict__ gerr) {
+// res[t] += sum_j w[t, j] * slot(t, j); out[t] = rmsnorm(res[t]) * gamma, with the
+// slots read as they arrive. Same per-element arithmetic and reduction order as
+// combine_add_rmsnorm (moe.cu), so results are bit-identical to the local path.
+__global__ void __launch_bounds__(256) ep_combine_add_rmsnorm_kernel(
+    EpArgs a, const int64_t* __restrict__ epoch_ptr, int layer, const float* __restrict__ w, bf16* __restrict__ res,
+    const bf16* __restrict__ gamma, bf16* __restrict__ out, long long ldo, float eps, long long budget,
+    int* __restrict__ gerr) {
   griddep_wait();
   griddep_launch();
-  const uint64_t e = uint64_t(*epoch_ptr) * a.moe_layers + layer;
-  const int buf = int(e & 1);
-  if (!wait_flags(comb_flag(a, a.rank, buf, 0), a.world, e + 1, budget) && threadIdx.x == 0)
-    atomicCAS(gerr, 0, kErrWaitTimeoutPeer);
+  int buf;
+  const uint32_t tag = epoch_tag(epoch_ptr, a, layer, &buf);
+  const int t = blockIdx.x, k = a.kk, H = a.H;
+  __shared__ float s_w[EP_MAX_KK];
+  __shared__ float part[8];
+  if (threadIdx.x < k) s_w[threadIdx.x] = w[t * k + threadIdx.x];
+  __syncthreads();
+  bf16* rr = res + (long long)t * H;
+  float v[4][8];
+  float ss = 0.f;
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c < H) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // issue the loads of every slot first, then consume them in slot order
+      u64 w[EP_MAX_KK][4];
+#pragma unroll
+      for (int j = 0; j < EP_MAX_KK; ++j)
+        if (j < k) {
+          const u64* p = comb_words(a, a.rank, buf, t * k + j) + c / 2;
+          ld_ll2(p, w[j][0], w[j][1]);
+          ld_ll2(p + 2, w[j][2], w[j][3]);
+        }
+#pragma unroll
+      for (int j = 0; j < EP_MAX_KK; ++j) {
+        if (j >= k) break;
+        uint32_t raw[4];
+        if (tag_of(w[j][0]) == tag && tag_of(w[j][1]) == tag && tag_of(w[j][2]) == tag && tag_of(w[j][3]) == tag) {
+          raw[0] = uint32_t(w[j][0]); raw[1] = uint32_t(w[j][1]); raw[2] = uint32_t(w[j][2]); raw[3] = uint32_t(w[j][3]);
+        } else if (!ok || !poll_ll4(comb_words(a, a.rank, buf, t * k + j) + c / 2, tag, budget, raw, gerr)) {
+          ok = false;
+          raw[0] = raw[1] = raw[2] = raw[3] = 0u;
+        }
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(raw);
+        float yv[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(h[q]);
+          yv[2 * q] = f.x;
+          yv[2 * q + 1] = f.y;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += s_w[j] * yv[e];
+      }
+      float r[8];
+      ld_bf16x8(rr + c, r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        v[i][e] = __bfloat162float(__float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(acc[e])) + r[e]));
+      st_bf16x8(rr + c, v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
+    }
+  }
+  if (!ok) atomicCAS(gerr, 0, kErrWaitTimeoutPeer);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += part[i];
+  const float inv = rsqrtf(tot / H + eps);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c < H) {
+      float g[8], o[8];
+      ld_bf16x8(gamma + c, g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = v[i][e] * inv * g[e];
+      st_bf16x8(out + (long long)t * ldo + c, o);
+    }
+  }
 }
 
 __global__ void ep_advance_kernel(int64_t* epoch_ptr) {
@@ -290,40 +475,54 @@ __global__ void ep_advance_kernel(int64_t* epoch_ptr) {
 static void check_args(const EpArgs& a) {
   if (a.world < 1 || a.world > EP_MAX_RANKS) throw std::runtime_error("ep: world size must be 1..8");
   if (a.kk < 1 || a.kk > EP_MAX_KK) throw std::runtime_error("ep: top-k + shared must be 1..16");
-  if (a.H % 8) throw std::runtime_error("ep: hidden size must be a multiple of 8");
+  if (a.H % 8 || a.H > 8192) throw std::runtime_error("ep: hidden size must be a multiple of 8, at most 8192");
   if (a.experts_per_rank + a.n_shared > EP_ALIGN_MAX_E) throw std::runtime_error("ep: too many local experts");
   if (a.cap >= (1 << 20) / a.kk) throw std::runtime_error("ep: token capacity too large for the slot encoding");
+  if (a.cap % EP_CHUNK_TOKENS || a.max_chunks != a.cap / EP_CHUNK_TOKENS)
+    throw std::runtime_error("ep: capacity must be whole token chunks");
 }
 
 void ep_dispatch(const void* x, int64_t ldx, const int* ids, int T, const EpArgs& a, const int64_t* epoch, int layer,
                  cudaStream_t s) {
   check_args(a);
   if (T > a.cap) throw std::runtime_error("ep: more tokens than the buffer capacity");
-  launch_k(ep_dispatch_kernel, dim3(T > 0 ? T : 1), dim3(256), 0, s, static_cast<const bf16*>(x), ldx, ids, T, a,
+  const int chunks = T > 0 ? (T + EP_CHUNK_TOKENS - 1) / EP_CHUNK_TOKENS : 1;
+  launch_k(ep_dispatch_kernel, dim3(a.world, chunks), dim3(256), 0, s, static_cast<const bf16*>(x), ldx, ids, T, a,
            epoch, layer);
 }
 
 void ep_recv_align(const EpArgs& a, const int64_t* epoch, int layer, int bn, int* grp_rows, int* grp_tiles,
                    int* src_row, int* comb_dst, long long budget, int* err, cudaStream_t s) {
   check_args(a);
-  launch_k(ep_recv_align_kernel, dim3(1), dim3(1024), 0, s, a, epoch, layer, bn, grp_rows, grp_tiles, src_row,
+  const int smem = a.world * a.max_chunks * (int)sizeof(int);
+  if (smem > 160 * 1024) throw std::runtime_error("ep: too many token chunks for the receive kernel");
+  if (smem > 32 * 1024)  // per current device; cheap, and legal during stream capture
+    cudaFuncSetAttribute(ep_recv_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+  launch_k(ep_recv_align_kernel, dim3(1), dim3(1024), smem, s, a, epoch, layer, bn, grp_rows, grp_tiles, src_row,
            comb_dst, budget, err);
 }
 
 void ep_gather(const EpArgs& a, const int64_t* epoch, int layer, const int* total, const int* src_row, void* xs,
-               int num_sms, cudaStream_t s) {
-  launch_k(ep_gather_kernel, dim3(num_sms * 2), dim3(256), 0, s, a, epoch, layer, total, src_row,
-           static_cast<bf16*>(xs));
+               long long budget, int* err, int num_sms, cudaStream_t s) {
+  launch_k(ep_gather_kernel, dim3(num_sms), dim3(256), 0, s, a, epoch, layer, total, src_row, static_cast<bf16*>(xs),
+           budget, err);
 }
 
 void ep_combine_send(const void* y, const int* total, const int* comb_dst, const EpArgs& a, const int64_t* epoch,
-                     int layer, int num_sms, cudaStream_t s) {
-  launch_k(ep_combine_send_kernel, dim3(num_sms * 2), dim3(256), 0, s, static_cast<const bf16*>(y), total, comb_dst,
-           a, epoch, layer);
+                     int layer, cudaStream_t s) {
+  launch_k(ep_combine_send_kernel, dim3(a.world, EP_COMBINE_CTAS), dim3(256), 0, s, static_cast<const bf16*>(y), total,
+           comb_dst, a, epoch, layer);
 }
 
-void ep_wait_combine(const EpArgs& a, const int64_t* epoch, int layer, long long budget, int* err, cudaStream_t s) {
-  launch_k(ep_wait_combine_kernel, dim3(1), dim3(32), 0, s, a, epoch, layer, budget, err);
+void ep_combine_add_rmsnorm(const EpArgs& a, const int64_t* epoch, int layer, const float* topk_w, void* residual,
+                            const void* gamma, void* out, long long ldo, int T, float eps, long long budget, int* err,
+                            cudaStream_t s) {
+  check_args(a);
+  if (T <= 0) return;
+  if (T > a.cap) throw std::runtime_error("ep: more tokens than the buffer capacity");
+  launch_k(ep_combine_add_rmsnorm_kernel, dim3(T), dim3(256), 0, s, a, epoch, layer, topk_w,
+           static_cast<bf16*>(residual), static_cast<const bf16*>(gamma), static_cast<bf16*>(out), ldo, eps, budget,
+           err);
 }
 
 void ep_advance(int64_t* epoch, cudaStream_t s) { launch_k(ep_advance_kernel, dim3(1), dim3(32), 0, s, epoch); }

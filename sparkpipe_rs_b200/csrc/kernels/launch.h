@@ -146,23 +146,27 @@ void decode_advance(const int* out_ids, int* ids, int* pos, int* ctx, int* slots
 // ---- expert-parallel dispatch / combine over peer memory (ep.cu)
 constexpr int EP_MAX_RANKS = 8;
 constexpr int EP_MAX_KK = 16;
+constexpr int EP_CHUNK_TOKENS = 8;   // tokens per dispatch CTA (at most 32)
+constexpr int EP_COMBINE_CTAS = 16;  // combine-send CTAs per destination
 // Every rank's EP buffer (mapped into this process) plus the byte offsets of
 // its regions; identical on all ranks except `rank`.
 struct EpArgs {
   unsigned long long base[EP_MAX_RANKS];
-  long long off_recv_flag, off_comb_flag, off_recv_count, off_recv_meta, off_recv_x, off_comb_x, off_scratch;
-  int world, rank, cap, H, kk, n_routed, experts_per_rank, n_shared, moe_layers;
+  long long off_ctrl, off_nch, off_meta, off_rows, off_comb;
+  int world, rank, cap, H, kk, n_routed, experts_per_rank, n_shared, moe_layers, max_chunks;
 };
-constexpr int EP_ARGS_WORDS = EP_MAX_RANKS + 7 + 9;
+constexpr int EP_ARGS_WORDS = EP_MAX_RANKS + 5 + 10;
 void ep_dispatch(const void* x, int64_t ldx, const int* ids, int T, const EpArgs& a, const int64_t* epoch, int layer,
                  cudaStream_t s);
 void ep_recv_align(const EpArgs& a, const int64_t* epoch, int layer, int bn, int* grp_rows, int* grp_tiles,
                    int* src_row, int* comb_dst, long long budget, int* err, cudaStream_t s);
 void ep_gather(const EpArgs& a, const int64_t* epoch, int layer, const int* total, const int* src_row, void* xs,
-               int num_sms, cudaStream_t s);
+               long long budget, int* err, int num_sms, cudaStream_t s);
 void ep_combine_send(const void* y, const int* total, const int* comb_dst, const EpArgs& a, const int64_t* epoch,
-                     int layer, int num_sms, cudaStream_t s);
-void ep_wait_combine(const EpArgs& a, const int64_t* epoch, int layer, long long budget, int* err, cudaStream_t s);
+                     int layer, cudaStream_t s);
+void ep_combine_add_rmsnorm(const EpArgs& a, const int64_t* epoch, int layer, const float* topk_w, void* residual,
+                            const void* gamma, void* out, long long ldo, int T, float eps, long long budget, int* err,
+                            cudaStream_t s);
 void ep_advance(int64_t* epoch, cudaStream_t s);
 
 }  // namespace sp

@@ -401,10 +401,10 @@ sp::EpArgs ep_args(const std::vector<int64_t>& v) {
   sp::EpArgs a{};
   int i = 0;
   for (int r = 0; r < sp::EP_MAX_RANKS; ++r) a.base[r] = (unsigned long long)v[i++];
-  a.off_recv_flag = v[i++]; a.off_comb_flag = v[i++]; a.off_recv_count = v[i++]; a.off_recv_meta = v[i++];
-  a.off_recv_x = v[i++]; a.off_comb_x = v[i++]; a.off_scratch = v[i++];
+  a.off_ctrl = v[i++]; a.off_nch = v[i++]; a.off_meta = v[i++]; a.off_rows = v[i++]; a.off_comb = v[i++];
   a.world = (int)v[i++]; a.rank = (int)v[i++]; a.cap = (int)v[i++]; a.H = (int)v[i++]; a.kk = (int)v[i++];
   a.n_routed = (int)v[i++]; a.experts_per_rank = (int)v[i++]; a.n_shared = (int)v[i++]; a.moe_layers = (int)v[i++];
+  a.max_chunks = (int)v[i++];
   for (int r = 0; r < a.world; ++r) TORCH_CHECK(a.base[r] != 0 && a.base[r] % 256 == 0, "ep: bad rank base pointer");
   return a;
 }
@@ -436,13 +436,13 @@ void ep_recv_align(const std::vector<int64_t>& args, const Tensor& epoch, int64_
 }
 
 void ep_gather(const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, const Tensor& total,
-               const Tensor& src_row, const Tensor& xs) {
+               const Tensor& src_row, const Tensor& xs, int64_t budget_cycles) {
   CHECK_BF16(xs); CHECK_CONTIG(xs); CHECK_I32(src_row); CHECK_I32(total);
   const c10::cuda::CUDAGuard guard(xs.device());
   const sp::EpArgs a = ep_args(args);
   TORCH_CHECK(xs.size(1) == a.H, "ep: xs width");
   sp::ep_gather(a, epoch.data_ptr<int64_t>(), (int)layer, total.data_ptr<int>(), src_row.data_ptr<int>(),
-                xs.data_ptr(), num_sms(), stream());
+                xs.data_ptr(), budget_cycles, err_word(), num_sms(), stream());
 }
 
 void ep_combine_send(const Tensor& y, const Tensor& total, const Tensor& comb_dst, const std::vector<int64_t>& args,
@@ -452,13 +452,20 @@ void ep_combine_send(const Tensor& y, const Tensor& total, const Tensor& comb_ds
   const sp::EpArgs a = ep_args(args);
   TORCH_CHECK(y.size(1) == a.H, "ep: y width");
   sp::ep_combine_send(y.data_ptr(), total.data_ptr<int>(), comb_dst.data_ptr<int>(), a, epoch.data_ptr<int64_t>(),
-                      (int)layer, num_sms(), stream());
+                      (int)layer, stream());
 }
 
-void ep_wait_combine(const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, int64_t budget_cycles) {
-  const c10::cuda::CUDAGuard guard(epoch.device());
+void ep_combine_add_rmsnorm(const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, const Tensor& w,
+                            const Tensor& residual, const Tensor& gamma, const Tensor& out, double eps,
+                            int64_t budget_cycles) {
+  CHECK_F32(w); CHECK_CONTIG(w); CHECK_BF16(residual); CHECK_CONTIG(residual); CHECK_BF16(gamma); CHECK_BF16(out);
+  TORCH_CHECK(out.stride(1) == 1 && out.stride(0) % 8 == 0, "ep: out rows must be contiguous and 16-byte aligned");
+  const c10::cuda::CUDAGuard guard(residual.device());
   const sp::EpArgs a = ep_args(args);
-  sp::ep_wait_combine(a, epoch.data_ptr<int64_t>(), (int)layer, budget_cycles, err_word(), stream());
+  TORCH_CHECK(residual.size(1) == a.H && w.numel() == residual.size(0) * a.kk, "ep: combine shape mismatch");
+  sp::ep_combine_add_rmsnorm(a, epoch.data_ptr<int64_t>(), (int)layer, w.data_ptr<float>(), residual.data_ptr(),
+                             gamma.data_ptr(), out.data_ptr(), out.stride(0), (int)residual.size(0), (float)eps,
+                             budget_cycles, err_word(), stream());
 }
 
 void ep_advance(const Tensor& epoch) {
@@ -502,8 +509,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_recv_align", &ep_recv_align);
   m.def("ep_gather", &ep_gather);
   m.def("ep_combine_send", &ep_combine_send);
-  m.def("ep_wait_combine", &ep_wait_combine);
+  m.def("ep_combine_add_rmsnorm", &ep_combine_add_rmsnorm);
   m.def("ep_advance", &ep_advance);
   m.attr("EP_ARGS_WORDS") = sp::EP_ARGS_WORDS;
   m.attr("EP_MAX_RANKS") = sp::EP_MAX_RANKS;
+  m.attr("EP_CHUNK_TOKENS") = sp::EP_CHUNK_TOKENS;
+  m.attr("EP_COMBINE_CTAS") = sp::EP_COMBINE_CTAS;
 }

@@ -211,6 +211,8 @@ class MLAMoEModel:
         eps = self.cfg.rms_norm_eps
         if pending is None:
             ops.add_rmsnorm(res, None, gamma, xn, eps)
+        elif isinstance(pending, tuple) and pending[0] == "ep_combine":
+            pending[1].combine_add_rmsnorm(pending[2], pending[3], res, gamma, xn, eps)
         elif isinstance(pending, tuple):
             _, y, inv_pos, wts, kk = pending
             ops.combine_add_rmsnorm(y, inv_pos, wts, res, gamma, xn, kk, eps)

@@ -4,13 +4,14 @@ token all-to-all done by fused peer-memory kernels (``csrc/kernels/ep.cu``).
 Attention stays data-parallel (every rank decodes its own requests); rank r
 holds routed experts [r*El, (r+1)*El) plus all shared experts. Per MoE layer:
 
-    dispatch -> recv/align -> gather -> grouped GEMM (gate/up + SwiGLU) ->
-    grouped GEMM (down) -> combine-send -> combine-wait
+    dispatch -> receive/align -> gather -> grouped GEMM (gate/up + SwiGLU) ->
+    grouped GEMM (down) -> combine-send
 
-and the weighted sum of the returned rows is fused into the next residual add
-+ RMSNorm, exactly like the single-GPU path. All of it is stream-ordered device
-work (CUDA-graph capturable): the layer epoch lives in device memory and is
-advanced once per forward by ``end_step``.
+and the weighted sum of the returned rows, the residual add and the next
+RMSNorm run in one kernel that reads the rows as they arrive. Every word that
+crosses to a peer carries its own epoch tag, so no fences or flags are needed.
+All of it is stream-ordered device work (CUDA-graph capturable): the layer
+epoch lives in device memory and is advanced once per forward by ``end_step``.
 
 Buffers: one ``cudaMalloc`` per rank, mapped by every peer through CUDA IPC.
 Two parity halves (per MoE layer index) make back-to-back layers race-free.
@@ -26,31 +27,35 @@ import torch
 
 from .. import _ext, ops
 
-DEFAULT_BUDGET_CYCLES = 20_000_000_000  # ~10 s at 2 GHz: far above any healthy wait
+DEFAULT_BUDGET_CYCLES = 4_000_000_000  # ~2 s at 2 GHz: far above any healthy wait
 
 
 def _align(x: int, a: int = 256) -> int:
     return (x + a - 1) // a * a
 
 
+CHUNK_TOKENS = 8    # tokens per dispatch CTA (csrc/kernels/launch.h EP_CHUNK_TOKENS)
+COMBINE_CTAS = 16   # combine-send CTAs per destination (EP_COMBINE_CTAS)
+
+
 def ep_layout(world: int, cap: int, hidden: int, kk: int) -> dict:
-    """Byte offsets of the EP regions inside one rank's buffer."""
+    """Byte offsets of the EP regions inside one rank's buffer (cap: whole token
+    chunks). Every region holds 8-byte tagged words (4 payload bytes each)."""
     off = {}
     pos = 0
 
-    def region(name, nbytes):
+    def region(name, words):
         nonlocal pos
         off[name] = pos
-        pos = _align(pos + nbytes)
+        pos = _align(pos + 8 * words)
 
     max_ranks = 8
-    region("recv_flag", 2 * max_ranks * 8)
-    region("comb_flag", 2 * max_ranks * 8)
-    region("recv_count", 2 * max_ranks * 4)
-    region("scratch", 64 * 4)
-    region("recv_meta", 2 * world * cap * (2 + 2 * kk) * 4)
-    region("recv_x", 2 * world * cap * hidden * 2)
-    region("comb_x", 2 * cap * kk * hidden * 2)
+    chunks = cap // CHUNK_TOKENS
+    region("ctrl", 2 * max_ranks * chunks)             # rows per (source, chunk)
+    region("nch", 2 * max_ranks)                       # chunks per source
+    region("meta", 2 * world * cap * (2 + 2 * kk))     # (token, n, experts, k-slots) per row
+    region("rows", 2 * world * cap * hidden // 2)      # received hidden rows
+    region("comb", 2 * cap * kk * hidden // 2)         # returned expert outputs per (token, k-slot)
     off["total"] = pos
     return off
 
@@ -60,6 +65,7 @@ class ExpertParallel:
                  budget_cycles: int = DEFAULT_BUDGET_CYCLES):
         assert cfg.n_routed_experts % world == 0, "routed experts must split evenly over the ranks"
         assert 1 <= world <= 8
+        cap_tokens = -(-cap_tokens // CHUNK_TOKENS) * CHUNK_TOKENS
         self.cfg, self.rank, self.world, self.cap = cfg, rank, world, cap_tokens
         self.device = torch.device(device)
         self.budget = int(budget_cycles)
@@ -98,10 +104,6 @@ class ExpertParallel:
         F = cfg.moe_intermediate_size
         self.act = torch.zeros(max_pairs, F, dtype=torch.bfloat16, device=dev)
         self.y = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
-        self.ident = torch.arange(cap_tokens * self.kk, dtype=torch.int32, device=dev)
-        o = self.layout["comb_x"]
-        n = 2 * cap_tokens * self.kk * self.H * 2
-        self.comb = self.buf[o:o + n].view(torch.bfloat16).view(2, cap_tokens * self.kk, self.H)
 
     @classmethod
     def emulated(cls, cfg, world: int, cap_tokens: int, device, budget_cycles: int = DEFAULT_BUDGET_CYCLES):
@@ -120,10 +122,9 @@ class ExpertParallel:
     def args(self) -> list[int]:
         L = self.layout
         c = self.cfg
-        return (list(self.bases) + [L["recv_flag"], L["comb_flag"], L["recv_count"], L["recv_meta"], L["recv_x"],
-                                    L["comb_x"], L["scratch"]] +
+        return (list(self.bases) + [L["ctrl"], L["nch"], L["meta"], L["rows"], L["comb"]] +
                 [self.world, self.rank, self.cap, self.H, self.kk, c.n_routed_experts, self.El,
-                 c.n_shared_experts, self.layers_per_step])
+                 c.n_shared_experts, self.layers_per_step, self.cap // CHUNK_TOKENS])
 
     def local_expert_range(self) -> tuple[int, int]:
         return self.rank * self.El, (self.rank + 1) * self.El
@@ -137,7 +138,7 @@ class ExpertParallel:
         j = self.moe_index[layer]
         self.K.ep_recv_align(self.args(), self.epoch, j, bn, self.grp_rows, self.grp_tiles, self.src_row,
                              self.comb_dst, self.budget)
-        self.K.ep_gather(self.args(), self.epoch, j, self.grp_rows[self.n_local:], self.src_row, self.xs)
+        self.K.ep_gather(self.args(), self.epoch, j, self.grp_rows[self.n_local:], self.src_row, self.xs, self.budget)
         ops._count(2)
 
     def experts(self, w13: torch.Tensor, w2: torch.Tensor, bn: int, fused_swiglu: bool = True):
@@ -154,11 +155,16 @@ class ExpertParallel:
                                self.moe_index[layer])
         ops._count(1)
 
-    def combine_wait(self, layer: int, T: int, wts: torch.Tensor):
-        j = self.moe_index[layer]
-        self.K.ep_wait_combine(self.args(), self.epoch, j, self.budget)
+    def combine(self, layer: int, wts: torch.Tensor):
+        """The deferred combine of this layer; ``model._residual_norm`` runs it as
+        ``combine_add_rmsnorm`` (slot sum + residual add + RMSNorm in one kernel)."""
+        return ("ep_combine", self, layer, wts)
+
+    def combine_add_rmsnorm(self, layer: int, wts: torch.Tensor, res: torch.Tensor, gamma: torch.Tensor,
+                            out: torch.Tensor, eps: float):
+        self.K.ep_combine_add_rmsnorm(self.args(), self.epoch, self.moe_index[layer], wts, res, gamma, out, eps,
+                                      self.budget)
         ops._count(1)
-        return ("combine", self.comb[j & 1], self.ident[: T * self.kk], wts, self.kk)
 
     def end_step(self):
         self.K.ep_advance(self.epoch)
@@ -174,7 +180,7 @@ class ExpertParallel:
         self.receive(layer, bn)
         self.experts(w13, w2, bn, fused_swiglu)
         self.combine_send(layer)
-        return self.combine_wait(layer, xn.shape[0], wts)
+        return self.combine(layer, wts)
 
 
 def block_n_for(tokens_per_rank: int, kk: int, n_local: int) -> int:

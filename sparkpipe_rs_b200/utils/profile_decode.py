@@ -7,12 +7,18 @@ diagnostic: the benchmark numbers come from CUDA-event timing without any
 profiler attached.
 
     python -m sparkpipe_rs_b200.utils.profile_decode --batch 64 --ctx 1024
+
+Launched with torch.distributed.run (N processes, one GPU each) it profiles the
+expert-parallel model: attention data-parallel, experts split over the ranks,
+and every rank prints its own breakdown.
 """
 from __future__ import annotations
 
 import argparse
 import collections
+import datetime
 import math
+import os
 
 import torch
 
@@ -25,7 +31,10 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = model default)")
     ap.add_argument("--no-trace", action="store_true", help="run the steps without the profiler (for ncu)")
+    ap.add_argument("--graph", action="store_true", help="replay the step as one CUDA graph")
     args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
 
     from sparkpipe_rs_b200.models.config import get_config
     from sparkpipe_rs_b200.models.mla_moe import DecodeGraph, KVCache, MLAMoEModel
@@ -33,14 +42,21 @@ def main():
     cfg = get_config(args.model)
     if args.layers:
         cfg = cfg.replace(num_layers=args.layers)
-    dev = torch.device("cuda", 0)
-    model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=args.ctx + 64)
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    ep = None
+    if world > 1:
+        import torch.distributed as dist
+        from sparkpipe_rs_b200.parallel.expert_parallel import ExpertParallel
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        ep = ExpertParallel(cfg, rank, world, args.batch, dev, group=dist.group.WORLD)
+    model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=args.ctx + 64, ep=ep)
     B, bs = args.batch, 64
     bps = math.ceil((args.ctx + args.steps + 8) / bs)
     cache = KVCache(cfg, num_blocks=B * bps, block_size=bs, device=dev)
     cache.data.normal_(0, 1)
     bt = torch.arange(B * bps, dtype=torch.int32, device=dev).view(B, bps)
-    dg = DecodeGraph(model, cache, B, bps, args.ctx + args.steps + 8, use_graph=False, self_advance=True)
+    dg = DecodeGraph(model, cache, B, bps, args.ctx + args.steps + 8, use_graph=args.graph, self_advance=True)
     dg.block_table.copy_(bt)
     dg.pos.fill_(args.ctx)
     dg.ctx.fill_(args.ctx + 1)
@@ -70,12 +86,17 @@ def main():
             tot[name] += ev.device_time_total
             cnt[name] += 1
     all_us = sum(tot.values()) / args.steps
-    print(f"decode step: batch {B}, context {args.ctx}, layers {cfg.num_layers}: "
+    print(f"[rank {rank}/{world}] decode step: batch {B}, context {args.ctx}, layers {cfg.num_layers}: "
           f"{all_us / 1000:.3f} ms of kernel time per step")
     print(f"{'kernel':80s} {'us/step':>10s} {'share':>7s} {'launches/step':>14s}")
     for name, us in sorted(tot.items(), key=lambda kv: -kv[1]):
         print(f"{name:80s} {us / args.steps:10.1f} {100 * us / args.steps / all_us:6.1f}% "
               f"{cnt[name] / args.steps:14.1f}")
+    if world > 1:
+        dg.release()
+        torch.distributed.barrier()
+        ep.close()
+        torch.distributed.destroy_process_group()
 
 
 if __name__ == "__main__":

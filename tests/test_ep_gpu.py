@@ -92,13 +92,12 @@ def test_emulated_ranks_match_single_gpu(world):
             for r in range(world):
                 ranks[r].combine_send(layer)
             for r in range(world):
-                if tokens[r] == 0:
-                    ranks[r].combine_wait(layer, 0, wts[r])
-                    continue
-                pend = ranks[r].combine_wait(layer, tokens[r], wts[r])
                 res_ep = res[r].clone()
                 out_ep = torch.empty_like(xs[r])
-                ops.combine_add_rmsnorm(pend[1], pend[2], pend[3], res_ep, gamma, out_ep, kk, cfg.rms_norm_eps)
+                # reads the returned rows as they arrive (all have: every send ran first)
+                ranks[r].combine_add_rmsnorm(layer, wts[r], res_ep, gamma, out_ep, cfg.rms_norm_eps)
+                if tokens[r] == 0:
+                    continue
                 res_ref = res[r].clone()
                 out_ref = _local_moe(cfg, xs[r], full[p + "e_w13"], full[p + "e_w2"], ids[r], wts[r], res_ref,
                                      gamma, cfg.rms_norm_eps)
@@ -126,6 +125,15 @@ def test_receive_wait_times_out_with_status():
     torch.cuda.synchronize()
     assert ops.status_word() == 4  # peer wait timeout
     assert int(ranks[0].grp_rows.sum()) == 0  # empty schedule: downstream kernels do nothing
+    ops.clear_status()
+    # combine side: nobody returned rows for rank 1's tokens this epoch, so its
+    # combine polls run out of budget
+    res = torch.zeros(2, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+    out = torch.empty_like(res)
+    gamma = torch.ones(cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+    ranks[1].combine_add_rmsnorm(layer, torch.ones(2, ranks[1].kk, device=dev), res, gamma, out, 1e-6)
+    torch.cuda.synchronize()
+    assert ops.status_word() == 4
     ops.clear_status()
     torch.cuda.synchronize()
     assert ops.status_word() == 0
