@@ -24,6 +24,7 @@ from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
 CSRC = PKG_DIR / "csrc"
+INCLUDE = PKG_DIR / "include"  # public C headers (driver ABI)
 EXT_DIR = PKG_DIR / "_ext"
 
 CUDA_ARCH_FLAGS = ["-gencode=arch=compute_100a,code=sm_100a"]
@@ -54,7 +55,7 @@ SPECS = {
     },
     "_sp_core": {
         "sources": _core_sources,
-        "headers": lambda: sorted((CSRC / "core").glob("*.h")),
+        "headers": lambda: sorted((CSRC / "core").glob("*.h")) + sorted(INCLUDE.rglob("*.h")),
         "cuda": False,
     },
 }
@@ -113,7 +114,8 @@ def build(name: str, verbose: bool = False):
         kw["extra_cuda_cflags"] = CUDA_FLAGS
         kw["extra_include_paths"] = [str(CSRC / "kernels")]
     else:
-        kw["extra_include_paths"] = [str(CSRC / "core")]
+        kw["extra_include_paths"] = [str(CSRC / "core"), str(INCLUDE)]
+        kw["extra_ldflags"] = ["-ldl"]
     mod = cpp_extension.load(**kw)
     (out / f"{name}.srchash").write_text(_digest(name))
     _loaded[name] = mod
