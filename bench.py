@@ -16,6 +16,11 @@ Two numbers are reported:
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 For N > 1 launch one process per GPU with torch.distributed.run.
+
+``--model k2`` runs the 1T Kimi-K2-shape workload instead: block-scaled fp8
+weights (128x128 e4m3 blocks, fp32 scales), 256 concurrent requests over the
+box, 2048-token prompts, 512 output tokens, attention data-parallel and the 384
+routed experts split over the GPUs (8 GPUs hold the 1T parameters).
 """
 from __future__ import annotations
 
@@ -38,15 +43,17 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="v2_lite")
-    ap.add_argument("--batch", type=int, default=64, help="concurrent requests per GPU")
-    ap.add_argument("--prompt", type=int, default=1024)
-    ap.add_argument("--output", type=int, default=256)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="concurrent requests per GPU (default: 64 for v2_lite; 256 over the box for k2)")
+    ap.add_argument("--prompt", type=int, default=0, help="prompt tokens (default 1024; 2048 for k2)")
+    ap.add_argument("--output", type=int, default=0, help="output tokens (default 256; 512 for k2)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--parallel", default="auto", choices=["auto", "dp", "ep"],
                     help="N>1: dp = replicated model per GPU; ep = data-parallel attention + experts split "
                          "over the GPUs (auto: ep when the experts divide evenly)")
-    ap.add_argument("--prefill-chunk", type=int, default=8192, help="max tokens per prefill forward")
+    ap.add_argument("--prefill-chunk", type=int, default=0,
+                    help="max tokens per prefill forward (default 8192; 2048 for k2)")
     return ap.parse_args()
 
 
@@ -83,6 +90,11 @@ def main():
     from sparkpipe_rs_b200.utils.clocks import ClockSampler
 
     cfg = get_config(args.model)
+    big = cfg.weight_dtype == "fp8_block"  # the 1T fp8 workload: 256 requests over the box, 2048 in / 512 out
+    args.batch = args.batch or (max(1, 256 // world) if big else 64)
+    args.prompt = args.prompt or (2048 if big else 1024)
+    args.output = args.output or (512 if big else 256)
+    args.prefill_chunk = args.prefill_chunk or (2048 if big else 8192)
     B, P = args.batch, args.prompt
     bs = 64
     par = args.parallel
@@ -95,7 +107,12 @@ def main():
     torch.manual_seed(1234 + rank)
     model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=P + args.output + args.warmup + args.steps + 64,
                         ep=ep)
-    weight_gb = sum(t.numel() * t.element_size() for t in model.w.values()) / 1e9
+    def _nbytes(t):
+        if isinstance(t, ops.Fp8Weight):
+            return t.q.numel() + t.s.numel() * 4
+        return t.numel() * t.element_size()
+
+    weight_gb = sum(_nbytes(t) for t in model.w.values()) / 1e9
     parallelism = f"dp{world}-ep{world}" if ep is not None else f"dp{world}"
 
     # ------------------------------------------------------------ device-timed decode
@@ -204,7 +221,8 @@ def main():
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": (value / PUBLISHED_BASELINE) if PUBLISHED_BASELINE else None,
-            "dtype": "bf16",
+            "dtype": ("fp8 (e4m3 128x128-block weights, 1x128-block activations, fp32 accumulate; bf16 attention "
+                      "and KV)") if cfg.weight_dtype == "fp8_block" else "bf16",
             "data": "synthetic: seeded uniform-random prompt ids, random-init N(0,0.02) weights",
             "config": {
                 "model": f"{cfg.name} ({cfg.num_layers} layers, hidden {cfg.hidden_size}, "

@@ -428,6 +428,13 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restri
 
 // ======================================================================= host
 
+void split_reduce(const float* ws, long long stride, int splits, int rows, int cols, void* out, long long ldo,
+                  int out_f32, cudaStream_t s) {
+  const long long n = (long long)rows * (cols / 4);
+  launch_k(split_reduce_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, ws, stride, splits, rows, cols,
+           out, ldo, out_f32);
+}
+
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -580,9 +587,7 @@ int gemm_bf16(const GemmLaunch& g) {
     if (g.slab_out) return -splits;  // the caller's next kernel sums the slabs itself
     const int rows = g.trans_out ? g.N : g.M;
     const int cols = g.trans_out ? g.M : g.N;
-    const long long n = (long long)rows * (cols / 4);
-    launch_k(split_reduce_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, g.stream, (const float*)g.ws,
-             slab, splits, rows, cols, g.D, g.ldd, g.out_f32);
+    split_reduce(g.ws, slab, splits, rows, cols, g.D, g.ldd, g.out_f32, g.stream);
     return 2;
   }
   dispatch_bn<MODE_DENSE>(bn, g, p);

@@ -41,6 +41,51 @@ struct GemmLaunch {
 int gemm_bf16(const GemmLaunch& g);
 void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, long long rows,
                   long long cols, long long ld, int box_rows, int box_cols);
+// out[r, c] = sum_s ws[s][r][c] for `splits` dense fp32 slabs [rows, cols] `stride` apart (cols % 4 == 0).
+void split_reduce(const float* ws, long long stride, int splits, int rows, int cols, void* out, long long ldo,
+                  int out_f32, cudaStream_t s);
+
+// ---- block-scaled fp8 GEMM (gemm_fp8.cu)
+// D[m, n] = sum_kb sa(m, kb) sb(n, kb) sum_{k in kb} A[m, k] B[n, k]; A, B e4m3 K-major,
+// sa[(row / sa_rows) * ldsa + kb] (weight rows of A as stored), sb[kb * ldsb + n].
+struct Fp8Launch {
+  const void* A = nullptr;
+  long long a_rows = 0, lda = 0;
+  const float* sa = nullptr;
+  long long ldsa = 0;
+  int sa_rows = 128;
+  const void* B = nullptr;
+  long long b_rows = 0, ldb = 0;
+  const float* sb = nullptr;
+  long long ldsb = 0;
+  void* D = nullptr;
+  long long ldd = 0;
+  int M = 0, N = 0, K = 0;
+  int trans_out = 0, out_f32 = 0;
+  int splits = 0, block_n = 0;
+  int grouped = 0;
+  const int* grp_rows = nullptr;
+  const int* grp_tiles = nullptr;
+  int num_groups = 0;
+  int a_evict_first = 1;
+  int swiglu = 0;
+  float* ws = nullptr;
+  long long ws_floats = 0;
+  int slab_out = 0;
+  int* err = nullptr;
+  int num_sms = 148;
+  cudaStream_t stream = 0;
+};
+int gemm_fp8(const Fp8Launch& g);
+// Activation quantisation: row r (source row src_idx[r] / idx_div when src_idx is given) of
+// bf16 x -> e4m3 q (pitch ldq) with one fp32 scale per 128 columns at s[kb * lds + r];
+// rows_dev (optional) holds the live row count in device memory (rows = capacity).
+void quant_act_fp8(const void* x, long long ldx, const int* src_idx, int idx_div, const int* rows_dev, void* q,
+                   long long ldq, float* s, long long lds, int rows, int cols, int num_sms, cudaStream_t st);
+// 128x128-block weight quantisation of bf16 `src` (or, when src is null, of seeded N(0, std)
+// samples at flat indices flat0 + row * cols + col): q e4m3 [rows, cols], s [ceil(rows/128), cols/128].
+void quant_weight_fp8(const void* src, uint64_t seed, long long flat0, float std_, void* q, float* s, int rows,
+                      int cols, cudaStream_t st);
 
 // ---- normalisation / rotary / KV cache (norm_rope.cu)
 // residual (optional, in/out) += x; out = rmsnorm(residual or x) * w.
@@ -111,7 +156,7 @@ void prefill_attention(const PrefillAttnLaunch& l);
 // `logits` may be split-K slabs: the logits are sum_s logits[s * slab_stride + ...] over `splits`.
 void moe_topk(const float* logits, long long slab_stride, int splits, const float* bias, int* topk_ids, float* topk_w,
               int T, int E, int k, int n_shared, int scoring, int renorm, float scaling, int n_group, int topk_group,
-              cudaStream_t s);
+              int group_top2, cudaStream_t s);
 // res[t] += sum_j w[t, j] * y[inv_pos[t*k + j]]; out[t] = rmsnorm(res[t]) * gamma
 void combine_add_rmsnorm(const void* y, long long ldy, const int* inv_pos, const float* topk_w, void* residual,
                          const void* gamma, void* out, long long ldo, int T, int k, int H, float eps, cudaStream_t s);

@@ -31,30 +31,76 @@ namespace sp {
 using bf16 = __nv_bfloat16;
 
 constexpr int TOPK_MAX_PER_LANE = 16;  // E <= 512
+constexpr int TOPK_THREADS = 256;
+constexpr int TOPK_MAX_E = 32 * TOPK_MAX_PER_LANE;
 
-__global__ void moe_topk_kernel(const float* __restrict__ logits, long long slab_stride, int splits,
-                                const float* __restrict__ bias, int* __restrict__ ids, float* __restrict__ wts, int T,
-                                int E, int k, int n_shared, int scoring, int renorm, float scaling) {
+// One CTA per token. The router logits arrive as `splits` fp32 split-K slabs: all
+// 256 threads load them at once (thread = (slab group g, VEC-wide column chunk v),
+// slabs g, g+G, ...), partial sums go through shared memory and are added in a
+// fixed order, so the result does not depend on timing. Warp 0 then scores,
+// optionally restricts the choice to the best `topk_group` of `n_group` expert
+// groups (group score: the group's best expert, or the sum of its best two as in
+// the bias-corrected sigmoid routers), and picks the top k by k rounds of a warp
+// argmax (ties to the lower expert id).
+template <int VEC>
+__global__ void __launch_bounds__(TOPK_THREADS)
+    moe_topk_kernel(const float* __restrict__ logits, long long slab_stride, int splits,
+                    const float* __restrict__ bias, int* __restrict__ ids, float* __restrict__ wts, int E, int k,
+                    int n_shared, int scoring, int renorm, float scaling, int n_group, int topk_group,
+                    int group_top2) {
+  __shared__ __align__(16) float s_part[TOPK_THREADS * 4 > TOPK_MAX_E ? TOPK_THREADS * 4 : TOPK_MAX_E];
+  __shared__ float s_logit[TOPK_MAX_E];
   griddep_wait();
   griddep_launch();
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
+  const int t = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
   const float* row = logits + (long long)t * E;
+  const int nvec = E / VEC;
+  if (nvec <= TOPK_THREADS) {
+    const int G = TOPK_THREADS / nvec;
+    const int g = tid / nvec, v = tid - g * nvec;
+    if (g < G) {
+      float acc[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) acc[j] = 0.f;
+#pragma unroll 4
+      for (int s2 = g; s2 < splits; s2 += G) {
+        const float* src = row + s2 * slab_stride + v * VEC;
+        if constexpr (VEC == 4) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(src));
+          acc[0] += x.x; acc[1] += x.y; acc[2] += x.z; acc[3] += x.w;
+        } else {
+          acc[0] += __ldcg(src);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) s_part[g * E + v * VEC + j] = acc[j];
+    }
+    __syncthreads();
+    const int used = G < splits ? G : splits;
+    for (int e = tid; e < E; e += TOPK_THREADS) {
+      float x = 0.f;
+      for (int g2 = 0; g2 < used; ++g2) x += s_part[g2 * E + e];
+      s_logit[e] = x;
+    }
+  } else {  // more columns than threads (only E > 256 with E % 4 != 0)
+    for (int e = tid; e < E; e += TOPK_THREADS) {
+      float x = 0.f;
+      for (int s2 = 0; s2 < splits; ++s2) x += __ldcg(row + s2 * slab_stride + e);
+      s_logit[e] = x;
+    }
+  }
+  __syncthreads();
+  if (tid >= 32) return;
+
   float score[TOPK_MAX_PER_LANE], sel[TOPK_MAX_PER_LANE];
   const int per = (E + 31) / 32;
   float mx = -INFINITY;
 #pragma unroll
   for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
     const int e = lane + i * 32;
-    if (i < per && e < E) {
-      float x = __ldcg(row + e);
-#pragma unroll 8
-      for (int s2 = 1; s2 < splits; ++s2) x += __ldcg(row + s2 * slab_stride + e);  // split-K slabs
-      score[i] = x;
-    } else {
-      score[i] = -INFINITY;
-    }
+    score[i] = (i < per && e < E) ? s_logit[e] : -INFINITY;
     mx = fmaxf(mx, score[i]);
   }
   if (scoring == 0) {
@@ -80,6 +126,44 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, long long slab
       const bool valid = i < per && e < E;
       score[i] = valid ? 1.f / (1.f + __expf(-score[i])) : 0.f;
       sel[i] = valid ? score[i] + (bias ? bias[e] : 0.f) : -INFINITY;
+    }
+  }
+  if (n_group > 1 && topk_group < n_group) {
+    // group-limited routing: lane g scores group g from the selection values
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      const int e = lane + i * 32;
+      if (i < per && e < E) s_part[e] = sel[i];
+    }
+    __syncwarp();
+    const int gs = E / n_group;
+    float gscore = -INFINITY;
+    if (lane < n_group) {
+      float b1 = -INFINITY, b2 = -INFINITY;
+      for (int e = lane * gs; e < (lane + 1) * gs; ++e) {
+        const float x = s_part[e];
+        if (x > b1) { b2 = b1; b1 = x; } else if (x > b2) { b2 = x; }
+      }
+      gscore = group_top2 ? b1 + b2 : b1;
+    }
+    unsigned keep = 0;
+    for (int j = 0; j < topk_group; ++j) {
+      float best = gscore;
+      int bi = lane < n_group ? lane : 0x7fffffff;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+      }
+      keep |= 1u << bi;
+      if (lane == bi) gscore = -INFINITY;
+    }
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      const int e = lane + i * 32;
+      if (i < per && e < E && !((keep >> (e / gs)) & 1u)) sel[i] = -INFINITY;
     }
   }
   float wsum = 0.f;
@@ -121,14 +205,24 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, long long slab
 
 void moe_topk(const float* logits, long long slab_stride, int splits, const float* bias, int* topk_ids, float* topk_w,
               int T, int E, int k, int n_shared, int scoring, int renorm, float scaling, int n_group, int topk_group,
-              cudaStream_t s) {
+              int group_top2, cudaStream_t s) {
   if (T <= 0) return;
-  if (E > 32 * TOPK_MAX_PER_LANE) throw std::runtime_error("moe_topk: at most 512 experts");
+  if (E > TOPK_MAX_E) throw std::runtime_error("moe_topk: at most 512 experts");
   if (k + n_shared > 32) throw std::runtime_error("moe_topk: k + shared <= 32");
-  if (n_group > 1 && topk_group < n_group) throw std::runtime_error("moe_topk: group-limited routing not supported");
-  const int warps = 1;
-  launch_k(moe_topk_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, s, logits, slab_stride,
-           splits < 1 ? 1 : splits, bias, topk_ids, topk_w, T, E, k, n_shared, scoring, renorm, scaling);
+  if (n_group < 1) n_group = 1;
+  if (n_group > 1) {
+    if (n_group > 32 || E % n_group) throw std::runtime_error("moe_topk: n_group must divide E and be <= 32");
+    if (topk_group < 1 || topk_group > n_group) throw std::runtime_error("moe_topk: 1 <= topk_group <= n_group");
+    if (topk_group * (E / n_group) < k) throw std::runtime_error("moe_topk: kept groups hold fewer than k experts");
+  }
+  splits = splits < 1 ? 1 : splits;
+  const bool vec4 = E % 4 == 0 && (splits == 1 || slab_stride % 4 == 0) && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
+  if (vec4)
+    launch_k(moe_topk_kernel<4>, dim3(T), dim3(TOPK_THREADS), 0, s, logits, slab_stride, splits, bias, topk_ids,
+             topk_w, E, k, n_shared, scoring, renorm, scaling, n_group, topk_group, group_top2);
+  else
+    launch_k(moe_topk_kernel<1>, dim3(T), dim3(TOPK_THREADS), 0, s, logits, slab_stride, splits, bias, topk_ids,
+             topk_w, E, k, n_shared, scoring, renorm, scaling, n_group, topk_group, group_top2);
 }
 
 // ---------------------------------------------------------------- align

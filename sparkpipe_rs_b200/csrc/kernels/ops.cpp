@@ -175,6 +175,102 @@ void quant_fp8_block(const Tensor& x, const Tensor& q, const Tensor& scales) {
                       (int)x.size(1), stream());
 }
 
+#define CHECK_FP8(x) \
+  TORCH_CHECK((x).scalar_type() == at::kFloat8_e4m3fn || (x).scalar_type() == at::kByte, #x " must be e4m3 (or bytes)")
+
+int64_t gemm_fp8(const Tensor& A, const Tensor& sa, int64_t sa_rows, const Tensor& B, const Tensor& sb,
+                 const Tensor& D, int64_t M, int64_t N, int64_t K, int64_t trans_out, int64_t splits, int64_t block_n,
+                 const c10::optional<Tensor>& grp_rows, const c10::optional<Tensor>& grp_tiles, int64_t num_groups,
+                 int64_t swiglu, int64_t slab_out) {
+  // A: weights [rows, K] e4m3 (2-D row-major view), sa [rows / sa_rows, K / 128] fp32;
+  // B: activations [b_rows, K] e4m3, sb [K / 128, ldsb] fp32 (K-block-major)
+  CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D); CHECK_FP8(A); CHECK_FP8(B); CHECK_F32(sa); CHECK_F32(sb);
+  TORCH_CHECK(A.dim() == 2 && A.stride(1) == 1 && B.dim() == 2 && B.stride(1) == 1, "gemm_fp8: 2-D row-major operands");
+  TORCH_CHECK(sa.dim() == 2 && sa.stride(1) == 1 && sb.dim() == 2 && sb.stride(1) == 1, "gemm_fp8: 2-D scale views");
+  TORCH_CHECK(sb.size(0) * 128 >= K && sa.size(1) * 128 >= K, "gemm_fp8: scale columns do not cover K");
+  TORCH_CHECK(sa.size(0) * sa_rows >= A.size(0), "gemm_fp8: weight scales do not cover A's rows");
+  TORCH_CHECK(D.scalar_type() == at::kBFloat16 || D.scalar_type() == at::kFloat, "D must be bf16 or fp32");
+  const c10::cuda::CUDAGuard guard(A.device());
+  sp::Fp8Launch g;
+  g.A = A.data_ptr(); g.a_rows = A.size(0); g.lda = A.stride(0);
+  g.sa = sa.data_ptr<float>(); g.ldsa = sa.stride(0); g.sa_rows = (int)sa_rows;
+  g.B = B.data_ptr(); g.b_rows = B.size(0); g.ldb = B.stride(0);
+  g.sb = sb.data_ptr<float>(); g.ldsb = sb.stride(0);
+  TORCH_CHECK(g.ldsb >= B.size(0), "gemm_fp8: activation scale pitch shorter than B's rows");
+  g.D = D.data_ptr(); g.ldd = D.stride(0);
+  g.M = (int)M; g.N = (int)N; g.K = (int)K;
+  g.trans_out = (int)trans_out;
+  g.out_f32 = D.scalar_type() == at::kFloat ? 1 : 0;
+  g.splits = (int)splits;
+  g.block_n = (int)block_n;
+  if (grp_rows.has_value()) {
+    TORCH_CHECK(grp_tiles.has_value(), "grouped GEMM needs grp_tiles");
+    CHECK_I32(*grp_rows); CHECK_I32(*grp_tiles);
+    g.grouped = 1;
+    g.grp_rows = grp_rows->data_ptr<int>();
+    g.grp_tiles = grp_tiles->data_ptr<int>();
+    g.num_groups = (int)num_groups;
+    TORCH_CHECK(A.size(0) >= (int64_t)num_groups * M, "gemm_fp8: A holds fewer than num_groups x M rows");
+  } else {
+    TORCH_CHECK(A.size(0) >= M && B.size(0) >= N, "gemm_fp8: operands smaller than M / N");
+    if (splits != 1) {
+      g.ws = split_ws();
+      g.ws_floats = kSplitWsFloats;
+    }
+  }
+  g.a_evict_first = 1;
+  g.swiglu = (int)swiglu;
+  g.slab_out = (int)slab_out;
+  g.err = err_word();
+  g.num_sms = num_sms();
+  g.stream = stream();
+  return sp::gemm_fp8(g);
+}
+
+void quant_act_fp8(const Tensor& x, const c10::optional<Tensor>& src_idx, int64_t idx_div,
+                   const c10::optional<Tensor>& rows_dev, const Tensor& q, const Tensor& s) {
+  // q [rows, K] e4m3; s [K / 128, lds] fp32; rows = q.size(0) (gathered from x when src_idx is given)
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_FP8(q); CHECK_F32(s);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && q.dim() == 2 && q.stride(1) == 1 && s.dim() == 2 &&
+                  s.stride(1) == 1, "quant_act_fp8: 2-D row-major views");
+  const int64_t rows = q.size(0), cols = q.size(1);
+  TORCH_CHECK(x.size(1) == cols && s.size(0) * 128 == cols && s.stride(0) >= rows, "quant_act_fp8: shapes");
+  const int* idx = nullptr;
+  if (src_idx.has_value()) {
+    CHECK_I32(*src_idx);
+    TORCH_CHECK(src_idx->numel() >= rows, "quant_act_fp8: gather index shorter than the rows");
+    idx = src_idx->data_ptr<int>();
+  } else {
+    TORCH_CHECK(x.size(0) >= rows, "quant_act_fp8: x has fewer rows than q");
+  }
+  const int* rd = nullptr;
+  if (rows_dev.has_value()) {
+    CHECK_I32(*rows_dev);
+    rd = rows_dev->data_ptr<int>();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  sp::quant_act_fp8(x.data_ptr(), x.stride(0), idx, (int)idx_div, rd, q.data_ptr(), q.stride(0),
+                    s.data_ptr<float>(), s.stride(0), (int)rows, (int)cols, num_sms(), stream());
+}
+
+void quant_weight_fp8(const c10::optional<Tensor>& src, int64_t seed, int64_t flat0, double std_, const Tensor& q,
+                      const Tensor& s) {
+  // q [rows, cols] e4m3 contiguous; s [ceil(rows / 128), cols / 128] fp32 contiguous
+  CHECK_CUDA(q); CHECK_FP8(q); CHECK_F32(s); CHECK_CONTIG(q); CHECK_CONTIG(s);
+  TORCH_CHECK(q.dim() == 2, "quant_weight_fp8: 2-D weight");
+  const int64_t rows = q.size(0), cols = q.size(1);
+  TORCH_CHECK(s.numel() == ((rows + 127) / 128) * (cols / 128), "quant_weight_fp8: scale shape");
+  const void* sp_ = nullptr;
+  if (src.has_value()) {
+    CHECK_BF16(*src); CHECK_CONTIG(*src);
+    TORCH_CHECK(src->numel() == rows * cols, "quant_weight_fp8: source shape");
+    sp_ = src->data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(q.device());
+  sp::quant_weight_fp8(sp_, (uint64_t)seed, flat0, (float)std_, q.data_ptr(), s.data_ptr<float>(), (int)rows,
+                       (int)cols, stream());
+}
+
 void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table, const Tensor& context_lens,
                 const Tensor& out, const c10::optional<Tensor>& o_part, const c10::optional<Tensor>& lse_part,
                 int64_t splits, double scale) {
@@ -229,15 +325,15 @@ void prefill_attention(const Tensor& q, const Tensor& k, const Tensor& kpe, cons
 
 void moe_topk(const Tensor& logits, const c10::optional<Tensor>& bias, const Tensor& ids, const Tensor& w,
               int64_t n_shared, int64_t scoring, bool renorm, double scaling, int64_t T, int64_t E,
-              int64_t slab_stride, int64_t splits) {
+              int64_t slab_stride, int64_t splits, int64_t n_group, int64_t topk_group, bool group_top2) {
   // logits: [T, E] fp32, or the split-K workspace holding `splits` [T, E] slabs slab_stride apart
   CHECK_CUDA(logits); CHECK_F32(logits); CHECK_CONTIG(logits); CHECK_I32(ids); CHECK_F32(w);
   const c10::cuda::CUDAGuard guard(logits.device());
   const float* b = nullptr;
   if (bias.has_value()) { CHECK_F32(*bias); b = bias->data_ptr<float>(); }
   sp::moe_topk(logits.data_ptr<float>(), slab_stride, (int)splits, b, ids.data_ptr<int>(), w.data_ptr<float>(), (int)T,
-               (int)E, (int)(ids.size(1) - n_shared), (int)n_shared, (int)scoring, renorm ? 1 : 0, (float)scaling, 1,
-               1, stream());
+               (int)E, (int)(ids.size(1) - n_shared), (int)n_shared, (int)scoring, renorm ? 1 : 0, (float)scaling,
+               (int)n_group, (int)topk_group, group_top2 ? 1 : 0, stream());
 }
 
 void slab_add_rmsnorm(const Tensor& slabs, int64_t stride, int64_t splits, const Tensor& residual, const Tensor& w,
@@ -483,6 +579,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_kv_write", &mla_kv_write);
   m.def("rope_q", &rope_q);
   m.def("quant_fp8_block", &quant_fp8_block);
+  m.def("gemm_fp8", &gemm_fp8);
+  m.def("quant_act_fp8", &quant_act_fp8);
+  m.def("quant_weight_fp8", &quant_weight_fp8);
   m.def("mla_decode", &mla_decode);
   m.def("prefill_attention", &prefill_attention);
   m.def("moe_topk", &moe_topk);

@@ -9,6 +9,7 @@ Presets are the serving workloads this engine is measured on:
   * ``tiny``     — 2-layer CPU plumbing model (hidden 256, 8 experts top-2 + 1 shared)
   * ``v2_lite``  — DeepSeek-V2-Lite shape (27 layers, hidden 2048, 64 experts top-6 + 2 shared)
   * ``k2``       — Kimi-K2 shape 1T (61 layers, hidden 7168, 384 experts top-8 + 1 shared)
+  * ``v3``       — DeepSeek-V3 shape 671B (256 experts top-8 in 8 groups, best 4 groups kept)
   * ``mtp_head`` — 1-layer MTP-style draft head for speculative decoding
 """
 from __future__ import annotations
@@ -37,6 +38,9 @@ class MLAMoEConfig:
     n_shared_experts: int = 1
     first_k_dense_replace: int = 0
     scoring_func: str = "softmax"         # "softmax" | "sigmoid"
+    n_group: int = 1                      # expert groups of group-limited routing (1 = off)
+    topk_group: int = 1                   # groups kept per token
+    topk_method: str = "greedy"           # "greedy" | "group_limited_greedy" (group = best expert) | "noaux_tc" (best two)
     norm_topk_prob: bool = False
     routed_scaling_factor: float = 1.0
     rms_norm_eps: float = 1e-6
@@ -65,6 +69,10 @@ class MLAMoEConfig:
     @property
     def shared_intermediate(self) -> int:
         return self.moe_intermediate_size * self.n_shared_experts
+
+    @property
+    def group_limited(self) -> bool:
+        return self.n_group > 1 and self.topk_group < self.n_group
 
     def softmax_scale(self) -> float:
         s = 1.0 / math.sqrt(self.qk_head_dim)
@@ -167,6 +175,7 @@ def k2() -> MLAMoEConfig:
         n_shared_experts=1,
         first_k_dense_replace=1,
         scoring_func="sigmoid",
+        topk_method="noaux_tc",
         norm_topk_prob=True,
         routed_scaling_factor=2.827,
         rms_norm_eps=1e-6,
@@ -178,6 +187,19 @@ def k2() -> MLAMoEConfig:
     )
 
 
+def v3() -> MLAMoEConfig:
+    """DeepSeek-V3 shape (671B): 61 layers (first 3 dense, FFN 18432), hidden 7168,
+    128 heads, q_lora 1536, kv_lora 512, 256 experts top-8 + 1 shared (FFN 2048) with
+    group-limited routing (8 groups, best 4 kept, group = sum of its best two),
+    vocab 129280, block-scaled fp8 weights."""
+    return k2().replace(
+        name="deepseek-v3-shape", vocab_size=129280, num_heads=128, first_k_dense_replace=3,
+        n_routed_experts=256, n_group=8, topk_group=4, routed_scaling_factor=2.5, rope_theta=10000.0,
+        rope_scaling={"type": "yarn", "factor": 40.0, "original_max_position_embeddings": 4096,
+                      "beta_fast": 32.0, "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0},
+        max_position_embeddings=163840)
+
+
 def mtp_head(target: MLAMoEConfig) -> MLAMoEConfig:
     """1-layer MTP-style draft head: same hidden/attention as the target, 1 MLA layer
     plus one dense FFN of width 1408."""
@@ -185,7 +207,7 @@ def mtp_head(target: MLAMoEConfig) -> MLAMoEConfig:
                           intermediate_size=1408)
 
 
-PRESETS = {"tiny": tiny, "v2_lite": v2_lite, "k2": k2}
+PRESETS = {"tiny": tiny, "v2_lite": v2_lite, "k2": k2, "v3": v3}
 
 
 def get_config(name: str) -> MLAMoEConfig:

@@ -39,6 +39,9 @@ def k27_view(doc) -> dict:
     return json.loads(doc.as_k27_json())
 
 
+_TOPK_METHOD = {"greedy": "greedy", "group_limited_greedy": "group_limited_greedy", "noaux_tc": "noaux_tc"}
+
+
 def config_from_k27(view: dict, name: str | None = None) -> MLAMoEConfig:
     m, a, r, e, q = view["model"], view["mla"], view["rope"], view["moe"], view["quantization"]
     if e["moe_layer_frequency"] != 1:
@@ -74,6 +77,9 @@ def config_from_k27(view: dict, name: str | None = None) -> MLAMoEConfig:
         n_shared_experts=e["shared_expert_count"],
         first_k_dense_replace=m["first_routed_layer"],
         scoring_func=scoring,
+        n_group=int(e["router_group_count"]) or 1,
+        topk_group=int(e.get("selected_group_count", e["router_group_count"])) or 1,
+        topk_method=_TOPK_METHOD.get(e["top_k_method"], "greedy"),
         norm_topk_prob=bool(e["renormalize_selected_probabilities"]),
         routed_scaling_factor=float(e["routed_scaling_factor"]),
         rms_norm_eps=float(m["rms_norm_epsilon"]),
@@ -114,6 +120,9 @@ def config_from_hf(cfg: dict, name: str | None = None) -> MLAMoEConfig:
         n_shared_experts=cfg.get("n_shared_experts", 0) or 0,
         first_k_dense_replace=cfg.get("first_k_dense_replace", 0),
         scoring_func=cfg.get("scoring_func", "softmax"),
+        n_group=int(cfg.get("n_group") or 1),
+        topk_group=int(cfg.get("topk_group") or 1),
+        topk_method=_TOPK_METHOD.get(cfg.get("topk_method", "greedy"), "greedy"),
         norm_topk_prob=bool(cfg.get("norm_topk_prob", False)),
         routed_scaling_factor=float(cfg.get("routed_scaling_factor", 1.0)),
         rms_norm_eps=float(cfg.get("rms_norm_eps", 1e-6)),

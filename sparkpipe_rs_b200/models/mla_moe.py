@@ -88,14 +88,15 @@ class MLAMoEModel:
         if weights is None:
             weights = init_weights(cfg, seed=seed, device=self.device, dtype=torch.bfloat16,
                                    experts=ep.local_expert_range() if ep is not None else None)
-        self.w = {k: v.to(self.device) for k, v in weights.items()}
+        self.w = {k: (v if isinstance(v, ops.Fp8Weight) else v.to(self.device)) for k, v in weights.items()}
         derive_decode_weights(cfg, self.w)
         # routed + shared expert gate/up weights in the fused-SwiGLU tile order
         self.fused_swiglu = cfg.moe_intermediate_size % 64 == 0
         for i in range(cfg.num_layers):
             k = f"l{i}.e_w13"
             if k in self.w and self.fused_swiglu:
-                self.w[k] = ops.interleave_gate_up(self.w[k])
+                v = self.w[k]
+                self.w[k] = ops.interleave_gate_up_fp8(v) if isinstance(v, ops.Fp8Weight) else ops.interleave_gate_up(v)
         maxp = max_positions or min(cfg.max_position_embeddings, 1 << 17)
         self.cos_sin = cos_sin_table(cfg, maxp, device=self.device)
         self.scale = cfg.softmax_scale()
@@ -103,6 +104,15 @@ class MLAMoEModel:
         self._layer_offset = 0
 
     # ------------------------------------------------------------------ pieces
+    def _lin(self, x: torch.Tensor, w, slab: bool = False, out_dtype=torch.bfloat16):
+        """x @ w.T for a bf16 or block-scaled fp8 weight; with ``slab`` a decode-shaped
+        result may stay split-K fp32 slabs (``ops.Slabs``) for a slab-aware consumer."""
+        if isinstance(w, ops.Fp8Weight):
+            return ops.linear_fp8(ops.quant_act_fp8(x), w, out_dtype=out_dtype, slab_out=slab)
+        if slab:
+            return ops.linear_slabs(x, w, out_dtype=out_dtype)
+        return ops.linear(x, w, out_dtype=out_dtype)
+
     def _q_view(self, q2d: torch.Tensor, T: int) -> torch.Tensor:
         c = self.cfg
         return torch.as_strided(q2d, (T, c.num_heads, c.qk_head_dim), (q2d.stride(0), c.qk_head_dim, 1))
@@ -110,11 +120,11 @@ class MLAMoEModel:
     def _project(self, i: int, xn: torch.Tensor):
         c, w = self.cfg, self.w
         p = f"l{i}."
-        a = ops.linear(xn, w[p + "w_qkv_a"])
+        a = self._lin(xn, w[p + "w_qkv_a"])
         if c.q_lora_rank:
             qa = torch.empty(xn.shape[0], c.q_lora_rank, dtype=torch.bfloat16, device=self.device)
             ops.add_rmsnorm(a[:, : c.q_lora_rank], None, w[p + "q_a_norm"], qa, c.rms_norm_eps)
-            q = ops.linear(qa, w[p + "w_q_b"])
+            q = self._lin(qa, w[p + "w_q_b"])
         else:
             q = a[:, : self.qa_dim]
         kv_a = a[:, self.qa_dim:]
@@ -137,7 +147,7 @@ class MLAMoEModel:
         else:
             # one kernel: split-K reduction of the q/kv projection, latent norm + RoPE
             # + cache write, query RoPE and the compact q_nope operand
-            qkv = ops.linear_slabs(xn, w[p + "w_qkv_a"])
+            qkv = self._lin(xn, w[p + "w_qkv_a"], slab=True)
             q_src = torch.empty(T, nh * dn, dtype=torch.bfloat16, device=self.device)
             ops.mla_decode_prep(qkv, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache,
                                 q_src, q_lat, dn, 0, self.qa_dim, c.rms_norm_eps)
@@ -152,7 +162,7 @@ class MLAMoEModel:
         # attn[t, h*dv + v] = o_lat[t, h] @ W_UV[h]^T
         ops.batched_gemm(w[p + "w_kv_b"], o_lat.view(T, nh * kvl), attn, M=dv, N=T, K=kvl, batch=nh, a_row0=dn,
                          a_batch_rows=dn + dv, b_batch_k=kvl, ldd=nh * dv, d_batch_stride=dv)
-        return ops.linear_slabs(attn, w[p + "w_o"])
+        return self._lin(attn, w[p + "w_o"], slab=True)
 
     def _attn_prefill(self, i: int, xn: torch.Tensor, fb: ForwardBatch, cache: KVCache) -> torch.Tensor:
         c, w = self.cfg, self.w
@@ -173,24 +183,36 @@ class MLAMoEModel:
         o = torch.empty(T, nh, dv, dtype=torch.bfloat16, device=self.device)
         ops.prefill_attention(q3, kv3[:, :, :dn], lat_ctx[:, kvl:], kv3[:, :, dn:], o, fb.cu_q, fb.cu_k, fb.max_q,
                               self.scale, True)
-        return ops.linear(o.view(T, nh * dv), w[p + "w_o"])
+        return self._lin(o.view(T, nh * dv), w[p + "w_o"])
 
     def _mlp(self, i: int, xn: torch.Tensor) -> torch.Tensor:
         c, w = self.cfg, self.w
         p = f"l{i}."
         if not c.is_moe_layer(i):
-            return ops.linear(ops.silu_mul(ops.linear(xn, w[p + "w13"])), w[p + "w2"])
+            return self._lin(ops.silu_mul(self._lin(xn, w[p + "w13"])), w[p + "w2"])
         T = xn.shape[0]
         E, k, F, S = c.n_routed_experts, c.num_experts_per_tok, c.moe_intermediate_size, c.n_shared_experts
         logits = ops.linear_slabs(xn, w[p + "gate"], out_dtype=torch.float32)
         sigmoid = c.scoring_func == "sigmoid"
         ids, wts = ops.moe_topk(logits, w[p + "gate_bias"] if sigmoid else None, k, 1 if sigmoid else 0,
-                                c.norm_topk_prob, c.routed_scaling_factor, n_shared=S)
+                                c.norm_topk_prob, c.routed_scaling_factor, n_shared=S, n_group=c.n_group,
+                                topk_group=c.topk_group, group_top2=c.topk_method == "noaux_tc")
         kk = k + S
         if self.ep is not None:
             bn = _moe_block_n(T * kk, self.ep.n_local)
+            if isinstance(w[p + "e_w13"], ops.Fp8Weight):
+                bn = max(32, min(bn, 128))
             return self.ep.moe(i, xn, ids, wts, w[p + "e_w13"], w[p + "e_w2"], bn, self.fused_swiglu)
         bn = _moe_block_n(T * kk, E + S)
+        if isinstance(w[p + "e_w13"], ops.Fp8Weight):
+            bn = max(32, min(bn, 128))
+            grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E + S, bn)
+            xq = ops.quant_act_fp8(xn, sorted_tok)  # gather into the expert-sorted order while quantising
+            act = torch.empty(T * kk, F, dtype=torch.bfloat16, device=self.device)
+            ops.grouped_gemm_fp8(w[p + "e_w13"], xq, act, grp_rows, grp_tiles, E + S, bn, swiglu=True)
+            y = torch.empty(T * kk, c.hidden_size, dtype=torch.bfloat16, device=self.device)
+            ops.grouped_gemm_fp8(w[p + "e_w2"], ops.quant_act_fp8(act), y, grp_rows, grp_tiles, E + S, bn)
+            return ("combine", y, inv_pos, wts, kk)
         grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E + S, bn)
         xs = ops.gather_rows(xn, sorted_tok)
         if self.fused_swiglu:

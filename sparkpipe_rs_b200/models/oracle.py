@@ -26,6 +26,12 @@ def route(cfg: MLAMoEConfig, x: torch.Tensor, gate: torch.Tensor, bias: torch.Te
     else:
         scores = logits.sigmoid()
         sel = scores + (bias.float() if bias is not None else 0.0)
+    if cfg.group_limited:
+        T, E = sel.shape
+        g = sel.view(T, cfg.n_group, E // cfg.n_group)
+        gscore = g.topk(2, -1).values.sum(-1) if cfg.topk_method == "noaux_tc" else g.max(-1).values
+        keep = torch.zeros_like(gscore, dtype=torch.bool).scatter_(1, gscore.topk(cfg.topk_group, -1).indices, True)
+        sel = sel.masked_fill(~keep.repeat_interleave(E // cfg.n_group, 1), float("-inf"))
     ids = sel.topk(cfg.num_experts_per_tok, dim=-1).indices
     w = scores.gather(-1, ids)
     if cfg.norm_topk_prob:

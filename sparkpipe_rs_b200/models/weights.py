@@ -18,6 +18,14 @@ and shared experts run in one grouped GEMM.
 Values are N(0, init_std) (norm weights 1, router bias 0), drawn per tensor from
 a generator seeded with (seed, tensor index), so any subset of layers or any
 device produces the same numbers.
+
+With ``weight_dtype == "fp8_block"`` (on a CUDA device) the projection and expert
+matrices (``FP8_WEIGHTS``) are block-scaled e4m3 (``ops.Fp8Weight``: 128x128
+blocks, fp32 scales), sampled and quantised on the device by one kernel from a
+counter-based generator: element (r, c) of a 2-D view is sample r * cols + c of
+the tensor's stream, so an expert-parallel rank's slice equals the same rows of
+the whole tensor. Embeddings, norms, the router, ``w_kv_b`` (the absorbed-MLA
+operands) and the LM head stay bf16.
 """
 from __future__ import annotations
 
@@ -61,6 +69,39 @@ def _is_norm(name: str) -> bool:
     return name.endswith("norm")
 
 
+FP8_WEIGHTS = ("w_qkv_a", "w_q_b", "w_o", "w13", "w2", "e_w13", "e_w2")
+
+
+def is_fp8_weight(cfg: MLAMoEConfig, name: str) -> bool:
+    return cfg.weight_dtype == "fp8_block" and name.split(".")[-1] in FP8_WEIGHTS
+
+
+def _fp8_tensor(cfg: MLAMoEConfig, shape: tuple, seed: int, dev, experts):
+    from .. import ops
+
+    if len(shape) == 2:
+        return ops.quant_weight_fp8(shape[0], shape[1], seed=seed, std=cfg.init_std, device=dev)
+    G, R, C = shape
+    parts = [(0, G)] if experts is None else [experts, (cfg.n_routed_experts, G)]
+    n = sum(hi - lo for lo, hi in parts)
+    q = torch.empty(n, R, C, dtype=torch.float8_e4m3fn, device=dev)
+    s = torch.empty(n, R // 128, C // 128, dtype=torch.float32, device=dev)
+    at = 0
+    for lo, hi in parts:
+        if hi > lo:
+            part = ops.Fp8Weight(q[at:at + hi - lo], s[at:at + hi - lo], 128)
+            ops.quant_weight_fp8((hi - lo) * R, C, seed=seed, std=cfg.init_std, flat0=lo * R * C, out=part)
+            at += hi - lo
+    return ops.Fp8Weight(q, s, 128)
+
+
+def dequant_weights(w: dict) -> dict:
+    """fp32 copy of a weight dict with every ``Fp8Weight`` dequantised (oracle use)."""
+    from .. import ops
+
+    return {k: (v.dequant() if isinstance(v, ops.Fp8Weight) else v.float()) for k, v in w.items()}
+
+
 def init_weights(cfg: MLAMoEConfig, seed: int = 0, device="cpu", dtype=torch.bfloat16,
                  layers: list[int] | None = None, experts: tuple[int, int] | None = None) -> dict[str, torch.Tensor]:
     """Random-init weights. ``layers`` restricts which decoder layers are created;
@@ -81,8 +122,12 @@ def init_weights(cfg: MLAMoEConfig, seed: int = 0, device="cpu", dtype=torch.bfl
         if name.endswith("gate_bias"):
             out[name] = torch.zeros(shape, dtype=torch.float32, device=dev)
             continue
+        tseed = (seed * 1_000_003 + idx) & 0x7FFFFFFFFFFFFFFF
+        if dev.type == "cuda" and is_fp8_weight(cfg, name):
+            out[name] = _fp8_tensor(cfg, shape, tseed, dev, experts if name.endswith(("e_w13", "e_w2")) else None)
+            continue
         g = torch.Generator(device=dev)
-        g.manual_seed((seed * 1_000_003 + idx) & 0x7FFFFFFFFFFFFFFF)
+        g.manual_seed(tseed)
         t = torch.empty(shape, dtype=dtype, device=dev)
         if dtype in (torch.float32, torch.bfloat16, torch.float16):
             t.normal_(0.0, cfg.init_std, generator=g)

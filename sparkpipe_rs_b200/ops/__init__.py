@@ -23,6 +23,13 @@ __all__ = [
     "mla_kv_write",
     "rope_q",
     "quant_fp8_block",
+    "Fp8Weight",
+    "Fp8Act",
+    "quant_weight_fp8",
+    "quant_act_fp8",
+    "linear_fp8",
+    "grouped_gemm_fp8",
+    "interleave_gate_up_fp8",
     "mla_decode",
     "mla_decode_splits",
     "prefill_attention",
@@ -190,6 +197,21 @@ def interleave_gate_up(w13: torch.Tensor) -> torch.Tensor:
     return v.reshape(*lead, two_f, K).contiguous()
 
 
+def interleave_gate_up_fp8(w13: Fp8Weight) -> Fp8Weight:
+    """fp8 [..., 2F, K] [gate; up] in 128x128 blocks -> the fused-SwiGLU tile layout
+    (per 128 rows: 64 gate rows, 64 up rows). A tile then mixes two source blocks,
+    so the result carries one scale per 64 rows (sa_rows = 64)."""
+    assert w13.sa_rows == 128
+    *lead, two_f, K = w13.q.shape
+    F = two_f // 2
+    assert F % 64 == 0, "fused SwiGLU needs the FFN width to be a multiple of 64"
+    q = interleave_gate_up(w13.q.view(torch.uint8)).view(torch.float8_e4m3fn)
+    s64 = w13.s.repeat_interleave(2, -2)[..., : two_f // 64, :]  # one scale per 64 source rows
+    s = interleave_gate_up(s64.unsqueeze(-2).expand(*s64.shape[:-1], 64, s64.shape[-1]).reshape(
+        *lead, two_f, s64.shape[-1]))[..., ::64, :].contiguous()
+    return Fp8Weight(q, s, 64)
+
+
 def add_rmsnorm(x, residual, w, out, eps):
     kernels().add_rmsnorm(x, residual, w, out, float(eps))
     _count(1)
@@ -212,6 +234,100 @@ def quant_fp8_block(x):
     kernels().quant_fp8_block(x, q, s)
     _count(1)
     return q, s
+
+
+class Fp8Weight:
+    """Block-scaled fp8 weight: e4m3 values ``q`` [..., rows, K] and fp32 scales ``s``
+    [..., rows / sa_rows, K / 128], one per (sa_rows x 128) block (128: the 128x128
+    block format)."""
+
+    def __init__(self, q: torch.Tensor, s: torch.Tensor, sa_rows: int = 128):
+        self.q, self.s, self.sa_rows = q, s, sa_rows
+
+    @property
+    def shape(self):
+        return self.q.shape
+
+    def dequant(self) -> torch.Tensor:
+        """fp32 weights (oracle / tests)."""
+        rep = self.s.repeat_interleave(self.sa_rows, -2)[..., : self.q.shape[-2], :].repeat_interleave(128, -1)
+        return self.q.float() * rep[..., : self.q.shape[-1]]
+
+
+class Fp8Act:
+    """Quantised activations: e4m3 ``q`` [rows, K] and K-block-major scales ``s`` [K / 128, rows]."""
+
+    def __init__(self, q: torch.Tensor, s: torch.Tensor):
+        self.q, self.s = q, s
+
+    @property
+    def rows(self) -> int:
+        return self.q.shape[0]
+
+
+def quant_weight_fp8(rows: int, cols: int, *, src: torch.Tensor | None = None, seed: int = 0, std: float = 0.02,
+                     flat0: int = 0, device=None, out: Fp8Weight | None = None) -> Fp8Weight:
+    """128x128-block e4m3 weight from a bf16 tensor or from seeded N(0, std) samples
+    (element (r, c) is sample flat0 + r * cols + c, so shards are reproducible).
+    ``out`` receives the result in place (contiguous q [rows, cols] / s views)."""
+    dev = src.device if src is not None else device
+    if out is None:
+        q = torch.empty(rows, cols, dtype=torch.float8_e4m3fn, device=dev)
+        s = torch.empty((rows + 127) // 128, cols // 128, dtype=torch.float32, device=dev)
+        out = Fp8Weight(q, s, 128)
+    kernels().quant_weight_fp8(src.contiguous() if src is not None else None, int(seed), int(flat0), float(std),
+                               out.q.view(rows, cols), out.s.view(-1, cols // 128))
+    _count(1)
+    return out
+
+
+def quant_act_fp8(x: torch.Tensor, src_idx: torch.Tensor | None = None, idx_div: int = 1,
+                  rows: int | None = None, rows_dev: torch.Tensor | None = None, out: Fp8Act | None = None) -> Fp8Act:
+    """Per-(row, 128-column) e4m3 quantisation of bf16 activations; with ``src_idx``
+    row r is x[src_idx[r] // idx_div] (the MoE expert-sorted layout). ``rows_dev``
+    (int32 on the device) bounds the live rows when the count is only known there."""
+    R = rows if rows is not None else (src_idx.numel() if src_idx is not None else x.shape[0])
+    K = x.shape[1]
+    if out is None:
+        q = torch.empty(R, K, dtype=torch.float8_e4m3fn, device=x.device)
+        s = torch.empty(K // 128, max(R, 1), dtype=torch.float32, device=x.device)
+        out = Fp8Act(q, s)
+    if R > 0:
+        kernels().quant_act_fp8(x, src_idx, int(idx_div), rows_dev, out.q[:R], out.s)
+        _count(1)
+    return out
+
+
+def linear_fp8(x: Fp8Act, w: Fp8Weight, out: torch.Tensor | None = None, out_dtype=torch.bfloat16,
+               slab_out: bool = False, splits: int = 0):
+    """y = x @ dequant(w).T with tcgen05 fp8 MMAs (weights as the A operand, output
+    written transposed). With ``slab_out`` a split-K result is returned as ``Slabs``."""
+    T, K = x.q.shape
+    O = w.q.shape[0]
+    if out is None:
+        out = torch.empty(T, O, dtype=out_dtype, device=x.q.device)
+    if T == 0:
+        return out
+    r = kernels().gemm_fp8(w.q, w.s, w.sa_rows, x.q, x.s, out, O, T, K, 1, splits, 0, None, None, 0, 0,
+                           int(slab_out))
+    if r < 0:
+        _count(1)
+        return Slabs(-r, T, O)
+    _count(r)
+    return out
+
+
+def grouped_gemm_fp8(w: Fp8Weight, x_sorted: Fp8Act, out: torch.Tensor, grp_rows: torch.Tensor,
+                     grp_tiles: torch.Tensor, num_groups: int, block_n: int, swiglu: bool = False) -> torch.Tensor:
+    """MoE expert GEMM on fp8: out[r] = dequant(W[g(r)]) @ x_sorted[r] (rows sorted by
+    group; weights [G, M, K] with scales [G, M / sa_rows, K / 128])."""
+    G, M, K = w.q.shape
+    A = w.q.reshape(G * M, K)
+    sa = w.s.reshape(-1, w.s.shape[-1])
+    kernels().gemm_fp8(A, sa, w.sa_rows, x_sorted.q, x_sorted.s, out, M, x_sorted.rows, K, 1, 1, block_n, grp_rows,
+                       grp_tiles, num_groups, int(swiglu), 0)
+    _count(1)
+    return out
 
 
 def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 148) -> int:
@@ -241,9 +357,11 @@ def prefill_attention(q, k, kpe, v, o, cu_q, cu_k, max_q, scale, causal=True):
     return o
 
 
-def moe_topk(logits, bias, k, scoring, renorm, scaling, n_shared=0):
+def moe_topk(logits, bias, k, scoring, renorm, scaling, n_shared=0, n_group=1, topk_group=1, group_top2=False):
     """Top-k routing; the last n_shared columns are the shared experts E.. (weight 1).
-    ``logits`` is a [T, E] fp32 tensor or router ``Slabs``."""
+    ``logits`` is a [T, E] fp32 tensor or router ``Slabs``. With n_group > 1 the
+    choice is limited to the best `topk_group` expert groups, a group scored by its
+    best expert or (group_top2) by the sum of its best two."""
     if isinstance(logits, Slabs):
         T, E, dev = logits.rows, logits.cols, logits.ws.device
         src, stride, splits = logits.ws, logits.stride, logits.splits
@@ -253,7 +371,7 @@ def moe_topk(logits, bias, k, scoring, renorm, scaling, n_shared=0):
     ids = torch.empty(T, k + n_shared, dtype=torch.int32, device=dev)
     w = torch.empty(T, k + n_shared, dtype=torch.float32, device=dev)
     kernels().moe_topk(src, bias, ids, w, int(n_shared), int(scoring), bool(renorm), float(scaling), T, E, stride,
-                       splits)
+                       splits, int(n_group), int(topk_group), bool(group_top2))
     _count(1)
     return ids, w
 

@@ -141,7 +141,22 @@ class ExpertParallel:
         self.K.ep_gather(self.args(), self.epoch, j, self.grp_rows[self.n_local:], self.src_row, self.xs, self.budget)
         ops._count(2)
 
-    def experts(self, w13: torch.Tensor, w2: torch.Tensor, bn: int, fused_swiglu: bool = True):
+    def experts(self, w13, w2, bn: int, fused_swiglu: bool = True):
+        if isinstance(w13, ops.Fp8Weight):
+            # block-scaled fp8 experts: the live row count stays on the device
+            rows_dev = self.grp_rows[self.n_local:]
+            if getattr(self, "xq", None) is None:
+                R = self.xs.shape[0]
+                self.xq = ops.Fp8Act(torch.empty(R, self.H, dtype=torch.float8_e4m3fn, device=self.device),
+                                     torch.empty(self.H // 128, R, dtype=torch.float32, device=self.device))
+                F = self.act.shape[1]
+                self.aq = ops.Fp8Act(torch.empty(R, F, dtype=torch.float8_e4m3fn, device=self.device),
+                                     torch.empty(F // 128, R, dtype=torch.float32, device=self.device))
+            ops.quant_act_fp8(self.xs, rows_dev=rows_dev, out=self.xq)
+            ops.grouped_gemm_fp8(w13, self.xq, self.act, self.grp_rows, self.grp_tiles, self.n_local, bn, swiglu=True)
+            ops.quant_act_fp8(self.act, rows_dev=rows_dev, out=self.aq)
+            ops.grouped_gemm_fp8(w2, self.aq, self.y, self.grp_rows, self.grp_tiles, self.n_local, bn)
+            return
         if fused_swiglu:
             ops.grouped_gemm(w13, self.xs, self.act, self.grp_rows, self.grp_tiles, self.n_local, bn, swiglu=True)
         else:

@@ -30,6 +30,9 @@ def main():
     ap.add_argument("--ctx", type=int, default=1024)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = model default)")
+    ap.add_argument("--routed-experts", type=int, default=0,
+                    help="override the routed expert count: E / N with the per-GPU batch reproduces the expert "
+                         "load and weight bytes of one rank of an N-way expert-parallel run")
     ap.add_argument("--no-trace", action="store_true", help="run the steps without the profiler (for ncu)")
     ap.add_argument("--graph", action="store_true", help="replay the step as one CUDA graph")
     args = ap.parse_args()
@@ -42,6 +45,8 @@ def main():
     cfg = get_config(args.model)
     if args.layers:
         cfg = cfg.replace(num_layers=args.layers)
+    if args.routed_experts:
+        cfg = cfg.replace(n_routed_experts=args.routed_experts, n_group=1, topk_group=1)
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
     ep = None

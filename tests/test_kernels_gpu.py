@@ -272,29 +272,48 @@ def test_prefill_attention(qlens, klens):
 
 
 # ------------------------------------------------------------------ MoE routing
-@pytest.mark.parametrize("scoring,renorm,E,k", [(0, False, 64, 6), (1, True, 384, 8), (0, True, 8, 2)])
-def test_moe_topk(scoring, renorm, E, k):
+@pytest.mark.parametrize("scoring,renorm,E,k,groups", [(0, False, 64, 6, None), (1, True, 384, 8, None),
+                                                        (0, True, 8, 2, None), (1, True, 256, 8, (8, 4, "noaux_tc")),
+                                                        (0, False, 160, 6, (8, 3, "group_limited_greedy")),
+                                                        (0, False, 66, 4, None)])
+def test_moe_topk(scoring, renorm, E, k, groups):
     ops = _ops()
+    from sparkpipe_rs_b200.models import oracle
+    from sparkpipe_rs_b200.models.config import MLAMoEConfig
     T = 77
     g = torch.Generator(device=DEV).manual_seed(E)
     logits = torch.randn(T, E, device=DEV, generator=g)
     bias = torch.randn(E, device=DEV, generator=g) * 0.1 if scoring == 1 else None
-    ids, w = ops.moe_topk(logits, bias, k, scoring, renorm, 2.5, n_shared=2)
+    ng, tg, method = groups or (1, 1, "greedy")
+    ids, w = ops.moe_topk(logits, bias, k, scoring, renorm, 2.5, n_shared=2, n_group=ng, topk_group=tg,
+                          group_top2=method == "noaux_tc")
     assert torch.equal(ids[:, k:].cpu(), torch.tensor([[E, E + 1]] * T, dtype=torch.int32))
     assert torch.equal(w[:, k:].cpu(), torch.ones(T, 2))
     ids, w = ids[:, :k].contiguous(), w[:, :k].contiguous()
-    if scoring == 0:
-        sc = logits.softmax(-1)
-        sel = sc
-    else:
-        sc = logits.sigmoid()
-        sel = sc + bias
-    ref_ids = sel.topk(k, -1).indices
+    cfg = MLAMoEConfig(n_routed_experts=E, num_experts_per_tok=k, scoring_func=["softmax", "sigmoid"][scoring],
+                       norm_topk_prob=renorm, routed_scaling_factor=2.5, n_group=ng, topk_group=tg, topk_method=method)
+    eye = torch.eye(E, device=DEV)
+    ref_ids, ref_w, _ = oracle.route(cfg, logits, eye, bias)  # x @ I.T = the logits
     assert torch.equal(ids.long().sort(-1).values, ref_ids.sort(-1).values)
+    sc = logits.softmax(-1) if scoring == 0 else logits.sigmoid()
     rw = sc.gather(-1, ids.long())
     if renorm:
         rw = rw / rw.sum(-1, keepdim=True)
     _close(w, rw * 2.5, atol=1e-5, rtol=1e-5)
+
+
+def test_moe_topk_many_slabs():
+    """Router logits left as 8 split-K slabs: the fused slab sum selects like fp32."""
+    ops = _ops()
+    T, E, S = 64, 64, 8
+    g = torch.Generator(device=DEV).manual_seed(5)
+    slabs = torch.randn(S, T, E, device=DEV, generator=g)
+    lg = ops.Slabs.__new__(ops.Slabs)
+    lg.splits, lg.rows, lg.cols, lg.ws, lg.stride = S, T, E, slabs, T * E
+    ids, w = ops.moe_topk(lg, None, 6, 0, False, 1.0, n_shared=2)
+    full = slabs.sum(0)
+    assert torch.equal(ids[:, :6].long().sort(-1).values, full.softmax(-1).topk(6, -1).indices.sort(-1).values)
+    _close(w[:, :6], full.softmax(-1).gather(-1, ids[:, :6].long()), atol=1e-5, rtol=1e-5)
 
 
 def test_silu_mul_and_combine():

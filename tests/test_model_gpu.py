@@ -84,3 +84,58 @@ def test_prefill_then_decode_matches_oracle(q_lora):
             cur = out.clone()
         dg.release()
     assert ops.status_word() == 0
+
+
+def test_fp8_block_model_matches_oracle():
+    """Block-scaled fp8 weights (128x128 e4m3 blocks, fp32 scales) on every projection
+    and expert: the kernel model (fp8 tcgen05 GEMMs, activations quantised per 1x128
+    block) against the fp32 oracle run on the dequantised weights."""
+    from sparkpipe_rs_b200 import ops
+    from sparkpipe_rs_b200.models import oracle
+    from sparkpipe_rs_b200.models.mla_moe import DecodeGraph, ForwardBatch, KVCache, MLAMoEModel
+    from sparkpipe_rs_b200.models.weights import dequant_weights, init_weights
+
+    cfg = small_cfg(384).replace(weight_dtype="fp8_block", scoring_func="sigmoid", norm_topk_prob=True,
+                                 routed_scaling_factor=2.0)
+    w = init_weights(cfg, seed=3, device=DEV)
+    assert isinstance(w["l1.e_w13"], ops.Fp8Weight) and isinstance(w["l0.w13"], ops.Fp8Weight)
+    assert not isinstance(w["l1.w_kv_b"], ops.Fp8Weight) and w["lm_head"].dtype == torch.bfloat16
+    w_ref = dequant_weights(w)
+    model = MLAMoEModel(cfg, weights=w, device=DEV, max_positions=4096)
+    cache = KVCache(cfg, num_blocks=16, block_size=64, device=DEV)
+    lens = [40, 130]
+    B = len(lens)
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g, dtype=torch.int32) for n in lens]
+    bps = 4
+    bt = torch.arange(B * bps, dtype=torch.int32, device=DEV).view(B, bps)
+    ids = torch.cat(prompts).to(DEV)
+    pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in lens]).to(DEV)
+    slots = torch.cat([bt[b, torch.arange(n, device=DEV) // 64] * 64 + torch.arange(n, device=DEV, dtype=torch.int32) % 64
+                       for b, n in enumerate(lens)]).int()
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    fb = ForwardBatch(mode="prefill", token_ids=ids, positions=pos, slot_mapping=slots, cu_q=cu, cu_k=cu,
+                      max_q=max(lens), logits_idx=(cu[1:] - 1).contiguous())
+    logits = model.forward(fb, cache)
+    seqs = [p.to(DEV) for p in prompts]
+    for b in range(B):
+        ref = oracle.forward(cfg, w_ref, seqs[b], model.cos_sin)[-1]
+        assert _cos(logits[b], ref) > 0.98, f"fp8 prefill logits of seq {b} diverge: {_cos(logits[b], ref)}"
+    cur = ops.sample_tokens(logits)
+    dg = DecodeGraph(model, cache, B, bps, 300, use_graph=True)
+    for step in range(2):
+        ctx = torch.tensor([s.shape[0] for s in seqs], dtype=torch.int32)
+        dg.ids.copy_(cur)
+        dg.pos.copy_(ctx.to(DEV))
+        dg.ctx.copy_((ctx + 1).to(DEV))
+        dg.block_table.copy_(bt)
+        dg.slots.copy_(bt[torch.arange(B, device=DEV), (ctx // 64).long().to(DEV)] * 64 + (ctx % 64).to(DEV).int())
+        step_logits = model.forward(dg.fb, cache)
+        out = dg.run()
+        for b in range(B):
+            seqs[b] = torch.cat([seqs[b], cur[b:b + 1].to(DEV)])
+            ref = oracle.forward(cfg, w_ref, seqs[b], model.cos_sin)[-1]
+            assert _cos(step_logits[b], ref) > 0.98, f"fp8 decode step {step} seq {b}"
+        cur = out.clone()
+    dg.release()
+    assert ops.status_word() == 0
