@@ -185,6 +185,11 @@ void sample_tokens(const void* logits, long long ldl, int T, int V, float temper
 void spec_verify(const int* draft, const int* target, int B, int L, float forced_accept_p, unsigned long long seed,
                  unsigned long long offset, int* accepted, int* committed, cudaStream_t s);
 
+// End of a speculative round over j-major row arrays (row j*B + b, j = 0..L): acceptance, committed
+// tokens, and the next round's inputs (see sampling.cu).
+void spec_finish(int* tok_rows, const int* tgt_rows, int B, int L, float p_accept, unsigned long long seed,
+                 int* pos_rows, int* ctx_rows, int* slot_rows, const int* block_table, int max_blocks,
+                 int block_size, int* accepted, int* committed, unsigned long long* total_committed, cudaStream_t s);
 void decode_advance(const int* out_ids, int* ids, int* pos, int* ctx, int* slots, const int* block_table,
                     int max_blocks, int B, int block_size, cudaStream_t s);
 

@@ -448,6 +448,30 @@ void spec_verify(const Tensor& draft, const Tensor& target, double p_accept, int
                   committed.data_ptr<int>(), stream());
 }
 
+void spec_finish(const Tensor& tok_rows, const Tensor& tgt_rows, int64_t L, double p_accept, int64_t seed,
+                 const Tensor& pos_rows, const Tensor& ctx_rows, const Tensor& slot_rows, const Tensor& block_table,
+                 int64_t block_size, const Tensor& accepted, const Tensor& committed,
+                 const c10::optional<Tensor>& total_committed) {
+  CHECK_CUDA(tok_rows); CHECK_I32(tok_rows); CHECK_I32(tgt_rows); CHECK_I32(pos_rows); CHECK_I32(ctx_rows);
+  CHECK_I32(slot_rows); CHECK_I32(block_table); CHECK_I32(accepted); CHECK_I32(committed);
+  CHECK_CONTIG(block_table); CHECK_CONTIG(committed);
+  const int64_t B = accepted.numel();
+  TORCH_CHECK(tok_rows.numel() == (L + 1) * B && tgt_rows.numel() >= (L + 1) * B && pos_rows.numel() == (L + 1) * B &&
+                  ctx_rows.numel() == (L + 1) * B && slot_rows.numel() == (L + 1) * B &&
+                  committed.numel() == (L + 1) * B && block_table.size(0) >= B,
+              "spec_finish: row arrays must hold (L + 1) x B entries");
+  unsigned long long* tc = nullptr;
+  if (total_committed.has_value()) {
+    TORCH_CHECK(total_committed->scalar_type() == at::kLong, "total_committed must be int64");
+    tc = reinterpret_cast<unsigned long long*>(total_committed->data_ptr<int64_t>());
+  }
+  const c10::cuda::CUDAGuard guard(tok_rows.device());
+  sp::spec_finish(tok_rows.data_ptr<int>(), tgt_rows.data_ptr<int>(), (int)B, (int)L, (float)p_accept,
+                  (unsigned long long)seed, pos_rows.data_ptr<int>(), ctx_rows.data_ptr<int>(),
+                  slot_rows.data_ptr<int>(), block_table.data_ptr<int>(), (int)block_table.size(1), (int)block_size,
+                  accepted.data_ptr<int>(), committed.data_ptr<int>(), tc, stream());
+}
+
 void decode_advance(const Tensor& out_ids, const Tensor& ids, const Tensor& pos, const Tensor& ctx,
                     const Tensor& slots, const Tensor& block_table, int64_t block_size) {
   CHECK_CUDA(ids); CHECK_I32(out_ids); CHECK_I32(ids); CHECK_I32(pos); CHECK_I32(ctx); CHECK_I32(slots);
@@ -593,6 +617,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample_tokens", &sample_tokens);
   m.def("spec_verify", &spec_verify);
   m.def("decode_advance", &decode_advance);
+  m.def("spec_finish", &spec_finish);
   m.def("slab_add_rmsnorm", &slab_add_rmsnorm);
   m.def("mla_decode_prep", &mla_decode_prep);
   m.def("combine_add_rmsnorm", &combine_add_rmsnorm);

@@ -153,6 +153,65 @@ void spec_verify(const int* draft, const int* target, int B, int L, float forced
            (uint64_t)seed, (uint64_t)offset, accepted, committed);
 }
 
+// End of one speculative round, one thread per sequence b. Row arrays are
+// j-major (row j*B + b, j = 0..L): tok_rows holds the round's inputs (t_0 = the
+// last committed token, t_j = draft token j), tgt_rows the verifier's greedy
+// token after each input. Acceptance is the longest draft prefix the verifier
+// agrees with, or (p_accept > 0, benchmarking) a seeded Bernoulli(p) chain keyed
+// by (seed, position of t_0, b, j). Writes the committed tokens (accepted drafts,
+// then the verifier's token at the first rejection), and advances the row arrays
+// in place for the next round: t_0 <- that verifier token, positions / context
+// lengths / cache slots of rows j = new position + j. Context lengths are clamped
+// to the block table, so a sequence that ran out of blocks never reads past it.
+__global__ void spec_finish_kernel(int* __restrict__ tok_rows, const int* __restrict__ tgt_rows, int B, int L,
+                                   float p_accept, uint64_t seed, int* __restrict__ pos_rows,
+                                   int* __restrict__ ctx_rows, int* __restrict__ slot_rows,
+                                   const int* __restrict__ block_table, int max_blocks, int block_size,
+                                   int* __restrict__ accepted, int* __restrict__ committed,
+                                   unsigned long long* __restrict__ total_committed) {
+  griddep_wait();
+  griddep_launch();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int p0 = pos_rows[b];
+  if (p0 < 0) return;  // idle row
+  int a = 0;
+  for (; a < L; ++a) {
+    bool ok;
+    if (p_accept > 0.f) ok = uniform01(seed, (uint64_t)p0, b, a) < p_accept;
+    else ok = tok_rows[(a + 1) * B + b] == tgt_rows[a * B + b];
+    if (!ok) break;
+  }
+  for (int i = 0; i <= L; ++i) {
+    int t = -1;
+    if (i < a) t = tok_rows[(i + 1) * B + b];
+    else if (i == a) t = tgt_rows[a * B + b];
+    committed[b * (L + 1) + i] = t;
+  }
+  accepted[b] = a;
+  if (total_committed) atomicAdd(total_committed, (unsigned long long)(a + 1));
+  tok_rows[b] = tgt_rows[a * B + b];
+  const int np = p0 + a + 1;
+  const int cap = max_blocks * block_size;
+  for (int j = 0; j <= L; ++j) {
+    const int p = np + j;
+    const int blk = p / block_size;
+    pos_rows[j * B + b] = p;
+    ctx_rows[j * B + b] = min(p + 1, cap);
+    slot_rows[j * B + b] = blk < max_blocks ? block_table[(long long)b * max_blocks + blk] * block_size + p % block_size
+                                            : -1;
+  }
+}
+
+void spec_finish(int* tok_rows, const int* tgt_rows, int B, int L, float p_accept, unsigned long long seed,
+                 int* pos_rows, int* ctx_rows, int* slot_rows, const int* block_table, int max_blocks,
+                 int block_size, int* accepted, int* committed, unsigned long long* total_committed, cudaStream_t s) {
+  if (B <= 0) return;
+  launch_k(spec_finish_kernel, dim3((B + 127) / 128), dim3(128), 0, s, tok_rows, tgt_rows, B, L, p_accept,
+           (uint64_t)seed, pos_rows, ctx_rows, slot_rows, block_table, max_blocks, block_size, accepted, committed,
+           total_committed);
+}
+
 // Feeds a decode step's sampled tokens back as the next step's inputs: token id,
 // position + 1, context length + 1 and the cache slot of the new position
 // (from the block table; -1 once the table is exhausted). Rows with a zero

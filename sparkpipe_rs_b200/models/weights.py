@@ -103,15 +103,21 @@ def dequant_weights(w: dict) -> dict:
 
 
 def init_weights(cfg: MLAMoEConfig, seed: int = 0, device="cpu", dtype=torch.bfloat16,
-                 layers: list[int] | None = None, experts: tuple[int, int] | None = None) -> dict[str, torch.Tensor]:
+                 layers: list[int] | None = None, experts: tuple[int, int] | None = None,
+                 share: dict | None = None) -> dict[str, torch.Tensor]:
     """Random-init weights. ``layers`` restricts which decoder layers are created;
     ``experts`` = (lo, hi) keeps only routed experts lo..hi-1 (plus every shared
     expert) of the expert tensors, as one expert-parallel rank holds them. The
-    kept rows are bit-identical to the same rows of the full tensors."""
+    kept rows are bit-identical to the same rows of the full tensors. Tensors
+    named in ``share`` are taken from it instead of being created (a draft head
+    sharing the target's embedding and LM head)."""
     shapes = weight_shapes(cfg)
     out: dict[str, torch.Tensor] = {}
     dev = torch.device(device)
     for idx, (name, shape) in enumerate(shapes.items()):
+        if share is not None and name in share:
+            out[name] = share[name]
+            continue
         if layers is not None and name.startswith("l"):
             li = int(name[1:name.index(".")])
             if li not in layers:

@@ -1,0 +1,138 @@
+"""Speculative decoding (draft head + batched verify + spec_finish) on the GPU.
+
+Greedy acceptance must reproduce greedy decoding of the target: every committed
+token is the target's (near-)argmax given the committed prefix, and every
+accepted draft token is the draft's argmax given the same prefix (which checks
+both models' KV handling across accepted and rejected rounds). The forced
+Bernoulli(p) mode must accept chains at the rate p implies."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _cfg():
+    from sparkpipe_rs_b200.models.config import v2_lite
+
+    return v2_lite().replace(name="small-spec", num_layers=2, hidden_size=1024, n_routed_experts=16,
+                             num_experts_per_tok=4, moe_intermediate_size=256, intermediate_size=2048,
+                             n_shared_experts=1, vocab_size=512, first_k_dense_replace=1, init_std=0.05)
+
+
+def _prefill(model, cache, prompts, bt):
+    from sparkpipe_rs_b200 import ops
+    from sparkpipe_rs_b200.models.mla_moe import ForwardBatch
+
+    lens = [len(p) for p in prompts]
+    ids = torch.cat(prompts).to(DEV)
+    pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in lens]).to(DEV)
+    slots = torch.cat([bt[b, torch.arange(n, device=DEV) // 64] * 64 + torch.arange(n, device=DEV, dtype=torch.int32) % 64
+                       for b, n in enumerate(lens)]).int()
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    fb = ForwardBatch(mode="prefill", token_ids=ids, positions=pos, slot_mapping=slots, cu_q=cu, cu_k=cu,
+                      max_q=max(lens), logits_idx=(cu[1:] - 1).contiguous())
+    return ops.sample_tokens(model.forward(fb, cache))
+
+
+def _full_logits(model, seq):
+    """Logits after every position of `seq` (a fresh prefill in a scratch cache)."""
+    from sparkpipe_rs_b200.models.mla_moe import ForwardBatch, KVCache
+
+    n = seq.shape[0]
+    cache = KVCache(model.cfg, num_blocks=(n + 63) // 64 + 1, block_size=64, device=DEV)
+    cu = torch.tensor([0, n], dtype=torch.int32, device=DEV)
+    fb = ForwardBatch(mode="prefill", token_ids=seq.to(DEV).int(), positions=torch.arange(n, dtype=torch.int32, device=DEV),
+                      slot_mapping=torch.arange(n, dtype=torch.int32, device=DEV), cu_q=cu, cu_k=cu, max_q=n)
+    return model.forward(fb, cache).float()
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_greedy_spec_decode_equals_greedy_target(use_graph):
+    from sparkpipe_rs_b200 import ops
+    from sparkpipe_rs_b200.models.mla_moe import KVCache, MLAMoEModel
+    from sparkpipe_rs_b200.serving.spec_decode import SpecDecoder, make_draft
+
+    cfg = _cfg()
+    target = MLAMoEModel(cfg, seed=0, device=DEV, max_positions=1024)
+    draft = make_draft(target, seed=5, max_positions=1024)
+    B, L, bps = 3, 3, 4
+    tc = KVCache(cfg, num_blocks=B * bps, device=DEV)
+    dc = KVCache(draft.cfg, num_blocks=B * bps, device=DEV)
+    bt = torch.arange(B * bps, dtype=torch.int32, device=DEV).view(B, bps)
+    g = torch.Generator().manual_seed(4)
+    lens = [20, 63, 90]
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g, dtype=torch.int32) for n in lens]
+    first = _prefill(target, tc, prompts, bt)
+    _prefill(draft, dc, prompts, bt)
+    sd = SpecDecoder(target, draft, tc, dc, B, L, bps, bps * 64, use_graph=use_graph)
+    sd.start(first, torch.tensor(lens, dtype=torch.int32), bt)
+    seqs = [torch.cat([p, first[b:b + 1].cpu()]) for b, p in enumerate(prompts)]
+    accepted_total = 0
+    for _ in range(12):
+        acc, com = sd.round()
+        acc, com = acc.cpu(), com.cpu()
+        for b in range(B):
+            a = int(acc[b])
+            accepted_total += a
+            seqs[b] = torch.cat([seqs[b], com[b, :a + 1]])
+            assert (com[b, a + 1:] == -1).all()
+    assert sd.committed_tokens() == sum(s.shape[0] for s in seqs) - sum(lens) - B
+    for b in range(B):
+        s = seqs[b]
+        tl = _full_logits(target, s)
+        for i in range(lens[b], s.shape[0]):
+            row = tl[i - 1]
+            # every committed token is the target's greedy choice (up to near ties)
+            assert row[int(s[i])] >= row.max() - 0.05, (b, i)
+    assert ops.status_word() == 0
+    sd.release()
+
+
+def test_forced_acceptance_rate():
+    """Seeded Bernoulli(0.7) acceptance: the accepted-chain rate matches 0.7; every
+    accepted draft is the draft head's greedy token and every verifier token the
+    target's, each given the committed prefix (the draft's KV survives rounds
+    that accepted all L drafts)."""
+    from sparkpipe_rs_b200 import ops
+    from sparkpipe_rs_b200.models.mla_moe import KVCache, MLAMoEModel
+    from sparkpipe_rs_b200.serving.spec_decode import SpecDecoder, make_draft
+
+    cfg = _cfg()
+    target = MLAMoEModel(cfg, seed=0, device=DEV, max_positions=4096)
+    draft = make_draft(target, seed=5, max_positions=4096)
+    B, L, bps = 32, 3, 4
+    tc = KVCache(cfg, num_blocks=B * bps, device=DEV)
+    dc = KVCache(draft.cfg, num_blocks=B * bps, device=DEV)
+    bt = torch.arange(B * bps, dtype=torch.int32, device=DEV).view(B, bps)
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, cfg.vocab_size, (16,), generator=g, dtype=torch.int32) for _ in range(B)]
+    first = _prefill(target, tc, prompts, bt)
+    _prefill(draft, dc, prompts, bt)
+    sd = SpecDecoder(target, draft, tc, dc, B, L, bps, bps * 64, p_accept=0.7, seed=11)
+    sd.start(first, torch.full((B,), 16, dtype=torch.int32), bt)
+    seqs = [torch.cat([p, first[b:b + 1].cpu()]) for b, p in enumerate(prompts)]
+    kinds = [[] for _ in range(B)]  # per committed token: "d" accepted draft, "v" verifier token
+    rounds, acc_sum = 40, 0
+    for _ in range(rounds):
+        acc, com = sd.round()
+        acc, com = acc.cpu(), com.cpu()
+        acc_sum += int(acc.sum())
+        for b in range(B):
+            a = int(acc[b])
+            seqs[b] = torch.cat([seqs[b], com[b, :a + 1]])
+            kinds[b] += ["d"] * a + ["v"]
+    mean = acc_sum / (rounds * B)
+    expect = 0.7 + 0.7 ** 2 + 0.7 ** 3  # E[accepted drafts] for L = 3
+    assert abs(mean - expect) < 0.12, mean
+    assert sd.committed_tokens() == acc_sum + rounds * B
+    for b in range(4):
+        s = seqs[b]
+        tl, dl = _full_logits(target, s), _full_logits(draft, s)
+        for n, kind in enumerate(kinds[b]):
+            i = 17 + n  # position of the committed token
+            row = (dl if kind == "d" else tl)[i - 1]
+            assert row[int(s[i])] >= row.max() - 0.05, (b, i, kind)
+    assert ops.status_word() == 0
+    sd.release()
