@@ -294,6 +294,19 @@ SP_DEVI float warp_max(float v) {
   return v;
 }
 
+// One warp quantises one 128-wide block (4 values per lane) to e4m3 with an fp32
+// scale amax / 448 (1 for an all-zero block). Every kernel that produces
+// block-scaled fp8 activations uses this, so all of them round identically.
+SP_DEVI uint32_t warp_quant_e4m3_block(float x0, float x1, float x2, float x3, float& scale) {
+  float amax = fmaxf(fmaxf(fabsf(x0), fabsf(x1)), fmaxf(fabsf(x2), fabsf(x3)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  scale = amax > 0.f ? amax / 448.f : 1.f;
+  const float inv = 1.f / scale;
+  __nv_fp8x4_e4m3 q(make_float4(x0 * inv, x1 * inv, x2 * inv, x3 * inv));
+  return *reinterpret_cast<uint32_t*>(&q);
+}
+
 SP_DEVI void st_bf16x8(__nv_bfloat16* dst, const float* v) {
   __align__(16) __nv_bfloat162 h[4];
 #pragma unroll

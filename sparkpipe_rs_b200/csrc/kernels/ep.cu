@@ -118,7 +118,7 @@ SP_DEVI u64* meta_words(const EpArgs& a, int r, int buf, int src, int row) {
          ((int64_t(buf) * a.world + src) * a.cap + row) * (2 + 2 * a.kk);
 }
 SP_DEVI u64* row_words(const EpArgs& a, int r, int buf, int src, int row) {
-  return reinterpret_cast<u64*>(rank_base(a, r) + a.off_rows) + ((int64_t(buf) * a.world + src) * a.cap + row) * (a.H / 2);
+  return reinterpret_cast<u64*>(rank_base(a, r) + a.off_rows) + ((int64_t(buf) * a.world + src) * a.cap + row) * a.row_words;
 }
 SP_DEVI u64* comb_words(const EpArgs& a, int r, int buf, int slot) {
   return reinterpret_cast<u64*>(rank_base(a, r) + a.off_comb) + (int64_t(buf) * a.cap * a.kk + slot) * (a.H / 2);
@@ -152,6 +152,31 @@ SP_DEVI void warp_send_row(u64* dst, const bf16* src, int H, uint32_t tag) {
         st_ll2(dst + 4 * c, ll_word(v[u].x, tag), ll_word(v[u].y, tag));
         st_ll2(dst + 4 * c + 2, ll_word(v[u].z, tag), ll_word(v[u].w, tag));
       }
+    }
+  }
+}
+
+// fp8 transport: one warp quantises and sends one row. Block b of 128 columns
+// becomes 32 payload words (4 e4m3 per lane) at words [32b, 32b + 32) and one
+// scale word at H/4 + b; the quantiser is the one quant_act_fp8 uses.
+SP_DEVI void warp_send_row_fp8(u64* dst, const bf16* src, int H, uint32_t tag) {
+  const int lane = threadIdx.x & 31;
+  const int nb = H / 128;
+  for (int b0 = 0; b0 < nb; b0 += EP_ROW_STEPS) {
+    uint2 v[EP_ROW_STEPS];
+#pragma unroll
+    for (int u = 0; u < EP_ROW_STEPS; ++u)
+      if (b0 + u < nb) v[u] = __ldcg(reinterpret_cast<const uint2*>(src + (b0 + u) * 128 + lane * 4));
+#pragma unroll
+    for (int u = 0; u < EP_ROW_STEPS; ++u) {
+      const int b = b0 + u;
+      if (b >= nb) break;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[u]);
+      const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
+      float scale;
+      const uint32_t q = warp_quant_e4m3_block(f0.x, f0.y, f1.x, f1.y, scale);
+      st_ll(dst + b * 32 + lane, ll_word(q, tag));
+      if (lane == 0) st_ll(dst + H / 4 + b, ll_word(__float_as_uint(scale), tag));
     }
   }
 }
@@ -203,8 +228,11 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const bf16* __restrict
   }
   __syncthreads();
   const int n = s_n;
-  for (int i = warp; i < n; i += blockDim.x / 32)
-    warp_send_row(row_words(a, d, buf, a.rank, c * EP_CHUNK_TOKENS + i), x + int64_t(s_tok[i]) * ldx, a.H, tag);
+  for (int i = warp; i < n; i += blockDim.x / 32) {
+    u64* dst = row_words(a, d, buf, a.rank, c * EP_CHUNK_TOKENS + i);
+    if (a.fp8) warp_send_row_fp8(dst, x + int64_t(s_tok[i]) * ldx, a.H, tag);
+    else warp_send_row(dst, x + int64_t(s_tok[i]) * ldx, a.H, tag);
+  }
 }
 
 constexpr int EP_ALIGN_MAX_E = 1024;
@@ -330,7 +358,7 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(EpArgs a, const int64_t*
   bool ok = true;
   const int nc = a.H / 8;
   for (int p = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); p < n && ok; p += warps) {
-    const u64* src = base + int64_t(src_row[p]) * (a.H / 2);
+    const u64* src = base + int64_t(src_row[p]) * a.row_words;
     uint4* dst = reinterpret_cast<uint4*>(xs + int64_t(p) * a.H);
     for (int c0 = 0; c0 < nc && ok; c0 += 32 * EP_ROW_STEPS) {
       u64 w[EP_ROW_STEPS][4];
@@ -356,6 +384,61 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(EpArgs a, const int64_t*
         }
         dst[c] = make_uint4(v[0], v[1], v[2], v[3]);
       }
+    }
+  }
+  if (!ok) atomicCAS(gerr, 0, kErrWaitTimeoutPeer);
+}
+
+// fp8 transport: received rows -> expert-sorted e4m3 rows + K-block-major scales;
+// one warp per row, lanes move 2 payload words (8 e4m3) per step.
+__global__ void __launch_bounds__(256) ep_gather_fp8_kernel(EpArgs a, const int64_t* __restrict__ epoch_ptr, int layer,
+                                                            const int* __restrict__ total,
+                                                            const int* __restrict__ src_row, uint8_t* __restrict__ xq,
+                                                            long long ldq, float* __restrict__ xs_scale, long long lds,
+                                                            long long budget, int* __restrict__ gerr) {
+  griddep_wait();
+  griddep_launch();
+  int buf;
+  const uint32_t tag = epoch_tag(epoch_ptr, a, layer, &buf);
+  const int n = *total;
+  const u64* base = row_words(a, a.rank, buf, 0, 0);
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x / 32);
+  const int npairs = a.H / 8;  // word pairs of payload
+  const int nb = a.H / 128;
+  bool ok = true;
+  for (int p = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); p < n && ok; p += warps) {
+    const u64* src = base + int64_t(src_row[p]) * a.row_words;
+    uint2* dst = reinterpret_cast<uint2*>(xq + int64_t(p) * ldq);
+    for (int c0 = 0; c0 < npairs && ok; c0 += 32 * EP_ROW_STEPS) {
+      u64 w[EP_ROW_STEPS][2];
+#pragma unroll
+      for (int u = 0; u < EP_ROW_STEPS; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < npairs) ld_ll2(src + 2 * c, w[u][0], w[u][1]);
+      }
+#pragma unroll
+      for (int u = 0; u < EP_ROW_STEPS; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c >= npairs) continue;
+        uint32_t v0, v1;
+        if (tag_of(w[u][0]) == tag && tag_of(w[u][1]) == tag) {
+          v0 = uint32_t(w[u][0]);
+          v1 = uint32_t(w[u][1]);
+        } else {
+          bool ok2 = true;
+          v0 = poll_ll(src + 2 * c, tag, budget, ok2, gerr);
+          v1 = poll_ll(src + 2 * c + 1, tag, budget, ok2, gerr);
+          if (!ok2) { ok = false; break; }
+        }
+        dst[c] = make_uint2(v0, v1);
+      }
+    }
+    for (int b = lane; b < nb && ok; b += 32) {
+      bool ok2 = true;
+      const uint32_t sc = poll_ll(src + a.H / 4 + b, tag, budget, ok2, gerr);
+      if (!ok2) { ok = false; break; }
+      xs_scale[int64_t(b) * lds + p] = __uint_as_float(sc);
     }
   }
   if (!ok) atomicCAS(gerr, 0, kErrWaitTimeoutPeer);
@@ -480,6 +563,9 @@ static void check_args(const EpArgs& a) {
   if (a.cap >= (1 << 20) / a.kk) throw std::runtime_error("ep: token capacity too large for the slot encoding");
   if (a.cap % EP_CHUNK_TOKENS || a.max_chunks != a.cap / EP_CHUNK_TOKENS)
     throw std::runtime_error("ep: capacity must be whole token chunks");
+  const long long need = a.fp8 ? a.H / 4 + ((a.H / 128 + 1) & ~1) : a.H / 2;
+  if (a.fp8 && a.H % 128) throw std::runtime_error("ep: the fp8 transport needs H % 128 == 0");
+  if (a.row_words != need) throw std::runtime_error("ep: row stride does not match the transport");
 }
 
 void ep_dispatch(const void* x, int64_t ldx, const int* ids, int T, const EpArgs& a, const int64_t* epoch, int layer,
@@ -506,6 +592,15 @@ void ep_gather(const EpArgs& a, const int64_t* epoch, int layer, const int* tota
                long long budget, int* err, int num_sms, cudaStream_t s) {
   launch_k(ep_gather_kernel, dim3(num_sms), dim3(256), 0, s, a, epoch, layer, total, src_row, static_cast<bf16*>(xs),
            budget, err);
+}
+
+void ep_gather_fp8(const EpArgs& a, const int64_t* epoch, int layer, const int* total, const int* src_row, void* xq,
+                   long long ldq, float* xs_scale, long long lds, long long budget, int* err, int num_sms,
+                   cudaStream_t s) {
+  check_args(a);
+  if (!a.fp8) throw std::runtime_error("ep: fp8 gather on a bf16 transport");
+  launch_k(ep_gather_fp8_kernel, dim3(num_sms), dim3(256), 0, s, a, epoch, layer, total, src_row,
+           static_cast<uint8_t*>(xq), ldq, xs_scale, lds, budget, err);
 }
 
 void ep_combine_send(const void* y, const int* total, const int* comb_dst, const EpArgs& a, const int64_t* epoch,

@@ -503,12 +503,9 @@ __global__ void quant_act_fp8_kernel(const __nv_bfloat16* __restrict__ x, long l
     const uint2 raw = *reinterpret_cast<const uint2*>(src);
     const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&raw);
     const float2 f0 = __bfloat1622float2(hv[0]), f1 = __bfloat1622float2(hv[1]);
-    float amax = fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y)));
-    amax = warp_max(amax);
-    const float scale = amax > 0.f ? amax / 448.f : 1.f;
-    const float inv = 1.f / scale;
-    __nv_fp8x4_e4m3 o(make_float4(f0.x * inv, f0.y * inv, f1.x * inv, f1.y * inv));
-    *reinterpret_cast<__nv_fp8x4_e4m3*>(q + (long long)r * ldq + b * 128 + lane * 4) = o;
+    float scale;
+    const uint32_t o = warp_quant_e4m3_block(f0.x, f0.y, f1.x, f1.y, scale);
+    *reinterpret_cast<uint32_t*>(q + (long long)r * ldq + b * 128 + lane * 4) = o;
     if (lane == 0) s[(long long)b * lds + r] = scale;
   }
 }

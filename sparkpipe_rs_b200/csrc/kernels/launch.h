@@ -204,12 +204,19 @@ struct EpArgs {
   unsigned long long base[EP_MAX_RANKS];
   long long off_ctrl, off_nch, off_meta, off_rows, off_comb;
   int world, rank, cap, H, kk, n_routed, experts_per_rank, n_shared, moe_layers, max_chunks;
+  int fp8;              // dispatched rows travel as e4m3 + one fp32 scale per 128 columns
+  long long row_words;  // tagged words per dispatched row (H/2 bf16; H/4 + even(H/128) fp8)
 };
-constexpr int EP_ARGS_WORDS = EP_MAX_RANKS + 5 + 10;
+constexpr int EP_ARGS_WORDS = EP_MAX_RANKS + 5 + 10 + 2;
 void ep_dispatch(const void* x, int64_t ldx, const int* ids, int T, const EpArgs& a, const int64_t* epoch, int layer,
                  cudaStream_t s);
 void ep_recv_align(const EpArgs& a, const int64_t* epoch, int layer, int bn, int* grp_rows, int* grp_tiles,
                    int* src_row, int* comb_dst, long long budget, int* err, cudaStream_t s);
+// fp8 transport: received rows -> expert-sorted e4m3 rows xq [*, H] (pitch ldq) and
+// K-block-major scales xs_scale[kb * lds + row]
+void ep_gather_fp8(const EpArgs& a, const int64_t* epoch, int layer, const int* total, const int* src_row, void* xq,
+                   long long ldq, float* xs_scale, long long lds, long long budget, int* err, int num_sms,
+                   cudaStream_t s);
 void ep_gather(const EpArgs& a, const int64_t* epoch, int layer, const int* total, const int* src_row, void* xs,
                long long budget, int* err, int num_sms, cudaStream_t s);
 void ep_combine_send(const void* y, const int* total, const int* comb_dst, const EpArgs& a, const int64_t* epoch,

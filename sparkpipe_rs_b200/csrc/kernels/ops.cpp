@@ -525,6 +525,7 @@ sp::EpArgs ep_args(const std::vector<int64_t>& v) {
   a.world = (int)v[i++]; a.rank = (int)v[i++]; a.cap = (int)v[i++]; a.H = (int)v[i++]; a.kk = (int)v[i++];
   a.n_routed = (int)v[i++]; a.experts_per_rank = (int)v[i++]; a.n_shared = (int)v[i++]; a.moe_layers = (int)v[i++];
   a.max_chunks = (int)v[i++];
+  a.fp8 = (int)v[i++]; a.row_words = v[i++];
   for (int r = 0; r < a.world; ++r) TORCH_CHECK(a.base[r] != 0 && a.base[r] % 256 == 0, "ep: bad rank base pointer");
   return a;
 }
@@ -563,6 +564,19 @@ void ep_gather(const std::vector<int64_t>& args, const Tensor& epoch, int64_t la
   TORCH_CHECK(xs.size(1) == a.H, "ep: xs width");
   sp::ep_gather(a, epoch.data_ptr<int64_t>(), (int)layer, total.data_ptr<int>(), src_row.data_ptr<int>(),
                 xs.data_ptr(), budget_cycles, err_word(), num_sms(), stream());
+}
+
+void ep_gather_fp8(const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, const Tensor& total,
+                   const Tensor& src_row, const Tensor& xq, const Tensor& xs_scale, int64_t budget_cycles) {
+  CHECK_FP8(xq); CHECK_F32(xs_scale); CHECK_I32(src_row); CHECK_I32(total);
+  TORCH_CHECK(xq.dim() == 2 && xq.stride(1) == 1 && xs_scale.dim() == 2 && xs_scale.stride(1) == 1, "ep: 2-D views");
+  const c10::cuda::CUDAGuard guard(xq.device());
+  const sp::EpArgs a = ep_args(args);
+  TORCH_CHECK(xq.size(1) == a.H && xs_scale.size(0) * 128 == a.H, "ep: fp8 gather shapes");
+  TORCH_CHECK(xq.size(0) >= src_row.numel() && xs_scale.stride(0) >= xq.size(0), "ep: fp8 gather capacity");
+  sp::ep_gather_fp8(a, epoch.data_ptr<int64_t>(), (int)layer, total.data_ptr<int>(), src_row.data_ptr<int>(),
+                    xq.data_ptr(), xq.stride(0), xs_scale.data_ptr<float>(), xs_scale.stride(0), budget_cycles,
+                    err_word(), num_sms(), stream());
 }
 
 void ep_combine_send(const Tensor& y, const Tensor& total, const Tensor& comb_dst, const std::vector<int64_t>& args,
@@ -632,6 +646,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dispatch", &ep_dispatch);
   m.def("ep_recv_align", &ep_recv_align);
   m.def("ep_gather", &ep_gather);
+  m.def("ep_gather_fp8", &ep_gather_fp8);
   m.def("ep_combine_send", &ep_combine_send);
   m.def("ep_combine_add_rmsnorm", &ep_combine_add_rmsnorm);
   m.def("ep_advance", &ep_advance);

@@ -38,7 +38,13 @@ CHUNK_TOKENS = 8    # tokens per dispatch CTA (csrc/kernels/launch.h EP_CHUNK_TO
 COMBINE_CTAS = 16   # combine-send CTAs per destination (EP_COMBINE_CTAS)
 
 
-def ep_layout(world: int, cap: int, hidden: int, kk: int) -> dict:
+def row_words(hidden: int, fp8: bool) -> int:
+    """Tagged words per dispatched row: H/2 for bf16 rows; for the fp8 transport
+    H/4 words of e4m3 plus one scale word per 128 columns (rounded to even)."""
+    return hidden // 4 + ((hidden // 128 + 1) & ~1) if fp8 else hidden // 2
+
+
+def ep_layout(world: int, cap: int, hidden: int, kk: int, fp8: bool = False) -> dict:
     """Byte offsets of the EP regions inside one rank's buffer (cap: whole token
     chunks). Every region holds 8-byte tagged words (4 payload bytes each)."""
     off = {}
@@ -54,7 +60,7 @@ def ep_layout(world: int, cap: int, hidden: int, kk: int) -> dict:
     region("ctrl", 2 * max_ranks * chunks)             # rows per (source, chunk)
     region("nch", 2 * max_ranks)                       # chunks per source
     region("meta", 2 * world * cap * (2 + 2 * kk))     # (token, n, experts, k-slots) per row
-    region("rows", 2 * world * cap * hidden // 2)      # received hidden rows
+    region("rows", 2 * world * cap * row_words(hidden, fp8))  # received hidden rows
     region("comb", 2 * cap * kk * hidden // 2)         # returned expert outputs per (token, k-slot)
     off["total"] = pos
     return off
@@ -62,7 +68,11 @@ def ep_layout(world: int, cap: int, hidden: int, kk: int) -> dict:
 
 class ExpertParallel:
     def __init__(self, cfg, rank: int, world: int, cap_tokens: int, device, group=None,
-                 budget_cycles: int = DEFAULT_BUDGET_CYCLES):
+                 budget_cycles: int = DEFAULT_BUDGET_CYCLES, fp8_transport: bool | None = None):
+        """``fp8_transport`` (default: the model has block-scaled fp8 weights) sends
+        dispatched rows as e4m3 with one fp32 scale per 128 columns, quantised
+        once in the dispatch kernel: half the NVLink bytes, and the receiver
+        gathers them straight into the fp8 expert GEMM's operand layout."""
         assert cfg.n_routed_experts % world == 0, "routed experts must split evenly over the ranks"
         assert 1 <= world <= 8
         cap_tokens = -(-cap_tokens // CHUNK_TOKENS) * CHUNK_TOKENS
@@ -77,7 +87,9 @@ class ExpertParallel:
         self.moe_index = {layer: j for j, layer in enumerate(self.moe_layers)}
         # even layer count per step -> MoE layer j always uses buffer parity j & 1
         self.layers_per_step = len(self.moe_layers) + (len(self.moe_layers) & 1)
-        self.layout = ep_layout(world, cap_tokens, self.H, self.kk)
+        self.fp8 = (cfg.weight_dtype == "fp8_block") if fp8_transport is None else bool(fp8_transport)
+        self.row_words = row_words(self.H, self.fp8)
+        self.layout = ep_layout(world, cap_tokens, self.H, self.kk, self.fp8)
         K = _ext.kernels()
         self.K = K
         self.buf = K.ep_alloc(self.layout["total"], self.device.index or 0)
@@ -100,8 +112,16 @@ class ExpertParallel:
         self.grp_tiles = torch.zeros(self.n_local + 1, dtype=torch.int32, device=dev)
         self.src_row = torch.zeros(max_pairs, dtype=torch.int32, device=dev)
         self.comb_dst = torch.zeros(max_pairs, dtype=torch.int32, device=dev)
-        self.xs = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
         F = cfg.moe_intermediate_size
+        if self.fp8:
+            self.xs = None
+            self.xq = ops.Fp8Act(torch.zeros(max_pairs, self.H, dtype=torch.float8_e4m3fn, device=dev),
+                                 torch.zeros(self.H // 128, max_pairs, dtype=torch.float32, device=dev))
+            self.aq = ops.Fp8Act(torch.zeros(max_pairs, F, dtype=torch.float8_e4m3fn, device=dev),
+                                 torch.zeros(F // 128, max_pairs, dtype=torch.float32, device=dev))
+        else:
+            self.xs = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
+            self.xq = self.aq = None
         self.act = torch.zeros(max_pairs, F, dtype=torch.bfloat16, device=dev)
         self.y = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
 
@@ -124,7 +144,7 @@ class ExpertParallel:
         c = self.cfg
         return (list(self.bases) + [L["ctrl"], L["nch"], L["meta"], L["rows"], L["comb"]] +
                 [self.world, self.rank, self.cap, self.H, self.kk, c.n_routed_experts, self.El,
-                 c.n_shared_experts, self.layers_per_step, self.cap // CHUNK_TOKENS])
+                 c.n_shared_experts, self.layers_per_step, self.cap // CHUNK_TOKENS, int(self.fp8), self.row_words])
 
     def local_expert_range(self) -> tuple[int, int]:
         return self.rank * self.El, (self.rank + 1) * self.El
@@ -138,25 +158,26 @@ class ExpertParallel:
         j = self.moe_index[layer]
         self.K.ep_recv_align(self.args(), self.epoch, j, bn, self.grp_rows, self.grp_tiles, self.src_row,
                              self.comb_dst, self.budget)
-        self.K.ep_gather(self.args(), self.epoch, j, self.grp_rows[self.n_local:], self.src_row, self.xs, self.budget)
+        if self.fp8:
+            self.K.ep_gather_fp8(self.args(), self.epoch, j, self.grp_rows[self.n_local:], self.src_row, self.xq.q,
+                                 self.xq.s, self.budget)
+        else:
+            self.K.ep_gather(self.args(), self.epoch, j, self.grp_rows[self.n_local:], self.src_row, self.xs,
+                             self.budget)
         ops._count(2)
 
     def experts(self, w13, w2, bn: int, fused_swiglu: bool = True):
         if isinstance(w13, ops.Fp8Weight):
-            # block-scaled fp8 experts: the live row count stays on the device
+            # block-scaled fp8 experts; the live row count stays on the device
+            if not self.fp8:
+                raise ValueError("expert parallel: fp8 expert weights need the fp8 transport")
             rows_dev = self.grp_rows[self.n_local:]
-            if getattr(self, "xq", None) is None:
-                R = self.xs.shape[0]
-                self.xq = ops.Fp8Act(torch.empty(R, self.H, dtype=torch.float8_e4m3fn, device=self.device),
-                                     torch.empty(self.H // 128, R, dtype=torch.float32, device=self.device))
-                F = self.act.shape[1]
-                self.aq = ops.Fp8Act(torch.empty(R, F, dtype=torch.float8_e4m3fn, device=self.device),
-                                     torch.empty(F // 128, R, dtype=torch.float32, device=self.device))
-            ops.quant_act_fp8(self.xs, rows_dev=rows_dev, out=self.xq)
             ops.grouped_gemm_fp8(w13, self.xq, self.act, self.grp_rows, self.grp_tiles, self.n_local, bn, swiglu=True)
             ops.quant_act_fp8(self.act, rows_dev=rows_dev, out=self.aq)
             ops.grouped_gemm_fp8(w2, self.aq, self.y, self.grp_rows, self.grp_tiles, self.n_local, bn)
             return
+        if self.fp8:
+            raise ValueError("expert parallel: the fp8 transport needs fp8 expert weights")
         if fused_swiglu:
             ops.grouped_gemm(w13, self.xs, self.act, self.grp_rows, self.grp_tiles, self.n_local, bn, swiglu=True)
         else:

@@ -111,6 +111,85 @@ def test_emulated_ranks_match_single_gpu(world):
     assert ops.status_word() == 0
 
 
+def _fp8_slice(w, lo, hi, E):
+    """Routed experts lo..hi-1 plus the shared ones of a 3-D Fp8Weight."""
+    q = torch.cat([w.q[lo:hi].view(torch.uint8), w.q[E:].view(torch.uint8)]).view(torch.float8_e4m3fn)
+    return ops.Fp8Weight(q.contiguous(), torch.cat([w.s[lo:hi], w.s[E:]]).contiguous(), w.sa_rows)
+
+
+def _local_moe_fp8(cfg, xn, w13i, w2, ids, wts, res, gamma, eps, bn):
+    E, S = cfg.n_routed_experts, cfg.n_shared_experts
+    kk = cfg.num_experts_per_tok + S
+    T = xn.shape[0]
+    grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E + S, bn)
+    xq = ops.quant_act_fp8(xn, sorted_tok)
+    act = torch.empty(T * kk, cfg.moe_intermediate_size, dtype=torch.bfloat16, device=xn.device)
+    ops.grouped_gemm_fp8(w13i, xq, act, grp_rows, grp_tiles, E + S, bn, swiglu=True)
+    y = torch.empty(T * kk, cfg.hidden_size, dtype=torch.bfloat16, device=xn.device)
+    ops.grouped_gemm_fp8(w2, ops.quant_act_fp8(act), y, grp_rows, grp_tiles, E + S, bn)
+    out = torch.empty_like(xn)
+    ops.combine_add_rmsnorm(y, inv_pos, wts, res, gamma, out, kk, eps)
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_emulated_ranks_fp8_transport_match_single_gpu(world):
+    """fp8 experts: rows cross as e4m3 + 128-column scales, quantised in the dispatch
+    kernel with the same quantiser as the local path, so EP equals local bit for bit."""
+    torch.manual_seed(1)
+    dev = torch.device("cuda")
+    cfg = _cfg().replace(weight_dtype="fp8_block")
+    E, S, H = cfg.n_routed_experts, cfg.n_shared_experts, cfg.hidden_size
+    kk = cfg.num_experts_per_tok + S
+    full = init_weights(cfg, seed=4, device=dev)
+    layers = [i for i in range(cfg.num_layers) if cfg.is_moe_layer(i)]
+    w13i = {i: ops.interleave_gate_up_fp8(full[f"l{i}.e_w13"]) for i in layers}
+    ranks = ExpertParallel.emulated(cfg, world, cap_tokens=48, device=dev)
+    assert ranks[0].fp8
+    El = E // world
+    local = [{i: (ops.interleave_gate_up_fp8(_fp8_slice(full[f"l{i}.e_w13"], r * El, (r + 1) * El, E)),
+                  _fp8_slice(full[f"l{i}.e_w2"], r * El, (r + 1) * El, E)) for i in layers} for r in range(world)]
+    tokens = [9, 0, 48, 30][:world]
+    gamma = torch.rand(H, device=dev, dtype=torch.bfloat16) + 0.5
+    ops.clear_status()
+    for layer in layers:
+        p = f"l{layer}."
+        xs, ids, wts, res = [], [], [], []
+        for r in range(world):
+            x = (torch.randn(tokens[r], H, device=dev) * 0.5).to(torch.bfloat16)
+            logits = (x.float() @ full[p + "gate"].float().t()).contiguous()
+            i, w_ = ops.moe_topk(logits, torch.randn(E, device=dev) * 0.1, cfg.num_experts_per_tok, 1, True, 2.5,
+                                 n_shared=S)
+            xs.append(x); ids.append(i); wts.append(w_)
+            res.append(torch.randn(tokens[r], H, device=dev).to(torch.bfloat16))
+        bn = max(32, min(128, _moe_block_n(max(tokens) * kk, ranks[0].n_local)))
+        for r in range(world):
+            ranks[r].dispatch(layer, xs[r], ids[r])
+        for r in range(world):
+            ranks[r].receive(layer, bn)
+        for r in range(world):
+            ranks[r].experts(local[r][layer][0], local[r][layer][1], bn)
+        for r in range(world):
+            ranks[r].combine_send(layer)
+        for r in range(world):
+            res_ep = res[r].clone()
+            out_ep = torch.empty_like(xs[r])
+            ranks[r].combine_add_rmsnorm(layer, wts[r], res_ep, gamma, out_ep, cfg.rms_norm_eps)
+            if tokens[r] == 0:
+                continue
+            res_ref = res[r].clone()
+            out_ref = _local_moe_fp8(cfg, xs[r], w13i[layer], full[p + "e_w2"], ids[r], wts[r], res_ref, gamma,
+                                     cfg.rms_norm_eps, 32)
+            torch.cuda.synchronize()
+            assert ops.status_word() == 0
+            assert torch.equal(res_ep, res_ref), (layer, r, (res_ep.float() - res_ref.float()).abs().max())
+            assert torch.equal(out_ep, out_ref)
+    for r in ranks:
+        r.end_step()
+    torch.cuda.synchronize()
+    assert ops.status_word() == 0
+
+
 def test_receive_wait_times_out_with_status():
     dev = torch.device("cuda")
     cfg = _cfg()
