@@ -62,6 +62,9 @@ def main():
     cache.data.normal_(0, 1)
     bt = torch.arange(B * bps, dtype=torch.int32, device=dev).view(B, bps)
     dg = DecodeGraph(model, cache, B, bps, args.ctx + args.steps + 8, use_graph=args.graph, self_advance=True)
+    # distinct tokens per row, so routing spreads over the experts as in serving
+    dg.ids.copy_(torch.randint(0, cfg.vocab_size, (B,), generator=torch.Generator().manual_seed(0),
+                               dtype=torch.int32))
     dg.block_table.copy_(bt)
     dg.pos.fill_(args.ctx)
     dg.ctx.fill_(args.ctx + 1)
