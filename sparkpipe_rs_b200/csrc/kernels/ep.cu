@@ -44,66 +44,14 @@
 // all-to-all of its own.
 #include "common.cuh"
 #include "launch.h"
+#include "ll.cuh"
 #include "pdl.h"
 
 namespace sp {
 
 using bf16 = __nv_bfloat16;
-using u64 = unsigned long long;
 
 namespace {
-SP_DEVI u64 ll_word(uint32_t payload, uint32_t tag) { return (u64(tag) << 32) | payload; }
-SP_DEVI void st_ll(u64* p, u64 w) { asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory"); }
-SP_DEVI void st_ll2(u64* p, u64 a, u64 b) {  // two independent 64-bit elements (each single-copy atomic)
-  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
-}
-SP_DEVI u64 ld_ll(const u64* p) {
-  u64 v;
-  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-SP_DEVI void ld_ll2(const u64* p, u64& a, u64& b) {
-  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
-}
-SP_DEVI uint32_t tag_of(u64 w) { return uint32_t(w >> 32); }
-
-// Every poll is bounded twice: by its own clock64 budget, and by the device
-// status word: once any poll of the device has given up (status set), every
-// other poll gives up at its next check, so a kernel whose peer is gone ends
-// after one budget, not one budget per word.
-SP_DEVI bool poll_abort(const int* gerr) { return *reinterpret_cast<const volatile int*>(gerr) != 0; }
-
-// Bounded poll of one word; returns its payload (0 and ok = false on timeout).
-SP_DEVI uint32_t poll_ll(const u64* p, uint32_t tag, long long budget, bool& ok, int* gerr) {
-  u64 w = ld_ll(p);
-  if (tag_of(w) == tag) return uint32_t(w);
-  const long long t0 = clock64();
-  for (unsigned it = 1;; ++it) {
-    w = ld_ll(p);
-    if (tag_of(w) == tag) return uint32_t(w);
-    if (clock64() - t0 > budget) { atomicCAS(gerr, 0, kErrWaitTimeoutPeer); ok = false; return 0; }
-    if ((it & 255) == 0 && poll_abort(gerr)) { ok = false; return 0; }
-  }
-}
-// Bounded poll of four consecutive words (8 bf16); false on timeout.
-SP_DEVI bool poll_ll4(const u64* p, uint32_t tag, long long budget, uint32_t (&v)[4], int* gerr) {
-  u64 w0, w1, w2, w3;
-  ld_ll2(p, w0, w1);
-  ld_ll2(p + 2, w2, w3);
-  if (tag_of(w0) != tag || tag_of(w1) != tag || tag_of(w2) != tag || tag_of(w3) != tag) {
-    const long long t0 = clock64();
-    for (unsigned it = 1;; ++it) {
-      ld_ll2(p, w0, w1);
-      ld_ll2(p + 2, w2, w3);
-      if (tag_of(w0) == tag && tag_of(w1) == tag && tag_of(w2) == tag && tag_of(w3) == tag) break;
-      if (clock64() - t0 > budget) { atomicCAS(gerr, 0, kErrWaitTimeoutPeer); return false; }
-      if ((it & 255) == 0 && poll_abort(gerr)) return false;
-    }
-  }
-  v[0] = uint32_t(w0); v[1] = uint32_t(w1); v[2] = uint32_t(w2); v[3] = uint32_t(w3);
-  return true;
-}
-
 SP_DEVI uint8_t* rank_base(const EpArgs& a, int r) { return reinterpret_cast<uint8_t*>(a.base[r]); }
 // (rows in chunk c of source src) on rank r
 SP_DEVI u64* ctrl_word(const EpArgs& a, int r, int buf, int src, int c) {

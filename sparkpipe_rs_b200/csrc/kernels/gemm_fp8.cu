@@ -51,7 +51,7 @@ struct Fp8KParams {
   int M, N, K;
   const float* sa;
   long long ldsa;
-  int sa_rows;
+  int sa_rows, sa_blocks;
   const float* sb;
   long long ldsb;
   void* D;
@@ -76,8 +76,25 @@ struct F8Cfg {
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int HALF = BN / 2;                       // columns per epilogue warp
   static constexpr int XBUF_BYTES = 2 * 64 * 17 * 4;        // SwiGLU exchange (2 halves x 64 rows x 16 cols)
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + XBUF_BYTES;
+  static constexpr int SC = 16;                              // K blocks per staged scale chunk
+  static constexpr int SCALE_BYTES = 2 * SC * (BN + 2) * 4;  // [2 chunks][SC][BN activation + 2 weight scales]
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + XBUF_BYTES + SCALE_BYTES;
 };
+
+// Named barrier 1 over the 256 epilogue threads that also ANDs a flag, so every
+// epilogue thread takes the same path after a timeout.
+SP_DEVI bool epi_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(uint32_t(v))
+      : "memory");
+  return r != 0;
+}
 
 struct F8Tile {
   int a_row, b_row;
@@ -156,8 +173,9 @@ SP_DEVI void f8_store_row(const Fp8KParams& p, void* Dp, long long ldd, int out_
   }
 }
 
+// Split-K CTAs with narrow tiles keep two per SM (registers capped at 102).
 template <int BN, int MODE>
-__global__ void __launch_bounds__(F8_THREADS, 1)
+__global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 2 : 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const Fp8KParams p) {
   using C = F8Cfg<BN, MODE>;
@@ -172,6 +190,8 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
   volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* s_ntiles = s_err + 1;
   float* xbuf = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + 256);
+  float* s_sb = xbuf + C::XBUF_BYTES / 4;            // [2][SC][BN]
+  float* s_sa = s_sb + 2 * C::SC * BN;               // [2][SC][2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -305,6 +325,13 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
     const int m = q * 32 + lane;  // tile row
     const int c_lo = h * HALF;
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
+    // Scales are staged per chunk of SC K blocks in shared memory (double buffered):
+    // the next chunk's global loads are in flight while this chunk is promoted, so no
+    // K block waits on a scale load.
+    constexpr int SC = C::SC;
+    constexpr int NSB = (SC * BN + 255) / 256;  // activation-scale items per thread per chunk
+    const int etid = threadIdx.x - 64;
+    const int my_sa = p.sa_rows == 64 ? (m >> 6) : 0;
     int it = 0;
     bool ok = true;
     for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
@@ -313,28 +340,69 @@ __global__ void __launch_bounds__(F8_THREADS, 1)
       float acc[HALF];
 #pragma unroll
       for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
-      const float* sa_row = p.sa + (long long)((ti.a_row + m) / p.sa_rows) * p.ldsa;
-      for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
-        const int b = it & 1;
-        const uint32_t bph = (it >> 1) & 1;
-        // scales first: their loads overlap the wait for the partial product
-        const float sa_v = (m < ti.m_valid) ? __ldg(sa_row + kb) : 0.f;
-        const float* sb_k = p.sb + (long long)kb * p.ldsb + ti.n_base + c_lo;
-        float sc[HALF];
+      const int nkb = kb_end - kb_begin;
+      const int nch = (nkb + SC - 1) / SC;
+      const int blk0 = ti.a_row / p.sa_rows;
+      float rsb[NSB], rsa = 0.f;
+      auto load_chunk = [&](int ch) {
+        const int kb0 = kb_begin + ch * SC;
 #pragma unroll
-        for (int j = 0; j < HALF; ++j)
-          sc[j] = (c_lo + j < ti.n_valid) ? sa_v * __ldg(sb_k + j) : 0.f;
-        if (!mbar_wait(&pfull[b], bph, s_err, p.err, kErrWaitTimeoutEpilogue)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < HALF; c += 16) {
-          float v[16];
-          tmem_ld16(lane_addr + b * BN + c_lo + c, v);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) acc[c + j] = fmaf(v[j], sc[c + j], acc[c + j]);
+        for (int u = 0; u < NSB; ++u) {
+          const int i = etid + u * 256;
+          const int j = i / BN, col = i - (i / BN) * BN;
+          const int kb = kb0 + j;
+          rsb[u] = (i < SC * BN && kb < kb_end && col < ti.n_valid)
+                       ? __ldg(p.sb + (long long)kb * p.ldsb + ti.n_base + col) : 0.f;
         }
-        tc_fence_before();
-        mbar_arrive(&pempty[b]);
+        if (etid < 2 * SC) {
+          const int j = etid >> 1, r = etid & 1, kb = kb0 + j;
+          const int blk = blk0 + r;
+          rsa = (kb < kb_end && r * p.sa_rows < F8_BM && blk < p.sa_blocks) ? __ldg(p.sa + (long long)blk * p.ldsa + kb)
+                                                                           : 0.f;
+        }
+      };
+      auto store_chunk = [&](int ch) {
+        float* dsb = s_sb + (ch & 1) * SC * BN;
+#pragma unroll
+        for (int u = 0; u < NSB; ++u) {
+          const int i = etid + u * 256;
+          if (i < SC * BN) dsb[i] = rsb[u];
+        }
+        if (etid < 2 * SC) s_sa[(ch & 1) * SC * 2 + etid] = rsa;
+      };
+      load_chunk(0);
+      store_chunk(0);
+      ok = epi_bar_and(ok);
+      for (int ch = 0; ch < nch; ++ch) {
+        if (ch + 1 < nch) load_chunk(ch + 1);
+        const float* csb = s_sb + (ch & 1) * SC * BN + c_lo;
+        const float* csa = s_sa + (ch & 1) * SC * 2 + my_sa;
+        const int kend = min(SC, nkb - ch * SC);
+        for (int j = 0; j < kend; ++j, ++it) {
+          if (!ok) continue;
+          const int b = it & 1;
+          const uint32_t bph = (it >> 1) & 1;
+          if (!mbar_wait(&pfull[b], bph, s_err, p.err, kErrWaitTimeoutEpilogue)) { ok = false; continue; }
+          tc_fence_after();
+          const float sa_v = m < ti.m_valid ? csa[j * 2] : 0.f;
+#pragma unroll
+          for (int c = 0; c < HALF; c += 16) {
+            float v[16];
+            tmem_ld16(lane_addr + b * BN + c_lo + c, v);
+#pragma unroll
+            for (int q4 = 0; q4 < 16; q4 += 4) {
+              const float4 sb4 = *reinterpret_cast<const float4*>(csb + j * BN + c + q4);
+              acc[c + q4] = fmaf(v[q4], sa_v * sb4.x, acc[c + q4]);
+              acc[c + q4 + 1] = fmaf(v[q4 + 1], sa_v * sb4.y, acc[c + q4 + 1]);
+              acc[c + q4 + 2] = fmaf(v[q4 + 2], sa_v * sb4.z, acc[c + q4 + 2]);
+              acc[c + q4 + 3] = fmaf(v[q4 + 3], sa_v * sb4.w, acc[c + q4 + 3]);
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(&pempty[b]);
+        }
+        if (ch + 1 < nch) store_chunk(ch + 1);
+        ok = epi_bar_and(ok);
       }
       if (!ok) break;
       if (MODE == F8_SPLITK) {
@@ -431,7 +499,7 @@ int gemm_fp8(const Fp8Launch& g) {
   if (!g.sa || !g.sb) throw std::runtime_error("gemm_fp8: scales missing");
   Fp8KParams p = {};
   p.M = g.M; p.N = g.N; p.K = g.K;
-  p.sa = g.sa; p.ldsa = g.ldsa; p.sa_rows = g.sa_rows;
+  p.sa = g.sa; p.ldsa = g.ldsa; p.sa_rows = g.sa_rows; p.sa_blocks = g.sa_blocks;
   p.sb = g.sb; p.ldsb = g.ldsb;
   p.D = g.D; p.ldd = g.ldd; p.trans_out = g.trans_out; p.out_f32 = g.out_f32;
   p.err = g.err;

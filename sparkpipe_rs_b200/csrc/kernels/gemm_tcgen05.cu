@@ -39,6 +39,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "ll.cuh"
 #include "pdl.h"
 
 namespace sp {
@@ -65,6 +66,20 @@ struct GemmKParams {
   float* ws;          // split-K partial slabs: [splits][N][M] (trans_out) or [splits][M][N], fp32
   long long split_stride;
   int* err;
+  // Tensor parallelism over peer memory (LL tagged words, ll.cuh):
+  //  * tp_rs: the epilogue sends fp32 partials of token n to rank n / tp_rows, slot
+  //    (tp_rank * splits + split) of its reduce-scatter region [2][W*S][tp_rows][M];
+  //  * tp_ag: B rows are read from this rank's all-gather region [2][rows][ag_row_words]
+  //    of bf16 pairs that the peers wrote; the producer warp polls them into the
+  //    swizzled shared-memory tile the MMA reads.
+  unsigned long long tp_base[8];
+  long long tp_rs_off;
+  int tp_rs, tp_rank, tp_world, tp_rows;
+  const unsigned long long* tp_ag;
+  long long tp_ag_parity_words, tp_ag_row_words;
+  const int64_t* tp_epoch;
+  int tp_layer, tp_layers_per_step;
+  long long tp_budget;
 };
 
 constexpr int BM = 128;
@@ -169,6 +184,66 @@ SP_DEVI void store_chunk(const GemmKParams& p, const TileInfo& ti, int m, int c0
   }
 }
 
+// Tensor-parallel reduce-scatter epilogue: 16 fp32 partials of row m (tile
+// columns c0..c0+15 = tokens) go to their owner ranks as tagged words. Lanes hold
+// consecutive m, so a warp's stores to one token are 256 contiguous bytes.
+template <int BN>
+SP_DEVI void rs_store16(const GemmKParams& p, const TileInfo& ti, int m, int c0, const float (&v)[16], int ks,
+                        uint32_t tag, int buf) {
+  if (m >= ti.m_valid) return;
+  const long long mg = ti.m_base + m;
+  const int slots = p.tp_world * p.splits;
+  const int slot = p.tp_rank * p.splits + ks;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int n = c0 + j;
+    if (n < ti.n_valid) {
+      const int ng = ti.n_base + n;
+      const int owner = ng / p.tp_rows, nl = ng - owner * p.tp_rows;
+      u64* dst = reinterpret_cast<u64*>(p.tp_base[owner] + p.tp_rs_off) +
+                 ((((long long)buf * slots + slot) * p.tp_rows + nl) * p.M + mg);
+      st_ll(dst, ll_word(__float_as_uint(v[j]), tag));
+    }
+  }
+}
+
+SP_DEVI uint32_t tp_tag(const GemmKParams& p, int* buf) {
+  const u64 e = u64(*p.tp_epoch) * p.tp_layers_per_step + p.tp_layer;
+  *buf = int(e & 1);
+  return uint32_t(e + 1);
+}
+
+// All-gather operand: the producer warp fills the B stage (BN rows x 64 bf16, the
+// 128-byte swizzled K-major layout TMA would write: 16-byte chunk c of row r at
+// chunk c ^ (r & 7)) from tagged words; rows past N are zero. Returns false when
+// a peer's words did not arrive within the budget (the tile is zero-filled).
+template <int BN>
+SP_DEVI bool ag_fill_b(const GemmKParams& p, uint8_t* sb, int b_row, int k0, uint32_t tag, int buf) {
+  const int lane = threadIdx.x & 31;
+  const u64* base = p.tp_ag + buf * p.tp_ag_parity_words;
+  bool ok = true;
+  for (int q = lane; q < BN * 8; q += 32) {
+    const int r = q >> 3, c = q & 7;
+    const int row = b_row + r;
+    uint32_t v[4] = {0u, 0u, 0u, 0u};
+    if (row < p.N && ok) {
+      const u64* w = base + (long long)row * p.tp_ag_row_words + (k0 >> 1) + c * 4;
+      u64 w0, w1, w2, w3;
+      ld_ll2(w, w0, w1);
+      ld_ll2(w + 2, w2, w3);
+      if (tag_of(w0) == tag && tag_of(w1) == tag && tag_of(w2) == tag && tag_of(w3) == tag) {
+        v[0] = uint32_t(w0); v[1] = uint32_t(w1); v[2] = uint32_t(w2); v[3] = uint32_t(w3);
+      } else if (!poll_ll4(w, tag, p.tp_budget, v, p.err)) {
+        ok = false;
+        v[0] = v[1] = v[2] = v[3] = 0u;
+      }
+    }
+    *reinterpret_cast<uint4*>(sb + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(v[0], v[1], v[2], v[3]);
+  }
+  fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor cores
+  return ok;
+}
+
 template <int BN, int MODE>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -192,7 +267,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], p.tp_ag ? 2 : 1);  // all-gather operand: TMA bytes of A + the warp's B fill
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -214,7 +289,7 @@ __global__ void __launch_bounds__(192, 1)
   // PDL: weights (A) never change while serving, so the producer may stream the
   // first stages of A before the previous kernel has finished; everything else
   // (B activations, outputs, device-side tile counts) waits for it.
-  const bool prefetch_a = (MODE != MODE_GROUPED) && p.a_evict_first;
+  const bool prefetch_a = (MODE != MODE_GROUPED) && p.a_evict_first && !p.tp_ag;
   const bool is_producer = (warp == 0 && lane == 0);
   if (MODE == MODE_GROUPED) griddep_wait();  // the tile count lives in device memory
   if (threadIdx.x == 0) {
@@ -242,7 +317,50 @@ __global__ void __launch_bounds__(192, 1)
     tile_step = 1 << 30;  // exactly one tile
   }
 
-  if (warp == 0) {
+  if (warp == 0 && p.tp_ag) {
+    // ------------------------------------------------------------ producer, all-gather operand
+    // A (weights) by TMA from lane 0; B rows polled from the peers' tagged words by the
+    // whole warp. Every stage gets both arrivals even after a timeout, so in-flight
+    // TMA loads always complete before the CTA exits.
+    int buf;
+    const uint32_t tag = tp_tag(p, &buf);
+    const uint64_t pol_a = p.a_evict_first ? policy_evict_first() : policy_evict_last();
+    int it = 0;
+    bool ok = true;
+    for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
+      TileInfo ti;
+      if (!get_tile<BN, MODE>(p, t, ti)) continue;
+      for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+        const int s = it % C::STAGES;
+        const uint32_t ph = (it / C::STAGES) & 1;
+        uint8_t* sa = smem + s * C::STAGE_BYTES;
+        int go = 1;
+        if (lane == 0) {
+          go = mbar_wait(&empty[s], ph ^ 1, s_err, p.err, kErrWaitTimeoutProducer) ? 1 : 0;
+          if (go) {
+            mbar_arrive_expect_tx(&full[s], C::A_BYTES);
+            tma_load_2d_hint(sa, &tmA, &full[s], ti.a_k + kb * BK, ti.a_row, pol_a);
+          }
+        }
+        go = __shfl_sync(0xffffffffu, go, 0);
+        if (!go) { ok = false; break; }
+        const bool filled = ag_fill_b<BN>(p, sa + C::A_BYTES, ti.b_row, ti.b_k + kb * BK, tag, buf);
+        __syncwarp();
+        if (lane == 0) {
+          if (!filled) *s_err = kErrWaitTimeoutPeer;
+          mbar_arrive(&full[s]);
+        }
+        if (__any_sync(0xffffffffu, !filled)) { ok = false; ++it; break; }
+      }
+    }
+    if (!ok && lane == 0) {
+      for (int j = 0; j < C::STAGES && j < it; ++j) {
+        const int i2 = it - 1 - j;
+        mbar_wait(&full[i2 % C::STAGES], (i2 / C::STAGES) & 1, s_err, nullptr, 0);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol_a = p.a_evict_first ? policy_evict_first() : policy_evict_last();
@@ -360,6 +478,14 @@ __global__ void __launch_bounds__(192, 1)
             }
             asm volatile("bar.sync 1, 128;" ::: "memory");
           }
+        } else if (p.tp_rs) {
+          int rbuf;
+          const uint32_t tag = tp_tag(p, &rbuf);
+          for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
+            float v[16];
+            tmem_ld16(lane_addr + buf * BN + c0, v);
+            rs_store16<BN>(p, ti, m, c0, v, 0, tag, rbuf);
+          }
         } else {
           for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
             float v[16];
@@ -383,10 +509,13 @@ __global__ void __launch_bounds__(192, 1)
       ti.d_off = 0;
       if (mbar_wait(&tfull[0], 0, s_err, p.err, kErrWaitTimeoutEpilogue)) {
         tc_fence_after();
+        int rbuf = 0;
+        const uint32_t tag = p.tp_rs ? tp_tag(p, &rbuf) : 0u;
         for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
           float v[16];
           tmem_ld16(lane_addr + c0, v);
-          store_chunk<BN>(q, ti, m, c0, v);
+          if (p.tp_rs) rs_store16<BN>(p, ti, m, c0, v, ks, tag, rbuf);
+          else store_chunk<BN>(q, ti, m, c0, v);
         }
         tc_fence_before();
       }
@@ -473,7 +602,8 @@ static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
   using C = GemmCfg<BN, MODE>;
   CUtensorMap ta, tb;
   make_tmap_2d(&ta, g.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.a_rows, g.a_cols, g.lda, BM, BK);
-  make_tmap_2d(&tb, g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.b_rows, g.b_cols, g.ldb, BN, BK);
+  if (p.tp_ag) tb = ta;  // B comes from tagged words, not TMA
+  else make_tmap_2d(&tb, g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.b_rows, g.b_cols, g.ldb, BN, BK);
   auto kern = gemm_bf16_kernel<BN, MODE>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -552,6 +682,23 @@ int gemm_bf16(const GemmLaunch& g) {
   if (g.swiglu && (!g.grouped || !g.trans_out || g.out_f32 || g.M % 128 != 0))
     throw std::runtime_error("gemm: fused SwiGLU needs a grouped, transposed bf16 GEMM with M % 128 == 0");
   p.m_tiles = (g.M + BM - 1) / BM;
+  if (g.tp) {
+    const TpGemm& t = *g.tp;
+    if (g.grouped || g.batch != 1) throw std::runtime_error("gemm: tensor-parallel operands need a plain GEMM");
+    if (!t.epoch || t.world < 1 || t.world > 8 || t.rank < 0 || t.rank >= t.world || t.rows <= 0)
+      throw std::runtime_error("gemm: bad tensor-parallel arguments");
+    for (int r = 0; r < t.world; ++r)
+      if (!t.base[r] || (t.base[r] & 255)) throw std::runtime_error("gemm: bad tensor-parallel rank base");
+    if (t.rs && (!g.trans_out || g.N > t.world * t.rows))
+      throw std::runtime_error("gemm: reduce-scatter needs a transposed output over world x rows tokens");
+    if (t.ag && (g.N > t.world * t.rows || g.b_k0 % BK || g.K % BK || (g.b_k0 + g.K) / 2 > t.ag_row_words))
+      throw std::runtime_error("gemm: all-gather operand needs whole 64-column K blocks inside its rows");
+    for (int r = 0; r < 8; ++r) p.tp_base[r] = t.base[r];
+    p.tp_rs_off = t.rs_off; p.tp_rs = t.rs; p.tp_rank = t.rank; p.tp_world = t.world; p.tp_rows = t.rows;
+    p.tp_ag = static_cast<const unsigned long long*>(t.ag);
+    p.tp_ag_parity_words = t.ag_parity_words; p.tp_ag_row_words = t.ag_row_words;
+    p.tp_epoch = t.epoch; p.tp_layer = t.layer; p.tp_layers_per_step = t.layers_per_step; p.tp_budget = t.budget;
+  }
   if (g.grouped) {
     const int bn = g.block_n > 0 ? g.block_n : 32;
     p.n_tiles = 0;
@@ -573,6 +720,14 @@ int gemm_bf16(const GemmLaunch& g) {
     while (splits < 8 && p.num_tiles * splits * 2 <= 2 * g.num_sms && kbs / (splits * 2) >= 2) splits *= 2;
   }
   if (splits > kbs) splits = kbs;  // every split CTA needs at least one K block
+  if (g.tp && g.tp->rs) {
+    // partials go straight to the owners' slots: no workspace, no reduction kernel
+    splits = std::max(1, std::min(splits, g.tp->max_splits));
+    p.splits = splits;
+    if (splits > 1) dispatch_bn<MODE_SPLITK>(bn, g, p);
+    else dispatch_bn<MODE_DENSE>(bn, g, p);
+    return 1;
+  }
   const long long slab = (long long)g.M * g.N;
   // the slab reduction needs dense, 4-aligned rows and a workspace that fits
   const int out_cols = g.trans_out ? g.M : g.N;

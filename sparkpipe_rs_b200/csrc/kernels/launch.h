@@ -9,6 +9,21 @@
 namespace sp {
 
 // D[m, n] = sum_k A[m, k] * B[n, k]; see gemm_tcgen05.cu for the modes.
+// Tensor-parallel operands of a GEMM over peer memory (gemm_tcgen05.cu): a
+// reduce-scatter epilogue into the owner ranks' slots and/or an all-gathered B
+// operand read from this rank's tagged-word region.
+struct TpGemm {
+  unsigned long long base[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // rank buffer bases (peer pointers)
+  long long rs_off = 0;          // reduce-scatter region: [2][world * splits][rows][M] words
+  int rs = 0, rank = 0, world = 1, rows = 0;
+  const void* ag = nullptr;      // all-gather region of this rank: [2][world * rows][ag_row_words] words
+  long long ag_parity_words = 0, ag_row_words = 0;
+  const int64_t* epoch = nullptr;
+  int layer = 0, layers_per_step = 2;
+  long long budget = 4000000000ll;
+  int max_splits = 4;
+};
+
 struct GemmLaunch {
   const void* A = nullptr;
   long long a_rows = 0, a_cols = 0, lda = 0;  // 2-D view of A as stored (elements)
@@ -35,6 +50,7 @@ struct GemmLaunch {
   int* err = nullptr;
   int num_sms = 148;
   cudaStream_t stream = 0;
+  const TpGemm* tp = nullptr;
 };
 // Returns the number of kernels launched, or -splits when the result was left as
 // `splits` fp32 slabs in g.ws (slab_out requested and K was split).
@@ -45,6 +61,20 @@ void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int
 void split_reduce(const float* ws, long long stride, int splits, int rows, int cols, void* out, long long ldo,
                   int out_f32, cudaStream_t s);
 
+// ---- tensor parallelism over peer memory (tp.cu)
+struct TpArgs {
+  unsigned long long base[8];  // rank buffer bases (peer pointers)
+  long long rs_off, ag_off;    // regions: RS [2][slots][rows][H], AG [2][world * rows][H / 2] tagged words
+  int world, rank, rows, H, layers_per_step;
+};
+// Owner side of the reduce-scatter: res[t] += sum of the `slots` partials of token t; out[t] =
+// rmsnorm(res[t]) * gamma; with ag_layer >= 0 the normed row is also all-gathered under that layer's tag.
+void tp_rs_add_rmsnorm(const TpArgs& a, const int64_t* epoch, int layer, int slots, void* residual, const void* gamma,
+                       void* out, long long ldo, float eps, int ag_layer, long long budget, int* err, int rows,
+                       cudaStream_t s);
+void tp_ag_send(const TpArgs& a, const int64_t* epoch, int layer, const void* x, long long ldx, int rows,
+                cudaStream_t s);
+
 // ---- block-scaled fp8 GEMM (gemm_fp8.cu)
 // D[m, n] = sum_kb sa(m, kb) sb(n, kb) sum_{k in kb} A[m, k] B[n, k]; A, B e4m3 K-major,
 // sa[(row / sa_rows) * ldsa + kb] (weight rows of A as stored), sb[kb * ldsb + n].
@@ -53,7 +83,7 @@ struct Fp8Launch {
   long long a_rows = 0, lda = 0;
   const float* sa = nullptr;
   long long ldsa = 0;
-  int sa_rows = 128;
+  int sa_rows = 128, sa_blocks = 0;  // scale rows: one per sa_rows weight rows
   const void* B = nullptr;
   long long b_rows = 0, ldb = 0;
   const float* sb = nullptr;

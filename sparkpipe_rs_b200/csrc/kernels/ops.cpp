@@ -125,6 +125,90 @@ int64_t gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, 
   return sp::gemm_bf16(g);
 }
 
+// ---- tensor parallelism (tp.cu, gemm_tcgen05.cu)
+constexpr int kTpArgsWords = 8 + 2 + 5;
+
+sp::TpArgs tp_args(const std::vector<int64_t>& v) {
+  TORCH_CHECK((int)v.size() == kTpArgsWords, "tp: argument vector must hold ", kTpArgsWords, " words");
+  sp::TpArgs a{};
+  int i = 0;
+  for (int r = 0; r < 8; ++r) a.base[r] = (unsigned long long)v[i++];
+  a.rs_off = v[i++]; a.ag_off = v[i++];
+  a.world = (int)v[i++]; a.rank = (int)v[i++]; a.rows = (int)v[i++]; a.H = (int)v[i++];
+  a.layers_per_step = (int)v[i++];
+  return a;
+}
+
+int64_t gemm_tp(const Tensor& A, const c10::optional<Tensor>& B, const Tensor& D, int64_t M, int64_t N, int64_t K,
+                const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, int64_t rs, int64_t ag,
+                int64_t rs_M, int64_t splits, int64_t block_n, int64_t budget_cycles) {
+  // rs: D is unused (partials go to the owners' reduce-scatter slots, rs_M = features per token);
+  // ag: B is unused (rows come from this rank's all-gather region, row length = args' H)
+  CHECK_CUDA(A); CHECK_BF16(A); CHECK_CUDA(D);
+  TORCH_CHECK(A.dim() == 2 && A.stride(1) == 1, "gemm_tp: A must be a 2-D row-major view");
+  TORCH_CHECK(epoch.scalar_type() == at::kLong && epoch.is_cuda(), "gemm_tp: epoch must be a CUDA int64 tensor");
+  const c10::cuda::CUDAGuard guard(A.device());
+  const sp::TpArgs a = tp_args(args);
+  sp::TpGemm t;
+  for (int r = 0; r < 8; ++r) t.base[r] = a.base[r];
+  t.rs_off = a.rs_off; t.rs = rs ? 1 : 0; t.rank = a.rank; t.world = a.world; t.rows = a.rows;
+  t.epoch = epoch.data_ptr<int64_t>(); t.layer = (int)layer; t.layers_per_step = a.layers_per_step;
+  t.budget = budget_cycles;
+  sp::GemmLaunch g;
+  g.A = A.data_ptr(); g.a_rows = A.size(0); g.a_cols = A.size(1); g.lda = A.stride(0);
+  if (ag) {
+    t.ag = reinterpret_cast<const void*>(a.base[a.rank] + a.ag_off);
+    t.ag_row_words = a.H / 2;
+    t.ag_parity_words = (long long)a.world * a.rows * (a.H / 2);
+    g.B = A.data_ptr();  // not read
+    g.b_rows = (long long)a.world * a.rows; g.b_cols = a.H; g.ldb = a.H;
+  } else {
+    TORCH_CHECK(B.has_value(), "gemm_tp: B is required without the all-gather operand");
+    CHECK_BF16(*B);
+    TORCH_CHECK(B->dim() == 2 && B->stride(1) == 1, "gemm_tp: B must be a 2-D row-major view");
+    g.B = B->data_ptr(); g.b_rows = B->size(0); g.b_cols = B->size(1); g.ldb = B->stride(0);
+  }
+  if (rs) {
+    TORCH_CHECK(rs_M == M, "gemm_tp: reduce-scatter features must equal M");
+  } else {
+    TORCH_CHECK(D.scalar_type() == at::kBFloat16 || D.scalar_type() == at::kFloat, "D must be bf16 or fp32");
+  }
+  g.D = D.data_ptr(); g.ldd = D.dim() == 2 ? D.stride(0) : M;
+  g.M = (int)M; g.N = (int)N; g.K = (int)K;
+  g.trans_out = 1;
+  g.out_f32 = D.scalar_type() == at::kFloat ? 1 : 0;
+  g.splits = rs ? (int)splits : 1;
+  g.block_n = (int)block_n;
+  g.a_evict_first = 1;
+  g.err = err_word();
+  g.num_sms = num_sms();
+  g.stream = stream();
+  g.tp = &t;
+  return sp::gemm_bf16(g);
+}
+
+void tp_rs_add_rmsnorm(const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, int64_t slots,
+                       const Tensor& residual, const Tensor& gamma, const Tensor& out, double eps, int64_t ag_layer,
+                       int64_t budget_cycles) {
+  CHECK_CUDA(residual); CHECK_BF16(residual); CHECK_BF16(gamma); CHECK_BF16(out); CHECK_CONTIG(residual);
+  TORCH_CHECK(out.stride(1) == 1 && out.stride(0) % 8 == 0, "tp: out rows must be 16-byte aligned");
+  const c10::cuda::CUDAGuard guard(residual.device());
+  const sp::TpArgs a = tp_args(args);
+  TORCH_CHECK(residual.size(1) == a.H && out.size(0) >= residual.size(0), "tp: shapes");
+  sp::tp_rs_add_rmsnorm(a, epoch.data_ptr<int64_t>(), (int)layer, (int)slots, residual.data_ptr(), gamma.data_ptr(),
+                        out.data_ptr(), out.stride(0), (float)eps, (int)ag_layer, budget_cycles, err_word(),
+                        (int)residual.size(0), stream());
+}
+
+void tp_ag_send(const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, const Tensor& x) {
+  CHECK_CUDA(x); CHECK_BF16(x);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.stride(0) % 8 == 0, "tp: x rows must be 16-byte aligned");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const sp::TpArgs a = tp_args(args);
+  TORCH_CHECK(x.size(1) == a.H, "tp: x width");
+  sp::tp_ag_send(a, epoch.data_ptr<int64_t>(), (int)layer, x.data_ptr(), x.stride(0), (int)x.size(0), stream());
+}
+
 void add_rmsnorm(const Tensor& x, const c10::optional<Tensor>& residual, const Tensor& w, const Tensor& out,
                  double eps) {
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_BF16(out);
@@ -193,7 +277,7 @@ int64_t gemm_fp8(const Tensor& A, const Tensor& sa, int64_t sa_rows, const Tenso
   const c10::cuda::CUDAGuard guard(A.device());
   sp::Fp8Launch g;
   g.A = A.data_ptr(); g.a_rows = A.size(0); g.lda = A.stride(0);
-  g.sa = sa.data_ptr<float>(); g.ldsa = sa.stride(0); g.sa_rows = (int)sa_rows;
+  g.sa = sa.data_ptr<float>(); g.ldsa = sa.stride(0); g.sa_rows = (int)sa_rows; g.sa_blocks = (int)sa.size(0);
   g.B = B.data_ptr(); g.b_rows = B.size(0); g.ldb = B.stride(0);
   g.sb = sb.data_ptr<float>(); g.ldsb = sb.stride(0);
   TORCH_CHECK(g.ldsb >= B.size(0), "gemm_fp8: activation scale pitch shorter than B's rows");
@@ -650,6 +734,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_combine_send", &ep_combine_send);
   m.def("ep_combine_add_rmsnorm", &ep_combine_add_rmsnorm);
   m.def("ep_advance", &ep_advance);
+  m.def("gemm_tp", &gemm_tp);
+  m.def("tp_rs_add_rmsnorm", &tp_rs_add_rmsnorm);
+  m.def("tp_ag_send", &tp_ag_send);
+  m.attr("TP_ARGS_WORDS") = kTpArgsWords;
   m.attr("EP_ARGS_WORDS") = sp::EP_ARGS_WORDS;
   m.attr("EP_MAX_RANKS") = sp::EP_MAX_RANKS;
   m.attr("EP_CHUNK_TOKENS") = sp::EP_CHUNK_TOKENS;

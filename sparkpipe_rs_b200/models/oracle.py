@@ -39,13 +39,31 @@ def route(cfg: MLAMoEConfig, x: torch.Tensor, gate: torch.Tensor, bias: torch.Te
     return ids, w * cfg.routed_scaling_factor, logits
 
 
-def swiglu_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
-    h = x @ w13.float().t()
+def fake_quant_e4m3(x: torch.Tensor) -> torch.Tensor:
+    """Per-(row, 128-column) e4m3 quantise-dequantise (scale = block amax / 448), the
+    activation rounding of the fp8 GEMM path."""
+    x = x.float()
+    S, K = x.shape
+    b = x.view(S, K // 128, 128)
+    amax = b.abs().amax(-1, keepdim=True)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    q = (b * (1.0 / scale)).to(torch.float8_e4m3fn).float()
+    return (q * scale).view(S, K)
+
+
+def _mm(x: torch.Tensor, w: torch.Tensor, aq: bool = False) -> torch.Tensor:
+    """x @ w.T in fp32; with ``aq`` the activations first take the fp8 rounding
+    (where the weight is stored in fp8: input dimension in whole 128-blocks)."""
+    return (fake_quant_e4m3(x) if aq and w.shape[-1] % 128 == 0 else x.float()) @ w.float().t()
+
+
+def swiglu_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, aq: bool = False) -> torch.Tensor:
+    h = _mm(x, w13, aq)
     f = w13.shape[0] // 2
-    return (F.silu(h[..., :f]) * h[..., f:]) @ w2.float().t()
+    return _mm(F.silu(h[..., :f]) * h[..., f:], w2, aq)
 
 
-def moe(cfg: MLAMoEConfig, W: dict, p: str, x: torch.Tensor, routing=None) -> torch.Tensor:
+def moe(cfg: MLAMoEConfig, W: dict, p: str, x: torch.Tensor, routing=None, aq: bool = False) -> torch.Tensor:
     """Routed experts 0..E-1 (top-k) plus the shared experts E..E+S-1 on every token."""
     ids, w, _ = route(cfg, x, W[p + "gate"], W.get(p + "gate_bias")) if routing is None else routing
     out = torch.zeros_like(x, dtype=torch.float32)
@@ -56,22 +74,24 @@ def moe(cfg: MLAMoEConfig, W: dict, p: str, x: torch.Tensor, routing=None) -> to
         if rows.numel() == 0:
             continue
         we = (w * mask).sum(-1)[rows]
-        y = swiglu_mlp(x[rows].float(), W[p + "e_w13"][e], W[p + "e_w2"][e])
+        y = swiglu_mlp(x[rows].float(), W[p + "e_w13"][e], W[p + "e_w2"][e], aq)
         out[rows] += we[:, None] * y
     for s in range(cfg.n_shared_experts):
-        out += swiglu_mlp(x.float(), W[p + "e_w13"][E + s], W[p + "e_w2"][E + s])
+        out += swiglu_mlp(x.float(), W[p + "e_w13"][E + s], W[p + "e_w2"][E + s], aq)
     return out
 
 
-def attention(cfg: MLAMoEConfig, W: dict, p: str, x: torch.Tensor, pos: torch.Tensor, table: torch.Tensor):
-    """x [S, H] of one sequence (positions pos) -> [S, H]."""
+def attention(cfg: MLAMoEConfig, W: dict, p: str, x: torch.Tensor, pos: torch.Tensor, table: torch.Tensor,
+              aq: bool = False):
+    """x [S, H] of one sequence (positions pos) -> [S, H]. ``aq``: the projections
+    take fp8-rounded activations (the block-scaled fp8 weight path)."""
     S = x.shape[0]
     nh, dn, dr, dv = cfg.num_heads, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
     kvl = cfg.kv_lora_rank
     qa_dim = cfg.q_lora_rank or cfg.q_out_dim
-    a = x @ W[p + "w_qkv_a"].float().t()
+    a = _mm(x, W[p + "w_qkv_a"], aq)
     if cfg.q_lora_rank:
-        q = rmsnorm(a[:, :qa_dim], W[p + "q_a_norm"], cfg.rms_norm_eps) @ W[p + "w_q_b"].float().t()
+        q = _mm(rmsnorm(a[:, :qa_dim], W[p + "q_a_norm"], cfg.rms_norm_eps), W[p + "w_q_b"], aq)
     else:
         q = a[:, :qa_dim]
     kv_a = a[:, qa_dim:]
@@ -88,12 +108,13 @@ def attention(cfg: MLAMoEConfig, W: dict, p: str, x: torch.Tensor, pos: torch.Te
     scores = scores.masked_fill(~mask, float("-inf"))
     o = scores.softmax(-1) @ v.transpose(0, 1)                        # [nh, S, dv]
     o = o.transpose(0, 1).reshape(S, nh * dv)
-    return o @ W[p + "w_o"].float().t()
+    return _mm(o, W[p + "w_o"], aq)
 
 
 def forward(cfg: MLAMoEConfig, W: dict, tokens: torch.Tensor, table: torch.Tensor | None = None,
-            return_hidden: bool = False):
-    """tokens [S] (one sequence) -> logits [S, V] in fp32."""
+            return_hidden: bool = False, act_quant: bool = False):
+    """tokens [S] (one sequence) -> logits [S, V] in fp32. ``act_quant`` rounds the
+    inputs of the fp8-weight GEMMs to e4m3 per 1x128 block, as the fp8 kernels do."""
     S = tokens.shape[0]
     pos = torch.arange(S, device=tokens.device)
     if table is None:
@@ -101,12 +122,12 @@ def forward(cfg: MLAMoEConfig, W: dict, tokens: torch.Tensor, table: torch.Tenso
     h = W["embed"][tokens.long()].float()
     for i in range(cfg.num_layers):
         p = f"l{i}."
-        h = h + attention(cfg, W, p, rmsnorm(h, W[p + "in_norm"], cfg.rms_norm_eps), pos, table)
+        h = h + attention(cfg, W, p, rmsnorm(h, W[p + "in_norm"], cfg.rms_norm_eps), pos, table, act_quant)
         x = rmsnorm(h, W[p + "post_norm"], cfg.rms_norm_eps)
         if cfg.is_moe_layer(i):
-            h = h + moe(cfg, W, p, x)
+            h = h + moe(cfg, W, p, x, aq=act_quant)
         else:
-            h = h + swiglu_mlp(x, W[p + "w13"], W[p + "w2"])
+            h = h + swiglu_mlp(x, W[p + "w13"], W[p + "w2"], act_quant)
     hn = rmsnorm(h, W["final_norm"], cfg.rms_norm_eps)
     logits = hn @ W["lm_head"].float().t()
     return (logits, h) if return_hidden else logits

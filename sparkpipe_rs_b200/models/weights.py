@@ -72,8 +72,11 @@ def _is_norm(name: str) -> bool:
 FP8_WEIGHTS = ("w_qkv_a", "w_q_b", "w_o", "w13", "w2", "e_w13", "e_w2")
 
 
-def is_fp8_weight(cfg: MLAMoEConfig, name: str) -> bool:
-    return cfg.weight_dtype == "fp8_block" and name.split(".")[-1] in FP8_WEIGHTS
+def is_fp8_weight(cfg: MLAMoEConfig, name: str, shape: tuple | None = None) -> bool:
+    """fp8 applies to the FP8_WEIGHTS whose input dimension is whole 128-column blocks."""
+    if cfg.weight_dtype != "fp8_block" or name.split(".")[-1] not in FP8_WEIGHTS:
+        return False
+    return shape is None or shape[-1] % 128 == 0
 
 
 def _fp8_tensor(cfg: MLAMoEConfig, shape: tuple, seed: int, dev, experts):
@@ -129,7 +132,7 @@ def init_weights(cfg: MLAMoEConfig, seed: int = 0, device="cpu", dtype=torch.bfl
             out[name] = torch.zeros(shape, dtype=torch.float32, device=dev)
             continue
         tseed = (seed * 1_000_003 + idx) & 0x7FFFFFFFFFFFFFFF
-        if dev.type == "cuda" and is_fp8_weight(cfg, name):
+        if dev.type == "cuda" and is_fp8_weight(cfg, name, shape):
             out[name] = _fp8_tensor(cfg, shape, tseed, dev, experts if name.endswith(("e_w13", "e_w2")) else None)
             continue
         g = torch.Generator(device=dev)

@@ -35,6 +35,8 @@ def main():
                          "load and weight bytes of one rank of an N-way expert-parallel run")
     ap.add_argument("--no-trace", action="store_true", help="run the steps without the profiler (for ncu)")
     ap.add_argument("--graph", action="store_true", help="replay the step as one CUDA graph")
+    ap.add_argument("--time", type=int, default=0,
+                    help="also time this many graph replays with CUDA events (device ms per step)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -55,23 +57,45 @@ def main():
         from sparkpipe_rs_b200.parallel.expert_parallel import ExpertParallel
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         ep = ExpertParallel(cfg, rank, world, args.batch, dev, group=dist.group.WORLD)
-    model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=args.ctx + 64, ep=ep)
+    horizon = args.ctx + 2 + args.steps + (args.time + 3 if args.time else 0) + 16  # every position a step reaches
+    model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=horizon + 64, ep=ep)
     B, bs = args.batch, 64
-    bps = math.ceil((args.ctx + args.steps + 8) / bs)
+    bps = math.ceil(horizon / bs)
     cache = KVCache(cfg, num_blocks=B * bps, block_size=bs, device=dev)
     cache.data.normal_(0, 1)
     bt = torch.arange(B * bps, dtype=torch.int32, device=dev).view(B, bps)
-    dg = DecodeGraph(model, cache, B, bps, args.ctx + args.steps + 8, use_graph=args.graph, self_advance=True)
-    # distinct tokens per row, so routing spreads over the experts as in serving
-    dg.ids.copy_(torch.randint(0, cfg.vocab_size, (B,), generator=torch.Generator().manual_seed(0),
-                               dtype=torch.int32))
-    dg.block_table.copy_(bt)
-    dg.pos.fill_(args.ctx)
-    dg.ctx.fill_(args.ctx + 1)
-    dg.slots.copy_(bt[:, args.ctx // bs] * bs + args.ctx % bs)
+
+    def start(g):
+        # distinct tokens per row, so routing spreads over the experts as in serving
+        g.ids.copy_(torch.randint(0, cfg.vocab_size, (B,), generator=torch.Generator().manual_seed(0),
+                                  dtype=torch.int32))
+        g.block_table.copy_(bt)
+        g.pos.fill_(args.ctx)
+        g.ctx.fill_(args.ctx + 1)
+        g.slots.copy_(bt[:, args.ctx // bs] * bs + args.ctx % bs)
+
+    dg = DecodeGraph(model, cache, B, bps, horizon, use_graph=args.graph, self_advance=True)
+    start(dg)
     for _ in range(2):
         dg.run()
     torch.cuda.synchronize()
+    if args.time:
+        tg = dg if args.graph else DecodeGraph(model, cache, B, bps, horizon, use_graph=True, self_advance=True)
+        start(tg)
+        for _ in range(3):
+            tg.run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.time):
+            tg.run()
+        e1.record()
+        torch.cuda.synchronize()
+        print(f"[rank {rank}/{world}] graph replay: {e0.elapsed_time(e1) / args.time:.3f} ms per decode step "
+              f"(batch {B}, context {args.ctx}, {cfg.num_layers} layers)", flush=True)
+        start(dg)
+        if tg is not dg:
+            tg.release()
     if args.no_trace:
         for _ in range(args.steps):
             dg.run()

@@ -89,7 +89,9 @@ def test_prefill_then_decode_matches_oracle(q_lora):
 def test_fp8_block_model_matches_oracle():
     """Block-scaled fp8 weights (128x128 e4m3 blocks, fp32 scales) on every projection
     and expert: the kernel model (fp8 tcgen05 GEMMs, activations quantised per 1x128
-    block) against the fp32 oracle run on the dequantised weights."""
+    block) against the fp32 oracle run on the dequantised weights with the same
+    activation rounding (without it the e4m3 rounding noise of random weights alone
+    moves the logits' cosine to ~0.96)."""
     from sparkpipe_rs_b200 import ops
     from sparkpipe_rs_b200.models import oracle
     from sparkpipe_rs_b200.models.mla_moe import DecodeGraph, ForwardBatch, KVCache, MLAMoEModel
@@ -119,8 +121,8 @@ def test_fp8_block_model_matches_oracle():
     logits = model.forward(fb, cache)
     seqs = [p.to(DEV) for p in prompts]
     for b in range(B):
-        ref = oracle.forward(cfg, w_ref, seqs[b], model.cos_sin)[-1]
-        assert _cos(logits[b], ref) > 0.98, f"fp8 prefill logits of seq {b} diverge: {_cos(logits[b], ref)}"
+        ref = oracle.forward(cfg, w_ref, seqs[b], model.cos_sin, act_quant=True)[-1]
+        assert _cos(logits[b], ref) > 0.99, f"fp8 prefill logits of seq {b} diverge: {_cos(logits[b], ref)}"
     cur = ops.sample_tokens(logits)
     dg = DecodeGraph(model, cache, B, bps, 300, use_graph=True)
     for step in range(2):
@@ -134,8 +136,8 @@ def test_fp8_block_model_matches_oracle():
         out = dg.run()
         for b in range(B):
             seqs[b] = torch.cat([seqs[b], cur[b:b + 1].to(DEV)])
-            ref = oracle.forward(cfg, w_ref, seqs[b], model.cos_sin)[-1]
-            assert _cos(step_logits[b], ref) > 0.98, f"fp8 decode step {step} seq {b}"
+            ref = oracle.forward(cfg, w_ref, seqs[b], model.cos_sin, act_quant=True)[-1]
+            assert _cos(step_logits[b], ref) > 0.99, f"fp8 decode step {step} seq {b}: {_cos(step_logits[b], ref)}"
         cur = out.clone()
     dg.release()
     assert ops.status_word() == 0
