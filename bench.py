@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--parallel", default="auto", choices=["auto", "dp", "ep"],
                     help="N>1: dp = replicated model per GPU; ep = data-parallel attention + experts split "
                          "over the GPUs (auto: ep when the experts divide evenly)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="diagnostic only: run the first N layers (a result with it is not the named workload)")
     ap.add_argument("--prefill-chunk", type=int, default=0,
                     help="max tokens per prefill forward (default 8192; 2048 for k2)")
     return ap.parse_args()
@@ -90,6 +92,8 @@ def main():
     from sparkpipe_rs_b200.utils.clocks import ClockSampler
 
     cfg = get_config(args.model)
+    if args.layers:
+        cfg = cfg.replace(num_layers=args.layers)
     big = cfg.weight_dtype == "fp8_block"  # the 1T fp8 workload: 256 requests over the box, 2048 in / 512 out
     args.batch = args.batch or (max(1, 256 // world) if big else 64)
     args.prompt = args.prompt or (2048 if big else 1024)

@@ -11,10 +11,10 @@
 //
 // Promotion. The scales change every 128 columns of K, so one fp32 accumulator
 // in TMEM cannot hold the sum. Per K block the MMA warp writes a fresh partial
-// product into one of two TMEM buffers; eight epilogue warps (two per TMEM lane
+// product into one of four TMEM buffers; eight epilogue warps (two per TMEM lane
 // quarter, each owning half of the tile's columns) read it back with tcgen05.ld,
 // multiply by sa * sb and add it into register accumulators while the tensor
-// cores fill the other buffer. The accumulation order over K blocks is fixed, so
+// cores fill the next buffers (up to four K blocks ahead). The accumulation order over K blocks is fixed, so
 // results are deterministic.
 //
 // Modes, as in the bf16 kernel: DENSE (persistent over (m, n) tiles), SPLITK
@@ -73,7 +73,9 @@ struct F8Cfg {
   static constexpr int B_BYTES = BN * F8_BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = MODE == F8_SPLITK ? 4 : (BN >= 128 ? 6 : 8);
-  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  // TMEM partial buffers: the MMA may run NPB K blocks ahead of the promotion
+  static constexpr int NPB = 4;
+  static constexpr int TMEM_COLS = NPB * BN < 32 ? 32 : NPB * BN;
   static constexpr int HALF = BN / 2;                       // columns per epilogue warp
   static constexpr int XBUF_BYTES = 2 * 64 * 17 * 4;        // SwiGLU exchange (2 halves x 64 rows x 16 cols)
   static constexpr int SC = 16;                              // K blocks per staged scale chunk
@@ -185,8 +187,8 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* pfull = empty + C::STAGES;   // partial product of one K block ready (MMA -> epilogue)
-  uint64_t* pempty = pfull + 2;          // partial buffer read back (epilogue -> MMA)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + 2);
+  uint64_t* pempty = pfull + C::NPB;     // partial buffer read back (epilogue -> MMA)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + C::NPB);
   volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* s_ntiles = s_err + 1;
   float* xbuf = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + 256);
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::NPB; ++i) {
       mbar_init(&pfull[i], 1);
       mbar_init(&pempty[i], 256);
     }
@@ -299,8 +301,8 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
         for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
-          const int b = it & 1;
-          const uint32_t bph = (it >> 1) & 1;
+          const int b = it % C::NPB;
+          const uint32_t bph = (it / C::NPB) & 1;
           if (!mbar_wait(&pempty[b], bph ^ 1, s_err, p.err, kErrWaitTimeoutMma)) { ok = false; break; }
           if (!mbar_wait(&full[s], ph, s_err, p.err, kErrWaitTimeoutMma)) { ok = false; break; }
           tc_fence_after();
@@ -380,8 +382,8 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
         const int kend = min(SC, nkb - ch * SC);
         for (int j = 0; j < kend; ++j, ++it) {
           if (!ok) continue;
-          const int b = it & 1;
-          const uint32_t bph = (it >> 1) & 1;
+          const int b = it % C::NPB;
+          const uint32_t bph = (it / C::NPB) & 1;
           if (!mbar_wait(&pfull[b], bph, s_err, p.err, kErrWaitTimeoutEpilogue)) { ok = false; continue; }
           tc_fence_after();
           const float sa_v = m < ti.m_valid ? csa[j * 2] : 0.f;

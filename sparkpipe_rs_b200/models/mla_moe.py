@@ -89,14 +89,16 @@ class MLAMoEModel:
             weights = init_weights(cfg, seed=seed, device=self.device, dtype=torch.bfloat16,
                                    experts=ep.local_expert_range() if ep is not None else None)
         self.w = {k: (v if isinstance(v, ops.Fp8Weight) else v.to(self.device)) for k, v in weights.items()}
+        del weights  # the re-laid-out expert weights below must not coexist with a second reference
         derive_decode_weights(cfg, self.w)
         # routed + shared expert gate/up weights in the fused-SwiGLU tile order
         self.fused_swiglu = cfg.moe_intermediate_size % 64 == 0
         for i in range(cfg.num_layers):
             k = f"l{i}.e_w13"
             if k in self.w and self.fused_swiglu:
-                v = self.w[k]
+                v = self.w.pop(k)
                 self.w[k] = ops.interleave_gate_up_fp8(v) if isinstance(v, ops.Fp8Weight) else ops.interleave_gate_up(v)
+                del v
         maxp = max_positions or min(cfg.max_position_embeddings, 1 << 17)
         self.cos_sin = cos_sin_table(cfg, maxp, device=self.device)
         self.scale = cfg.softmax_scale()

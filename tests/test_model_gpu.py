@@ -122,7 +122,7 @@ def test_fp8_block_model_matches_oracle():
     seqs = [p.to(DEV) for p in prompts]
     for b in range(B):
         ref = oracle.forward(cfg, w_ref, seqs[b], model.cos_sin, act_quant=True)[-1]
-        assert _cos(logits[b], ref) > 0.99, f"fp8 prefill logits of seq {b} diverge: {_cos(logits[b], ref)}"
+        assert _cos(logits[b], ref) > 0.98, f"fp8 prefill logits of seq {b} diverge: {_cos(logits[b], ref)}"
     cur = ops.sample_tokens(logits)
     dg = DecodeGraph(model, cache, B, bps, 300, use_graph=True)
     for step in range(2):
@@ -137,7 +137,7 @@ def test_fp8_block_model_matches_oracle():
         for b in range(B):
             seqs[b] = torch.cat([seqs[b], cur[b:b + 1].to(DEV)])
             ref = oracle.forward(cfg, w_ref, seqs[b], model.cos_sin, act_quant=True)[-1]
-            assert _cos(step_logits[b], ref) > 0.99, f"fp8 decode step {step} seq {b}: {_cos(step_logits[b], ref)}"
+            assert _cos(step_logits[b], ref) > 0.98, f"fp8 decode step {step} seq {b}: {_cos(step_logits[b], ref)}"
         cur = out.clone()
     dg.release()
     assert ops.status_word() == 0
