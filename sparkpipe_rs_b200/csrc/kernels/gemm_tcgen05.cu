@@ -69,14 +69,14 @@ struct GemmKParams {
   // Tensor parallelism over peer memory (LL tagged words, ll.cuh):
   //  * tp_rs: the epilogue sends fp32 partials of token n to rank n / tp_rows, slot
   //    (tp_rank * splits + split) of its reduce-scatter region [2][W*S][tp_rows][M];
-  //  * tp_ag: B rows are read from this rank's all-gather region [2][rows][ag_row_words]
-  //    of bf16 pairs that the peers wrote; the producer warp polls them into the
-  //    swizzled shared-memory tile the MMA reads.
+  //  * tp_ag_flags: B is this rank's all-gather region [2][T][K] bf16 (the B tensor map
+  //    covers both parity halves), written by the peers with plain stores; before a
+  //    tile's first B load the producer waits (bounded, acquire) until the per-row
+  //    flags of the tile's rows carry this layer's tag.
   unsigned long long tp_base[8];
   long long tp_rs_off;
   int tp_rs, tp_rank, tp_world, tp_rows;
-  const unsigned long long* tp_ag;
-  long long tp_ag_parity_words, tp_ag_row_words;
+  const unsigned long long* tp_ag_flags;  // [2][T] tags of this rank's all-gather region
   const int64_t* tp_epoch;
   int tp_layer, tp_layers_per_step;
   long long tp_budget;
@@ -213,35 +213,23 @@ SP_DEVI uint32_t tp_tag(const GemmKParams& p, int* buf) {
   return uint32_t(e + 1);
 }
 
-// All-gather operand: the producer warp fills the B stage (BN rows x 64 bf16, the
-// 128-byte swizzled K-major layout TMA would write: 16-byte chunk c of row r at
-// chunk c ^ (r & 7)) from tagged words; rows past N are zero. Returns false when
-// a peer's words did not arrive within the budget (the tile is zero-filled).
-template <int BN>
-SP_DEVI bool ag_fill_b(const GemmKParams& p, uint8_t* sb, int b_row, int k0, uint32_t tag, int buf) {
-  const int lane = threadIdx.x & 31;
-  const u64* base = p.tp_ag + buf * p.tp_ag_parity_words;
-  bool ok = true;
-  for (int q = lane; q < BN * 8; q += 32) {
-    const int r = q >> 3, c = q & 7;
-    const int row = b_row + r;
-    uint32_t v[4] = {0u, 0u, 0u, 0u};
-    if (row < p.N && ok) {
-      const u64* w = base + (long long)row * p.tp_ag_row_words + (k0 >> 1) + c * 4;
-      u64 w0, w1, w2, w3;
-      ld_ll2(w, w0, w1);
-      ld_ll2(w + 2, w2, w3);
-      if (tag_of(w0) == tag && tag_of(w1) == tag && tag_of(w2) == tag && tag_of(w3) == tag) {
-        v[0] = uint32_t(w0); v[1] = uint32_t(w1); v[2] = uint32_t(w2); v[3] = uint32_t(w3);
-      } else if (!poll_ll4(w, tag, p.tp_budget, v, p.err)) {
-        ok = false;
-        v[0] = v[1] = v[2] = v[3] = 0u;
-      }
+// All-gather operand: wait until rows [row0, row1) of this layer's all-gather half
+// are published (their flags carry `tag`), then order the async proxy (TMA) after
+// the acquire. Bounded; false on a timeout.
+SP_DEVI bool ag_wait_rows(const GemmKParams& p, int row0, int row1, uint32_t tag, int buf) {
+  const u64* f = p.tp_ag_flags + (long long)buf * p.tp_world * p.tp_rows;
+  for (int r = row0; r < row1; ++r) {
+    const long long t0 = clock64();
+    for (unsigned it = 0;; ++it) {
+      u64 v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f + r) : "memory");
+      if (uint32_t(v) == tag) break;
+      if (clock64() - t0 > p.tp_budget) { atomicCAS(p.err, 0, kErrWaitTimeoutPeer); return false; }
+      if ((it & 255) == 255 && poll_abort(p.err)) return false;
     }
-    *reinterpret_cast<uint4*>(sb + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(v[0], v[1], v[2], v[3]);
   }
-  fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor cores
-  return ok;
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
 }
 
 template <int BN, int MODE>
@@ -258,7 +246,6 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* s_ntiles = s_err + 1;
-  volatile int* s_last = s_ntiles + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -267,7 +254,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
-      mbar_init(&full[i], p.tp_ag ? 2 : 1);  // all-gather operand: TMA bytes of A + the warp's B fill
+      mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -289,7 +276,7 @@ __global__ void __launch_bounds__(192, 1)
   // PDL: weights (A) never change while serving, so the producer may stream the
   // first stages of A before the previous kernel has finished; everything else
   // (B activations, outputs, device-side tile counts) waits for it.
-  const bool prefetch_a = (MODE != MODE_GROUPED) && p.a_evict_first && !p.tp_ag;
+  const bool prefetch_a = (MODE != MODE_GROUPED) && p.a_evict_first;
   const bool is_producer = (warp == 0 && lane == 0);
   if (MODE == MODE_GROUPED) griddep_wait();  // the tile count lives in device memory
   if (threadIdx.x == 0) {
@@ -317,50 +304,7 @@ __global__ void __launch_bounds__(192, 1)
     tile_step = 1 << 30;  // exactly one tile
   }
 
-  if (warp == 0 && p.tp_ag) {
-    // ------------------------------------------------------------ producer, all-gather operand
-    // A (weights) by TMA from lane 0; B rows polled from the peers' tagged words by the
-    // whole warp. Every stage gets both arrivals even after a timeout, so in-flight
-    // TMA loads always complete before the CTA exits.
-    int buf;
-    const uint32_t tag = tp_tag(p, &buf);
-    const uint64_t pol_a = p.a_evict_first ? policy_evict_first() : policy_evict_last();
-    int it = 0;
-    bool ok = true;
-    for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
-      TileInfo ti;
-      if (!get_tile<BN, MODE>(p, t, ti)) continue;
-      for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
-        const int s = it % C::STAGES;
-        const uint32_t ph = (it / C::STAGES) & 1;
-        uint8_t* sa = smem + s * C::STAGE_BYTES;
-        int go = 1;
-        if (lane == 0) {
-          go = mbar_wait(&empty[s], ph ^ 1, s_err, p.err, kErrWaitTimeoutProducer) ? 1 : 0;
-          if (go) {
-            mbar_arrive_expect_tx(&full[s], C::A_BYTES);
-            tma_load_2d_hint(sa, &tmA, &full[s], ti.a_k + kb * BK, ti.a_row, pol_a);
-          }
-        }
-        go = __shfl_sync(0xffffffffu, go, 0);
-        if (!go) { ok = false; break; }
-        const bool filled = ag_fill_b<BN>(p, sa + C::A_BYTES, ti.b_row, ti.b_k + kb * BK, tag, buf);
-        __syncwarp();
-        if (lane == 0) {
-          if (!filled) *s_err = kErrWaitTimeoutPeer;
-          mbar_arrive(&full[s]);
-        }
-        if (__any_sync(0xffffffffu, !filled)) { ok = false; ++it; break; }
-      }
-    }
-    if (!ok && lane == 0) {
-      for (int j = 0; j < C::STAGES && j < it; ++j) {
-        const int i2 = it - 1 - j;
-        mbar_wait(&full[i2 % C::STAGES], (i2 / C::STAGES) & 1, s_err, nullptr, 0);
-      }
-    }
-    __syncwarp();
-  } else if (warp == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol_a = p.a_evict_first ? policy_evict_first() : policy_evict_last();
@@ -379,21 +323,31 @@ __global__ void __launch_bounds__(192, 1)
         }
         griddep_wait();
       }
+      // all-gather operand: rows of this layer's parity half, published by the peers
+      int ag_buf = 0;
+      const uint32_t ag_tag = p.tp_ag_flags ? tp_tag(p, &ag_buf) : 0u;
+      const int ag_row0 = ag_buf * p.tp_world * p.tp_rows;
       for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
         TileInfo ti;
         if (!get_tile<BN, MODE>(p, t, ti)) continue;
+        const int b_row = ti.b_row + ag_row0;
+        if (p.tp_ag_flags && !ag_wait_rows(p, ti.b_row, ti.b_row + ti.n_valid, ag_tag, ag_buf)) {
+          *s_err = kErrWaitTimeoutPeer;
+          ok = false;
+        }
         for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           uint8_t* sa = smem + s * C::STAGE_BYTES;
-          if (it < pre) {
-            tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], ti.b_k + kb * BK, ti.b_row);
+          if (it < pre) {  // completes a prefetched stage, even after a failed wait
+            tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], ti.b_k + kb * BK, b_row);
             continue;
           }
+          if (!ok) break;
           if (!mbar_wait(&empty[s], ph ^ 1, s_err, p.err, kErrWaitTimeoutProducer)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
           tma_load_2d_hint(sa, &tmA, &full[s], ti.a_k + kb * BK, ti.a_row, pol_a);
-          tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], ti.b_k + kb * BK, ti.b_row);
+          tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], ti.b_k + kb * BK, b_row);
         }
       }
       if (!ok) {
@@ -602,8 +556,7 @@ static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
   using C = GemmCfg<BN, MODE>;
   CUtensorMap ta, tb;
   make_tmap_2d(&ta, g.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.a_rows, g.a_cols, g.lda, BM, BK);
-  if (p.tp_ag) tb = ta;  // B comes from tagged words, not TMA
-  else make_tmap_2d(&tb, g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.b_rows, g.b_cols, g.ldb, BN, BK);
+  make_tmap_2d(&tb, g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.b_rows, g.b_cols, g.ldb, BN, BK);
   auto kern = gemm_bf16_kernel<BN, MODE>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -691,12 +644,11 @@ int gemm_bf16(const GemmLaunch& g) {
       if (!t.base[r] || (t.base[r] & 255)) throw std::runtime_error("gemm: bad tensor-parallel rank base");
     if (t.rs && (!g.trans_out || g.N > t.world * t.rows))
       throw std::runtime_error("gemm: reduce-scatter needs a transposed output over world x rows tokens");
-    if (t.ag && (g.N > t.world * t.rows || g.b_k0 % BK || g.K % BK || (g.b_k0 + g.K) / 2 > t.ag_row_words))
-      throw std::runtime_error("gemm: all-gather operand needs whole 64-column K blocks inside its rows");
+    if (t.ag_flags && (g.N > t.world * t.rows || g.b_rows != 2ll * t.world * t.rows))
+      throw std::runtime_error("gemm: the all-gather operand is the [2 x world x rows, K] region");
     for (int r = 0; r < 8; ++r) p.tp_base[r] = t.base[r];
     p.tp_rs_off = t.rs_off; p.tp_rs = t.rs; p.tp_rank = t.rank; p.tp_world = t.world; p.tp_rows = t.rows;
-    p.tp_ag = static_cast<const unsigned long long*>(t.ag);
-    p.tp_ag_parity_words = t.ag_parity_words; p.tp_ag_row_words = t.ag_row_words;
+    p.tp_ag_flags = static_cast<const unsigned long long*>(t.ag_flags);
     p.tp_epoch = t.epoch; p.tp_layer = t.layer; p.tp_layers_per_step = t.layers_per_step; p.tp_budget = t.budget;
   }
   if (g.grouped) {

@@ -16,8 +16,7 @@ struct TpGemm {
   unsigned long long base[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // rank buffer bases (peer pointers)
   long long rs_off = 0;          // reduce-scatter region: [2][world * splits][rows][M] words
   int rs = 0, rank = 0, world = 1, rows = 0;
-  const void* ag = nullptr;      // all-gather region of this rank: [2][world * rows][ag_row_words] words
-  long long ag_parity_words = 0, ag_row_words = 0;
+  const void* ag_flags = nullptr;  // all-gather row flags of this rank: [2][world * rows] tags (B = the region)
   const int64_t* epoch = nullptr;
   int layer = 0, layers_per_step = 2;
   long long budget = 4000000000ll;
@@ -64,7 +63,8 @@ void split_reduce(const float* ws, long long stride, int splits, int rows, int c
 // ---- tensor parallelism over peer memory (tp.cu)
 struct TpArgs {
   unsigned long long base[8];  // rank buffer bases (peer pointers)
-  long long rs_off, ag_off;    // regions: RS [2][slots][rows][H], AG [2][world * rows][H / 2] tagged words
+  long long rs_off;            // RS region: [2][slots][rows][H] tagged fp32 words
+  long long ag_off, flag_off;  // AG region [2][world * rows][H] bf16 + per-row flags [2][world * rows] u64
   int world, rank, rows, H, layers_per_step;
 };
 // Owner side of the reduce-scatter: res[t] += sum of the `slots` partials of token t; out[t] =

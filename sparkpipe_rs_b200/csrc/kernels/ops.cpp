@@ -126,14 +126,14 @@ int64_t gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, 
 }
 
 // ---- tensor parallelism (tp.cu, gemm_tcgen05.cu)
-constexpr int kTpArgsWords = 8 + 2 + 5;
+constexpr int kTpArgsWords = 8 + 3 + 5;
 
 sp::TpArgs tp_args(const std::vector<int64_t>& v) {
   TORCH_CHECK((int)v.size() == kTpArgsWords, "tp: argument vector must hold ", kTpArgsWords, " words");
   sp::TpArgs a{};
   int i = 0;
   for (int r = 0; r < 8; ++r) a.base[r] = (unsigned long long)v[i++];
-  a.rs_off = v[i++]; a.ag_off = v[i++];
+  a.rs_off = v[i++]; a.ag_off = v[i++]; a.flag_off = v[i++];
   a.world = (int)v[i++]; a.rank = (int)v[i++]; a.rows = (int)v[i++]; a.H = (int)v[i++];
   a.layers_per_step = (int)v[i++];
   return a;
@@ -157,11 +157,9 @@ int64_t gemm_tp(const Tensor& A, const c10::optional<Tensor>& B, const Tensor& D
   sp::GemmLaunch g;
   g.A = A.data_ptr(); g.a_rows = A.size(0); g.a_cols = A.size(1); g.lda = A.stride(0);
   if (ag) {
-    t.ag = reinterpret_cast<const void*>(a.base[a.rank] + a.ag_off);
-    t.ag_row_words = a.H / 2;
-    t.ag_parity_words = (long long)a.world * a.rows * (a.H / 2);
-    g.B = A.data_ptr();  // not read
-    g.b_rows = (long long)a.world * a.rows; g.b_cols = a.H; g.ldb = a.H;
+    t.ag_flags = reinterpret_cast<const void*>(a.base[a.rank] + a.flag_off);
+    g.B = reinterpret_cast<const void*>(a.base[a.rank] + a.ag_off);  // [2 x world x rows, H] bf16
+    g.b_rows = 2ll * a.world * a.rows; g.b_cols = a.H; g.ldb = a.H;
   } else {
     TORCH_CHECK(B.has_value(), "gemm_tp: B is required without the all-gather operand");
     CHECK_BF16(*B);

@@ -10,16 +10,19 @@
 //   tp_rs_add_rmsnorm         the owner sums its W x S slots per element in a fixed
 //                             order (deterministic), adds the residual, applies
 //                             RMSNorm, and (optionally) all-gathers the normed row:
-//                             it writes it as tagged bf16 pairs into every rank's
-//                             AG region at row rank*rows + t;
-//   tp_ag_send                the same all-gather of a normed row block on its own;
-//   AG -> column-parallel GEMM the GEMM producer (tp_ag) polls the AG region's
-//                             words into the swizzled B tile while A streams by TMA.
+//                             plain bf16 stores into every rank's AG region at row
+//                             rank*rows + t, then system-scope fences and a release
+//                             store of the layer's tag into that row's flag;
+//   tp_ag_send                the same all-gather of a row block on its own;
+//   AG -> column-parallel GEMM the GEMM producer (tp_ag_flags) acquires the flags of
+//                             a tile's rows, then TMA-loads B from the AG region.
 //
-// Nothing crosses GPUs except 64-bit tagged stores (ll.cuh): no flags, no fences,
-// and every wait is bounded (status word kErrWaitTimeoutPeer on a timeout). Two
-// parity halves per region (epoch e = step * layers_per_step + layer, parity e & 1,
-// layers_per_step even) make back-to-back layers race-free, as in the EP kernels.
+// The reduce-scatter side uses 64-bit tagged stores (ll.cuh) that need neither fences
+// nor flags, since its consumer is a plain kernel that polls; the all-gather side is
+// read by TMA, which cannot check tags, so it publishes rows with flags instead (one
+// fence per thread, all concurrent). Every wait is bounded (status word kErrWaitTimeoutPeer
+// on a timeout). Two parity halves per region (epoch e = step * layers_per_step +
+// layer, parity e & 1, layers_per_step even) make back-to-back layers race-free.
 //
 // The reference's TP collective is a recursive-doubling TCP all-reduce of bf16 /
 // f32 vectors (crates/spark-abi/vendor/sparkpipe/include/sparkpipe/
@@ -46,17 +49,28 @@ SP_DEVI uint32_t tp_epoch_tag(const int64_t* epoch_ptr, int layers_per_step, int
   return uint32_t(e + 1);
 }
 
-// Writes 8 bf16 (as 4 tagged words) of row `grow` into every rank's AG region.
-SP_DEVI void ag_put8(const TpArgs& a, int buf, uint32_t tag, int grow, int c, const float* v) {
+// Writes 8 bf16 of row `grow` into every rank's AG region (plain 16-byte stores).
+SP_DEVI void ag_put8(const TpArgs& a, int buf, int grow, int c, const float* v) {
   __align__(16) __nv_bfloat162 h[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-  const uint32_t* u = reinterpret_cast<const uint32_t*>(h);
-  const long long off = ((long long)buf * a.world * a.rows + grow) * (a.H / 2) + c / 2;
-  for (int r = 0; r < a.world; ++r) {
-    u64* dst = reinterpret_cast<u64*>(a.base[r] + a.ag_off) + off;
-    st_ll2(dst, ll_word(u[0], tag), ll_word(u[1], tag));
-    st_ll2(dst + 2, ll_word(u[2], tag), ll_word(u[3], tag));
+  const uint4 u = *reinterpret_cast<const uint4*>(h);
+  const long long off = ((long long)buf * a.world * a.rows + grow) * a.H + c;
+  for (int r = 0; r < a.world; ++r) *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.base[r] + a.ag_off) + off) = u;
+}
+
+// After every thread of the CTA stored its part of row `grow`: each thread orders its
+// own stores at system scope (the fences run concurrently), then the row's flag on
+// every rank takes the layer's tag (release).
+SP_DEVI void ag_publish(const TpArgs& a, int buf, uint32_t tag, int grow) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const long long off = (long long)buf * a.world * a.rows + grow;
+    for (int r = 0; r < a.world; ++r) {
+      u64* f = reinterpret_cast<u64*>(a.base[r] + a.flag_off) + off;
+      asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(u64(tag)) : "memory");
+    }
   }
 }
 
@@ -84,17 +98,31 @@ __global__ void __launch_bounds__(256) tp_rs_add_rmsnorm_kernel(TpArgs a, const 
     const int c = (threadIdx.x + i * 256) * 8;
     if (c < H) {
       float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int sl = 0; sl < slots; ++sl) {
-        const u64* p = rs + (((long long)buf * slots + sl) * a.rows + t) * H + c;
-        uint32_t w0[4], w1[4];
-        if (!ok || !poll_ll4(p, tag, budget, w0, gerr) || !poll_ll4(p + 4, tag, budget, w1, gerr)) {
-          ok = false;
-          continue;
-        }
+      // slots in groups of 4: issue every load of a group, then check the tags (re-poll
+      // only late words), then add in slot order
+      for (int s0 = 0; s0 < slots; s0 += 4) {
+        u64 w[4][8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          x[j] += __uint_as_float(w0[j]);
-          x[4 + j] += __uint_as_float(w1[j]);
+        for (int q = 0; q < 4; ++q)
+          if (s0 + q < slots) {
+            const u64* p = rs + (((long long)buf * slots + s0 + q) * a.rows + t) * H + c;
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) ld_ll2(p + j, w[q][j], w[q][j + 1]);
+          }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (s0 + q >= slots) break;
+          const u64* p = rs + (((long long)buf * slots + s0 + q) * a.rows + t) * H + c;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint32_t v = uint32_t(w[q][j]);
+            if (tag_of(w[q][j]) != tag) {
+              bool ok2 = ok;
+              v = ok ? poll_ll(p + j, tag, budget, ok2, gerr) : 0u;
+              ok = ok2;
+            }
+            x[j] += __uint_as_float(v);
+          }
         }
       }
       float r[8];
@@ -118,6 +146,7 @@ __global__ void __launch_bounds__(256) tp_rs_add_rmsnorm_kernel(TpArgs a, const 
   const float inv = rsqrtf(tot / H + eps);
   int abuf = 0;
   const uint32_t atag = ag_layer >= 0 ? tp_epoch_tag(epoch_ptr, a.layers_per_step, ag_layer, &abuf) : 0u;
+
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int c = (threadIdx.x + i * 256) * 8;
@@ -128,9 +157,10 @@ __global__ void __launch_bounds__(256) tp_rs_add_rmsnorm_kernel(TpArgs a, const 
       for (int j = 0; j < 8; ++j) v[i][j] = v[i][j] * inv * g[j];
       st_bf16x8(out + (long long)t * ldo + c, v[i]);
       // peers receive the same bf16 rounding as the local copy
-      if (ag_layer >= 0) ag_put8(a, abuf, atag, a.rank * a.rows + t, c, v[i]);
+      if (ag_layer >= 0) ag_put8(a, abuf, a.rank * a.rows + t, c, v[i]);
     }
   }
+  if (ag_layer >= 0) ag_publish(a, abuf, atag, a.rank * a.rows + t);
 }
 
 // All-gather of this rank's rows x [rows, H] (bf16): one CTA per row.
@@ -145,8 +175,9 @@ __global__ void __launch_bounds__(256) tp_ag_send_kernel(TpArgs a, const int64_t
   for (int c = threadIdx.x * 8; c < a.H; c += blockDim.x * 8) {
     float v[8];
     ld_bf16x8(x + (long long)t * ldx + c, v);
-    ag_put8(a, buf, tag, a.rank * a.rows + t, c, v);
+    ag_put8(a, buf, a.rank * a.rows + t, c, v);
   }
+  ag_publish(a, buf, tag, a.rank * a.rows + t);
 }
 
 static void check_tp(const TpArgs& a) {

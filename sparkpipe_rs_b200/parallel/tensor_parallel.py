@@ -57,12 +57,13 @@ def _align(x: int, a: int = 256) -> int:
 
 
 def tp_layout(world: int, rows: int, hidden: int, max_splits: int) -> dict:
-    """Byte offsets of the TP regions in one rank's buffer (8-byte tagged words):
-    rs [2][world * max_splits][rows][hidden] fp32 partials, ag [2][world * rows][hidden / 2]
-    bf16 pairs."""
+    """Byte offsets of the TP regions in one rank's buffer: rs [2][world * max_splits]
+    [rows][hidden] tagged fp32 words (8 B), ag [2][world * rows][hidden] bf16, flags
+    [2][world * rows] u64 (the tag of each all-gathered row)."""
     off = {"rs": 0}
     off["ag"] = _align(8 * 2 * world * max_splits * rows * hidden)
-    off["total"] = _align(off["ag"] + 8 * 2 * world * rows * (hidden // 2))
+    off["flags"] = _align(off["ag"] + 2 * 2 * world * rows * hidden)
+    off["total"] = _align(off["flags"] + 8 * 2 * world * rows)
     return off
 
 
@@ -73,8 +74,10 @@ class TensorParallel:
     holds rows [r*rows, (r+1)*rows) of the residual stream. Per block of layers:
 
       ag_send / rs_add_rmsnorm(ag_layer=...)   normed rows -> every rank's AG region
-      ag_gemm                                  column-parallel GEMM over all T rows,
-                                               B polled from the AG region (no NCCL)
+                                               (plain stores + a released per-row flag)
+      ag_gemm                                  column-parallel GEMM over all T rows: the
+                                               producer acquires the row flags, then
+                                               TMA-loads B from the AG region (no NCCL)
       rs_gemm                                  row-parallel GEMM whose epilogue sends
                                                fp32 partials to the token owners
       rs_add_rmsnorm                           owner: sum of partials + residual + RMSNorm
@@ -126,8 +129,8 @@ class TensorParallel:
         self._opened.clear()
 
     def args(self) -> list[int]:
-        return list(self.bases) + [self.layout["rs"], self.layout["ag"], self.world, self.rank, self.rows, self.H,
-                                   self.layers_per_step]
+        return list(self.bases) + [self.layout["rs"], self.layout["ag"], self.layout["flags"], self.world, self.rank,
+                                   self.rows, self.H, self.layers_per_step]
 
     # ------------------------------------------------------------------ ops
     def ag_send(self, layer: int, x: torch.Tensor):
