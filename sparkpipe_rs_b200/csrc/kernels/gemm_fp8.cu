@@ -33,6 +33,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -65,6 +66,7 @@ struct Fp8KParams {
   float* ws;
   long long split_stride;
   int* err;
+  int no_promote;  // diagnostic: accumulate every K block in TMEM unscaled (wrong values, streaming ceiling)
 };
 
 template <int BN, int MODE>
@@ -293,17 +295,19 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_e4m3_f32(F8_BM, BN);
-      int it = 0;
+      int it = 0, tcount = 0;
       bool ok = true;
+      const bool np = p.no_promote != 0;
       for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
         F8Tile ti;
         if (!f8_tile<BN, MODE>(p, t, ti)) continue;
+        if (np && !mbar_wait(&pempty[0], ((tcount & 1) ^ 1), s_err, p.err, kErrWaitTimeoutMma)) { ok = false; break; }
         for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
-          const int b = it % C::NPB;
+          const int b = np ? 0 : it % C::NPB;
           const uint32_t bph = (it / C::NPB) & 1;
-          if (!mbar_wait(&pempty[b], bph ^ 1, s_err, p.err, kErrWaitTimeoutMma)) { ok = false; break; }
+          if (!np && !mbar_wait(&pempty[b], bph ^ 1, s_err, p.err, kErrWaitTimeoutMma)) { ok = false; break; }
           if (!mbar_wait(&full[s], ph, s_err, p.err, kErrWaitTimeoutMma)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
@@ -312,10 +316,12 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
           const uint32_t d_tmem = tmem_base + b * BN;
 #pragma unroll
           for (int k = 0; k < F8_BK / 32; ++k)  // 32 fp8 of K = 32 bytes -> +2 in the start-address field
-            umma_f8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, k > 0 ? 1u : 0u);
+            umma_f8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (k > 0 || (np && kb > kb_begin)) ? 1u : 0u);
           umma_commit(&empty[s]);
-          umma_commit(&pfull[b]);
+          if (!np) umma_commit(&pfull[b]);
         }
+        if (np && ok) umma_commit(&pfull[0]);
+        ++tcount;
       }
     }
     __syncwarp();
@@ -334,7 +340,7 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
     constexpr int NSB = (SC * BN + 255) / 256;  // activation-scale items per thread per chunk
     const int etid = threadIdx.x - 64;
     const int my_sa = p.sa_rows == 64 ? (m >> 6) : 0;
-    int it = 0;
+    int it = 0, tcount = 0;
     bool ok = true;
     for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
       F8Tile ti;
@@ -342,7 +348,25 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
       float acc[HALF];
 #pragma unroll
       for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
-      const int nkb = kb_end - kb_begin;
+      if (p.no_promote) {
+        if (!mbar_wait(&pfull[0], tcount & 1, s_err, p.err, kErrWaitTimeoutEpilogue)) { ok = false; }
+        if (ok) {
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < HALF; c += 16) {
+            float v[16];
+            tmem_ld16(lane_addr + c_lo + c, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[c + j] = v[j];
+          }
+          tc_fence_before();
+          mbar_arrive(&pempty[0]);
+        }
+        ++tcount;
+        ok = epi_bar_and(ok);
+        if (!ok) break;
+      }
+      const int nkb = p.no_promote ? 0 : kb_end - kb_begin;
       const int nch = (nkb + SC - 1) / SC;
       const int blk0 = ti.a_row / p.sa_rows;
       float rsb[NSB], rsa = 0.f;
@@ -507,6 +531,11 @@ int gemm_fp8(const Fp8Launch& g) {
   p.err = g.err;
   p.a_evict_first = g.a_evict_first;
   p.swiglu = g.swiglu;
+  static const int no_promote = [] {  // diagnostic only: SPARKPIPE_FP8_NOPROMOTE=1 gives wrong values
+    const char* e = std::getenv("SPARKPIPE_FP8_NOPROMOTE");
+    return (e && e[0] == '1') ? 1 : 0;
+  }();
+  p.no_promote = no_promote;
   if (g.swiglu && (!g.grouped || !g.trans_out || g.out_f32 || g.M % 128 != 0))
     throw std::runtime_error("gemm_fp8: fused SwiGLU needs a grouped, transposed bf16 GEMM with M % 128 == 0");
   p.m_tiles = (g.M + F8_BM - 1) / F8_BM;
