@@ -213,23 +213,27 @@ SP_DEVI uint32_t tp_tag(const GemmKParams& p, int* buf) {
   return uint32_t(e + 1);
 }
 
-// All-gather operand: wait until rows [row0, row1) of this layer's all-gather half
-// are published (their flags carry `tag`), then order the async proxy (TMA) after
-// the acquire. Bounded; false on a timeout.
-SP_DEVI bool ag_wait_rows(const GemmKParams& p, int row0, int row1, uint32_t tag, int buf) {
+// All-gather operand: the producer warp waits until rows [0, n) of this layer's
+// all-gather half are published (their flags carry `tag`); the 32 lanes poll
+// disjoint rows at once, so the wait costs about one flag round trip. Then the
+// async proxy (TMA) is ordered after the acquires. Bounded; false on a timeout
+// (the same on every lane).
+SP_DEVI bool ag_wait_rows_warp(const GemmKParams& p, int n, uint32_t tag, int buf) {
+  const int lane = threadIdx.x & 31;
   const u64* f = p.tp_ag_flags + (long long)buf * p.tp_world * p.tp_rows;
-  for (int r = row0; r < row1; ++r) {
+  bool ok = true;
+  for (int r = lane; r < n && ok; r += 32) {
     const long long t0 = clock64();
     for (unsigned it = 0;; ++it) {
       u64 v;
       asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f + r) : "memory");
       if (uint32_t(v) == tag) break;
-      if (clock64() - t0 > p.tp_budget) { atomicCAS(p.err, 0, kErrWaitTimeoutPeer); return false; }
-      if ((it & 255) == 255 && poll_abort(p.err)) return false;
+      if (clock64() - t0 > p.tp_budget) { atomicCAS(p.err, 0, kErrWaitTimeoutPeer); ok = false; break; }
+      if ((it & 255) == 255 && poll_abort(p.err)) { ok = false; break; }
     }
   }
   asm volatile("fence.proxy.async.global;" ::: "memory");
-  return true;
+  return __all_sync(0xffffffffu, ok);
 }
 
 template <int BN, int MODE>
@@ -276,7 +280,8 @@ __global__ void __launch_bounds__(192, 1)
   // PDL: weights (A) never change while serving, so the producer may stream the
   // first stages of A before the previous kernel has finished; everything else
   // (B activations, outputs, device-side tile counts) waits for it.
-  const bool prefetch_a = (MODE != MODE_GROUPED) && p.a_evict_first;
+  // (the all-gather operand's warp-wide flag wait needs the whole producer warp past the PDL wait)
+  const bool prefetch_a = (MODE != MODE_GROUPED) && p.a_evict_first && !p.tp_ag_flags;
   const bool is_producer = (warp == 0 && lane == 0);
   if (MODE == MODE_GROUPED) griddep_wait();  // the tile count lives in device memory
   if (threadIdx.x == 0) {
@@ -306,7 +311,11 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    int ag_buf = 0;
+    const uint32_t ag_tag = p.tp_ag_flags ? tp_tag(p, &ag_buf) : 0u;
+    const bool ag_ok = !p.tp_ag_flags || ag_wait_rows_warp(p, p.N, ag_tag, ag_buf);
+    if (!ag_ok && lane == 0) *s_err = kErrWaitTimeoutPeer;
+    if (lane == 0 && ag_ok) {
       const uint64_t pol_a = p.a_evict_first ? policy_evict_first() : policy_evict_last();
       int it = 0;
       bool ok = true;
@@ -323,27 +332,20 @@ __global__ void __launch_bounds__(192, 1)
         }
         griddep_wait();
       }
-      // all-gather operand: rows of this layer's parity half, published by the peers
-      int ag_buf = 0;
-      const uint32_t ag_tag = p.tp_ag_flags ? tp_tag(p, &ag_buf) : 0u;
+      // all-gather operand: rows of this layer's parity half (published, waited for above)
       const int ag_row0 = ag_buf * p.tp_world * p.tp_rows;
       for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
         TileInfo ti;
         if (!get_tile<BN, MODE>(p, t, ti)) continue;
         const int b_row = ti.b_row + ag_row0;
-        if (p.tp_ag_flags && !ag_wait_rows(p, ti.b_row, ti.b_row + ti.n_valid, ag_tag, ag_buf)) {
-          *s_err = kErrWaitTimeoutPeer;
-          ok = false;
-        }
         for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           uint8_t* sa = smem + s * C::STAGE_BYTES;
-          if (it < pre) {  // completes a prefetched stage, even after a failed wait
+          if (it < pre) {
             tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], ti.b_k + kb * BK, b_row);
             continue;
           }
-          if (!ok) break;
           if (!mbar_wait(&empty[s], ph ^ 1, s_err, p.err, kErrWaitTimeoutProducer)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
           tma_load_2d_hint(sa, &tmA, &full[s], ti.a_k + kb * BK, ti.a_row, pol_a);

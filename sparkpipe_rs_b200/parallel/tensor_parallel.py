@@ -151,12 +151,14 @@ class TensorParallel:
         ops._count(1)
         return out
 
-    def rs_gemm(self, layer: int, x: torch.Tensor, w: torch.Tensor, splits: int = 0, block_n: int = 0) -> int:
+    def rs_gemm(self, layer: int, x: torch.Tensor, w: torch.Tensor, splits: int = 1, block_n: int = 64) -> int:
         """Row-parallel: partials of x [T, Kl] @ w[H, Kl].T go to the token owners.
-        Returns the number of partial slots per owner row (world x splits)."""
+        Returns the number of partial slots per owner row (world x splits). Split-K
+        multiplies the bytes sent (every split sends its own partial), so the
+        default spreads the work over 64-token tiles instead."""
         from .. import ops
         T = x.shape[0]
-        splits = splits or self.max_splits
+        splits = max(1, splits)
         dummy = self.epoch  # D is not written
         self.K.gemm_tp(w, x, dummy, w.shape[0], T, x.shape[1], self.args(), self.epoch, layer, 1, 0, w.shape[0],
                        min(splits, self.max_splits), block_n, self.budget)
