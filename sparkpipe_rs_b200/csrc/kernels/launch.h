@@ -161,6 +161,10 @@ struct MlaDecodeLaunch {
   int* err = nullptr;
   cudaStream_t stream = 0;
 };
+// KV tokens per pipeline stage of the decode kernel (32, or 64 when SPARKPIPE_MLA_STAGE_TOKENS=64)
+// and how many decode CTAs of a head count fit on one SM.
+int mla_stage_tokens();
+int mla_ctas_per_sm(int heads);
 void mla_decode(const MlaDecodeLaunch& l);
 
 // ---- prefill attention (prefill_attn.cu)

@@ -3,13 +3,19 @@
 // For each sequence b and head h:  o[b,h,:] = softmax(scale * q[b,h,:] . K^T) V
 // where K = cache rows [latent (kv_lora) | rope key (rope)] of the sequence's
 // paged blocks and V = the latent part of the same rows. All heads of a head
-// group share every KV byte, so one CTA streams each 64-token block once (TMA,
+// group share every KV byte, so one CTA streams each KV stage once (TMA,
 // 128-byte swizzled sub-tiles, double buffered) and all of its warps consume it.
 //
-// Warp layout: NJ warps per 16-head tile. For each 64-token block a warp
-// computes the scores of 64/NJ tokens and the output of 512/NJ latent dims, so
-// NJ = 8 halves the serial mma.sync work per warp; measured on 16-head
-// decode (B=64, ctx 1024) it was 6% slower than NJ = 4, so both widths use 4.
+// Stages hold TOK tokens: 64 (one whole cache block, 74 KB per stage, one CTA per
+// SM) or 32 (half a cache block, 37 KB per stage, so two CTAs share an SM and
+// twice as many stages are in flight per SM). The ncu capture of the 64-token
+// version showed a latency-bound kernel (one 4-warp CTA per SM, 0.45 of measured
+// HBM bandwidth), which the 32-token stages address.
+//
+// Warp layout: NJ warps per 16-head tile. For each stage a warp computes the
+// scores of TOK/NJ tokens and the output of 512/NJ latent dims, so NJ = 8 halves
+// the serial mma.sync work per warp; measured on 16-head decode (B=64, ctx 1024)
+// it was 6% slower than NJ = 4, so both widths use 4.
 //
 // Split-KV: a sequence's blocks are divided over `splits` CTAs; each writes a
 // normalised partial output and its log-sum-exp, and a combine kernel merges
@@ -21,6 +27,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -49,31 +56,33 @@ constexpr int MLA_DIM = 576;     // kv_lora 512 + rope 64
 constexpr int MLA_LAT = 512;
 constexpr int MLA_CHUNKS = 9;    // 64-element (128-byte) column chunks
 constexpr int MLA_BLK = 64;      // tokens per cache block
-constexpr int KV_STAGE_BYTES = MLA_CHUNKS * MLA_BLK * 128;
 
-template <int HG, int NJ>
+template <int HG, int NJ, int TOK>
 struct MlaCfg {
   static constexpr int WARPS = NJ * (HG / 16);
-  static constexpr int TOKW = MLA_BLK / NJ;   // tokens per warp in S = Q K^T
+  static constexpr int STAGE_BYTES = MLA_CHUNKS * TOK * 128;
+  static constexpr int PER_BLOCK = MLA_BLK / TOK;  // stages per cache block
+  static constexpr int TOKW = TOK / NJ;       // tokens per warp in S = Q K^T
   static constexpr int NT = TOKW / 8;         // n8 tiles per warp in S
   static constexpr int DIMW = MLA_LAT / NJ;   // latent dims per warp in O = P V
   static constexpr int NP = DIMW / 16;        // n8-tile pairs per warp in O
   static constexpr int Q_BYTES = MLA_CHUNKS * HG * 128;
-  static constexpr int P_PITCH = 72;  // bf16 elements per P row (64 + 8 pad)
+  static constexpr int P_PITCH = TOK + 8;     // bf16 elements per P row (padded)
   static constexpr int OFF_KV = (Q_BYTES + 1023) / 1024 * 1024;
-  static constexpr int OFF_P = OFF_KV + 2 * KV_STAGE_BYTES;
+  static constexpr int OFF_P = OFF_KV + 2 * STAGE_BYTES;
   static constexpr int OFF_STAT = OFF_P + HG * P_PITCH * 2;
   static constexpr int OFF_BAR = OFF_STAT + 2 * NJ * HG * 4;
   static constexpr int SMEM = OFF_BAR + 64 + 1024;
+  static constexpr int MIN_CTAS = (2 * SMEM <= 227 * 1024) ? 2 : 1;
 };
 
-template <int HG, int NJ>
-__global__ void __launch_bounds__(MlaCfg<HG, NJ>::WARPS * 32, 1)
+template <int HG, int NJ, int TOK>
+__global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ, TOK>::MIN_CTAS)
     mla_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       const MlaKParams p) {
   griddep_wait();
   griddep_launch();
-  using C = MlaCfg<HG, NJ>;
+  using C = MlaCfg<HG, NJ, TOK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sQ = smem_u32(smem);
@@ -96,7 +105,8 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ>::WARPS * 32, 1)
   const int per = (nblk + p.splits - 1) / p.splits;
   const int kb0 = min(nblk, split * per);
   const int kb1 = min(nblk, kb0 + per);
-  const int nb = kb1 - kb0;
+  // stages of this split: PER_BLOCK per cache block, none past the context
+  const int nb = max(0, min((kb1 - kb0) * C::PER_BLOCK, (ctx - kb0 * MLA_BLK + TOK - 1) / TOK));
   const int* bt = p.block_table + (long long)b * p.max_blocks;
 
   if (threadIdx.x == 0) {
@@ -110,14 +120,15 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ>::WARPS * 32, 1)
   }
   __syncthreads();
 
-  auto issue_block = [&](int i) {  // thread 0 only
+  auto issue_block = [&](int i) {  // thread 0 only; stage i = part (i % PER_BLOCK) of block kb0 + i / PER_BLOCK
     const int s = i & 1;
-    const int pb = bt[kb0 + i];
+    const int pb = bt[kb0 + i / C::PER_BLOCK];
+    const int row = pb * MLA_BLK + (i % C::PER_BLOCK) * TOK;
     uint64_t* bar = &full[s];
-    mbar_arrive_expect_tx(bar, KV_STAGE_BYTES);
-    uint8_t* dst = smem + C::OFF_KV + s * KV_STAGE_BYTES;
+    mbar_arrive_expect_tx(bar, C::STAGE_BYTES);
+    uint8_t* dst = smem + C::OFF_KV + s * C::STAGE_BYTES;
 #pragma unroll 1
-    for (int c = 0; c < MLA_CHUNKS; ++c) tma_load_2d(dst + c * MLA_BLK * 128, &tmKV, bar, c * 64, pb * MLA_BLK);
+    for (int c = 0; c < MLA_CHUNKS; ++c) tma_load_2d(dst + c * TOK * 128, &tmKV, bar, c * 64, row);
   };
   int issued = 0;
   if (threadIdx.x == 0) {
@@ -141,7 +152,7 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ>::WARPS * 32, 1)
     const int s = i & 1;
     bool got = mbar_wait(&full[s], (i >> 1) & 1, s_err, p.err, kErrWaitTimeoutMma);
     if (!__syncthreads_and(got)) { ok = false; break; }
-    const uint32_t kvb = sKV + s * KV_STAGE_BYTES;
+    const uint32_t kvb = sKV + s * C::STAGE_BYTES;
 
     // ---- S = Q K^T for 16 heads x TOKW tokens of this warp
     float sc[C::NT][4];
@@ -155,17 +166,17 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ>::WARPS * 32, 1)
       ldsm_x4(a, swz128(sQ + c * HG * 128, qrow + (lane & 15), cc + (lane >> 4) * 8));
       if constexpr (C::NT == 2) {
         uint32_t bb[4];
-        ldsm_x4(bb, swz128(kvb + c * MLA_BLK * 128, j * 16 + (lane & 7) + (lane >> 4) * 8, cc + ((lane >> 3) & 1) * 8));
+        ldsm_x4(bb, swz128(kvb + c * TOK * 128, j * 16 + (lane & 7) + (lane >> 4) * 8, cc + ((lane >> 3) & 1) * 8));
         mma16816(sc[0], a, bb[0], bb[1]);
         mma16816(sc[1], a, bb[2], bb[3]);
       } else {
         uint32_t bb[2];
-        ldsm_x2(bb, swz128(kvb + c * MLA_BLK * 128, j * 8 + (lane & 7), cc + ((lane >> 3) & 1) * 8));
+        ldsm_x2(bb, swz128(kvb + c * TOK * 128, j * 8 + (lane & 7), cc + ((lane >> 3) & 1) * 8));
         mma16816(sc[0], a, bb[0], bb[1]);
       }
     }
     // ---- scale, mask, row max
-    const int tok0 = (kb0 + i) * MLA_BLK + j * C::TOKW;
+    const int tok0 = kb0 * MLA_BLK + i * TOK + j * C::TOKW;
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int n = 0; n < C::NT; ++n)
@@ -218,10 +229,10 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ>::WARPS * 32, 1)
       o[n][2] *= alpha[1]; o[n][3] *= alpha[1];
     }
     __syncthreads();
-    // ---- O[16 heads, DIMW dims of slice j] += P[16, 64] V[64, DIMW]
+    // ---- O[16 heads, DIMW dims of slice j] += P[16, TOK] V[TOK, DIMW]
     const uint32_t sPa = smem_u32(sP);
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
+    for (int kk = 0; kk < TOK / 16; ++kk) {
       uint32_t a[4];
       ldsm_x4(a, sPa + ((qrow + (lane & 15)) * C::P_PITCH + kk * 16 + (lane >> 4) * 8) * 2);
       const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
@@ -229,7 +240,7 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ>::WARPS * 32, 1)
       for (int np = 0; np < C::NP; ++np) {
         const int dim = j * C::DIMW + np * 16 + (lane >> 4) * 8;
         uint32_t bb[4];
-        ldsm_x4_t(bb, swz128(kvb + (dim >> 6) * MLA_BLK * 128, tok, dim & 63));
+        ldsm_x4_t(bb, swz128(kvb + (dim >> 6) * TOK * 128, tok, dim & 63));
         mma16816(o[2 * np], a, bb[0], bb[1]);
         mma16816(o[2 * np + 1], a, bb[2], bb[3]);
       }
@@ -314,13 +325,13 @@ __global__ void mla_combine_kernel(const float* __restrict__ o_part, const float
   *reinterpret_cast<uint32_t*>(orow + 2) = pack_bf16(acc[2] * inv, acc[3] * inv);
 }
 
-template <int HG, int NJ>
+template <int HG, int NJ, int TOK>
 static void launch_mla(const MlaDecodeLaunch& l) {
-  using C = MlaCfg<HG, NJ>;
+  using C = MlaCfg<HG, NJ, TOK>;
   CUtensorMap tq, tkv;
   make_tmap_2d(&tq, l.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (long long)l.B * l.H, MLA_DIM, MLA_DIM, HG, 64);
-  make_tmap_2d(&tkv, l.cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.num_slots, MLA_DIM, MLA_DIM, MLA_BLK, 64);
-  auto kern = mla_decode_kernel<HG, NJ>;
+  make_tmap_2d(&tkv, l.cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.num_slots, MLA_DIM, MLA_DIM, TOK, 64);
+  auto kern = mla_decode_kernel<HG, NJ, TOK>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
@@ -346,14 +357,36 @@ static void launch_mla(const MlaDecodeLaunch& l) {
   }
 }
 
+// Tokens per KV stage: 32 (default) or 64 (SPARKPIPE_MLA_STAGE_TOKENS=64, the
+// one-CTA-per-SM layout, kept for comparison).
+int mla_stage_tokens() {
+  static const int t = [] {
+    const char* e = std::getenv("SPARKPIPE_MLA_STAGE_TOKENS");
+    return (e && std::string(e) == "64") ? 64 : 32;
+  }();
+  return t;
+}
+
+int mla_ctas_per_sm(int heads) {
+  const int tok = mla_stage_tokens();
+  if (heads % 32 == 0) return tok == 64 ? MlaCfg<32, 4, 64>::MIN_CTAS : MlaCfg<32, 4, 32>::MIN_CTAS;
+  return tok == 64 ? MlaCfg<16, 4, 64>::MIN_CTAS : MlaCfg<16, 4, 32>::MIN_CTAS;
+}
+
 void mla_decode(const MlaDecodeLaunch& l) {
   if (l.B <= 0) return;
   if (l.kv_lora != MLA_LAT || l.rope != 64 || l.block_size != MLA_BLK)
     throw std::runtime_error("mla_decode: supports kv_lora 512, rope 64, 64-token blocks");
   if (l.splits > 1 && (!l.o_part || !l.lse_part)) throw std::runtime_error("mla_decode: split-KV needs scratch");
-  if (l.H % 32 == 0) launch_mla<32, 4>(l);
-  else if (l.H % 16 == 0) launch_mla<16, 4>(l);
-  else throw std::runtime_error("mla_decode: heads must be a multiple of 16");
+  if (l.H % 32 == 0) {
+    if (mla_stage_tokens() == 64) launch_mla<32, 4, 64>(l);
+    else launch_mla<32, 4, 32>(l);
+  } else if (l.H % 16 == 0) {
+    if (mla_stage_tokens() == 64) launch_mla<16, 4, 64>(l);
+    else launch_mla<16, 4, 32>(l);
+  } else {
+    throw std::runtime_error("mla_decode: heads must be a multiple of 16");
+  }
 }
 
 }  // namespace sp

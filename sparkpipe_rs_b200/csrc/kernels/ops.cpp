@@ -721,6 +721,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_word", &status_word);
   m.def("clear_status", &clear_status);
   m.def("num_sms", &num_sms);
+  m.def("mla_ctas_per_sm", [](int64_t heads) { return sp::mla_ctas_per_sm((int)heads); });
+  m.def("mla_stage_tokens", []() { return sp::mla_stage_tokens(); });
   m.def("ep_alloc", &ep_alloc);
   m.def("ep_ipc_handle", &ep_ipc_handle);
   m.def("ep_ipc_open", &ep_ipc_open);
