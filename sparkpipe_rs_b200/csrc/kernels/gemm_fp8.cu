@@ -338,6 +338,7 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
     // K block waits on a scale load.
     constexpr int SC = C::SC;
     constexpr int NSB = (SC * BN + 255) / 256;  // activation-scale items per thread per chunk
+    constexpr int KBP = 2;                      // K blocks promoted per TMEM round trip (narrow tiles)
     const int etid = threadIdx.x - 64;
     const int my_sa = p.sa_rows == 64 ? (m >> 6) : 0;
     int it = 0, tcount = 0;
@@ -404,28 +405,86 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
         const float* csb = s_sb + (ch & 1) * SC * BN + c_lo;
         const float* csa = s_sa + (ch & 1) * SC * 2 + my_sa;
         const int kend = min(SC, nkb - ch * SC);
-        for (int j = 0; j < kend; ++j, ++it) {
-          if (!ok) continue;
-          const int b = it % C::NPB;
-          const uint32_t bph = (it / C::NPB) & 1;
-          if (!mbar_wait(&pfull[b], bph, s_err, p.err, kErrWaitTimeoutEpilogue)) { ok = false; continue; }
-          tc_fence_after();
-          const float sa_v = m < ti.m_valid ? csa[j * 2] : 0.f;
+        if constexpr (HALF > 32) {
+          // wide tiles: one K block at a time, one 16-column TMEM load in registers at once
+          for (int j = 0; j < kend; ++j, ++it) {
+            if (!ok) continue;
+            const int b = it % C::NPB;
+            const uint32_t bph = (it / C::NPB) & 1;
+            if (!mbar_wait(&pfull[b], bph, s_err, p.err, kErrWaitTimeoutEpilogue)) { ok = false; continue; }
+            tc_fence_after();
+            const float sa_v = m < ti.m_valid ? csa[j * 2] : 0.f;
 #pragma unroll
-          for (int c = 0; c < HALF; c += 16) {
-            float v[16];
-            tmem_ld16(lane_addr + b * BN + c_lo + c, v);
+            for (int c = 0; c < HALF; c += 16) {
+              float v[16];
+              tmem_ld16(lane_addr + b * BN + c_lo + c, v);
 #pragma unroll
-            for (int q4 = 0; q4 < 16; q4 += 4) {
-              const float4 sb4 = *reinterpret_cast<const float4*>(csb + j * BN + c + q4);
-              acc[c + q4] = fmaf(v[q4], sa_v * sb4.x, acc[c + q4]);
-              acc[c + q4 + 1] = fmaf(v[q4 + 1], sa_v * sb4.y, acc[c + q4 + 1]);
-              acc[c + q4 + 2] = fmaf(v[q4 + 2], sa_v * sb4.z, acc[c + q4 + 2]);
-              acc[c + q4 + 3] = fmaf(v[q4 + 3], sa_v * sb4.w, acc[c + q4 + 3]);
+              for (int q4 = 0; q4 < 16; q4 += 4) {
+                const float4 sb4 = *reinterpret_cast<const float4*>(csb + j * BN + c + q4);
+                acc[c + q4] = fmaf(v[q4], sa_v * sb4.x, acc[c + q4]);
+                acc[c + q4 + 1] = fmaf(v[q4 + 1], sa_v * sb4.y, acc[c + q4 + 1]);
+                acc[c + q4 + 2] = fmaf(v[q4 + 2], sa_v * sb4.z, acc[c + q4 + 2]);
+                acc[c + q4 + 3] = fmaf(v[q4 + 3], sa_v * sb4.w, acc[c + q4 + 3]);
+              }
             }
+            tc_fence_before();
+            mbar_arrive(&pempty[b]);
           }
-          tc_fence_before();
-          mbar_arrive(&pempty[b]);
+        } else {
+          // K blocks in groups of KBP: every partial of a group is waited for, then all of
+          // their TMEM loads are issued before one wait (one round trip per group)
+          for (int j = 0; j < kend; j += KBP) {
+            const int nk = min(KBP, kend - j);
+            if (!ok) { it += nk; continue; }
+            int bufs[KBP];
+            bool got = true;
+#pragma unroll
+            for (int u = 0; u < KBP; ++u) {
+              if (u >= nk) break;
+              bufs[u] = (it + u) % C::NPB;
+              if (got && !mbar_wait(&pfull[bufs[u]], ((it + u) / C::NPB) & 1, s_err, p.err, kErrWaitTimeoutEpilogue))
+                got = false;
+            }
+            if (!got) { ok = false; it += nk; continue; }
+            tc_fence_after();
+            uint32_t r[KBP][HALF / 16][16];
+#pragma unroll
+            for (int u = 0; u < KBP; ++u) {
+              if (u >= nk) break;
+#pragma unroll
+              for (int c = 0; c < HALF / 16; ++c) tmem_ld16_issue(lane_addr + bufs[u] * BN + c_lo + c * 16, r[u][c]);
+            }
+#pragma unroll
+            for (int u = 0; u < KBP; ++u) {
+              if (u >= nk) break;
+#pragma unroll
+              for (int c = 0; c < HALF / 16; ++c) tmem_ld_wait(r[u][c]);
+            }
+            tc_fence_before();
+#pragma unroll
+            for (int u = 0; u < KBP; ++u) {
+              if (u >= nk) break;
+              mbar_arrive(&pempty[bufs[u]]);  // the partials are in registers: release the buffers first
+            }
+#pragma unroll
+            for (int u = 0; u < KBP; ++u) {
+              if (u >= nk) break;
+              const float sa_v = m < ti.m_valid ? csa[(j + u) * 2] : 0.f;
+#pragma unroll
+              for (int c = 0; c < HALF / 16; ++c) {
+#pragma unroll
+                for (int q4 = 0; q4 < 16; q4 += 4) {
+                  const float4 sb4 = *reinterpret_cast<const float4*>(csb + (j + u) * BN + c * 16 + q4);
+                  const int a0 = c * 16 + q4;
+                  acc[a0] = fmaf(__uint_as_float(r[u][c][q4]), sa_v * sb4.x, acc[a0]);
+                  acc[a0 + 1] = fmaf(__uint_as_float(r[u][c][q4 + 1]), sa_v * sb4.y, acc[a0 + 1]);
+                  acc[a0 + 2] = fmaf(__uint_as_float(r[u][c][q4 + 2]), sa_v * sb4.z, acc[a0 + 2]);
+                  acc[a0 + 3] = fmaf(__uint_as_float(r[u][c][q4 + 3]), sa_v * sb4.w, acc[a0 + 3]);
+                }
+              }
+            }
+            it += nk;
+          }
         }
         if (ch + 1 < nch) store_chunk(ch + 1);
         ok = epi_bar_and(ok);
