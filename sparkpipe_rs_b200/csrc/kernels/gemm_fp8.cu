@@ -39,6 +39,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "ll.cuh"
 #include "pdl.h"
 
 namespace sp {
@@ -67,6 +68,8 @@ struct Fp8KParams {
   long long split_stride;
   int* err;
   int no_promote;  // diagnostic: accumulate every K block in TMEM unscaled (wrong values, streaming ceiling)
+  int ep_on;       // grouped: rows go straight to their source ranks' combine slots
+  EpCombDev ep;
 };
 
 template <int BN, int MODE>
@@ -338,7 +341,10 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
     // K block waits on a scale load.
     constexpr int SC = C::SC;
     constexpr int NSB = (SC * BN + 255) / 256;  // activation-scale items per thread per chunk
-    constexpr int KBP = 2;                      // K blocks promoted per TMEM round trip (narrow tiles)
+    // K blocks promoted per TMEM round trip (narrow tiles). Two measured slower on the
+    // Kimi-K2 decode shape (8-layer step 4.98 -> ~5.12 ms): waiting for a pair of partials
+    // holds the first one back.
+    constexpr int KBP = 1;
     const int etid = threadIdx.x - 64;
     const int my_sa = p.sa_rows == 64 ? (m >> 6) : 0;
     int it = 0, tcount = 0;
@@ -518,6 +524,13 @@ __global__ void __launch_bounds__(F8_THREADS, (MODE == F8_SPLITK && BN <= 32) ? 
           }
           asm volatile("bar.sync 1, 256;" ::: "memory");
         }
+      } else if (MODE == F8_GROUPED && p.ep_on) {
+        int ebuf;
+        const uint32_t etag = ep_comb_tag(p.ep, &ebuf);
+#pragma unroll
+        for (int j = 0; j < HALF; ++j)
+          if (c_lo + j < ti.n_valid)
+            ep_comb_store(p.ep, ebuf, etag, ti.n_base + c_lo + j, ti.m_base + m, acc[j], m < ti.m_valid);
       } else {
         f8_store_row<BN>(p, p.D, p.ldd, p.out_f32, p.trans_out, ti, m, c_lo, acc);
       }
@@ -598,6 +611,15 @@ int gemm_fp8(const Fp8Launch& g) {
   if (g.swiglu && (!g.grouped || !g.trans_out || g.out_f32 || g.M % 128 != 0))
     throw std::runtime_error("gemm_fp8: fused SwiGLU needs a grouped, transposed bf16 GEMM with M % 128 == 0");
   p.m_tiles = (g.M + F8_BM - 1) / F8_BM;
+  if (g.ep) {
+    if (!g.grouped || !g.trans_out || g.out_f32 || g.swiglu || g.M != g.ep->H || g.ep->H % 2)
+      throw std::runtime_error("gemm_fp8: the combine epilogue needs a grouped, transposed bf16 GEMM with M = hidden");
+    p.ep_on = 1;
+    const EpComb& e = *g.ep;
+    for (int r = 0; r < 8; ++r) p.ep.base[r] = e.base[r];
+    p.ep.comb_off = e.comb_off; p.ep.cap = e.cap; p.ep.kk = e.kk; p.ep.H = e.H;
+    p.ep.layers_per_step = e.layers_per_step; p.ep.comb_dst = e.comb_dst; p.ep.epoch = e.epoch; p.ep.layer = e.layer;
+  }
   if (g.grouped) {
     if (g.M % g.sa_rows != 0) throw std::runtime_error("gemm_fp8: grouped M must be a multiple of the scale block");
     const int bn = g.block_n > 0 ? g.block_n : 32;

@@ -80,6 +80,9 @@ struct GemmKParams {
   const int64_t* tp_epoch;
   int tp_layer, tp_layers_per_step;
   long long tp_budget;
+  // expert-parallel combine epilogue (grouped): rows go to their source ranks' slots
+  int ep_on;
+  EpCombDev ep;
 };
 
 constexpr int BM = 128;
@@ -434,6 +437,17 @@ __global__ void __launch_bounds__(192, 1)
             }
             asm volatile("bar.sync 1, 128;" ::: "memory");
           }
+        } else if (MODE == MODE_GROUPED && p.ep_on) {
+          int ebuf;
+          const uint32_t etag = ep_comb_tag(p.ep, &ebuf);
+          for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
+            float v[16];
+            tmem_ld16(lane_addr + buf * BN + c0, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (c0 + j < ti.n_valid)
+                ep_comb_store(p.ep, ebuf, etag, ti.n_base + c0 + j, ti.m_base + m, v[j], m < ti.m_valid);
+          }
         } else if (p.tp_rs) {
           int rbuf;
           const uint32_t tag = tp_tag(p, &rbuf);
@@ -652,6 +666,15 @@ int gemm_bf16(const GemmLaunch& g) {
     p.tp_rs_off = t.rs_off; p.tp_rs = t.rs; p.tp_rank = t.rank; p.tp_world = t.world; p.tp_rows = t.rows;
     p.tp_ag_flags = static_cast<const unsigned long long*>(t.ag_flags);
     p.tp_epoch = t.epoch; p.tp_layer = t.layer; p.tp_layers_per_step = t.layers_per_step; p.tp_budget = t.budget;
+  }
+  if (g.ep) {
+    if (!g.grouped || !g.trans_out || g.out_f32 || g.swiglu || g.M != g.ep->H || g.ep->H % 2)
+      throw std::runtime_error("gemm: the combine epilogue needs a grouped, transposed bf16 GEMM with M = hidden");
+    p.ep_on = 1;
+    const EpComb& e = *g.ep;
+    for (int r = 0; r < 8; ++r) p.ep.base[r] = e.base[r];
+    p.ep.comb_off = e.comb_off; p.ep.cap = e.cap; p.ep.kk = e.kk; p.ep.H = e.H;
+    p.ep.layers_per_step = e.layers_per_step; p.ep.comb_dst = e.comb_dst; p.ep.epoch = e.epoch; p.ep.layer = e.layer;
   }
   if (g.grouped) {
     const int bn = g.block_n > 0 ? g.block_n : 32;

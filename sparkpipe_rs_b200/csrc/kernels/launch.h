@@ -23,6 +23,18 @@ struct TpGemm {
   int max_splits = 4;
 };
 
+// Expert-parallel combine fused into a grouped GEMM's epilogue: output row p goes to
+// rank comb_dst[p] >> 20, combine slot comb_dst[p] & 0xFFFFF, as tagged bf16 pairs
+// (the layout ep.cu's combine reads; see parallel/expert_parallel.py for the regions).
+struct EpComb {
+  unsigned long long base[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  long long comb_off = 0;
+  int cap = 0, kk = 0, H = 0, layers_per_step = 2;
+  const int* comb_dst = nullptr;
+  const int64_t* epoch = nullptr;
+  int layer = 0;
+};
+
 struct GemmLaunch {
   const void* A = nullptr;
   long long a_rows = 0, a_cols = 0, lda = 0;  // 2-D view of A as stored (elements)
@@ -50,6 +62,7 @@ struct GemmLaunch {
   int num_sms = 148;
   cudaStream_t stream = 0;
   const TpGemm* tp = nullptr;
+  const EpComb* ep = nullptr;  // grouped only: send the output rows to their source ranks
 };
 // Returns the number of kernels launched, or -splits when the result was left as
 // `splits` fp32 slabs in g.ws (slab_out requested and K was split).
@@ -105,6 +118,7 @@ struct Fp8Launch {
   int* err = nullptr;
   int num_sms = 148;
   cudaStream_t stream = 0;
+  const EpComb* ep = nullptr;  // grouped only: send the output rows to their source ranks
 };
 int gemm_fp8(const Fp8Launch& g);
 // Activation quantisation: row r (source row src_idx[r] / idx_div when src_idx is given) of

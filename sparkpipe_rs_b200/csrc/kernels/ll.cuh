@@ -67,4 +67,36 @@ SP_DEVI bool poll_ll4(const u64* p, uint32_t tag, long long budget, uint32_t (&v
   return true;
 }
 
+// Expert-parallel combine from a GEMM epilogue. A thread holds output feature m of
+// a tile row (lanes hold consecutive features) and the value for sorted row `row`;
+// lane pairs (m even, m + 1) pack their bf16 values into one tagged word of the
+// source rank's combine slot. Call with the whole warp (it shuffles); `active`
+// marks lanes whose feature is inside the tile.
+struct EpCombDev {
+  unsigned long long base[8];
+  long long comb_off;
+  int cap, kk, H, layers_per_step;
+  const int* comb_dst;
+  const int64_t* epoch;
+  int layer;
+};
+
+SP_DEVI uint32_t ep_comb_tag(const EpCombDev& e, int* buf) {
+  const u64 x = u64(*e.epoch) * e.layers_per_step + e.layer;
+  *buf = int(x & 1);
+  return uint32_t(x + 1);
+}
+
+SP_DEVI void ep_comb_store(const EpCombDev& e, int buf, uint32_t tag, int row, long long m, float v, bool active) {
+  const int dst = __ldg(e.comb_dst + row);
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  const uint32_t mine = uint32_t(*reinterpret_cast<const unsigned short*>(&h));
+  const uint32_t other = __shfl_down_sync(0xffffffffu, mine, 1);
+  if (active && (m & 1) == 0) {
+    const int r = dst >> 20, slot = dst & 0xFFFFF;
+    u64* w = reinterpret_cast<u64*>(e.base[r] + e.comb_off) + ((long long)buf * e.cap * e.kk + slot) * (e.H / 2) + m / 2;
+    st_ll(w, ll_word(mine | (other << 16), tag));
+  }
+}
+
 }  // namespace sp

@@ -7,10 +7,11 @@
 // 128-byte swizzled sub-tiles, double buffered) and all of its warps consume it.
 //
 // Stages hold TOK tokens: 64 (one whole cache block, 74 KB per stage, one CTA per
-// SM) or 32 (half a cache block, 37 KB per stage, so two CTAs share an SM and
-// twice as many stages are in flight per SM). The ncu capture of the 64-token
-// version showed a latency-bound kernel (one 4-warp CTA per SM, 0.45 of measured
-// HBM bandwidth), which the 32-token stages address.
+// SM; the default) or 32 (half a cache block, 37 KB per stage, two CTAs per SM).
+//
+// Head groups of one (sequence, split) are adjacent in the grid (blockIdx.x), so
+// with more heads than one CTA holds (64 heads = 2 groups of 32) the groups stream
+// the same KV blocks at about the same time and the second read hits L2.
 //
 // Warp layout: NJ warps per 16-head tile. For each stage a warp computes the
 // scores of TOK/NJ tokens and the output of 512/NJ latent dims, so NJ = 8 halves
@@ -94,9 +95,9 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ
   uint64_t* qbar = full + 2;
   volatile int* s_err = reinterpret_cast<volatile int*>(qbar + 1);
 
-  const int b = blockIdx.x;
-  const int split = blockIdx.y;
-  const int hg = blockIdx.z;
+  const int hg = blockIdx.x;
+  const int b = blockIdx.y;
+  const int split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = warp / NJ, j = warp % NJ;
 
@@ -349,7 +350,8 @@ static void launch_mla(const MlaDecodeLaunch& l) {
   p.splits = l.splits;
   p.scale_log2 = l.scale * 1.4426950408889634f;
   p.err = l.err;
-  dim3 grid(l.B, l.splits, l.H / HG);
+  if (l.B > 65535 || l.splits > 65535) throw std::runtime_error("mla_decode: batch / splits beyond the grid limits");
+  dim3 grid(l.H / HG, l.B, l.splits);
   launch_k(kern, grid, dim3(C::WARPS * 32), C::SMEM, l.stream, tq, tkv, p);
   if (l.splits > 1) {
     launch_k(mla_combine_kernel, dim3(l.B * l.H), dim3(MLA_LAT / 4), 0, l.stream, (const float*)l.o_part,
@@ -357,12 +359,14 @@ static void launch_mla(const MlaDecodeLaunch& l) {
   }
 }
 
-// Tokens per KV stage: 32 (default) or 64 (SPARKPIPE_MLA_STAGE_TOKENS=64, the
-// one-CTA-per-SM layout, kept for comparison).
+// Tokens per KV stage: 64 (default) or 32 (SPARKPIPE_MLA_STAGE_TOKENS=32). Measured
+// with utils/bench_attention.py at the best split each: B=64, 16 heads, ctx 1024:
+// 25.4 us (64) vs 27.8 us (32); B=32, 64 heads, ctx 2048: 57.5 us vs 66.6 us. Twice
+// the CTAs per SM did not pay for twice the per-stage synchronisation.
 int mla_stage_tokens() {
   static const int t = [] {
     const char* e = std::getenv("SPARKPIPE_MLA_STAGE_TOKENS");
-    return (e && std::string(e) == "64") ? 64 : 32;
+    return (e && std::string(e) == "32") ? 32 : 64;
   }();
   return t;
 }

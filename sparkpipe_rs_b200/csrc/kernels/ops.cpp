@@ -83,12 +83,32 @@ void clear_status() {
   TORCH_CHECK(cudaMemset(p, 0, sizeof(int)) == cudaSuccess, "status clear failed");
 }
 
+sp::EpArgs ep_args(const std::vector<int64_t>& v);
+
+// Expert-parallel combine epilogue of a grouped GEMM: (EP argument vector, comb_dst, epoch, MoE layer).
+bool fill_ep_comb(sp::EpComb& e, const std::vector<int64_t>& ep, const c10::optional<Tensor>& comb_dst,
+                  const c10::optional<Tensor>& epoch, int64_t layer) {
+  if (ep.empty()) return false;
+  TORCH_CHECK(comb_dst.has_value() && epoch.has_value(), "ep combine epilogue: comb_dst and epoch are required");
+  CHECK_I32(*comb_dst);
+  TORCH_CHECK(epoch->scalar_type() == at::kLong, "ep combine epilogue: epoch must be int64");
+  const sp::EpArgs a = ep_args(ep);
+  for (int r = 0; r < 8; ++r) e.base[r] = a.base[r];
+  e.comb_off = a.off_comb; e.cap = a.cap; e.kk = a.kk; e.H = a.H; e.layers_per_step = a.moe_layers;
+  e.comb_dst = comb_dst->data_ptr<int>();
+  e.epoch = epoch->data_ptr<int64_t>();
+  e.layer = (int)layer;
+  return true;
+}
+
 int64_t gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, int64_t a_cols, int64_t lda,
           int64_t b_rows, int64_t b_cols, int64_t ldb, int64_t ldd, int64_t d_batch_stride, int64_t M, int64_t N,
           int64_t K, int64_t batch, int64_t a_row0, int64_t a_batch_rows, int64_t a_k0, int64_t a_batch_k,
           int64_t b_row0, int64_t b_batch_rows, int64_t b_k0, int64_t b_batch_k, int64_t trans_out, int64_t splits,
           int64_t block_n, const c10::optional<Tensor>& grp_rows, const c10::optional<Tensor>& grp_tiles,
-          int64_t num_groups, int64_t a_evict_first, int64_t swiglu, int64_t slab_out) {
+          int64_t num_groups, int64_t a_evict_first, int64_t swiglu, int64_t slab_out,
+          const std::vector<int64_t>& ep, const c10::optional<Tensor>& comb_dst, const c10::optional<Tensor>& epoch,
+          int64_t ep_layer) {
   CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D);
   CHECK_BF16(A); CHECK_BF16(B);
   TORCH_CHECK(D.scalar_type() == at::kBFloat16 || D.scalar_type() == at::kFloat, "D must be bf16 or fp32");
@@ -122,6 +142,8 @@ int64_t gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, 
   g.err = err_word();
   g.num_sms = num_sms();
   g.stream = stream();
+  sp::EpComb ec;
+  if (fill_ep_comb(ec, ep, comb_dst, epoch, ep_layer)) g.ep = &ec;
   return sp::gemm_bf16(g);
 }
 
@@ -263,7 +285,8 @@ void quant_fp8_block(const Tensor& x, const Tensor& q, const Tensor& scales) {
 int64_t gemm_fp8(const Tensor& A, const Tensor& sa, int64_t sa_rows, const Tensor& B, const Tensor& sb,
                  const Tensor& D, int64_t M, int64_t N, int64_t K, int64_t trans_out, int64_t splits, int64_t block_n,
                  const c10::optional<Tensor>& grp_rows, const c10::optional<Tensor>& grp_tiles, int64_t num_groups,
-                 int64_t swiglu, int64_t slab_out) {
+                 int64_t swiglu, int64_t slab_out, const std::vector<int64_t>& ep,
+                 const c10::optional<Tensor>& comb_dst, const c10::optional<Tensor>& epoch, int64_t ep_layer) {
   // A: weights [rows, K] e4m3 (2-D row-major view), sa [rows / sa_rows, K / 128] fp32;
   // B: activations [b_rows, K] e4m3, sb [K / 128, ldsb] fp32 (K-block-major)
   CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D); CHECK_FP8(A); CHECK_FP8(B); CHECK_F32(sa); CHECK_F32(sb);
@@ -306,6 +329,8 @@ int64_t gemm_fp8(const Tensor& A, const Tensor& sa, int64_t sa_rows, const Tenso
   g.err = err_word();
   g.num_sms = num_sms();
   g.stream = stream();
+  sp::EpComb ec;
+  if (fill_ep_comb(ec, ep, comb_dst, epoch, ep_layer)) g.ep = &ec;
   return sp::gemm_fp8(g);
 }
 

@@ -88,8 +88,11 @@ def gemm(a: torch.Tensor, b: torch.Tensor, d: torch.Tensor, *, M: int, N: int, K
          batch: int = 1, a_row0: int = 0, a_batch_rows: int = 0, a_k0: int = 0, a_batch_k: int = 0,
          b_row0: int = 0, b_batch_rows: int = 0, b_k0: int = 0, b_batch_k: int = 0, ldd: int | None = None,
          d_batch_stride: int = 0, splits: int = 0, block_n: int = 0, grp_rows=None, grp_tiles=None,
-         num_groups: int = 0, a_evict_first: bool = False, swiglu: bool = False, slab_out: bool = False):
+         num_groups: int = 0, a_evict_first: bool = False, swiglu: bool = False, slab_out: bool = False,
+         ep_combine=None):
     """Raw tcgen05 GEMM: D[m, n] = sum_k A[m, k] B[n, k] (see gemm_tcgen05.cu).
+    ``ep_combine`` = (EP argument vector, comb_dst, epoch, MoE layer) sends a grouped
+    GEMM's output rows straight to their source ranks' combine slots (D unused).
 
     Returns D, or with ``slab_out`` and a split K, ``-splits``: the result then
     is the sum of `splits` fp32 slabs in the split workspace (dense, D's
@@ -98,10 +101,11 @@ def gemm(a: torch.Tensor, b: torch.Tensor, d: torch.Tensor, *, M: int, N: int, K
     br, bc, ldb = _rows_cols_ld(b)
     if ldd is None:
         ldd = d.stride(0)
+    ep_args, comb_dst, epoch, ep_layer = ep_combine if ep_combine is not None else ([], None, None, 0)
     r = kernels().gemm(a, b, d, ar, ac, lda, br, bc, ldb, ldd, d_batch_stride, M, N, K, batch, a_row0,
                        a_batch_rows, a_k0, a_batch_k, b_row0, b_batch_rows, b_k0, b_batch_k, int(trans_out),
                        splits, block_n, grp_rows, grp_tiles, num_groups, int(a_evict_first), int(swiglu),
-                       int(slab_out))
+                       int(slab_out), ep_args, comb_dst, epoch, ep_layer)
     if r < 0:
         _count(1)
         return r
@@ -169,7 +173,8 @@ def batched_gemm(a, b, d, *, M, N, K, batch, a_row0=0, a_batch_rows=0, a_k0=0, a
 
 
 def grouped_gemm(w: torch.Tensor, x_sorted: torch.Tensor, out: torch.Tensor, grp_rows: torch.Tensor,
-                 grp_tiles: torch.Tensor, num_groups: int, block_n: int, swiglu: bool = False) -> torch.Tensor:
+                 grp_tiles: torch.Tensor, num_groups: int, block_n: int, swiglu: bool = False,
+                 ep_combine=None) -> torch.Tensor:
     """MoE expert GEMM: out[r] = W[g(r)] @ x_sorted[r] for rows r sorted by group.
 
     w is [G, M, K] (or its [G*M, K] view), x_sorted [R, K], out [R, M]. With
@@ -184,7 +189,8 @@ def grouped_gemm(w: torch.Tensor, x_sorted: torch.Tensor, out: torch.Tensor, grp
         M = w.shape[0] // num_groups
         K = w.shape[1]
     gemm(w2, x_sorted, out, M=M, N=x_sorted.shape[0], K=K, trans_out=True, a_batch_rows=M, block_n=block_n,
-         grp_rows=grp_rows, grp_tiles=grp_tiles, num_groups=num_groups, a_evict_first=True, swiglu=swiglu)
+         grp_rows=grp_rows, grp_tiles=grp_tiles, num_groups=num_groups, a_evict_first=True, swiglu=swiglu,
+         ep_combine=ep_combine)
     return out
 
 
@@ -309,7 +315,7 @@ def linear_fp8(x: Fp8Act, w: Fp8Weight, out: torch.Tensor | None = None, out_dty
     if T == 0:
         return out
     r = kernels().gemm_fp8(w.q, w.s, w.sa_rows, x.q, x.s, out, O, T, K, 1, splits, 0, None, None, 0, 0,
-                           int(slab_out))
+                           int(slab_out), [], None, None, 0)
     if r < 0:
         _count(1)
         return Slabs(-r, T, O)
@@ -318,14 +324,16 @@ def linear_fp8(x: Fp8Act, w: Fp8Weight, out: torch.Tensor | None = None, out_dty
 
 
 def grouped_gemm_fp8(w: Fp8Weight, x_sorted: Fp8Act, out: torch.Tensor, grp_rows: torch.Tensor,
-                     grp_tiles: torch.Tensor, num_groups: int, block_n: int, swiglu: bool = False) -> torch.Tensor:
+                     grp_tiles: torch.Tensor, num_groups: int, block_n: int, swiglu: bool = False,
+                     ep_combine=None) -> torch.Tensor:
     """MoE expert GEMM on fp8: out[r] = dequant(W[g(r)]) @ x_sorted[r] (rows sorted by
     group; weights [G, M, K] with scales [G, M / sa_rows, K / 128])."""
     G, M, K = w.q.shape
     A = w.q.reshape(G * M, K)
     sa = w.s.reshape(-1, w.s.shape[-1])
+    ep_args, comb_dst, epoch, ep_layer = ep_combine if ep_combine is not None else ([], None, None, 0)
     kernels().gemm_fp8(A, sa, w.sa_rows, x_sorted.q, x_sorted.s, out, M, x_sorted.rows, K, 1, 1, block_n, grp_rows,
-                       grp_tiles, num_groups, int(swiglu), 0)
+                       grp_tiles, num_groups, int(swiglu), 0, ep_args, comb_dst, epoch, ep_layer)
     _count(1)
     return out
 

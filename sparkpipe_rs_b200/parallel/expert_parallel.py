@@ -5,7 +5,8 @@ Attention stays data-parallel (every rank decodes its own requests); rank r
 holds routed experts [r*El, (r+1)*El) plus all shared experts. Per MoE layer:
 
     dispatch -> receive/align -> gather -> grouped GEMM (gate/up + SwiGLU) ->
-    grouped GEMM (down) -> combine-send
+    grouped GEMM (down, whose epilogue stores each output row straight into its
+    source rank's combine slot)
 
 and the weighted sum of the returned rows, the residual add and the next
 RMSNorm run in one kernel that reads the rows as they arrive. Every word that
@@ -166,7 +167,15 @@ class ExpertParallel:
                              self.budget)
         ops._count(2)
 
-    def experts(self, w13, w2, bn: int, fused_swiglu: bool = True):
+    def _comb(self, layer: int):
+        """Combine epilogue arguments of the down-projection GEMM for MoE layer `layer`."""
+        return (self.args(), self.comb_dst, self.epoch, self.moe_index[layer])
+
+    def experts(self, w13, w2, bn: int, fused_swiglu: bool = True, layer: int | None = None):
+        """Expert GEMMs of the received rows. With `layer` the down projection's epilogue
+        sends every output row straight into its source rank's combine slot (the
+        combine-send kernel is not needed); without it the rows land in ``self.y``."""
+        comb = self._comb(layer) if layer is not None else None
         if isinstance(w13, ops.Fp8Weight):
             # block-scaled fp8 experts; the live row count stays on the device
             if not self.fp8:
@@ -174,7 +183,7 @@ class ExpertParallel:
             rows_dev = self.grp_rows[self.n_local:]
             ops.grouped_gemm_fp8(w13, self.xq, self.act, self.grp_rows, self.grp_tiles, self.n_local, bn, swiglu=True)
             ops.quant_act_fp8(self.act, rows_dev=rows_dev, out=self.aq)
-            ops.grouped_gemm_fp8(w2, self.aq, self.y, self.grp_rows, self.grp_tiles, self.n_local, bn)
+            ops.grouped_gemm_fp8(w2, self.aq, self.y, self.grp_rows, self.grp_tiles, self.n_local, bn, ep_combine=comb)
             return
         if self.fp8:
             raise ValueError("expert parallel: the fp8 transport needs fp8 expert weights")
@@ -184,7 +193,7 @@ class ExpertParallel:
             h13 = torch.empty(self.xs.shape[0], 2 * self.act.shape[1], dtype=torch.bfloat16, device=self.device)
             ops.grouped_gemm(w13, self.xs, h13, self.grp_rows, self.grp_tiles, self.n_local, bn)
             ops.silu_mul(h13, out=self.act)
-        ops.grouped_gemm(w2, self.act, self.y, self.grp_rows, self.grp_tiles, self.n_local, bn)
+        ops.grouped_gemm(w2, self.act, self.y, self.grp_rows, self.grp_tiles, self.n_local, bn, ep_combine=comb)
 
     def combine_send(self, layer: int):
         self.K.ep_combine_send(self.y, self.grp_rows[self.n_local:], self.comb_dst, self.args(), self.epoch,
@@ -214,8 +223,7 @@ class ExpertParallel:
             raise ValueError(f"expert parallel: {xn.shape[0]} tokens exceed the buffer capacity {self.cap}")
         self.dispatch(layer, xn, ids)
         self.receive(layer, bn)
-        self.experts(w13, w2, bn, fused_swiglu)
-        self.combine_send(layer)
+        self.experts(w13, w2, bn, fused_swiglu, layer=layer)  # down projection sends to the source ranks
         return self.combine(layer, wts)
 
 

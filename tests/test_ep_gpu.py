@@ -53,8 +53,10 @@ def _local_moe(cfg, xn, w13, w2, ids, wts, res, gamma, eps):
     return out
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_emulated_ranks_match_single_gpu(world):
+@pytest.mark.parametrize("world,fused", [(2, False), (4, False), (2, True), (4, True)])
+def test_emulated_ranks_match_single_gpu(world, fused):
+    """fused: the down-projection GEMM's epilogue sends its rows to the source ranks
+    (no combine-send kernel); both paths must equal the single-GPU MoE bit for bit."""
     torch.manual_seed(0)
     dev = torch.device("cuda")
     cfg = _cfg()
@@ -88,9 +90,10 @@ def test_emulated_ranks_match_single_gpu(world):
             for r in range(world):
                 ranks[r].receive(layer, bn)
             for r in range(world):
-                ranks[r].experts(local[r][p + "e_w13"], local[r][p + "e_w2"], bn)
-            for r in range(world):
-                ranks[r].combine_send(layer)
+                ranks[r].experts(local[r][p + "e_w13"], local[r][p + "e_w2"], bn, layer=layer if fused else None)
+            if not fused:
+                for r in range(world):
+                    ranks[r].combine_send(layer)
             for r in range(world):
                 res_ep = res[r].clone()
                 out_ep = torch.empty_like(xs[r])
@@ -132,8 +135,8 @@ def _local_moe_fp8(cfg, xn, w13i, w2, ids, wts, res, gamma, eps, bn):
     return out
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_emulated_ranks_fp8_transport_match_single_gpu(world):
+@pytest.mark.parametrize("world,fused", [(2, False), (4, True)])
+def test_emulated_ranks_fp8_transport_match_single_gpu(world, fused):
     """fp8 experts: rows cross as e4m3 + 128-column scales, quantised in the dispatch
     kernel with the same quantiser as the local path, so EP equals local bit for bit."""
     torch.manual_seed(1)
@@ -168,9 +171,10 @@ def test_emulated_ranks_fp8_transport_match_single_gpu(world):
         for r in range(world):
             ranks[r].receive(layer, bn)
         for r in range(world):
-            ranks[r].experts(local[r][layer][0], local[r][layer][1], bn)
-        for r in range(world):
-            ranks[r].combine_send(layer)
+            ranks[r].experts(local[r][layer][0], local[r][layer][1], bn, layer=layer if fused else None)
+        if not fused:
+            for r in range(world):
+                ranks[r].combine_send(layer)
         for r in range(world):
             res_ep = res[r].clone()
             out_ep = torch.empty_like(xs[r])
