@@ -347,7 +347,10 @@ def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 1
     slots = num_sms * int(kernels().mla_ctas_per_sm(heads))  # CTAs resident at once
     want = max(1, slots // ctas)
     blocks = max(1, math.ceil(max_context / 64))
-    return int(max(1, min(want, blocks // 2 if blocks >= 2 else 1, 16)))
+    # few long sequences need many splits to use the SMs (one 131K-token sequence:
+    # 128 splits of 16 blocks); the fp32 partials cost B x splits x H x 2 KB
+    cap = max(1, min(128, 4096 // ctas))
+    return int(max(1, min(want, blocks // 2 if blocks >= 2 else 1, cap)))
 
 
 def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=None, lse_part=None):

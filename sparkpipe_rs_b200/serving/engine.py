@@ -259,7 +259,7 @@ class LLMEngine:
             self.scheduler.fail_step(plan)
             raise
         now = time.perf_counter()
-        self.step_log.append(("prefill" if plan.kind == 1 else "decode", plan.num_seqs, now - t0))
+        self.step_log.append(("prefill" if plan.kind == 1 else "decode", plan.num_seqs, now - t0, plan.num_tokens))
         events = self.scheduler.complete_tensor(plan, host[:plan.num_seqs].contiguous())
         changed = {}
         for ev in events:
@@ -310,6 +310,8 @@ class LLMEngine:
             "decode_tokens_per_s": dec_tokens / dec_secs if dec_secs > 0 else 0.0,
             "decode_steps": len(dec),
             "prefill_steps": len(log) - len(dec),
+            "prefill_tokens": sum(s[3] for s in log if s[0] == "prefill"),
+            "prefill_seconds": sum(s[2] for s in log if s[0] == "prefill"),
             "ttft_p50_ms": statistics.median(ttft) if ttft else 0.0,
             "tpot_p50_ms": statistics.median(tpot) if tpot else 0.0,
             "h2d_bytes_per_step": (self.h2d_bytes - h2d0) / steps,

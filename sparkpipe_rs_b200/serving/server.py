@@ -181,7 +181,7 @@ class ServingServer:
     def _update_counters(self):
         c = self.counters
         log = self.engine.step_log
-        for kind, seqs, _secs in log:  # consume the engine's step log incrementally
+        for kind, seqs, _secs, _tokens in log:  # consume the engine's step log incrementally
             if kind == "decode":
                 c.decode_dispatches += 1
                 c.max_decode_lanes = max(c.max_decode_lanes, seqs)

@@ -54,9 +54,7 @@ def main():
     for r in ranks:
         r.receive(layer, bn)
     for r in ranks:
-        r.experts(w13, w2, bn)
-    for r in ranks:
-        r.combine_send(layer)
+        r.experts(w13, w2, bn, layer=layer)  # the down projection sends the rows to their sources
     res = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
     out = torch.empty_like(res)
     gamma = torch.ones(H, dtype=torch.bfloat16, device=dev)
@@ -71,7 +69,9 @@ def main():
                                               r0.comb_dst, r0.budget),
         "gather": lambda: K.ep_gather(r0.args(), r0.epoch, j, r0.grp_rows[r0.n_local:], r0.src_row, r0.xs, r0.budget),
         "experts (2 grouped GEMMs)": lambda: r0.experts(w13, w2, bn),
-        "combine_send": lambda: K.ep_combine_send(r0.y, r0.grp_rows[r0.n_local:], r0.comb_dst, r0.args(), r0.epoch, j),
+        "experts, down GEMM sends to sources": lambda: r0.experts(w13, w2, bn, layer=layer),
+        "combine_send (unfused path)": lambda: K.ep_combine_send(r0.y, r0.grp_rows[r0.n_local:], r0.comb_dst,
+                                                                 r0.args(), r0.epoch, j),
         "ep_combine_add_rmsnorm": lambda: r0.combine_add_rmsnorm(layer, wts, res, gamma, out, cfg.rms_norm_eps),
         "combine_add_rmsnorm (local)": lambda: ops.combine_add_rmsnorm(r0.y, r0.src_row, wts, res, gamma, out, kk,
                                                                        cfg.rms_norm_eps),
