@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const bf16* __restrict
     if (lane < EP_CHUNK_TOKENS && t < T) {
       for (int j = 0; j < a.kk; ++j) {
         const int id = ids[t * a.kk + j];
+        if (a.shared_local && id >= a.n_routed) continue;  // computed on this rank, not dispatched
         const int dd = id >= a.n_routed ? a.rank : id / a.experts_per_rank;
         if (dd == d) {
           le[n] = id >= a.n_routed ? a.experts_per_rank + (id - a.n_routed) : id - dd * a.experts_per_rank;
@@ -416,7 +417,7 @@ __global__ void __launch_bounds__(256) ep_combine_send_kernel(const bf16* __rest
 __global__ void __launch_bounds__(256) ep_combine_add_rmsnorm_kernel(
     EpArgs a, const int64_t* __restrict__ epoch_ptr, int layer, const float* __restrict__ w, bf16* __restrict__ res,
     const bf16* __restrict__ gamma, bf16* __restrict__ out, long long ldo, float eps, long long budget,
-    int* __restrict__ gerr) {
+    int* __restrict__ gerr, const bf16* __restrict__ y_shared, int T) {
   griddep_wait();
   griddep_launch();
   int buf;
@@ -436,10 +437,12 @@ __global__ void __launch_bounds__(256) ep_combine_add_rmsnorm_kernel(
     if (c < H) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       // issue the loads of every slot first, then consume them in slot order
+      // slots of shared experts computed here (shared_local) come from y_shared
+      const int k_remote = a.shared_local ? k - a.n_shared : k;
       u64 w[EP_MAX_KK][4];
 #pragma unroll
       for (int j = 0; j < EP_MAX_KK; ++j)
-        if (j < k) {
+        if (j < k_remote) {
           const u64* p = comb_words(a, a.rank, buf, t * k + j) + c / 2;
           ld_ll2(p, w[j][0], w[j][1]);
           ld_ll2(p + 2, w[j][2], w[j][3]);
@@ -448,7 +451,10 @@ __global__ void __launch_bounds__(256) ep_combine_add_rmsnorm_kernel(
       for (int j = 0; j < EP_MAX_KK; ++j) {
         if (j >= k) break;
         uint32_t raw[4];
-        if (tag_of(w[j][0]) == tag && tag_of(w[j][1]) == tag && tag_of(w[j][2]) == tag && tag_of(w[j][3]) == tag) {
+        if (j >= k_remote) {
+          const uint4 u = *reinterpret_cast<const uint4*>(y_shared + ((long long)(j - k_remote) * T + t) * H + c);
+          raw[0] = u.x; raw[1] = u.y; raw[2] = u.z; raw[3] = u.w;
+        } else if (tag_of(w[j][0]) == tag && tag_of(w[j][1]) == tag && tag_of(w[j][2]) == tag && tag_of(w[j][3]) == tag) {
           raw[0] = uint32_t(w[j][0]); raw[1] = uint32_t(w[j][1]); raw[2] = uint32_t(w[j][2]); raw[3] = uint32_t(w[j][3]);
         } else if (!ok || !poll_ll4(comb_words(a, a.rank, buf, t * k + j) + c / 2, tag, budget, raw, gerr)) {
           ok = false;
@@ -559,13 +565,15 @@ void ep_combine_send(const void* y, const int* total, const int* comb_dst, const
 
 void ep_combine_add_rmsnorm(const EpArgs& a, const int64_t* epoch, int layer, const float* topk_w, void* residual,
                             const void* gamma, void* out, long long ldo, int T, float eps, long long budget, int* err,
-                            cudaStream_t s) {
+                            const void* y_shared, cudaStream_t s) {
   check_args(a);
   if (T <= 0) return;
   if (T > a.cap) throw std::runtime_error("ep: more tokens than the buffer capacity");
+  if (a.shared_local && a.n_shared > 0 && !y_shared)
+    throw std::runtime_error("ep: the shared experts' rows are needed when they run locally");
   launch_k(ep_combine_add_rmsnorm_kernel, dim3(T), dim3(256), 0, s, a, epoch, layer, topk_w,
            static_cast<bf16*>(residual), static_cast<const bf16*>(gamma), static_cast<bf16*>(out), ldo, eps, budget,
-           err);
+           err, static_cast<const bf16*>(y_shared), T);
 }
 
 void ep_advance(int64_t* epoch, cudaStream_t s) { launch_k(ep_advance_kernel, dim3(1), dim3(32), 0, s, epoch); }

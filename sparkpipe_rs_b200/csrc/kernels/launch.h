@@ -254,8 +254,10 @@ struct EpArgs {
   int world, rank, cap, H, kk, n_routed, experts_per_rank, n_shared, moe_layers, max_chunks;
   int fp8;              // dispatched rows travel as e4m3 + one fp32 scale per 128 columns
   long long row_words;  // tagged words per dispatched row (H/2 bf16; H/4 + even(H/128) fp8)
+  int shared_local;     // shared experts (ids >= n_routed) are not dispatched: each rank runs them on
+                        // its own tokens while the routed rows travel, and the combine reads their rows
 };
-constexpr int EP_ARGS_WORDS = EP_MAX_RANKS + 5 + 10 + 2;
+constexpr int EP_ARGS_WORDS = EP_MAX_RANKS + 5 + 10 + 3;
 void ep_dispatch(const void* x, int64_t ldx, const int* ids, int T, const EpArgs& a, const int64_t* epoch, int layer,
                  cudaStream_t s);
 void ep_recv_align(const EpArgs& a, const int64_t* epoch, int layer, int bn, int* grp_rows, int* grp_tiles,
@@ -269,9 +271,10 @@ void ep_gather(const EpArgs& a, const int64_t* epoch, int layer, const int* tota
                long long budget, int* err, int num_sms, cudaStream_t s);
 void ep_combine_send(const void* y, const int* total, const int* comb_dst, const EpArgs& a, const int64_t* epoch,
                      int layer, cudaStream_t s);
+// y_shared (shared_local): [n_shared, T, H] bf16 outputs of the shared experts, slots kk - n_shared .. kk - 1.
 void ep_combine_add_rmsnorm(const EpArgs& a, const int64_t* epoch, int layer, const float* topk_w, void* residual,
                             const void* gamma, void* out, long long ldo, int T, float eps, long long budget, int* err,
-                            cudaStream_t s);
+                            const void* y_shared, cudaStream_t s);
 void ep_advance(int64_t* epoch, cudaStream_t s);
 
 }  // namespace sp

@@ -632,7 +632,7 @@ sp::EpArgs ep_args(const std::vector<int64_t>& v) {
   a.world = (int)v[i++]; a.rank = (int)v[i++]; a.cap = (int)v[i++]; a.H = (int)v[i++]; a.kk = (int)v[i++];
   a.n_routed = (int)v[i++]; a.experts_per_rank = (int)v[i++]; a.n_shared = (int)v[i++]; a.moe_layers = (int)v[i++];
   a.max_chunks = (int)v[i++];
-  a.fp8 = (int)v[i++]; a.row_words = v[i++];
+  a.fp8 = (int)v[i++]; a.row_words = v[i++]; a.shared_local = (int)v[i++];
   for (int r = 0; r < a.world; ++r) TORCH_CHECK(a.base[r] != 0 && a.base[r] % 256 == 0, "ep: bad rank base pointer");
   return a;
 }
@@ -698,15 +698,21 @@ void ep_combine_send(const Tensor& y, const Tensor& total, const Tensor& comb_ds
 
 void ep_combine_add_rmsnorm(const std::vector<int64_t>& args, const Tensor& epoch, int64_t layer, const Tensor& w,
                             const Tensor& residual, const Tensor& gamma, const Tensor& out, double eps,
-                            int64_t budget_cycles) {
+                            int64_t budget_cycles, const c10::optional<Tensor>& y_shared) {
   CHECK_F32(w); CHECK_CONTIG(w); CHECK_BF16(residual); CHECK_CONTIG(residual); CHECK_BF16(gamma); CHECK_BF16(out);
   TORCH_CHECK(out.stride(1) == 1 && out.stride(0) % 8 == 0, "ep: out rows must be contiguous and 16-byte aligned");
   const c10::cuda::CUDAGuard guard(residual.device());
   const sp::EpArgs a = ep_args(args);
   TORCH_CHECK(residual.size(1) == a.H && w.numel() == residual.size(0) * a.kk, "ep: combine shape mismatch");
+  const void* ys = nullptr;
+  if (y_shared.has_value()) {
+    CHECK_BF16(*y_shared); CHECK_CONTIG(*y_shared);
+    TORCH_CHECK(y_shared->numel() >= (int64_t)a.n_shared * residual.size(0) * a.H, "ep: shared rows too small");
+    ys = y_shared->data_ptr();
+  }
   sp::ep_combine_add_rmsnorm(a, epoch.data_ptr<int64_t>(), (int)layer, w.data_ptr<float>(), residual.data_ptr(),
                              gamma.data_ptr(), out.data_ptr(), out.stride(0), (int)residual.size(0), (float)eps,
-                             budget_cycles, err_word(), stream());
+                             budget_cycles, err_word(), ys, stream());
 }
 
 void ep_advance(const Tensor& epoch) {

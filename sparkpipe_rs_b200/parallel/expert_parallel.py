@@ -4,9 +4,10 @@ token all-to-all done by fused peer-memory kernels (``csrc/kernels/ep.cu``).
 Attention stays data-parallel (every rank decodes its own requests); rank r
 holds routed experts [r*El, (r+1)*El) plus all shared experts. Per MoE layer:
 
-    dispatch -> receive/align -> gather -> grouped GEMM (gate/up + SwiGLU) ->
-    grouped GEMM (down, whose epilogue stores each output row straight into its
-    source rank's combine slot)
+    dispatch -> shared experts on the local tokens (while the routed rows travel)
+    -> receive/align -> gather -> grouped GEMM (gate/up + SwiGLU) -> grouped GEMM
+    (down, whose epilogue stores each output row straight into its source rank's
+    combine slot)
 
 and the weighted sum of the returned rows, the residual add and the next
 RMSNorm run in one kernel that reads the rows as they arrive. Every word that
@@ -69,11 +70,16 @@ def ep_layout(world: int, cap: int, hidden: int, kk: int, fp8: bool = False) -> 
 
 class ExpertParallel:
     def __init__(self, cfg, rank: int, world: int, cap_tokens: int, device, group=None,
-                 budget_cycles: int = DEFAULT_BUDGET_CYCLES, fp8_transport: bool | None = None):
+                 budget_cycles: int = DEFAULT_BUDGET_CYCLES, fp8_transport: bool | None = None,
+                 shared_local: bool = True):
         """``fp8_transport`` (default: the model has block-scaled fp8 weights) sends
         dispatched rows as e4m3 with one fp32 scale per 128 columns, quantised
         once in the dispatch kernel: half the NVLink bytes, and the receiver
-        gathers them straight into the fp8 expert GEMM's operand layout."""
+        gathers them straight into the fp8 expert GEMM's operand layout.
+
+        ``shared_local``: the shared experts are not dispatched; every rank runs them
+        on its own tokens right after the dispatch, while the routed rows are still
+        crossing NVLink, and the combine reads their rows locally."""
         assert cfg.n_routed_experts % world == 0, "routed experts must split evenly over the ranks"
         assert 1 <= world <= 8
         cap_tokens = -(-cap_tokens // CHUNK_TOKENS) * CHUNK_TOKENS
@@ -89,6 +95,8 @@ class ExpertParallel:
         # even layer count per step -> MoE layer j always uses buffer parity j & 1
         self.layers_per_step = len(self.moe_layers) + (len(self.moe_layers) & 1)
         self.fp8 = (cfg.weight_dtype == "fp8_block") if fp8_transport is None else bool(fp8_transport)
+        self.S = cfg.n_shared_experts
+        self.shared_local = bool(shared_local) and self.S > 0
         self.row_words = row_words(self.H, self.fp8)
         self.layout = ep_layout(world, cap_tokens, self.H, self.kk, self.fp8)
         K = _ext.kernels()
@@ -124,6 +132,7 @@ class ExpertParallel:
             self.xs = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
             self.xq = self.aq = None
         self.act = torch.zeros(max_pairs, F, dtype=torch.bfloat16, device=dev)
+        self._sh = {}  # shared-expert buffers per token count
         self.y = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
 
     @classmethod
@@ -145,7 +154,8 @@ class ExpertParallel:
         c = self.cfg
         return (list(self.bases) + [L["ctrl"], L["nch"], L["meta"], L["rows"], L["comb"]] +
                 [self.world, self.rank, self.cap, self.H, self.kk, c.n_routed_experts, self.El,
-                 c.n_shared_experts, self.layers_per_step, self.cap // CHUNK_TOKENS, int(self.fp8), self.row_words])
+                 c.n_shared_experts, self.layers_per_step, self.cap // CHUNK_TOKENS, int(self.fp8), self.row_words,
+                 int(self.shared_local)])
 
     def local_expert_range(self) -> tuple[int, int]:
         return self.rank * self.El, (self.rank + 1) * self.El
@@ -195,6 +205,43 @@ class ExpertParallel:
             ops.silu_mul(h13, out=self.act)
         ops.grouped_gemm(w2, self.act, self.y, self.grp_rows, self.grp_tiles, self.n_local, bn, ep_combine=comb)
 
+    def shared(self, xn: torch.Tensor, w13, w2, fused_swiglu: bool = True):
+        """The shared experts on this rank's tokens (S groups of T rows, the same grouped
+        kernels as the routed experts); rows land in ``self.y_sh`` [S, T, H]."""
+        T, S, F = xn.shape[0], self.S, self.act.shape[1]
+        if T == 0:
+            return
+        key = T
+        if key not in self._sh:
+            bn = max(32, min(128, 1 << max(0, (T - 1).bit_length()))) if self.fp8 else \
+                 max(16, min(256, 1 << max(0, (T - 1).bit_length())))
+            dev = self.device
+            rows = torch.arange(0, (S + 1) * T, T, dtype=torch.int32, device=dev)
+            tiles = torch.arange(0, S + 1, dtype=torch.int32, device=dev) * ((T + bn - 1) // bn)
+            src = (torch.arange(S * T, device=dev) % T).to(torch.int32)
+            self._sh[key] = dict(bn=bn, rows=rows, tiles=tiles, src=src,
+                                 act=torch.empty(S * T, F, dtype=torch.bfloat16, device=dev),
+                                 y=torch.empty(S, T, self.H, dtype=torch.bfloat16, device=dev))
+        b = self._sh[key]
+        El = self.El
+        if isinstance(w13, ops.Fp8Weight):
+            w13s = ops.Fp8Weight(w13.q[El:], w13.s[El:], w13.sa_rows)
+            w2s = ops.Fp8Weight(w2.q[El:], w2.s[El:], w2.sa_rows)
+            xq = ops.quant_act_fp8(xn, b["src"])  # each shared expert sees every token
+            ops.grouped_gemm_fp8(w13s, xq, b["act"], b["rows"], b["tiles"], S, b["bn"], swiglu=True)
+            ops.grouped_gemm_fp8(w2s, ops.quant_act_fp8(b["act"]), b["y"].view(S * T, self.H), b["rows"], b["tiles"],
+                                 S, b["bn"])
+        else:
+            xs = ops.gather_rows(xn, b["src"])
+            if fused_swiglu:
+                ops.grouped_gemm(w13[El:], xs, b["act"], b["rows"], b["tiles"], S, b["bn"], swiglu=True)
+            else:
+                h13 = torch.empty(S * T, 2 * F, dtype=torch.bfloat16, device=self.device)
+                ops.grouped_gemm(w13[El:], xs, h13, b["rows"], b["tiles"], S, b["bn"])
+                ops.silu_mul(h13, out=b["act"])
+            ops.grouped_gemm(w2[El:], b["act"], b["y"].view(S * T, self.H), b["rows"], b["tiles"], S, b["bn"])
+        self.y_sh = b["y"]
+
     def combine_send(self, layer: int):
         self.K.ep_combine_send(self.y, self.grp_rows[self.n_local:], self.comb_dst, self.args(), self.epoch,
                                self.moe_index[layer])
@@ -207,8 +254,9 @@ class ExpertParallel:
 
     def combine_add_rmsnorm(self, layer: int, wts: torch.Tensor, res: torch.Tensor, gamma: torch.Tensor,
                             out: torch.Tensor, eps: float):
+        ys = self.y_sh if self.shared_local and res.shape[0] > 0 else None
         self.K.ep_combine_add_rmsnorm(self.args(), self.epoch, self.moe_index[layer], wts, res, gamma, out, eps,
-                                      self.budget)
+                                      self.budget, ys)
         ops._count(1)
 
     def end_step(self):
@@ -222,6 +270,8 @@ class ExpertParallel:
         if xn.shape[0] > self.cap:
             raise ValueError(f"expert parallel: {xn.shape[0]} tokens exceed the buffer capacity {self.cap}")
         self.dispatch(layer, xn, ids)
+        if self.shared_local:
+            self.shared(xn, w13, w2, fused_swiglu)  # runs while the routed rows cross NVLink
         self.receive(layer, bn)
         self.experts(w13, w2, bn, fused_swiglu, layer=layer)  # down projection sends to the source ranks
         return self.combine(layer, wts)
