@@ -136,8 +136,8 @@ class ExpertParallel:
         self.y = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
 
     @classmethod
-    def emulated(cls, cfg, world: int, cap_tokens: int, device, budget_cycles: int = DEFAULT_BUDGET_CYCLES):
-        ranks = [cls(cfg, r, world, cap_tokens, device, budget_cycles=budget_cycles) for r in range(world)]
+    def emulated(cls, cfg, world: int, cap_tokens: int, device, budget_cycles: int = DEFAULT_BUDGET_CYCLES, **kw):
+        ranks = [cls(cfg, r, world, cap_tokens, device, budget_cycles=budget_cycles, **kw) for r in range(world)]
         bases = [r.buf.data_ptr() for r in ranks] + [0] * (8 - world)
         for r in ranks:
             r.bases = list(bases)

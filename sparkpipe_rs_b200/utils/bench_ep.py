@@ -51,6 +51,8 @@ def main():
     bn = _moe_block_n(T * kk, ranks[0].n_local)
     for r in ranks:
         r.dispatch(layer, xs[ranks.index(r)], ids[ranks.index(r)])
+        if r.shared_local:
+            r.shared(xs[ranks.index(r)], w13, w2)
     for r in ranks:
         r.receive(layer, bn)
     for r in ranks:
@@ -65,6 +67,7 @@ def main():
     j = r0.moe_index[layer]
     phases = {
         "dispatch": lambda: K.ep_dispatch(xs[0], ids[0], r0.args(), r0.epoch, j),
+        "shared experts on local tokens": lambda: r0.shared(xs[0], w13, w2),
         "recv_align": lambda: K.ep_recv_align(r0.args(), r0.epoch, j, bn, r0.grp_rows, r0.grp_tiles, r0.src_row,
                                               r0.comb_dst, r0.budget),
         "gather": lambda: K.ep_gather(r0.args(), r0.epoch, j, r0.grp_rows[r0.n_local:], r0.src_row, r0.xs, r0.budget),

@@ -53,10 +53,13 @@ def _local_moe(cfg, xn, w13, w2, ids, wts, res, gamma, eps):
     return out
 
 
-@pytest.mark.parametrize("world,fused", [(2, False), (4, False), (2, True), (4, True)])
-def test_emulated_ranks_match_single_gpu(world, fused):
+@pytest.mark.parametrize("world,fused,shared_local", [(2, False, False), (4, False, False), (2, True, True),
+                                                     (4, True, True), (4, True, False)])
+def test_emulated_ranks_match_single_gpu(world, fused, shared_local):
     """fused: the down-projection GEMM's epilogue sends its rows to the source ranks
-    (no combine-send kernel); both paths must equal the single-GPU MoE bit for bit."""
+    (no combine-send kernel); shared_local: the shared experts run on each rank's own
+    tokens instead of being dispatched. Every variant must equal the single-GPU MoE
+    bit for bit."""
     torch.manual_seed(0)
     dev = torch.device("cuda")
     cfg = _cfg()
@@ -66,7 +69,7 @@ def test_emulated_ranks_match_single_gpu(world, fused):
     for k in list(full):
         if k.endswith("e_w13"):
             full[k] = ops.interleave_gate_up(full[k])
-    ranks = ExpertParallel.emulated(cfg, world, cap_tokens=48, device=dev)
+    ranks = ExpertParallel.emulated(cfg, world, cap_tokens=48, device=dev, shared_local=shared_local)
     El = E // world
     local = [{k: torch.cat([v[r * El:(r + 1) * El], v[E:]]).contiguous() for k, v in full.items()
               if k.endswith("e_w13") or k.endswith("e_w2")} for r in range(world)]
@@ -87,6 +90,8 @@ def test_emulated_ranks_match_single_gpu(world, fused):
             bn = _moe_block_n(max(tokens) * kk, ranks[0].n_local)
             for r in range(world):
                 ranks[r].dispatch(layer, xs[r], ids[r])
+                if shared_local:
+                    ranks[r].shared(xs[r], local[r][p + "e_w13"], local[r][p + "e_w2"])
             for r in range(world):
                 ranks[r].receive(layer, bn)
             for r in range(world):
@@ -147,7 +152,7 @@ def test_emulated_ranks_fp8_transport_match_single_gpu(world, fused):
     full = init_weights(cfg, seed=4, device=dev)
     layers = [i for i in range(cfg.num_layers) if cfg.is_moe_layer(i)]
     w13i = {i: ops.interleave_gate_up_fp8(full[f"l{i}.e_w13"]) for i in layers}
-    ranks = ExpertParallel.emulated(cfg, world, cap_tokens=48, device=dev)
+    ranks = ExpertParallel.emulated(cfg, world, cap_tokens=48, device=dev, shared_local=fused)
     assert ranks[0].fp8
     El = E // world
     local = [{i: (ops.interleave_gate_up_fp8(_fp8_slice(full[f"l{i}.e_w13"], r * El, (r + 1) * El, E)),
@@ -168,6 +173,8 @@ def test_emulated_ranks_fp8_transport_match_single_gpu(world, fused):
         bn = max(32, min(128, _moe_block_n(max(tokens) * kk, ranks[0].n_local)))
         for r in range(world):
             ranks[r].dispatch(layer, xs[r], ids[r])
+            if fused:  # the shared experts run locally too
+                ranks[r].shared(xs[r], local[r][layer][0], local[r][layer][1])
         for r in range(world):
             ranks[r].receive(layer, bn)
         for r in range(world):
@@ -197,7 +204,8 @@ def test_emulated_ranks_fp8_transport_match_single_gpu(world, fused):
 def test_receive_wait_times_out_with_status():
     dev = torch.device("cuda")
     cfg = _cfg()
-    ranks = ExpertParallel.emulated(cfg, 2, cap_tokens=8, device=dev, budget_cycles=2_000_000)  # ~1 ms
+    ranks = ExpertParallel.emulated(cfg, 2, cap_tokens=8, device=dev, budget_cycles=2_000_000,  # ~1 ms
+                                    shared_local=False)
     ops.clear_status()
     x = torch.randn(4, cfg.hidden_size, device=dev).to(torch.bfloat16)
     ids = torch.zeros(4, ranks[0].kk, dtype=torch.int32, device=dev)
