@@ -579,6 +579,20 @@ void spec_finish(const Tensor& tok_rows, const Tensor& tgt_rows, int64_t L, doub
                   accepted.data_ptr<int>(), committed.data_ptr<int>(), tc, stream());
 }
 
+void phase_mark(const Tensor& stamps, const c10::optional<Tensor>& totals, int64_t slot, int64_t prev) {
+  TORCH_CHECK(stamps.is_cuda() && stamps.scalar_type() == at::kLong && slot >= 0 && slot < stamps.numel(),
+              "phase_mark: stamps must be a CUDA int64 tensor holding the slot");
+  unsigned long long* tot = nullptr;
+  if (totals.has_value()) {
+    TORCH_CHECK(totals->scalar_type() == at::kLong && totals->numel() == stamps.numel(), "phase_mark: totals");
+    tot = reinterpret_cast<unsigned long long*>(totals->data_ptr<int64_t>());
+  }
+  const c10::cuda::CUDAGuard guard(stamps.device());
+  TORCH_CHECK(prev < stamps.numel(), "phase_mark: previous slot");
+  sp::phase_mark(reinterpret_cast<unsigned long long*>(stamps.data_ptr<int64_t>()), tot, (int)slot, (int)prev,
+                 stream());
+}
+
 void decode_advance(const Tensor& out_ids, const Tensor& ids, const Tensor& pos, const Tensor& ctx,
                     const Tensor& slots, const Tensor& block_table, int64_t block_size) {
   CHECK_CUDA(ids); CHECK_I32(out_ids); CHECK_I32(ids); CHECK_I32(pos); CHECK_I32(ctx); CHECK_I32(slots);
@@ -745,6 +759,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("spec_verify", &spec_verify);
   m.def("decode_advance", &decode_advance);
   m.def("spec_finish", &spec_finish);
+  m.def("phase_mark", &phase_mark);
   m.def("slab_add_rmsnorm", &slab_add_rmsnorm);
   m.def("mla_decode_prep", &mla_decode_prep);
   m.def("combine_add_rmsnorm", &combine_add_rmsnorm);

@@ -212,6 +212,25 @@ void spec_finish(int* tok_rows, const int* tgt_rows, int B, int L, float p_accep
            total_committed);
 }
 
+// Phase clock: one thread stamps the device's global timer (ns) into slot `slot`
+// of a step's clock array and adds the time since slot `prev`'s stamp to the
+// phase's running total. Stream-ordered with the kernels around it (it waits for
+// its predecessor before reading the timer, and with programmatic launch every
+// predecessor has waited for its own), so the totals are the device time of the
+// phases between marks, accumulated over layers and steps.
+__global__ void phase_mark_kernel(unsigned long long* stamps, unsigned long long* totals, int slot, int prev) {
+  griddep_wait();
+  griddep_launch();
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  if (totals && prev >= 0) totals[slot] += t - stamps[prev];
+  stamps[slot] = t;
+}
+
+void phase_mark(unsigned long long* stamps, unsigned long long* totals, int slot, int prev, cudaStream_t s) {
+  launch_k(phase_mark_kernel, dim3(1), dim3(1), 0, s, stamps, totals, slot, prev);
+}
+
 // Feeds a decode step's sampled tokens back as the next step's inputs: token id,
 // position + 1, context length + 1 and the cache slot of the new position
 // (from the block table; -1 once the table is exhausted). Rows with a zero

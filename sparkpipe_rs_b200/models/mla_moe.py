@@ -47,6 +47,36 @@ class ForwardBatch:
     logits_idx: torch.Tensor | None = None    # rows to compute logits for (None = all)
 
 
+class PhaseClock:
+    """Device phase clocks of the forward pass (off unless attached to a model).
+
+    Slots: 0 step start, 1 embedding, 2 attention (input norm, projections, KV
+    write, MLA, output projection; summed over layers), 3 MLP / MoE (post-attention
+    norm, router, experts, combine; summed over layers), 4 final norm + LM head.
+    Each mark is one single-thread kernel reading the device global timer, so the
+    totals are device time without a profiler, and they survive CUDA-graph replay.
+    With ``nvtx`` the host also emits NVTX ranges per layer.
+    """
+
+    NAMES = ("start", "embedding", "attention", "mlp_moe", "lm_head")
+
+    def __init__(self, device, nvtx: bool = False):
+        self.stamps = torch.zeros(16, dtype=torch.int64, device=device)
+        self.totals = torch.zeros(16, dtype=torch.int64, device=device)
+        self.nvtx = nvtx
+
+    def mark(self, slot: int, prev: int = -1):
+        ops.kernels().phase_mark(self.stamps, self.totals, slot, prev)
+        ops._count(1)
+
+    def reset(self):
+        self.totals.zero_()
+
+    def report(self, steps: int = 1) -> dict:
+        t = self.totals.cpu().tolist()
+        return {self.NAMES[i]: t[i] / 1000.0 / max(1, steps) for i in range(1, len(self.NAMES))}  # us per step
+
+
 class KVCache:
     """Paged latent KV cache: [layers, num_blocks * block_size, kv_lora + rope] bf16."""
 
@@ -104,6 +134,7 @@ class MLAMoEModel:
         self.scale = cfg.softmax_scale()
         self.qa_dim = cfg.q_lora_rank or cfg.q_out_dim
         self._layer_offset = 0
+        self.phase_clock: PhaseClock | None = None
 
     # ------------------------------------------------------------------ pieces
     def _lin(self, x: torch.Tensor, w, slab: bool = False, out_dtype=torch.bfloat16):
@@ -254,21 +285,36 @@ class MLAMoEModel:
         T = fb.token_ids.shape[0]
         layers = layers if layers is not None else range(c.num_layers)
         eps = c.rms_norm_eps
+        pc = self.phase_clock
+        if pc is not None:
+            pc.mark(0)
         if hidden_in is None:
             res = ops.embedding(w["embed"], fb.token_ids)
         else:
             res = hidden_in.clone()
         xn = torch.empty_like(res)
         pending = None
+        if pc is not None:
+            pc.mark(1, 0)
+        prev = 1
         for i in layers:
             p = f"l{i}."
+            if pc is not None and pc.nvtx:
+                torch.cuda.nvtx.range_push(f"layer {i}")
             self._residual_norm(pending, res, w[p + "in_norm"], xn)
             if fb.mode == "decode":
                 o = self._attn_decode(i, xn, fb, cache)
             else:
                 o = self._attn_prefill(i, xn, fb, cache)
+            if pc is not None:
+                pc.mark(2, prev)
             self._residual_norm(o, res, w[p + "post_norm"], xn)
             pending = self._mlp(i, xn)
+            if pc is not None:
+                pc.mark(3, 2)
+                prev = 3
+                if pc.nvtx:
+                    torch.cuda.nvtx.range_pop()
         if return_hidden:
             if pending is not None:
                 self._residual_norm(pending, res, w["final_norm"], xn)
@@ -279,7 +325,10 @@ class MLAMoEModel:
         if self.ep is not None:
             self.ep.end_step()
         sel = xn if fb.logits_idx is None else ops.gather_rows(xn, fb.logits_idx)
-        return ops.linear(sel, w["lm_head"])
+        logits = ops.linear(sel, w["lm_head"])
+        if pc is not None:
+            pc.mark(4, prev)
+        return logits
 
 
 class DecodeGraph:

@@ -35,6 +35,8 @@ def main():
                          "load and weight bytes of one rank of an N-way expert-parallel run")
     ap.add_argument("--no-trace", action="store_true", help="run the steps without the profiler (for ncu)")
     ap.add_argument("--graph", action="store_true", help="replay the step as one CUDA graph")
+    ap.add_argument("--phase-clock", action="store_true",
+                    help="report device phase clocks (attention / MLP-MoE / LM head) of the timed replays")
     ap.add_argument("--time", type=int, default=0,
                     help="also time this many graph replays with CUDA events (device ms per step)")
     args = ap.parse_args()
@@ -80,6 +82,9 @@ def main():
         dg.run()
     torch.cuda.synchronize()
     if args.time:
+        if args.phase_clock:
+            from sparkpipe_rs_b200.models.mla_moe import PhaseClock
+            model.phase_clock = PhaseClock(dev)
         tg = dg if args.graph else DecodeGraph(model, cache, B, bps, horizon, use_graph=True, self_advance=True)
         start(tg)
         for _ in range(3):
@@ -93,6 +98,12 @@ def main():
         torch.cuda.synchronize()
         print(f"[rank {rank}/{world}] graph replay: {e0.elapsed_time(e1) / args.time:.3f} ms per decode step "
               f"(batch {B}, context {args.ctx}, {cfg.num_layers} layers)", flush=True)
+        if model.phase_clock is not None:
+            # warm-up replays (3) + timed replays, all through the same graph
+            rep = model.phase_clock.report(3 + args.time)
+            print(f"[rank {rank}/{world}] phase clocks, us per step: " +
+                  ", ".join(f"{k} {v:.1f}" for k, v in rep.items()), flush=True)
+            model.phase_clock = None
         start(dg)
         if tg is not dg:
             tg.release()
