@@ -238,6 +238,9 @@ void spec_verify(const int* draft, const int* target, int B, int L, float forced
 void spec_finish(int* tok_rows, const int* tgt_rows, int B, int L, float p_accept, unsigned long long seed,
                  int* pos_rows, int* ctx_rows, int* slot_rows, const int* block_table, int max_blocks,
                  int block_size, int* accepted, int* committed, unsigned long long* total_committed, cudaStream_t s);
+// Paged KV blocks of a [layers][slots][row] bf16 cache <-> staging [n][layers][block_size][row].
+void kv_blocks_copy(void* cache, long long layer_stride, const int* blocks, int n, void* staging, int layers,
+                    int block_size, int row, int to_staging, cudaStream_t s);
 // Phase clocks: totals[slot] += now - stamps[prev] (prev >= 0); stamps[slot] <- device global timer (ns).
 void phase_mark(unsigned long long* stamps, unsigned long long* totals, int slot, int prev, cudaStream_t s);
 void decode_advance(const int* out_ids, int* ids, int* pos, int* ctx, int* slots, const int* block_table,

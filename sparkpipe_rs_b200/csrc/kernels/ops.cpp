@@ -579,6 +579,19 @@ void spec_finish(const Tensor& tok_rows, const Tensor& tgt_rows, int64_t L, doub
                   accepted.data_ptr<int>(), committed.data_ptr<int>(), tc, stream());
 }
 
+void kv_blocks_copy(const Tensor& cache, const Tensor& blocks, const Tensor& staging, int64_t block_size,
+                    bool to_staging) {
+  // cache [layers, slots, row] bf16 (contiguous); staging [n, layers, block_size, row] bf16
+  CHECK_CUDA(cache); CHECK_BF16(cache); CHECK_CONTIG(cache); CHECK_BF16(staging); CHECK_CONTIG(staging);
+  CHECK_I32(blocks); CHECK_CONTIG(blocks);
+  TORCH_CHECK(cache.dim() == 3 && cache.size(1) % block_size == 0, "kv_blocks_copy: cache [layers, slots, row]");
+  const int64_t n = blocks.numel(), L = cache.size(0), row = cache.size(2);
+  TORCH_CHECK(staging.numel() >= n * L * block_size * row, "kv_blocks_copy: staging too small");
+  const c10::cuda::CUDAGuard guard(cache.device());
+  sp::kv_blocks_copy(cache.data_ptr(), cache.stride(0), blocks.data_ptr<int>(), (int)n, staging.data_ptr(), (int)L,
+                     (int)block_size, (int)row, to_staging ? 1 : 0, stream());
+}
+
 void phase_mark(const Tensor& stamps, const c10::optional<Tensor>& totals, int64_t slot, int64_t prev) {
   TORCH_CHECK(stamps.is_cuda() && stamps.scalar_type() == at::kLong && slot >= 0 && slot < stamps.numel(),
               "phase_mark: stamps must be a CUDA int64 tensor holding the slot");
@@ -760,6 +773,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_advance", &decode_advance);
   m.def("spec_finish", &spec_finish);
   m.def("phase_mark", &phase_mark);
+  m.def("kv_blocks_copy", &kv_blocks_copy);
   m.def("slab_add_rmsnorm", &slab_add_rmsnorm);
   m.def("mla_decode_prep", &mla_decode_prep);
   m.def("combine_add_rmsnorm", &combine_add_rmsnorm);

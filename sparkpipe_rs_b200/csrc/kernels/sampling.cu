@@ -212,6 +212,34 @@ void spec_finish(int* tok_rows, const int* tgt_rows, int B, int L, float p_accep
            total_committed);
 }
 
+// Paged KV blocks <-> a contiguous staging buffer, for moving blocks between the
+// device cache [layers][slots][row] and a host tier. One CTA per (block, layer)
+// copies block_size rows of `row` bf16 with 16-byte accesses; the staging layout is
+// [n][layers][block_size][row], so a batch of blocks moves to or from pinned host
+// memory in one copy.
+__global__ void __launch_bounds__(256) kv_blocks_copy_kernel(bf16* __restrict__ cache, long long layer_stride,
+                                                              const int* __restrict__ blocks, bf16* __restrict__ staging,
+                                                              int layers, int block_size, int row, int to_staging) {
+  griddep_wait();
+  griddep_launch();
+  const int i = blockIdx.x / layers, l = blockIdx.x - (blockIdx.x / layers) * layers;
+  const long long n8 = (long long)block_size * row / 8;
+  uint4* c = reinterpret_cast<uint4*>(cache + l * layer_stride + (long long)blocks[i] * block_size * row);
+  uint4* st = reinterpret_cast<uint4*>(staging + ((long long)i * layers + l) * block_size * row);
+  for (long long k = threadIdx.x; k < n8; k += blockDim.x) {
+    if (to_staging) st[k] = c[k];
+    else c[k] = st[k];
+  }
+}
+
+void kv_blocks_copy(void* cache, long long layer_stride, const int* blocks, int n, void* staging, int layers,
+                    int block_size, int row, int to_staging, cudaStream_t s) {
+  if (n <= 0) return;
+  if ((long long)block_size * row % 8 || layer_stride % 8) throw std::runtime_error("kv_blocks_copy: 16-byte rows");
+  launch_k(kv_blocks_copy_kernel, dim3((unsigned)(n * layers)), dim3(256), 0, s, static_cast<bf16*>(cache),
+           layer_stride, blocks, static_cast<bf16*>(staging), layers, block_size, row, to_staging);
+}
+
 // Phase clock: one thread stamps the device's global timer (ns) into slot `slot`
 // of a step's clock array and adds the time since slot `prev`'s stamp to the
 // phase's running total. Stream-ordered with the kernels around it (it waits for

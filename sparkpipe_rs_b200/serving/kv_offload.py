@@ -1,0 +1,109 @@
+"""Host-memory tier for paged KV blocks: evict blocks of the device cache into
+pinned host memory and restore them (possibly into other physical blocks) ahead of
+use, on a side stream.
+
+  evict(blocks)    kv_blocks_copy gathers the blocks' rows of every layer into a
+                   device staging buffer, then one device->host copy per batch moves
+                   them into pinned host slots; returns the host slot ids.
+  prefetch(slots, blocks)  one host->device copy into staging (on the copy stream,
+                   overlapping whatever runs on the compute stream), then
+                   kv_blocks_copy scatters the rows into the target blocks; an event
+                   marks completion and ``wait(handle)`` orders the compute stream
+                   after it, so a decode step that needs the blocks waits only for them.
+
+The residency bookkeeping (which blocks are resident, eviction order) is the C++
+KvArena's; this is the data mover. Batches are capped so the staging buffer stays
+small; every copy is one cudaMemcpyAsync (no batched-copy API).
+
+Reference behaviour: the KV cache async prefetch backend declared in
+crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_kv_cache.h:227-300 (copy
+engine, in-flight capacity) and the tier-3 lookahead design of spark_nvme_tier.h; the
+reference ships neither.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+
+
+class HostKvTier:
+    def __init__(self, cache, host_blocks: int, max_batch_blocks: int = 64):
+        self.cache = cache
+        data = cache.data
+        self.layers, _, self.row = data.shape
+        self.bs = cache.block_size
+        self.block_elems = self.layers * self.bs * self.row
+        self.max_batch = max_batch_blocks
+        self.host = torch.empty(host_blocks, self.block_elems, dtype=data.dtype, pin_memory=True)
+        self.free = list(range(host_blocks))[::-1]
+        self.pending = []  # (event, host slots) of restores still reading their slots
+        # one staging buffer per direction: evictions run on the compute stream,
+        # restores on the copy stream
+        self.staging_out = torch.empty(max_batch_blocks * self.block_elems, dtype=data.dtype, device=data.device)
+        self.staging_in = torch.empty(max_batch_blocks * self.block_elems, dtype=data.dtype, device=data.device)
+        self.stream = torch.cuda.Stream(device=data.device)
+        self.evicted_blocks = 0
+        self.restored_blocks = 0
+
+    def _ids(self, blocks):
+        return torch.as_tensor(blocks, dtype=torch.int32).to(self.cache.data.device, non_blocking=True)
+
+    def _reclaim(self, block: bool = False):
+        keep = []
+        for ev, slots in self.pending:
+            if block:
+                ev.synchronize()
+            if block or ev.query():
+                self.free.extend(slots)
+            else:
+                keep.append((ev, slots))
+        self.pending = keep
+
+    def evict(self, blocks: list[int]) -> list[int]:
+        """Copies the blocks to host slots (blocking until the copy is done); the device
+        blocks may be reused afterwards. Returns one host slot per block."""
+        self._reclaim(block=len(blocks) > len(self.free))
+        if len(blocks) > len(self.free):
+            raise RuntimeError("host KV tier full")
+        slots = [self.free.pop() for _ in blocks]
+        for i in range(0, len(blocks), self.max_batch):
+            chunk, sl = blocks[i:i + self.max_batch], slots[i:i + self.max_batch]
+            n = len(chunk)
+            ops.kernels().kv_blocks_copy(self.cache.data, self._ids(chunk), self.staging_out, self.bs, True)
+            st = self.staging_out[:n * self.block_elems].view(n, self.block_elems)
+            # host slots of one batch are copied one contiguous run at a time
+            j = 0
+            while j < n:
+                k = j
+                while k + 1 < n and sl[k + 1] == sl[k] + 1:
+                    k += 1
+                self.host[sl[j]:sl[k] + 1].copy_(st[j:k + 1], non_blocking=True)
+                j = k + 1
+        torch.cuda.current_stream().synchronize()
+        self.evicted_blocks += len(blocks)
+        return slots
+
+    def prefetch(self, slots: list[int], blocks: list[int]):
+        """Starts restoring host slots into device blocks on the copy stream; returns a
+        handle for ``wait``. The host slots return to the free list once the copy that
+        reads them has completed."""
+        assert len(slots) == len(blocks)
+        done = torch.cuda.Event()
+        cur = torch.cuda.current_stream()
+        self.stream.wait_stream(cur)  # the target blocks may have been in use just before
+        with torch.cuda.stream(self.stream):
+            for i in range(0, len(blocks), self.max_batch):
+                chunk, sl = blocks[i:i + self.max_batch], slots[i:i + self.max_batch]
+                n = len(chunk)
+                st = self.staging_in[:n * self.block_elems].view(n, self.block_elems)
+                for j, s in enumerate(sl):
+                    st[j].copy_(self.host[s], non_blocking=True)
+                ops.kernels().kv_blocks_copy(self.cache.data, self._ids(chunk), self.staging_in, self.bs, False)
+            done.record(self.stream)
+        self.pending.append((done, list(slots)))
+        self.restored_blocks += len(blocks)
+        return done
+
+    def wait(self, handle):
+        torch.cuda.current_stream().wait_event(handle)
