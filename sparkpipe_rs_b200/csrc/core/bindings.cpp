@@ -262,6 +262,7 @@ void bind_scheduler(py::module_& m) {
   m.attr("DECISION_CUDAGRAPH_PADDING") = kDecisionCudaGraphPadding;
   m.attr("DECISION_DECODE_STEP") = kDecisionDecodeStep;
   m.attr("DECISION_PREFILL_STEP") = kDecisionPrefillStep;
+  m.attr("DECISION_SCHEDULED_AHEAD") = kDecisionScheduledAhead;
   m.attr("DECISION_PREEMPTED") = kDecisionPreempted;
 
   py::class_<SchedulerConfig>(m, "SchedulerConfig")
@@ -279,7 +280,7 @@ void bind_scheduler(py::module_& m) {
   py::class_<RequestSpec>(m, "RequestSpec")
       .def(py::init<>())
       .def(py::init([](uint64_t id, const std::vector<uint32_t>& prompt, uint32_t max_new, uint32_t priority,
-                       const std::vector<uint32_t>& stops, bool ignore_eos) {
+                       const std::vector<uint32_t>& stops, bool ignore_eos, float temperature, uint64_t seed) {
              RequestSpec r;
              r.id = id;
              r.prompt = prompt;
@@ -287,10 +288,15 @@ void bind_scheduler(py::module_& m) {
              r.priority = priority;
              r.stop_token_ids = stops;
              r.ignore_eos = ignore_eos;
+             r.temperature = temperature;
+             r.seed = seed;
              return r;
            }),
            py::arg("id"), py::arg("prompt"), py::arg("max_new_tokens") = 16, py::arg("priority") = 1000000,
-           py::arg("stop_token_ids") = std::vector<uint32_t>{}, py::arg("ignore_eos") = false)
+           py::arg("stop_token_ids") = std::vector<uint32_t>{}, py::arg("ignore_eos") = false,
+           py::arg("temperature") = 0.f, py::arg("seed") = 0)
+      .def_readwrite("temperature", &RequestSpec::temperature)
+      .def_readwrite("seed", &RequestSpec::seed)
       .def_readwrite("id", &RequestSpec::id)
       .def_readwrite("prompt", &RequestSpec::prompt)
       .def_readwrite("max_new_tokens", &RequestSpec::max_new_tokens)
@@ -321,6 +327,7 @@ void bind_scheduler(py::module_& m) {
       .def_property_readonly("chunk_lens", [](const StepPlan& p) { return to_np(p.chunk_lens); })
       .def_property_readonly("block_table", [](const StepPlan& p) { return to_np(p.block_table); })
       .def_property_readonly("context_lens", [](const StepPlan& p) { return to_np(p.context_lens); })
+      .def_property_readonly("src_rows", [](const StepPlan& p) { return to_np(p.src_rows); })
       // Fast path: copy the decode inputs into preallocated (pinned) CPU tensors.
       .def("write_decode_inputs",
            [](const StepPlan& p, const torch::Tensor& ids, const torch::Tensor& pos, const torch::Tensor& slots,
@@ -361,6 +368,17 @@ void bind_scheduler(py::module_& m) {
       .def(py::init<const SchedulerConfig&>())
       .def("add_request", &Scheduler::add_request)
       .def("schedule", &Scheduler::schedule)
+      .def("schedule_ahead", &Scheduler::schedule_ahead)
+      .def("sampling_rows",
+           [](const Scheduler& s, const StepPlan& p, const torch::Tensor& temp, const torch::Tensor& key) {
+             TORCH_CHECK(!temp.is_cuda() && temp.scalar_type() == at::kFloat && temp.is_contiguous(),
+                         "temperature rows: float32 CPU tensor");
+             TORCH_CHECK(!key.is_cuda() && key.scalar_type() == at::kLong && key.is_contiguous(),
+                         "key rows: int64 CPU tensor");
+             TORCH_CHECK(temp.numel() == key.numel(), "sampling_rows: row counts differ");
+             return s.sampling_rows(p, temp.data_ptr<float>(), reinterpret_cast<uint64_t*>(key.data_ptr<int64_t>()),
+                                    (uint32_t)temp.numel());
+           })
       .def("complete",
            [](Scheduler& s, const StepPlan& p, py::array_t<int32_t, py::array::c_style | py::array::forcecast> t) {
              return s.complete(p, t.data(), (uint32_t)t.size());

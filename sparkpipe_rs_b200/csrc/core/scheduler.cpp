@@ -235,6 +235,97 @@ StepPlan Scheduler::build_decode() {
   return p;
 }
 
+StepPlan Scheduler::schedule_ahead(const StepPlan& inflight) {
+  if (inflight.kind != StepPlan::Decode) return StepPlan{};
+  // the policy would run a prefill next (a waiting prompt and a free seat)
+  if (!waiting_.empty() && running_count_ < cfg_.max_batch) return StepPlan{};
+  // the decode set must be the in-flight step's live sequences, in order
+  std::vector<uint32_t> rows;
+  rows.reserve(inflight.num_seqs);
+  for (uint32_t i = 0; i < inflight.num_seqs; ++i)
+    if (reqs_.count(inflight.seq_ids[i])) rows.push_back(i);
+  if (rows.size() != running_.size()) return StepPlan{};
+  for (size_t k = 0; k < rows.size(); ++k)
+    if (running_[k] != inflight.seq_ids[rows[k]]) return StepPlan{};
+  // keep the sequences that cannot end by length or context at the in-flight step
+  std::vector<uint32_t> keep;
+  for (uint32_t i : rows) {
+    const uint64_t id = inflight.seq_ids[i];
+    const Req& r = reqs_.at(id);
+    const uint32_t len = (uint32_t)r.tokens.size();
+    if (r.generated + 1 >= r.spec.max_new_tokens || len + 1 >= cfg_.max_model_len) continue;
+    try {
+      cache_->ensure_sequence_token_capacity(id, len + 1);
+    } catch (const StatusError& e) {
+      if (e.status == Status::CapacityExceeded) return StepPlan{};  // the synchronous path preempts
+      throw;
+    }
+    keep.push_back(i);
+  }
+  const uint32_t n = (uint32_t)keep.size();
+  if (n == 0) return StepPlan{};
+  StepPlan p;
+  p.kind = StepPlan::Decode;
+  p.flags = kDecisionDecodeStep | kDecisionScheduledAhead;
+  p.step_index = ++step_clock_;
+  const uint32_t padded = bucket_for(n);
+  if (padded != n) p.flags |= kDecisionCudaGraphPadding;
+  p.num_seqs = n;
+  p.padded_seqs = padded;
+  p.max_blocks = max_blocks_;
+  p.token_ids.assign(padded, 0);
+  p.src_rows.assign(padded, -1);
+  p.positions.assign(padded, 0);
+  p.slot_mapping.assign(padded, -1);
+  p.context_lens.assign(padded, 0);
+  p.block_table.assign(size_t(padded) * max_blocks_, 0);
+  for (uint32_t k = 0; k < n; ++k) {
+    const uint64_t id = inflight.seq_ids[keep[k]];
+    const Req& r = reqs_.at(id);
+    const uint32_t pos = (uint32_t)r.tokens.size();  // the in-flight step's token lands here
+    p.seq_ids.push_back(id);
+    p.token_ids[k] = int32_t(keep[k]);
+    p.src_rows[k] = int32_t(keep[k]);
+    p.positions[k] = int32_t(pos);
+    p.slot_mapping[k] = slot_of(r, id, pos);
+    p.context_lens[k] = int32_t(pos + 1);
+    const auto& blocks = cache_->block_list(id);
+    std::copy(blocks.begin(), blocks.end(), p.block_table.begin() + size_t(k) * max_blocks_);
+    p.max_context = std::max(p.max_context, pos + 1);
+  }
+  p.num_tokens = n;
+  ++stats_.steps;
+  ++stats_.decode_steps;
+  stats_.decode_tokens += n;
+  return p;
+}
+
+namespace {
+uint64_t mix64(uint64_t z) {  // SplitMix64 finaliser (Steele, Lea & Flood, OOPSLA 2014)
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+}  // namespace
+
+bool Scheduler::sampling_rows(const StepPlan& p, float* temp, uint64_t* key, uint32_t rows) const {
+  bool any = false;
+  for (uint32_t i = 0; i < rows; ++i) {
+    temp[i] = 0.f;
+    key[i] = 0;
+    if (i >= p.num_seqs) continue;
+    auto it = reqs_.find(p.seq_ids[i]);
+    if (it == reqs_.end() || it->second.spec.temperature <= 0.f) continue;
+    // position of the token whose successor this row samples
+    int32_t pos = p.kind == StepPlan::Prefill ? p.positions[size_t(p.cu_q[i + 1]) - 1] : p.positions[i];
+    temp[i] = it->second.spec.temperature;
+    key[i] = mix64(it->second.spec.seed ^ mix64(uint64_t(uint32_t(pos)) + 1));
+    any = true;
+  }
+  return any;
+}
+
 void Scheduler::finish(Req& r, uint64_t id, FinishReason why, std::vector<SchedEvent>& ev) {
   if (r.reserved) cache_->release_sequence(id);
   r.reserved = false;

@@ -56,6 +56,7 @@ constexpr uint32_t kDecisionPrefixCacheUsed = 0x004;
 constexpr uint32_t kDecisionCudaGraphPadding = 0x008;
 constexpr uint32_t kDecisionDecodeStep = 0x010;
 constexpr uint32_t kDecisionPrefillStep = 0x020;
+constexpr uint32_t kDecisionScheduledAhead = 0x040;  // decode planned before the previous step's tokens were read
 constexpr uint32_t kDecisionPreempted = 0x800;
 
 // finish reasons
@@ -81,6 +82,8 @@ struct RequestSpec {
   uint32_t priority = 1000000;        // higher runs first; ties by arrival
   std::vector<uint32_t> stop_token_ids;
   bool ignore_eos = false;
+  float temperature = 0.f;            // <= 0: greedy
+  uint64_t seed = 0;
 };
 
 struct StepPlan {
@@ -101,6 +104,9 @@ struct StepPlan {
   uint32_t cached_prefix_tokens = 0;
   // decode
   std::vector<int32_t> block_table, context_lens;
+  // decode scheduled ahead: row i's input token is the previous step's sampled
+  // token of row src_rows[i] (token_ids carries the same indices)
+  std::vector<int32_t> src_rows;
   uint32_t max_blocks = 0;
   uint32_t max_context = 0;
 };
@@ -125,7 +131,19 @@ class Scheduler {
   explicit Scheduler(const SchedulerConfig& cfg);
   void add_request(const RequestSpec& spec);
   StepPlan schedule();
+  // The decode step that follows the in-flight decode step `inflight`, planned
+  // before its tokens are known (every earlier step must be completed). Each of
+  // its sequences is assumed to continue; one that stops at `inflight` gets one
+  // discarded extra token. Returns an empty plan (kind None) when that is not
+  // safe or not the policy's choice: a prefill may be due, the decode set
+  // changed, or the KV blocks for one more token are not free.
+  StepPlan schedule_ahead(const StepPlan& inflight);
   std::vector<SchedEvent> complete(const StepPlan& plan, const int32_t* sampled, uint32_t n_sampled);
+  // Per-row sampling parameters of a plan (rows beyond num_seqs are greedy):
+  // temperature and a noise key derived from the request's seed and the position
+  // of the token that is sampled, so a request draws the same tokens however it
+  // is batched. Returns whether any row samples (temperature > 0).
+  bool sampling_rows(const StepPlan& plan, float* temp, uint64_t* key, uint32_t rows) const;
   bool cancel(uint64_t id);  // false when unknown / already finished
   void fail_step(const StepPlan& plan);  // a dispatched step failed: cancel its sequences
 

@@ -226,7 +226,9 @@ void embedding(const void* table, long long ld, const int* ids, void* out, long 
                cudaStream_t s);
 // temperature <= 0 -> greedy argmax; else Gumbel-max sampling seeded by (seed, offset, row).
 void sample_tokens(const void* logits, long long ldl, int T, int V, float temperature, unsigned long long seed,
-                   unsigned long long offset, int* out_ids, float* out_logit, cudaStream_t s);
+                   unsigned long long offset, int* out_ids, float* out_logit, const float* row_temp,
+                   const unsigned long long* row_key, cudaStream_t s);
+void gather_prev_tokens(int* ids, const int* prev, int n, int prev_rows, cudaStream_t s);
 // Greedy speculative verification over a chain of L drafts per row.
 // target: [B, L+1] argmax tokens of the verifier; draft: [B, L].
 // forced_accept_p > 0 replaces the token comparison by a seeded Bernoulli(p).

@@ -534,15 +534,34 @@ void embedding(const Tensor& table, const Tensor& ids, const Tensor& out) {
 }
 
 void sample_tokens(const Tensor& logits, double temperature, int64_t seed, int64_t offset, const Tensor& out_ids,
-                   const c10::optional<Tensor>& out_logit) {
+                   const c10::optional<Tensor>& out_logit, const c10::optional<Tensor>& row_temp,
+                   const c10::optional<Tensor>& row_key) {
   CHECK_CUDA(logits); CHECK_BF16(logits); CHECK_I32(out_ids);
   TORCH_CHECK(logits.stride(1) == 1, "logits rows must be contiguous");
   const c10::cuda::CUDAGuard guard(logits.device());
   float* ol = nullptr;
   if (out_logit.has_value()) { CHECK_F32(*out_logit); ol = out_logit->data_ptr<float>(); }
+  const float* rt = nullptr;
+  const unsigned long long* rk = nullptr;
+  TORCH_CHECK(row_temp.has_value() == row_key.has_value(), "sample_tokens: row_temp and row_key go together");
+  if (row_temp.has_value()) {
+    CHECK_F32(*row_temp); CHECK_CONTIG(*row_temp); CHECK_CONTIG(*row_key);
+    TORCH_CHECK(row_key->scalar_type() == torch::kInt64, "row_key must be int64");
+    TORCH_CHECK(row_temp->numel() >= logits.size(0) && row_key->numel() >= logits.size(0),
+                "sample_tokens: fewer row parameters than logits rows");
+    rt = row_temp->data_ptr<float>();
+    rk = reinterpret_cast<const unsigned long long*>(row_key->data_ptr<int64_t>());
+  }
   sp::sample_tokens(logits.data_ptr(), logits.stride(0), (int)logits.size(0), (int)logits.size(1),
                     (float)temperature, (unsigned long long)seed, (unsigned long long)offset, out_ids.data_ptr<int>(),
-                    ol, stream());
+                    ol, rt, rk, stream());
+}
+
+void gather_prev_tokens(const Tensor& ids, const Tensor& prev, int64_t n) {
+  CHECK_CUDA(ids); CHECK_I32(ids); CHECK_I32(prev); CHECK_CONTIG(ids); CHECK_CONTIG(prev);
+  TORCH_CHECK(n >= 0 && n <= ids.numel(), "gather_prev_tokens: n out of range");
+  const c10::cuda::CUDAGuard guard(ids.device());
+  sp::gather_prev_tokens(ids.data_ptr<int>(), prev.data_ptr<int>(), (int)n, (int)prev.numel(), stream());
 }
 
 void spec_verify(const Tensor& draft, const Tensor& target, double p_accept, int64_t seed, int64_t offset,
@@ -769,6 +788,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine);
   m.def("embedding", &embedding);
   m.def("sample_tokens", &sample_tokens);
+  m.def("gather_prev_tokens", &gather_prev_tokens);
   m.def("spec_verify", &spec_verify);
   m.def("decode_advance", &decode_advance);
   m.def("spec_finish", &spec_finish);

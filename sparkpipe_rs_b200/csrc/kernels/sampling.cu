@@ -37,11 +37,22 @@ SP_DEVI float uniform01(uint64_t seed, uint64_t a, uint64_t b, uint64_t c) {
   return ((h >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
 }
 
+// With per-row parameters (row_temp != nullptr) each row has its own temperature
+// and noise key, and the noise does not depend on the row's place in the batch:
+// the same request draws the same tokens however it is batched.
 __global__ void sample_kernel(const bf16* __restrict__ logits, long long ldl, int V, float temp, uint64_t seed,
-                              uint64_t offset, int* __restrict__ out_ids, float* __restrict__ out_logit) {
+                              uint64_t offset, int* __restrict__ out_ids, float* __restrict__ out_logit,
+                              const float* __restrict__ row_temp, const unsigned long long* __restrict__ row_key) {
   griddep_wait();
   griddep_launch();
   const int row = blockIdx.x;
+  uint64_t hrow = row;
+  if (row_temp) {
+    temp = row_temp[row];
+    seed = row_key[row];
+    offset = 0;
+    hrow = 0;
+  }
   const bf16* lr = logits + (long long)row * ldl;
   float best = -INFINITY;
   int bi = 0x7fffffff;
@@ -54,14 +65,14 @@ __global__ void sample_kernel(const bf16* __restrict__ logits, long long ldl, in
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         float s = v[e];
-        if (temp > 0.f) s = s * inv_t - __logf(-__logf(uniform01(seed, offset, row, c + e)));
+        if (temp > 0.f) s = s * inv_t - __logf(-__logf(uniform01(seed, offset, hrow, c + e)));
         if (s > best) { best = s; bi = c + e; }
       }
     }
   } else {
     for (int c = threadIdx.x; c < V; c += blockDim.x) {
       float s = __bfloat162float(lr[c]);
-      if (temp > 0.f) s = s * inv_t - __logf(-__logf(uniform01(seed, offset, row, c)));
+      if (temp > 0.f) s = s * inv_t - __logf(-__logf(uniform01(seed, offset, hrow, c)));
       if (s > best) { best = s; bi = c; }
     }
   }
@@ -94,10 +105,27 @@ __global__ void sample_kernel(const bf16* __restrict__ logits, long long ldl, in
 }
 
 void sample_tokens(const void* logits, long long ldl, int T, int V, float temperature, unsigned long long seed,
-                   unsigned long long offset, int* out_ids, float* out_logit, cudaStream_t s) {
+                   unsigned long long offset, int* out_ids, float* out_logit, const float* row_temp,
+                   const unsigned long long* row_key, cudaStream_t s) {
   if (T <= 0) return;
   launch_k(sample_kernel, dim3(T), dim3(1024), 0, s, (const bf16*)logits, ldl, V, temperature, (uint64_t)seed,
-           (uint64_t)offset, out_ids, out_logit);
+           (uint64_t)offset, out_ids, out_logit, row_temp, row_key);
+}
+
+// Fills the first n rows of a decode step's token ids from the previous step's
+// sampled tokens: on entry ids[i] holds the previous step's row index.
+__global__ void gather_prev_tokens_kernel(int* __restrict__ ids, const int* __restrict__ prev, int n, int prev_rows) {
+  griddep_wait();
+  griddep_launch();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int r = ids[i];
+  ids[i] = (r >= 0 && r < prev_rows) ? prev[r] : 0;
+}
+
+void gather_prev_tokens(int* ids, const int* prev, int n, int prev_rows, cudaStream_t s) {
+  if (n <= 0) return;
+  launch_k(gather_prev_tokens_kernel, dim3((n + 127) / 128), dim3(128), 0, s, ids, prev, n, prev_rows);
 }
 
 __global__ void embedding_kernel(const bf16* __restrict__ table, long long ld, const int* __restrict__ ids,

@@ -332,11 +332,13 @@ class MLAMoEModel:
 
 
 class DecodeGraph:
-    """One CUDA graph of a full decode step (forward + greedy/seeded sampling) for a
-    fixed batch size. Inputs are copied into static device buffers before replay."""
+    """One CUDA graph of a full decode step (forward + sampling) for a fixed batch
+    size. Inputs are copied into static device buffers before replay; sampling reads
+    a per-row temperature and noise key (``temps`` / ``keys``, zero = greedy), so one
+    graph serves greedy and sampled requests in the same batch."""
 
     def __init__(self, model: MLAMoEModel, cache: KVCache, batch: int, max_blocks: int, max_context: int,
-                 temperature: float = 0.0, seed: int = 0, use_graph: bool = True, self_advance: bool = False):
+                 use_graph: bool = True, self_advance: bool = False):
         self.model, self.cache, self.B = model, cache, batch
         dev = model.device
         self.ids = torch.zeros(batch, dtype=torch.int32, device=dev)
@@ -345,7 +347,9 @@ class DecodeGraph:
         self.block_table = torch.zeros(batch, max_blocks, dtype=torch.int32, device=dev)
         self.ctx = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.out_ids = torch.zeros(batch, dtype=torch.int32, device=dev)
-        self.temperature, self.seed = temperature, seed
+        self.temps = torch.zeros(batch, dtype=torch.float32, device=dev)
+        self.keys = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.sampling_dirty = False  # temps / keys hold a sampled batch's values
         self.self_advance = self_advance
         self.step_offset = torch.zeros(1, dtype=torch.int64)
         heads = model.cfg.num_heads
@@ -368,7 +372,7 @@ class DecodeGraph:
 
     def _step(self):
         logits = self.model.forward(self.fb, self.cache)
-        ops.sample_tokens(logits, self.temperature, self.seed, 0, out_ids=self.out_ids)
+        ops.sample_tokens(logits, out_ids=self.out_ids, row_temp=self.temps, row_key=self.keys)
         if self.self_advance:
             ops.decode_advance(self.out_ids, self.ids, self.pos, self.ctx, self.slots, self.block_table,
                                self.cache.block_size)

@@ -430,12 +430,22 @@ def embedding(table, ids, out=None):
     return out
 
 
-def sample_tokens(logits, temperature=0.0, seed=0, offset=0, out_ids=None, out_logit=None):
+def sample_tokens(logits, temperature=0.0, seed=0, offset=0, out_ids=None, out_logit=None, row_temp=None,
+                  row_key=None):
+    """Greedy / Gumbel-max sampling of each logits row. One temperature and seed for
+    the batch, or per-row ``row_temp`` (float32) and ``row_key`` (int64 noise key) tensors."""
     if out_ids is None:
         out_ids = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
-    kernels().sample_tokens(logits, float(temperature), int(seed), int(offset), out_ids, out_logit)
+    kernels().sample_tokens(logits, float(temperature), int(seed), int(offset), out_ids, out_logit, row_temp, row_key)
     _count(1)
     return out_ids
+
+
+def gather_prev_tokens(ids, prev, n):
+    """ids[i] = prev[ids[i]] for i < n: a decode step scheduled ahead takes its input
+    tokens from the previous step's sampled tokens without a host round trip."""
+    kernels().gather_prev_tokens(ids, prev, int(n))
+    _count(1)
 
 
 def spec_verify(draft, target, p_accept=0.0, seed=0, offset=0):

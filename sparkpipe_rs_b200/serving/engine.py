@@ -11,6 +11,13 @@ One engine owns one model replica on one GPU. Each ``step()``:
   4. reads the sampled tokens back (device->host) and hands them to the
      scheduler, which advances every request and reports token / finish events.
 
+Decode steps overlap the host with the GPU: while step n runs, the scheduler
+plans step n+1 ahead of n's tokens (``Scheduler.schedule_ahead``), its inputs are
+copied, and its graph is launched with the token ids gathered on the device from
+n's sampled tokens; only then does the host wait for n's tokens. A sequence that
+stops at step n gets one discarded extra token. Decode graphs for every batch
+bucket are captured when the engine starts.
+
 Request lifecycle and event names follow the reference's serving engine
 (crates/spark-serve/src/serving_engine/engine.rs:1381-2050: invoke_prefill /
 invoke_decode / complete_*_dispatch / pump) with the reference's ring dispatch
@@ -43,6 +50,8 @@ class EngineConfig:
     prefix_caching: bool = True
     chunked_prefill: bool = True
     seed: int = 0
+    async_decode: bool = True         # plan and launch decode step n+1 before reading step n's tokens
+    capture_graphs_at_start: bool = True
 
 
 @dataclass
@@ -99,6 +108,16 @@ class _Pinned:
         return t[:n]
 
 
+@dataclass
+class _Launched:
+    """A step whose GPU work is enqueued: its sampled tokens land in ``host``."""
+    plan: object
+    host: torch.Tensor
+    event: object          # CUDA event after the device->host copy (None on CPU)
+    out: torch.Tensor      # device tensor of the sampled tokens
+    t0: float
+
+
 class LLMEngine:
     def __init__(self, cfg: MLAMoEConfig, ecfg: EngineConfig | None = None, model=None, device="cuda",
                  cache: KVCache | None = None):
@@ -141,6 +160,16 @@ class LLMEngine:
         self._ids = itertools.count(1)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
+        # CUDA eager decode reuses one set of pinned input buffers, so it stays synchronous
+        self.async_decode = e.async_decode and (self.use_graphs or not self.is_cuda)
+        self._inflight: _Launched | None = None
+        self.ahead_steps = 0  # decode steps launched ahead of the previous step's tokens
+        self._parity = 0
+        self._last_done = 0.0
+        self._random: set[int] = set()  # live requests that sample (temperature > 0)
+        if self.use_graphs and e.capture_graphs_at_start:
+            for b in sc.decode_buckets:
+                self._graph(b)
         self.step_log: list[tuple[str, int, float]] = []  # (kind, seqs, seconds)
 
     # ------------------------------------------------------------------ requests
@@ -149,14 +178,17 @@ class LLMEngine:
         rid = request_id if request_id is not None else next(self._ids)
         spec = self.core.RequestSpec(rid, [int(t) for t in prompt_token_ids], int(params.max_tokens),
                                      int(params.priority), [int(t) for t in params.stop_token_ids],
-                                     bool(params.ignore_eos))
+                                     bool(params.ignore_eos), float(params.temperature), int(params.seed))
         self.scheduler.add_request(spec)
         self.outputs[rid] = RequestOutput(rid, len(prompt_token_ids), arrival=time.perf_counter())
         self.params[rid] = params
+        if params.temperature > 0:
+            self._random.add(rid)
         return rid
 
     def abort_request(self, request_id: int) -> bool:
         ok = self.scheduler.cancel(request_id)
+        self._random.discard(request_id)
         out = self.outputs.get(request_id)
         if ok and out is not None:
             out.finished = True
@@ -165,7 +197,7 @@ class LLMEngine:
         return ok
 
     def has_unfinished_requests(self) -> bool:
-        return self.scheduler.has_work()
+        return self.scheduler.has_work() or self._inflight is not None
 
     # ------------------------------------------------------------------ GPU steps
     def _h2d(self, name: str, arr) -> torch.Tensor:
@@ -176,16 +208,32 @@ class LLMEngine:
         self.h2d_bytes += host.numel() * host.element_size()
         return host.to(self.device, non_blocking=True)
 
-    def _sample(self, logits: torch.Tensor, seq_ids, step_index: int) -> torch.Tensor:
-        p0 = self.params.get(seq_ids[0]) if seq_ids else None
-        temp = p0.temperature if p0 else 0.0
+    def _sampling_rows(self, plan, rows: int, tag: str):
+        """Per-row (temperature, noise key) host tensors of a plan, or None when every row is greedy."""
+        if not self._random:
+            return None
+        temps = self.pinned.get(f"t_{tag}", rows, torch.float32) if self.is_cuda else torch.empty(rows)
+        keys = self.pinned.get(f"k_{tag}", rows, torch.int64) if self.is_cuda else torch.empty(rows, dtype=torch.int64)
+        return (temps, keys) if self.scheduler.sampling_rows(plan, temps, keys) else None
+
+    def _sample(self, logits: torch.Tensor, plan) -> torch.Tensor:
+        rows = self._sampling_rows(plan, logits.shape[0], "p")
         if self.is_cuda:
-            return ops.sample_tokens(logits, temp, p0.seed if p0 else 0, step_index)
-        if temp <= 0:
-            return logits.float().argmax(-1).to(torch.int32)
-        g = torch.Generator().manual_seed((p0.seed if p0 else 0) * 1_000_003 + step_index)
-        u = torch.rand(logits.shape, generator=g).clamp_min(1e-20)
-        return (logits.float() / temp - torch.log(-torch.log(u))).argmax(-1).to(torch.int32)
+            if rows is None:
+                return ops.sample_tokens(logits)
+            temps, keys = rows
+            self.h2d_bytes += temps.numel() * 12
+            return ops.sample_tokens(logits, row_temp=temps.to(self.device, non_blocking=True),
+                                     row_key=keys.to(self.device, non_blocking=True))
+        out = logits.float().argmax(-1).to(torch.int32)
+        if rows is not None:  # Gumbel-max per sampled row, noise seeded by the row's key
+            temps, keys = rows
+            for i in range(logits.shape[0]):
+                if temps[i] > 0:
+                    g = torch.Generator().manual_seed(int(keys[i]) & ((1 << 63) - 1))
+                    u = torch.rand(logits.shape[1], generator=g).clamp_min(1e-20)
+                    out[i] = int((logits[i].float() / float(temps[i]) - torch.log(-torch.log(u))).argmax())
+        return out
 
     def _graph(self, bucket: int) -> DecodeGraph:
         g = self.graphs.get(bucket)
@@ -208,12 +256,16 @@ class LLMEngine:
             logits_idx=self._h2d("p_lidx", plan.logits_idx),
         )
         logits = self.model.forward(fb, self.cache)
-        return self._sample(logits, plan.seq_ids, plan.step_index)
+        return self._sample(logits, plan)
 
-    def _run_decode(self, plan) -> torch.Tensor:
+    def _run_decode(self, plan, prev: _Launched | None = None) -> torch.Tensor:
         if not self.use_graphs:
             B = plan.padded_seqs
-            fb = ForwardBatch(mode="decode", token_ids=self._h2d("d_ids", plan.token_ids),
+            tok = self._h2d("d_ids", plan.token_ids)
+            if plan.flags & self.core.DECISION_SCHEDULED_AHEAD:
+                n = plan.num_seqs
+                tok[:n] = prev.out.to(tok.device)[tok[:n].long()]
+            fb = ForwardBatch(mode="decode", token_ids=tok,
                               positions=self._h2d("d_pos", plan.positions),
                               slot_mapping=self._h2d("d_slots", plan.slot_mapping),
                               block_table=self._h2d("d_bt", plan.block_table).view(B, plan.max_blocks),
@@ -221,46 +273,96 @@ class LLMEngine:
                               decode_splits=ops.mla_decode_splits(B, self.cfg.num_heads, plan.max_context)
                               if self.is_cuda else 1)
             logits = self.model.forward(fb, self.cache)
-            return self._sample(logits, plan.seq_ids, plan.step_index)
+            return self._sample(logits, plan)
         g = self._graph(plan.padded_seqs)
         B = plan.padded_seqs
-        ids = self.pinned.get("d_ids", B)
-        pos = self.pinned.get("d_pos", B)
-        slots = self.pinned.get("d_slots", B)
-        ctx = self.pinned.get("d_ctx", B)
-        bt = self.pinned.get(f"d_bt{B}", B * self.max_blocks).view(B, self.max_blocks)
+        # two sets of pinned input buffers: the set written now was last read by the
+        # step before the previous one, whose copies have completed
+        par = self._parity
+        self._parity ^= 1
+        ids = self.pinned.get(f"d_ids{par}", B)
+        pos = self.pinned.get(f"d_pos{par}", B)
+        slots = self.pinned.get(f"d_slots{par}", B)
+        ctx = self.pinned.get(f"d_ctx{par}", B)
+        bt = self.pinned.get(f"d_bt{B}_{par}", B * self.max_blocks).view(B, self.max_blocks)
         self.h2d_bytes += plan.write_decode_inputs(ids, pos, slots, ctx, bt)
         g.ids.copy_(ids, non_blocking=True)
         g.pos.copy_(pos, non_blocking=True)
         g.slots.copy_(slots, non_blocking=True)
         g.ctx.copy_(ctx, non_blocking=True)
         g.block_table.copy_(bt, non_blocking=True)
+        rows = self._sampling_rows(plan, B, f"d{par}")
+        if rows is not None or g.sampling_dirty:
+            if rows is None:
+                g.temps.zero_()
+                g.keys.zero_()
+            else:
+                g.temps.copy_(rows[0], non_blocking=True)
+                g.keys.copy_(rows[1], non_blocking=True)
+                self.h2d_bytes += B * 12
+            g.sampling_dirty = rows is not None
+        if plan.flags & self.core.DECISION_SCHEDULED_AHEAD:
+            ops.gather_prev_tokens(g.ids, prev.out, plan.num_seqs)
         return g.run()
 
-    def step(self) -> list[RequestOutput]:
-        """Runs one scheduler step on the GPU; returns the requests that changed."""
-        plan = self.scheduler.schedule()
-        if plan.kind == 0:
-            return []
+    def _launch(self, plan, prev: _Launched | None = None) -> _Launched:
         t0 = time.perf_counter()
         try:
             if plan.kind == 1:
                 sampled = self._run_prefill(plan)
             else:
-                sampled = self._run_decode(plan)
+                sampled = self._run_decode(plan, prev)
+            n = plan.num_seqs
             if self.is_cuda:
-                host = self.pinned.get("sampled", sampled.numel())
-                host.copy_(sampled, non_blocking=True)
-                torch.cuda.current_stream(self.device).synchronize()
-                self.d2h_bytes += plan.num_seqs * 4
+                host = self.pinned.get(f"sampled{self._parity}", n)
+                host.copy_(sampled[:n], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record()
+                self.d2h_bytes += n * 4
             else:
-                host = sampled.to(torch.int32)
+                host, ev = sampled[:n].to(torch.int32).contiguous(), None
         except Exception:
             self.scheduler.fail_step(plan)
             raise
+        return _Launched(plan, host, ev, sampled, t0)
+
+    def step(self) -> list[RequestOutput]:
+        """Runs one scheduler step on the GPU; returns the requests that changed."""
+        if self._inflight is not None:
+            cur, self._inflight = self._inflight, None
+        else:
+            plan = self.scheduler.schedule()
+            if plan.kind == 0:
+                return []
+            cur = self._launch(plan)
+        if self.async_decode and cur.plan.kind == 2:
+            nxt = self.scheduler.schedule_ahead(cur.plan)
+            if nxt.kind == 2:
+                try:
+                    self._inflight = self._launch(nxt, cur)
+                    self.ahead_steps += 1
+                except Exception:
+                    self.scheduler.fail_step(cur.plan)
+                    raise
+        return self._complete(cur)
+
+    def _complete(self, cur: _Launched) -> list[RequestOutput]:
+        plan = cur.plan
+        try:
+            if cur.event is not None:
+                cur.event.synchronize()
+        except Exception:
+            self.scheduler.fail_step(plan)
+            if self._inflight is not None:
+                self.scheduler.fail_step(self._inflight.plan)
+                self._inflight = None
+            raise
         now = time.perf_counter()
-        self.step_log.append(("prefill" if plan.kind == 1 else "decode", plan.num_seqs, now - t0, plan.num_tokens))
-        events = self.scheduler.complete_tensor(plan, host[:plan.num_seqs].contiguous())
+        # with overlapped steps a step's time is the interval since the previous step ended
+        dt = now - max(cur.t0, self._last_done)
+        self._last_done = now
+        self.step_log.append(("prefill" if plan.kind == 1 else "decode", plan.num_seqs, dt, plan.num_tokens))
+        events = self.scheduler.complete_tensor(plan, cur.host)
         changed = {}
         for ev in events:
             out = self.outputs.get(ev.id)
@@ -276,6 +378,7 @@ class LLMEngine:
                 out.finish_reason = FINISH_REASONS.get(int(ev.reason), "unknown")
                 out.finish_time = now
                 changed[ev.id] = out
+                self._random.discard(ev.id)
         return list(changed.values())
 
     # ------------------------------------------------------------------ batch API
@@ -286,7 +389,7 @@ class LLMEngine:
         h2d0, d2h0 = self.h2d_bytes, self.d2h_bytes
         log0 = len(self.step_log)
         t0 = time.perf_counter()
-        while self.scheduler.has_work():
+        while self.has_unfinished_requests():
             self.step()
         wall = time.perf_counter() - t0
         outs = [self.outputs.pop(i) for i in ids]
@@ -320,6 +423,9 @@ class LLMEngine:
         return GenerateResult(outs, stats)
 
     def shutdown(self):
+        if self._inflight is not None:  # drain a step planned ahead
+            cur, self._inflight = self._inflight, None
+            self._complete(cur)
         for g in self.graphs.values():
             g.release()
         self.graphs.clear()

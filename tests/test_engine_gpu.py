@@ -1,0 +1,59 @@
+"""The serving engine on the GPU: CUDA-graph decode with steps scheduled ahead of
+the previous step's tokens against the synchronous loop, and per-request sampling."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg():
+    from sparkpipe_rs_b200.models.config import v2_lite
+
+    return v2_lite().replace(name="small-mla-moe", num_layers=3, hidden_size=1024, n_routed_experts=16,
+                             num_experts_per_tok=4, moe_intermediate_size=256, intermediate_size=2048,
+                             n_shared_experts=1, vocab_size=4096, first_k_dense_replace=1, init_std=0.05)
+
+
+def _engine(model, cfg, **kw):
+    from sparkpipe_rs_b200.serving.engine import EngineConfig, LLMEngine
+
+    ec = EngineConfig(max_batch=8, block_size=64, max_model_len=512, max_prefill_tokens=256,
+                      decode_buckets=(1, 2, 4, 8), **kw)
+    return LLMEngine(cfg, ec, model=model, device="cuda")
+
+
+def _run(eng, prompts, params):
+    ids = [eng.add_request(p, sp) for p, sp in zip(prompts, params)]
+    got = {}
+    while eng.has_unfinished_requests():
+        for o in eng.step():
+            if o.finished:
+                got[o.request_id] = (list(o.token_ids), o.finish_reason)
+    return [got[i] for i in ids]
+
+
+def test_ahead_decode_matches_synchronous_graph_loop():
+    from sparkpipe_rs_b200.models.mla_moe import MLAMoEModel
+    from sparkpipe_rs_b200.serving.engine import SamplingParams
+
+    cfg = _cfg()
+    model = MLAMoEModel(cfg, seed=0, device="cuda", max_positions=1024)
+    sync = _engine(model, cfg, async_decode=False)
+    ahead = _engine(model, cfg, async_decode=True)
+    assert sorted(sync.graphs) == [1, 2, 4, 8]  # captured when the engine starts
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (40, 65, 17, 90, 33, 128, 9)]
+    probe = _run(sync, prompts[:1], [SamplingParams(max_tokens=12, ignore_eos=True)])[0][0]
+    stop = probe[5]
+    params = [SamplingParams(max_tokens=24, stop_token_ids=(stop,))]
+    params += [SamplingParams(max_tokens=n, ignore_eos=True) for n in (20, 7, 31, 3)]
+    params += [SamplingParams(max_tokens=16, temperature=0.8, seed=s, ignore_eos=True) for s in (1, 2)]
+    a = _run(sync, prompts, params)
+    b = _run(ahead, prompts, params)
+    assert ahead.ahead_steps > 0 and sync.ahead_steps == 0
+    assert a == b
+    assert b[0][1] == "stop" and b[0][0][-1] == stop and len(b[0][0]) == 6
+    assert [len(t) for t, _ in b[1:5]] == [20, 7, 31, 3]
+    assert b[5][0] != b[6][0]  # two seeds, two samples
+    for e in (sync, ahead):
+        e.shutdown()
