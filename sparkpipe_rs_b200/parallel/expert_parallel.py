@@ -87,6 +87,7 @@ class ExpertParallel:
         assert 1 <= world <= 8
         cap_tokens = -(-cap_tokens // CHUNK_TOKENS) * CHUNK_TOKENS
         self.cfg, self.rank, self.world, self.cap = cfg, rank, world, cap_tokens
+        self.group = group  # None: ranks emulated in one process
         self.device = torch.device(device)
         self.budget = int(budget_cycles)
         self.kk = cfg.num_experts_per_tok + cfg.n_shared_experts

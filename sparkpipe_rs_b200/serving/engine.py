@@ -11,6 +11,13 @@ One engine owns one model replica on one GPU. Each ``step()``:
   4. reads the sampled tokens back (device->host) and hands them to the
      scheduler, which advances every request and reports token / finish events.
 
+Expert-parallel ranks (attention data-parallel, experts split over the GPUs)
+each run their own engine, but every forward is a collective over the group. The
+engines therefore step in lockstep: each step the ranks agree on the host (a gloo
+all-reduce of two flags) whether any of them launches a forward, and a rank
+without work of its own launches an idle forward (one row that reads no context
+and writes no KV) so the others' dispatch and combine find it.
+
 Decode steps overlap the host with the GPU: while step n runs, the scheduler
 plans step n+1 ahead of n's tokens (``Scheduler.schedule_ahead``), its inputs are
 copied, and its graph is launched with the token ids gathered on the device from
@@ -108,11 +115,32 @@ class _Pinned:
         return t[:n]
 
 
+class _Lockstep:
+    """Host-side agreement of the ranks of one expert-parallel group: per step, does
+    any rank launch a forward, and does any rank still have work."""
+
+    def __init__(self, ep_group):
+        import torch.distributed as dist
+
+        self.dist = dist
+        ranks = dist.get_process_group_ranks(ep_group) if ep_group is not dist.group.WORLD else \
+            list(range(dist.get_world_size()))
+        self.group = dist.new_group(ranks=ranks, backend="gloo")
+        self.buf = torch.zeros(2, dtype=torch.int32)
+
+    def agree(self, has_plan: bool, busy: bool) -> tuple[bool, bool]:
+        self.buf[0] = int(has_plan)
+        self.buf[1] = int(busy)
+        self.dist.all_reduce(self.buf, op=self.dist.ReduceOp.MAX, group=self.group)
+        return bool(self.buf[0]), bool(self.buf[1])
+
+
 @dataclass
 class _Launched:
-    """A step whose GPU work is enqueued: its sampled tokens land in ``host``."""
+    """A step whose GPU work is enqueued: its sampled tokens land in ``host``
+    (``plan`` None: an idle forward of a lockstep rank)."""
     plan: object
-    host: torch.Tensor
+    host: torch.Tensor | None
     event: object          # CUDA event after the device->host copy (None on CPU)
     out: torch.Tensor      # device tensor of the sampled tokens
     t0: float
@@ -164,10 +192,16 @@ class LLMEngine:
         self.async_decode = e.async_decode and (self.use_graphs or not self.is_cuda)
         self._inflight: _Launched | None = None
         self.ahead_steps = 0  # decode steps launched ahead of the previous step's tokens
+        self.idle_steps = 0   # idle forwards of a lockstep rank
+        ep = getattr(self.model, "ep", None)
+        self._lockstep = _Lockstep(ep.group) if ep is not None and getattr(ep, "group", None) is not None \
+            and ep.world > 1 else None
+        self._more = True     # lockstep: some rank of the group still has work
         self._parity = 0
         self._last_done = 0.0
         self._random: set[int] = set()  # live requests that sample (temperature > 0)
-        if self.use_graphs and e.capture_graphs_at_start:
+        # lockstep ranks capture every bucket up front: a capture's warm-up forward is a collective
+        if self.use_graphs and (e.capture_graphs_at_start or self._lockstep is not None):
             for b in sc.decode_buckets:
                 self._graph(b)
         self.step_log: list[tuple[str, int, float]] = []  # (kind, seqs, seconds)
@@ -196,8 +230,16 @@ class LLMEngine:
             out.finish_time = time.perf_counter()
         return ok
 
+    @property
+    def lockstep(self) -> bool:
+        """This engine is one rank of an expert-parallel group and must step with it."""
+        return self._lockstep is not None
+
     def has_unfinished_requests(self) -> bool:
-        return self.scheduler.has_work() or self._inflight is not None
+        """This engine still has work; for a lockstep rank, some rank of the group has
+        (as agreed at the last step), so the caller keeps stepping."""
+        local = self.scheduler.has_work() or self._inflight is not None
+        return local or (self._lockstep is not None and self._more)
 
     # ------------------------------------------------------------------ GPU steps
     def _h2d(self, name: str, arr) -> torch.Tensor:
@@ -326,37 +368,90 @@ class LLMEngine:
             raise
         return _Launched(plan, host, ev, sampled, t0)
 
-    def step(self) -> list[RequestOutput]:
-        """Runs one scheduler step on the GPU; returns the requests that changed."""
-        if self._inflight is not None:
-            cur, self._inflight = self._inflight, None
+    def _launch_idle(self) -> _Launched:
+        """A forward that serves no sequence (one row, no context, no KV write), so
+        this rank joins a collective step in which only other ranks have work."""
+        t0 = time.perf_counter()
+        if self.use_graphs:
+            g = self._graph(self.scheduler.bucket_for(1))
+            g.ids.zero_()
+            g.pos.zero_()
+            g.ctx.zero_()
+            g.slots.fill_(-1)
+            out = g.run()
+        elif hasattr(self.model, "idle_forward"):
+            out = self.model.idle_forward(self.cache)
         else:
-            plan = self.scheduler.schedule()
-            if plan.kind == 0:
-                return []
-            cur = self._launch(plan)
-        if self.async_decode and cur.plan.kind == 2:
-            nxt = self.scheduler.schedule_ahead(cur.plan)
-            if nxt.kind == 2:
-                try:
-                    self._inflight = self._launch(nxt, cur)
-                    self.ahead_steps += 1
-                except Exception:
-                    self.scheduler.fail_step(cur.plan)
-                    raise
-        return self._complete(cur)
+            z = torch.zeros(1, dtype=torch.int32, device=self.device)
+            fb = ForwardBatch(mode="decode", token_ids=z, positions=z.clone(), slot_mapping=z - 1,
+                              block_table=torch.zeros(1, self.max_blocks, dtype=torch.int32, device=self.device),
+                              context_lens=z.clone(), decode_splits=1)
+            out = self.model.forward(fb, self.cache)
+        ev = None
+        if self.is_cuda:
+            ev = torch.cuda.Event()
+            ev.record()
+        self.idle_steps += 1
+        return _Launched(None, None, ev, out, t0)
 
-    def _complete(self, cur: _Launched) -> list[RequestOutput]:
+    def step(self) -> list[RequestOutput]:
+        """One engine step: launches at most one GPU step and completes the step
+        before it; returns the requests that changed."""
+        changed: dict[int, RequestOutput] = {}
+        cur, self._inflight = self._inflight, None
+        plan = None
+        if cur is not None and cur.plan is not None and self.async_decode and cur.plan.kind == 2:
+            a = self.scheduler.schedule_ahead(cur.plan)
+            if a.kind == 2:
+                plan = a
+        if plan is None:
+            if cur is not None:
+                changed.update(self._complete(cur))
+                cur = None
+            p = self.scheduler.schedule()
+            plan = p if p.kind != 0 else None
+        idle = False
+        if self._lockstep is not None:
+            busy = plan is not None or cur is not None or self.scheduler.has_work()
+            any_plan, self._more = self._lockstep.agree(plan is not None, busy)
+            idle = plan is None and any_plan
+        launched = None
+        try:
+            if plan is not None:
+                launched = self._launch(plan, cur)
+                if plan.flags & self.core.DECISION_SCHEDULED_AHEAD:
+                    self.ahead_steps += 1
+            elif idle:
+                launched = self._launch_idle()
+        except Exception:
+            if cur is not None:
+                self.scheduler.fail_step(cur.plan)
+            raise
+        try:
+            if cur is not None:
+                changed.update(self._complete(cur))
+        except Exception:
+            if launched is not None and launched.plan is not None:
+                self.scheduler.fail_step(launched.plan)
+            raise
+        if launched is not None:
+            if self.async_decode and (launched.plan is None or launched.plan.kind == 2):
+                self._inflight = launched  # completed by the next step, after it launches its successor
+            else:
+                changed.update(self._complete(launched))
+        return list(changed.values())
+
+    def _complete(self, cur: _Launched) -> dict[int, RequestOutput]:
         plan = cur.plan
         try:
             if cur.event is not None:
                 cur.event.synchronize()
         except Exception:
-            self.scheduler.fail_step(plan)
-            if self._inflight is not None:
-                self.scheduler.fail_step(self._inflight.plan)
-                self._inflight = None
+            if plan is not None:
+                self.scheduler.fail_step(plan)
             raise
+        if plan is None:  # idle forward
+            return {}
         now = time.perf_counter()
         # with overlapped steps a step's time is the interval since the previous step ended
         dt = now - max(cur.t0, self._last_done)
@@ -379,7 +474,7 @@ class LLMEngine:
                 out.finish_time = now
                 changed[ev.id] = out
                 self._random.discard(ev.id)
-        return list(changed.values())
+        return changed
 
     # ------------------------------------------------------------------ batch API
     def generate(self, prompts, params: SamplingParams | None = None) -> GenerateResult:
@@ -389,8 +484,15 @@ class LLMEngine:
         h2d0, d2h0 = self.h2d_bytes, self.d2h_bytes
         log0 = len(self.step_log)
         t0 = time.perf_counter()
-        while self.has_unfinished_requests():
-            self.step()
+        if self._lockstep is not None:
+            # every rank of the group calls generate; all leave at the same agreed step
+            while True:
+                self.step()
+                if not self._more:
+                    break
+        else:
+            while self.has_unfinished_requests():
+                self.step()
         wall = time.perf_counter() - t0
         outs = [self.outputs.pop(i) for i in ids]
         for i in ids:

@@ -115,7 +115,8 @@ class ServingServer:
                     self._submit(w)
                 else:
                     events += self._cancel(w.handle)
-            if eng.has_unfinished_requests():
+            # a lockstep (expert-parallel) rank steps every turn: its peers may have work
+            if eng.lockstep or eng.has_unfinished_requests():
                 try:
                     outs = eng.step()
                 except Exception as exc:  # fail every live request, keep serving

@@ -287,3 +287,57 @@ def test_two_gpu_expert_parallel_model_matches_single_gpu():
         p.join(timeout=120)
     for rank, ok, diff, status in sorted(results, key=lambda r: r[0]):
         assert ok and status == 0, (rank, diff, status)
+
+
+def _lockstep_engine_worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    from sparkpipe_rs_b200.models.mla_moe import MLAMoEModel
+    from sparkpipe_rs_b200.serving.engine import EngineConfig, LLMEngine, SamplingParams
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        cfg = _model_cfg()
+        ep = ExpertParallel(cfg, rank, world, cap_tokens=128, device=dev, group=dist.group.WORLD)
+        ec = dict(max_batch=4, block_size=64, max_model_len=256, max_prefill_tokens=128, decode_buckets=(1, 2, 4))
+        eng = LLMEngine(cfg, EngineConfig(**ec), model=MLAMoEModel(cfg, seed=5, device=dev, ep=ep), device=dev)
+        ref = LLMEngine(cfg, EngineConfig(**ec), model=MLAMoEModel(cfg, seed=5, device=dev), device=dev)
+        g = torch.Generator().manual_seed(20 + rank)
+        # rank 0: three requests; rank 1: one short one, so it idles while rank 0 decodes
+        reqs = [(40, 12), (70, 20), (9, 5)] if rank == 0 else [(30, 3)]
+        prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n, _ in reqs]
+        ids = [eng.add_request(p, SamplingParams(max_tokens=k, ignore_eos=True)) for p, (_, k) in zip(prompts, reqs)]
+        eng.generate([], SamplingParams())
+        got = [eng.outputs.pop(i).token_ids for i in ids]
+        want = [ref.generate([p], SamplingParams(max_tokens=k, ignore_eos=True)).outputs[0].token_ids
+                for p, (_, k) in zip(prompts, reqs)]
+        q.put((rank, got == want, eng.idle_steps, ops.status_word()))
+        eng.shutdown()
+        ref.shutdown()
+        dist.barrier()
+        ep.close()
+        dist.destroy_process_group()
+    except Exception as e:  # report, never hang the parent
+        q.put((rank, False, repr(e), -1))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_engines_step_in_lockstep():
+    """Expert-parallel engines with uneven work: the rank that runs out of requests
+    keeps joining the other's steps with idle forwards; both ranks' tokens equal a
+    single-GPU engine's."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_lockstep_engine_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = sorted([q.get(timeout=600) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+    for rank, ok, idle, status in results:
+        assert ok and status == 0, (rank, idle, status)
+    assert results[1][2] > 0 and results[0][2] == 0
