@@ -155,6 +155,8 @@ class LLMEngine:
         self.ecfg = ecfg or EngineConfig()
         self.device = torch.device(device)
         self.is_cuda = self.device.type == "cuda"
+        if self.is_cuda and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         if self.is_cuda:
             torch.cuda.set_device(self.device)
         self.core = _ext.core()
