@@ -74,6 +74,20 @@ SP_DEVI bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of phase `parity` (try_wait may suspend the thread for a
+// while; a thread that polls several barriers in turn must not).
+SP_DEVI bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on phase `parity`. `cta_err` is a shared-memory error word of the
 // CTA: the wait gives up early once any role has set it, and sets it (plus the
 // global status word `gerr`) with `code` when the time budget runs out.
@@ -91,6 +105,15 @@ SP_DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* cta_err, in
       return false;
     }
   }
+}
+
+// Bounded wait that ignores the CTA error word: drains copies and MMAs still in
+// flight before a CTA that gave up releases its shared and tensor memory.
+SP_DEVI bool mbar_drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > kWaitBudgetCycles) return false;
+  return true;
 }
 
 // ---------------------------------------------------------------- TMA

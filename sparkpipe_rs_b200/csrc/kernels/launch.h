@@ -173,12 +173,15 @@ struct MlaDecodeLaunch {
   int splits = 1;
   float scale = 1.f;
   int* err = nullptr;
+  int impl = 0;                   // MLA_IMPL_*
+  unsigned long long* trace = nullptr;  // tcgen05 kernel: [6][64] event times of CTA (0,0,0)
   cudaStream_t stream = 0;
 };
-// KV tokens per pipeline stage of the decode kernel (32, or 64 when SPARKPIPE_MLA_STAGE_TOKENS=64)
-// and how many decode CTAs of a head count fit on one SM.
+enum { MLA_IMPL_AUTO = 0, MLA_IMPL_TC = 1, MLA_IMPL_MMA = 2 };
+// KV tokens per pipeline stage of the mma.sync decode kernel (64, or 32 when
+// SPARKPIPE_MLA_STAGE_TOKENS=32) and how many decode CTAs of a head count fit on one SM.
 int mla_stage_tokens();
-int mla_ctas_per_sm(int heads);
+int mla_ctas_per_sm(int heads, int impl = MLA_IMPL_AUTO);
 void mla_decode(const MlaDecodeLaunch& l);
 
 // ---- prefill attention (prefill_attn.cu)

@@ -380,7 +380,7 @@ void quant_weight_fp8(const c10::optional<Tensor>& src, int64_t seed, int64_t fl
 
 void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table, const Tensor& context_lens,
                 const Tensor& out, const c10::optional<Tensor>& o_part, const c10::optional<Tensor>& lse_part,
-                int64_t splits, double scale) {
+                int64_t splits, double scale, int64_t impl, const c10::optional<Tensor>& trace) {
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(cache); CHECK_I32(block_table); CHECK_I32(context_lens); CHECK_BF16(out);
   CHECK_CONTIG(q); CHECK_CONTIG(block_table); CHECK_CONTIG(out);
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 576, "q: [B, H, 576]");
@@ -394,11 +394,28 @@ void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table,
   l.max_blocks = (int)block_table.size(1);
   l.context_lens = context_lens.data_ptr<int>();
   l.out = out.data_ptr();
-  if (o_part.has_value()) { CHECK_F32(*o_part); l.o_part = o_part->data_ptr<float>(); }
-  if (lse_part.has_value()) { CHECK_F32(*lse_part); l.lse_part = lse_part->data_ptr<float>(); }
-  l.B = (int)q.size(0);
-  l.H = (int)q.size(1);
+  const int64_t B = q.size(0), H = q.size(1);
+  TORCH_CHECK(block_table.size(0) >= B && context_lens.numel() >= B, "mla_decode: block table / lengths too short");
+  TORCH_CHECK(out.numel() >= B * H * 512, "mla_decode: output too small");
+  if (o_part.has_value()) {
+    CHECK_F32(*o_part);
+    TORCH_CHECK(o_part->numel() >= B * splits * H * 512, "mla_decode: split partials too small");
+    l.o_part = o_part->data_ptr<float>();
+  }
+  if (lse_part.has_value()) {
+    CHECK_F32(*lse_part);
+    TORCH_CHECK(lse_part->numel() >= B * splits * H, "mla_decode: split log-sum-exps too small");
+    l.lse_part = lse_part->data_ptr<float>();
+  }
+  l.B = (int)B;
+  l.H = (int)H;
   l.splits = (int)splits;
+  l.impl = (int)impl;
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == torch::kInt64 && trace->numel() >= 6 * 64,
+                "mla_decode: trace must be an int64 CUDA tensor of 384 entries");
+    l.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
   l.scale = (float)scale;
   l.err = err_word();
   l.stream = stream();
@@ -801,7 +818,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_word", &status_word);
   m.def("clear_status", &clear_status);
   m.def("num_sms", &num_sms);
-  m.def("mla_ctas_per_sm", [](int64_t heads) { return sp::mla_ctas_per_sm((int)heads); });
+  m.def("mla_ctas_per_sm", [](int64_t heads, int64_t impl) { return sp::mla_ctas_per_sm((int)heads, (int)impl); },
+        py::arg("heads"), py::arg("impl") = 0);
   m.def("mla_stage_tokens", []() { return sp::mla_stage_tokens(); });
   m.def("ep_alloc", &ep_alloc);
   m.def("ep_ipc_handle", &ep_ipc_handle);

@@ -338,13 +338,16 @@ def grouped_gemm_fp8(w: Fp8Weight, x_sorted: Fp8Act, out: torch.Tensor, grp_rows
     return out
 
 
-def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 148) -> int:
+MLA_IMPL = {"auto": 0, "tc": 1, "mma": 2}  # MLA decode kernels: default, tcgen05, mma.sync
+
+
+def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 148, impl: str = "auto") -> int:
     """Split-KV factor: the most CTAs that still fit one wave on the SMs, without
     splits of under two blocks (a second partial wave costs more than it hides:
     B=64, 16 heads, ctx 1024 measured 27 us at 2 splits, 34 us at 3)."""
     groups = heads // (32 if heads % 32 == 0 else 16)
     ctas = max(1, batch * groups)
-    slots = num_sms * int(kernels().mla_ctas_per_sm(heads))  # CTAs resident at once
+    slots = num_sms * int(kernels().mla_ctas_per_sm(heads, MLA_IMPL[impl]))  # CTAs resident at once
     want = max(1, slots // ctas)
     blocks = max(1, math.ceil(max_context / 64))
     # few long sequences need many splits to use the SMs (one 131K-token sequence:
@@ -353,12 +356,20 @@ def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 1
     return int(max(1, min(want, blocks // 2 if blocks >= 2 else 1, cap)))
 
 
-def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=None, lse_part=None):
+def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=None, lse_part=None, impl="auto",
+               trace=None):
+    """Absorbed-MLA paged decode attention. ``impl``: "mma" (mma.sync kernel, the
+    default), "tc" (tcgen05 tensor cores) or "auto" (the default one, which the
+    SPARKPIPE_MLA_KERNEL environment variable can switch). ``trace``: an int64
+    CUDA tensor of 6 x 64 entries that receives the tcgen05 kernel's pipeline event
+    times (global timer, ns) of its first CTA: TMA issue, S^T issue, S^T seen by the
+    softmax, P^T ready, O^T issue per tile; start and end."""
     B, H, _ = q.shape
     if splits > 1 and o_part is None:
         o_part = torch.empty(B, splits, H, 512, dtype=torch.float32, device=q.device)
         lse_part = torch.empty(B, splits, H, dtype=torch.float32, device=q.device)
-    kernels().mla_decode(q, cache, block_table, context_lens, out, o_part, lse_part, splits, float(scale))
+    kernels().mla_decode(q, cache, block_table, context_lens, out, o_part, lse_part, splits, float(scale),
+                         MLA_IMPL[impl], trace)
     _count(1 + (1 if splits > 1 else 0))
     return out
 

@@ -24,6 +24,7 @@ def main():
     ap.add_argument("--ctx", type=int, default=1024)
     ap.add_argument("--splits", default="0,1,2,3,4,5,6,8")
     ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--impl", default="tc,mma", help="kernels to time: tc (tcgen05), mma (mma.sync)")
     args = ap.parse_args()
     from sparkpipe_rs_b200 import ops
 
@@ -39,14 +40,15 @@ def main():
     out = torch.empty(B, H, 512, device=dev, dtype=torch.bfloat16)
     nbytes = B * L * 576 * 2
     scale = 1 / math.sqrt(192)
-    for sp in [int(s) for s in args.splits.split(",")]:
-        splits = sp or ops.mla_decode_splits(B, H, L, ops.kernels().num_sms())
-        o_part = torch.empty(B, splits, H, 512, device=dev, dtype=torch.float32)
-        lse = torch.empty(B, splits, H, device=dev, dtype=torch.float32)
-        us = time_fn(lambda i: ops.mla_decode(q, caches[i % n_caches], bt, ctx, out, splits, scale, o_part, lse),
-                     args.iters)
-        print(f"mla_decode B={B} H={H} ctx={L} splits={splits}{' (auto)' if sp == 0 else ''}: {us:8.2f} us  "
-              f"{nbytes / us / 1e6:6.2f} TB/s of KV")
+    for impl in args.impl.split(","):
+        for sp in [int(s) for s in args.splits.split(",")]:
+            splits = sp or ops.mla_decode_splits(B, H, L, ops.kernels().num_sms(), impl=impl)
+            o_part = torch.empty(B, splits, H, 512, device=dev, dtype=torch.float32)
+            lse = torch.empty(B, splits, H, device=dev, dtype=torch.float32)
+            us = time_fn(lambda i: ops.mla_decode(q, caches[i % n_caches], bt, ctx, out, splits, scale, o_part, lse,
+                                                  impl=impl), args.iters)
+            print(f"mla_decode[{impl}] B={B} H={H} ctx={L} splits={splits}{' (auto)' if sp == 0 else ''}: "
+                  f"{us:8.2f} us  {nbytes / us / 1e6:6.2f} TB/s of KV")
 
 
 if __name__ == "__main__":

@@ -213,6 +213,9 @@ def _mla_ref(q, cache, bt, ctx, scale):
     out = torch.empty(B, H, 512, device=q.device)
     for b in range(B):
         L = int(ctx[b])
+        if L == 0:  # an idle row reads nothing and yields zeros
+            out[b] = 0
+            continue
         blocks = bt[b, : (L + 63) // 64].long()
         rows = (blocks[:, None] * 64 + torch.arange(64, device=q.device)).flatten()[:L]
         kv = cache[rows].float()
@@ -221,18 +224,19 @@ def _mla_ref(q, cache, bt, ctx, scale):
     return out
 
 
+@pytest.mark.parametrize("impl", ["tc", "mma"])
 @pytest.mark.parametrize("H,splits", [(16, 1), (16, 3), (32, 2), (64, 1), (128, 4)])
-def test_mla_decode(H, splits):
+def test_mla_decode(H, splits, impl):
     ops = _ops()
     g = torch.Generator(device=DEV).manual_seed(H + splits)
-    B, nblocks, maxb = 6, 64, 10
+    B, nblocks, maxb = 7, 64, 10
     cache = torch.randn(nblocks * 64, 576, device=DEV, generator=g).bfloat16()
-    ctx = torch.tensor([1, 63, 64, 65, 300, 640][:B], device=DEV, dtype=torch.int32)
+    ctx = torch.tensor([1, 63, 64, 65, 300, 640, 0][:B], device=DEV, dtype=torch.int32)
     bt = torch.stack([torch.randperm(nblocks, device=DEV, generator=g)[:maxb] for _ in range(B)]).int()
     q = torch.randn(B, H, 576, device=DEV, generator=g).bfloat16()
     out = torch.empty(B, H, 512, device=DEV, dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(192)
-    ops.mla_decode(q, cache, bt, ctx, out, splits, scale)
+    ops.mla_decode(q, cache, bt, ctx, out, splits, scale, impl=impl)
     _close(out, _mla_ref(q, cache, bt, ctx, scale), atol=2e-2, rtol=2e-2)
     _status_ok()
 
