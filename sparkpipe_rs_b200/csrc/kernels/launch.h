@@ -196,9 +196,15 @@ struct PrefillAttnLaunch {
   int dn = 128, dr = 64, dv = 128;
   float scale = 1.f;
   int causal = 1;
+  long long q_rows = 0, k_rows = 0;  // rows of the q / k (kpe, v) tensors (TMA extents)
+  int impl = 0;                       // ATTN_IMPL_*
+  int* err = nullptr;
   cudaStream_t stream = 0;
 };
+enum { ATTN_IMPL_AUTO = 0, ATTN_IMPL_TC = 1, ATTN_IMPL_MMA = 2 };
 void prefill_attention(const PrefillAttnLaunch& l);
+bool prefill_attention_tc_ok(const PrefillAttnLaunch& l);
+void prefill_attention_tc(const PrefillAttnLaunch& l);
 
 // ---- MoE routing (moe.cu)
 // scoring: 0 = softmax, 1 = sigmoid (+bias for selection). Weights are renormalised

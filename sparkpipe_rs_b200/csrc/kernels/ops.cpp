@@ -423,7 +423,8 @@ void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table,
 }
 
 void prefill_attention(const Tensor& q, const Tensor& k, const Tensor& kpe, const Tensor& v, const Tensor& o,
-                       const Tensor& cu_q, const Tensor& cu_k, int64_t max_q, double scale, bool causal) {
+                       const Tensor& cu_q, const Tensor& cu_k, int64_t max_q, double scale, bool causal,
+                       int64_t impl) {
   // q [Tq, H, 192], k [Tk, H, >=128] (nope part at offset 0), kpe [Tk, 64], v [Tk, H, 128], o [Tq, H, 128]
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(kpe); CHECK_BF16(v); CHECK_BF16(o);
   CHECK_I32(cu_q); CHECK_I32(cu_k);
@@ -443,6 +444,12 @@ void prefill_attention(const Tensor& q, const Tensor& k, const Tensor& kpe, cons
   l.max_q = (int)max_q;
   l.scale = (float)scale;
   l.causal = causal ? 1 : 0;
+  l.q_rows = q.size(0);
+  l.k_rows = k.size(0);
+  TORCH_CHECK(kpe.size(0) == k.size(0) && v.size(0) == k.size(0), "prefill: k / kpe / v rows differ");
+  TORCH_CHECK(cu_q.numel() == cu_k.numel(), "prefill: cu_q / cu_k lengths differ");
+  l.impl = (int)impl;
+  l.err = err_word();
   l.stream = stream();
   sp::prefill_attention(l);
 }

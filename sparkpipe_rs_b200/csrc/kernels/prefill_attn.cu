@@ -15,6 +15,7 @@
 // crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_resident_decode_stage.h:736-779.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -208,10 +209,25 @@ __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(const PrefillAttnL
   }
 }
 
+// Default: the tcgen05 kernel (prefill_attn_tc.cu) when the tensors suit TMA;
+// SPARKPIPE_ATTN_KERNEL=mma selects this mma.sync kernel.
+static int attn_default_impl() {
+  static const int t = [] {
+    const char* e = std::getenv("SPARKPIPE_ATTN_KERNEL");
+    return (e && std::string(e) == "mma") ? ATTN_IMPL_MMA : ATTN_IMPL_TC;
+  }();
+  return t;
+}
+
 void prefill_attention(const PrefillAttnLaunch& l) {
   if (l.B <= 0 || l.max_q <= 0) return;
   if (l.dn != DN || l.dr != DR || l.dv != DV)
     throw std::runtime_error("prefill_attention: supports dn 128, dr 64, dv 128");
+  const int impl = l.impl == ATTN_IMPL_AUTO ? attn_default_impl() : l.impl;
+  if (impl == ATTN_IMPL_TC && prefill_attention_tc_ok(l)) {
+    prefill_attention_tc(l);
+    return;
+  }
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);

@@ -1,0 +1,367 @@
+// Chunked / paged MLA prefill attention on the 5th-generation tensor cores
+// (tcgen05), sm_100a. Same contract as prefill_attn.cu (expanded form: per-head
+// q_nope/k_nope 128, shared rope key 64, v 128; variable-length batches; query i
+// of a chunk of Lq against Lk keys sees keys j <= Lk - Lq + i).
+//
+// One CTA = 128 queries of one head. Per 64-key tile:
+//
+//   S[128 q, 64 k]  = Q[128, 192] . K_tile[64, 192]^T    (12 x tcgen05.mma M=128 N=64 K=16)
+//   O[128 q, 128 d] += P[128, 64] . V_tile[64, 128]       ( 4 x tcgen05.mma M=128 N=128 K=16)
+//
+// S and O accumulate in tensor memory (two S buffers of 64 columns, O 128
+// columns). Q (three 64-dim boxes) is loaded once by TMA; K (two nope boxes + the
+// rope box) and V (two boxes) of a tile form one 40 KB stage of a three-stage TMA
+// ring. V is the B operand of the second product read MN-major (keys are its K).
+//
+// The TMEM data-path lane of a query row is its thread in the 4 softmax warps, so
+// the online softmax needs no cross-thread reduction: each thread reads its row of
+// S, masks, takes the row max, exponentiates, keeps its own running sum and writes
+// its row of P (bf16, 128-byte swizzled, K-major: the A operand of the second
+// product). The running max is lazy: P is taken against the current max unless the
+// row's tile max exceeds it by more than 2^8; only then (warp-uniformly) is the
+// row's O rescaled in TMEM, after the previous tile's second product finished.
+//
+// Warp roles (192 threads): warps 0-3 softmax / epilogue, warp 4 TMA producer,
+// warp 5 tensor-core issue (one thread, never blocking on one product while the
+// other could go) and TMEM allocation. Barriers that one side may pass twice before
+// the other looks are kept per tile parity. Every wait is bounded; on a timeout the
+// CTA records the error, drains its copies and MMAs and returns.
+//
+// Reference: PagedPrefillPlan / BulkPrefillPlan in
+// crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_resident_decode_stage.h:736-779.
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+
+#include "common.cuh"
+#include "launch.h"
+#include "mma_sync.cuh"
+#include "pdl.h"
+
+namespace sp {
+
+using bf16 = __nv_bfloat16;
+
+namespace fatc {
+constexpr int BM = 128;                  // queries per CTA
+constexpr int BN = 64;                   // keys per tile
+constexpr int QBOX = BM * 128;           // 128 rows x 64 dims bf16
+constexpr int KBOX = BN * 128;           // 64 keys x 64 dims bf16
+constexpr int STAGES = 3;
+constexpr int STAGE = 5 * KBOX;          // K nope (2) + K rope (1) + V (2)
+constexpr int OFF_Q = 0;
+constexpr int OFF_KV = 3 * QBOX;
+constexpr int OFF_P = OFF_KV + STAGES * STAGE;
+constexpr int PBYTES = BM * 128;         // P: 128 rows x 64 keys bf16
+constexpr int OFF_BAR = OFF_P + 2 * PBYTES;
+constexpr int NBAR = 16;
+constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+constexpr int S_COL = 0;                 // two S buffers of 64 columns
+constexpr int O_COL = 128;               // O: 128 columns
+constexpr int TMEM_COLS = 256;
+constexpr int THREADS = 192;
+constexpr float RESCALE_LOG2 = 8.f;
+}  // namespace fatc
+
+struct FaTcParams {
+  const int* cu_q;
+  const int* cu_k;
+  bf16* o;
+  long long o_tok, o_head;
+  int H, causal;
+  int q_x0, k_x0, v_x0;          // x coordinate of head 0 in the q / k / v tensor maps
+  int q_xh, k_xh, v_xh;          // x stride per head (elements)
+  float scale_log2;
+  int* err;
+};
+
+__global__ void __launch_bounds__(fatc::THREADS, 1)
+    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmKpe, const __grid_constant__ CUtensorMap tmV,
+                           const FaTcParams p) {
+  using namespace fatc;
+  griddep_wait();
+  griddep_launch();
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int q_begin = p.cu_q[b], q_len = p.cu_q[b + 1] - q_begin;
+  const int k_begin = p.cu_k[b], k_len = p.cu_k[b + 1] - k_begin;
+  const int q0 = blockIdx.x * BM;
+  if (q0 >= q_len) return;  // uniform over the CTA
+  const int diag = k_len - q_len;  // query i sees keys <= diag + i
+  const int kend = p.causal ? min(k_len, diag + min(q0 + BM, q_len)) : k_len;
+  const int nkt = kend > 0 ? (kend + BN - 1) / BN : 0;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sQ = smem_u32(smem + OFF_Q);
+  const uint32_t sKV = smem_u32(smem + OFF_KV);
+  const uint32_t sP = smem_u32(smem + OFF_P);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* full = bars;        // [3] stage landed
+  uint64_t* empty = bars + 3;   // [3] second product of the stage's tile done
+  uint64_t* sdone = bars + 6;   // [2] S ready, by tile parity
+  uint64_t* odone = bars + 8;   // [2] O product of a tile done, by tile parity
+  uint64_t* pready = bars + 10; // [2] P written (and O rescaled), by tile parity
+  uint64_t* qbar = bars + 12;
+  uint64_t* fin = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBAR);
+  volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 14; ++i) mbar_init(&bars[i], (i >= 10 && i < 12) ? 128 : 1);
+    *s_err = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc<TMEM_COLS>(tmem_slot);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0 && nkt > 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmKpe);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(qbar, 3 * QBOX);
+      for (int c = 0; c < 3; ++c)
+        tma_load_2d(smem + OFF_Q + c * QBOX, &tmQ, qbar, p.q_x0 + h * p.q_xh + c * 64, q_begin + q0);
+      int issued = 0;
+      for (int j = 0; j < nkt; ++j) {
+        const int s = j % STAGES, n = j / STAGES;
+        if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, s_err, p.err, kErrWaitTimeoutProducer)) break;
+        const int row = k_begin + j * BN;
+        uint8_t* st = smem + OFF_KV + s * STAGE;
+        mbar_arrive_expect_tx(&full[s], STAGE);
+        tma_load_2d(st, &tmK, &full[s], p.k_x0 + h * p.k_xh, row);
+        tma_load_2d(st + KBOX, &tmK, &full[s], p.k_x0 + h * p.k_xh + 64, row);
+        tma_load_2d(st + 2 * KBOX, &tmKpe, &full[s], 0, row);
+        tma_load_2d(st + 3 * KBOX, &tmV, &full[s], p.v_x0 + h * p.v_xh, row);
+        tma_load_2d(st + 4 * KBOX, &tmV, &full[s], p.v_x0 + h * p.v_xh + 64, row);
+        issued = j + 1;
+      }
+      if (*s_err != 0) {  // drain this CTA's copies still in flight
+        mbar_drain(qbar, 0);
+        for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_drain(&full[j % STAGES], (j / STAGES) & 1);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- tensor-core issue
+    if (lane == 0 && nkt > 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(BM, BN);
+      constexpr uint32_t idO = idesc_bf16_f32_bmn(BM, 128);
+      auto issue_s = [&](int j) {
+        const uint32_t st = sKV + (j % STAGES) * STAGE;
+        const uint32_t d = tbase + S_COL + (j & 1) * BN;
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(d, sdesc_kmajor_sw128(sQ + c * QBOX + kk * 32), sdesc_kmajor_sw128(st + c * KBOX + kk * 32), idS,
+                     (c | kk) != 0);
+        umma_commit(&sdone[j & 1]);
+      };
+      auto issue_o = [&](int j) {
+        const uint32_t st = sKV + (j % STAGES) * STAGE;
+        const uint32_t pb = sP + (j & 1) * PBYTES;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tbase + O_COL, sdesc_kmajor_sw128(pb + kk * 32),
+                   sdesc_mnmajor_sw128(st + 3 * KBOX + kk * 2048, KBOX), idO, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&odone[j & 1]);
+        umma_commit(&empty[j % STAGES]);
+      };
+      bool ok = mbar_wait(qbar, 0, s_err, p.err, kErrWaitTimeoutMma);
+      int ns = 0, no = 0;
+      long long t0 = clock64();
+      while (ok && no < nkt) {
+        bool progressed = false;
+        // S of tile ns once its stage landed and the softmax is done with the S buffer
+        // it overwrites (the O product of tile ns - 2 was issued)
+        if (ns < nkt && ns <= no + 1 && mbar_test_wait(&full[ns % STAGES], (ns / STAGES) & 1)) {
+          tc_fence_after();
+          issue_s(ns);
+          ++ns;
+          progressed = true;
+        }
+        if (no < ns && mbar_test_wait(&pready[no & 1], (no >> 1) & 1)) {
+          tc_fence_after();
+          issue_o(no);
+          ++no;
+          progressed = true;
+        }
+        if (progressed) {
+          t0 = clock64();
+        } else if (*s_err != 0) {
+          ok = false;
+        } else if (clock64() - t0 > kWaitBudgetCycles) {
+          *s_err = kErrWaitTimeoutMma;
+          atomicCAS(p.err, 0, kErrWaitTimeoutMma);
+          ok = false;
+        }
+      }
+      umma_commit(fin);
+      mbar_drain(fin, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax warps 0-3
+    const int r = threadIdx.x;         // query row of the tile = TMEM lane
+    const int qi = q0 + r;
+    const int limit = qi < q_len ? (p.causal ? min(k_len, diag + qi + 1) : k_len) : 0;  // keys [0, limit)
+    const uint32_t t_lane = tbase + (uint32_t(warp * 32) << 16);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkt; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&sdone[j & 1], (j >> 1) & 1, s_err, p.err, kErrWaitTimeoutEpilogue));
+      if (!ok) break;
+      tc_fence_after();
+      float sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN; c += 16) {
+        float t[16];
+        tmem_ld16(t_lane + S_COL + (j & 1) * BN + c, t);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) sv[c + e] = t[e];
+      }
+      const int kbase = j * BN;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        sv[c] = (kbase + c < limit) ? sv[c] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, sv[c]);
+      }
+      // the P buffer of this parity was read by the O product of two tiles back
+      if (j >= 2) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&odone[j & 1], ((j - 2) >> 1) & 1, s_err, p.err, kErrWaitTimeoutEpilogue));
+        if (!ok) break;
+      }
+      const bool need = mt > m_run + fatc::RESCALE_LOG2;
+      if (__any_sync(0xffffffffu, need)) {
+        float alpha = 1.f;
+        if (need) {
+          alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - mt);
+          m_run = mt;
+          l_run *= alpha;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          // O holds tiles 0 .. j-1 once the previous O product is done
+          ok = __all_sync(0xffffffffu, mbar_wait(&odone[(j - 1) & 1], ((j - 1) >> 1) & 1, s_err, p.err,
+                                                 kErrWaitTimeoutEpilogue));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 128; c += 16) {
+            float v[16];
+            tmem_ld16(t_lane + O_COL + c, v);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] *= alpha;
+            tmem_st16(t_lane + O_COL + c, v);
+          }
+        }
+      }
+      // P = exp2(S - m) as bf16, row r of a K-major 128-byte-swizzled tile
+      uint8_t* prow = smem + OFF_P + (j & 1) * PBYTES + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = sv[c * 8 + 2 * e] == -INFINITY ? 0.f : exp2f(sv[c * 8 + 2 * e] - m_run);
+          const float bq = sv[c * 8 + 2 * e + 1] == -INFINITY ? 0.f : exp2f(sv[c * 8 + 2 * e + 1] - m_run);
+          l_run += a + bq;
+          w[e] = pack_bf16(a, bq);
+        }
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&pready[j & 1]);
+    }
+    if (ok && nkt > 0)
+      ok = __all_sync(0xffffffffu, mbar_wait(&odone[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, s_err, p.err,
+                                             kErrWaitTimeoutEpilogue));
+    if (ok) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      bf16* orow = p.o + (long long)(q_begin + qi) * p.o_tok + (long long)h * p.o_head;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 16) {
+        float v[16];
+        if (nkt > 0) {
+          tmem_ld16(t_lane + O_COL + c, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = 0.f;
+        }
+        if (qi < q_len) {
+          uint4 w0 = make_uint4(pack_bf16(v[0] * inv, v[1] * inv), pack_bf16(v[2] * inv, v[3] * inv),
+                                pack_bf16(v[4] * inv, v[5] * inv), pack_bf16(v[6] * inv, v[7] * inv));
+          uint4 w1 = make_uint4(pack_bf16(v[8] * inv, v[9] * inv), pack_bf16(v[10] * inv, v[11] * inv),
+                                pack_bf16(v[12] * inv, v[13] * inv), pack_bf16(v[14] * inv, v[15] * inv));
+          *reinterpret_cast<uint4*>(orow + c) = w0;
+          *reinterpret_cast<uint4*>(orow + c + 8) = w1;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc<fatc::TMEM_COLS>(tbase);
+  }
+}
+
+// TMA needs 16-byte aligned bases and row strides and head offsets that keep every
+// box's x coordinate a multiple of 8 elements; otherwise the mma.sync kernel runs.
+bool prefill_attention_tc_ok(const PrefillAttnLaunch& l) {
+  auto al = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  return al(l.q) && al(l.k) && al(l.kpe) && al(l.v) && al(l.o) && l.q_tok % 8 == 0 && l.k_tok % 8 == 0 &&
+         l.kpe_tok % 8 == 0 && l.v_tok % 8 == 0 && l.q_head % 8 == 0 && l.k_head % 8 == 0 && l.v_head % 8 == 0 &&
+         l.o_tok % 8 == 0 && l.o_head % 8 == 0 && l.q_rows > 0 && l.k_rows > 0;
+}
+
+void prefill_attention_tc(const PrefillAttnLaunch& l) {
+  using namespace fatc;
+  CUtensorMap tq, tk, tkpe, tv;
+  // each map starts at the tensor's base and spans every head's columns of a row
+  const long long qcols = (long long)(l.H - 1) * l.q_head + 192;
+  const long long kcols = (long long)(l.H - 1) * l.k_head + 128;
+  const long long vcols = (long long)(l.H - 1) * l.v_head + 128;
+  make_tmap_2d(&tq, l.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.q_rows, qcols, l.q_tok, BM, 64);
+  make_tmap_2d(&tk, l.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.k_rows, kcols, l.k_tok, BN, 64);
+  make_tmap_2d(&tkpe, l.kpe, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.k_rows, 64, l.kpe_tok, BN, 64);
+  make_tmap_2d(&tv, l.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.k_rows, vcols, l.v_tok, BN, 64);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    attr = true;
+  }
+  FaTcParams p;
+  p.cu_q = l.cu_q;
+  p.cu_k = l.cu_k;
+  p.o = (bf16*)l.o;
+  p.o_tok = l.o_tok;
+  p.o_head = l.o_head;
+  p.H = l.H;
+  p.causal = l.causal;
+  p.q_x0 = 0;
+  p.k_x0 = 0;
+  p.v_x0 = 0;
+  p.q_xh = (int)l.q_head;
+  p.k_xh = (int)l.k_head;
+  p.v_xh = (int)l.v_head;
+  p.scale_log2 = l.scale * 1.4426950408889634f;
+  p.err = l.err;
+  if (l.B > 65535 || l.H > 65535) throw std::runtime_error("prefill_attention: grid limits");
+  dim3 grid((l.max_q + BM - 1) / BM, l.H, l.B);
+  launch_k(prefill_attn_tc_kernel, grid, dim3(THREADS), SMEM, l.stream, tq, tk, tkpe, tv, p);
+}
+
+}  // namespace sp

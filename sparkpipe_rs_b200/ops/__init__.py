@@ -374,8 +374,13 @@ def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=N
     return out
 
 
-def prefill_attention(q, k, kpe, v, o, cu_q, cu_k, max_q, scale, causal=True):
-    kernels().prefill_attention(q, k, kpe, v, o, cu_q, cu_k, int(max_q), float(scale), bool(causal))
+ATTN_IMPL = {"auto": 0, "tc": 1, "mma": 2}  # prefill attention kernels: default, tcgen05, mma.sync
+
+
+def prefill_attention(q, k, kpe, v, o, cu_q, cu_k, max_q, scale, causal=True, impl="auto"):
+    """Chunked causal MLA prefill attention (expanded form). ``impl``: "tc" (tcgen05,
+    the default when the tensors suit TMA), "mma" (mma.sync) or "auto"."""
+    kernels().prefill_attention(q, k, kpe, v, o, cu_q, cu_k, int(max_q), float(scale), bool(causal), ATTN_IMPL[impl])
     _count(1)
     return o
 

@@ -257,8 +257,10 @@ def _prefill_ref(q, k, kpe, v, cu_q, cu_k, scale):
     return out
 
 
-@pytest.mark.parametrize("qlens,klens", [([100, 64, 1], [100, 130, 50]), ([1024], [1024]), ([7, 200], [7, 333])])
-def test_prefill_attention(qlens, klens):
+@pytest.mark.parametrize("impl", ["tc", "mma"])
+@pytest.mark.parametrize("qlens,klens", [([100, 64, 1], [100, 130, 50]), ([1024], [1024]), ([7, 200], [7, 333]),
+                                         ([300], [1000])])
+def test_prefill_attention(qlens, klens, impl):
     ops = _ops()
     H = 4
     g = torch.Generator(device=DEV).manual_seed(sum(qlens))
@@ -270,7 +272,7 @@ def test_prefill_attention(qlens, klens):
     cu_k = torch.tensor([0] + list(torch.tensor(klens).cumsum(0)), device=DEV, dtype=torch.int32)
     o = torch.empty(Tq, H, 128, device=DEV, dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(192)
-    ops.prefill_attention(q, kv[:, :, :128], kpe, kv[:, :, 128:], o, cu_q, cu_k, max(qlens), scale)
+    ops.prefill_attention(q, kv[:, :, :128], kpe, kv[:, :, 128:], o, cu_q, cu_k, max(qlens), scale, impl=impl)
     ref = _prefill_ref(q, kv[:, :, :128], kpe, kv[:, :, 128:], cu_q.cpu(), cu_k.cpu(), scale)
     _close(o, ref, atol=2e-2, rtol=2e-2)
 
