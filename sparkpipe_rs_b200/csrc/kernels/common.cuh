@@ -321,6 +321,15 @@ SP_DEVI float4 ld_dsmem_f32x4(uint32_t addr) {
 // is still running. It must call griddep_wait() before touching memory the
 // predecessor writes (or reads, for buffers it overwrites); griddep_launch()
 // lets the next kernel in the stream start its own prologue.
+// 2^x by the hardware approximation (PTX ex2.approx.ftz.f32: ~2 ulp, subnormal
+// results flushed to zero; 2^-inf = +0). For softmax weights, whose subnormals do
+// not matter.
+SP_DEVI float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 SP_DEVI void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 SP_DEVI void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

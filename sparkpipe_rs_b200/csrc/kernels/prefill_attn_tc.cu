@@ -230,12 +230,16 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
         for (int e = 0; e < 16; ++e) sv[c + e] = t[e];
       }
       const int kbase = j * BN;
-      float mt = -INFINITY;
+      if (kbase + BN > limit) {  // tile crosses the row's key limit (causal diagonal, tail, padding rows)
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        sv[c] = (kbase + c < limit) ? sv[c] * p.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, sv[c]);
+        for (int c = 0; c < BN; ++c)
+          if (kbase + c >= limit) sv[c] = -INFINITY;
       }
+      float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};  // four independent chains
+#pragma unroll
+      for (int c = 4; c < BN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
+      const float mraw = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const float mt = mraw * p.scale_log2;  // scale > 0: the max of the scaled scores
       // the P buffer of this parity was read by the O product of two tiles back
       if (j >= 2) {
         ok = __all_sync(0xffffffffu,
@@ -246,7 +250,7 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
       if (__any_sync(0xffffffffu, need)) {
         float alpha = 1.f;
         if (need) {
-          alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - mt);
+          alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mt);
           m_run = mt;
           l_run *= alpha;
         }
@@ -266,20 +270,24 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
           }
         }
       }
-      // P = exp2(S - m) as bf16, row r of a K-major 128-byte-swizzled tile
+      // P = 2^(s * scale - m) as bf16 (masked scores are -inf: 2^-inf = 0; a row with
+      // no key yet uses m = 0), row r of a K-major 128-byte-swizzled tile
+      const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
       uint8_t* prow = smem + OFF_P + (j & 1) * PBYTES + (r >> 3) * 1024 + (r & 7) * 128;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float a = sv[c * 8 + 2 * e] == -INFINITY ? 0.f : exp2f(sv[c * 8 + 2 * e] - m_run);
-          const float bq = sv[c * 8 + 2 * e + 1] == -INFINITY ? 0.f : exp2f(sv[c * 8 + 2 * e + 1] - m_run);
-          l_run += a + bq;
+          const float a = fast_exp2(fmaf(sv[c * 8 + 2 * e], p.scale_log2, neg_m));
+          const float bq = fast_exp2(fmaf(sv[c * 8 + 2 * e + 1], p.scale_log2, neg_m));
+          ls[e] += a + bq;
           w[e] = pack_bf16(a, bq);
         }
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
+      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&pready[j & 1]);
