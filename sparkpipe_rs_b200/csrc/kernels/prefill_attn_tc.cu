@@ -13,17 +13,19 @@
 // rope box) and V (two boxes) of a tile form one 40 KB stage of a three-stage TMA
 // ring. V is the B operand of the second product read MN-major (keys are its K).
 //
-// The TMEM data-path lane of a query row is its thread in the 4 softmax warps, so
-// the online softmax needs no cross-thread reduction: each thread reads its row of
-// S, masks, takes the row max, exponentiates, keeps its own running sum and writes
-// its row of P (bf16, 128-byte swizzled, K-major: the A operand of the second
-// product). The running max is lazy: P is taken against the current max unless the
+// A query row's TMEM data-path lane belongs to two softmax threads (warps w and
+// w + 4), each reading half of the row of S: they mask, take the half-row max,
+// agree on the row max through shared memory, exponentiate, keep their own partial
+// sums and write their half of the row of P (bf16, 128-byte swizzled, K-major: the
+// A operand of the second product). One warp per sub-partition left the tensor
+// pipe idle two thirds of the time (the softmax latency per tile). The running max is lazy: P is taken against the current max unless the
 // row's tile max exceeds it by more than 2^8; only then (warp-uniformly) is the
 // row's O rescaled in TMEM, after the previous tile's second product finished.
 //
-// Warp roles (192 threads): warps 0-3 softmax / epilogue, warp 4 TMA producer,
-// warp 5 tensor-core issue (one thread, never blocking on one product while the
-// other could go) and TMEM allocation. Barriers that one side may pass twice before
+// Warp roles (320 threads): warps 0-7 softmax / epilogue (two per TMEM lane
+// quadrant, each owning half of its query rows), warp 8 TMA producer, warp 9
+// tensor-core issue (one thread, never blocking on one product while the other
+// could go) and TMEM allocation. Barriers that one side may pass twice before
 // the other looks are kept per tile parity. Every wait is bounded; on a timeout the
 // CTA records the error, drains its copies and MMAs and returns.
 //
@@ -53,13 +55,16 @@ constexpr int OFF_Q = 0;
 constexpr int OFF_KV = 3 * QBOX;
 constexpr int OFF_P = OFF_KV + STAGES * STAGE;
 constexpr int PBYTES = BM * 128;         // P: 128 rows x 64 keys bf16
-constexpr int OFF_BAR = OFF_P + 2 * PBYTES;
+constexpr int OFF_XCH = OFF_P + 2 * PBYTES;   // [2 parity][2 halves][128 rows] half-row maxima
+constexpr int OFF_BAR = OFF_XCH + 2 * 2 * BM * 4;
 constexpr int NBAR = 16;
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
 constexpr int S_COL = 0;                 // two S buffers of 64 columns
 constexpr int O_COL = 128;               // O: 128 columns
 constexpr int TMEM_COLS = 256;
-constexpr int THREADS = 192;
+constexpr int SOFTMAX_THREADS = 256;     // 8 warps: two per TMEM lane quadrant, one per half row
+constexpr int PRODUCER_WARP = 8, MMA_WARP = 9;
+constexpr int THREADS = 320;
 constexpr float RESCALE_LOG2 = 8.f;
 }  // namespace fatc
 
@@ -74,6 +79,20 @@ struct FaTcParams {
   float scale_log2;
   int* err;
 };
+
+// AND of `v` over `n` threads at named barrier `id` (also a memory barrier among them).
+SP_DEVI bool named_bar_and(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(uint32_t(v)), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
 
 __global__ void __launch_bounds__(fatc::THREADS, 1)
     prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -109,11 +128,11 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 14; ++i) mbar_init(&bars[i], (i >= 10 && i < 12) ? 128 : 1);
+    for (int i = 0; i < 14; ++i) mbar_init(&bars[i], (i >= 10 && i < 12) ? SOFTMAX_THREADS : 1);
     *s_err = 0;
     fence_mbarrier_init();
   }
-  if (warp == 5) {
+  if (warp == MMA_WARP) {
     tmem_alloc<TMEM_COLS>(tmem_slot);
     tmem_relinquish();
     tc_fence_before();
@@ -122,7 +141,7 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == PRODUCER_WARP) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0 && nkt > 0) {
       prefetch_tmap(&tmQ);
@@ -151,7 +170,7 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
         for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_drain(&full[j % STAGES], (j / STAGES) & 1);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == MMA_WARP) {
     // ---------------------------------------------------------------- tensor-core issue
     if (lane == 0 && nkt > 0) {
       constexpr uint32_t idS = idesc_bf16_f32(BM, BN);
@@ -210,73 +229,91 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
       mbar_drain(fin, 0);
     }
   } else {
-    // ---------------------------------------------------------------- softmax warps 0-3
-    const int r = threadIdx.x;         // query row of the tile = TMEM lane
+    // ---------------------------------------------------------------- softmax warps 0-7
+    // Warps w and w + 4 share TMEM lane quadrant w % 4: each thread owns half of its
+    // query row (keys [32 hf, 32 hf + 32) of a tile, O columns [64 hf, 64 hf + 64)).
+    // The halves agree on the row max through shared memory at the per-tile barrier,
+    // which is also where all 256 threads agree whether every wait succeeded (a
+    // thread never leaves the loop alone, so nobody is left at the barrier).
+    const int quad = warp & 3, hf = warp >> 2;
+    const int r = quad * 32 + lane;    // query row of the tile = TMEM lane
     const int qi = q0 + r;
     const int limit = qi < q_len ? (p.causal ? min(k_len, diag + qi + 1) : k_len) : 0;  // keys [0, limit)
-    const uint32_t t_lane = tbase + (uint32_t(warp * 32) << 16);
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
+    const uint32_t t_lane = tbase + (uint32_t(quad * 32) << 16);
+    float* xch = reinterpret_cast<float*>(smem + OFF_XCH);
+    float m_run = -INFINITY, l_part = 0.f;
+    bool ok = true, bad = false;
     for (int j = 0; j < nkt; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&sdone[j & 1], (j >> 1) & 1, s_err, p.err, kErrWaitTimeoutEpilogue));
-      if (!ok) break;
-      tc_fence_after();
-      float sv[BN];
+      bool okl = !bad && mbar_wait(&sdone[j & 1], (j >> 1) & 1, s_err, p.err, kErrWaitTimeoutEpilogue);
+      float sv[32];
+      float mh = -INFINITY;
+      const int kb = j * BN + hf * 32;
+      if (okl) {
+        tc_fence_after();
+        uint32_t a0[16], a1[16];
+        const uint32_t ta = t_lane + S_COL + (j & 1) * BN + hf * 32;
+        tmem_ld16_issue(ta, a0);
+        tmem_ld16_issue(ta + 16, a1);
+        tmem_ld_wait(a0);
+        tmem_ld_wait(a1);
 #pragma unroll
-      for (int c = 0; c < BN; c += 16) {
-        float t[16];
-        tmem_ld16(t_lane + S_COL + (j & 1) * BN + c, t);
+        for (int c = 0; c < 16; ++c) {
+          sv[c] = __uint_as_float(a0[c]);
+          sv[16 + c] = __uint_as_float(a1[c]);
+        }
+        if (kb + 32 > limit) {  // half tile crosses the row's key limit
 #pragma unroll
-        for (int e = 0; e < 16; ++e) sv[c + e] = t[e];
+          for (int c = 0; c < 32; ++c)
+            if (kb + c >= limit) sv[c] = -INFINITY;
+        }
+        float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+        for (int c = 4; c < 32; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
+        mh = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       }
-      const int kbase = j * BN;
-      if (kbase + BN > limit) {  // tile crosses the row's key limit (causal diagonal, tail, padding rows)
-#pragma unroll
-        for (int c = 0; c < BN; ++c)
-          if (kbase + c >= limit) sv[c] = -INFINITY;
-      }
-      float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};  // four independent chains
-#pragma unroll
-      for (int c = 4; c < BN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
-      const float mraw = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      const float mt = mraw * p.scale_log2;  // scale > 0: the max of the scaled scores
       // the P buffer of this parity was read by the O product of two tiles back
-      if (j >= 2) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(&odone[j & 1], ((j - 2) >> 1) & 1, s_err, p.err, kErrWaitTimeoutEpilogue));
-        if (!ok) break;
-      }
-      const bool need = mt > m_run + fatc::RESCALE_LOG2;
+      if (okl && j >= 2) okl = mbar_wait(&odone[j & 1], ((j - 2) >> 1) & 1, s_err, p.err, kErrWaitTimeoutEpilogue);
+      float* xj = xch + (j & 1) * 2 * BM;
+      xj[hf * BM + r] = mh;
+      ok = named_bar_and(1, SOFTMAX_THREADS, okl);
+      if (!ok) break;
+      const float mt = fmaxf(mh, xj[(1 - hf) * BM + r]) * p.scale_log2;  // scale > 0
+      const bool need = mt > m_run + fatc::RESCALE_LOG2;  // the same in both halves of the row
       if (__any_sync(0xffffffffu, need)) {
         float alpha = 1.f;
         if (need) {
           alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mt);
           m_run = mt;
-          l_run *= alpha;
+          l_part *= alpha;
         }
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-          // O holds tiles 0 .. j-1 once the previous O product is done
-          ok = __all_sync(0xffffffffu, mbar_wait(&odone[(j - 1) & 1], ((j - 1) >> 1) & 1, s_err, p.err,
-                                                 kErrWaitTimeoutEpilogue));
-          if (!ok) break;
-          tc_fence_after();
+          // O holds tiles 0 .. j-1 once the previous O product is done; this thread
+          // rescales its half of the row
+          const bool okw = __all_sync(0xffffffffu, mbar_wait(&odone[(j - 1) & 1], ((j - 1) >> 1) & 1, s_err, p.err,
+                                                              kErrWaitTimeoutEpilogue));
+          if (okw) {
+            tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < 128; c += 16) {
-            float v[16];
-            tmem_ld16(t_lane + O_COL + c, v);
+            for (int c = 0; c < 64; c += 16) {
+              float v[16];
+              tmem_ld16(t_lane + O_COL + hf * 64 + c, v);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] *= alpha;
-            tmem_st16(t_lane + O_COL + c, v);
+              for (int e = 0; e < 16; ++e) v[e] *= alpha;
+              tmem_st16(t_lane + O_COL + hf * 64 + c, v);
+            }
+          } else {
+            bad = true;  // reported at the next tile's barrier
           }
         }
       }
       // P = 2^(s * scale - m) as bf16 (masked scores are -inf: 2^-inf = 0; a row with
-      // no key yet uses m = 0), row r of a K-major 128-byte-swizzled tile
+      // no key yet uses m = 0), chunks 4 hf .. 4 hf + 3 of row r of a K-major
+      // 128-byte-swizzled tile
       const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
       uint8_t* prow = smem + OFF_P + (j & 1) * PBYTES + (r >> 3) * 1024 + (r & 7) * 128;
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -285,25 +322,32 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
           ls[e] += a + bq;
           w[e] = pack_bf16(a, bq);
         }
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(prow + (((hf * 4 + c) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      l_part += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&pready[j & 1]);
     }
-    if (ok && nkt > 0)
-      ok = __all_sync(0xffffffffu, mbar_wait(&odone[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, s_err, p.err,
-                                             kErrWaitTimeoutEpilogue));
+    if (ok) {
+      const bool okl = !bad && (nkt == 0 || mbar_wait(&odone[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, s_err, p.err,
+                                                       kErrWaitTimeoutEpilogue));
+      // the exchange slots of tile nkt - 2's parity: their readers all passed tile nkt - 1's barrier
+      float* xl = xch + (nkt & 1) * 2 * BM;
+      xl[hf * BM + r] = l_part;
+      ok = named_bar_and(1, SOFTMAX_THREADS, okl);
+    }
     if (ok) {
       tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      bf16* orow = p.o + (long long)(q_begin + qi) * p.o_tok + (long long)h * p.o_head;
+      const float* xl = xch + (nkt & 1) * 2 * BM;
+      const float l = xl[r] + xl[BM + r];
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      bf16* orow = p.o + (long long)(q_begin + qi) * p.o_tok + (long long)h * p.o_head + hf * 64;
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 16) {
+      for (int c = 0; c < 64; c += 16) {
         float v[16];
         if (nkt > 0) {
-          tmem_ld16(t_lane + O_COL + c, v);
+          tmem_ld16(t_lane + O_COL + hf * 64 + c, v);
         } else {
 #pragma unroll
           for (int e = 0; e < 16; ++e) v[e] = 0.f;
@@ -320,7 +364,7 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
     }
   }
   __syncthreads();
-  if (warp == 5) {
+  if (warp == fatc::MMA_WARP) {
     tc_fence_after();
     tmem_dealloc<fatc::TMEM_COLS>(tbase);
   }
