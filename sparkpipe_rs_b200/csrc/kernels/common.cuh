@@ -185,6 +185,17 @@ SP_DEVI void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_
       : "memory");
 }
 
+// D(tmem) (+)= A(tmem) x B(smem desc)^T, kind::f16: A read from tensor memory
+// (M lanes, K/2 columns of packed 16-bit pairs, the lower k in the low half).
+SP_DEVI void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // kind::f8f6f4 (e4m3/e5m2 in, fp32 acc).
 SP_DEVI void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(

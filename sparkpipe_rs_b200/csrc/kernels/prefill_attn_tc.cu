@@ -3,21 +3,22 @@
 // q_nope/k_nope 128, shared rope key 64, v 128; variable-length batches; query i
 // of a chunk of Lq against Lk keys sees keys j <= Lk - Lq + i).
 //
-// One CTA = 128 queries of one head. Per 64-key tile:
+// One CTA = 128 queries of one head. Per 128-key tile:
 //
-//   S[128 q, 64 k]  = Q[128, 192] . K_tile[64, 192]^T    (12 x tcgen05.mma M=128 N=64 K=16)
-//   O[128 q, 128 d] += P[128, 64] . V_tile[64, 128]       ( 4 x tcgen05.mma M=128 N=128 K=16)
+//   S[128 q, 128 k]  = Q[128, 192] . K_tile[128, 192]^T   (12 x tcgen05.mma M=128 N=128 K=16)
+//   O[128 q, 128 d] += P[128, 128] . V_tile[128, 128]      ( 8 x tcgen05.mma M=128 N=128 K=16)
 //
-// S and O accumulate in tensor memory (two S buffers of 64 columns, O 128
-// columns). Q (three 64-dim boxes) is loaded once by TMA; K (two nope boxes + the
-// rope box) and V (two boxes) of a tile form one 40 KB stage of a three-stage TMA
-// ring. V is the B operand of the second product read MN-major (keys are its K).
+// S and O accumulate in tensor memory (two S buffers, O), and P is written back
+// into tensor memory (two buffers, bf16 pairs per column) as the A operand of the
+// second product, so it costs no shared memory: Q (three 64-dim boxes, 48 KB) and
+// a double-buffered 80 KB stage of K (two nope boxes + the rope box) and V (two
+// boxes) fit. V is the B operand of the second product read MN-major (keys are
+// its K). 64-key tiles with P in shared memory measured 800 TFLOP/s.
 //
 // A query row's TMEM data-path lane belongs to two softmax threads (warps w and
 // w + 4), each reading half of the row of S: they mask, take the half-row max,
 // agree on the row max through shared memory, exponentiate, keep their own partial
-// sums and write their half of the row of P (bf16, 128-byte swizzled, K-major: the
-// A operand of the second product). One warp per sub-partition left the tensor
+// sums and store their half of the row of P into tensor memory. One warp per sub-partition left the tensor
 // pipe idle two thirds of the time (the softmax latency per tile). The running max is lazy: P is taken against the current max unless the
 // row's tile max exceeds it by more than 2^8; only then (warp-uniformly) is the
 // row's O rescaled in TMEM, after the previous tile's second product finished.
@@ -46,22 +47,21 @@ using bf16 = __nv_bfloat16;
 
 namespace fatc {
 constexpr int BM = 128;                  // queries per CTA
-constexpr int BN = 64;                   // keys per tile
+constexpr int BN = 128;                  // keys per tile
 constexpr int QBOX = BM * 128;           // 128 rows x 64 dims bf16
-constexpr int KBOX = BN * 128;           // 64 keys x 64 dims bf16
-constexpr int STAGES = 3;
-constexpr int STAGE = 5 * KBOX;          // K nope (2) + K rope (1) + V (2)
+constexpr int KBOX = BN * 128;           // 128 keys x 64 dims bf16
+constexpr int STAGES = 2;
+constexpr int STAGE = 5 * KBOX;          // K nope (2) + K rope (1) + V (2): 80 KB
 constexpr int OFF_Q = 0;
 constexpr int OFF_KV = 3 * QBOX;
-constexpr int OFF_P = OFF_KV + STAGES * STAGE;
-constexpr int PBYTES = BM * 128;         // P: 128 rows x 64 keys bf16
-constexpr int OFF_XCH = OFF_P + 2 * PBYTES;   // [2 parity][2 halves][128 rows] half-row maxima
+constexpr int OFF_XCH = OFF_KV + STAGES * STAGE;  // [2 parity][2 halves][128 rows] half-row maxima
 constexpr int OFF_BAR = OFF_XCH + 2 * 2 * BM * 4;
 constexpr int NBAR = 16;
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
-constexpr int S_COL = 0;                 // two S buffers of 64 columns
-constexpr int O_COL = 128;               // O: 128 columns
-constexpr int TMEM_COLS = 256;
+constexpr int S_COL = 0;                 // two S buffers of 128 fp32 columns
+constexpr int O_COL = 256;               // O: 128 fp32 columns
+constexpr int P_COL = 384;               // two P buffers of 64 columns (128 bf16 keys, packed pairs)
+constexpr int TMEM_COLS = 512;
 constexpr int SOFTMAX_THREADS = 256;     // 8 warps: two per TMEM lane quadrant, one per half row
 constexpr int PRODUCER_WARP = 8, MMA_WARP = 9;
 constexpr int THREADS = 320;
@@ -114,7 +114,6 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sQ = smem_u32(smem + OFF_Q);
   const uint32_t sKV = smem_u32(smem + OFF_KV);
-  const uint32_t sP = smem_u32(smem + OFF_P);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* full = bars;        // [3] stage landed
   uint64_t* empty = bars + 3;   // [3] second product of the stage's tile done
@@ -188,11 +187,11 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
       };
       auto issue_o = [&](int j) {
         const uint32_t st = sKV + (j % STAGES) * STAGE;
-        const uint32_t pb = sP + (j & 1) * PBYTES;
+        const uint32_t pa = tbase + P_COL + (j & 1) * (BN / 2);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tbase + O_COL, sdesc_kmajor_sw128(pb + kk * 32),
-                   sdesc_mnmajor_sw128(st + 3 * KBOX + kk * 2048, KBOX), idO, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BN / 16; ++kk)  // A = P from tensor memory: 16 keys = 8 columns
+          umma_f16_ts(tbase + O_COL, pa + kk * 8, sdesc_mnmajor_sw128(st + 3 * KBOX + kk * 2048, KBOX), idO,
+                      (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&odone[j & 1]);
         umma_commit(&empty[j % STAGES]);
       };
@@ -245,30 +244,30 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
     bool ok = true, bad = false;
     for (int j = 0; j < nkt; ++j) {
       bool okl = !bad && mbar_wait(&sdone[j & 1], (j >> 1) & 1, s_err, p.err, kErrWaitTimeoutEpilogue);
-      float sv[32];
+      constexpr int HK = BN / 2;  // keys per half row
+      float sv[HK];
       float mh = -INFINITY;
-      const int kb = j * BN + hf * 32;
+      const int kb = j * BN + hf * HK;
       if (okl) {
         tc_fence_after();
-        uint32_t a0[16], a1[16];
-        const uint32_t ta = t_lane + S_COL + (j & 1) * BN + hf * 32;
-        tmem_ld16_issue(ta, a0);
-        tmem_ld16_issue(ta + 16, a1);
-        tmem_ld_wait(a0);
-        tmem_ld_wait(a1);
+        uint32_t a[4][16];
+        const uint32_t ta = t_lane + S_COL + (j & 1) * BN + hf * HK;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          sv[c] = __uint_as_float(a0[c]);
-          sv[16 + c] = __uint_as_float(a1[c]);
-        }
-        if (kb + 32 > limit) {  // half tile crosses the row's key limit
+        for (int q = 0; q < 4; ++q) tmem_ld16_issue(ta + q * 16, a[q]);
 #pragma unroll
-          for (int c = 0; c < 32; ++c)
+        for (int q = 0; q < 4; ++q) tmem_ld_wait(a[q]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int c = 0; c < 16; ++c) sv[q * 16 + c] = __uint_as_float(a[q][c]);
+        if (kb + HK > limit) {  // half tile crosses the row's key limit
+#pragma unroll
+          for (int c = 0; c < HK; ++c)
             if (kb + c >= limit) sv[c] = -INFINITY;
         }
         float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-        for (int c = 4; c < 32; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
+        for (int c = 4; c < HK; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
         mh = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       }
       // the P buffer of this parity was read by the O product of two tiles back
@@ -307,25 +306,22 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
         }
       }
       // P = 2^(s * scale - m) as bf16 (masked scores are -inf: 2^-inf = 0; a row with
-      // no key yet uses m = 0), chunks 4 hf .. 4 hf + 3 of row r of a K-major
-      // 128-byte-swizzled tile
+      // no key yet uses m = 0), this half row's 32 columns of the P buffer in TMEM
       const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
-      uint8_t* prow = smem + OFF_P + (j & 1) * PBYTES + (r >> 3) * 1024 + (r & 7) * 128;
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t w[4];
+      for (int q = 0; q < 2; ++q) {
+        float w[16];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float a = fast_exp2(fmaf(sv[c * 8 + 2 * e], p.scale_log2, neg_m));
-          const float bq = fast_exp2(fmaf(sv[c * 8 + 2 * e + 1], p.scale_log2, neg_m));
-          ls[e] += a + bq;
-          w[e] = pack_bf16(a, bq);
+        for (int e = 0; e < 16; ++e) {
+          const float a = fast_exp2(fmaf(sv[q * 32 + 2 * e], p.scale_log2, neg_m));
+          const float bq = fast_exp2(fmaf(sv[q * 32 + 2 * e + 1], p.scale_log2, neg_m));
+          ls[e & 3] += a + bq;
+          w[e] = __uint_as_float(pack_bf16(a, bq));
         }
-        *reinterpret_cast<uint4*>(prow + (((hf * 4 + c) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        tmem_st16(t_lane + P_COL + (j & 1) * (BN / 2) + hf * (HK / 2) + q * 16, w);
       }
       l_part += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&pready[j & 1]);
     }
