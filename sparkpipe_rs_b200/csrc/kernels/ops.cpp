@@ -659,6 +659,26 @@ void decode_advance(const Tensor& out_ids, const Tensor& ids, const Tensor& pos,
                      (int)block_size, stream());
 }
 
+// ---------------------------------------------------------------- raw device memory
+// Untyped device allocations for native components that keep their own ledger
+// (stage modules): pointers cross as integers.
+int64_t raw_alloc(int64_t bytes, int64_t device) {
+  const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, (size_t)bytes) == cudaSuccess, "raw_alloc: cudaMalloc failed");
+  return (int64_t)reinterpret_cast<uintptr_t>(p);
+}
+void raw_free(int64_t ptr) { cudaFree(reinterpret_cast<void*>((uintptr_t)ptr)); }
+int64_t raw_zero(int64_t ptr, int64_t bytes) {
+  return cudaMemset(reinterpret_cast<void*>((uintptr_t)ptr), 0, (size_t)bytes) == cudaSuccess ? 0 : 17;
+}
+int64_t raw_copy(int64_t dst, int64_t src, int64_t bytes) {
+  return cudaMemcpy(reinterpret_cast<void*>((uintptr_t)dst), reinterpret_cast<const void*>((uintptr_t)src),
+                    (size_t)bytes, cudaMemcpyDefault) == cudaSuccess
+             ? 0
+             : 17;
+}
+
 // ---------------------------------------------------------------- expert parallel
 // One cudaMalloc per rank holds every EP region; its IPC handle is exchanged
 // over the process group and each peer maps it (cudaIpcOpenMemHandle), so the
@@ -828,6 +848,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_ctas_per_sm", [](int64_t heads, int64_t impl) { return sp::mla_ctas_per_sm((int)heads, (int)impl); },
         py::arg("heads"), py::arg("impl") = 0);
   m.def("mla_stage_tokens", []() { return sp::mla_stage_tokens(); });
+  m.def("raw_alloc", &raw_alloc);
+  m.def("raw_free", &raw_free);
+  m.def("raw_zero", &raw_zero);
+  m.def("raw_copy", &raw_copy);
   m.def("ep_alloc", &ep_alloc);
   m.def("ep_ipc_handle", &ep_ipc_handle);
   m.def("ep_ipc_open", &ep_ipc_open);
