@@ -795,4 +795,12 @@ void quant_weight_fp8(const void* src, uint64_t seed, long long flat0, float std
            std_, (__nv_fp8_e4m3*)q, s, rows, cols);
 }
 
+void kernel_attrs_fp8(std::vector<KernelAttr>& out) {
+#define SP_F8_ATTR(BN, MODE) push_kernel_attr(out, "gemm_fp8_kernel<" #BN "," #MODE ">", gemm_fp8_kernel<BN, MODE>)
+  SP_F8_ATTR(32, 0); SP_F8_ATTR(64, 0); SP_F8_ATTR(128, 0);
+  SP_F8_ATTR(32, 1); SP_F8_ATTR(64, 1); SP_F8_ATTR(128, 1);
+  SP_F8_ATTR(32, 2); SP_F8_ATTR(64, 2); SP_F8_ATTR(128, 2);
+#undef SP_F8_ATTR
+}
+
 }  // namespace sp

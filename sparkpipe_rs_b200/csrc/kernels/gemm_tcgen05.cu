@@ -726,4 +726,12 @@ int gemm_bf16(const GemmLaunch& g) {
   return 1;
 }
 
+void kernel_attrs_gemm(std::vector<KernelAttr>& out) {
+#define SP_GEMM_ATTR(BN, MODE) push_kernel_attr(out, "gemm_bf16_kernel<" #BN "," #MODE ">", gemm_bf16_kernel<BN, MODE>)
+  SP_GEMM_ATTR(16, 0); SP_GEMM_ATTR(32, 0); SP_GEMM_ATTR(64, 0); SP_GEMM_ATTR(128, 0); SP_GEMM_ATTR(256, 0);
+  SP_GEMM_ATTR(16, 1); SP_GEMM_ATTR(32, 1); SP_GEMM_ATTR(64, 1); SP_GEMM_ATTR(128, 1); SP_GEMM_ATTR(256, 1);
+  SP_GEMM_ATTR(16, 2); SP_GEMM_ATTR(32, 2); SP_GEMM_ATTR(64, 2); SP_GEMM_ATTR(128, 2); SP_GEMM_ATTR(256, 2);
+#undef SP_GEMM_ATTR
+}
+
 }  // namespace sp

@@ -2,6 +2,8 @@
 // headers) so the .cu translation units compile quickly; ops.cpp binds these
 // to torch tensors.
 #pragma once
+#include <string>
+#include <vector>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -183,6 +185,28 @@ enum { MLA_IMPL_AUTO = 0, MLA_IMPL_TC = 1, MLA_IMPL_MMA = 2 };
 int mla_stage_tokens();
 int mla_ctas_per_sm(int heads, int impl = MLA_IMPL_AUTO);
 void mla_decode(const MlaDecodeLaunch& l);
+
+// ---- kernel resource receipts (registers, local memory, static shared memory) of
+// the hot kernels, for the hardware probes; each file adds its own kernels.
+struct KernelAttr {
+  std::string name;
+  int regs = 0, local_bytes = 0, static_smem = 0, max_threads = 0, ptx_version = 0, binary_version = 0;
+};
+template <class F>
+inline void push_kernel_attr(std::vector<KernelAttr>& out, const std::string& name, F fn) {
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, reinterpret_cast<const void*>(fn)) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  out.push_back(KernelAttr{name, a.numRegs, (int)a.localSizeBytes, (int)a.sharedSizeBytes, a.maxThreadsPerBlock,
+                           a.ptxVersion, a.binaryVersion});
+}
+void kernel_attrs_gemm(std::vector<KernelAttr>& out);
+void kernel_attrs_fp8(std::vector<KernelAttr>& out);
+void kernel_attrs_mla(std::vector<KernelAttr>& out);
+void kernel_attrs_prefill(std::vector<KernelAttr>& out);
+void kernel_attrs_moe(std::vector<KernelAttr>& out);
 
 // ---- prefill attention (prefill_attn.cu)
 struct PrefillAttnLaunch {

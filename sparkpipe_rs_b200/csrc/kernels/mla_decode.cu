@@ -864,4 +864,12 @@ void mla_decode(const MlaDecodeLaunch& l) {
   }
 }
 
+void kernel_attrs_mla(std::vector<KernelAttr>& out) {
+  push_kernel_attr(out, "mla_decode_kernel<16,4,64>", mla_decode_kernel<16, 4, 64>);
+  push_kernel_attr(out, "mla_decode_kernel<32,4,64>", mla_decode_kernel<32, 4, 64>);
+  push_kernel_attr(out, "mla_decode_tc_kernel<16>", mla_decode_tc_kernel<16>);
+  push_kernel_attr(out, "mla_decode_tc_kernel<32>", mla_decode_tc_kernel<32>);
+  push_kernel_attr(out, "mla_combine_kernel", mla_combine_kernel);
+}
+
 }  // namespace sp

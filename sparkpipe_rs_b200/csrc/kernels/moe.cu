@@ -492,4 +492,10 @@ void combine_add_rmsnorm(const void* y, long long ldy, const int* inv_pos, const
            (bf16*)residual, (const bf16*)gamma, (bf16*)out, ldo, k, H, eps);
 }
 
+void kernel_attrs_moe(std::vector<KernelAttr>& out) {
+  push_kernel_attr(out, "moe_topk_kernel<4>", moe_topk_kernel<4>);
+  push_kernel_attr(out, "moe_topk_kernel<1>", moe_topk_kernel<1>);
+  push_kernel_attr(out, "moe_align_small_kernel", moe_align_small_kernel);
+}
+
 }  // namespace sp

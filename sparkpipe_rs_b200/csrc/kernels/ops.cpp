@@ -848,6 +848,27 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_ctas_per_sm", [](int64_t heads, int64_t impl) { return sp::mla_ctas_per_sm((int)heads, (int)impl); },
         py::arg("heads"), py::arg("impl") = 0);
   m.def("mla_stage_tokens", []() { return sp::mla_stage_tokens(); });
+  m.def("kernel_attributes", []() {
+    std::vector<sp::KernelAttr> v;
+    sp::kernel_attrs_gemm(v);
+    sp::kernel_attrs_fp8(v);
+    sp::kernel_attrs_mla(v);
+    sp::kernel_attrs_prefill(v);
+    sp::kernel_attrs_moe(v);
+    py::list out;
+    for (const auto& a : v) {
+      py::dict d;
+      d["name"] = a.name;
+      d["registers"] = a.regs;
+      d["local_bytes"] = a.local_bytes;
+      d["static_smem"] = a.static_smem;
+      d["max_threads"] = a.max_threads;
+      d["ptx_version"] = a.ptx_version;
+      d["binary_version"] = a.binary_version;
+      out.append(d);
+    }
+    return out;
+  });
   m.def("raw_alloc", &raw_alloc);
   m.def("raw_free", &raw_free);
   m.def("raw_zero", &raw_zero);

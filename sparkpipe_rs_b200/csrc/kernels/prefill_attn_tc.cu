@@ -412,4 +412,8 @@ void prefill_attention_tc(const PrefillAttnLaunch& l) {
   launch_k(prefill_attn_tc_kernel, grid, dim3(THREADS), SMEM, l.stream, tq, tk, tkpe, tv, p);
 }
 
+void kernel_attrs_prefill(std::vector<KernelAttr>& out) {
+  push_kernel_attr(out, "prefill_attn_tc_kernel", prefill_attn_tc_kernel);
+}
+
 }  // namespace sp
