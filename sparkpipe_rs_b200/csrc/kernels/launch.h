@@ -186,6 +186,12 @@ int mla_stage_tokens();
 int mla_ctas_per_sm(int heads, int impl = MLA_IMPL_AUTO);
 void mla_decode(const MlaDecodeLaunch& l);
 
+// ---- DSA token selection (dsa.cu)
+void paged_slots(const int* block_table, int max_blocks, const int* lens, const int* positions, int B, int rows,
+                 int block_size, int* slots, cudaStream_t s);
+void dsa_topk(const float* raw, const float* w, int B, int Hi, int rows, const int* lens, int topk, float* scores,
+              int* out, int* counts, cudaStream_t s);
+
 // ---- kernel resource receipts (registers, local memory, static shared memory) of
 // the hot kernels, for the hardware probes; each file adds its own kernels.
 struct KernelAttr {

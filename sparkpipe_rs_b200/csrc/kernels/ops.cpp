@@ -659,6 +659,37 @@ void decode_advance(const Tensor& out_ids, const Tensor& ids, const Tensor& pos,
                      (int)block_size, stream());
 }
 
+// ---------------------------------------------------------------- DSA selection
+void paged_slots(const Tensor& block_table, const Tensor& lens, const c10::optional<Tensor>& positions,
+                 int64_t rows, int64_t block_size, const Tensor& slots) {
+  CHECK_CUDA(block_table); CHECK_I32(block_table); CHECK_I32(lens); CHECK_I32(slots); CHECK_CONTIG(block_table);
+  const int64_t B = block_table.size(0);
+  TORCH_CHECK(lens.numel() >= B && slots.numel() >= B * rows, "paged_slots: lengths / output too small");
+  const int* pp = nullptr;
+  if (positions.has_value()) {
+    CHECK_I32(*positions); CHECK_CONTIG(*positions);
+    TORCH_CHECK(positions->numel() >= B * rows, "paged_slots: positions too small");
+    pp = positions->data_ptr<int>();
+  }
+  const c10::cuda::CUDAGuard guard(block_table.device());
+  sp::paged_slots(block_table.data_ptr<int>(), (int)block_table.size(1), lens.data_ptr<int>(), pp, (int)B, (int)rows,
+                  (int)block_size, slots.data_ptr<int>(), stream());
+}
+
+void dsa_topk(const Tensor& raw, const Tensor& w, const Tensor& lens, int64_t topk, const Tensor& scores,
+              const Tensor& out, const Tensor& counts) {
+  CHECK_CUDA(raw); CHECK_F32(raw); CHECK_F32(w); CHECK_I32(lens); CHECK_F32(scores); CHECK_I32(out);
+  CHECK_I32(counts); CHECK_CONTIG(raw); CHECK_CONTIG(w); CHECK_CONTIG(scores); CHECK_CONTIG(out);
+  TORCH_CHECK(raw.dim() == 3, "dsa_topk: raw [B, heads, rows]");
+  const int64_t B = raw.size(0), Hi = raw.size(1), rows = raw.size(2);
+  TORCH_CHECK(w.numel() >= B * Hi && lens.numel() >= B && scores.numel() >= B * rows && out.numel() >= B * topk &&
+                  counts.numel() >= B,
+              "dsa_topk: operand too small");
+  const c10::cuda::CUDAGuard guard(raw.device());
+  sp::dsa_topk(raw.data_ptr<float>(), w.data_ptr<float>(), (int)B, (int)Hi, (int)rows, lens.data_ptr<int>(),
+               (int)topk, scores.data_ptr<float>(), out.data_ptr<int>(), counts.data_ptr<int>(), stream());
+}
+
 // ---------------------------------------------------------------- raw device memory
 // Untyped device allocations for native components that keep their own ledger
 // (stage modules): pointers cross as integers.
@@ -869,6 +900,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     }
     return out;
   });
+  m.def("paged_slots", &paged_slots);
+  m.def("dsa_topk", &dsa_topk);
   m.def("raw_alloc", &raw_alloc);
   m.def("raw_free", &raw_free);
   m.def("raw_zero", &raw_zero);

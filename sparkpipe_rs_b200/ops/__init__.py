@@ -511,3 +511,53 @@ def status_word() -> int:
 
 def clear_status() -> None:
     kernels().clear_status()
+
+
+# ------------------------------------------------------------------ DSA sparse attention
+def paged_slots(block_table, lens, rows, positions=None, block_size=64):
+    """Cache slot of positions [0, lens[b]) (or of ``positions[b, :lens[b]]``) of each
+    sequence through its block table, [B, rows] int32 (slot 0 past the length)."""
+    B = block_table.shape[0]
+    slots = torch.empty(B, rows, dtype=torch.int32, device=block_table.device)
+    kernels().paged_slots(block_table, lens, positions, int(rows), int(block_size), slots)
+    _count(1)
+    return slots
+
+
+def dsa_select(q_idx, w_idx, k_cache, block_table, context_lens, max_context, topk=2048, block_size=64):
+    """DeepSeek sparse attention token selection for one decode step.
+
+    q_idx [B, Hi, 128] bf16 index queries, w_idx [B, Hi] fp32 head weights, k_cache
+    [slots, 128] bf16 paged index keys, block_table / context_lens as for decode,
+    ``max_context`` an upper bound of the lengths. score[b, s] = sum_h w[b, h] *
+    relu(q[b, h] . k[s]); returns (positions [B, topk] int32: the topk best positions
+    of each sequence ascending, -1 padded; counts [B]). The q.k products run on the
+    tcgen05 GEMM over the gathered keys; reduce, radix select and sort in one kernel."""
+    B, Hi, D = q_idx.shape
+    rows = -(-int(max_context) // 8) * 8  # aligned score rows; positions past a length are masked
+    dev = q_idx.device
+    slots = paged_slots(block_table, context_lens, rows, block_size=block_size)
+    keys = gather_rows(k_cache, slots.view(-1))                       # [B * rows, 128]
+    raw = torch.empty(B, Hi, rows, dtype=torch.float32, device=dev)
+    batched_gemm(keys, q_idx.reshape(B * Hi, D), raw, M=rows, N=Hi, K=D, batch=B, a_batch_rows=rows,
+                 b_batch_rows=Hi, ldd=rows, d_batch_stride=Hi * rows)
+    scores = torch.empty(B, rows, dtype=torch.float32, device=dev)
+    pos = torch.empty(B, topk, dtype=torch.int32, device=dev)
+    counts = torch.empty(B, dtype=torch.int32, device=dev)
+    kernels().dsa_topk(raw, w_idx.float().contiguous(), context_lens, int(topk), scores, pos, counts)
+    _count(1)
+    return pos, counts
+
+
+def dsa_sparse_decode(q_lat, cache, block_table, positions, counts, out, scale, block_size=64):
+    """MLA decode over only the selected positions: their latent KV rows are gathered
+    into 64-token blocks and the paged decode kernel runs on them."""
+    B, topk = positions.shape
+    if topk % block_size:
+        raise ValueError("topk must be a multiple of the block size")
+    slots = paged_slots(block_table, counts, topk, positions=positions, block_size=block_size)
+    rows = gather_rows(cache, slots.view(-1))                         # [B * topk, 576]
+    nb = topk // block_size
+    bt = torch.arange(B * nb, dtype=torch.int32, device=q_lat.device).view(B, nb)
+    splits = mla_decode_splits(B, q_lat.shape[1], topk, kernels().num_sms())
+    return mla_decode(q_lat, rows, bt, counts, out, splits, scale)
