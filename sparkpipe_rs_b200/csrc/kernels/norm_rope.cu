@@ -248,8 +248,8 @@ __global__ void __launch_bounds__(128) mla_decode_prep_kernel(
     if (h >= H) break;
     const int c = (j % per_head) * 4;
     const float4 x = prep_load4(src, t, qoff + h * (dn + dr) + c);
-    if (c < dn) {
-      bf16* qn = q_nope_out + ((long long)t * H + h) * dn + c;
+    if (c < dn) {  // no q_nope_out: the nope part (absorbed, dn == kv_lora) goes to q_lat's latent columns
+      bf16* qn = q_nope_out ? q_nope_out + ((long long)t * H + h) * dn + c : q_lat + ((long long)t * H + h) * W + c;
       reinterpret_cast<__nv_bfloat162*>(qn)[0] = __floats2bfloat162_rn(x.x, x.y);
       reinterpret_cast<__nv_bfloat162*>(qn)[1] = __floats2bfloat162_rn(x.z, x.w);
     } else {
@@ -268,6 +268,8 @@ void mla_decode_prep(const float* slab, long long stride, int splits, const void
     throw std::runtime_error("mla_decode_prep: 4-aligned dims, kv_lora <= 1024 required");
   if (!slab && (lds % 4 || (reinterpret_cast<uintptr_t>(src) & 7)))
     throw std::runtime_error("mla_decode_prep: bf16 source rows must be 8-byte aligned");
+  if (!q_nope_out && dn != kv_lora)
+    throw std::runtime_error("mla_decode_prep: without a q_nope output the nope width must equal kv_lora");
   PrepSrc ps{slab, stride, splits < 1 ? 1 : splits, (const bf16*)src, lds, row_len};
   launch_k(mla_decode_prep_kernel, dim3(T, 1 + (H + 3) / 4), dim3(128), 0, s, ps, (const bf16*)norm_w, positions,
            cos_sin, slot_mapping, (bf16*)cache, (bf16*)q_nope_out, (bf16*)q_lat, H, dn, dr, kv_lora, q_off, kv_off,

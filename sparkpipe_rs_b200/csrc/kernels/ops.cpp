@@ -478,11 +478,16 @@ void slab_add_rmsnorm(const Tensor& slabs, int64_t stride, int64_t splits, const
 
 void mla_decode_prep(const c10::optional<Tensor>& slabs, int64_t stride, int64_t splits,
                      const c10::optional<Tensor>& src, const Tensor& norm_w, const Tensor& positions,
-                     const Tensor& cos_sin, const Tensor& slot_mapping, const Tensor& cache, const Tensor& q_nope_out,
-                     const Tensor& q_lat, int64_t T, int64_t dn, int64_t q_off, int64_t kv_off, int64_t row_len,
-                     double eps) {
-  CHECK_I32(positions); CHECK_F32(cos_sin); CHECK_I32(slot_mapping); CHECK_BF16(cache); CHECK_BF16(q_nope_out);
-  CHECK_BF16(q_lat); CHECK_CONTIG(q_nope_out); CHECK_CONTIG(q_lat);
+                     const Tensor& cos_sin, const Tensor& slot_mapping, const Tensor& cache,
+                     const c10::optional<Tensor>& q_nope_out, const Tensor& q_lat, int64_t T, int64_t dn,
+                     int64_t q_off, int64_t kv_off, int64_t row_len, double eps) {
+  CHECK_I32(positions); CHECK_F32(cos_sin); CHECK_I32(slot_mapping); CHECK_BF16(cache);
+  CHECK_BF16(q_lat); CHECK_CONTIG(q_lat);
+  void* qn = nullptr;
+  if (q_nope_out.has_value()) {
+    CHECK_BF16(*q_nope_out); CHECK_CONTIG(*q_nope_out);
+    qn = q_nope_out->data_ptr();
+  }
   const c10::cuda::CUDAGuard guard(q_lat.device());
   const float* sl = nullptr;
   const void* sr = nullptr;
@@ -493,7 +498,7 @@ void mla_decode_prep(const c10::optional<Tensor>& slabs, int64_t stride, int64_t
   const int H = (int)q_lat.size(1), W = (int)q_lat.size(2);
   const int kvl = (int)norm_w.size(0);
   sp::mla_decode_prep(sl, stride, (int)splits, sr, lds, norm_w.data_ptr(), positions.data_ptr<int>(),
-                      cos_sin.data_ptr<float>(), slot_mapping.data_ptr<int>(), cache.data_ptr(), q_nope_out.data_ptr(),
+                      cos_sin.data_ptr<float>(), slot_mapping.data_ptr<int>(), cache.data_ptr(), qn,
                       q_lat.data_ptr(), (int)T, H, (int)dn, W - kvl, kvl, (int)q_off, (int)kv_off, (int)row_len,
                       (float)eps, stream());
 }

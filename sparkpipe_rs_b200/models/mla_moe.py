@@ -17,6 +17,8 @@ RESTRICTED_LOGITS (crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_res
 """
 from __future__ import annotations
 
+import os
+
 from dataclasses import dataclass
 
 import torch
@@ -24,7 +26,7 @@ import torch
 from .. import ops
 from .config import MLAMoEConfig
 from .rope import cos_sin_table
-from .weights import derive_decode_weights, init_weights
+from .weights import absorb_decode_weights, derive_decode_weights, init_weights
 
 
 @dataclass
@@ -121,6 +123,8 @@ class MLAMoEModel:
         self.w = {k: (v if isinstance(v, ops.Fp8Weight) else v.to(self.device)) for k, v in weights.items()}
         del weights  # the re-laid-out expert weights below must not coexist with a second reference
         derive_decode_weights(cfg, self.w)
+        # latent up-projections folded into the decode projections (SPARKPIPE_ABSORB=0: the four-GEMM form)
+        self.absorbed = os.environ.get("SPARKPIPE_ABSORB", "1") != "0" and absorb_decode_weights(cfg, self.w)
         # routed + shared expert gate/up weights in the fused-SwiGLU tile order
         self.fused_swiglu = cfg.moe_intermediate_size % 64 == 0
         for i in range(cfg.num_layers):
@@ -177,6 +181,16 @@ class MLAMoEModel:
                              None, kvl, c.qk_rope_head_dim, c.rms_norm_eps)
             ops.rope_q(self._q_view(q, T), dn, q_lat, kvl, fb.positions, self.cos_sin, c.qk_rope_head_dim)
             q_src, q_batch_k = q, c.qk_head_dim
+        elif self.absorbed:
+            # absorbed form: the projection yields q_lat (latent + rope per head) and
+            # kv_a; one kernel sums its split-K slabs, writes q_lat with query RoPE and
+            # normalises / ropes / caches the latent KV
+            qkv = self._lin(xn, w[p + "w_qkv_abs"], slab=True)
+            ops.mla_decode_prep(qkv, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache,
+                                None, q_lat, kvl, 0, nh * c.kv_cache_dim, c.rms_norm_eps)
+            o_lat = torch.empty(T, nh, kvl, dtype=torch.bfloat16, device=self.device)
+            ops.mla_decode(q_lat, layer_cache, fb.block_table, fb.context_lens, o_lat, fb.decode_splits, self.scale)
+            return self._lin(o_lat.view(T, nh * kvl), w[p + "w_ov"], slab=True)
         else:
             # one kernel: split-K reduction of the q/kv projection, latent norm + RoPE
             # + cache write, query RoPE and the compact q_nope operand

@@ -160,3 +160,39 @@ def derive_decode_weights(cfg: MLAMoEConfig, w: dict[str, torch.Tensor]) -> None
             continue
         kvb = w[k].view(nh, dn + dv, kvl)
         w[f"l{i}.w_uk_t"] = kvb[:, :dn, :].transpose(1, 2).contiguous().view(nh * kvl, dn)
+
+
+def absorb_decode_weights(cfg: MLAMoEConfig, w: dict[str, torch.Tensor]) -> bool:
+    """Folds the latent up-projections into the decode projections (bf16 models
+    without a q LoRA), so decode attention needs two weight GEMMs instead of four:
+
+      l{i}.w_qkv_abs [Hh * (kv_lora + rope) + kv_lora + rope, H]: per head the
+          absorbed query rows W_uk[h] . W_q_nope[h] (kv_lora x H) followed by the
+          head's rope rows, then the kv_a rows: one GEMM yields q_lat directly.
+      l{i}.w_ov [H, Hh * kv_lora]: per head W_o[:, head] . W_uv[h]: the output
+          projection straight from the latent attention output.
+
+    Products in fp32, stored bf16. Returns False (and adds nothing) for other models."""
+    if cfg.q_lora_rank:
+        return False
+    nh, dn, dr, dv, kvl = cfg.num_heads, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
+    for i in range(cfg.num_layers):
+        p = f"l{i}."
+        if p + "w_qkv_a" not in w or not isinstance(w[p + "w_qkv_a"], torch.Tensor) or \
+                not isinstance(w.get(p + "w_o"), torch.Tensor) or w[p + "w_qkv_a"].dtype != torch.bfloat16:
+            return False
+    for i in range(cfg.num_layers):
+        p = f"l{i}."
+        wqa = w[p + "w_qkv_a"]
+        H = wqa.shape[1]
+        q = wqa[: nh * (dn + dr)].view(nh, dn + dr, H).float()
+        uk = w[p + "w_uk_t"].view(nh, kvl, dn).float()
+        q_abs = torch.bmm(uk, q[:, :dn, :])                                     # [nh, kvl, H]
+        rows = torch.cat([q_abs, q[:, dn:, :]], dim=1).reshape(nh * (kvl + dr), H)
+        w[p + "w_qkv_abs"] = torch.cat([rows.to(torch.bfloat16), wqa[nh * (dn + dr):]], dim=0).contiguous()
+        del q, q_abs, rows
+        uv = w[p + "w_kv_b"].view(nh, dn + dv, kvl)[:, dn:, :].float()           # [nh, dv, kvl]
+        wo = w[p + "w_o"].view(H, nh, dv).permute(1, 0, 2).float()               # [nh, H, dv]
+        w[p + "w_ov"] = torch.bmm(wo, uv).permute(1, 0, 2).reshape(H, nh * kvl).to(torch.bfloat16).contiguous()
+        del uv, wo
+    return True
