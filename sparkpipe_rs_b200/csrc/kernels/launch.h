@@ -243,7 +243,8 @@ void prefill_attention_tc(const PrefillAttnLaunch& l);
 // `logits` may be split-K slabs: the logits are sum_s logits[s * slab_stride + ...] over `splits`.
 void moe_topk(const float* logits, long long slab_stride, int splits, const float* bias, int* topk_ids, float* topk_w,
               int T, int E, int k, int n_shared, int scoring, int renorm, float scaling, int n_group, int topk_group,
-              int group_top2, cudaStream_t s);
+              int group_top2, cudaStream_t s, const void* gate_x = nullptr, long long ldx = 0,
+              const void* gate_w = nullptr, int H = 0);
 // res[t] += sum_j w[t, j] * y[inv_pos[t*k + j]]; out[t] = rmsnorm(res[t]) * gamma
 void combine_add_rmsnorm(const void* y, long long ldy, const int* inv_pos, const float* topk_w, void* residual,
                          const void* gamma, void* out, long long ldo, int T, int k, int H, float eps, cudaStream_t s);

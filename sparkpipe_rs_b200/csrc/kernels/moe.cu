@@ -1,6 +1,8 @@
 // Mixture-of-experts routing and token layout kernels, sm_100a.
 //
-//  * moe_topk     — router scores (softmax, or sigmoid with a selection bias as in
+//  * moe_topk     — router logits (from split-K slabs of the gate GEMM, or computed
+//                   in the kernel from the token row and the gate for small routers),
+//                   router scores (softmax, or sigmoid with a selection bias as in
 //                   the noaux_tc routers), top-k selection, optional renormalisation
 //                   and the routed scaling factor. Shared experts are appended as
 //                   always-selected experts E .. E+S-1 with weight 1, so they run
@@ -47,7 +49,8 @@ __global__ void __launch_bounds__(TOPK_THREADS)
     moe_topk_kernel(const float* __restrict__ logits, long long slab_stride, int splits,
                     const float* __restrict__ bias, int* __restrict__ ids, float* __restrict__ wts, int E, int k,
                     int n_shared, int scoring, int renorm, float scaling, int n_group, int topk_group,
-                    int group_top2) {
+                    int group_top2, const bf16* __restrict__ gx, long long ldx, const bf16* __restrict__ gw,
+                    int Hd) {
   __shared__ __align__(16) float s_part[TOPK_THREADS * 4 > TOPK_MAX_E ? TOPK_THREADS * 4 : TOPK_MAX_E];
   __shared__ float s_logit[TOPK_MAX_E];
   griddep_wait();
@@ -57,7 +60,55 @@ __global__ void __launch_bounds__(TOPK_THREADS)
   const int lane = tid & 31;
   const float* row = logits + (long long)t * E;
   const int nvec = E / VEC;
-  if (nvec <= TOPK_THREADS) {
+  if (gx) {
+    // fused router: logits = x[t] . gate[e] (bf16 in, fp32 accumulate). The token row
+    // is staged in shared memory; each warp takes two experts at a time and keeps
+    // four 16-byte gate loads per expert in flight (the rows come from L2), since a
+    // single dependent load chain per warp measured slower than the gate GEMM.
+    bf16* s_x = reinterpret_cast<bf16*>(s_part);  // Hd <= 2 * TOPK_THREADS * 4 = 2048 elements
+    const bf16* xr = gx + (long long)t * ldx;
+    for (int c = tid * 8; c < Hd; c += TOPK_THREADS * 8)
+      *reinterpret_cast<uint4*>(s_x + c) = *reinterpret_cast<const uint4*>(xr + c);
+    __syncthreads();
+    for (int e0 = (tid >> 5) * 2; e0 < E; e0 += TOPK_THREADS / 32 * 2) {
+      const bf16* w0 = gw + (long long)e0 * Hd;
+      const bf16* w1 = gw + (long long)min(e0 + 1, E - 1) * Hd;
+      float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int c0 = lane * 8; c0 < Hd; c0 += 4 * 256) {
+        uint4 p[4], q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u * 256;
+          if (c < Hd) {
+            p[u] = __ldg(reinterpret_cast<const uint4*>(w0 + c));
+            q[u] = __ldg(reinterpret_cast<const uint4*>(w1 + c));
+          } else {
+            p[u] = q[u] = make_uint4(0, 0, 0, 0);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u * 256;
+          if (c >= Hd) continue;
+          float xv[8], pv[8], qv[8];
+          ld_bf16x8(s_x + c, xv);
+          ld_bf16x8(reinterpret_cast<const bf16*>(&p[u]), pv);
+          ld_bf16x8(reinterpret_cast<const bf16*>(&q[u]), qv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            acc0[u] = fmaf(xv[j], pv[j], acc0[u]);
+            acc1[u] = fmaf(xv[j], qv[j], acc1[u]);
+          }
+        }
+      }
+      const float l0 = warp_sum((acc0[0] + acc0[1]) + (acc0[2] + acc0[3]));
+      const float l1 = warp_sum((acc1[0] + acc1[1]) + (acc1[2] + acc1[3]));
+      if (lane == 0) {
+        s_logit[e0] = l0;
+        if (e0 + 1 < E) s_logit[e0 + 1] = l1;
+      }
+    }
+  } else if (nvec <= TOPK_THREADS) {
     const int G = TOPK_THREADS / nvec;
     const int g = tid / nvec, v = tid - g * nvec;
     if (g < G) {
@@ -205,7 +256,7 @@ __global__ void __launch_bounds__(TOPK_THREADS)
 
 void moe_topk(const float* logits, long long slab_stride, int splits, const float* bias, int* topk_ids, float* topk_w,
               int T, int E, int k, int n_shared, int scoring, int renorm, float scaling, int n_group, int topk_group,
-              int group_top2, cudaStream_t s) {
+              int group_top2, cudaStream_t s, const void* gate_x, long long ldx, const void* gate_w, int H) {
   if (T <= 0) return;
   if (E > TOPK_MAX_E) throw std::runtime_error("moe_topk: at most 512 experts");
   if (k + n_shared > 32) throw std::runtime_error("moe_topk: k + shared <= 32");
@@ -216,13 +267,25 @@ void moe_topk(const float* logits, long long slab_stride, int splits, const floa
     if (topk_group * (E / n_group) < k) throw std::runtime_error("moe_topk: kept groups hold fewer than k experts");
   }
   splits = splits < 1 ? 1 : splits;
+  if (gate_x) {
+    if (H > TOPK_THREADS * 4 * 2) throw std::runtime_error("moe_topk: fused router supports hidden <= 2048");
+    if (!gate_w || H % 8 || ldx % 8 || (reinterpret_cast<uintptr_t>(gate_x) & 15) ||
+        (reinterpret_cast<uintptr_t>(gate_w) & 15))
+      throw std::runtime_error("moe_topk: fused router needs 16-byte aligned rows, hidden % 8 == 0");
+    launch_k(moe_topk_kernel<1>, dim3(T), dim3(TOPK_THREADS), 0, s, (const float*)nullptr, 0ll, 1, bias, topk_ids,
+             topk_w, E, k, n_shared, scoring, renorm, scaling, n_group, topk_group, group_top2, (const bf16*)gate_x,
+             ldx, (const bf16*)gate_w, H);
+    return;
+  }
   const bool vec4 = E % 4 == 0 && (splits == 1 || slab_stride % 4 == 0) && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
   if (vec4)
     launch_k(moe_topk_kernel<4>, dim3(T), dim3(TOPK_THREADS), 0, s, logits, slab_stride, splits, bias, topk_ids,
-             topk_w, E, k, n_shared, scoring, renorm, scaling, n_group, topk_group, group_top2);
+             topk_w, E, k, n_shared, scoring, renorm, scaling, n_group, topk_group, group_top2, (const bf16*)nullptr,
+             0ll, (const bf16*)nullptr, 0);
   else
     launch_k(moe_topk_kernel<1>, dim3(T), dim3(TOPK_THREADS), 0, s, logits, slab_stride, splits, bias, topk_ids,
-             topk_w, E, k, n_shared, scoring, renorm, scaling, n_group, topk_group, group_top2);
+             topk_w, E, k, n_shared, scoring, renorm, scaling, n_group, topk_group, group_top2, (const bf16*)nullptr,
+             0ll, (const bf16*)nullptr, 0);
 }
 
 // ---------------------------------------------------------------- align

@@ -467,6 +467,22 @@ void moe_topk(const Tensor& logits, const c10::optional<Tensor>& bias, const Ten
                (int)n_group, (int)topk_group, group_top2 ? 1 : 0, stream());
 }
 
+// Router top-k with the logits computed in the kernel: x [T, H] bf16, gate [E, H] bf16.
+void moe_route(const Tensor& x, const Tensor& gate, const c10::optional<Tensor>& bias, const Tensor& ids,
+               const Tensor& w, int64_t n_shared, int64_t scoring, bool renorm, double scaling, int64_t n_group,
+               int64_t topk_group, bool group_top2) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(gate); CHECK_CONTIG(gate); CHECK_I32(ids); CHECK_F32(w);
+  TORCH_CHECK(x.stride(1) == 1 && x.size(1) == gate.size(1), "moe_route: x [T, H] and gate [E, H]");
+  TORCH_CHECK(ids.size(0) >= x.size(0) && w.size(0) >= x.size(0), "moe_route: outputs too small");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const float* b = nullptr;
+  if (bias.has_value()) { CHECK_F32(*bias); b = bias->data_ptr<float>(); }
+  sp::moe_topk(nullptr, 0, 1, b, ids.data_ptr<int>(), w.data_ptr<float>(), (int)x.size(0), (int)gate.size(0),
+               (int)(ids.size(1) - n_shared), (int)n_shared, (int)scoring, renorm ? 1 : 0, (float)scaling,
+               (int)n_group, (int)topk_group, group_top2 ? 1 : 0, stream(), x.data_ptr(), x.stride(0),
+               gate.data_ptr(), (int)x.size(1));
+}
+
 void slab_add_rmsnorm(const Tensor& slabs, int64_t stride, int64_t splits, const Tensor& residual, const Tensor& w,
                       const Tensor& out, double eps) {
   CHECK_CUDA(slabs); CHECK_F32(slabs); CHECK_BF16(residual); CHECK_CONTIG(residual); CHECK_BF16(w); CHECK_BF16(out);
@@ -905,6 +921,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     }
     return out;
   });
+  m.def("moe_route", &moe_route);
   m.def("paged_slots", &paged_slots);
   m.def("dsa_topk", &dsa_topk);
   m.def("raw_alloc", &raw_alloc);

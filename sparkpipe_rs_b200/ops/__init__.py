@@ -385,6 +385,18 @@ def prefill_attention(q, k, kpe, v, o, cu_q, cu_k, max_q, scale, causal=True, im
     return o
 
 
+def moe_route(x, gate, bias, k, scoring, renorm, scaling, n_shared=0, n_group=1, topk_group=1, group_top2=False):
+    """``moe_topk`` with the router logits x @ gate.T computed inside the kernel
+    (decode-sized batches of small routers: no separate gate GEMM)."""
+    T = x.shape[0]
+    ids = torch.empty(T, k + n_shared, dtype=torch.int32, device=x.device)
+    w = torch.empty(T, k + n_shared, dtype=torch.float32, device=x.device)
+    kernels().moe_route(x, gate, bias, ids, w, int(n_shared), int(scoring), bool(renorm), float(scaling),
+                        int(n_group), int(topk_group), bool(group_top2))
+    _count(1)
+    return ids, w
+
+
 def moe_topk(logits, bias, k, scoring, renorm, scaling, n_shared=0, n_group=1, topk_group=1, group_top2=False):
     """Top-k routing; the last n_shared columns are the shared experts E.. (weight 1).
     ``logits`` is a [T, E] fp32 tensor or router ``Slabs``. With n_group > 1 the

@@ -444,3 +444,26 @@ def test_combine_add_rmsnorm_matches_unfused():
     ops.add_rmsnorm(comb, r2, gamma, o2, 1e-6)
     _close(r1, r2, atol=2e-2, rtol=2e-2)
     _close(o1, o2)
+
+
+@pytest.mark.parametrize("scoring,E,k,groups", [(0, 64, 6, None), (1, 256, 8, (8, 4, "noaux_tc"))])
+def test_moe_route_fused_matches_gemm_router(scoring, E, k, groups):
+    """The router with its logits computed inside the top-k kernel selects like the
+    gate GEMM + top-k path, with the same weights."""
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(E + k)
+    T, H = 64, 2048
+    x = torch.randn(T, H, device=DEV, generator=g).bfloat16()
+    gate = (torch.randn(E, H, device=DEV, generator=g) * 0.05).bfloat16()
+    bias = torch.randn(E, device=DEV, generator=g) * 0.1 if scoring == 1 else None
+    ng, tg, method = groups or (1, 1, "greedy")
+    kw = dict(n_shared=2, n_group=ng, topk_group=tg, group_top2=method == "noaux_tc")
+    ids, w = ops.moe_route(x, gate, bias, k, scoring, True, 2.5, **kw)
+    logits = x.float() @ gate.float().t()
+    ids2, w2 = ops.moe_topk(logits, bias, k, scoring, True, 2.5, **kw)
+    assert torch.equal(ids[:, :k].sort(-1).values, ids2[:, :k].sort(-1).values)
+    assert torch.equal(ids[:, k:], ids2[:, k:])
+    order = ids[:, :k].sort(-1).indices
+    order2 = ids2[:, :k].sort(-1).indices
+    _close(w[:, :k].gather(1, order), w2[:, :k].gather(1, order2), atol=1e-4, rtol=1e-3)
+    _status_ok()
