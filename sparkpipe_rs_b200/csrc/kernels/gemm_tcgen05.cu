@@ -692,9 +692,12 @@ int gemm_bf16(const GemmLaunch& g) {
   int splits = g.splits;
   const int kbs = (g.K + BK - 1) / BK;
   if (splits <= 0) {
-    // Auto: split K until the grid covers the SMs (two split CTAs fit per SM).
-    splits = 1;
-    while (splits < 8 && p.num_tiles * splits * 2 <= 2 * g.num_sms && kbs / (splits * 2) >= 2) splits *= 2;
+    // Auto: the most splits that keep one CTA per SM (tiles x splits <= SMs), at
+    // least two K blocks per split, at most 16. Each SM streams its own share of
+    // the weights: two CTAs on some SMs and one on others leaves the doubled SMs as
+    // the tail. (64 x 3648 x 2048: 5 splits, 145 CTAs; the old power-of-two rule
+    // chose 8 splits, 232 CTAs.)
+    splits = std::max(1, std::min({g.num_sms / std::max(1, p.num_tiles), kbs / 2, 16}));
   }
   if (splits > kbs) splits = kbs;  // every split CTA needs at least one K block
   if (g.tp && g.tp->rs) {
