@@ -635,8 +635,8 @@ int gemm_fp8(const Fp8Launch& g) {
   const int kbs = g.K / F8_BK;
   int splits = g.splits;
   if (splits <= 0) {
-    splits = 1;
-    while (splits < 16 && p.num_tiles * splits * 2 <= 2 * g.num_sms && kbs / (splits * 2) >= 2) splits *= 2;
+    // the most splits that keep one CTA per SM, at least two K blocks each (as the bf16 GEMM)
+    splits = std::max(1, std::min({g.num_sms / std::max(1, p.num_tiles), kbs / 2, 16}));
   }
   if (splits > kbs) splits = kbs;
   const long long slab = (long long)g.M * g.N;

@@ -30,6 +30,8 @@ def main():
     ap.add_argument("--rows", type=int, default=16384)
     ap.add_argument("--k", type=int, default=7168)
     ap.add_argument("--ffn", type=int, default=2048)
+    ap.add_argument("--splits", default="0", help="split-K settings of the dense GEMMs (0 = automatic)")
+    ap.add_argument("--no-grouped", action="store_true")
     args = ap.parse_args()
     from sparkpipe_rs_b200 import ops
 
@@ -42,15 +44,18 @@ def main():
         xq = ops.quant_act_fp8(x)
         out = torch.empty(T, O, device=dev, dtype=torch.bfloat16)
         flops = 2.0 * T * O * K
-        us = time_fn(lambda i: ops.linear_fp8(xq, ws[i % n_pool], out=out), args.iters)
-        print(f"linear_fp8 T={T:5d} O={O:6d} K={K:6d}: {us:9.2f} us  {wbytes / us / 1e6:6.2f} TB/s of weights  "
-              f"{flops / us / 1e6:8.1f} TFLOP/s", flush=True)
+        for sp in [int(v) for v in args.splits.split(",")]:
+            us = time_fn(lambda i: ops.linear_fp8(xq, ws[i % n_pool], out=out, splits=sp), args.iters)
+            print(f"linear_fp8 T={T:5d} O={O:6d} K={K:6d} splits={sp}: {us:9.2f} us  "
+                  f"{wbytes / us / 1e6:6.2f} TB/s of weights  {flops / us / 1e6:8.1f} TFLOP/s", flush=True)
         wb = [torch.randn(O, K, device=dev).mul_(0.02).bfloat16() for _ in range(max(1, n_pool // 2))]
         us = time_fn(lambda i: torch.matmul(x, wb[i % len(wb)].t(), out=out), args.iters)
         print(f"torch.matmul bf16 (cuBLAS) T={T:5d} O={O:6d} K={K:6d}: {us:9.2f} us  "
               f"{flops / us / 1e6:8.1f} TFLOP/s", flush=True)
         del ws, wb
         torch.cuda.empty_cache()
+    if args.no_grouped:
+        return
     # grouped expert gate/up GEMM with fused SwiGLU
     E, R, K, F = args.experts, args.rows, args.k, args.ffn
     flat = ops.quant_weight_fp8(E * 2 * F, K, seed=1, device=dev)
