@@ -269,6 +269,9 @@ void sample_tokens(const void* logits, long long ldl, int T, int V, float temper
                    unsigned long long offset, int* out_ids, float* out_logit, const float* row_temp,
                    const unsigned long long* row_key, cudaStream_t s);
 void gather_prev_tokens(int* ids, const int* prev, int n, int prev_rows, cudaStream_t s);
+// NVFP4 (E2M1 values, E4M3 scale per 16, FP32 tensor scale) rows to bf16
+void dequant_nvfp4(const uint8_t* packed, const uint8_t* scales, float tensor_scale, long long elements, void* out,
+                   cudaStream_t s);
 // Greedy speculative verification over a chain of L drafts per row.
 // target: [B, L+1] argmax tokens of the verifier; draft: [B, L].
 // forced_accept_p > 0 replaces the token comparison by a seeded Bernoulli(p).

@@ -1,0 +1,62 @@
+// NVFP4 weight storage for sm_100a: 4-bit E2M1 values in 16-element blocks, one
+// FP8 E4M3 scale per block and one FP32 scale per tensor
+// (x = e2m1 * e4m3_block_scale * tensor_scale). Two values per byte, element 2i in
+// the low nibble. This file expands NVFP4 rows to bf16: one thread per 16-element
+// block (8 packed bytes in, 32 bf16 bytes out, both 16-byte aligned), so a row of K
+// elements is K/16 independent threads and the kernel runs at copy bandwidth.
+//
+// Reference: the NVFP4 expert path named in crates/spark-abi/vendor/sparkpipe (b12x
+// packs, QUANTIZATION_NVFP4_4BIT in crates/spark-node/src/rank_daemon/ring_runtime.rs:85);
+// the format is the published NVFP4 layout, the kernel is this framework's own.
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+
+#include "common.cuh"
+#include "launch.h"
+#include "pdl.h"
+
+namespace sp {
+
+namespace {
+// E2M1 magnitudes by 3-bit code; bit 3 is the sign
+__constant__ float kE2m1[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+}
+
+__global__ void dequant_nvfp4_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ scales,
+                                     float tensor_scale, long long blocks, __nv_bfloat16* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
+  const long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= blocks) return;
+  const uint2 q = reinterpret_cast<const uint2*>(packed)[b];
+  __nv_fp8_e4m3 s8;
+  s8.__x = scales[b];
+  const float s = float(s8) * tensor_scale;
+  uint32_t words[2] = {q.x, q.y};
+  __align__(16) __nv_bfloat16 v[16];
+#pragma unroll
+  for (int w = 0; w < 2; ++w)
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const uint32_t code = (words[w] >> (4 * n)) & 0xf;
+      const float mag = kE2m1[code & 7] * s;
+      v[w * 8 + n] = __float2bfloat16(code & 8 ? -mag : mag);
+    }
+  uint4* o = reinterpret_cast<uint4*>(out + b * 16);
+  o[0] = reinterpret_cast<const uint4*>(v)[0];
+  o[1] = reinterpret_cast<const uint4*>(v)[1];
+}
+
+void dequant_nvfp4(const uint8_t* packed, const uint8_t* scales, float tensor_scale, long long elements, void* out,
+                   cudaStream_t s) {
+  if (elements <= 0) return;
+  if (elements % 16) throw std::runtime_error("dequant_nvfp4: element count must be a multiple of 16");
+  const long long blocks = elements / 16;
+  launch_k(dequant_nvfp4_kernel, dim3((unsigned)((blocks + 255) / 256)), dim3(256), 0, s, packed, scales, tensor_scale,
+           blocks, reinterpret_cast<__nv_bfloat16*>(out));
+}
+
+}  // namespace sp

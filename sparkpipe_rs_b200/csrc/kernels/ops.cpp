@@ -609,6 +609,18 @@ void gather_prev_tokens(const Tensor& ids, const Tensor& prev, int64_t n) {
   sp::gather_prev_tokens(ids.data_ptr<int>(), prev.data_ptr<int>(), (int)n, (int)prev.numel(), stream());
 }
 
+void dequant_nvfp4(const Tensor& packed, const Tensor& scales, double tensor_scale, const Tensor& out) {
+  CHECK_CUDA(packed); CHECK_CONTIG(packed); CHECK_CONTIG(scales); CHECK_CONTIG(out);
+  TORCH_CHECK(packed.scalar_type() == at::kByte && scales.scalar_type() == at::kByte, "dequant_nvfp4: uint8 inputs");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16, "dequant_nvfp4: bf16 output");
+  TORCH_CHECK(out.numel() == packed.numel() * 2 && out.numel() == scales.numel() * 16, "dequant_nvfp4: sizes");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(packed.data_ptr()) % 8 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "dequant_nvfp4: alignment");
+  const c10::cuda::CUDAGuard guard(packed.device());
+  sp::dequant_nvfp4(packed.data_ptr<uint8_t>(), scales.data_ptr<uint8_t>(), (float)tensor_scale, out.numel(),
+                    out.data_ptr(), stream());
+}
+
 void spec_verify(const Tensor& draft, const Tensor& target, double p_accept, int64_t seed, int64_t offset,
                  const Tensor& accepted, const Tensor& committed) {
   CHECK_CUDA(draft); CHECK_I32(draft); CHECK_I32(target); CHECK_I32(accepted); CHECK_I32(committed);
@@ -885,6 +897,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &embedding);
   m.def("sample_tokens", &sample_tokens);
   m.def("gather_prev_tokens", &gather_prev_tokens);
+  m.def("dequant_nvfp4", &dequant_nvfp4);
   m.def("spec_verify", &spec_verify);
   m.def("decode_advance", &decode_advance);
   m.def("spec_finish", &spec_finish);
