@@ -21,9 +21,16 @@
 namespace sp {
 
 namespace {
-// E2M1 magnitudes by 3-bit code; bit 3 is the sign
-__constant__ float kE2m1[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+// E2M1 nibble -> float from the format's fields, no table: bit 3 sign, bits 2..1
+// exponent (bias 1), bit 0 mantissa. Exponent 0 is the subnormal 0 / 0.5; otherwise
+// (1 + m/2) * 2^(e-1), whose fp32 pattern is exponent e + 126 and mantissa bit 22.
+// (A __constant__ table indexed per lane serialises on the constant cache.)
+SP_DEVI float e2m1_to_float(uint32_t code) {
+  const uint32_t e = (code >> 1) & 3u, m = code & 1u;
+  const float mag = e ? __uint_as_float(((e + 126u) << 23) | (m << 22)) : (m ? 0.5f : 0.f);
+  return (code & 8u) ? -mag : mag;
 }
+}  // namespace
 
 __global__ void dequant_nvfp4_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ scales,
                                      float tensor_scale, long long blocks, __nv_bfloat16* __restrict__ out) {
@@ -41,9 +48,7 @@ __global__ void dequant_nvfp4_kernel(const uint8_t* __restrict__ packed, const u
   for (int w = 0; w < 2; ++w)
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
-      const uint32_t code = (words[w] >> (4 * n)) & 0xf;
-      const float mag = kE2m1[code & 7] * s;
-      v[w * 8 + n] = __float2bfloat16(code & 8 ? -mag : mag);
+      v[w * 8 + n] = __float2bfloat16(e2m1_to_float((words[w] >> (4 * n)) & 0xf) * s);
     }
   uint4* o = reinterpret_cast<uint4*>(out + b * 16);
   o[0] = reinterpret_cast<const uint4*>(v)[0];
