@@ -42,13 +42,28 @@ __global__ void dequant_nvfp4_kernel(const uint8_t* __restrict__ packed, const u
   __nv_fp8_e4m3 s8;
   s8.__x = scales[b];
   const float s = float(s8) * tensor_scale;
-  uint32_t words[2] = {q.x, q.y};
-  __align__(16) __nv_bfloat16 v[16];
+  // The block's 16 values share one scale, so the 8 scaled magnitudes are rounded to
+  // bf16 once and kept as a 16-byte table in two 64-bit registers; each value is then a
+  // shift out of the table plus the sign bit (bf16 rounding is symmetric, so
+  // -round(m * s) == round(-m * s)).
+  uint64_t lo = 0, hi = 0;
+#pragma unroll
+  for (uint32_t k = 0; k < 4; ++k) {
+    lo |= uint64_t(__bfloat16_as_ushort(__float2bfloat16(e2m1_to_float(k) * s))) << (16 * k);
+    hi |= uint64_t(__bfloat16_as_ushort(__float2bfloat16(e2m1_to_float(k + 4) * s))) << (16 * k);
+  }
+  auto bits = [&](uint32_t c) -> uint32_t {
+    const uint64_t t = (c & 4u) ? hi : lo;
+    return (uint32_t(t >> ((c & 3u) * 16u)) & 0xffffu) | ((c & 8u) << 12);
+  };
+  const uint32_t words[2] = {q.x, q.y};
+  __align__(16) uint32_t v[8];
 #pragma unroll
   for (int w = 0; w < 2; ++w)
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      v[w * 8 + n] = __float2bfloat16(e2m1_to_float((words[w] >> (4 * n)) & 0xf) * s);
+    for (int n = 0; n < 4; ++n) {
+      const uint32_t pair = words[w] >> (8 * n);
+      v[w * 4 + n] = bits(pair & 0xfu) | (bits((pair >> 4) & 0xfu) << 16);
     }
   uint4* o = reinterpret_cast<uint4*>(out + b * 16);
   o[0] = reinterpret_cast<const uint4*>(v)[0];
