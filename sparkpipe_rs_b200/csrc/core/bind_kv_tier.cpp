@@ -21,9 +21,9 @@ static BindRegistrar reg([](py::module_& m) {
   k.attr("STATE_BLOCK") = kvt::kStateBlock;
   k.attr("GET") = uint32_t(kvt::Get);
   k.attr("PUT") = uint32_t(kvt::Put);
-  k.attr("IDLE") = uint32_t(kvt::Idle);
-  k.attr("SUBMITTED") = uint32_t(kvt::Submitted);
-  k.attr("READY") = uint32_t(kvt::Ready);
+  k.attr("FREE") = uint32_t(kvt::Free);
+  k.attr("IN_FLIGHT") = uint32_t(kvt::InFlight);
+  k.attr("LANDED") = uint32_t(kvt::Landed);
   k.def("format_key", &kvt::format_key);
   k.def("normalize_lookahead", &kvt::normalize_lookahead);
   k.def("select_lookahead", &kvt::select_lookahead);
@@ -82,12 +82,14 @@ static BindRegistrar reg([](py::module_& m) {
              return l;
            }),
            py::arg("sequence"), py::arg("blocks"), py::arg("state_nonresident") = false);
-  py::class_<kvt::BatchState>(k, "BatchState")
-      .def(py::init<>())
-      .def_readonly("batch_id", &kvt::BatchState::batch_id)
-      .def_property_readonly("status", [](const kvt::BatchState& b) { return uint32_t(b.status); })
-      .def_readonly("phase", &kvt::BatchState::phase)
-      .def_readonly("submitted_blocks", &kvt::BatchState::submitted_blocks);
+  py::enum_<kvt::Direction>(k, "Direction")
+      .value("RESTORE", kvt::Direction::Restore)
+      .value("EVICT", kvt::Direction::Evict);
+  py::class_<kvt::Channel>(k, "Channel")
+      .def_readonly("batch_id", &kvt::Channel::batch_id)
+      .def_readonly("stage", &kvt::Channel::stage)
+      .def_readonly("blocks", &kvt::Channel::blocks)
+      .def_property_readonly("outcome", [](const kvt::Channel& ch) { return uint32_t(ch.outcome); });
   py::class_<kvt::RestoreBatch>(k, "RestoreBatch")
       .def_readonly("blocks", &kvt::RestoreBatch::blocks)
       .def_readonly("lanes_built", &kvt::RestoreBatch::lanes_built)
@@ -95,20 +97,31 @@ static BindRegistrar reg([](py::module_& m) {
       .def_readonly("state_records", &kvt::RestoreBatch::state_records);
   k.def("state_block_equivalents", &kvt::state_block_equivalents);
   k.def("cumulative_nonresident", &kvt::cumulative_nonresident);
-  k.def("select_restore_packets", &kvt::select_restore_packets);
-  k.def("build_restore_batch",
-        [](const kvt::PlanConfig& c, const std::vector<kvt::PendingLane>& lanes, const std::vector<uint32_t>& counts,
-           uint64_t block_staging, uint32_t block_records, uint64_t state_staging, uint32_t state_records,
-           uint32_t capacity) {
-          return kvt::build_restore_batch(c, lanes, counts, addr(block_staging), block_records, addr(state_staging),
-                                          state_records, capacity);
-        });
-  k.def("build_evict_batch",
-        [](const kvt::PlanConfig& c, uint64_t seq, const std::vector<uint32_t>& resident, bool state,
-           uint64_t block_staging, uint64_t state_staging, uint32_t capacity) {
-          return kvt::build_evict_batch(c, seq, resident, state, addr(block_staging), addr(state_staging), capacity);
-        });
-  k.def("submit_batch", &kvt::submit_batch);
-  k.def("progress", &kvt::progress);
-  k.def("acknowledge", &kvt::acknowledge);
+  py::class_<kvt::TierMover>(k, "TierMover")
+      .def(py::init([](const kvt::PlanConfig& c, kvt::StageKvClient& client, uint64_t block_staging,
+                       uint32_t block_records, uint64_t state_staging, uint32_t state_records,
+                       uint32_t batch_blocks) {
+             kvt::Staging s;
+             s.blocks = addr(block_staging);
+             s.block_records = block_records;
+             s.states = addr(state_staging);
+             s.state_records = state_records;
+             s.batch_blocks = batch_blocks;
+             return new kvt::TierMover(c, client, s);
+           }),
+           py::arg("plan"), py::arg("client"), py::arg("block_staging"), py::arg("block_records"),
+           py::arg("state_staging"), py::arg("state_records"), py::arg("batch_blocks"),
+           py::keep_alive<1, 3>())
+      .def("restore_packets", &kvt::TierMover::restore_packets)
+      .def("plan_restore", &kvt::TierMover::plan_restore)
+      .def("plan_evict",
+           [](const kvt::TierMover& m, uint64_t seq, const std::vector<uint32_t>& resident, bool state,
+              uint64_t block_src, uint64_t state_src) {
+             return m.plan_evict(seq, resident, state, addr(block_src), addr(state_src));
+           })
+      .def("start", &kvt::TierMover::start)
+      .def("poll", &kvt::TierMover::poll)
+      .def("channel", &kvt::TierMover::channel, py::return_value_policy::copy)
+      .def("collect", [](kvt::TierMover& m, kvt::Direction d) { return uint32_t(m.collect(d)); })
+      .def("set_pressure", &kvt::TierMover::set_pressure);
 });

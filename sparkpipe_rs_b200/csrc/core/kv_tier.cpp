@@ -143,23 +143,7 @@ Status StageKvClient::poll(uint64_t batch_id, Completion& out) {
   return s;
 }
 
-// ---------------------------------------------------------------- work control
-static void check_plan(const PlanConfig& c) {
-  if (!c.model_fp || !c.layout_fp || !c.block_bytes || !c.state_bytes)
-    fail(Status::InvalidArgument, "work control: fingerprints and record sizes must be non-zero");
-}
-
-static Block make_block(const PlanConfig& c, uint64_t seq, uint32_t logical, uint32_t op, uint8_t* payload,
-                        uint32_t bytes) {
-  if (!seq || !payload || !bytes) fail(Status::InvalidArgument, "work control: block");
-  Block b;
-  b.op = op;
-  b.key = format_key(c.model_fp, c.layout_fp, c.rank, seq, logical);
-  b.payload = payload;
-  b.bytes = bytes;
-  return b;
-}
-
+// ---------------------------------------------------------------- tier mover
 uint32_t state_block_equivalents(uint32_t state_bytes, uint32_t block_bytes) {
   if (!state_bytes || !block_bytes) return 0;
   return (state_bytes + block_bytes - 1) / block_bytes;
@@ -168,110 +152,147 @@ uint32_t state_block_equivalents(uint32_t state_bytes, uint32_t block_bytes) {
 std::vector<uint32_t> cumulative_nonresident(const std::vector<PendingLane>& lanes,
                                              const std::vector<uint32_t>& packet_lane_counts,
                                              uint32_t state_equivalents) {
-  if (lanes.empty() || packet_lane_counts.empty()) fail(Status::InvalidArgument, "work control: empty plan");
-  std::vector<uint32_t> out;
-  uint64_t total = 0;
-  size_t li = 0;
+  if (lanes.empty() || packet_lane_counts.empty()) fail(Status::InvalidArgument, "tier mover: empty plan");
+  uint64_t covered = 0;
   for (uint32_t n : packet_lane_counts) {
-    if (n == 0 || n > lanes.size() - li) fail(Status::InvalidArgument, "work control: packet lane counts");
-    for (uint32_t k = 0; k < n; ++k) {
-      const PendingLane& l = lanes[li++];
-      if (!l.sequence) fail(Status::InvalidArgument, "work control: sequence id 0");
-      total += l.blocks.size() + (l.state_nonresident ? state_equivalents : 0);
-      if (total > 0xffffffffull) fail(Status::CapacityExceeded, "work control: block count overflow");
-    }
-    out.push_back(uint32_t(total));
+    if (n == 0) fail(Status::InvalidArgument, "tier mover: a packet without lanes");
+    covered += n;
   }
-  if (li != lanes.size()) fail(Status::InvalidArgument, "work control: lanes not covered by packets");
+  if (covered != lanes.size()) fail(Status::InvalidArgument, "tier mover: packet lane counts do not cover the lanes");
+  std::vector<uint32_t> out(packet_lane_counts.size());
+  uint64_t total = 0;
+  auto lane = lanes.begin();
+  for (size_t p = 0; p < packet_lane_counts.size(); ++p) {
+    for (auto end = lane + packet_lane_counts[p]; lane != end; ++lane) {
+      if (!lane->sequence) fail(Status::InvalidArgument, "tier mover: sequence id 0");
+      total += lane->blocks.size() + (lane->state_nonresident ? state_equivalents : 0);
+    }
+    if (total > 0xffffffffull) fail(Status::CapacityExceeded, "tier mover: block count overflow");
+    out[p] = uint32_t(total);
+  }
   return out;
 }
 
-uint32_t select_restore_packets(const PlanConfig& c, const std::vector<uint32_t>& cumulative) {
-  return select_lookahead(c.lookahead, uint32_t(cumulative.size()), c.physical_capacity, c.allocated,
-                          c.staging_capacity, cumulative);
+TierMover::TierMover(const PlanConfig& c, StageKvClient& client, const Staging& staging)
+    : cfg_(c), client_(client), st_(staging) {
+  if (!c.model_fp || !c.layout_fp || !c.block_bytes || !c.state_bytes)
+    fail(Status::InvalidArgument, "tier mover: fingerprints and record sizes must be non-zero");
+  if (!staging.blocks || !staging.states || !staging.block_records || !staging.batch_blocks)
+    fail(Status::InvalidArgument, "tier mover: staging area");
 }
 
-RestoreBatch build_restore_batch(const PlanConfig& c, const std::vector<PendingLane>& lanes,
-                                 const std::vector<uint32_t>& packet_lane_counts, uint8_t* block_staging,
-                                 uint32_t block_staging_records, uint8_t* state_staging,
-                                 uint32_t state_staging_records, uint32_t block_capacity) {
-  check_plan(c);
-  if (lanes.empty() || !block_staging || !state_staging || !block_capacity)
-    fail(Status::InvalidArgument, "work control: restore inputs");
-  uint64_t declared = 0;
-  for (uint32_t n : packet_lane_counts) declared += n;
-  if (declared != lanes.size()) fail(Status::InvalidArgument, "work control: packet lane counts");
+void TierMover::set_pressure(uint32_t physical_capacity, uint32_t allocated, uint32_t staging_capacity) {
+  cfg_.physical_capacity = physical_capacity;
+  cfg_.allocated = allocated;
+  cfg_.staging_capacity = staging_capacity;
+}
+
+uint32_t TierMover::restore_packets(const std::vector<uint32_t>& cumulative) const {
+  return select_lookahead(cfg_.lookahead, uint32_t(cumulative.size()), cfg_.physical_capacity, cfg_.allocated,
+                          cfg_.staging_capacity, cumulative);
+}
+
+Block TierMover::record(uint64_t sequence, uint32_t logical, uint32_t op, uint8_t* at, uint32_t bytes) const {
+  Block b;
+  b.op = op;
+  b.key = format_key(cfg_.model_fp, cfg_.layout_fp, cfg_.rank, sequence, logical);
+  b.payload = at;
+  b.bytes = bytes;
+  return b;
+}
+
+RestoreBatch TierMover::plan_restore(const std::vector<PendingLane>& lanes,
+                                     const std::vector<uint32_t>& packet_lane_counts) const {
+  if (lanes.empty()) fail(Status::InvalidArgument, "tier mover: nothing to restore");
+  uint64_t covered = 0;
+  for (uint32_t n : packet_lane_counts) covered += n;
+  if (covered != lanes.size()) fail(Status::InvalidArgument, "tier mover: packet lane counts do not cover the lanes");
+  // Prefix sums of the three resources a lane consumes; all three are monotone, so
+  // the lanes that fit are a prefix whose length is the smallest of three searches.
+  const size_t n = lanes.size();
+  std::vector<uint64_t> recs(n + 1, 0), blks(n + 1, 0), states(n + 1, 0);
+  for (size_t i = 0; i < n; ++i) {
+    if (!lanes[i].sequence) fail(Status::InvalidArgument, "tier mover: sequence id 0");
+    const uint32_t s = lanes[i].state_nonresident ? 1 : 0;
+    blks[i + 1] = blks[i] + lanes[i].blocks.size();
+    states[i + 1] = states[i] + s;
+    recs[i + 1] = recs[i] + lanes[i].blocks.size() + s;
+  }
+  auto fitting = [](const std::vector<uint64_t>& prefix, uint64_t cap) {
+    return size_t(std::upper_bound(prefix.begin() + 1, prefix.end(), cap) - (prefix.begin() + 1));
+  };
+  const size_t take = std::min({fitting(recs, st_.batch_blocks), fitting(blks, st_.block_records),
+                                fitting(states, st_.state_records)});
+  if (take == 0) fail(Status::CapacityExceeded, "tier mover: the first lane does not fit");
   RestoreBatch rb;
-  for (const PendingLane& l : lanes) {
-    if (!l.sequence) fail(Status::InvalidArgument, "work control: sequence id 0");
-    const uint32_t need = uint32_t(l.blocks.size()) + (l.state_nonresident ? 1 : 0);
-    const bool fits = need <= block_capacity - rb.blocks.size() &&
-                      l.blocks.size() <= block_staging_records - rb.block_records &&
-                      (!l.state_nonresident || rb.state_records < state_staging_records);
-    if (!fits) {
-      if (rb.lanes_built == 0) fail(Status::CapacityExceeded, "work control: the first lane does not fit");
-      break;
+  rb.lanes_built = uint32_t(take);
+  rb.block_records = uint32_t(blks[take]);
+  rb.state_records = uint32_t(states[take]);
+  rb.blocks.reserve(recs[take]);
+  for (size_t i = 0; i < take; ++i) {
+    const PendingLane& l = lanes[i];
+    if (l.state_nonresident)
+      rb.blocks.push_back(record(l.sequence, kStateBlock, Get, st_.states + states[i] * cfg_.state_bytes,
+                                 cfg_.state_bytes));
+    uint8_t* at = st_.blocks + blks[i] * cfg_.block_bytes;
+    for (uint32_t logical : l.blocks) {
+      rb.blocks.push_back(record(l.sequence, logical, Get, at, cfg_.block_bytes));
+      at += cfg_.block_bytes;
     }
-    if (l.state_nonresident) {
-      rb.blocks.push_back(make_block(c, l.sequence, kStateBlock, Get,
-                                     state_staging + uint64_t(rb.state_records) * c.state_bytes, c.state_bytes));
-      ++rb.state_records;
-    }
-    for (uint32_t blk : l.blocks) {
-      rb.blocks.push_back(make_block(c, l.sequence, blk, Get,
-                                     block_staging + uint64_t(rb.block_records) * c.block_bytes, c.block_bytes));
-      ++rb.block_records;
-    }
-    ++rb.lanes_built;
   }
   return rb;
 }
 
-std::vector<Block> build_evict_batch(const PlanConfig& c, uint64_t sequence, const std::vector<uint32_t>& resident,
-                                     bool include_state, uint8_t* block_staging, uint8_t* state_staging,
-                                     uint32_t block_capacity) {
-  check_plan(c);
-  if (!sequence || !block_staging || !state_staging) fail(Status::InvalidArgument, "work control: evict inputs");
-  const uint32_t n = uint32_t(resident.size()) + (include_state ? 1 : 0);
-  if (n == 0) fail(Status::InvalidArgument, "work control: nothing to evict");
-  if (n > block_capacity) fail(Status::CapacityExceeded, "work control: evict batch too large");
+std::vector<Block> TierMover::plan_evict(uint64_t sequence, const std::vector<uint32_t>& resident,
+                                         bool include_state, const uint8_t* block_src,
+                                         const uint8_t* state_src) const {
+  if (!sequence) fail(Status::InvalidArgument, "tier mover: sequence id 0");
+  const size_t n = resident.size() + (include_state ? 1 : 0);
+  if (n == 0) fail(Status::InvalidArgument, "tier mover: nothing to evict");
+  if (n > st_.batch_blocks) fail(Status::CapacityExceeded, "tier mover: evict batch too large");
+  if ((!resident.empty() && !block_src) || (include_state && !state_src))
+    fail(Status::InvalidArgument, "tier mover: evict source");
   std::vector<Block> out;
-  if (include_state) out.push_back(make_block(c, sequence, kStateBlock, Put, state_staging, c.state_bytes));
+  out.reserve(n);
+  if (include_state)
+    out.push_back(record(sequence, kStateBlock, Put, const_cast<uint8_t*>(state_src), cfg_.state_bytes));
   for (size_t i = 0; i < resident.size(); ++i)
-    out.push_back(make_block(c, sequence, resident[i], Put, block_staging + i * c.block_bytes, c.block_bytes));
+    out.push_back(record(sequence, resident[i], Put, const_cast<uint8_t*>(block_src) + i * cfg_.block_bytes,
+                         cfg_.block_bytes));
   return out;
 }
 
-void submit_batch(StageKvClient& client, BatchState& state, uint32_t op, const std::vector<Block>& blocks,
-                  uint32_t priority) {
-  if (priority > kPrioritySpeculative) fail(Status::InvalidArgument, "work control: priority");
-  if (state.phase != Idle) fail(Status::InvalidArgument, "work control: a batch is already outstanding");
-  state.batch_id = client.submit(op, blocks, priority);
-  state.status = Status::Pending;
-  state.phase = Submitted;
-  state.submitted_blocks = uint32_t(blocks.size());
+void TierMover::start(Direction d, const std::vector<Block>& blocks, uint32_t priority) {
+  if (priority > kPrioritySpeculative) fail(Status::InvalidArgument, "tier mover: priority");
+  Channel& ch = ch_[uint32_t(d)];
+  if (ch.stage != Free) fail(Status::InvalidArgument, "tier mover: the channel already carries a batch");
+  const uint32_t op = d == Direction::Restore ? Get : Put;
+  ch.batch_id = client_.submit(op, blocks, priority);
+  ch.blocks = uint32_t(blocks.size());
+  ch.outcome = Status::Pending;
+  ch.stage = InFlight;
 }
 
-static void progress_one(StageKvClient& client, BatchState& s) {
-  if (s.phase != Submitted) return;
-  Completion c;
-  const Status st = client.poll(s.batch_id, c);
-  if (st == Status::Pending || st == Status::Busy) return;
-  if (st != Status::Ok) fail(st, "work control: poll failed");
-  if (c.batch_id != s.batch_id || c.completed_blocks > s.submitted_blocks)
-    fail(Status::AbiMismatch, "work control: completion does not match the batch");
-  s.status = c.status;
-  s.phase = Ready;
+void TierMover::poll() {
+  for (Channel& ch : ch_) {
+    if (ch.stage != InFlight) continue;
+    Completion done;
+    const Status s = client_.poll(ch.batch_id, done);
+    if (s == Status::Pending || s == Status::Busy) continue;
+    if (s != Status::Ok) fail(s, "tier mover: poll failed");
+    if (done.batch_id != ch.batch_id || done.completed_blocks > ch.blocks)
+      fail(Status::AbiMismatch, "tier mover: completion does not match the batch");
+    ch.outcome = done.status;
+    ch.stage = Landed;
+  }
 }
 
-void progress(StageKvClient& client, BatchState& restore, BatchState& evict) {
-  progress_one(client, restore);
-  progress_one(client, evict);
-}
-
-void acknowledge(BatchState& state) {
-  if (state.phase != Ready) fail(Status::InvalidArgument, "work control: nothing to acknowledge");
-  state = BatchState{};
+Status TierMover::collect(Direction d) {
+  Channel& ch = ch_[uint32_t(d)];
+  if (ch.stage != Landed) fail(Status::InvalidArgument, "tier mover: no landed batch to collect");
+  const Status s = ch.outcome;
+  ch = Channel{};
+  return s;
 }
 
 }  // namespace kvt

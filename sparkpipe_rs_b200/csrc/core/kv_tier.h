@@ -16,16 +16,18 @@
 //                       within the normalised lookahead whose cumulative
 //                       non-resident blocks fit both the free physical blocks and
 //                       the staging capacity
-//   WorkControl         restore batches (GET: state record first, then the lane's
-//                       blocks, lanes whole or not at all), evict batches (PUT),
-//                       and the submit -> progress -> acknowledge state machine of
-//                       one restore and one evict batch
+//   TierMover           one restore (GET) and one evict (PUT) channel over the
+//                       client: restore batches take whole lanes (state record
+//                       first, then the lane's blocks), chosen by binary search
+//                       over the lanes' monotone record prefix sums; each channel
+//                       is Free -> InFlight -> Landed -> collected
 //
 // Reference behaviour: crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_kv_store.h
 // (constants, operations, completion contract), spark_stage_kv_client.h (client, key
-// binding), and V/model-families/qwen36/src/spark_qwen36_work_control.c (batch
-// building and state machine). The reference ships no store or client
-// implementation; these are this framework's own.
+// binding), and the Qwen 3.6 work control's batch rules
+// (V/model-families/qwen36/include/sparkpipe/spark_qwen36_work_control.h: lanes
+// whole, state record first, one restore and one evict batch outstanding). The
+// reference ships no store or client implementation; these are this framework's own.
 #pragma once
 
 #include <condition_variable>
@@ -127,7 +129,9 @@ class StageKvClient {
   std::map<uint64_t, bool> inflight_;
 };
 
-// ---------------------------------------------------------------- work control
+// ---------------------------------------------------------------- tier mover
+// Moves the KV of a model whose per-sequence state is paged KV blocks plus one
+// recurrent-state record between the device's staging area and the backing store.
 struct PlanConfig {
   uint64_t model_fp = 0, layout_fp = 0;
   uint32_t rank = 0, block_bytes = 0, state_bytes = 0;
@@ -140,13 +144,24 @@ struct PendingLane {
   bool state_nonresident = false;
 };
 
-enum BatchPhase : uint32_t { Idle = 0, Submitted = 1, Ready = 2 };
+// Host staging records: block records of block_bytes at `blocks`, state records of
+// state_bytes at `states`; `batch_blocks` caps the records of one batch.
+struct Staging {
+  uint8_t* blocks = nullptr;
+  uint32_t block_records = 0;
+  uint8_t* states = nullptr;
+  uint32_t state_records = 0;
+  uint32_t batch_blocks = 0;
+};
+
+enum class Direction : uint32_t { Restore = 0, Evict = 1 };
+enum ChannelStage : uint32_t { Free = 0, InFlight = 1, Landed = 2 };
 constexpr uint32_t kPriorityImmediate = 0, kPrioritySpeculative = 1;
 
-struct BatchState {
+struct Channel {
   uint64_t batch_id = 0;
-  Status status = Status::Ok;
-  uint32_t phase = Idle, submitted_blocks = 0;
+  uint32_t stage = Free, blocks = 0;
+  Status outcome = Status::Ok;
 };
 
 struct RestoreBatch {
@@ -155,24 +170,39 @@ struct RestoreBatch {
 };
 
 uint32_t state_block_equivalents(uint32_t state_bytes, uint32_t block_bytes);
+// Non-resident block counts summed packet by packet (a packet owns consecutive lanes).
 std::vector<uint32_t> cumulative_nonresident(const std::vector<PendingLane>& lanes,
                                              const std::vector<uint32_t>& packet_lane_counts,
                                              uint32_t state_equivalents);
-uint32_t select_restore_packets(const PlanConfig& c, const std::vector<uint32_t>& cumulative);
-// Staging: block records of block_bytes at block_staging, state records of state_bytes at
-// state_staging. Lanes are taken whole; the first lane that does not fit ends the batch
-// (CapacityExceeded if it is the first lane).
-RestoreBatch build_restore_batch(const PlanConfig& c, const std::vector<PendingLane>& lanes,
-                                 const std::vector<uint32_t>& packet_lane_counts, uint8_t* block_staging,
-                                 uint32_t block_staging_records, uint8_t* state_staging,
-                                 uint32_t state_staging_records, uint32_t block_capacity);
-std::vector<Block> build_evict_batch(const PlanConfig& c, uint64_t sequence, const std::vector<uint32_t>& resident,
-                                     bool include_state, uint8_t* block_staging, uint8_t* state_staging,
-                                     uint32_t block_capacity);
-void submit_batch(StageKvClient& client, BatchState& state, uint32_t op, const std::vector<Block>& blocks,
-                  uint32_t priority);
-void progress(StageKvClient& client, BatchState& restore, BatchState& evict);
-void acknowledge(BatchState& state);
+
+// One restore channel and one evict channel over a stage KV client. A restore takes
+// whole lanes in order, each lane's state record ahead of its blocks; the batch ends
+// before the first lane whose records would overflow the batch or either staging
+// area (CapacityExceeded when even the first lane does not fit).
+class TierMover {
+ public:
+  TierMover(const PlanConfig& c, StageKvClient& client, const Staging& staging);
+  // how many queued packets to restore ahead under the current memory pressure
+  uint32_t restore_packets(const std::vector<uint32_t>& cumulative) const;
+  RestoreBatch plan_restore(const std::vector<PendingLane>& lanes,
+                            const std::vector<uint32_t>& packet_lane_counts) const;
+  // Evicted bytes are read from the caller's buffers: resident[i] at block_src + i * block_bytes.
+  std::vector<Block> plan_evict(uint64_t sequence, const std::vector<uint32_t>& resident, bool include_state,
+                                const uint8_t* block_src, const uint8_t* state_src) const;
+  void start(Direction d, const std::vector<Block>& blocks, uint32_t priority);
+  void poll();                         // advances both channels; never blocks
+  const Channel& channel(Direction d) const { return ch_[uint32_t(d)]; }
+  Status collect(Direction d);         // outcome of a landed batch; frees the channel
+  const PlanConfig& plan() const { return cfg_; }
+  void set_pressure(uint32_t physical_capacity, uint32_t allocated, uint32_t staging_capacity);
+
+ private:
+  Block record(uint64_t sequence, uint32_t logical, uint32_t op, uint8_t* at, uint32_t bytes) const;
+  PlanConfig cfg_;
+  StageKvClient& client_;
+  Staging st_;
+  Channel ch_[2];
+};
 
 }  // namespace kvt
 }  // namespace spc

@@ -99,3 +99,66 @@ def test_seal_rejects_slots_larger_than_a_firing_and_low_latency_cannot_seal():
     with pytest.raises(StatusError) as e:
         _q().seal(0)
     assert e.value.code == UNSUPPORTED
+
+
+class _ScanModel:
+    """Plain model of the firing rule: scan slots in (layer, expert) order."""
+
+    def __init__(self, layers, experts, threshold, deadline, sealed_mode):
+        self.L, self.E, self.t, self.d, self.sm = layers, experts, threshold, deadline, sealed_mode
+        self.rows = {}
+        self.sealed = [False] * layers
+
+    def enqueue(self, l, e, rid, ts):
+        self.rows.setdefault((l, e), []).append((rid, ts))
+
+    def next(self, now):
+        for l in range(self.L):
+            for e in range(self.E):
+                r = self.rows.get((l, e), [])
+                if not r:
+                    continue
+                if self.sm:
+                    due = self.sealed[l]
+                else:
+                    due = len(r) >= self.t or (now >= r[0][1] and now - r[0][1] >= self.d)
+                if due:
+                    take = len(r) if self.sm else min(len(r), 1024)
+                    out, self.rows[(l, e)] = r[:take], r[take:]
+                    if self.sm and not any(self.rows.get((l, x)) for x in range(self.E)):
+                        self.sealed[l] = False
+                    return (l, e, [x[0] for x in out])
+        return None
+
+
+@pytest.mark.parametrize("mode", [LOW, SEALED])
+def test_random_operations_match_a_slot_scan(mode):
+    import random
+    rnd = random.Random(11 if mode == LOW else 12)
+    L, E, T, D = 3, 5, 4, 50
+    q, m = _q(mode=mode, layers=L, experts=E, threshold=T, deadline=D), _ScanModel(L, E, T, D, mode == SEALED)
+    now, rid = 0, 0
+    for _ in range(3000):
+        op = rnd.random()
+        now += rnd.randint(0, 7)
+        if op < 0.55:
+            l, e = rnd.randrange(L), rnd.randrange(E)
+            if mode == SEALED and m.sealed[l]:
+                with pytest.raises(StatusError):
+                    q.enqueue(l, e, rid, now)
+            else:
+                q.enqueue(l, e, rid, now)
+                m.enqueue(l, e, rid, now)
+            rid += 1
+        elif op < 0.65 and mode == SEALED:
+            l = rnd.randrange(L)
+            if not m.sealed[l] and any(m.rows.get((l, x)) for x in range(E)):
+                q.seal(l)
+                m.sealed[l] = True
+        elif op < 0.68 and mode == LOW:
+            m.t = rnd.randint(1, 8)
+            q.set_firing_threshold(m.t)
+        else:
+            assert q.next_firing(now) == m.next(now)
+    while (f := m.next(10 ** 18)) is not None:
+        assert q.next_firing(10 ** 18) == f

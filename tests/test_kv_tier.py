@@ -83,63 +83,108 @@ def _plan(**kw):
     return p
 
 
+def _mover(client, plan, block_records=8, state_records=2, batch=16):
+    bstage = np.zeros((max(block_records, 1), plan.block_bytes), np.uint8)
+    sstage = np.zeros((max(state_records, 1), plan.state_bytes), np.uint8)
+    m = K.TierMover(plan, client, bstage.ctypes.data, block_records, sstage.ctypes.data, state_records, batch)
+    return m, bstage, sstage
+
+
 def test_cumulative_counts_and_restore_selection():
     eq = K.state_block_equivalents(160, 64)
     assert eq == 3 and K.state_block_equivalents(0, 64) == 0
     lanes = [K.PendingLane(7, [0, 1], True), K.PendingLane(8, [4]), K.PendingLane(9, [2, 3, 5], True)]
     cum = K.cumulative_nonresident(lanes, [2, 1], eq)
     assert cum == [2 + 3 + 1, 6 + 3 + 3]
-    assert K.select_restore_packets(_plan(), cum) == 2          # room min(24 free, 16 staging): 6 and 12 fit
-    assert K.select_restore_packets(_plan(staging_capacity=8), cum) == 1
+    plan = _plan()
+    c = K.StageKvClient("memory", K.MemoryStore(), plan.rank, plan.model_fp, plan.layout_fp)
+    m, _, _ = _mover(c, plan)
+    assert m.restore_packets(cum) == 2                            # room min(24 free, 16 staging): 6 and 12 fit
+    m.set_pressure(64, 40, 8)
+    assert m.restore_packets(cum) == 1
     for bad in ([2, 2], [0, 3], [4]):
         with pytest.raises(StatusError):
             K.cumulative_nonresident(lanes, bad, eq)
+
+
+def _wait_landed(m, d):
+    t0 = time.time()
+    while m.channel(d).stage != K.LANDED and time.time() - t0 < 5:
+        m.poll()
+    return m.channel(d)
 
 
 def test_evict_then_restore_round_trips_bytes():
     plan = _plan()
     store = K.MemoryStore()
     c = K.StageKvClient("memory", store, plan.rank, plan.model_fp, plan.layout_fp)
+    RESTORE, EVICT = K.Direction.RESTORE, K.Direction.EVICT
     rng = np.random.default_rng(0)
     kv = {7: rng.integers(0, 255, (3, 64), dtype=np.uint8), 9: rng.integers(0, 255, (2, 64), dtype=np.uint8)}
     st = {7: rng.integers(0, 255, 160, dtype=np.uint8), 9: rng.integers(0, 255, 160, dtype=np.uint8)}
-    restore, evict = K.BatchState(), K.BatchState()
+    m, bstage, sstage = _mover(c, plan)
     for seq in (7, 9):
-        blocks = K.build_evict_batch(plan, seq, list(range(kv[seq].shape[0])), True, kv[seq].ctypes.data,
-                                     st[seq].ctypes.data, 16)
+        blocks = m.plan_evict(seq, list(range(kv[seq].shape[0])), True, kv[seq].ctypes.data, st[seq].ctypes.data)
         assert blocks[0].key.endswith("/state") and [b.op for b in blocks] == [K.PUT] * len(blocks)
-        K.submit_batch(c, evict, K.PUT, blocks, 0)
+        m.start(EVICT, blocks, 0)
         with pytest.raises(StatusError):
-            K.submit_batch(c, evict, K.PUT, blocks, 0)          # one outstanding batch per kind
-        t0 = time.time()
-        while evict.phase != K.READY and time.time() - t0 < 5:
-            K.progress(c, restore, evict)
-        assert evict.status == 0
-        K.acknowledge(evict)
+            m.start(EVICT, blocks, 0)                               # one batch per channel
+        assert _wait_landed(m, EVICT).outcome == 0
+        assert m.collect(EVICT) == 0
+        assert m.channel(EVICT).stage == K.FREE
     with pytest.raises(StatusError):
-        K.acknowledge(evict)
+        m.collect(EVICT)
     # restore both sequences into staging, lane by lane
-    bstage = np.zeros((8, 64), np.uint8)
-    sstage = np.zeros((2, 160), np.uint8)
     lanes = [K.PendingLane(7, [0, 1, 2], True), K.PendingLane(9, [0, 1], True)]
-    rb = K.build_restore_batch(plan, lanes, [1, 1], bstage.ctypes.data, 8, sstage.ctypes.data, 2, 16)
+    rb = m.plan_restore(lanes, [1, 1])
     assert (rb.lanes_built, rb.block_records, rb.state_records, len(rb.blocks)) == (2, 5, 2, 7)
-    K.submit_batch(c, restore, K.GET, rb.blocks, 1)
-    t0 = time.time()
-    while restore.phase != K.READY and time.time() - t0 < 5:
-        K.progress(c, restore, evict)
-    assert restore.status == 0
+    assert rb.blocks[0].key.endswith("/state") and rb.blocks[4].key.endswith("/state")   # state record first
+    m.start(RESTORE, rb.blocks, 1)
+    assert _wait_landed(m, RESTORE).outcome == 0
     assert np.array_equal(bstage[:3], kv[7]) and np.array_equal(bstage[3:5], kv[9])
     assert np.array_equal(sstage[0], st[7]) and np.array_equal(sstage[1], st[9])
-    K.acknowledge(restore)
+    assert m.collect(RESTORE) == 0
     # a lane that does not fit ends the batch; the first lane must fit
-    rb = K.build_restore_batch(plan, lanes, [1, 1], bstage.ctypes.data, 4, sstage.ctypes.data, 2, 16)
+    m4, _, _ = _mover(c, plan, block_records=4)
+    rb = m4.plan_restore(lanes, [1, 1])
     assert rb.lanes_built == 1 and rb.block_records == 3
+    m1, _, _ = _mover(c, plan, state_records=1)
+    assert m1.plan_restore(lanes, [1, 1]).lanes_built == 1              # one state record of staging
+    mb, _, _ = _mover(c, plan, batch=5)
+    assert mb.plan_restore(lanes, [1, 1]).lanes_built == 1              # 4 + 3 records > 5
+    m2, _, _ = _mover(c, plan, block_records=2)
     with pytest.raises(StatusError) as e:
-        K.build_restore_batch(plan, lanes, [1, 1], bstage.ctypes.data, 2, sstage.ctypes.data, 2, 16)
+        m2.plan_restore(lanes, [1, 1])
     assert e.value.code == CAP
     with pytest.raises(StatusError):
-        K.build_evict_batch(plan, 7, [], False, bstage.ctypes.data, sstage.ctypes.data, 16)
+        m.plan_evict(7, [], False, bstage.ctypes.data, sstage.ctypes.data)
     with pytest.raises(StatusError) as e:
-        K.build_evict_batch(plan, 7, list(range(20)), False, bstage.ctypes.data, sstage.ctypes.data, 16)
+        m.plan_evict(7, list(range(20)), False, bstage.ctypes.data, sstage.ctypes.data)
     assert e.value.code == CAP
+
+
+def test_restore_prefix_matches_lane_by_lane_rule():
+    """The binary search over prefix sums picks the same lanes as adding lanes one at a
+    time until the first one that would overflow a resource."""
+    plan = _plan()
+    c = K.StageKvClient("memory", K.MemoryStore(), plan.rank, plan.model_fp, plan.layout_fp)
+    rng = np.random.default_rng(5)
+    for trial in range(200):
+        n = int(rng.integers(1, 7))
+        spec = [(list(range(int(rng.integers(0, 5)))), bool(rng.integers(0, 2))) for _ in range(n)]
+        spec = [(b, st) if (b or st) else ([0], st) for b, st in spec]
+        lanes = [K.PendingLane(i + 1, b, st) for i, (b, st) in enumerate(spec)]
+        br, sr, batch = int(rng.integers(1, 12)), int(rng.integers(1, 4)), int(rng.integers(1, 14))
+        m, _, _ = _mover(c, plan, block_records=br, state_records=sr, batch=batch)
+        taken, recs, blks, sts = 0, 0, 0, 0
+        for b, st in spec:
+            s = 1 if st else 0
+            if recs + len(b) + s > batch or blks + len(b) > br or sts + s > sr:
+                break
+            recs, blks, sts, taken = recs + len(b) + s, blks + len(b), sts + s, taken + 1
+        if taken == 0:
+            with pytest.raises(StatusError):
+                m.plan_restore(lanes, [1] * n)
+        else:
+            rb = m.plan_restore(lanes, [1] * n)
+            assert (rb.lanes_built, rb.block_records, rb.state_records) == (taken, blks, sts)
