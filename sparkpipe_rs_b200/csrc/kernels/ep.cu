@@ -536,8 +536,7 @@ void ep_recv_align(const EpArgs& a, const int64_t* epoch, int layer, int bn, int
   check_args(a);
   const int smem = a.world * a.max_chunks * (int)sizeof(int);
   if (smem > 160 * 1024) throw std::runtime_error("ep: too many token chunks for the receive kernel");
-  if (smem > 32 * 1024)  // per current device; cheap, and legal during stream capture
-    cudaFuncSetAttribute(ep_recv_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+  if (smem > 32 * 1024) set_smem_bytes(ep_recv_align_kernel, 160 * 1024);
   launch_k(ep_recv_align_kernel, dim3(1), dim3(1024), smem, s, a, epoch, layer, bn, grp_rows, grp_tiles, src_row,
            comb_dst, budget, err);
 }

@@ -553,12 +553,8 @@ static void launch_fp8(const Fp8Launch& g, Fp8KParams& p) {
   make_tmap_2d(&ta, g.A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.a_rows, g.K, g.lda, F8_BM, F8_BK);
   make_tmap_2d(&tb, g.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.b_rows, g.K, g.ldb, BN, F8_BK);
   auto kern = gemm_fp8_kernel<BN, MODE>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attr_set = true;
-  }
+  set_smem_bytes(kern, C::SMEM_BYTES);
+  prefer_max_smem_carveout(reinterpret_cast<const void*>(kern));
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attrs[1];
   cfg.blockDim = dim3(F8_THREADS, 1, 1);

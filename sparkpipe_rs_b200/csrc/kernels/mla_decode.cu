@@ -745,11 +745,7 @@ static void launch_mla_tc(const MlaDecodeLaunch& l) {
   make_tmap_2d(&tq, l.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (long long)l.B * l.H, MLA_DIM, MLA_DIM, HG, 64);
   make_tmap_2d(&tkv, l.cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.num_slots, MLA_DIM, MLA_DIM, mtc::TOK, 64);
   auto kern = mla_decode_tc_kernel<HG>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    attr = true;
-  }
+  set_smem_bytes(kern, C::SMEM);
   MlaKParams p;
   p.block_table = l.block_table;
   p.max_blocks = l.max_blocks;
@@ -778,11 +774,7 @@ static void launch_mla(const MlaDecodeLaunch& l) {
   make_tmap_2d(&tq, l.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (long long)l.B * l.H, MLA_DIM, MLA_DIM, HG, 64);
   make_tmap_2d(&tkv, l.cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.num_slots, MLA_DIM, MLA_DIM, TOK, 64);
   auto kern = mla_decode_kernel<HG, NJ, TOK>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    attr = true;
-  }
+  set_smem_bytes(kern, C::SMEM);
   MlaKParams p;
   p.block_table = l.block_table;
   p.max_blocks = l.max_blocks;

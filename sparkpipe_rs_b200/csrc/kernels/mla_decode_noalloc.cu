@@ -96,11 +96,13 @@ extern "C" int sp_mla_decode_noalloc(const void* q, const void* cache, long long
   return e == cudaSuccess ? SP_NOALLOC_OK : int(e);
 }
 
-extern "C" int sp_mla_decode_noalloc_status(void) {
+extern "C" int sp_mla_decode_noalloc_status(void* stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   DeviceSymbols* sym = nullptr;
   if (resolve_symbols(dev, &sym) != SP_NOALLOC_OK) return -1;
+  // the kernels of the caller's stream must have finished before the word is read
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return -1;
   int v = 0;
   if (cudaMemcpy(&v, sym->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
   if (cudaMemset(sym->status, 0, sizeof(int)) != cudaSuccess) return -1;

@@ -51,9 +51,12 @@ __attribute__((visibility("default"))) int sp_mla_decode_noalloc(
     const void* q, const void* cache, long long num_slots, const int* block_table, int max_blocks,
     const int* context_lens, void* out, int batch, int heads, int splits, float scale, void* stream);
 
-// Reads (and clears) the status word of the last call on the current device:
-// 0 = no bounded wait ran out. Synchronous; returns a negative value on failure.
-__attribute__((visibility("default"))) int sp_mla_decode_noalloc_status(void);
+// Reads (and clears) the status word of the calls made on the current device:
+// 0 = no bounded wait ran out. It first waits for `stream` (the stream the calls
+// were launched on; 0 = legacy default stream) to finish, so a call launched on a
+// non-blocking stream has written its status before it is read. Blocks the host;
+// returns a negative value on failure.
+__attribute__((visibility("default"))) int sp_mla_decode_noalloc_status(void* stream);
 
 #ifdef __cplusplus
 }

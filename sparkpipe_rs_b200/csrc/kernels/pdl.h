@@ -7,9 +7,10 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <set>
 #include <stdexcept>
 #include <string>
-#include <unordered_set>
+#include <tuple>
 
 namespace sp {
 
@@ -22,13 +23,34 @@ inline bool pdl_enabled() {
   return on == 1;
 }
 
+// Function attributes belong to each device's instance of a kernel, so every
+// (attribute, value) is applied once per (kernel, device), under a lock, with the
+// return code checked: a second GPU driven by the same process gets its own opt-in.
+inline void set_func_attr_once(const void* kern, cudaFuncAttribute attr, int value) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lk(mu);
+  if (!done.insert({kern, dev, int(attr), value}).second) return;
+  e = cudaFuncSetAttribute(kern, attr, value);
+  if (e != cudaSuccess) {
+    done.erase({kern, dev, int(attr), value});
+    throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  }
+}
+
+// Opt-in to `bytes` of dynamic shared memory (kernels above 48 KB need it).
+template <typename K>
+inline void set_smem_bytes(K kern, int bytes) {
+  set_func_attr_once(reinterpret_cast<const void*>(kern), cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
 // Every kernel asks for the maximum shared-memory carveout, so consecutive
 // kernels of a decode step never force an SM to reconfigure L1 / shared memory.
 inline void prefer_max_smem_carveout(const void* kern) {
-  static std::mutex mu;
-  static std::unordered_set<const void*> done;
-  std::lock_guard<std::mutex> lk(mu);
-  if (done.insert(kern).second) cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  set_func_attr_once(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
 }
 
 template <typename... KArgs, typename... Args>

@@ -228,11 +228,7 @@ void prefill_attention(const PrefillAttnLaunch& l) {
     prefill_attention_tc(l);
     return;
   }
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    attr = true;
-  }
+  set_smem_bytes(prefill_attn_kernel, SMEM);
   dim3 grid((l.max_q + QT - 1) / QT, l.H, l.B);
   launch_k(prefill_attn_kernel, grid, dim3(128), SMEM, l.stream, l, l.scale * 1.4426950408889634f);
 }

@@ -386,11 +386,7 @@ void prefill_attention_tc(const PrefillAttnLaunch& l) {
   make_tmap_2d(&tk, l.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.k_rows, kcols, l.k_tok, BN, 64);
   make_tmap_2d(&tkpe, l.kpe, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.k_rows, 64, l.kpe_tok, BN, 64);
   make_tmap_2d(&tv, l.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.k_rows, vcols, l.v_tok, BN, 64);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    attr = true;
-  }
+  set_smem_bytes(prefill_attn_tc_kernel, SMEM);
   FaTcParams p;
   p.cu_q = l.cu_q;
   p.cu_k = l.cu_k;
