@@ -33,6 +33,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstdio>
 #include <stdexcept>
 #include <string>
@@ -65,6 +66,10 @@ struct GemmKParams {
   int swiglu;         // grouped: A rows are [64 gate | 64 up] per tile; write silu(gate) * up
   float* ws;          // split-K partial slabs: [splits][N][M] (trans_out) or [splits][M][N], fp32
   long long split_stride;
+  // stream-K split (sk_ctas > 0): CTA c owns the flattened (tile, K-block) units
+  // [c*T/G, (c+1)*T/G), G = sk_ctas; a tile's partials fill slab slots 0..nseg-1 and
+  // the CTA finishing the tile zeroes slots nseg..sk_slots-1
+  int sk_ctas, sk_slots;
   int* err;
   // Tensor parallelism over peer memory (LL tagged words, ll.cuh):
   //  * tp_rs: the epilogue sends fp32 partials of token n to rank n / tp_rows, slot
@@ -93,7 +98,8 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // split-K CTAs own only a few K blocks: a short pipeline keeps two CTAs per SM
+  // split-K CTAs own only a few K blocks: a short pipeline keeps two CTAs per SM, so
+  // under PDL the next kernel's CTAs can become resident beside them
   static constexpr int STAGES = MODE == MODE_SPLITK ? 4 : (BN >= 256 ? 4 : (BN >= 128 ? 6 : 8));
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int XBUF_BYTES = 64 * 17 * 4;  // SwiGLU exchange buffer (64 rows x 16 cols, padded)
@@ -148,6 +154,51 @@ SP_DEVI bool get_tile(const GemmKParams& p, int t, TileInfo& ti) {
     ti.d_off = (long long)z * p.d_batch_stride;
     return true;
   }
+}
+
+// CTA owning flattened unit w when W units are split over G CTAs.
+SP_DEVI int sk_cta_of(long long w, long long W, int G) { return int(((w + 1) * G + W - 1) / W) - 1; }
+
+// One item of a CTA's work: a tile, its K-block range [kb0, kb1), and (split-K) the
+// slab slot of the partial and how many slots the tile's partials fill.
+struct WorkItem {
+  int tile, kb0, kb1, slot, nseg;
+};
+
+// The idx-th work item of this CTA; false past the last one.
+template <int MODE>
+SP_DEVI bool work_item(const GemmKParams& p, int num_tiles, int idx, WorkItem& w) {
+  const int kbs = (p.K + BK - 1) / BK;
+  if (MODE != MODE_SPLITK) {  // persistent: tiles blockIdx.x, + gridDim.x, ...
+    const long long t = blockIdx.x + (long long)idx * gridDim.x;
+    if (t >= num_tiles) return false;
+    w.tile = int(t); w.kb0 = 0; w.kb1 = kbs; w.slot = 0; w.nseg = 1;
+    return true;
+  }
+  if (p.sk_ctas == 0) {  // fixed split: CTA (tile, ks) owns K-block slice ks of one tile
+    if (idx > 0) return false;
+    const int ks = blockIdx.x % p.splits;
+    w.tile = blockIdx.x / p.splits;
+    w.kb0 = int((long long)kbs * ks / p.splits);
+    w.kb1 = int((long long)kbs * (ks + 1) / p.splits);
+    w.slot = ks;
+    w.nseg = p.splits;
+    return w.tile < num_tiles;
+  }
+  const long long T = (long long)num_tiles * kbs;
+  const int G = p.sk_ctas, c = blockIdx.x;
+  const long long u_end = T * (c + 1) / G;
+  long long u = T * c / G;
+  for (int i = 0; i < idx && u < u_end; ++i) u = min(u_end, (u / kbs + 1) * kbs);  // skip idx pieces
+  if (u >= u_end) return false;
+  const long long t = u / kbs;
+  w.tile = int(t);
+  w.kb0 = int(u - t * kbs);
+  w.kb1 = int(min(u_end, (t + 1) * kbs) - t * kbs);
+  const int cf = sk_cta_of(t * kbs, T, G), cl = sk_cta_of(t * kbs + kbs - 1, T, G);
+  w.slot = c - cf;
+  w.nseg = cl - cf + 1;
+  return true;
 }
 
 template <int BN>
@@ -299,18 +350,6 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int num_tiles = *s_ntiles;
 
-  // Split-K: CTA (tile, ks) owns K-block slice ks of exactly one tile.
-  int kb_begin = 0, kb_end = (p.K + BK - 1) / BK;
-  int tile_first = blockIdx.x, tile_step = gridDim.x;
-  int ks = 0;
-  if (MODE == MODE_SPLITK) {
-    ks = blockIdx.x % p.splits;
-    const int total_kb = kb_end;
-    kb_begin = (int)((long long)total_kb * ks / p.splits);
-    kb_end = (int)((long long)total_kb * (ks + 1) / p.splits);
-    tile_first = blockIdx.x / p.splits;
-    tile_step = 1 << 30;  // exactly one tile
-  }
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -324,24 +363,26 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       int pre = 0;  // stages whose A tile went out before the PDL wait
       if (prefetch_a) {
-        if (tile_first < num_tiles) {
+        // A stages of the first work items, in the main loop's order
+        WorkItem w0;
+        for (int wi = 0; pre < C::STAGES && work_item<MODE>(p, num_tiles, wi, w0); ++wi) {
           TileInfo t0;
-          get_tile<BN, MODE>(p, tile_first, t0);
-          pre = min(C::STAGES, kb_end - kb_begin);
-          for (int j = 0; j < pre; ++j) {
-            mbar_arrive_expect_tx(&full[j], C::STAGE_BYTES);
-            tma_load_2d_hint(smem + j * C::STAGE_BYTES, &tmA, &full[j], t0.a_k + (kb_begin + j) * BK, t0.a_row, pol_a);
+          get_tile<BN, MODE>(p, w0.tile, t0);
+          for (int kb = w0.kb0; kb < w0.kb1 && pre < C::STAGES; ++kb, ++pre) {
+            mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
+            tma_load_2d_hint(smem + pre * C::STAGE_BYTES, &tmA, &full[pre], t0.a_k + kb * BK, t0.a_row, pol_a);
           }
         }
         griddep_wait();
       }
       // all-gather operand: rows of this layer's parity half (published, waited for above)
       const int ag_row0 = ag_buf * p.tp_world * p.tp_rows;
-      for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
+      WorkItem w;
+      for (int wi = 0; ok && work_item<MODE>(p, num_tiles, wi, w); ++wi) {
         TileInfo ti;
-        if (!get_tile<BN, MODE>(p, t, ti)) continue;
+        if (!get_tile<BN, MODE>(p, w.tile, ti)) continue;
         const int b_row = ti.b_row + ag_row0;
-        for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           uint8_t* sa = smem + s * C::STAGE_BYTES;
@@ -370,15 +411,16 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
       int it = 0, tc = 0;
       bool ok = true;
-      for (int t = tile_first; t < num_tiles && ok; t += tile_step) {
+      WorkItem w;
+      for (int wi = 0; ok && work_item<MODE>(p, num_tiles, wi, w); ++wi) {
         TileInfo ti;
-        if (!get_tile<BN, MODE>(p, t, ti)) continue;
+        if (!get_tile<BN, MODE>(p, w.tile, ti)) continue;
         const int buf = tc & 1;
         const uint32_t tph = (tc >> 1) & 1;
         if (!mbar_wait(&tempty[buf], tph ^ 1, s_err, p.err, kErrWaitTimeoutMma)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           if (!mbar_wait(&full[s], ph, s_err, p.err, kErrWaitTimeoutMma)) { ok = false; break; }
@@ -389,7 +431,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             // +32 bytes of K per step -> +2 in the encoded start address
-            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
+            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > w.kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);
         }
@@ -406,9 +448,10 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
     if (MODE != MODE_SPLITK) {
       int tc = 0;
-      for (int t = tile_first; t < num_tiles; t += tile_step) {
+      WorkItem w;
+      for (int wi = 0; work_item<MODE>(p, num_tiles, wi, w); ++wi) {
         TileInfo ti;
-        if (!get_tile<BN, MODE>(p, t, ti)) continue;
+        if (!get_tile<BN, MODE>(p, w.tile, ti)) continue;
         const int buf = tc & 1;
         const uint32_t tph = (tc >> 1) & 1;
         if (!mbar_wait(&tfull[buf], tph, s_err, p.err, kErrWaitTimeoutEpilogue)) break;
@@ -468,26 +511,41 @@ __global__ void __launch_bounds__(192, 1)
         ++tc;
       }
     } else {
-      // Split-K: this CTA's fp32 partial goes to its own slab of the workspace,
-      // in the output's (n, m) coordinates with a dense pitch.
-      TileInfo ti;
-      get_tile<BN, MODE>(p, tile_first, ti);
-      GemmKParams q = p;
-      q.D = p.ws + (size_t)ks * p.split_stride;
-      q.out_f32 = 1;
-      q.ldd = p.trans_out ? p.M : p.N;
-      ti.d_off = 0;
-      if (mbar_wait(&tfull[0], 0, s_err, p.err, kErrWaitTimeoutEpilogue)) {
+      // Split-K: each work item's fp32 partial goes to slab `slot` of the workspace,
+      // in the output's (n, m) coordinates with a dense pitch; the CTA that finishes a
+      // tile (its last slot) zeroes the tile's slots the stream-K split leaves unused.
+      int tc = 0;
+      WorkItem w;
+      for (int wi = 0; work_item<MODE>(p, num_tiles, wi, w); ++wi) {
+        TileInfo ti;
+        get_tile<BN, MODE>(p, w.tile, ti);
+        GemmKParams q = p;
+        q.out_f32 = 1;
+        q.ldd = p.trans_out ? p.M : p.N;
+        ti.d_off = 0;
+        const int buf = tc & 1;
+        const uint32_t tph = (tc >> 1) & 1;
+        if (!mbar_wait(&tfull[buf], tph, s_err, p.err, kErrWaitTimeoutEpilogue)) break;
         tc_fence_after();
         int rbuf = 0;
         const uint32_t tag = p.tp_rs ? tp_tag(p, &rbuf) : 0u;
+        q.D = p.ws + (size_t)w.slot * p.split_stride;
         for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) {
           float v[16];
-          tmem_ld16(lane_addr + c0, v);
-          if (p.tp_rs) rs_store16<BN>(p, ti, m, c0, v, ks, tag, rbuf);
+          tmem_ld16(lane_addr + buf * BN + c0, v);
+          if (p.tp_rs) rs_store16<BN>(p, ti, m, c0, v, w.slot, tag, rbuf);
           else store_chunk<BN>(q, ti, m, c0, v);
         }
         tc_fence_before();
+        mbar_arrive(&tempty[buf]);
+        ++tc;
+        if (p.sk_ctas > 0 && w.slot == w.nseg - 1) {
+          const float z[16] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (int sl = w.nseg; sl < p.sk_slots; ++sl) {
+            q.D = p.ws + (size_t)sl * p.split_stride;
+            for (int c0 = 0; c0 < BN && c0 < ti.n_valid; c0 += 16) store_chunk<BN>(q, ti, m, c0, z);
+          }
+        }
       }
     }
   }
@@ -574,19 +632,15 @@ static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
   make_tmap_2d(&ta, g.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.a_rows, g.a_cols, g.lda, BM, BK);
   make_tmap_2d(&tb, g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.b_rows, g.b_cols, g.ldb, BN, BK);
   auto kern = gemm_bf16_kernel<BN, MODE>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attr_set = true;
-  }
+  set_smem_bytes(kern, C::SMEM_BYTES);
+  prefer_max_smem_carveout(reinterpret_cast<const void*>(kern));
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attrs[2];
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = g.stream;
   if (MODE == MODE_SPLITK) {
-    cfg.gridDim = dim3(p.num_tiles * p.splits, 1, 1);
+    cfg.gridDim = dim3(p.sk_ctas > 0 ? p.sk_ctas : p.num_tiles * p.splits, 1, 1);
     cfg.attrs = attrs;
     cfg.numAttrs = 0;
   } else {
@@ -624,6 +678,8 @@ static int pick_bn(int n) {
   if (n <= 128) return 128;
   return 256;
 }
+
+static int pick_or(const GemmLaunch& g, const GemmKParams&) { return g.block_n > 0 ? g.block_n : pick_bn(g.N); }
 
 static void check_k_window(long long cols, int k0, int batch_k, int K, int batch) {
   const long long kmax = (long long)k0 + (long long)batch_k * (batch - 1) + K;
@@ -686,18 +742,59 @@ int gemm_bf16(const GemmLaunch& g) {
     dispatch_bn<MODE_GROUPED>(bn, g, p);
     return 1;
   }
-  const int bn = g.block_n > 0 ? g.block_n : pick_bn(g.N);
+  const int bn = pick_or(g, p);
   p.n_tiles = (g.N + bn - 1) / bn;
   p.num_tiles = p.m_tiles * p.n_tiles * g.batch;
   int splits = g.splits;
   const int kbs = (g.K + BK - 1) / BK;
+  const long long slab = (long long)g.M * g.N;
+  const int out_cols = g.trans_out ? g.M : g.N;
+  // partial slabs need dense, 4-aligned rows, a workspace, and (reduced here) an aligned output
+  const bool slabs_ok = g.ws && g.batch == 1 && out_cols % 4 == 0 &&
+                        (g.slab_out || (g.ldd % 4 == 0 && (reinterpret_cast<uintptr_t>(g.D) & 15) == 0));
+  // The fixed split below keeps one CTA per SM: tiles x splits <= SMs.
+  const int fixed_splits = std::max(1, std::min({g.num_sms / std::max(1, p.num_tiles), kbs / 2, 16}));
+  static const bool streamk_on = [] {
+    const char* e = std::getenv("SPARKPIPE_GEMM_STREAMK");
+    return !(e && e[0] == '0');
+  }();
+  if (streamk_on && splits <= 0 && !g.tp && slabs_ok && p.num_tiles >= 8 &&
+      p.num_tiles * fixed_splits * 10 < g.num_sms * 6 && kbs >= 2) {
+    // Stream-K split, when the fixed split would leave over 40% of the SMs idle and
+    // there are enough tiles to share (77 tiles on 148 SMs: one split, 77 CTAs): the (tile, K-block) units are spread
+    // evenly over one CTA per SM, a tile's K range shared by consecutive CTAs. G is
+    // lowered until no tile needs more than 16 partial slots. Measured (64 tokens,
+    // K 2048, 9792 rows): 16.4 -> 15.9 us; where the fixed split fills the SMs it is
+    // faster (2048 rows: 9.2 us fixed vs 11.3 us stream-K).
+    const long long T = (long long)p.num_tiles * kbs;
+    auto cta_of = [](long long w, long long W, int G) { return int(((w + 1) * G + W - 1) / W) - 1; };
+    int G = (int)std::min<long long>(g.num_sms, T), slots = 0;
+    for (; G >= 1; --G) {
+      slots = 0;
+      for (int t = 0; t < p.num_tiles; ++t)
+        slots = std::max(slots, cta_of((long long)t * kbs + kbs - 1, T, G) - cta_of((long long)t * kbs, T, G) + 1);
+      if (slots <= 16) break;
+    }
+    if (G > p.num_tiles && slots > 1 && slab * slots <= g.ws_floats) {
+      p.ws = g.ws;
+      p.split_stride = slab;
+      p.splits = slots;
+      p.sk_ctas = G;
+      p.sk_slots = slots;
+      dispatch_bn<MODE_SPLITK>(pick_or(g, p), g, p);
+      if (g.slab_out) return -slots;
+      const int rows = g.trans_out ? g.N : g.M;
+      split_reduce(g.ws, slab, slots, rows, out_cols, g.D, g.ldd, g.out_f32, g.stream);
+      return 2;
+    }
+  }
   if (splits <= 0) {
     // Auto: the most splits that keep one CTA per SM (tiles x splits <= SMs), at
     // least two K blocks per split, at most 16. Each SM streams its own share of
     // the weights: two CTAs on some SMs and one on others leaves the doubled SMs as
     // the tail. (64 x 3648 x 2048: 5 splits, 145 CTAs; the old power-of-two rule
     // chose 8 splits, 232 CTAs.)
-    splits = std::max(1, std::min({g.num_sms / std::max(1, p.num_tiles), kbs / 2, 16}));
+    splits = fixed_splits;
   }
   if (splits > kbs) splits = kbs;  // every split CTA needs at least one K block
   if (g.tp && g.tp->rs) {
@@ -708,12 +805,8 @@ int gemm_bf16(const GemmLaunch& g) {
     else dispatch_bn<MODE_DENSE>(bn, g, p);
     return 1;
   }
-  const long long slab = (long long)g.M * g.N;
   // the slab reduction needs dense, 4-aligned rows and a workspace that fits
-  const int out_cols = g.trans_out ? g.M : g.N;
-  if (splits > 1 && (!g.ws || g.batch != 1 || slab * splits > g.ws_floats || out_cols % 4 != 0 ||
-                     (!g.slab_out && (g.ldd % 4 != 0 || (reinterpret_cast<uintptr_t>(g.D) & 15) != 0))))
-    splits = 1;
+  if (splits > 1 && (!slabs_ok || slab * splits > g.ws_floats)) splits = 1;
   p.ws = g.ws;
   p.split_stride = slab;
   p.splits = splits;

@@ -177,6 +177,8 @@ struct MlaDecodeLaunch {
   int* err = nullptr;
   int impl = 0;                   // MLA_IMPL_*
   unsigned long long* trace = nullptr;  // tcgen05 kernel: [6][64] event times of CTA (0,0,0)
+  int* counters = nullptr;        // stream-K kernel: per-row arrival counters, zero between launches
+  int early = 0;                  // stream-K kernel: earlier-position KV may load before the PDL wait
   cudaStream_t stream = 0;
 };
 enum { MLA_IMPL_AUTO = 0, MLA_IMPL_TC = 1, MLA_IMPL_MMA = 2 };
@@ -185,6 +187,13 @@ enum { MLA_IMPL_AUTO = 0, MLA_IMPL_TC = 1, MLA_IMPL_MMA = 2 };
 int mla_stage_tokens();
 int mla_ctas_per_sm(int heads, int impl = MLA_IMPL_AUTO);
 void mla_decode(const MlaDecodeLaunch& l);
+// Stream-K decode kernel (mla_decode_sk.cu): one CTA per SM over the flattened KV units.
+// Scratch: o_part [segments][heads per CTA][512] fp32, lse_part [segments][heads per CTA],
+// counters [(H / heads per CTA) * B] int32 zeroed once (the kernel leaves them zero).
+bool mla_sk_supported(int B, int H);
+int mla_sk_heads_per_cta(int heads);
+long long mla_sk_segments(int B, int H, int num_sms);
+void mla_decode_sk(const MlaDecodeLaunch& l, int num_sms);
 
 // ---- DSA token selection (dsa.cu)
 void paged_slots(const int* block_table, int max_blocks, const int* lens, const int* positions, int B, int rows,
@@ -211,6 +220,7 @@ inline void push_kernel_attr(std::vector<KernelAttr>& out, const std::string& na
 void kernel_attrs_gemm(std::vector<KernelAttr>& out);
 void kernel_attrs_fp8(std::vector<KernelAttr>& out);
 void kernel_attrs_mla(std::vector<KernelAttr>& out);
+void kernel_attrs_mla_sk(std::vector<KernelAttr>& out);
 void kernel_attrs_prefill(std::vector<KernelAttr>& out);
 void kernel_attrs_moe(std::vector<KernelAttr>& out);
 

@@ -20,6 +20,9 @@ using torch::Tensor;
 #define CHECK_I32(x) TORCH_CHECK((x).scalar_type() == at::kInt, #x " must be int32")
 #define CHECK_F32(x) TORCH_CHECK((x).scalar_type() == at::kFloat, #x " must be fp32")
 #define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+// every operand a kernel dereferences lives on the launching tensor's device
+#define CHECK_ON(ref, x) \
+  TORCH_CHECK((x).is_cuda() && (x).device() == (ref).device(), #x " must be a CUDA tensor on " #ref "'s device")
 
 cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
 
@@ -382,6 +385,7 @@ void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table,
                 const Tensor& out, const c10::optional<Tensor>& o_part, const c10::optional<Tensor>& lse_part,
                 int64_t splits, double scale, int64_t impl, const c10::optional<Tensor>& trace) {
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(cache); CHECK_I32(block_table); CHECK_I32(context_lens); CHECK_BF16(out);
+  CHECK_ON(q, cache); CHECK_ON(q, block_table); CHECK_ON(q, context_lens); CHECK_ON(q, out);
   CHECK_CONTIG(q); CHECK_CONTIG(block_table); CHECK_CONTIG(out);
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 576, "q: [B, H, 576]");
   TORCH_CHECK(cache.size(-1) == 576 && cache.stride(-1) == 1, "cache rows of 576");
@@ -398,12 +402,12 @@ void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table,
   TORCH_CHECK(block_table.size(0) >= B && context_lens.numel() >= B, "mla_decode: block table / lengths too short");
   TORCH_CHECK(out.numel() >= B * H * 512, "mla_decode: output too small");
   if (o_part.has_value()) {
-    CHECK_F32(*o_part);
+    CHECK_F32(*o_part); CHECK_ON(q, *o_part);
     TORCH_CHECK(o_part->numel() >= B * splits * H * 512, "mla_decode: split partials too small");
     l.o_part = o_part->data_ptr<float>();
   }
   if (lse_part.has_value()) {
-    CHECK_F32(*lse_part);
+    CHECK_F32(*lse_part); CHECK_ON(q, *lse_part);
     TORCH_CHECK(lse_part->numel() >= B * splits * H, "mla_decode: split log-sum-exps too small");
     l.lse_part = lse_part->data_ptr<float>();
   }
@@ -420,6 +424,53 @@ void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table,
   l.err = err_word();
   l.stream = stream();
   sp::mla_decode(l);
+}
+
+// Stream-K MLA decode (mla_decode_sk.cu); scratch sizes from mla_sk_segments / mla_sk_heads_per_cta.
+void mla_decode_sk(const Tensor& q, const Tensor& cache, const Tensor& block_table, const Tensor& context_lens,
+                   const Tensor& out, const Tensor& o_part, const Tensor& lse_part, const Tensor& counters,
+                   double scale, bool early, const c10::optional<Tensor>& trace) {
+  CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(cache); CHECK_I32(block_table); CHECK_I32(context_lens); CHECK_BF16(out);
+  CHECK_CONTIG(q); CHECK_CONTIG(block_table); CHECK_CONTIG(out); CHECK_CONTIG(context_lens);
+  CHECK_F32(o_part); CHECK_F32(lse_part); CHECK_I32(counters);
+  CHECK_ON(q, cache); CHECK_ON(q, block_table); CHECK_ON(q, context_lens); CHECK_ON(q, out);
+  CHECK_ON(q, o_part); CHECK_ON(q, lse_part); CHECK_ON(q, counters);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 576, "q: [B, H, 576]");
+  TORCH_CHECK(cache.size(-1) == 576 && cache.stride(-1) == 1 && cache.is_contiguous(), "cache rows of 576");
+  const int64_t B = q.size(0), H = q.size(1);
+  TORCH_CHECK(sp::mla_sk_supported((int)B, (int)H), "mla_decode_sk: unsupported batch / head count");
+  TORCH_CHECK(block_table.size(0) >= B && context_lens.numel() >= B, "mla_decode_sk: block table / lengths too short");
+  TORCH_CHECK(out.numel() >= B * H * 512, "mla_decode_sk: output too small");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int sms = num_sms();
+  const int64_t hg = sp::mla_sk_heads_per_cta((int)H);
+  const int64_t segs = sp::mla_sk_segments((int)B, (int)H, sms);
+  TORCH_CHECK(o_part.numel() >= segs * hg * 512 && lse_part.numel() >= segs * hg, "mla_decode_sk: scratch too small");
+  TORCH_CHECK(counters.numel() >= (H / hg) * B, "mla_decode_sk: counters too small");
+  sp::MlaDecodeLaunch l;
+  l.q = q.data_ptr();
+  l.cache = cache.data_ptr();
+  l.num_slots = cache.numel() / 576;
+  l.block_table = block_table.data_ptr<int>();
+  l.max_blocks = (int)block_table.size(1);
+  l.context_lens = context_lens.data_ptr<int>();
+  l.out = out.data_ptr();
+  l.o_part = o_part.data_ptr<float>();
+  l.lse_part = lse_part.data_ptr<float>();
+  l.counters = counters.data_ptr<int>();
+  l.B = (int)B;
+  l.H = (int)H;
+  l.scale = (float)scale;
+  l.early = early ? 1 : 0;
+  if (trace.has_value()) {
+    CHECK_ON(q, *trace);
+    TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->numel() >= 4 * 64,
+                "mla_decode_sk: trace must be an int64 CUDA tensor of 256 entries");
+    l.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
+  l.err = err_word();
+  l.stream = stream();
+  sp::mla_decode_sk(l, sms);
 }
 
 void prefill_attention(const Tensor& q, const Tensor& k, const Tensor& kpe, const Tensor& v, const Tensor& o,
@@ -610,7 +661,8 @@ void gather_prev_tokens(const Tensor& ids, const Tensor& prev, int64_t n) {
 }
 
 void dequant_nvfp4(const Tensor& packed, const Tensor& scales, double tensor_scale, const Tensor& out) {
-  CHECK_CUDA(packed); CHECK_CONTIG(packed); CHECK_CONTIG(scales); CHECK_CONTIG(out);
+  CHECK_CUDA(packed); CHECK_ON(packed, scales); CHECK_ON(packed, out);
+  CHECK_CONTIG(packed); CHECK_CONTIG(scales); CHECK_CONTIG(out);
   TORCH_CHECK(packed.scalar_type() == at::kByte && scales.scalar_type() == at::kByte, "dequant_nvfp4: uint8 inputs");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16, "dequant_nvfp4: bf16 output");
   TORCH_CHECK(out.numel() == packed.numel() * 2 && out.numel() == scales.numel() * 16, "dequant_nvfp4: sizes");
@@ -624,6 +676,7 @@ void dequant_nvfp4(const Tensor& packed, const Tensor& scales, double tensor_sca
 void spec_verify(const Tensor& draft, const Tensor& target, double p_accept, int64_t seed, int64_t offset,
                  const Tensor& accepted, const Tensor& committed) {
   CHECK_CUDA(draft); CHECK_I32(draft); CHECK_I32(target); CHECK_I32(accepted); CHECK_I32(committed);
+  CHECK_ON(draft, target); CHECK_ON(draft, accepted); CHECK_ON(draft, committed);
   CHECK_CONTIG(draft); CHECK_CONTIG(target); CHECK_CONTIG(committed);
   const c10::cuda::CUDAGuard guard(draft.device());
   sp::spec_verify(draft.data_ptr<int>(), target.data_ptr<int>(), (int)draft.size(0), (int)draft.size(1),
@@ -888,6 +941,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_act_fp8", &quant_act_fp8);
   m.def("quant_weight_fp8", &quant_weight_fp8);
   m.def("mla_decode", &mla_decode);
+  m.def("mla_decode_sk", &mla_decode_sk);
+  m.def("mla_sk_supported", [](int64_t B, int64_t H) { return sp::mla_sk_supported((int)B, (int)H); });
+  m.def("mla_sk_heads_per_cta", [](int64_t H) { return sp::mla_sk_heads_per_cta((int)H); });
+  m.def("mla_sk_segments", [](int64_t B, int64_t H, int64_t sms) { return sp::mla_sk_segments((int)B, (int)H, (int)sms); });
   m.def("prefill_attention", &prefill_attention);
   m.def("moe_topk", &moe_topk);
   m.def("moe_align", &moe_align);
@@ -918,6 +975,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     sp::kernel_attrs_gemm(v);
     sp::kernel_attrs_fp8(v);
     sp::kernel_attrs_mla(v);
+    sp::kernel_attrs_mla_sk(v);
     sp::kernel_attrs_prefill(v);
     sp::kernel_attrs_moe(v);
     py::list out;

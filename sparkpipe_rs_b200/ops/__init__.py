@@ -7,6 +7,7 @@ without the compiled extension or without a CUDA device they raise.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -338,16 +339,25 @@ def grouped_gemm_fp8(w: Fp8Weight, x_sorted: Fp8Act, out: torch.Tensor, grp_rows
     return out
 
 
-MLA_IMPL = {"auto": 0, "tc": 1, "mma": 2}  # MLA decode kernels: default, tcgen05, mma.sync
+MLA_IMPL = {"auto": 0, "tc": 1, "mma": 2, "sk": 3}  # MLA decode kernels: default, tcgen05, mma.sync, stream-K
+
+# Decode kernel: "mma" (split-KV mma.sync, default), "sk" (stream-K) or "tc" (split-KV tcgen05),
+# chosen with SPARKPIPE_MLA_KERNEL.
+_MLA_DEFAULT = os.environ.get("SPARKPIPE_MLA_KERNEL", "mma")
+# SPARKPIPE_MLA_SK_EARLY=0: the stream-K kernel waits for its predecessor before any load,
+# inside CUDA graphs too.
+_MLA_SK_EARLY = os.environ.get("SPARKPIPE_MLA_SK_EARLY", "1") != "0"
 
 
 def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 148, impl: str = "auto") -> int:
-    """Split-KV factor: the most CTAs that still fit one wave on the SMs, without
-    splits of under two blocks (a second partial wave costs more than it hides:
-    B=64, 16 heads, ctx 1024 measured 27 us at 2 splits, 34 us at 3)."""
+    """Split-KV factor of the split-KV kernels ("mma", "tc"): the most CTAs that still fit
+    one wave on the SMs, without splits of under two blocks (a second partial wave costs
+    more than it hides: B=64, 16 heads, ctx 1024 measured 27 us at 2 splits, 34 us at 3).
+    The stream-K kernel ignores it."""
     groups = heads // (32 if heads % 32 == 0 else 16)
     ctas = max(1, batch * groups)
-    slots = num_sms * int(kernels().mla_ctas_per_sm(heads, MLA_IMPL[impl]))  # CTAs resident at once
+    k_impl = impl if impl in ("tc", "mma") else ("tc" if _MLA_DEFAULT == "tc" else "mma")
+    slots = num_sms * int(kernels().mla_ctas_per_sm(heads, MLA_IMPL[k_impl]))  # CTAs resident at once
     want = max(1, slots // ctas)
     blocks = max(1, math.ceil(max_context / 64))
     # few long sequences need many splits to use the SMs (one 131K-token sequence:
@@ -356,15 +366,72 @@ def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 1
     return int(max(1, min(want, blocks // 2 if blocks >= 2 else 1, cap)))
 
 
+class _SkWorkspace:
+    """Scratch of the stream-K decode kernel on one device: per-segment partial outputs
+    and log-sum-exps, and per-row arrival counters that the kernel leaves at zero.
+    Grown outside graph capture only; replaced buffers stay referenced so graphs
+    captured with them remain valid."""
+
+    def __init__(self):
+        self.o = self.lse = self.cnt = None
+        self.retired = []
+
+    def get(self, device, B, H):
+        K = kernels()
+        hg = int(K.mla_sk_heads_per_cta(H))
+        segs = int(K.mla_sk_segments(B, H, K.num_sms()))
+        need = (segs * hg * 512, segs * hg, (H // hg) * B)
+        if self.o is None or self.o.numel() < need[0] or self.lse.numel() < need[1] or self.cnt.numel() < need[2]:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("mla_decode: the stream-K scratch must be sized by an eager call before capture")
+            if self.o is not None:
+                self.retired.append((self.o, self.lse, self.cnt))
+            o = max(need[0], 0 if self.o is None else self.o.numel())
+            lse = max(need[1], 0 if self.lse is None else self.lse.numel())
+            cnt = max(need[2], 0 if self.cnt is None else self.cnt.numel())
+            self.o = torch.empty(o, dtype=torch.float32, device=device)
+            self.lse = torch.empty(lse, dtype=torch.float32, device=device)
+            self.cnt = torch.zeros(cnt, dtype=torch.int32, device=device)
+        return self.o, self.lse, self.cnt
+
+    def reset_counters(self):
+        if self.cnt is not None:
+            self.cnt.zero_()
+
+
+_SK_WS: dict = {}
+
+
+def _sk_workspace(device) -> _SkWorkspace:
+    key = torch.device(device).index
+    ws = _SK_WS.get(key)
+    if ws is None:
+        ws = _SK_WS[key] = _SkWorkspace()
+    return ws
+
+
 def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=None, lse_part=None, impl="auto",
                trace=None):
-    """Absorbed-MLA paged decode attention. ``impl``: "mma" (mma.sync kernel, the
-    default), "tc" (tcgen05 tensor cores) or "auto" (the default one, which the
-    SPARKPIPE_MLA_KERNEL environment variable can switch). ``trace``: an int64
-    CUDA tensor of 6 x 64 entries that receives the tcgen05 kernel's pipeline event
-    times (global timer, ns) of its first CTA: TMA issue, S^T issue, S^T seen by the
-    softmax, P^T ready, O^T issue per tile; start and end."""
+    """Absorbed-MLA paged decode attention. ``impl``: "sk" (stream-K kernel: all SMs
+    over the flattened 32-token KV units, the default), "mma" (split-KV mma.sync
+    kernel), "tc" (split-KV tcgen05 kernel) or "auto" (the default, which the
+    SPARKPIPE_MLA_KERNEL environment variable can switch). ``splits`` applies to the
+    split-KV kernels only. ``trace`` (diagnostics, int64 CUDA tensor): for "sk", 4 x 64
+    global-timer stamps (ns) of four CTAs (first, second, middle, last): start,
+    schedule ready, dependency wait passed, per piece queries landed / finished, per
+    stage consumed, merge start / end, end (see mla_decode_sk.cu); for "tc", 6 x 64
+    pipeline event times of its first CTA."""
     B, H, _ = q.shape
+    if impl == "auto":
+        impl = _MLA_DEFAULT
+    if impl == "sk" and kernels().mla_sk_supported(B, H):
+        o_ws, lse_ws, cnt = _sk_workspace(q.device).get(q.device, B, H)
+        kernels().mla_decode_sk(q, cache, block_table, context_lens, out, o_ws, lse_ws, cnt, float(scale),
+                                _MLA_SK_EARLY and bool(torch.cuda.is_current_stream_capturing()), trace)
+        _count(1)
+        return out
+    if impl == "sk":
+        impl = "mma"
     if splits > 1 and o_part is None:
         o_part = torch.empty(B, splits, H, 512, dtype=torch.float32, device=q.device)
         lse_part = torch.empty(B, splits, H, dtype=torch.float32, device=q.device)
@@ -522,7 +589,12 @@ def status_word() -> int:
 
 
 def clear_status() -> None:
+    """Clears the device status word; a launch that gave up on a bounded wait may have
+    left stream-K decode counters set, so those are zeroed too."""
     kernels().clear_status()
+    ws = _SK_WS.get(torch.cuda.current_device())
+    if ws is not None:
+        ws.reset_counters()
 
 
 # ------------------------------------------------------------------ DSA sparse attention

@@ -24,7 +24,10 @@ def main():
     ap.add_argument("--ctx", type=int, default=1024)
     ap.add_argument("--splits", default="0,1,2,3,4,5,6,8")
     ap.add_argument("--iters", type=int, default=50)
-    ap.add_argument("--impl", default="tc,mma", help="kernels to time: tc (tcgen05), mma (mma.sync)")
+    ap.add_argument("--trace", action="store_true",
+                    help="sk only: print the kernel's device event trace of four CTAs (one eager launch)")
+    ap.add_argument("--impl", default="sk,mma", help="kernels to time: sk (stream-K), tc (tcgen05 split-KV), "
+                                                      "mma (mma.sync split-KV)")
     args = ap.parse_args()
     from sparkpipe_rs_b200 import ops
 
@@ -41,6 +44,28 @@ def main():
     nbytes = B * L * 576 * 2
     scale = 1 / math.sqrt(192)
     for impl in args.impl.split(","):
+        if impl == "sk":  # one schedule over all SMs: no split factor
+            ops.mla_decode(q, caches[0], bt, ctx, out, 1, scale, impl="sk")  # sizes the scratch outside capture
+            us = time_fn(lambda i: ops.mla_decode(q, caches[i % n_caches], bt, ctx, out, 1, scale, impl="sk"),
+                         args.iters)
+            print(f"mla_decode[sk] B={B} H={H} ctx={L}: {us:8.2f} us  {nbytes / us / 1e6:6.2f} TB/s of KV")
+            if args.trace:
+                tr = torch.zeros(4 * 64, dtype=torch.int64, device=dev)
+                ops.mla_decode(q, caches[0], bt, ctx, out, 1, scale, impl="sk")
+                ops.mla_decode(q, caches[-1], bt, ctx, out, 1, scale, impl="sk", trace=tr)
+                torch.cuda.synchronize()
+                t = tr.view(4, 64).cpu()
+                t0 = int(t[t > 0].min())
+                names = {0: "start", 1: "sched", 2: "dep", 60: "merge0", 61: "merge1", 63: "end"}
+                for c in range(4):
+                    row = []
+                    for i in range(64):
+                        if int(t[c, i]) > 0:
+                            nm = names.get(i, f"q{(i - 3) // 2}" if 3 <= i < 19 and i % 2 == 1 else
+                                           f"p{(i - 4) // 2}" if 4 <= i < 20 else f"s{i - 20}")
+                            row.append(f"{nm}:{(int(t[c, i]) - t0) / 1000:.1f}")
+                    print(f"  trace cta#{c}: " + " ".join(row))
+            continue
         for sp in [int(s) for s in args.splits.split(",")]:
             splits = sp or ops.mla_decode_splits(B, H, L, ops.kernels().num_sms(), impl=impl)
             o_part = torch.empty(B, splits, H, 512, device=dev, dtype=torch.float32)

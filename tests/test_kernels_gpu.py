@@ -48,6 +48,31 @@ def test_linear_split_k_cluster(splits):
     _status_ok()
 
 
+@pytest.mark.parametrize("T,O,K", [(64, 9792, 2048),    # 77 tiles: units spread over every SM
+                                   (64, 2048, 8192),    # 16 tiles, long K: many partial slots per tile
+                                   (64, 64, 2048),      # one tile
+                                   (16, 1408, 1000),    # ragged last K block
+                                   (128, 3648, 128)])   # two K blocks per tile
+def test_linear_stream_k_split(T, O, K):
+    """Decode GEMMs with fewer tiles than SMs use the stream-K split: partial sums
+    reduced here (linear) or left as slabs (linear_slabs) must both equal the fp32
+    product, also on a second call through the same workspace."""
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(T + O + K)
+    x = torch.randn(T, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(O, K, device=DEV, generator=g) * 0.02).bfloat16()
+    ref = x.float() @ w.float().t()
+    for _ in range(2):
+        _close(ops.linear(x, w), ref)
+        sl = ops.linear_slabs(x, w, out_dtype=torch.float32)
+        if isinstance(sl, ops.Slabs):
+            got = sl.ws[: sl.splits * sl.stride].view(sl.splits, T, O).sum(0)
+        else:
+            got = sl
+        _close(got, ref)
+    _status_ok()
+
+
 @pytest.mark.parametrize("T,O,K", [(1000, 3648, 2048), (4096, 2048, 2048), (300, 102400 // 8, 2048), (513, 4096, 512)])
 def test_linear_prefill(T, O, K):
     ops = _ops()
@@ -224,7 +249,7 @@ def _mla_ref(q, cache, bt, ctx, scale):
     return out
 
 
-@pytest.mark.parametrize("impl", ["tc", "mma"])
+@pytest.mark.parametrize("impl", ["tc", "mma", "sk"])
 @pytest.mark.parametrize("H,splits", [(16, 1), (16, 3), (32, 2), (64, 1), (128, 4)])
 def test_mla_decode(H, splits, impl):
     ops = _ops()
@@ -238,6 +263,45 @@ def test_mla_decode(H, splits, impl):
     scale = 1.0 / math.sqrt(192)
     ops.mla_decode(q, cache, bt, ctx, out, splits, scale, impl=impl)
     _close(out, _mla_ref(q, cache, bt, ctx, scale), atol=2e-2, rtol=2e-2)
+    _status_ok()
+
+
+@pytest.mark.parametrize("H", [16, 64])
+def test_mla_decode_stream_k_balanced_schedule_graph_replay(H):
+    """Stream-K decode on a decode-shaped batch (many sequences split over several
+    CTAs, short ones kept whole, an idle row), three launches in a row (the arrival
+    counters must come back to zero) and a CUDA-graph replay, where the kernel loads
+    earlier-position KV before its dependency wait."""
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(100 + H)
+    B, maxb = 48, 20
+    nblocks = B * maxb
+    cache = torch.randn(nblocks * 64, 576, device=DEV, generator=g).bfloat16()
+    lens = [int(x) for x in torch.randint(1, maxb * 64, (B,), generator=g, device=DEV)]
+    lens[3], lens[7], lens[11] = 0, 1, maxb * 64
+    ctx = torch.tensor(lens, device=DEV, dtype=torch.int32)
+    bt = torch.randperm(nblocks, device=DEV, generator=g).int().view(B, maxb)
+    q = torch.randn(B, H, 576, device=DEV, generator=g).bfloat16()
+    scale = 1.0 / math.sqrt(192)
+    ref = _mla_ref(q, cache, bt, ctx, scale)
+    for _ in range(3):
+        out = torch.full((B, H, 512), 7.0, device=DEV, dtype=torch.bfloat16)
+        ops.mla_decode(q, cache, bt, ctx, out, 1, scale, impl="sk")
+        _close(out, ref, atol=2e-2, rtol=2e-2)
+    _status_ok()
+    out = torch.empty(B, H, 512, device=DEV, dtype=torch.bfloat16)
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s), torch.cuda.graph(graph, stream=s):
+        ops.mla_decode(q, cache, bt, ctx, out, 1, scale, impl="sk")
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(2):
+        out.fill_(7.0)
+        graph.replay()
+        torch.cuda.synchronize()
+        _close(out, ref, atol=2e-2, rtol=2e-2)
+    del graph
     _status_ok()
 
 

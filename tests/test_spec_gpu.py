@@ -85,7 +85,7 @@ def test_greedy_spec_decode_equals_greedy_target(use_graph):
         for i in range(lens[b], s.shape[0]):
             row = tl[i - 1]
             # every committed token is the target's greedy choice (up to near ties)
-            assert row[int(s[i])] >= row.max() - 0.05, (b, i)
+            assert row[int(s[i])] >= row.max() - 0.1, (b, i)  # ~3 bf16 ulps, as below
     assert ops.status_word() == 0
     sd.release()
 
@@ -133,7 +133,10 @@ def test_forced_acceptance_rate():
         for n, kind in enumerate(kinds[b]):
             i = 17 + n  # position of the committed token
             row = (dl if kind == "d" else tl)[i - 1]
-            assert row[int(s[i])] >= row.max() - 0.05, (b, i, kind)
+            # the step-by-step decode and this full-sequence recompute round their bf16
+            # logits differently (other split-K and attention orders): a near-tie may
+            # resolve either way within ~3 bf16 ulps at |logit| ~ 4
+            assert row[int(s[i])] >= row.max() - 0.1, (b, i, kind)
     assert ops.status_word() == 0
     sd.release()
 
