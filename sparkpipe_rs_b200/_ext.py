@@ -37,6 +37,37 @@ CUDA_FLAGS = CUDA_ARCH_FLAGS + [
 ]
 CXX_FLAGS = ["-O3", "-std=c++17"]
 
+# SPARKPIPE_SANITIZE=address (AddressSanitizer + UndefinedBehaviorSanitizer) or thread
+# (ThreadSanitizer) builds the host runtime extension `_sp_core` instrumented, into its
+# own directory, and loads that build; the sanitizer runtime must be preloaded into the
+# interpreter (utils/sanitize.py does both). The CUDA extension is never instrumented.
+SANITIZE = os.environ.get("SPARKPIPE_SANITIZE", "")
+_SAN_FLAGS = {
+    "address": ["-fsanitize=address,undefined", "-fno-sanitize-recover=undefined", "-fno-omit-frame-pointer",
+                "-g", "-O1"],
+    "thread": ["-fsanitize=thread", "-fno-omit-frame-pointer", "-g", "-O1"],
+}
+if SANITIZE and SANITIZE not in _SAN_FLAGS:
+    raise RuntimeError(f"SPARKPIPE_SANITIZE must be one of {sorted(_SAN_FLAGS)}")
+
+
+def _sanitizer_link_flags() -> list[str]:
+    """-fsanitize for the link plus the directory of the sanitizer runtime as the system
+    compiler reports it (a compiler wrapper may not search that directory itself)."""
+    import subprocess
+
+    lib = "libasan.so" if SANITIZE == "address" else "libtsan.so"
+    flags = [f"-fsanitize={'address,undefined' if SANITIZE == 'address' else 'thread'}"]
+    for cc in ("g++", "/usr/bin/g++"):
+        try:
+            path = subprocess.run([cc, f"-print-file-name={lib}"], capture_output=True, text=True).stdout.strip()
+        except OSError:
+            continue
+        if os.path.isabs(path) and os.path.exists(path):
+            flags.append(f"-L{os.path.dirname(path)}")
+            break
+    return flags
+
 
 def _kernel_sources() -> list[Path]:
     d = CSRC / "kernels"
@@ -64,6 +95,20 @@ _lock = threading.Lock()
 _loaded: dict[str, object] = {}
 
 
+def _sanitized(name: str) -> bool:
+    return bool(SANITIZE) and not SPECS[name]["cuda"]
+
+
+def _cxx_flags(name: str) -> list[str]:
+    if _sanitized(name):
+        return ["-std=c++17"] + _SAN_FLAGS[SANITIZE]
+    return CXX_FLAGS
+
+
+def _build_dir(name: str) -> Path:
+    return EXT_DIR / (f"{name}_{SANITIZE}" if _sanitized(name) else name)
+
+
 def _digest(name: str) -> str:
     spec = SPECS[name]
     h = hashlib.sha256()
@@ -71,7 +116,7 @@ def _digest(name: str) -> str:
         h.update(p.name.encode())
         h.update(p.read_bytes())
     h.update(repr(CUDA_FLAGS if spec["cuda"] else []).encode())
-    h.update(repr(CXX_FLAGS).encode())
+    h.update(repr(_cxx_flags(name)).encode())
     import torch
 
     h.update(torch.__version__.encode())
@@ -79,7 +124,7 @@ def _digest(name: str) -> str:
 
 
 def _so_path(name: str) -> Path:
-    return EXT_DIR / name / f"{name}.so"
+    return _build_dir(name) / f"{name}.so"
 
 
 def _import_so(name: str, path: Path):
@@ -96,7 +141,7 @@ def build(name: str, verbose: bool = False):
     from torch.utils import cpp_extension
 
     spec = SPECS[name]
-    out = EXT_DIR / name
+    out = _build_dir(name)
     out.mkdir(parents=True, exist_ok=True)
     os.environ.setdefault("MAX_JOBS", str(max(1, os.cpu_count() or 1)))
     srcs = [str(p) for p in spec["sources"]()]
@@ -105,7 +150,7 @@ def build(name: str, verbose: bool = False):
     kw = dict(
         name=name,
         sources=srcs,
-        extra_cflags=CXX_FLAGS,
+        extra_cflags=_cxx_flags(name),
         build_directory=str(out),
         verbose=verbose,
         with_cuda=spec["cuda"],
@@ -115,7 +160,7 @@ def build(name: str, verbose: bool = False):
         kw["extra_include_paths"] = [str(CSRC / "kernels")]
     else:
         kw["extra_include_paths"] = [str(CSRC / "core"), str(INCLUDE)]
-        kw["extra_ldflags"] = ["-ldl"]
+        kw["extra_ldflags"] = ["-ldl"] + (_sanitizer_link_flags() if _sanitized(name) else [])
     mod = cpp_extension.load(**kw)
     (out / f"{name}.srchash").write_text(_digest(name))
     _loaded[name] = mod
@@ -128,7 +173,7 @@ def load(name: str):
         if name in _loaded:
             return _loaded[name]
         so = _so_path(name)
-        stamp = EXT_DIR / name / f"{name}.srchash"
+        stamp = _build_dir(name) / f"{name}.srchash"
         if so.exists() and stamp.exists() and stamp.read_text().strip() == _digest(name):
             mod = _import_so(name, so)
         else:
@@ -142,7 +187,7 @@ def build_all(verbose: bool = False) -> None:
         if not SPECS[name]["sources"]():
             continue
         so = _so_path(name)
-        stamp = EXT_DIR / name / f"{name}.srchash"
+        stamp = _build_dir(name) / f"{name}.srchash"
         if so.exists() and stamp.exists() and stamp.read_text().strip() == _digest(name):
             continue
         build(name, verbose=verbose)

@@ -245,11 +245,11 @@ void Tokenizer::encode_piece(const char* p, size_t n, std::vector<uint32_t>& out
   if (cache) {
     auto it = cache->find(key);
     if (it != cache->end()) {
-      ++hits_;
+      hits_.fetch_add(1, std::memory_order_relaxed);
       out.insert(out.end(), it->second.begin(), it->second.end());
       return;
     }
-    ++misses_;
+    misses_.fetch_add(1, std::memory_order_relaxed);
   }
   // symbols: one per byte, doubly linked; merges applied lowest rank first
   std::vector<int64_t> sym(n);

@@ -15,6 +15,7 @@
 // crates/spark-text/src/chat_template.rs:25-215.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <memory>
 #include <mutex>
@@ -42,8 +43,8 @@ class Tokenizer {
   int64_t token_to_id(const std::string& token) const;  // byte-level token string; -1 if absent
   bool is_special(uint32_t id) const;
   int64_t unk_id() const { return unk_; }
-  uint64_t cache_hits() const { return hits_; }
-  uint64_t cache_misses() const { return misses_; }
+  uint64_t cache_hits() const { return hits_.load(std::memory_order_relaxed); }
+  uint64_t cache_misses() const { return misses_.load(std::memory_order_relaxed); }
 
   // piece boundaries of `text` (start, length) with the GPT-2 byte classes
   static std::vector<std::pair<uint32_t, uint32_t>> split_pieces(const std::string& text);
@@ -73,7 +74,8 @@ class Tokenizer {
   int64_t unk_ = -1;
   mutable Cache cache_;
   mutable std::mutex cache_mu_;
-  mutable uint64_t hits_ = 0, misses_ = 0;
+  // statistics, bumped by every encode thread of a batch
+  mutable std::atomic<uint64_t> hits_{0}, misses_{0};
   static constexpr size_t kCacheCap = 16384;
 };
 

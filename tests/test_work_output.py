@@ -137,6 +137,7 @@ def test_send_to_rank_daemon_and_duplicates():
     out.enqueue(packet(2, seqs=(2,)))
     assert pump_until(out) == OK and out.stats.duplicates == 1
     out.drop_socket()
+    peer.join(5)  # the peer sees end of stream; close its socket only after it stopped reading
     b.close()
 
 
@@ -157,6 +158,7 @@ def test_hard_negative_and_full_receiver():
     assert failed == [(2, VF)] and out.queued == 0
     assert peer.seen[0] == peer.seen[1]  # the resend is byte-identical
     out.drop_socket()
+    peer.join(5)  # the peer sees end of stream; close its socket only after it stopped reading
     b.close()
 
 
@@ -181,6 +183,7 @@ def test_broken_connection_then_reconnect_over_tcp():
     assert pump_until(out) == OK and out.stats.acknowledged == 1 and out.stats.socket_drops == 1
     assert len(peer.seen) == 1 and WC.deserialize(peer.seen[0]).identity.transaction_id == 1
     out.drop_socket()
+    peer.join(5)
     conn2.close()
     srv.close()
 
