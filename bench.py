@@ -56,6 +56,9 @@ def parse_args():
                     help="diagnostic only: run the first N layers (a result with it is not the named workload)")
     ap.add_argument("--prefill-chunk", type=int, default=0,
                     help="max tokens per prefill forward (default 8192; 2048 for k2)")
+    ap.add_argument("--weights-pack", default="",
+                    help="load the model's weights from this stage-pack checkpoint directory (written first, "
+                         "from the seeded random init, when it has no index yet)")
     return ap.parse_args()
 
 
@@ -66,6 +69,27 @@ def reference_arm(args):
                        "pyproject.toml), this image has no Rust toolchain, and its GPU kernels are not in its tree",
         "metric": METRIC, "n_gpus": args.gpus,
     }))
+
+
+def load_weights_pack(root, cfg, dev, ep, rank, world):
+    """This rank's weights from a stage pack (an expert-parallel rank reads only its
+    experts); rank 0 writes the pack from the seeded random init if it has none."""
+    import os as _os
+
+    import torch
+    import torch.distributed as dist
+
+    from sparkpipe_rs_b200.core import core
+    from sparkpipe_rs_b200.models.checkpoint import load_pack, save_pack
+    from sparkpipe_rs_b200.models.weights import init_weights
+
+    index = _os.path.join(root, core().stagepack.INDEX_FILE)
+    if rank == 0 and not _os.path.exists(index):
+        save_pack(root, cfg, init_weights(cfg, seed=0, device=dev, dtype=torch.bfloat16))
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+    return load_pack(root, cfg, device=dev, experts=ep.local_expert_range() if ep is not None else None)
 
 
 def main():
@@ -109,8 +133,12 @@ def main():
     if par == "ep" and world > 1:
         ep = ExpertParallel(cfg, rank, world, max(B, seqs_per_chunk * P), dev, group=dist.group.WORLD)
     torch.manual_seed(1234 + rank)
-    model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=P + args.output + args.warmup + args.steps + 64,
-                        ep=ep)
+    weights = None
+    if args.weights_pack:
+        weights = load_weights_pack(args.weights_pack, cfg, dev, ep, rank, world)
+    model = MLAMoEModel(cfg, weights=weights, seed=0, device=dev,
+                        max_positions=P + args.output + args.warmup + args.steps + 64, ep=ep)
+    del weights
     def _nbytes(t):
         if isinstance(t, ops.Fp8Weight):
             return t.q.numel() + t.s.numel() * 4
