@@ -237,7 +237,43 @@ void bind_prefix(py::module_& m) {
       .def_property_readonly("stats", &PrefixCache::stats);
 }
 
+void bind_speculation(py::module_& m) {
+  auto s = m.def_submodule("speculation", "speculative-decode policy: lane EMA, row allocator, utility");
+  s.attr("EMA_INITIAL_MILLI") = spec::kEmaInitialMilli;
+  s.attr("SUPPRESS_MILLI") = spec::kSuppressMilli;
+  s.attr("REPROBE_INTERVAL") = spec::kReprobeInterval;
+  s.attr("MAX_SPECULATIVE_TOKENS") = spec::kMaxSpeculativeTokens;
+  s.def("alpha_milli", &spec::alpha_milli);
+  s.def("row_allocator_assign",
+        [](const std::vector<std::tuple<uint32_t, uint32_t, uint32_t>>& lanes, uint32_t cap, uint32_t cost) {
+          std::vector<spec::SlotInput> in;
+          for (const auto& t : lanes) in.push_back(spec::SlotInput{std::get<0>(t), std::get<1>(t), std::get<2>(t)});
+          std::vector<uint32_t> out(in.size(), 0);
+          const uint32_t total = spec::row_allocator_assign(in, cap, cost, out);
+          return py::make_tuple(total, out);
+        },
+        py::arg("lanes"), py::arg("firing_row_cap"), py::arg("spec_row_relative_cost_milli") = 1000);
+  s.def("observe",
+        [](uint32_t ema, uint32_t budget, uint32_t countdown, const std::vector<std::pair<char, uint32_t>>& events,
+           uint32_t full) {
+          // replays ('v', committed) verify rounds and ('p', committed) plain steps on one lane
+          spec::LaneState l;
+          l.ema_milli = ema;
+          l.budget = budget;
+          l.countdown = countdown;
+          py::list out;
+          for (const auto& e : events) {
+            if (e.first == 'v') spec::observe_verify(l, e.second, full);
+            else spec::observe_plain(l, e.second, full);
+            out.append(py::make_tuple(l.ema_milli, l.budget, l.countdown));
+          }
+          return out;
+        });
+  s.def("outranks_plain", &spec::outranks_plain);
+}
+
 void bind_scheduler(py::module_& m) {
+  bind_speculation(m);
   py::enum_<SlotState>(m, "SlotState")
       .value("FREE", SlotState::Free)
       .value("QUEUED_PREFILL", SlotState::QueuedPrefill)
@@ -264,6 +300,12 @@ void bind_scheduler(py::module_& m) {
   m.attr("DECISION_PREFILL_STEP") = kDecisionPrefillStep;
   m.attr("DECISION_SCHEDULED_AHEAD") = kDecisionScheduledAhead;
   m.attr("DECISION_PREEMPTED") = kDecisionPreempted;
+  m.attr("DECISION_SPECULATIVE_VERIFY") = kDecisionSpeculativeVerify;
+  m.attr("DECISION_MTP_TREE_VERIFY") = kDecisionMtpTreeVerify;
+  m.attr("SCHED_MTP_FORCE_ENABLE") = kSchedMtpForceEnable;
+  m.attr("SPEC_OFF") = uint32_t(SpecMode::Off);
+  m.attr("SPEC_CHAIN") = uint32_t(SpecMode::Chain);
+  m.attr("SPEC_MTP_TREE") = uint32_t(SpecMode::MtpTree);
 
   py::class_<SchedulerConfig>(m, "SchedulerConfig")
       .def(py::init<>())
@@ -276,7 +318,12 @@ void bind_scheduler(py::module_& m) {
       .def_readwrite("max_sequences", &SchedulerConfig::max_sequences)
       .def_readwrite("flags", &SchedulerConfig::flags)
       .def_readwrite("max_consecutive_prefills", &SchedulerConfig::max_consecutive_prefills)
-      .def_readwrite("decode_buckets", &SchedulerConfig::decode_buckets);
+      .def_readwrite("decode_buckets", &SchedulerConfig::decode_buckets)
+      .def_readwrite("spec_mode", &SchedulerConfig::spec_mode)
+      .def_readwrite("spec_draft_len", &SchedulerConfig::spec_draft_len)
+      .def_readwrite("spec_row_cap", &SchedulerConfig::spec_row_cap)
+      .def_readwrite("spec_row_cost_milli", &SchedulerConfig::spec_row_cost_milli)
+      .def_readwrite("spec_shadow_slot_base", &SchedulerConfig::spec_shadow_slot_base);
   py::class_<RequestSpec>(m, "RequestSpec")
       .def(py::init<>())
       .def(py::init([](uint64_t id, const std::vector<uint32_t>& prompt, uint32_t max_new, uint32_t priority,
@@ -302,7 +349,8 @@ void bind_scheduler(py::module_& m) {
       .def_readwrite("max_new_tokens", &RequestSpec::max_new_tokens)
       .def_readwrite("priority", &RequestSpec::priority)
       .def_readwrite("stop_token_ids", &RequestSpec::stop_token_ids)
-      .def_readwrite("ignore_eos", &RequestSpec::ignore_eos);
+      .def_readwrite("ignore_eos", &RequestSpec::ignore_eos)
+      .def_readwrite("disable_speculation", &RequestSpec::disable_speculation);
   py::class_<StepPlan>(m, "StepPlan")
       .def_readonly("kind", &StepPlan::kind)
       .def_readonly("flags", &StepPlan::flags)
@@ -328,6 +376,50 @@ void bind_scheduler(py::module_& m) {
       .def_property_readonly("block_table", [](const StepPlan& p) { return to_np(p.block_table); })
       .def_property_readonly("context_lens", [](const StepPlan& p) { return to_np(p.context_lens); })
       .def_property_readonly("src_rows", [](const StepPlan& p) { return to_np(p.src_rows); })
+      .def_readonly("rows_per_seq", &StepPlan::rows_per_seq)
+      .def_property_readonly("draft_budget", [](const StepPlan& p) { return to_np(p.draft_budget); })
+      .def_property_readonly("accept_keys", [](const StepPlan& p) {
+        py::array_t<int64_t> a((py::ssize_t)p.accept_keys.size());
+        std::memcpy(a.mutable_data(), p.accept_keys.data(), p.accept_keys.size() * 8);
+        return a;
+      })
+      .def_property_readonly("sync_token_ids", [](const StepPlan& p) { return to_np(p.sync_token_ids); })
+      .def_property_readonly("sync_positions", [](const StepPlan& p) { return to_np(p.sync_positions); })
+      .def_property_readonly("sync_slots", [](const StepPlan& p) { return to_np(p.sync_slots); })
+      // Verify inputs into preallocated (pinned) CPU tensors: the row arrays
+      // [rows x padded], the per-sequence block table, draft budgets and acceptance
+      // keys, and (tree) the draft-sync rows. Returns the bytes written.
+      .def("write_verify_inputs",
+           [](const StepPlan& p, const torch::Tensor& ids, const torch::Tensor& pos, const torch::Tensor& slots,
+              const torch::Tensor& ctx, const torch::Tensor& bt, const torch::Tensor& budget,
+              const torch::Tensor& keys, const c10::optional<torch::Tensor>& sync) {
+             TORCH_CHECK(p.kind == StepPlan::Verify, "not a verify plan");
+             copy_into(ids, p.token_ids.data(), p.token_ids.size() * 4);
+             copy_into(pos, p.positions.data(), p.positions.size() * 4);
+             copy_into(slots, p.slot_mapping.data(), p.slot_mapping.size() * 4);
+             copy_into(ctx, p.context_lens.data(), p.context_lens.size() * 4);
+             copy_into(budget, p.draft_budget.data(), p.draft_budget.size() * 4);
+             copy_into(keys, p.accept_keys.data(), p.accept_keys.size() * 8);
+             const int64_t cols = bt.size(1);
+             TORCH_CHECK(bt.size(0) >= p.padded_seqs, "block table tensor has too few rows");
+             int32_t* dst = bt.data_ptr<int32_t>();
+             for (uint32_t r = 0; r < p.padded_seqs; ++r)
+               std::memcpy(dst + r * cols, p.block_table.data() + size_t(r) * p.max_blocks,
+                           sizeof(int32_t) * std::min<int64_t>(cols, p.max_blocks));
+             int64_t bytes = int64_t(p.token_ids.size() * 16 + p.draft_budget.size() * 12) +
+                             int64_t(p.padded_seqs) * cols * 4;
+             if (sync.has_value() && !p.sync_slots.empty()) {
+               // [3][n] token ids, positions, slots
+               const size_t n = p.sync_slots.size();
+               TORCH_CHECK(sync->numel() >= int64_t(3 * n), "sync tensor too small");
+               int32_t* d = sync->data_ptr<int32_t>();
+               std::memcpy(d, p.sync_token_ids.data(), n * 4);
+               std::memcpy(d + n, p.sync_positions.data(), n * 4);
+               std::memcpy(d + 2 * n, p.sync_slots.data(), n * 4);
+               bytes += int64_t(12 * n);
+             }
+             return bytes;
+           })
       // Fast path: copy the decode inputs into preallocated (pinned) CPU tensors.
       .def("write_decode_inputs",
            [](const StepPlan& p, const torch::Tensor& ids, const torch::Tensor& pos, const torch::Tensor& slots,
@@ -356,6 +448,7 @@ void bind_scheduler(py::module_& m) {
       .def_readonly("steps", &SchedulerStats::steps)
       .def_readonly("prefill_steps", &SchedulerStats::prefill_steps)
       .def_readonly("decode_steps", &SchedulerStats::decode_steps)
+      .def_readonly("verify_steps", &SchedulerStats::verify_steps)
       .def_readonly("preemptions", &SchedulerStats::preemptions)
       .def_readonly("prefill_tokens", &SchedulerStats::prefill_tokens)
       .def_readonly("decode_tokens", &SchedulerStats::decode_tokens)
@@ -388,6 +481,50 @@ void bind_scheduler(py::module_& m) {
              TORCH_CHECK(!t.is_cuda() && t.scalar_type() == at::kInt && t.is_contiguous(), "int32 CPU tensor");
              return s.complete(p, t.data_ptr<int32_t>(), (uint32_t)t.numel());
            })
+      .def("complete_verify",
+           [](Scheduler& s, const StepPlan& p, py::array_t<int32_t, py::array::c_style | py::array::forcecast> committed,
+              py::array_t<int32_t, py::array::c_style | py::array::forcecast> counts,
+              py::object paths) {
+             TORCH_CHECK(committed.ndim() == 2, "committed: [sequences, stride]");
+             const int32_t* pp = nullptr;
+             py::array_t<int32_t, py::array::c_style | py::array::forcecast> pa;
+             if (!paths.is_none()) {
+               pa = paths.cast<py::array_t<int32_t, py::array::c_style | py::array::forcecast>>();
+               TORCH_CHECK(pa.size() >= counts.size(), "paths shorter than counts");
+               pp = pa.data();
+             }
+             TORCH_CHECK(committed.shape(0) >= counts.size(), "committed rows shorter than counts");
+             return s.complete_verify(p, committed.data(), (uint32_t)committed.shape(1), counts.data(), pp,
+                                      (uint32_t)counts.size());
+           },
+           py::arg("plan"), py::arg("committed"), py::arg("counts"), py::arg("paths") = py::none())
+      .def("set_step_cost", &Scheduler::set_step_cost, py::arg("kind"), py::arg("seqs"), py::arg("ns"))
+      .def("estimate_step_ns", &Scheduler::estimate_step_ns)
+      .def("lane_state",
+           [](const Scheduler& s, uint64_t id) {
+             const spec::LaneState l = s.lane_state(id);
+             py::dict d;
+             d["ema_milli"] = l.ema_milli;
+             d["budget"] = l.budget;
+             d["countdown"] = l.countdown;
+             d["disabled"] = l.disabled;
+             return d;
+           })
+      .def_property_readonly("spec_rows_per_seq", &Scheduler::spec_rows_per_seq)
+      .def_property_readonly("spec_totals",
+                             [](const Scheduler& s) {
+                               const spec::Totals& t = s.spec_totals();
+                               py::dict d;
+                               d["rounds"] = t.rounds;
+                               d["proposed"] = t.proposed;
+                               d["accepted"] = t.accepted;
+                               d["committed"] = t.committed;
+                               d["verify_steps"] = t.verify_steps;
+                               d["suppressed"] = t.suppressed;
+                               d["reprobes"] = t.reprobes;
+                               d["expected_committed_milli"] = spec::expected_committed_scaled(t);
+                               return d;
+                             })
       .def("cancel", &Scheduler::cancel)
       .def("fail_step", &Scheduler::fail_step)
       .def("has_work", &Scheduler::has_work)

@@ -2,6 +2,8 @@
 
 #include <algorithm>
 
+#include "work_control.h"
+
 namespace spc {
 
 Scheduler::Scheduler(const SchedulerConfig& cfg) : cfg_(cfg) {
@@ -9,8 +11,34 @@ Scheduler::Scheduler(const SchedulerConfig& cfg) : cfg_(cfg) {
       cfg.max_model_len < 2 || cfg.max_sequences == 0)
     fail(Status::InvalidArgument, "Scheduler: invalid configuration");
   std::sort(cfg_.decode_buckets.begin(), cfg_.decode_buckets.end());
+  if (cfg.spec_mode > uint32_t(SpecMode::MtpTree)) fail(Status::InvalidArgument, "Scheduler: unknown speculation mode");
+  if (cfg.spec_mode == uint32_t(SpecMode::Chain) &&
+      (cfg.spec_draft_len == 0 || cfg.spec_draft_len > spec::kMaxSpeculativeTokens))
+    fail(Status::InvalidArgument, "Scheduler: chain draft length must be 1..7");
+  if (cfg.spec_mode == uint32_t(SpecMode::MtpTree) && cfg.spec_shadow_slot_base < 0)
+    fail(Status::InvalidArgument, "Scheduler: tree speculation needs shadow slots");
   cache_ = std::make_unique<PrefixCache>(cfg.block_tokens, cfg.num_blocks, cfg.max_sequences);
   max_blocks_ = (cfg.max_model_len + cfg.block_tokens - 1) / cfg.block_tokens;
+}
+
+uint32_t Scheduler::full_budget() const {
+  return cfg_.spec_mode == uint32_t(SpecMode::MtpTree) ? wc::mtp::kCandidates : cfg_.spec_draft_len;
+}
+
+uint32_t Scheduler::spec_rows_per_seq() const {
+  if (cfg_.spec_mode == uint32_t(SpecMode::MtpTree)) return wc::mtp::kVerifierRows;
+  if (cfg_.spec_mode == uint32_t(SpecMode::Chain)) return cfg_.spec_draft_len + 1;
+  return 1;
+}
+
+uint64_t Scheduler::estimate_step_ns(uint32_t kind, uint32_t seqs) const {
+  return cost_.estimate(kind, bucket_for(seqs), kind == StepPlan::Verify ? spec_rows_per_seq() : 1);
+}
+
+spec::LaneState Scheduler::lane_state(uint64_t id) const {
+  auto it = reqs_.find(id);
+  if (it == reqs_.end()) fail(Status::NotFound, "Scheduler: unknown request");
+  return it->second.lane;
 }
 
 uint32_t Scheduler::bucket_for(uint32_t n) const {
@@ -37,6 +65,8 @@ void Scheduler::add_request(const RequestSpec& spec) {
   r.prompt_len = (uint32_t)spec.prompt.size();
   r.arrival = ++arrival_clock_;
   r.state = SlotState::QueuedPrefill;
+  r.lane.disabled = spec.disable_speculation || spec.temperature > 0.f || cfg_.spec_mode == 0;
+  r.lane.budget = r.lane.disabled ? 0 : full_budget();
   // priority order (higher first), arrival order within a priority
   auto pos = waiting_.end();
   for (auto it = waiting_.begin(); it != waiting_.end(); ++it) {
@@ -79,7 +109,12 @@ StepPlan Scheduler::schedule() {
   }
   if (running_count_ > 0) {
     consecutive_prefills_ = 0;
-    return build_decode();
+    StepPlan d = build_decode();
+    if (cfg_.spec_mode && d.kind == StepPlan::Decode) {
+      StepPlan v = try_build_verify(d);
+      if (v.kind == StepPlan::Verify) return v;
+    }
+    return d;
   }
   return StepPlan{};
 }
@@ -235,6 +270,131 @@ StepPlan Scheduler::build_decode() {
   return p;
 }
 
+namespace {
+uint64_t mix64(uint64_t z) {  // SplitMix64 finaliser (Steele, Lea & Flood, OOPSLA 2014)
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+}  // namespace
+
+bool Scheduler::spec_grants(const std::vector<uint64_t>& ids, std::vector<uint32_t>& grant) const {
+  const bool tree = cfg_.spec_mode == uint32_t(SpecMode::MtpTree);
+  const uint32_t n = (uint32_t)ids.size(), full = full_budget();
+  if (!cfg_.spec_mode || n == 0) return false;
+  std::vector<spec::SlotInput> in(n);
+  for (uint32_t i = 0; i < n; ++i) {
+    const Req& r = reqs_.at(ids[i]);
+    const uint32_t len = (uint32_t)r.tokens.size();
+    const uint32_t remaining = r.spec.max_new_tokens > r.generated ? r.spec.max_new_tokens - r.generated : 0;
+    uint32_t depth = spec::max_depth(r.lane, full);
+    // a round commits at most depth + 1 tokens, within the length budget and the context
+    if (tree) {
+      if (remaining < wc::mtp::kMaxCommitted + 1 || len + wc::mtp::kMaxCommitted > cfg_.max_model_len) depth = 0;
+    } else {
+      depth = std::min(depth, remaining ? remaining - 1 : 0);
+      depth = std::min(depth, cfg_.max_model_len > len ? cfg_.max_model_len - len - 1 : 0);
+    }
+    in[i] = spec::SlotInput{r.lane.ema_milli, depth, 0};
+  }
+  const uint32_t rows = spec_rows_per_seq();
+  const uint32_t cap = cfg_.spec_row_cap ? cfg_.spec_row_cap : rows * cfg_.max_batch;
+  spec::row_allocator_assign(in, cap, cfg_.spec_row_cost_milli, grant);
+  bool any = false, all = true;
+  for (uint32_t g : grant) {
+    any |= g > 0;
+    all &= g == full;
+  }
+  // the tree verifies a batch only when every lane drafts the full tree
+  if (tree ? !all : !any) return false;
+  if (cfg_.flags & kSchedMtpForceEnable) return true;
+  const uint64_t plain = estimate_step_ns(StepPlan::Decode, n), round = estimate_step_ns(StepPlan::Verify, n);
+  return spec::outranks_plain(spec::expected_committed_scaled(spec_), n, n, plain, round);
+}
+
+StepPlan Scheduler::try_build_verify(const StepPlan& d) {
+  const bool tree = cfg_.spec_mode == uint32_t(SpecMode::MtpTree);
+  const uint32_t n = d.num_seqs, Bp = d.padded_seqs, rows = spec_rows_per_seq();
+  std::vector<uint32_t> grant;
+  if (!spec_grants(d.seq_ids, grant)) return StepPlan{};
+  // KV blocks for every position a lane's rows write; without them this step decodes plainly
+  for (uint32_t i = 0; i < n; ++i) {
+    if (!grant[i]) continue;
+    const Req& r = reqs_.at(d.seq_ids[i]);
+    const uint32_t ext = tree ? wc::mtp::kContextExtension : grant[i];
+    try {
+      cache_->ensure_sequence_token_capacity(d.seq_ids[i], (uint32_t)r.tokens.size() + ext);
+    } catch (const StatusError& e) {
+      if (e.status == Status::CapacityExceeded) return StepPlan{};
+      throw;
+    }
+  }
+  StepPlan v;
+  v.kind = StepPlan::Verify;
+  v.flags = kDecisionDecodeStep | kDecisionSpeculativeVerify | (tree ? kDecisionMtpTreeVerify : 0u) |
+            (d.flags & (kDecisionCudaGraphPadding | kDecisionPreempted));
+  v.step_index = d.step_index;
+  v.num_seqs = n;
+  v.padded_seqs = Bp;
+  v.max_blocks = max_blocks_;
+  v.rows_per_seq = rows;
+  v.seq_ids = d.seq_ids;
+  v.block_table.assign(size_t(Bp) * max_blocks_, 0);
+  const size_t R = size_t(rows) * Bp;
+  v.token_ids.assign(R, 0);
+  v.positions.assign(R, 0);
+  v.slot_mapping.assign(R, -1);
+  v.context_lens.assign(R, 0);
+  v.draft_budget.assign(Bp, 0);
+  v.accept_keys.assign(Bp, 0);
+  if (tree) {
+    v.sync_token_ids.assign(size_t(3) * Bp, 0);
+    v.sync_positions.assign(size_t(3) * Bp, 0);
+    v.sync_slots.assign(size_t(3) * Bp, -1);
+  }
+  for (uint32_t b = 0; b < n; ++b) {
+    const uint64_t id = d.seq_ids[b];
+    Req& r = reqs_.at(id);
+    const uint32_t len = (uint32_t)r.tokens.size(), p = len - 1;
+    const auto& blocks = cache_->block_list(id);
+    std::copy(blocks.begin(), blocks.end(), v.block_table.begin() + size_t(b) * max_blocks_);
+    v.draft_budget[b] = int32_t(grant[b]);
+    v.accept_keys[b] = mix64(id);
+    v.token_ids[b] = int32_t(r.tokens.back());
+    for (uint32_t j = 0; j < rows; ++j) {
+      if (!tree && j > grant[b]) break;  // rows past the lane's budget stay idle
+      const uint32_t depth = tree ? wc::mtp::node_at(j)->depth : j;
+      const uint32_t q = p + depth;
+      const size_t row = size_t(j) * Bp + b;
+      v.positions[row] = int32_t(q);
+      v.context_lens[row] = int32_t(q + 1);
+      // the tree's alternate leaves (rows 3 and 5) share a position with a primary
+      // row: their KV goes to this batch row's shadow slots
+      if (tree && (j == 3 || j == 5))
+        v.slot_mapping[row] = int32_t(cfg_.spec_shadow_slot_base + 2 * int64_t(b) + (j == 5 ? 1 : 0));
+      else
+        v.slot_mapping[row] = slot_of(r, id, q);
+    }
+    if (tree) {
+      for (uint32_t k = 0; k < 3; ++k) {
+        if (p < 3 - k) continue;
+        const uint32_t q = p - 3 + k;
+        const size_t row = size_t(k) * Bp + b;
+        v.sync_token_ids[row] = int32_t(r.tokens[q]);
+        v.sync_positions[row] = int32_t(q);
+        v.sync_slots[row] = slot_of(r, id, q);
+      }
+    }
+    v.max_context = std::max(v.max_context, p + (tree ? wc::mtp::kContextExtension : grant[b]) + 1);
+    r.state = SlotState::RunningSpeculativeVerify;
+  }
+  v.num_tokens = n;
+  --stats_.decode_steps;
+  ++stats_.verify_steps;
+  return v;
+}
+
 StepPlan Scheduler::schedule_ahead(const StepPlan& inflight) {
   if (inflight.kind != StepPlan::Decode) return StepPlan{};
   // the policy would run a prefill next (a waiting prompt and a free seat)
@@ -247,6 +407,10 @@ StepPlan Scheduler::schedule_ahead(const StepPlan& inflight) {
   if (rows.size() != running_.size()) return StepPlan{};
   for (size_t k = 0; k < rows.size(); ++k)
     if (running_[k] != inflight.seq_ids[rows[k]]) return StepPlan{};
+  if (cfg_.spec_mode) {  // the next step may be a verify round, which needs this step's tokens
+    std::vector<uint32_t> grant;
+    if (spec_grants(running_, grant)) return StepPlan{};
+  }
   // keep the sequences that cannot end by length or context at the in-flight step
   std::vector<uint32_t> keep;
   for (uint32_t i : rows) {
@@ -299,15 +463,6 @@ StepPlan Scheduler::schedule_ahead(const StepPlan& inflight) {
   stats_.decode_tokens += n;
   return p;
 }
-
-namespace {
-uint64_t mix64(uint64_t z) {  // SplitMix64 finaliser (Steele, Lea & Flood, OOPSLA 2014)
-  z += 0x9E3779B97F4A7C15ull;
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
-}
-}  // namespace
 
 bool Scheduler::sampling_rows(const StepPlan& p, float* temp, uint64_t* key, uint32_t rows) const {
   bool any = false;
@@ -370,13 +525,18 @@ std::vector<SchedEvent> Scheduler::complete(const StepPlan& p, const int32_t* sa
     } else {
       r.computed = (uint32_t)r.tokens.size();
       emits = true;
+      if (cfg_.spec_mode && !r.lane.disabled) {
+        const bool was = r.lane.budget == 0 && r.lane.countdown != 0;
+        spec::observe_plain(r.lane, 1, full_budget());
+        if (was && r.lane.budget) ++spec_.reprobes;
+      }
     }
     if (cfg_.flags & kSchedPrefixCache) cache_->commit(id, r.computed);
     const int32_t tok = sampled[i];
     r.tokens.push_back(uint32_t(tok));
     cache_->append_tokens(id, reinterpret_cast<const uint32_t*>(&tok), 1);
     ++r.generated;
-    r.state = SlotState::ReadyDecode;
+    r.state = r.lane.budget ? SlotState::ReadySpeculativeVerify : SlotState::ReadyDecode;
     ev.push_back(SchedEvent{SchedEvent::Token, id, tok, 0, r.generated});
     FinishReason why = FinishReason::None;
     if (!r.spec.ignore_eos && std::find(r.spec.stop_token_ids.begin(), r.spec.stop_token_ids.end(), uint32_t(tok)) !=
@@ -388,6 +548,76 @@ std::vector<SchedEvent> Scheduler::complete(const StepPlan& p, const int32_t* sa
       why = FinishReason::ContextLimit;
     if (why != FinishReason::None) finish(r, id, why, ev);
   }
+  return ev;
+}
+
+std::vector<SchedEvent> Scheduler::complete_verify(const StepPlan& p, const int32_t* committed, uint32_t stride,
+                                                   const int32_t* counts, const int32_t* paths, uint32_t n) {
+  std::vector<SchedEvent> ev;
+  if (p.kind != StepPlan::Verify) fail(Status::InvalidArgument, "Scheduler: complete_verify needs a verify plan");
+  if (n < p.num_seqs || stride < p.rows_per_seq) fail(Status::InvalidArgument, "Scheduler: verify results too short");
+  const bool tree = p.flags & kDecisionMtpTreeVerify;
+  if (tree && !paths) fail(Status::InvalidArgument, "Scheduler: tree verify needs resolution paths");
+  const uint32_t full = full_budget();
+  for (uint32_t i = 0; i < p.num_seqs; ++i) {  // validate every lane before applying any
+    const uint32_t c = uint32_t(counts[i]), g = uint32_t(p.draft_budget[i]);
+    if (counts[i] <= 0 || c > g + 1) fail(Status::InvalidArgument, "Scheduler: committed token count out of range");
+    if (tree && (c > wc::mtp::kMaxCommitted ||
+                 !wc::mtp::resolution_is_valid(wc::mtp::kCandidates, c - 1, uint32_t(paths[i]))))
+      fail(Status::InvalidArgument, "Scheduler: invalid tree resolution");
+  }
+  ++spec_.verify_steps;
+  for (uint32_t i = 0; i < p.num_seqs; ++i) {
+    const uint64_t id = p.seq_ids[i];
+    auto it = reqs_.find(id);
+    if (it == reqs_.end()) continue;  // cancelled while the round ran
+    Req& r = it->second;
+    const uint32_t c = uint32_t(counts[i]), g = uint32_t(p.draft_budget[i]);
+    if (g > 0) {
+      spec::observe_verify(r.lane, c, full);
+      if (r.lane.budget == 0) ++spec_.suppressed;
+      ++spec_.rounds;
+      spec_.proposed += g;
+      spec_.accepted += c - 1;
+      spec_.committed += c;
+    } else {
+      const bool was = r.lane.budget == 0 && r.lane.countdown != 0;
+      spec::observe_plain(r.lane, c, full);
+      if (was && r.lane.budget) ++spec_.reprobes;
+    }
+    auto e = append_committed(r, id, committed + size_t(i) * stride, c);
+    ev.insert(ev.end(), e.begin(), e.end());
+  }
+  return ev;
+}
+
+std::vector<SchedEvent> Scheduler::append_committed(Req& r, uint64_t id, const int32_t* toks, uint32_t c) {
+  std::vector<SchedEvent> ev;
+  // the cache now holds the KV of the input token and of the accepted drafts
+  const uint32_t len = (uint32_t)r.tokens.size();
+  for (uint32_t k = 0; k < c; ++k) {
+    const int32_t tok = toks[k];
+    r.tokens.push_back(uint32_t(tok));
+    cache_->append_tokens(id, reinterpret_cast<const uint32_t*>(&tok), 1);
+    ++r.generated;
+    ev.push_back(SchedEvent{SchedEvent::Token, id, tok, 0, r.generated});
+    FinishReason why = FinishReason::None;
+    if (!r.spec.ignore_eos &&
+        std::find(r.spec.stop_token_ids.begin(), r.spec.stop_token_ids.end(), uint32_t(tok)) !=
+            r.spec.stop_token_ids.end())
+      why = FinishReason::Stop;
+    else if (r.generated >= r.spec.max_new_tokens)
+      why = FinishReason::Length;
+    else if (r.tokens.size() >= cfg_.max_model_len)
+      why = FinishReason::ContextLimit;
+    if (why != FinishReason::None) {
+      finish(r, id, why, ev);
+      return ev;
+    }
+  }
+  r.computed = len + c - 1;
+  if (cfg_.flags & kSchedPrefixCache) cache_->commit(id, r.computed);
+  r.state = r.lane.budget ? SlotState::ReadySpeculativeVerify : SlotState::ReadyDecode;
   return ev;
 }
 

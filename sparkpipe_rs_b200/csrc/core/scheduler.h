@@ -23,6 +23,7 @@
 
 #include "common.h"
 #include "prefix_cache.h"
+#include "speculation.h"
 
 namespace spc {
 
@@ -46,6 +47,7 @@ constexpr uint32_t kSchedCudaGraphPadding = 0x04;
 constexpr uint32_t kSchedPrefillDecodeInterleave = 0x08;
 constexpr uint32_t kSchedKvCacheRequired = 0x10;
 constexpr uint32_t kSchedCrossSequencePrefixReuse = 0x40;
+constexpr uint32_t kSchedMtpForceEnable = 0x200;  // verify whenever the lanes qualify (no utility comparison)
 constexpr uint32_t kSchedDefaultFlags = kSchedChunkedPrefill | kSchedPrefixCache | kSchedCudaGraphPadding |
                                         kSchedPrefillDecodeInterleave | kSchedKvCacheRequired |
                                         kSchedCrossSequencePrefixReuse;
@@ -57,7 +59,13 @@ constexpr uint32_t kDecisionCudaGraphPadding = 0x008;
 constexpr uint32_t kDecisionDecodeStep = 0x010;
 constexpr uint32_t kDecisionPrefillStep = 0x020;
 constexpr uint32_t kDecisionScheduledAhead = 0x040;  // decode planned before the previous step's tokens were read
+constexpr uint32_t kDecisionSpeculativeVerify = 0x080;
+constexpr uint32_t kDecisionMtpTreeVerify = 0x100;
 constexpr uint32_t kDecisionPreempted = 0x800;
+
+// speculation modes: a draft chain of spec_draft_len tokens per lane, or the fixed
+// MTP draft tree (5 candidates verified in 6 rows, work_control.h mtp::)
+enum class SpecMode : uint32_t { Off = 0, Chain = 1, MtpTree = 2 };
 
 // finish reasons
 enum class FinishReason : uint32_t { None = 0, Length = 1, Stop = 2, Cancelled = 3, ContextLimit = 4, Error = 5 };
@@ -73,6 +81,12 @@ struct SchedulerConfig {
   uint32_t flags = kSchedDefaultFlags;
   uint32_t max_consecutive_prefills = 4;  // interleave cap while decodes wait
   std::vector<uint32_t> decode_buckets = {1, 2, 4, 8, 16, 32, 64, 128, 256};
+  // speculation
+  uint32_t spec_mode = 0;               // SpecMode
+  uint32_t spec_draft_len = 3;          // chain: draft tokens per round (1..7)
+  uint32_t spec_row_cap = 0;            // firing rows of a verify round (0: rows per lane x max_batch)
+  uint32_t spec_row_cost_milli = 1000;  // a draft row's cost relative to a real row
+  int64_t spec_shadow_slot_base = -1;   // tree: cache row of the first shadow slot (2 per batch row)
 };
 
 struct RequestSpec {
@@ -84,10 +98,11 @@ struct RequestSpec {
   bool ignore_eos = false;
   float temperature = 0.f;            // <= 0: greedy
   uint64_t seed = 0;
+  bool disable_speculation = false;   // sampled requests (temperature > 0) never speculate either
 };
 
 struct StepPlan {
-  enum Kind : uint32_t { None = 0, Prefill = 1, Decode = 2 };
+  enum Kind : uint32_t { None = 0, Prefill = 1, Decode = 2, Verify = 3 };
   uint32_t kind = None;
   uint32_t flags = 0;
   uint32_t num_seqs = 0;      // real sequences
@@ -109,6 +124,14 @@ struct StepPlan {
   std::vector<int32_t> src_rows;
   uint32_t max_blocks = 0;
   uint32_t max_context = 0;
+  // verify: rows_per_seq rows per sequence, laid out row-major by draft depth / tree
+  // row (row j * padded_seqs + b); block_table stays one row per sequence
+  uint32_t rows_per_seq = 1;
+  std::vector<int32_t> draft_budget;      // per sequence: drafts it may accept
+  std::vector<uint64_t> accept_keys;      // per sequence: key of forced-acceptance draws
+  // tree: the draft model's KV of the 3 positions before each lane's input token
+  // (rewritten every round: accepted tree tokens may not be in the draft cache)
+  std::vector<int32_t> sync_token_ids, sync_positions, sync_slots;  // [3 x padded_seqs], row k * padded + b
 };
 
 struct SchedEvent {
@@ -121,7 +144,7 @@ struct SchedEvent {
 };
 
 struct SchedulerStats {
-  uint64_t steps = 0, prefill_steps = 0, decode_steps = 0, preemptions = 0;
+  uint64_t steps = 0, prefill_steps = 0, decode_steps = 0, verify_steps = 0, preemptions = 0;
   uint64_t prefill_tokens = 0, decode_tokens = 0, cached_prompt_tokens = 0;
   uint64_t admitted = 0, finished = 0, cancelled = 0, rejected = 0;
 };
@@ -139,6 +162,18 @@ class Scheduler {
   // changed, or the KV blocks for one more token are not free.
   StepPlan schedule_ahead(const StepPlan& inflight);
   std::vector<SchedEvent> complete(const StepPlan& plan, const int32_t* sampled, uint32_t n_sampled);
+  // Completes a verify plan: sequence b committed counts[b] tokens, committed[b *
+  // stride ..]; paths[b] is the tree resolution (tree mode). Updates each lane's
+  // speculation state and stops a sequence at its first stop token / length limit.
+  std::vector<SchedEvent> complete_verify(const StepPlan& plan, const int32_t* committed, uint32_t stride,
+                                          const int32_t* counts, const int32_t* paths, uint32_t n);
+  // Measured device time of one plain decode step (kind 2) or verify round (kind 3)
+  // of a padded batch; the speculation utility compares them.
+  void set_step_cost(uint32_t kind, uint32_t seqs, uint64_t ns) { cost_.set(kind, seqs, ns); }
+  uint64_t estimate_step_ns(uint32_t kind, uint32_t seqs) const;
+  const spec::Totals& spec_totals() const { return spec_; }
+  spec::LaneState lane_state(uint64_t id) const;
+  uint32_t spec_rows_per_seq() const;
   // Per-row sampling parameters of a plan (rows beyond num_seqs are greedy):
   // temperature and a noise key derived from the request's seed and the position
   // of the token that is sampled, so a request draws the same tokens however it
@@ -166,12 +201,19 @@ class Scheduler {
     uint32_t computed = 0;         // tokens with KV in the cache
     uint32_t generated = 0;
     SlotState state = SlotState::QueuedPrefill;
+    spec::LaneState lane;
     bool reserved = false;
     uint64_t arrival = 0;
     FinishReason reason = FinishReason::None;
   };
   StepPlan build_prefill();
   StepPlan build_decode();
+  // the verify form of a decode plan, or an empty plan when the policy keeps plain decode
+  StepPlan try_build_verify(const StepPlan& decode);
+  // per-lane draft budgets of a verify round over `ids`; false when the policy keeps plain decode
+  bool spec_grants(const std::vector<uint64_t>& ids, std::vector<uint32_t>& grant) const;
+  uint32_t full_budget() const;
+  std::vector<SchedEvent> append_committed(Req& r, uint64_t id, const int32_t* toks, uint32_t n);
   void preempt_one(uint64_t keep);
   void finish(Req& r, uint64_t id, FinishReason why, std::vector<SchedEvent>& ev);
   int32_t slot_of(const Req& r, uint64_t id, uint32_t pos) const;
@@ -187,6 +229,8 @@ class Scheduler {
   uint64_t arrival_clock_ = 0;
   uint64_t step_clock_ = 0;
   SchedulerStats stats_;
+  spec::Totals spec_;
+  spec::StepCost cost_;
 };
 
 }  // namespace spc
