@@ -179,6 +179,7 @@ struct MlaDecodeLaunch {
   unsigned long long* trace = nullptr;  // tcgen05 kernel: [6][64] event times of CTA (0,0,0)
   int* counters = nullptr;        // stream-K kernel: per-row arrival counters, zero between launches
   int early = 0;                  // stream-K kernel: earlier-position KV may load before the PDL wait
+  const int* last_slot = nullptr; // mma.sync kernel: [B] cache row of each row's last context token (-1: its block)
   cudaStream_t stream = 0;
 };
 enum { MLA_IMPL_AUTO = 0, MLA_IMPL_TC = 1, MLA_IMPL_MMA = 2 };
@@ -290,6 +291,14 @@ void spec_verify(const int* draft, const int* target, int B, int L, float forced
 
 // End of a speculative round over j-major row arrays (row j*B + b, j = 0..L): acceptance, committed
 // tokens, and the next round's inputs (see sampling.cu).
+// Verify kernels of the serving engine (spec_verify.cu); row arrays [rows][B].
+void spec_chain_commit(const int* tok, const int* tgt, const int* ctx, const int* pos, const int* budget,
+                       const unsigned long long* keys, int B, int L, float p_accept, unsigned long long seed,
+                       int* committed, int* counts, cudaStream_t s);
+void mtp_tree_commit(const int* tok, const int* tgt, const int* ctx, const int* slots, int B, void* cache,
+                     long long layer_stride, int layers, int row_elems, int* committed, int* counts, int* paths,
+                     cudaStream_t s);
+void top2_rows(const void* logits, long long ldl, int T, int V, int* out0, int* out1, cudaStream_t s);
 void spec_finish(int* tok_rows, const int* tgt_rows, int B, int L, float p_accept, unsigned long long seed,
                  int* pos_rows, int* ctx_rows, int* slot_rows, const int* block_table, int max_blocks,
                  int block_size, int* accepted, int* committed, unsigned long long* total_committed, cudaStream_t s);

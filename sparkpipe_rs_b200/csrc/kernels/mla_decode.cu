@@ -56,6 +56,11 @@ struct MlaKParams {
   float scale_log2;
   int* err;
   unsigned long long* trace;  // tcgen05 kernel: event times of CTA (0,0,0), or null
+  // mma.sync kernel: when set, row b's last context token is read from cache row
+  // last_slot[b] instead of its block-table position (the alternate leaves of a
+  // tree verify, whose KV sits in a shadow slot)
+  const int* last_slot;
+  const bf16* cache;
 };
 
 constexpr int MLA_DIM = 576;     // kv_lora 512 + rope 64
@@ -82,7 +87,7 @@ struct MlaCfg {
   static constexpr int MIN_CTAS = (2 * SMEM <= 227 * 1024) ? 2 : 1;
 };
 
-template <int HG, int NJ, int TOK>
+template <int HG, int NJ, int TOK, bool LAST = false>
 __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ, TOK>::MIN_CTAS)
     mla_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       const MlaKParams p) {
@@ -159,6 +164,23 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ
     bool got = mbar_wait(&full[s], (i >> 1) & 1, s_err, p.err, kErrWaitTimeoutMma);
     if (!__syncthreads_and(got)) { ok = false; break; }
     const uint32_t kvb = sKV + s * C::STAGE_BYTES;
+    if constexpr (LAST) {
+      const int t_last = ctx - 1, t0 = kb0 * MLA_BLK + i * TOK;
+      const int src = p.last_slot[b];
+      if (t_last >= t0 && t_last < t0 + TOK && src >= 0 &&
+          src != bt[t_last / MLA_BLK] * MLA_BLK + t_last % MLA_BLK) {  // block-uniform
+        // overwrite the stage's row of that token (128-byte swizzled, 16-byte units)
+        const int tr = t_last - t0;
+        uint8_t* st = smem + C::OFF_KV + s * C::STAGE_BYTES;
+        for (int e = threadIdx.x; e < MLA_CHUNKS * 8; e += blockDim.x) {
+          const int c = e >> 3, u = e & 7;
+          const uint4 v = *reinterpret_cast<const uint4*>(p.cache + (long long)src * MLA_DIM + c * 64 + u * 8);
+          *reinterpret_cast<uint4*>(st + c * TOK * 128 + tr * 128 + ((u ^ (tr & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();  // the next TMA write of this stage is ordered after these
+        __syncthreads();
+      }
+    }
 
     // ---- S = Q K^T for 16 heads x TOKW tokens of this warp
     float sc[C::NT][4];
@@ -759,6 +781,8 @@ static void launch_mla_tc(const MlaDecodeLaunch& l) {
   p.scale_log2 = l.scale * 1.4426950408889634f;
   p.err = l.err;
   p.trace = l.trace;
+  p.last_slot = nullptr;
+  p.cache = (const bf16*)l.cache;
   if (l.B > 65535 || l.splits > 65535) throw std::runtime_error("mla_decode: batch / splits beyond the grid limits");
   launch_k(kern, dim3(l.H / HG, l.B, l.splits), dim3(C::THREADS), C::SMEM, l.stream, tq, tkv, p);
   if (l.splits > 1) {
@@ -773,7 +797,7 @@ static void launch_mla(const MlaDecodeLaunch& l) {
   CUtensorMap tq, tkv;
   make_tmap_2d(&tq, l.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (long long)l.B * l.H, MLA_DIM, MLA_DIM, HG, 64);
   make_tmap_2d(&tkv, l.cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.num_slots, MLA_DIM, MLA_DIM, TOK, 64);
-  auto kern = mla_decode_kernel<HG, NJ, TOK>;
+  auto kern = l.last_slot ? mla_decode_kernel<HG, NJ, TOK, true> : mla_decode_kernel<HG, NJ, TOK, false>;
   set_smem_bytes(kern, C::SMEM);
   MlaKParams p;
   p.block_table = l.block_table;
@@ -788,6 +812,8 @@ static void launch_mla(const MlaDecodeLaunch& l) {
   p.scale_log2 = l.scale * 1.4426950408889634f;
   p.err = l.err;
   p.trace = nullptr;
+  p.last_slot = l.last_slot;
+  p.cache = (const bf16*)l.cache;
   if (l.B > 65535 || l.splits > 65535) throw std::runtime_error("mla_decode: batch / splits beyond the grid limits");
   dim3 grid(l.H / HG, l.B, l.splits);
   launch_k(kern, grid, dim3(C::WARPS * 32), C::SMEM, l.stream, tq, tkv, p);
@@ -842,6 +868,7 @@ void mla_decode(const MlaDecodeLaunch& l) {
   if (l.splits > 1 && (!l.o_part || !l.lse_part)) throw std::runtime_error("mla_decode: split-KV needs scratch");
   if (l.H % 16 != 0) throw std::runtime_error("mla_decode: heads must be a multiple of 16");
   const int impl = l.impl == MLA_IMPL_AUTO ? mla_default_impl() : l.impl;
+  if (impl == MLA_IMPL_TC && l.last_slot) throw std::runtime_error("mla_decode: last_slot needs the mma.sync kernel");
   if (impl == MLA_IMPL_TC) {
     if (l.H % 32 == 0) launch_mla_tc<32>(l);
     else launch_mla_tc<16>(l);

@@ -383,7 +383,8 @@ void quant_weight_fp8(const c10::optional<Tensor>& src, int64_t seed, int64_t fl
 
 void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table, const Tensor& context_lens,
                 const Tensor& out, const c10::optional<Tensor>& o_part, const c10::optional<Tensor>& lse_part,
-                int64_t splits, double scale, int64_t impl, const c10::optional<Tensor>& trace) {
+                int64_t splits, double scale, int64_t impl, const c10::optional<Tensor>& trace,
+                const c10::optional<Tensor>& last_slot) {
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(cache); CHECK_I32(block_table); CHECK_I32(context_lens); CHECK_BF16(out);
   CHECK_ON(q, cache); CHECK_ON(q, block_table); CHECK_ON(q, context_lens); CHECK_ON(q, out);
   CHECK_CONTIG(q); CHECK_CONTIG(block_table); CHECK_CONTIG(out);
@@ -419,6 +420,11 @@ void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table,
     TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == torch::kInt64 && trace->numel() >= 6 * 64,
                 "mla_decode: trace must be an int64 CUDA tensor of 384 entries");
     l.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
+  if (last_slot.has_value()) {
+    CHECK_I32(*last_slot); CHECK_ON(q, *last_slot); CHECK_CONTIG(*last_slot);
+    TORCH_CHECK(last_slot->numel() >= B, "mla_decode: last_slot shorter than the batch");
+    l.last_slot = last_slot->data_ptr<int>();
   }
   l.scale = (float)scale;
   l.err = err_word();
@@ -708,6 +714,56 @@ void spec_finish(const Tensor& tok_rows, const Tensor& tgt_rows, int64_t L, doub
                   accepted.data_ptr<int>(), committed.data_ptr<int>(), tc, stream());
 }
 
+// Verify round of the serving engine: chain acceptance with per-lane budgets.
+void spec_chain_commit(const Tensor& tok, const Tensor& tgt, const Tensor& ctx, const Tensor& pos,
+                       const Tensor& budget, const Tensor& keys, int64_t L, double p_accept, int64_t seed,
+                       const Tensor& committed, const Tensor& counts) {
+  CHECK_CUDA(tok); CHECK_I32(tok); CHECK_I32(tgt); CHECK_I32(ctx); CHECK_I32(pos); CHECK_I32(budget);
+  CHECK_I32(committed); CHECK_I32(counts);
+  TORCH_CHECK(keys.scalar_type() == at::kLong, "keys must be int64");
+  for (const Tensor* t : {&tgt, &ctx, &pos, &budget, &keys, &committed, &counts}) { CHECK_ON(tok, *t); CHECK_CONTIG(*t); }
+  CHECK_CONTIG(tok);
+  const int64_t B = counts.numel();
+  TORCH_CHECK(L >= 1 && tok.numel() >= (L + 1) * B && tgt.numel() >= (L + 1) * B && ctx.numel() >= B &&
+                  pos.numel() >= B && budget.numel() >= B && keys.numel() >= B && committed.numel() >= (L + 1) * B,
+              "spec_chain_commit: row arrays must hold (L + 1) x B entries");
+  const c10::cuda::CUDAGuard guard(tok.device());
+  sp::spec_chain_commit(tok.data_ptr<int>(), tgt.data_ptr<int>(), ctx.data_ptr<int>(), pos.data_ptr<int>(),
+                        budget.data_ptr<int>(), reinterpret_cast<const unsigned long long*>(keys.data_ptr<int64_t>()),
+                        (int)B, (int)L, (float)p_accept, (unsigned long long)seed, committed.data_ptr<int>(),
+                        counts.data_ptr<int>(), stream());
+}
+
+// Verify round of the serving engine: the MTP tree (6 rows per lane) and the KV move
+// of an accepted alternate leaf in `cache` [layers, slots, row].
+void mtp_tree_commit(const Tensor& tok, const Tensor& tgt, const Tensor& ctx, const Tensor& slots,
+                     const Tensor& cache, const Tensor& committed, const Tensor& counts, const Tensor& paths) {
+  CHECK_CUDA(tok); CHECK_I32(tok); CHECK_I32(tgt); CHECK_I32(ctx); CHECK_I32(slots); CHECK_BF16(cache);
+  CHECK_I32(committed); CHECK_I32(counts); CHECK_I32(paths); CHECK_CONTIG(cache);
+  for (const Tensor* t : {&tgt, &ctx, &slots, &cache, &committed, &counts, &paths}) CHECK_ON(tok, *t);
+  for (const Tensor* t : {&tok, &tgt, &ctx, &slots, &committed, &counts, &paths}) CHECK_CONTIG(*t);
+  TORCH_CHECK(cache.dim() == 3, "cache: [layers, slots, row]");
+  const int64_t B = counts.numel();
+  TORCH_CHECK(tok.numel() >= 6 * B && tgt.numel() >= 6 * B && slots.numel() >= 6 * B && ctx.numel() >= B &&
+                  committed.numel() >= 6 * B && paths.numel() >= B,
+              "mtp_tree_commit: row arrays must hold 6 x B entries");
+  const c10::cuda::CUDAGuard guard(tok.device());
+  sp::mtp_tree_commit(tok.data_ptr<int>(), tgt.data_ptr<int>(), ctx.data_ptr<int>(), slots.data_ptr<int>(), (int)B,
+                      cache.data_ptr(), cache.stride(0), (int)cache.size(0), (int)cache.size(2),
+                      committed.data_ptr<int>(), counts.data_ptr<int>(), paths.data_ptr<int>(), stream());
+}
+
+void top2_rows(const Tensor& logits, const Tensor& out0, const Tensor& out1) {
+  CHECK_CUDA(logits); CHECK_BF16(logits); CHECK_I32(out0); CHECK_I32(out1);
+  CHECK_ON(logits, out0); CHECK_ON(logits, out1); CHECK_CONTIG(out0); CHECK_CONTIG(out1);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits: [T, V] with unit column stride");
+  const int64_t T = logits.size(0);
+  TORCH_CHECK(out0.numel() >= T && out1.numel() >= T, "top2_rows: outputs shorter than the rows");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  sp::top2_rows(logits.data_ptr(), logits.stride(0), (int)T, (int)logits.size(1), out0.data_ptr<int>(),
+                out1.data_ptr<int>(), stream());
+}
+
 void kv_blocks_copy(const Tensor& cache, const Tensor& blocks, const Tensor& staging, int64_t block_size,
                     bool to_staging) {
   // cache [layers, slots, row] bf16 (contiguous); staging [n, layers, block_size, row] bf16
@@ -958,6 +1014,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("spec_verify", &spec_verify);
   m.def("decode_advance", &decode_advance);
   m.def("spec_finish", &spec_finish);
+  m.def("spec_chain_commit", &spec_chain_commit);
+  m.def("mtp_tree_commit", &mtp_tree_commit);
+  m.def("top2_rows", &top2_rows);
   m.def("phase_mark", &phase_mark);
   m.def("kv_blocks_copy", &kv_blocks_copy);
   m.def("slab_add_rmsnorm", &slab_add_rmsnorm);

@@ -72,6 +72,16 @@ class CpuMLAMoEModel:
             return oracle.moe(c, w, p, x)
         return oracle.swiglu_mlp(x, w[p + "w13"], w[p + "w2"])
 
+    def write_kv(self, fb: ForwardBatch, cache: KVCache):
+        """Layer 0's latent KV of the rows of ``fb`` only (see MLAMoEModel.write_kv)."""
+        c = self.cfg
+        h = self.w["embed"][fb.token_ids.long()].float()
+        _, row = self._qkv("l0.", oracle.rmsnorm(h, self.w["l0.in_norm"], c.rms_norm_eps), fb.positions.long())
+        slots = fb.slot_mapping.long()
+        keep = slots >= 0
+        lc = cache.layer(0)
+        lc[slots[keep]] = row[keep].to(lc.dtype)
+
     # ------------------------------------------------------------------ forward
     def forward(self, fb: ForwardBatch, cache: KVCache, layers=None, hidden_in=None, return_hidden=False,
                 layer_offset: int = 0):
@@ -100,6 +110,9 @@ class CpuMLAMoEModel:
                         continue
                     blocks = fb.block_table[b, : (L + bs - 1) // bs].long()
                     rows = (blocks[:, None] * bs + torch.arange(bs)).flatten()[:L]
+                    if fb.self_slots is not None and int(fb.self_slots[b]) >= 0:
+                        rows = rows.clone()
+                        rows[-1] = int(fb.self_slots[b])
                     out[b] = self._attend(p, q[b:b + 1], lc[rows].float(), pos[b:b + 1])[0]
             else:
                 cu_q = fb.cu_q.long().tolist()

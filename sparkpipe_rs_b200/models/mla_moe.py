@@ -41,6 +41,10 @@ class ForwardBatch:
     block_table: torch.Tensor | None = None   # [B, max_blocks]
     context_lens: torch.Tensor | None = None  # [B] (including the current token)
     decode_splits: int = 1
+    # decode: row b's own token (its last context token) is read from cache row
+    # self_slots[b] rather than its block-table position; a tree verify's alternate
+    # leaves write their KV to shadow rows (None: every row reads its block table)
+    self_slots: torch.Tensor | None = None
     # prefill
     cu_q: torch.Tensor | None = None          # [B + 1]
     cu_k: torch.Tensor | None = None          # [B + 1]
@@ -197,7 +201,8 @@ class MLAMoEModel:
             ops.mla_decode_prep(qkv, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache,
                                 None, q_lat, kvl, 0, nh * c.kv_cache_dim, c.rms_norm_eps)
             o_lat = torch.empty(T, nh, kvl, dtype=torch.bfloat16, device=self.device)
-            ops.mla_decode(q_lat, layer_cache, fb.block_table, fb.context_lens, o_lat, fb.decode_splits, self.scale)
+            ops.mla_decode(q_lat, layer_cache, fb.block_table, fb.context_lens, o_lat, fb.decode_splits, self.scale,
+                           last_slot=fb.self_slots)
             return self._lin(o_lat.view(T, nh * kvl), w[p + "w_ov"], slab=True)
         else:
             # one kernel: split-K reduction of the q/kv projection, latent norm + RoPE
@@ -212,7 +217,8 @@ class MLAMoEModel:
                          a_batch_rows=kvl, b_k0=0, b_batch_k=q_batch_k, ldd=nh * c.kv_cache_dim,
                          d_batch_stride=c.kv_cache_dim)
         o_lat = torch.empty(T, nh, kvl, dtype=torch.bfloat16, device=self.device)
-        ops.mla_decode(q_lat, layer_cache, fb.block_table, fb.context_lens, o_lat, fb.decode_splits, self.scale)
+        ops.mla_decode(q_lat, layer_cache, fb.block_table, fb.context_lens, o_lat, fb.decode_splits, self.scale,
+                           last_slot=fb.self_slots)
         attn = torch.empty(T, nh * dv, dtype=torch.bfloat16, device=self.device)
         # attn[t, h*dv + v] = o_lat[t, h] @ W_UV[h]^T
         ops.batched_gemm(w[p + "w_kv_b"], o_lat.view(T, nh * kvl), attn, M=dv, N=T, K=kvl, batch=nh, a_row0=dn,
@@ -303,6 +309,23 @@ class MLAMoEModel:
         else:
             ops.slab_add_rmsnorm(pending, res, gamma, xn, eps)
 
+    def write_kv(self, fb: ForwardBatch, cache: KVCache):
+        """Writes layer 0's latent KV of the rows of ``fb`` (token ids, positions, cache
+        slots) and nothing else: embedding, input norm, the latent KV projection, its
+        norm and RoPE. Layer 0's KV of a token depends only on the token and its
+        position, so this keeps a one-layer draft model's cache current for tokens it
+        did not decode itself (prompts, plainly decoded tokens, accepted tree drafts)."""
+        c, w = self.cfg, self.w
+        wt = w["l0.w_qkv_a"]
+        if isinstance(wt, ops.Fp8Weight):
+            raise ValueError("write_kv needs a bf16 latent projection")
+        x = ops.embedding(w["embed"], fb.token_ids)
+        xn = torch.empty_like(x)
+        ops.add_rmsnorm(x, None, w["l0.in_norm"], xn, c.rms_norm_eps)
+        kv_a = ops.linear(xn, wt[self.qa_dim:])
+        ops.mla_kv_write(kv_a, w["l0.kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, cache.layer(0), None,
+                         c.kv_lora_rank, c.qk_rope_head_dim, c.rms_norm_eps)
+
     # ------------------------------------------------------------------ forward
     def forward(self, fb: ForwardBatch, cache: KVCache, layers: range | None = None,
                 hidden_in: torch.Tensor | None = None, return_hidden: bool = False, layer_offset: int = 0):
@@ -367,8 +390,11 @@ class DecodeGraph:
     graph serves greedy and sampled requests in the same batch."""
 
     def __init__(self, model: MLAMoEModel, cache: KVCache, batch: int, max_blocks: int, max_context: int,
-                 use_graph: bool = True, self_advance: bool = False):
+                 use_graph: bool = True, self_advance: bool = False, extra=None):
+        """``extra(fb)``: more device work of the step, captured into the same graph
+        (the serving engine keeps a draft model's KV current with it)."""
         self.model, self.cache, self.B = model, cache, batch
+        self.extra = extra
         dev = model.device
         self.ids = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
@@ -402,6 +428,8 @@ class DecodeGraph:
     def _step(self):
         logits = self.model.forward(self.fb, self.cache)
         ops.sample_tokens(logits, out_ids=self.out_ids, row_temp=self.temps, row_key=self.keys)
+        if self.extra is not None:
+            self.extra(self.fb)
         if self.self_advance:
             ops.decode_advance(self.out_ids, self.ids, self.pos, self.ctx, self.slots, self.block_table,
                                self.cache.block_size)

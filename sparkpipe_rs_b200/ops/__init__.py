@@ -411,7 +411,7 @@ def _sk_workspace(device) -> _SkWorkspace:
 
 
 def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=None, lse_part=None, impl="auto",
-               trace=None):
+               trace=None, last_slot=None):
     """Absorbed-MLA paged decode attention. ``impl``: "sk" (stream-K kernel: all SMs
     over the flattened 32-token KV units, the default), "mma" (split-KV mma.sync
     kernel), "tc" (split-KV tcgen05 kernel) or "auto" (the default, which the
@@ -420,10 +420,14 @@ def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=N
     global-timer stamps (ns) of four CTAs (first, second, middle, last): start,
     schedule ready, dependency wait passed, per piece queries landed / finished, per
     stage consumed, merge start / end, end (see mla_decode_sk.cu); for "tc", 6 x 64
-    pipeline event times of its first CTA."""
+    pipeline event times of its first CTA. ``last_slot`` (int32 [B], mma kernel): row b
+    reads its last context token from cache row last_slot[b] (-1: from its block
+    table), as a tree verify's alternate leaves need."""
     B, H, _ = q.shape
     if impl == "auto":
         impl = _MLA_DEFAULT
+    if last_slot is not None:
+        impl = "mma"
     if impl == "sk" and kernels().mla_sk_supported(B, H):
         o_ws, lse_ws, cnt = _sk_workspace(q.device).get(q.device, B, H)
         kernels().mla_decode_sk(q, cache, block_table, context_lens, out, o_ws, lse_ws, cnt, float(scale),
@@ -436,7 +440,7 @@ def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=N
         o_part = torch.empty(B, splits, H, 512, dtype=torch.float32, device=q.device)
         lse_part = torch.empty(B, splits, H, dtype=torch.float32, device=q.device)
     kernels().mla_decode(q, cache, block_table, context_lens, out, o_part, lse_part, splits, float(scale),
-                         MLA_IMPL[impl], trace)
+                         MLA_IMPL[impl], trace, last_slot)
     _count(1 + (1 if splits > 1 else 0))
     return out
 
@@ -550,6 +554,29 @@ def spec_verify(draft, target, p_accept=0.0, seed=0, offset=0):
     kernels().spec_verify(draft, target, float(p_accept), int(seed), int(offset), accepted, committed)
     _count(1)
     return accepted, committed
+
+
+def spec_chain_commit(tok, tgt, ctx, pos, budget, keys, L, committed, counts, p_accept=0.0, seed=0):
+    """Verify round, chain drafts: lane b (rows j * B + b) accepts its longest agreeing
+    draft prefix within budget[b] (or a seeded Bernoulli(p_accept) chain keyed by
+    keys[b] and its position) and commits it plus the verifier's next token:
+    committed [B, L + 1] (-1 padded), counts [B] (0 for idle lanes)."""
+    kernels().spec_chain_commit(tok, tgt, ctx, pos, budget, keys, int(L), float(p_accept), int(seed), committed, counts)
+    _count(1)
+
+
+def mtp_tree_commit(tok, tgt, ctx, slots, cache_data, committed, counts, paths):
+    """Verify round, the fixed MTP tree (rows r * B + b, r = 0..5): resolved path per
+    lane, committed [B, 6] / counts [B], and the KV move of an accepted alternate leaf
+    from its shadow slot in ``cache_data`` [layers, slots, row]."""
+    kernels().mtp_tree_commit(tok, tgt, ctx, slots, cache_data, committed, counts, paths)
+    _count(1)
+
+
+def top2_rows(logits, out0, out1):
+    """Ids of the two largest logits of each row (ties to the lower id)."""
+    kernels().top2_rows(logits, out0, out1)
+    _count(1)
 
 
 def decode_advance(out_ids, ids, pos, ctx, slots, block_table, block_size=64):

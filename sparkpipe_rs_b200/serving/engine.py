@@ -25,6 +25,15 @@ n's sampled tokens; only then does the host wait for n's tokens. A sequence that
 stops at step n gets one discarded extra token. Decode graphs for every batch
 bucket are captured when the engine starts.
 
+With speculation on (``EngineConfig.speculation``: "chain" or "mtp_tree"), a draft
+model keeps its own KV cache current (its first-layer KV is written for prompts and
+plainly decoded tokens inside the same step), and the scheduler turns a decode step
+into a verify round whenever its policy grants the lanes draft rows: drafts, one
+batched target forward over every lane's rows and the commit kernel run as one CUDA
+graph per padded batch (``serving/verify.py``), and each lane commits between one and
+(drafts + 1) tokens. Measured device times of plain steps and verify rounds feed the
+scheduler's utility comparison.
+
 Request lifecycle and event names follow the reference's serving engine
 (crates/spark-serve/src/serving_engine/engine.rs:1381-2050: invoke_prefill /
 invoke_decode / complete_*_dispatch / pump) with the reference's ring dispatch
@@ -37,11 +46,13 @@ import statistics
 import time
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 from .. import _ext, ops
 from ..models.config import MLAMoEConfig
 from ..models.mla_moe import DecodeGraph, ForwardBatch, KVCache, MLAMoEModel
+from .verify import VerifyRound
 
 
 @dataclass
@@ -59,6 +70,12 @@ class EngineConfig:
     seed: int = 0
     async_decode: bool = True         # plan and launch decode step n+1 before reading step n's tokens
     capture_graphs_at_start: bool = True
+    speculation: str = ""             # "", "chain" (draft_len drafts per lane) or "mtp_tree" (5 candidates, 6 rows)
+    draft_len: int = 3
+    spec_p_accept: float = 0.0        # > 0: forced Bernoulli acceptance of each draft token (benchmarks)
+    spec_force: bool = False          # verify whenever the lanes qualify (no utility comparison)
+    spec_seed: int = 17
+    spec_row_cap: int = 0             # firing rows of a verify round (0: rows per lane x max_batch)
 
 
 @dataclass
@@ -101,6 +118,23 @@ class GenerateResult:
 FINISH_REASONS = {1: "length", 2: "stop", 3: "cancelled", 4: "context_limit", 5: "error"}
 
 
+def _default_draft(model, e: EngineConfig):
+    """A one-layer MTP-style draft head of ``model`` sharing its embedding and LM head:
+    on the GPU model's device, or an fp32 CPU stage driver for the CPU model."""
+    from .spec_decode import make_draft
+
+    if isinstance(model, MLAMoEModel):
+        return make_draft(model, seed=e.seed + 1, max_positions=e.max_model_len + 8)
+    from ..models.config import mtp_head
+    from ..models.cpu_model import CpuMLAMoEModel
+    from ..models.weights import init_weights
+
+    cfg = mtp_head(model.cfg)
+    w = init_weights(cfg, seed=e.seed + 1, device="cpu", dtype=torch.float32,
+                     share={"embed": model.w["embed"], "lm_head": model.w["lm_head"]})
+    return CpuMLAMoEModel(cfg, weights=w, max_positions=e.max_model_len + 8)
+
+
 class _Pinned:
     """Reusable pinned host buffers for the per-step host->device copies."""
 
@@ -138,19 +172,22 @@ class _Lockstep:
 @dataclass
 class _Launched:
     """A step whose GPU work is enqueued: its sampled tokens land in ``host``
-    (``plan`` None: an idle forward of a lockstep rank)."""
+    (``plan`` None: an idle forward of a lockstep rank; a verify round: the host
+    tensors (committed, counts, paths))."""
     plan: object
-    host: torch.Tensor | None
+    host: object
     event: object          # CUDA event after the device->host copy (None on CPU)
     out: torch.Tensor      # device tensor of the sampled tokens
     t0: float
+    timing: tuple | None = None  # CUDA events around the step's device work (cost model)
 
 
 class LLMEngine:
     def __init__(self, cfg: MLAMoEConfig, ecfg: EngineConfig | None = None, model=None, device="cuda",
-                 cache: KVCache | None = None):
+                 cache: KVCache | None = None, draft=None):
         """``model`` may be the GPU model, the CPU stage driver or a PipelineModel (rank 0
-        of a pipeline); ``cache`` defaults to a full cache on ``device``."""
+        of a pipeline); ``cache`` defaults to a full cache on ``device``. ``draft``: the
+        draft model of speculation (default: a one-layer MTP-style head of ``model``)."""
         self.cfg = cfg
         self.ecfg = ecfg or EngineConfig()
         self.device = torch.device(device)
@@ -164,8 +201,23 @@ class LLMEngine:
         max_blocks = -(-e.max_model_len // e.block_size)
         num_blocks = e.num_blocks or e.max_batch * max_blocks + 16
         self.model = model or MLAMoEModel(cfg, seed=e.seed, device=self.device, max_positions=e.max_model_len + 8)
-        self.cache = cache or KVCache(cfg, num_blocks=num_blocks, block_size=e.block_size, device=self.device)
+        if e.speculation not in ("", "chain", "mtp_tree"):
+            raise ValueError(f"unknown speculation mode {e.speculation!r}")
+        self.spec = e.speculation
+        buckets = [b for b in e.decode_buckets if b <= max(e.max_batch, 1)] + (
+            [e.max_batch] if e.max_batch not in e.decode_buckets else [])
+        # tree verify: two shadow KV rows per batch row, past the scheduler's blocks
+        shadow_blocks = -(-2 * max(buckets) // e.block_size) if self.spec == "mtp_tree" else 0
+        if cache is not None and shadow_blocks and cache.num_blocks < num_blocks + shadow_blocks:
+            raise ValueError("tree speculation needs a cache with room for the shadow blocks")
+        self.cache = cache or KVCache(cfg, num_blocks=num_blocks + shadow_blocks, block_size=e.block_size,
+                                      device=self.device)
         self.use_graphs = self.is_cuda and e.use_cuda_graph and isinstance(self.model, MLAMoEModel)
+        self.draft = self.dcache = None
+        if self.spec:
+            self.draft = draft or _default_draft(self.model, e)
+            self.dcache = KVCache(self.draft.cfg, num_blocks=num_blocks, block_size=e.block_size, device=self.device,
+                                  layers=1)
         sc = self.core.SchedulerConfig()
         sc.max_batch = e.max_batch
         sc.max_prefill_tokens = e.max_prefill_tokens
@@ -173,17 +225,28 @@ class LLMEngine:
         sc.num_blocks = num_blocks
         sc.max_model_len = e.max_model_len
         sc.max_consecutive_prefills = e.max_consecutive_prefills
-        sc.decode_buckets = [b for b in e.decode_buckets if b <= max(e.max_batch, 1)] + (
-            [e.max_batch] if e.max_batch not in e.decode_buckets else [])
+        sc.decode_buckets = buckets
         flags = self.core.SCHED_DEFAULT_FLAGS
         if not e.prefix_caching:
             flags &= ~self.core.SCHED_PREFIX_CACHE
         if not e.chunked_prefill:
             flags &= ~self.core.SCHED_CHUNKED_PREFILL
+        if self.spec:
+            sc.spec_mode = self.core.SPEC_CHAIN if self.spec == "chain" else self.core.SPEC_MTP_TREE
+            sc.spec_draft_len = e.draft_len
+            sc.spec_row_cap = e.spec_row_cap
+            sc.spec_shadow_slot_base = num_blocks * e.block_size
+            if e.spec_force:
+                flags |= self.core.SCHED_MTP_FORCE_ENABLE
         sc.flags = flags
         self.scheduler = self.core.Scheduler(sc)
         self.max_blocks = self.scheduler.max_blocks_per_seq
         self.graphs: dict[int, DecodeGraph] = {}
+        self.verify_rounds: dict[int, VerifyRound] = {}
+        self._cost_ema: dict[tuple[int, int], float] = {}
+        self._timing = None
+        self.tree_paths = [0] * 6  # resolved MTP tree paths over every verified lane
+        self.device_ms: dict[int, float] = {}  # CUDA-event time of timed steps by plan kind
         self.pinned = _Pinned()
         self.outputs: dict[int, RequestOutput] = {}
         self.params: dict[int, SamplingParams] = {}
@@ -206,7 +269,11 @@ class LLMEngine:
         if self.use_graphs and (e.capture_graphs_at_start or self._lockstep is not None):
             for b in sc.decode_buckets:
                 self._graph(b)
-        self.step_log: list[tuple[str, int, float]] = []  # (kind, seqs, seconds)
+                if self.spec:
+                    self._verify_round(b)
+        if self.spec and self.use_graphs and not e.spec_force:
+            self._prime_step_costs()
+        self.step_log: list[tuple[str, int, float, int]] = []  # (kind, seqs, seconds, tokens)
 
     # ------------------------------------------------------------------ requests
     def add_request(self, prompt_token_ids, params: SamplingParams | None = None, request_id: int | None = None) -> int:
@@ -221,6 +288,9 @@ class LLMEngine:
         if params.temperature > 0:
             self._random.add(rid)
         return rid
+
+    def _draft_kv(self, fb):
+        self.draft.write_kv(fb, self.dcache)
 
     def abort_request(self, request_id: int) -> bool:
         ok = self.scheduler.cancel(request_id)
@@ -283,9 +353,41 @@ class LLMEngine:
         g = self.graphs.get(bucket)
         if g is None:
             g = DecodeGraph(self.model, self.cache, bucket, self.max_blocks, self.ecfg.max_model_len,
-                            use_graph=self.ecfg.use_cuda_graph)
+                            use_graph=self.ecfg.use_cuda_graph, extra=self._draft_kv if self.spec else None)
             self.graphs[bucket] = g
         return g
+
+    def _verify_round(self, bucket: int) -> VerifyRound:
+        v = self.verify_rounds.get(bucket)
+        if v is None:
+            e = self.ecfg
+            v = VerifyRound(self.model, self.draft, self.cache, self.dcache, bucket, self.spec, e.draft_len,
+                            self.max_blocks, e.max_model_len, e.spec_p_accept, e.spec_seed,
+                            use_graph=self.use_graphs)
+            v.capture()
+            self.verify_rounds[bucket] = v
+        return v
+
+    def _record_cost(self, kind: int, bucket: int, ms: float):
+        """Device time of a plain step (kind 2) / verify round (kind 3) into the
+        scheduler's cost model, as an exponential average per padded batch."""
+        key = (kind, bucket)
+        prev = self._cost_ema.get(key)
+        ema = ms if prev is None else 0.75 * prev + 0.25 * ms
+        self._cost_ema[key] = ema
+        self.scheduler.set_step_cost(kind, bucket, int(ema * 1e6))
+
+    def _prime_step_costs(self):
+        """One timed replay per captured graph with idle rows: a first estimate of each
+        step kind's cost, replaced by the times measured while serving."""
+        for b in list(self.graphs):
+            for kind, run in ((2, self.graphs[b].run), (3, self.verify_rounds[b].run)):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                run()
+                e1.record()
+                e1.synchronize()
+                self._record_cost(kind, b, e0.elapsed_time(e1))
 
     def _run_prefill(self, plan) -> torch.Tensor:
         fb = ForwardBatch(
@@ -300,7 +402,44 @@ class LLMEngine:
             logits_idx=self._h2d("p_lidx", plan.logits_idx),
         )
         logits = self.model.forward(fb, self.cache)
+        if self.spec:
+            self._draft_kv(fb)
         return self._sample(logits, plan)
+
+    def _run_verify(self, plan):
+        """Copies a verify plan's rows into its round's device arrays and runs the round."""
+        B = plan.padded_seqs
+        v = self._verify_round(B)
+        R = B * v.rows
+        if self.is_cuda:
+            par = self._parity
+            self._parity ^= 1
+            ids = self.pinned.get(f"v_ids{par}", R)
+            pos = self.pinned.get(f"v_pos{par}", R)
+            slots = self.pinned.get(f"v_slots{par}", R)
+            ctx = self.pinned.get(f"v_ctx{par}", R)
+            bt = self.pinned.get(f"v_bt{B}_{par}", B * self.max_blocks).view(B, self.max_blocks)
+            budget = self.pinned.get(f"v_budget{par}", B)
+            keys = self.pinned.get(f"v_keys{par}", B, torch.int64)
+            sync = self.pinned.get(f"v_sync{par}", 9 * B) if self.spec == "mtp_tree" else None
+            self.h2d_bytes += plan.write_verify_inputs(ids, pos, slots, ctx, bt, budget, keys, sync)
+            for dst, src in ((v.tok, ids), (v.pos, pos), (v.slot, slots), (v.ctx, ctx), (v.bt, bt),
+                             (v.budget, budget), (v.keys, keys)):
+                dst.copy_(src, non_blocking=True)
+            if sync is not None:
+                v.sync.view(-1).copy_(sync, non_blocking=True)
+        else:
+            v.tok.copy_(torch.from_numpy(plan.token_ids))
+            v.pos.copy_(torch.from_numpy(plan.positions))
+            v.slot.copy_(torch.from_numpy(plan.slot_mapping))
+            v.ctx.copy_(torch.from_numpy(plan.context_lens))
+            v.bt.copy_(torch.from_numpy(plan.block_table).view(B, -1)[:, : v.bt.shape[1]])
+            v.budget.copy_(torch.from_numpy(plan.draft_budget))
+            v.keys.copy_(torch.from_numpy(plan.accept_keys))
+            if self.spec == "mtp_tree":
+                v.sync.copy_(torch.stack([torch.from_numpy(plan.sync_token_ids), torch.from_numpy(plan.sync_positions),
+                                          torch.from_numpy(plan.sync_slots)]))
+        return v.run(timed=True)
 
     def _run_decode(self, plan, prev: _Launched | None = None) -> torch.Tensor:
         if not self.use_graphs:
@@ -317,6 +456,8 @@ class LLMEngine:
                               decode_splits=ops.mla_decode_splits(B, self.cfg.num_heads, plan.max_context)
                               if self.is_cuda else 1)
             logits = self.model.forward(fb, self.cache)
+            if self.spec:
+                self._draft_kv(fb)
             return self._sample(logits, plan)
         g = self._graph(plan.padded_seqs)
         B = plan.padded_seqs
@@ -347,11 +488,20 @@ class LLMEngine:
             g.sampling_dirty = rows is not None
         if plan.flags & self.core.DECISION_SCHEDULED_AHEAD:
             ops.gather_prev_tokens(g.ids, prev.out, plan.num_seqs)
+        if self.spec:  # plain-step cost for the speculation utility
+            self._timing = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            self._timing[0].record()
+            out = g.run()
+            self._timing[1].record()
+            return out
         return g.run()
 
     def _launch(self, plan, prev: _Launched | None = None) -> _Launched:
         t0 = time.perf_counter()
+        self._timing = None
         try:
+            if plan.kind == 3:
+                return self._launch_verify(plan, t0)
             if plan.kind == 1:
                 sampled = self._run_prefill(plan)
             else:
@@ -368,7 +518,26 @@ class LLMEngine:
         except Exception:
             self.scheduler.fail_step(plan)
             raise
-        return _Launched(plan, host, ev, sampled, t0)
+        return _Launched(plan, host, ev, sampled, t0, self._timing)
+
+    def _launch_verify(self, plan, t0: float) -> _Launched:
+        committed, counts, paths = self._run_verify(plan)
+        v = self.verify_rounds[plan.padded_seqs]
+        n, rows = plan.num_seqs, v.rows
+        if self.is_cuda:
+            par = self._parity
+            hc = self.pinned.get(f"vc{par}", n * rows)
+            hn = self.pinned.get(f"vn{par}", n)
+            hp = self.pinned.get(f"vp{par}", n)
+            hc.copy_(committed[:n].reshape(-1), non_blocking=True)
+            hn.copy_(counts[:n], non_blocking=True)
+            hp.copy_(paths[:n], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            self.d2h_bytes += n * (rows + 2) * 4
+        else:
+            hc, hn, hp, ev = committed[:n].reshape(-1).clone(), counts[:n].clone(), paths[:n].clone(), None
+        return _Launched(plan, (hc, hn, hp), ev, counts, t0, v.timing)
 
     def _launch_idle(self) -> _Launched:
         """A forward that serves no sequence (one row, no context, no KV write), so
@@ -458,8 +627,23 @@ class LLMEngine:
         # with overlapped steps a step's time is the interval since the previous step ended
         dt = now - max(cur.t0, self._last_done)
         self._last_done = now
-        self.step_log.append(("prefill" if plan.kind == 1 else "decode", plan.num_seqs, dt, plan.num_tokens))
-        events = self.scheduler.complete_tensor(plan, cur.host)
+        if cur.timing is not None:
+            ms = cur.timing[0].elapsed_time(cur.timing[1])
+            self.device_ms[plan.kind] = self.device_ms.get(plan.kind, 0.0) + ms
+            self._record_cost(plan.kind, plan.padded_seqs, ms)
+        if plan.kind == 3:
+            hc, hn, hp = cur.host
+            n = plan.num_seqs
+            counts = hn.numpy()[:n]
+            self.step_log.append(("verify", n, dt, int(counts.sum())))
+            if self.spec == "mtp_tree":
+                for k, c in enumerate(np.bincount(hp.numpy()[:n], minlength=6)[:6]):
+                    self.tree_paths[k] += int(c)
+            events = self.scheduler.complete_verify(plan, hc.numpy()[: n * plan.rows_per_seq].reshape(n, -1), counts,
+                                                    hp.numpy()[:n] if self.spec == "mtp_tree" else None)
+        else:
+            self.step_log.append(("prefill" if plan.kind == 1 else "decode", plan.num_seqs, dt, plan.num_tokens))
+            events = self.scheduler.complete_tensor(plan, cur.host)
         changed = {}
         for ev in events:
             out = self.outputs.get(ev.id)
@@ -500,8 +684,9 @@ class LLMEngine:
         for i in ids:
             self.params.pop(i, None)
         log = self.step_log[log0:]
-        dec = [s for s in log if s[0] == "decode"]
-        dec_tokens = sum(s[1] for s in dec)
+        dec = [s for s in log if s[0] in ("decode", "verify")]
+        ver = [s for s in log if s[0] == "verify"]
+        dec_tokens = sum(s[3] for s in dec)
         dec_secs = sum(s[2] for s in dec)
         gen = sum(len(o.token_ids) for o in outs)
         ttft = [o.ttft * 1000 for o in outs if o.token_ids]
@@ -516,6 +701,10 @@ class LLMEngine:
             "decode_seconds": dec_secs,
             "decode_tokens_per_s": dec_tokens / dec_secs if dec_secs > 0 else 0.0,
             "decode_steps": len(dec),
+            "verify_steps": len(ver),
+            "verify_lanes": sum(s[1] for s in ver),
+            "verify_committed_tokens": sum(s[3] for s in ver),
+            "tokens_per_verify_lane": sum(s[3] for s in ver) / max(1, sum(s[1] for s in ver)),
             "prefill_steps": len(log) - len(dec),
             "prefill_tokens": sum(s[3] for s in log if s[0] == "prefill"),
             "prefill_seconds": sum(s[2] for s in log if s[0] == "prefill"),
@@ -533,6 +722,9 @@ class LLMEngine:
         for g in self.graphs.values():
             g.release()
         self.graphs.clear()
+        for v in self.verify_rounds.values():
+            v.release()
+        self.verify_rounds.clear()
         if hasattr(self.model, "shutdown"):
             self.model.shutdown()
         if self.is_cuda:

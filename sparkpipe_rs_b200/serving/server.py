@@ -69,6 +69,8 @@ class ServingServer:
         self.view.adaptive_decode_batch_width = ec.max_batch
         self.view.decode_batch_capacity = ec.max_batch
         self.view.prefill_wave_token_count = ec.max_prefill_tokens
+        if engine.spec:  # draft / verify speculation runs inside the engine
+            self.view.speculation_flags = self.view.speculation_flags | S.BACKEND_FLAG_MTP
         self.counters = S.ServingCounters()
         self._published: dict[int, int] = {}
         self._stop = threading.Event()
@@ -183,8 +185,9 @@ class ServingServer:
         c = self.counters
         log = self.engine.step_log
         for kind, seqs, _secs, _tokens in log:  # consume the engine's step log incrementally
-            if kind == "decode":
+            if kind in ("decode", "verify"):
                 c.decode_dispatches += 1
+                c.mtp_verify_dispatches += int(kind == "verify")
                 c.max_decode_lanes = max(c.max_decode_lanes, seqs)
                 c.max_decode_active = c.max_decode_lanes
             else:
@@ -195,6 +198,12 @@ class ServingServer:
         log.clear()
         c.queued_requests = int(self.engine.scheduler.waiting_count)
         c.prefill_tokens = int(self.engine.scheduler.stats.prefill_tokens)
+        if self.engine.spec:
+            t = self.engine.scheduler.spec_totals
+            c.mtp_draft_tokens = t["proposed"]
+            c.mtp_accepted_draft_tokens = t["accepted"]
+            c.mtp_committed_tokens = t["committed"]
+            c.mtp_rejected_tokens = t["proposed"] - t["accepted"]
         self.gateway.set_serving_counters(c)
 
 
@@ -213,10 +222,16 @@ def main(argv=None):
     ap.add_argument("--max-model-len", type=int, default=4096)
     ap.add_argument("--max-tokens", type=int, default=256)
     ap.add_argument("--stop-token", type=int, action="append", default=[])
+    ap.add_argument("--speculation", default="", choices=["", "chain", "mtp_tree"],
+                    help="speculative decoding with a one-layer draft head")
+    ap.add_argument("--draft-len", type=int, default=3)
+    ap.add_argument("--spec-p-accept", type=float, default=0.0, help="> 0: forced acceptance (benchmarks)")
+    ap.add_argument("--spec-force", action="store_true", help="verify whenever lanes qualify")
     args = ap.parse_args(argv)
     from ..models.config import get_config
     cfg = get_config(args.model)
-    ec = EngineConfig(max_batch=args.max_batch, max_model_len=args.max_model_len)
+    ec = EngineConfig(max_batch=args.max_batch, max_model_len=args.max_model_len, speculation=args.speculation,
+                      draft_len=args.draft_len, spec_p_accept=args.spec_p_accept, spec_force=args.spec_force)
     model = None
     if args.device == "cpu":
         from ..models.cpu_model import CpuMLAMoEModel

@@ -108,3 +108,37 @@ def test_disconnect_aborts_engine_request():
         assert not srv.engine.has_unfinished_requests()
         assert srv.gateway.cancelled_by_disconnect == 1
         assert srv.engine.scheduler.stats.cancelled == 1
+
+
+def test_stream_with_tree_speculation_matches_oracle():
+    """Speculative decoding through the HTTP path: MTP-tree verify rounds inside the
+    engine thread, tokens equal to the oracle's greedy continuation, MTP counters in
+    the health body."""
+    from sparkpipe_rs_b200.models.config import mtp_head
+
+    cfg = mtp_head(tiny())
+    m = CpuMLAMoEModel(cfg, seed=0)
+    g = torch.Generator().manual_seed(99)
+    wd = {k: (v + 0.15 * v.std() * torch.randn(v.shape, generator=g)) if k not in ("embed", "lm_head") and v.dim() > 1
+          else v.clone() for k, v in m.w.items()}
+    eng = LLMEngine(cfg, EngineConfig(max_batch=4, block_size=16, max_model_len=256, max_prefill_tokens=64,
+                                      speculation="mtp_tree", spec_force=True),
+                    model=m, device="cpu", draft=CpuMLAMoEModel(cfg, weights=wd))
+    tok = byte_level_tokenizer(cfg.vocab_size)
+    srv = ServingServer(eng, tok, default_max_tokens=6)
+    with srv:
+        body = json.dumps({"stream": True, "max_tokens": 24, "messages": [{"role": "user", "content": "speculate"}]})
+        r = _http.request(srv.port, "POST", "/v1/chat/completions", body)
+        evs = _sse_events(r.body)
+        toks = [d["token_id"] for n, d in evs if n == "token"]
+        ids = tok.encode(S.prepare_openai_json(body, 1 << 20).text)
+        ref, _ = oracle.greedy_generate(cfg, m.w, torch.tensor(ids), 24)
+        assert toks == ref.tolist()
+        assert eng.scheduler.stats.verify_steps > 0
+        deadline = time.time() + 5
+        h = _http.request(srv.port, "GET", "/health").body.decode()
+        while '"mtp_status":"OBSERVED"' not in h and time.time() < deadline:
+            time.sleep(0.06)
+            h = _http.request(srv.port, "GET", "/health").body.decode()
+        assert '"mtp_status":"OBSERVED"' in h
+    assert srv.error is None
