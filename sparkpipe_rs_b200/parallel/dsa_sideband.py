@@ -6,8 +6,9 @@ Transport row layout (layer-major, one row per execution row): the row's hidden
 state as bf16 (hidden x 2 bytes) followed by its selected positions as int32
 (selected x 4 bytes, -1 padding past the row's count). ``pack`` writes rows into
 one contiguous uint8 buffer (a single NVLink / fabric transfer per step); ``unpack``
-returns views into it, so the receiving stage reads hidden rows and indices without
-a copy. The row size equals the ring geometry's ``transport_bytes_per_row`` with
+returns strided views into it (row stride = the row size), so the receiving stage
+reads hidden rows and indices without a copy; an odd hidden size (int32 columns off
+their 4-byte alignment) or a non-contiguous buffer falls back to copies. The row size equals the ring geometry's ``transport_bytes_per_row`` with
 ``dsa_index_bytes_per_sequence = selected x 4``.
 
 Reference behaviour: the DSA index-share sidebands of the production topology and
@@ -42,10 +43,14 @@ def pack(hidden_rows: torch.Tensor, selected: torch.Tensor, out: torch.Tensor | 
 
 
 def unpack(buf: torch.Tensor, hidden: int, selected: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """uint8 [R, row_bytes] -> (hidden rows [R, H] bf16, selections [R, k] int32), views when aligned."""
+    """uint8 [R, row_bytes] -> (hidden rows [R, H] bf16, selections [R, k] int32): strided
+    views of ``buf`` when it is contiguous with 4-byte aligned rows and columns, else copies."""
     R = buf.shape[0]
-    if buf.shape[1] != row_bytes(hidden, selected):
+    rb = row_bytes(hidden, selected)
+    if buf.shape[1] != rb:
         raise ValueError("dsa sideband: row size")
+    if buf.is_contiguous() and hidden % 2 == 0 and buf.storage_offset() % 4 == 0:
+        return buf.view(torch.bfloat16)[:, :hidden], buf.view(torch.int32)[:, hidden // 2:hidden // 2 + selected]
     h = buf[:, : 2 * hidden].contiguous().view(torch.bfloat16)
     s = buf[:, 2 * hidden:].contiguous().view(torch.int32)
     return h.view(R, hidden), s.view(R, selected)
