@@ -142,7 +142,10 @@ def test_engine_verify_rounds_commit_the_targets_tokens(mode):
     from sparkpipe_rs_b200.serving.engine import EngineConfig, LLMEngine, SamplingParams
 
     cfg = _small(layers=1)
-    target, draft = _perturbed_pair(cfg, 0.15)
+    # chain: an unperturbed copy drafts exactly what the target decodes, so nearly every
+    # draft is accepted unless the draft's KV (prefill, plain steps, rounds) is wrong;
+    # tree: a perturbed copy, so the alternate leaves win now and then
+    target, draft = _perturbed_pair(cfg, 0.0 if mode == "chain" else 0.05)
     ec = EngineConfig(max_batch=8, block_size=64, max_model_len=512, max_prefill_tokens=512,
                       decode_buckets=(1, 2, 4, 8), speculation=mode, draft_len=3, spec_force=True)
     eng = LLMEngine(cfg, ec, model=target, device=DEV, draft=draft)
@@ -152,7 +155,8 @@ def test_engine_verify_rounds_commit_the_targets_tokens(mode):
     outs = [o.token_ids for o in res.outputs]
     assert all(len(o) == 48 for o in outs)
     st = res.stats
-    assert st["verify_steps"] > 5 and st["tokens_per_verify_lane"] > 1.3, st
+    assert st["verify_steps"] > 5, st
+    assert st["tokens_per_verify_lane"] > (3.5 if mode == "chain" else 1.1), st
     if mode == "mtp_tree":
         assert eng.tree_paths[3] + eng.tree_paths[5] > 0 and eng.tree_paths[4] > 0, eng.tree_paths
     _check_near_argmax(target, prompts, outs)
