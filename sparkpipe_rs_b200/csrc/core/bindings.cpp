@@ -204,7 +204,10 @@ void bind_prefix(py::module_& m) {
       .def_readonly("evicted_blocks", &PrefixCacheStats::evicted_blocks)
       .def_readonly("reservations", &PrefixCacheStats::reservations)
       .def_readonly("cancellations", &PrefixCacheStats::cancellations)
-      .def_readonly("released_sequences", &PrefixCacheStats::released_sequences);
+      .def_readonly("released_sequences", &PrefixCacheStats::released_sequences)
+      .def_readonly("lookahead_protections", &PrefixCacheStats::lookahead_protections)
+      .def_readonly("protected_evictions", &PrefixCacheStats::protected_evictions)
+      .def_readonly("trimmed_blocks", &PrefixCacheStats::trimmed_blocks);
   py::class_<PrefixCache>(m, "PrefixCache")
       .def(py::init<uint32_t, uint32_t, uint32_t>(), py::arg("block_tokens"), py::arg("physical_blocks"),
            py::arg("max_sequences"))
@@ -226,6 +229,12 @@ void bind_prefix(py::module_& m) {
       .def("has_sequence", &PrefixCache::has_sequence)
       .def("release_sequence", &PrefixCache::release_sequence)
       .def("evict_to_free", &PrefixCache::evict_to_free)
+      .def("reset_lookahead_protection", &PrefixCache::reset_lookahead_protection)
+      .def("protect_prompt_lookahead", [](PrefixCache& c, const std::vector<uint32_t>& t, uint32_t weight) {
+        return c.protect_prompt_lookahead(t.data(), (uint32_t)t.size(), weight);
+      })
+      .def_property_readonly("protected_warm_blocks", &PrefixCache::protected_warm_blocks)
+      .def("trim_warm_blocks", &PrefixCache::trim_warm_blocks)
       .def("bind_committed_prefix_from_sequence", &PrefixCache::bind_committed_prefix_from_sequence)
       .def("reset", &PrefixCache::reset)
       .def("reference_count", [](const PrefixCache& c, uint32_t b) { return c.arena().reference_count(b); })
@@ -284,7 +293,8 @@ void bind_scheduler(py::module_& m) {
       .value("CANCELLED", SlotState::Cancelled)
       .value("WAITING_PREFIX_COHORT", SlotState::WaitingPrefixCohort)
       .value("READY_SPECULATIVE_VERIFY", SlotState::ReadySpeculativeVerify)
-      .value("RUNNING_SPECULATIVE_VERIFY", SlotState::RunningSpeculativeVerify);
+      .value("RUNNING_SPECULATIVE_VERIFY", SlotState::RunningSpeculativeVerify)
+      .value("SWAPPED", SlotState::Swapped);
   m.attr("SCHED_CHUNKED_PREFILL") = kSchedChunkedPrefill;
   m.attr("SCHED_PREFIX_CACHE") = kSchedPrefixCache;
   m.attr("SCHED_CUDAGRAPH_PADDING") = kSchedCudaGraphPadding;
@@ -303,6 +313,10 @@ void bind_scheduler(py::module_& m) {
   m.attr("DECISION_SPECULATIVE_VERIFY") = kDecisionSpeculativeVerify;
   m.attr("DECISION_MTP_TREE_VERIFY") = kDecisionMtpTreeVerify;
   m.attr("SCHED_MTP_FORCE_ENABLE") = kSchedMtpForceEnable;
+  m.attr("SCHED_PREFIX_COHORTING") = kSchedPrefixCohorting;
+  m.attr("SCHED_LOOKAHEAD_PROTECTION") = kSchedLookaheadProtection;
+  m.attr("DECISION_PREFIX_FAMILY") = kDecisionPrefixFamily;
+  m.attr("DECISION_SWAP") = kDecisionSwap;
   m.attr("SPEC_OFF") = uint32_t(SpecMode::Off);
   m.attr("SPEC_CHAIN") = uint32_t(SpecMode::Chain);
   m.attr("SPEC_MTP_TREE") = uint32_t(SpecMode::MtpTree);
@@ -323,7 +337,9 @@ void bind_scheduler(py::module_& m) {
       .def_readwrite("spec_draft_len", &SchedulerConfig::spec_draft_len)
       .def_readwrite("spec_row_cap", &SchedulerConfig::spec_row_cap)
       .def_readwrite("spec_row_cost_milli", &SchedulerConfig::spec_row_cost_milli)
-      .def_readwrite("spec_shadow_slot_base", &SchedulerConfig::spec_shadow_slot_base);
+      .def_readwrite("spec_shadow_slot_base", &SchedulerConfig::spec_shadow_slot_base)
+      .def_readwrite("host_blocks", &SchedulerConfig::host_blocks)
+      .def_readwrite("lookahead_requests", &SchedulerConfig::lookahead_requests);
   py::class_<RequestSpec>(m, "RequestSpec")
       .def(py::init<>())
       .def(py::init([](uint64_t id, const std::vector<uint32_t>& prompt, uint32_t max_new, uint32_t priority,
@@ -377,6 +393,8 @@ void bind_scheduler(py::module_& m) {
       .def_property_readonly("context_lens", [](const StepPlan& p) { return to_np(p.context_lens); })
       .def_property_readonly("src_rows", [](const StepPlan& p) { return to_np(p.src_rows); })
       .def_readonly("rows_per_seq", &StepPlan::rows_per_seq)
+      .def_property_readonly("swap_out", [](const StepPlan& p) { return to_np(p.swap_out); })
+      .def_property_readonly("swap_in", [](const StepPlan& p) { return to_np(p.swap_in); })
       .def_property_readonly("draft_budget", [](const StepPlan& p) { return to_np(p.draft_budget); })
       .def_property_readonly("accept_keys", [](const StepPlan& p) {
         py::array_t<int64_t> a((py::ssize_t)p.accept_keys.size());
@@ -449,6 +467,13 @@ void bind_scheduler(py::module_& m) {
       .def_readonly("prefill_steps", &SchedulerStats::prefill_steps)
       .def_readonly("decode_steps", &SchedulerStats::decode_steps)
       .def_readonly("verify_steps", &SchedulerStats::verify_steps)
+      .def_readonly("swapped_out", &SchedulerStats::swapped_out)
+      .def_readonly("swapped_in", &SchedulerStats::swapped_in)
+      .def_readonly("swap_out_blocks", &SchedulerStats::swap_out_blocks)
+      .def_readonly("swap_in_blocks", &SchedulerStats::swap_in_blocks)
+      .def_readonly("family_deferrals", &SchedulerStats::family_deferrals)
+      .def_readonly("family_steps", &SchedulerStats::family_steps)
+      .def_readonly("lookahead_protected_blocks", &SchedulerStats::lookahead_protected_blocks)
       .def_readonly("preemptions", &SchedulerStats::preemptions)
       .def_readonly("prefill_tokens", &SchedulerStats::prefill_tokens)
       .def_readonly("decode_tokens", &SchedulerStats::decode_tokens)
@@ -533,6 +558,8 @@ void bind_scheduler(py::module_& m) {
       .def("bucket_for", &Scheduler::bucket_for)
       .def_property_readonly("waiting_count", &Scheduler::waiting_count)
       .def_property_readonly("running_count", &Scheduler::running_count)
+      .def_property_readonly("swapped_count", &Scheduler::swapped_count)
+      .def_property_readonly("free_host_blocks", &Scheduler::free_host_blocks)
       .def_property_readonly("max_blocks_per_seq", &Scheduler::max_blocks_per_seq)
       .def_property_readonly("stats", &Scheduler::stats)
       .def_property_readonly("prefix_cache", &Scheduler::prefix_cache, py::return_value_policy::reference_internal);

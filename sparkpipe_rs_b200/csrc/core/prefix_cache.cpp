@@ -102,19 +102,92 @@ void PrefixCache::drop(uint32_t b) {
   }
 }
 
+uint32_t PrefixCache::evict_one() {
+  // the oldest unprotected warm block, else the protected one with the least demand
+  auto victim = lru_.end();
+  const Entry* best = nullptr;
+  for (auto it = lru_.begin(); it != lru_.end(); ++it) {
+    const Entry& e = entries_.at(block_hash_[*it]);
+    if (e.protect_epoch != protect_epoch_) {
+      victim = it;
+      best = nullptr;
+      break;
+    }
+    if (!best || e.protect_weight < best->protect_weight ||
+        (e.protect_weight == best->protect_weight && e.protect_count < best->protect_count)) {
+      best = &e;
+      victim = it;
+    }
+  }
+  if (best) ++stats_.protected_evictions;
+  const uint32_t b = *victim;
+  lru_.erase(victim);
+  in_lru_[b] = 0;
+  entries_.erase(block_hash_[b]);
+  block_has_entry_[b] = 0;
+  block_hash_[b] = 0;
+  arena_.free_block(b);
+  ++stats_.evicted_blocks;
+  return b;
+}
+
 uint32_t PrefixCache::evict_to_free(uint32_t want) {
   uint32_t ev = 0;
   while (arena_.free_block_count() < want && !lru_.empty()) {
-    const uint32_t b = lru_.front();
-    lru_.pop_front();
-    in_lru_[b] = 0;
-    entries_.erase(block_hash_[b]);
-    block_has_entry_[b] = 0;
-    block_hash_[b] = 0;
-    arena_.free_block(b);
-    ++stats_.evicted_blocks;
+    evict_one();
     ++ev;
   }
+  return ev;
+}
+
+void PrefixCache::reset_lookahead_protection() { ++protect_epoch_; }
+
+uint32_t PrefixCache::protect_prompt_lookahead(const uint32_t* t, uint32_t n, uint32_t weight) {
+  if (n == 0) fail(Status::InvalidArgument, "PrefixCache: empty prompt");
+  const uint32_t max_blocks = (n - 1) / block_tokens_;
+  uint64_t h = kEmptyParentHash;
+  uint32_t marked = 0;
+  for (uint32_t b = 0; b < max_blocks; ++b) {
+    const uint32_t* bt = t + size_t(b) * block_tokens_;
+    const uint64_t nh = prefix_hash_block(bt, block_tokens_, h);
+    auto it = entries_.find(nh);
+    if (it == entries_.end() || it->second.content != prefix_content_hash(bt, block_tokens_)) break;
+    Entry& e = it->second;
+    if (e.protect_epoch != protect_epoch_) {
+      e.protect_epoch = protect_epoch_;
+      e.protect_weight = weight;
+      e.protect_count = 1;
+      ++stats_.lookahead_protections;
+    } else {
+      e.protect_weight = std::max(e.protect_weight, weight);
+      ++e.protect_count;
+    }
+    h = nh;
+    ++marked;
+  }
+  return marked;
+}
+
+uint32_t PrefixCache::cached_prefix_blocks(const std::vector<uint64_t>& chain) const {
+  uint32_t n = 0;
+  while (n < chain.size() && entries_.count(chain[n])) ++n;
+  return n;
+}
+
+uint32_t PrefixCache::protected_warm_blocks() const {
+  uint32_t n = 0;
+  for (uint32_t b : lru_)
+    if (entries_.at(block_hash_[b]).protect_epoch == protect_epoch_) ++n;
+  return n;
+}
+
+uint32_t PrefixCache::trim_warm_blocks(uint32_t max_warm) {
+  uint32_t ev = 0;
+  while (lru_.size() > max_warm) {
+    evict_one();
+    ++ev;
+  }
+  stats_.trimmed_blocks += ev;
   return ev;
 }
 

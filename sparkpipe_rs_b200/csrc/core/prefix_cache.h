@@ -62,6 +62,7 @@ struct PrefixCacheStats {
   uint64_t lookups = 0, hits = 0, hit_tokens = 0, missed_tokens = 0;
   uint64_t committed_blocks = 0, evicted_blocks = 0, reservations = 0, cancellations = 0;
   uint64_t released_sequences = 0;
+  uint64_t lookahead_protections = 0, protected_evictions = 0, trimmed_blocks = 0;
 };
 
 class PrefixCache {
@@ -92,6 +93,18 @@ class PrefixCache {
   void release_sequence(uint64_t seq);
   // Evicts warm (unreferenced, committed) blocks, oldest first, until `free_blocks` are free.
   uint32_t evict_to_free(uint32_t free_blocks);
+  // Lookahead protection: a queued prompt marks the cached blocks it will reuse for
+  // the current epoch with a demand weight (its priority). Eviction takes unprotected
+  // warm blocks first, oldest first, and protected ones last, lowest demand (then
+  // fewest requesters, then oldest) first. A new epoch clears every mark.
+  void reset_lookahead_protection();
+  uint32_t protect_prompt_lookahead(const uint32_t* tokens, uint32_t n, uint32_t weight);  // blocks marked
+  uint32_t protected_warm_blocks() const;
+  // Leading chain hashes (block 0, 1, ...) that have a cache entry: a prompt's cached
+  // prefix in blocks, from hashes its caller keeps (no content check).
+  uint32_t cached_prefix_blocks(const std::vector<uint64_t>& chain_hashes) const;
+  // Evicts warm blocks in that order until at most `max_warm` stay warm; returns how many.
+  uint32_t trim_warm_blocks(uint32_t max_warm);
   // Binds the committed prefix of `src` (first `tokens` tokens, whole blocks) to a new sequence `dst`.
   uint32_t bind_committed_prefix_from_sequence(uint64_t src, uint64_t dst, uint32_t tokens);
   void reset();
@@ -109,7 +122,10 @@ class PrefixCache {
     uint32_t block;
     uint64_t content;
     uint64_t last_used;
+    uint64_t protect_epoch = 0;
+    uint32_t protect_weight = 0, protect_count = 0;
   };
+  uint32_t evict_one();  // frees the warm block that eviction order picks; returns it
   struct Seq {
     std::vector<uint32_t> tokens;   // prompt + generated tokens known so far
     std::vector<uint32_t> blocks;
@@ -133,6 +149,7 @@ class PrefixCache {
   std::vector<uint8_t> in_lru_;
   std::unordered_map<uint64_t, Seq> seqs_;
   uint64_t clock_ = 0;
+  uint64_t protect_epoch_ = 1;
   PrefixCacheStats stats_;
 };
 

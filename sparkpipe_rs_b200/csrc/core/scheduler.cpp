@@ -19,6 +19,7 @@ Scheduler::Scheduler(const SchedulerConfig& cfg) : cfg_(cfg) {
     fail(Status::InvalidArgument, "Scheduler: tree speculation needs shadow slots");
   cache_ = std::make_unique<PrefixCache>(cfg.block_tokens, cfg.num_blocks, cfg.max_sequences);
   max_blocks_ = (cfg.max_model_len + cfg.block_tokens - 1) / cfg.block_tokens;
+  for (uint32_t i = cfg.host_blocks; i > 0; --i) host_free_.push_back(i - 1);
 }
 
 uint32_t Scheduler::full_budget() const {
@@ -95,7 +96,27 @@ int32_t Scheduler::slot_of(const Req&, uint64_t id, uint32_t pos) const {
   return int32_t(blocks.at(b) * cfg_.block_tokens + pos % cfg_.block_tokens);
 }
 
+void Scheduler::attach_swaps(StepPlan& p) {
+  if (pending_out_.empty() && pending_in_.empty()) return;
+  p.swap_out = std::move(pending_out_);
+  p.swap_in = std::move(pending_in_);
+  pending_out_.clear();
+  pending_in_.clear();
+  p.flags |= kDecisionSwap;
+}
+
 StepPlan Scheduler::schedule() {
+  // host slots read by the previous plan's restores are ordered before any copy
+  // this plan issues, so they can be handed out again
+  host_free_.insert(host_free_.end(), host_release_.begin(), host_release_.end());
+  host_release_.clear();
+  resume_swapped();
+  StepPlan p = schedule_step();
+  attach_swaps(p);
+  return p;
+}
+
+StepPlan Scheduler::schedule_step() {
   bool prefill = !waiting_.empty() && running_count_ < cfg_.max_batch;
   if (prefill && running_count_ > 0 && (cfg_.flags & kSchedPrefillDecodeInterleave) &&
       consecutive_prefills_ >= cfg_.max_consecutive_prefills)
@@ -119,6 +140,77 @@ StepPlan Scheduler::schedule() {
   return StepPlan{};
 }
 
+const std::vector<uint64_t>& Scheduler::prompt_hashes(Req& r) {
+  // full blocks of the reusable part of the prompt (all but its last token)
+  const uint32_t bt = cfg_.block_tokens, nb = r.prompt_len ? (r.prompt_len - 1) / bt : 0;
+  if (r.block_hashes.size() != nb) {
+    r.block_hashes.clear();
+    uint64_t h = kEmptyParentHash;
+    for (uint32_t b = 0; b < nb; ++b) {
+      h = prefix_hash_block(r.tokens.data() + size_t(b) * bt, bt, h);
+      r.block_hashes.push_back(h);
+    }
+  }
+  return r.block_hashes;
+}
+
+std::vector<uint64_t> Scheduler::family_followers() {
+  // Requests whose prompts share a block-aligned prefix that nobody has cached yet
+  // form a family per shared prefix length; the best family (highest priority, then
+  // most prompt tokens saved = shared x (members - 1), more members, longer prefix,
+  // earlier leader) prefills its leader alone and holds its followers back until the
+  // leader's KV for the shared prefix is in the cache, where they find it. A request
+  // already in chunked prefill leads any family it is in.
+  struct Group {
+    uint32_t blocks = 0, count = 0, prio = 0;
+    uint64_t leader = 0, leader_arrival = ~0ull;
+    bool leader_running = false;
+    std::vector<uint64_t> members;
+  };
+  std::unordered_map<uint64_t, Group> groups;
+  uint32_t scanned = 0;
+  for (uint64_t id : waiting_) {
+    if (++scanned > 256) break;
+    Req& r = reqs_.at(id);
+    const auto& hs = prompt_hashes(r);
+    const uint32_t from = r.reserved ? r.computed / cfg_.block_tokens : cache_->cached_prefix_blocks(hs);
+    for (uint32_t k = from; k < hs.size(); ++k) {
+      Group& g = groups[hs[k]];
+      g.blocks = k + 1;
+      ++g.count;
+      g.prio = std::max(g.prio, r.spec.priority);
+      g.members.push_back(id);
+      const bool better = r.reserved != g.leader_running ? r.reserved
+                          : g.leader == 0 || r.spec.priority > reqs_.at(g.leader).spec.priority ||
+                                (r.spec.priority == reqs_.at(g.leader).spec.priority && r.arrival < g.leader_arrival);
+      if (better) {
+        g.leader = id;
+        g.leader_arrival = r.arrival;
+        g.leader_running = r.reserved;
+      }
+    }
+  }
+  const Group* best = nullptr;
+  for (const auto& kv : groups) {
+    const Group& g = kv.second;
+    if (g.count < 2) continue;
+    if (!best) { best = &g; continue; }
+    const uint64_t sg = uint64_t(g.blocks) * (g.count - 1), sb = uint64_t(best->blocks) * (best->count - 1);
+    if (g.prio != best->prio ? g.prio > best->prio
+        : sg != sb           ? sg > sb
+        : g.count != best->count ? g.count > best->count
+        : g.blocks != best->blocks ? g.blocks > best->blocks
+                                   : g.leader_arrival < best->leader_arrival)
+      best = &g;
+  }
+  std::vector<uint64_t> hold;
+  if (!best) return hold;
+  for (uint64_t id : best->members)
+    if (id != best->leader && !reqs_.at(id).reserved) hold.push_back(id);
+  if (!hold.empty()) ++stats_.family_steps;
+  return hold;
+}
+
 StepPlan Scheduler::build_prefill() {
   StepPlan p;
   p.kind = StepPlan::Prefill;
@@ -126,6 +218,24 @@ StepPlan Scheduler::build_prefill() {
   p.step_index = ++step_clock_;
   p.cu_q.push_back(0);
   p.cu_k.push_back(0);
+  const bool caching = cfg_.flags & kSchedPrefixCache;
+  if (caching && (cfg_.flags & kSchedLookaheadProtection)) {
+    cache_->reset_lookahead_protection();
+    uint32_t k = 0;
+    for (uint64_t id : waiting_) {
+      if (k++ >= cfg_.lookahead_requests) break;
+      Req& r = reqs_.at(id);
+      if (!r.reserved)
+        stats_.lookahead_protected_blocks +=
+            cache_->protect_prompt_lookahead(r.tokens.data(), r.prompt_len, r.spec.priority);
+    }
+  }
+  std::vector<uint64_t> hold;
+  if (caching && (cfg_.flags & kSchedPrefixCohorting)) hold = family_followers();
+  for (uint64_t id : waiting_) {
+    Req& r = reqs_.at(id);
+    if (r.state == SlotState::WaitingPrefixCohort) r.state = SlotState::QueuedPrefill;
+  }
   uint32_t budget = cfg_.max_prefill_tokens;
   uint32_t held = 0;  // waiting sequences that already hold a decode seat
   for (uint64_t id : waiting_)
@@ -135,6 +245,12 @@ StepPlan Scheduler::build_prefill() {
   for (uint64_t id : waiting_) {
     if (budget == 0 || p.num_seqs >= cfg_.max_prefill_seqs) break;
     Req& r = reqs_.at(id);
+    if (!r.reserved && std::find(hold.begin(), hold.end(), id) != hold.end()) {
+      r.state = SlotState::WaitingPrefixCohort;  // its prefix is being prefilled by the family's leader
+      p.flags |= kDecisionPrefixFamily;
+      ++stats_.family_deferrals;
+      continue;
+    }
     if (!r.reserved) {
       if (seats == 0) break;
       try {
@@ -203,6 +319,7 @@ void Scheduler::preempt_one(uint64_t keep) {
     if (r.arrival > newest) { newest = r.arrival; victim = id; }
   }
   if (newest == 0) victim = keep;
+  if (cfg_.host_blocks && swap_out(victim)) return;
   Req& r = reqs_.at(victim);
   cache_->release_sequence(victim);
   r.reserved = false;
@@ -213,6 +330,64 @@ void Scheduler::preempt_one(uint64_t keep) {
   --running_count_;
   waiting_.push_front(victim);
   ++stats_.preemptions;
+}
+
+bool Scheduler::swap_out(uint64_t id) {
+  Req& r = reqs_.at(id);
+  const uint32_t kv_blocks = (r.computed + cfg_.block_tokens - 1) / cfg_.block_tokens;
+  if (kv_blocks > host_free_.size()) return false;
+  const auto& blocks = cache_->block_list(id);
+  r.host_slots.clear();
+  for (uint32_t b = 0; b < kv_blocks; ++b) {
+    const uint32_t slot = host_free_.back();
+    host_free_.pop_back();
+    r.host_slots.push_back(slot);
+    pending_out_.push_back(int32_t(blocks[b]));
+    pending_out_.push_back(int32_t(slot));
+  }
+  // the copies run before this plan's step, so the blocks may be reused by it
+  cache_->release_sequence(id);
+  r.reserved = false;
+  r.state = SlotState::Swapped;
+  running_.erase(std::find(running_.begin(), running_.end(), id));
+  --running_count_;
+  swapped_.push_back(id);
+  ++stats_.swapped_out;
+  ++stats_.preemptions;
+  stats_.swap_out_blocks += kv_blocks;
+  return true;
+}
+
+void Scheduler::resume_swapped() {
+  while (!swapped_.empty() && running_count_ < cfg_.max_batch) {
+    const uint64_t id = swapped_.front();
+    Req& r = reqs_.at(id);
+    const uint32_t len = (uint32_t)r.tokens.size();
+    PrefixReservation res;
+    try {
+      // blocks for every token; a cached prefix is bound instead of restored
+      res = cache_->reserve_prompt(id, r.tokens.data(), len);
+    } catch (const StatusError& e) {
+      if (e.status == Status::CapacityExceeded) break;
+      throw;
+    }
+    const uint32_t bt = cfg_.block_tokens;
+    const uint32_t hit = res.reusable_token_count / bt, kv_blocks = (r.computed + bt - 1) / bt;
+    const auto& blocks = cache_->block_list(id);
+    for (uint32_t b = hit; b < kv_blocks; ++b) {
+      pending_in_.push_back(int32_t(r.host_slots[b]));
+      pending_in_.push_back(int32_t(blocks[b]));
+    }
+    stats_.swap_in_blocks += kv_blocks > hit ? kv_blocks - hit : 0;
+    host_release_.insert(host_release_.end(), r.host_slots.begin(), r.host_slots.end());
+    r.host_slots.clear();
+    r.reserved = true;
+    r.state = r.lane.budget ? SlotState::ReadySpeculativeVerify : SlotState::ReadyDecode;
+    running_.push_back(id);
+    ++running_count_;
+    swapped_.pop_front();
+    ++stats_.swapped_in;
+  }
 }
 
 StepPlan Scheduler::build_decode() {
@@ -397,6 +572,7 @@ StepPlan Scheduler::try_build_verify(const StepPlan& d) {
 
 StepPlan Scheduler::schedule_ahead(const StepPlan& inflight) {
   if (inflight.kind != StepPlan::Decode) return StepPlan{};
+  if (!swapped_.empty() || !pending_out_.empty() || !pending_in_.empty()) return StepPlan{};
   // the policy would run a prefill next (a waiting prompt and a free seat)
   if (!waiting_.empty() && running_count_ < cfg_.max_batch) return StepPlan{};
   // the decode set must be the in-flight step's live sequences, in order
@@ -482,6 +658,11 @@ bool Scheduler::sampling_rows(const StepPlan& p, float* temp, uint64_t* key, uin
 }
 
 void Scheduler::finish(Req& r, uint64_t id, FinishReason why, std::vector<SchedEvent>& ev) {
+  if (r.state == SlotState::Swapped) {
+    host_release_.insert(host_release_.end(), r.host_slots.begin(), r.host_slots.end());
+    r.host_slots.clear();
+    swapped_.erase(std::find(swapped_.begin(), swapped_.end(), id));
+  }
   if (r.reserved) cache_->release_sequence(id);
   r.reserved = false;
   r.state = why == FinishReason::Cancelled ? SlotState::Cancelled : SlotState::Completed;

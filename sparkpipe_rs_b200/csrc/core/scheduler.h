@@ -38,6 +38,7 @@ enum class SlotState : uint32_t {
   WaitingPrefixCohort = 7,
   ReadySpeculativeVerify = 8,
   RunningSpeculativeVerify = 9,
+  Swapped = 10,  // preempted with its KV copied to the host tier, waiting to be restored
 };
 
 // configuration flags
@@ -47,10 +48,13 @@ constexpr uint32_t kSchedCudaGraphPadding = 0x04;
 constexpr uint32_t kSchedPrefillDecodeInterleave = 0x08;
 constexpr uint32_t kSchedKvCacheRequired = 0x10;
 constexpr uint32_t kSchedCrossSequencePrefixReuse = 0x40;
+constexpr uint32_t kSchedPrefixCohorting = 0x80;     // prefill a prefix family's leader before its followers
+constexpr uint32_t kSchedLookaheadProtection = 0x100;  // queued prompts protect the cached blocks they will reuse
 constexpr uint32_t kSchedMtpForceEnable = 0x200;  // verify whenever the lanes qualify (no utility comparison)
 constexpr uint32_t kSchedDefaultFlags = kSchedChunkedPrefill | kSchedPrefixCache | kSchedCudaGraphPadding |
                                         kSchedPrefillDecodeInterleave | kSchedKvCacheRequired |
-                                        kSchedCrossSequencePrefixReuse;
+                                        kSchedCrossSequencePrefixReuse | kSchedPrefixCohorting |
+                                        kSchedLookaheadProtection;
 // decision flags
 constexpr uint32_t kDecisionPrefillChunk = 0x001;
 constexpr uint32_t kDecisionPrefillFinalChunk = 0x002;
@@ -61,6 +65,8 @@ constexpr uint32_t kDecisionPrefillStep = 0x020;
 constexpr uint32_t kDecisionScheduledAhead = 0x040;  // decode planned before the previous step's tokens were read
 constexpr uint32_t kDecisionSpeculativeVerify = 0x080;
 constexpr uint32_t kDecisionMtpTreeVerify = 0x100;
+constexpr uint32_t kDecisionPrefixFamily = 0x200;   // followers of a prefix family wait for their leader
+constexpr uint32_t kDecisionSwap = 0x400;           // the plan carries host-tier swap-out / swap-in copies
 constexpr uint32_t kDecisionPreempted = 0x800;
 
 // speculation modes: a draft chain of spec_draft_len tokens per lane, or the fixed
@@ -87,6 +93,10 @@ struct SchedulerConfig {
   uint32_t spec_row_cap = 0;            // firing rows of a verify round (0: rows per lane x max_batch)
   uint32_t spec_row_cost_milli = 1000;  // a draft row's cost relative to a real row
   int64_t spec_shadow_slot_base = -1;   // tree: cache row of the first shadow slot (2 per batch row)
+  // host KV tier: preemption copies a sequence's KV blocks to host slots and
+  // restores them later instead of recomputing its context (0: recompute)
+  uint32_t host_blocks = 0;
+  uint32_t lookahead_requests = 64;     // queued prompts that protect their cached prefix
 };
 
 struct RequestSpec {
@@ -132,6 +142,9 @@ struct StepPlan {
   // tree: the draft model's KV of the 3 positions before each lane's input token
   // (rewritten every round: accepted tree tokens may not be in the draft cache)
   std::vector<int32_t> sync_token_ids, sync_positions, sync_slots;  // [3 x padded_seqs], row k * padded + b
+  // host tier, applied before the step in this order: (device block, host slot)
+  // pairs to copy out, then (host slot, device block) pairs to copy in
+  std::vector<int32_t> swap_out, swap_in;
 };
 
 struct SchedEvent {
@@ -145,6 +158,8 @@ struct SchedEvent {
 
 struct SchedulerStats {
   uint64_t steps = 0, prefill_steps = 0, decode_steps = 0, verify_steps = 0, preemptions = 0;
+  uint64_t swapped_out = 0, swapped_in = 0, swap_out_blocks = 0, swap_in_blocks = 0;
+  uint64_t family_deferrals = 0, family_steps = 0, lookahead_protected_blocks = 0;
   uint64_t prefill_tokens = 0, decode_tokens = 0, cached_prompt_tokens = 0;
   uint64_t admitted = 0, finished = 0, cancelled = 0, rejected = 0;
 };
@@ -182,7 +197,9 @@ class Scheduler {
   bool cancel(uint64_t id);  // false when unknown / already finished
   void fail_step(const StepPlan& plan);  // a dispatched step failed: cancel its sequences
 
-  bool has_work() const { return !waiting_.empty() || running_count_ > 0; }
+  bool has_work() const { return !waiting_.empty() || running_count_ > 0 || !swapped_.empty(); }
+  uint32_t swapped_count() const { return (uint32_t)swapped_.size(); }
+  uint32_t free_host_blocks() const { return (uint32_t)host_free_.size(); }
   uint32_t waiting_count() const { return (uint32_t)waiting_.size(); }
   uint32_t running_count() const { return running_count_; }
   SlotState state(uint64_t id) const;
@@ -202,6 +219,8 @@ class Scheduler {
     uint32_t generated = 0;
     SlotState state = SlotState::QueuedPrefill;
     spec::LaneState lane;
+    std::vector<uint64_t> block_hashes;  // chain hashes of the prompt's full blocks (prefix families)
+    std::vector<uint32_t> host_slots;    // swapped: host slot of each of its leading blocks
     bool reserved = false;
     uint64_t arrival = 0;
     FinishReason reason = FinishReason::None;
@@ -215,6 +234,13 @@ class Scheduler {
   uint32_t full_budget() const;
   std::vector<SchedEvent> append_committed(Req& r, uint64_t id, const int32_t* toks, uint32_t n);
   void preempt_one(uint64_t keep);
+  bool swap_out(uint64_t id);   // false when the host tier has no room
+  void resume_swapped();         // restores swapped sequences while seats and blocks allow
+  void attach_swaps(StepPlan& p);
+  // prefix families among queued, unreserved prompts: the requests to hold back this step
+  std::vector<uint64_t> family_followers();
+  StepPlan schedule_step();
+  const std::vector<uint64_t>& prompt_hashes(Req& r);
   void finish(Req& r, uint64_t id, FinishReason why, std::vector<SchedEvent>& ev);
   int32_t slot_of(const Req& r, uint64_t id, uint32_t pos) const;
 
@@ -223,6 +249,10 @@ class Scheduler {
   std::unordered_map<uint64_t, Req> reqs_;
   std::deque<uint64_t> waiting_;   // queued for (more) prefill, in admission order
   std::vector<uint64_t> running_;  // ready to decode, in admission order
+  std::deque<uint64_t> swapped_;   // swapped out, oldest first
+  std::vector<uint32_t> host_free_;
+  std::vector<int32_t> pending_out_, pending_in_;
+  std::vector<uint32_t> host_release_;  // host slots free from the next plan on
   uint32_t running_count_ = 0;
   uint32_t consecutive_prefills_ = 0;
   uint32_t max_blocks_;

@@ -76,6 +76,7 @@ class EngineConfig:
     spec_force: bool = False          # verify whenever the lanes qualify (no utility comparison)
     spec_seed: int = 17
     spec_row_cap: int = 0             # firing rows of a verify round (0: rows per lane x max_batch)
+    host_kv_blocks: int = 0           # host KV tier: preempted sequences swap their KV out (0: recompute)
 
 
 @dataclass
@@ -239,8 +240,14 @@ class LLMEngine:
             if e.spec_force:
                 flags |= self.core.SCHED_MTP_FORCE_ENABLE
         sc.flags = flags
+        sc.host_blocks = e.host_kv_blocks
         self.scheduler = self.core.Scheduler(sc)
         self.max_blocks = self.scheduler.max_blocks_per_seq
+        self.host_tier = None
+        if e.host_kv_blocks:
+            from .kv_offload import HostKvTier
+
+            self.host_tier = HostKvTier(self.cache, e.host_kv_blocks)
         self.graphs: dict[int, DecodeGraph] = {}
         self.verify_rounds: dict[int, VerifyRound] = {}
         self._cost_ema: dict[tuple[int, int], float] = {}
@@ -565,6 +572,15 @@ class LLMEngine:
         self.idle_steps += 1
         return _Launched(None, None, ev, out, t0)
 
+    def _apply_swaps(self, plan):
+        """Host-tier copies of a plan, before its step: KV blocks of preempted sequences
+        out to their host slots, then restored sequences' slots back into blocks."""
+        out, inn = plan.swap_out, plan.swap_in
+        if len(out):
+            self.host_tier.evict_to(out[0::2].tolist(), out[1::2].tolist())
+        if len(inn):
+            self.host_tier.restore(inn[0::2].tolist(), inn[1::2].tolist())
+
     def step(self) -> list[RequestOutput]:
         """One engine step: launches at most one GPU step and completes the step
         before it; returns the requests that changed."""
@@ -580,6 +596,8 @@ class LLMEngine:
                 changed.update(self._complete(cur))
                 cur = None
             p = self.scheduler.schedule()
+            if p.flags & self.core.DECISION_SWAP:
+                self._apply_swaps(p)
             plan = p if p.kind != 0 else None
         idle = False
         if self._lockstep is not None:

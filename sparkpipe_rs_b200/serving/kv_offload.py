@@ -11,8 +11,14 @@ use, on a side stream.
                    marks completion and ``wait(handle)`` orders the compute stream
                    after it, so a decode step that needs the blocks waits only for them.
 
+  evict_to / restore  the same with host slots chosen by the caller: the scheduler
+                   owns the host tier's slot allocation when it preempts a sequence to
+                   host memory and restores it later (StepPlan.swap_out / swap_in).
+
+On a CPU cache (the CPU stage driver) the same calls copy with plain indexing.
+
 The residency bookkeeping (which blocks are resident, eviction order) is the C++
-KvArena's; this is the data mover. Batches are capped so the staging buffer stays
+KvArena's / scheduler's; this is the data mover. Batches are capped so the staging buffer stays
 small; every copy is one cudaMemcpyAsync (no batched-copy API).
 
 Reference behaviour: the KV cache async prefetch backend declared in
@@ -35,6 +41,13 @@ class HostKvTier:
         self.bs = cache.block_size
         self.block_elems = self.layers * self.bs * self.row
         self.max_batch = max_batch_blocks
+        self.is_cuda = data.device.type == "cuda"
+        self.evicted_blocks = 0
+        self.restored_blocks = 0
+        if not self.is_cuda:
+            self.host = torch.empty(host_blocks, self.layers, self.bs, self.row, dtype=data.dtype)
+            self.free, self.pending = list(range(host_blocks))[::-1], []
+            return
         self.host = torch.empty(host_blocks, self.block_elems, dtype=data.dtype, pin_memory=True)
         self.free = list(range(host_blocks))[::-1]
         self.pending = []  # (event, host slots) of restores still reading their slots
@@ -43,8 +56,6 @@ class HostKvTier:
         self.staging_out = torch.empty(max_batch_blocks * self.block_elems, dtype=data.dtype, device=data.device)
         self.staging_in = torch.empty(max_batch_blocks * self.block_elems, dtype=data.dtype, device=data.device)
         self.stream = torch.cuda.Stream(device=data.device)
-        self.evicted_blocks = 0
-        self.restored_blocks = 0
 
     def _ids(self, blocks):
         return torch.as_tensor(blocks, dtype=torch.int32).to(self.cache.data.device, non_blocking=True)
@@ -67,6 +78,23 @@ class HostKvTier:
         if len(blocks) > len(self.free):
             raise RuntimeError("host KV tier full")
         slots = [self.free.pop() for _ in blocks]
+        self.evict_to(blocks, slots)
+        return slots
+
+    def _cpu_view(self):
+        return self.cache.data.view(self.layers, -1, self.bs, self.row)
+
+    def evict_to(self, blocks: list[int], slots: list[int]):
+        """Copies device blocks into the given host slots; returns when the copy is done
+        (earlier restores reading any host slot are waited for first)."""
+        assert len(slots) == len(blocks)
+        if not self.is_cuda:
+            v = self._cpu_view()
+            for b, s in zip(blocks, slots):
+                self.host[s].copy_(v[:, b])
+            self.evicted_blocks += len(blocks)
+            return
+        self._reclaim(block=True)
         for i in range(0, len(blocks), self.max_batch):
             chunk, sl = blocks[i:i + self.max_batch], slots[i:i + self.max_batch]
             n = len(chunk)
@@ -82,12 +110,21 @@ class HostKvTier:
                 j = k + 1
         torch.cuda.current_stream().synchronize()
         self.evicted_blocks += len(blocks)
-        return slots
 
-    def prefetch(self, slots: list[int], blocks: list[int]):
+    def restore(self, slots: list[int], blocks: list[int]):
+        """Copies host slots into device blocks; the compute stream waits for the copy."""
+        if not self.is_cuda:
+            v = self._cpu_view()
+            for s, b in zip(slots, blocks):
+                v[:, b].copy_(self.host[s])
+            self.restored_blocks += len(blocks)
+            return
+        self.wait(self.prefetch(slots, blocks, owned=False))
+
+    def prefetch(self, slots: list[int], blocks: list[int], owned: bool = True):
         """Starts restoring host slots into device blocks on the copy stream; returns a
         handle for ``wait``. The host slots return to the free list once the copy that
-        reads them has completed."""
+        reads them has completed (``owned``: slots from ``evict``)."""
         assert len(slots) == len(blocks)
         done = torch.cuda.Event()
         cur = torch.cuda.current_stream()
@@ -101,7 +138,9 @@ class HostKvTier:
                     st[j].copy_(self.host[s], non_blocking=True)
                 ops.kernels().kv_blocks_copy(self.cache.data, self._ids(chunk), self.staging_in, self.bs, False)
             done.record(self.stream)
-        self.pending.append((done, list(slots)))
+        # slots this tier handed out return to its free list once read; caller-owned
+        # slots are only waited for before the next eviction
+        self.pending.append((done, list(slots) if owned else []))
         self.restored_blocks += len(blocks)
         return done
 
