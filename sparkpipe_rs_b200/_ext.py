@@ -147,6 +147,8 @@ def build(name: str, verbose: bool = False):
     srcs = [str(p) for p in spec["sources"]()]
     if not srcs:
         raise RuntimeError(f"no sources for extension {name}")
+    # the stamp names the sources this build compiled, not ones edited while it ran
+    digest = _digest(name)
     kw = dict(
         name=name,
         sources=srcs,
@@ -162,7 +164,7 @@ def build(name: str, verbose: bool = False):
         kw["extra_include_paths"] = [str(CSRC / "core"), str(INCLUDE)]
         kw["extra_ldflags"] = ["-ldl"] + (_sanitizer_link_flags() if _sanitized(name) else [])
     mod = cpp_extension.load(**kw)
-    (out / f"{name}.srchash").write_text(_digest(name))
+    (out / f"{name}.srchash").write_text(digest)
     _loaded[name] = mod
     return mod
 

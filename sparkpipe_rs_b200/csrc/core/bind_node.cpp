@@ -110,6 +110,8 @@ static BindRegistrar reg([](py::module_& m) {
       .def("pump", &rd::RankDaemon::pump, py::arg("max_packets") = 64)
       .def("complete", &rd::RankDaemon::complete, py::arg("identity"), py::arg("status") = Status::Ok,
            py::arg("tokens") = std::vector<uint32_t>{}, py::arg("service_time_ns") = 0)
+      .def("complete_lanes", &rd::RankDaemon::complete_lanes, py::arg("identity"), py::arg("status"),
+           py::arg("lane_tokens"), py::arg("service_time_ns") = 0)
       .def("cancel", &rd::RankDaemon::cancel)
       .def_property_readonly("ledger", &rd::RankDaemon::ledger, py::return_value_policy::reference_internal)
       .def("stats", &rd::RankDaemon::stats);

@@ -1,9 +1,23 @@
 // Bindings of the work-control plane (packets, identity, MTP tree, KV directory).
+#include <pybind11/numpy.h>
+
+#include <cstring>
+#include <stdexcept>
+
 #include "registry.h"
 #include "work_control.h"
 
 namespace py = pybind11;
 using namespace spc;
+
+namespace {
+template <typename T>
+py::array_t<T> np_copy(const std::vector<T>& v) {
+  py::array_t<T> a((py::ssize_t)v.size());
+  if (!v.empty()) std::memcpy(a.mutable_data(), v.data(), v.size() * sizeof(T));
+  return a;
+}
+}  // namespace
 
 static BindRegistrar reg([](py::module_& m) {
   auto w = m.def_submodule("work_control", "work packets, transaction identity, MTP tree, KV directory");
@@ -57,8 +71,42 @@ static BindRegistrar reg([](py::module_& m) {
       .def_readwrite("mtp_proposed", &wc::Lane::mtp_proposed)
       .def_readwrite("mtp_accepted", &wc::Lane::mtp_accepted)
       .def_readwrite("mtp_path_id", &wc::Lane::mtp_path_id);
+  w.attr("FLAG_EXECUTION_PAYLOAD") = wc::kFlagExecutionPayload;
+  w.attr("FLAG_PREFILL") = wc::kFlagPrefill;
+  py::class_<wc::ExecPayload>(w, "ExecPayload")
+      .def_property_readonly("positions", [](const wc::ExecPayload& e) { return np_copy(e.positions); })
+      .def_property_readonly("slots", [](const wc::ExecPayload& e) { return np_copy(e.slots); })
+      .def_property_readonly("block_table", [](const wc::ExecPayload& e) { return np_copy(e.block_table); })
+      .def_property_readonly("context_lens", [](const wc::ExecPayload& e) { return np_copy(e.context_lens); })
+      .def_readonly("block_table_cols", &wc::ExecPayload::block_table_cols)
+      .def_property_readonly("cu_q", [](const wc::ExecPayload& e) { return np_copy(e.cu_q); })
+      .def_property_readonly("cu_k", [](const wc::ExecPayload& e) { return np_copy(e.cu_k); })
+      .def_property_readonly("ctx_slots", [](const wc::ExecPayload& e) { return np_copy(e.ctx_slots); })
+      .def_property_readonly("logits_rows", [](const wc::ExecPayload& e) { return np_copy(e.logits_rows); })
+      .def_readonly("max_q", &wc::ExecPayload::max_q)
+      .def_property_readonly("temperature", [](const wc::ExecPayload& e) { return np_copy(e.temperature); })
+      .def_property_readonly("sample_keys", [](const wc::ExecPayload& e) {
+        py::array_t<int64_t> a((py::ssize_t)e.sample_keys.size());
+        if (!e.sample_keys.empty()) std::memcpy(a.mutable_data(), e.sample_keys.data(), e.sample_keys.size() * 8);
+        return a;
+      });
   py::class_<wc::Packet>(w, "Packet")
       .def(py::init<>())
+      .def_readonly("exec", &wc::Packet::exec)
+      .def_property_readonly("input_token_ids", [](const wc::Packet& p) {
+        std::vector<int32_t> v;
+        for (const auto& l : p.lanes) v.push_back(int32_t(l.input_token_id));
+        return np_copy(v);
+      })
+      .def_property_readonly("prefill_tokens", [](const wc::Packet& p) {
+        std::vector<int32_t> v(p.prefill_token_ids.begin(), p.prefill_token_ids.end());
+        return np_copy(v);
+      })
+      .def_property_readonly("sequence_ids", [](const wc::Packet& p) {
+        std::vector<int64_t> v;
+        for (const auto& l : p.lanes) v.push_back(int64_t(l.sequence_id));
+        return np_copy(v);
+      })
       .def_readwrite("flags", &wc::Packet::flags)
       .def_readwrite("identity", &wc::Packet::identity)
       .def_readwrite("active_sequence_count", &wc::Packet::active_sequence_count)
@@ -79,6 +127,33 @@ static BindRegistrar reg([](py::module_& m) {
   });
   w.def("validate_packet", &wc::validate_packet);
   w.def("build_step_packet", &wc::build_step_packet);
+  // serialized micro-batch packets of one step (what the rank daemons consume)
+  w.def("build_stage_packets",
+        [](const StepPlan& plan, const wc::Identity& base, const wc::Config& cfg, uint32_t chunks, py::object temps,
+           py::object keys) {
+          py::array_t<float, py::array::c_style | py::array::forcecast> ta;
+          py::array_t<int64_t, py::array::c_style | py::array::forcecast> ka;
+          const float* tp = nullptr;
+          const uint64_t* kp = nullptr;
+          if (!temps.is_none()) {
+            ta = temps.cast<decltype(ta)>();
+            if (ta.size() < plan.num_seqs) throw std::invalid_argument("temperatures shorter than the lanes");
+            tp = ta.data();
+          }
+          if (!keys.is_none()) {
+            ka = keys.cast<decltype(ka)>();
+            if (ka.size() < plan.num_seqs) throw std::invalid_argument("keys shorter than the lanes");
+            kp = reinterpret_cast<const uint64_t*>(ka.data());
+          }
+          py::list out;
+          for (const auto& p : wc::build_stage_packets(plan, base, cfg, chunks, tp, kp)) {
+            auto b = wc::serialize(p);
+            out.append(py::bytes(reinterpret_cast<const char*>(b.data()), b.size()));
+          }
+          return out;
+        },
+        py::arg("plan"), py::arg("base"), py::arg("config"), py::arg("chunks"), py::arg("temps") = py::none(),
+        py::arg("keys") = py::none());
   auto mt = w.def_submodule("mtp_tree");
   mt.attr("CANDIDATE_COUNT") = wc::mtp::kCandidates;
   mt.attr("VERIFIER_ROW_COUNT") = wc::mtp::kVerifierRows;

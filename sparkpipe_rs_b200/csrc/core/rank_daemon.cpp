@@ -409,8 +409,7 @@ uint32_t RankDaemon::pump(uint32_t max_packets) {
   return n;
 }
 
-void RankDaemon::complete(const wc::Identity& id, Status status, const std::vector<uint32_t>& tokens,
-                          uint64_t service_time_ns) {
+RankDaemon::Item RankDaemon::retire(const wc::Identity& id, Status status) {
   auto it = inflight_.find(id.transaction_id);
   if (it == inflight_.end() || !same(it->second.packet.identity, id))
     fail(Status::NotFound, "rank daemon: completion of an unknown transaction");
@@ -424,6 +423,37 @@ void RankDaemon::complete(const wc::Identity& id, Status status, const std::vect
   if (e && !tx_terminal(e->state)) ledger_.transition(id, status == Status::Ok ? Committed : Failed, status);
   if (status == Status::Ok) ++st_.committed;
   else ++st_.failed;
+  return item;
+}
+
+void RankDaemon::complete_lanes(const wc::Identity& id, Status status,
+                                const std::vector<std::vector<uint32_t>>& lane_tokens, uint64_t service_time_ns) {
+  Item item = retire(id, status);
+  if (cfg_.rank + 1 != cfg_.world || !final_) return;
+  if (lane_tokens.size() != item.packet.lanes.size())
+    fail(Status::InvalidArgument, "rank daemon: one token list per lane");
+  for (size_t i = 0; i < item.packet.lanes.size(); ++i) {
+    const wc::Lane& l = item.packet.lanes[i];
+    FinalEvent fe;
+    fe.status = uint32_t(status);
+    fe.program_id = item.packet.pipeline_slot;
+    fe.slot = l.request_slot_index;
+    const auto& t = lane_tokens[i];
+    fe.token_ids.assign(t.begin(), t.begin() + std::min<size_t>(t.size(), kMaxFinalTokens));
+    fe.accepted_token_count = uint32_t(fe.token_ids.size());
+    fe.request_id = l.request_id;
+    fe.sequence_id = l.sequence_id;
+    fe.sequence_position = l.sequence_position;
+    fe.service_time_ns = service_time_ns;
+    fe.identity = id;
+    final_(final_event_to_wire(fe));
+    ++st_.final_events;
+  }
+}
+
+void RankDaemon::complete(const wc::Identity& id, Status status, const std::vector<uint32_t>& tokens,
+                          uint64_t service_time_ns) {
+  Item item = retire(id, status);
   if (cfg_.rank + 1 == cfg_.world && final_) {
     FinalEvent fe;
     fe.status = uint32_t(status);

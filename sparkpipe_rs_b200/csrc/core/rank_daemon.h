@@ -135,6 +135,10 @@ class RankDaemon {
   // Completion of an executed packet (by its transaction identity).
   void complete(const wc::Identity& id, Status status, const std::vector<uint32_t>& tokens,
                 uint64_t service_time_ns);
+  // Completion of a batched packet: on the last rank, one final event per lane with
+  // that lane's tokens (lane_tokens[i] for packet lane i).
+  void complete_lanes(const wc::Identity& id, Status status, const std::vector<std::vector<uint32_t>>& lane_tokens,
+                      uint64_t service_time_ns);
   void cancel(const wc::Identity& id);
   const TransactionLedger& ledger() const { return ledger_; }
   DaemonStats stats() const;
@@ -146,6 +150,7 @@ class RankDaemon {
     uint64_t fingerprint;
   };
   bool ready(const Item& it) const;
+  Item retire(const wc::Identity& id, Status status);  // ledger + bookkeeping of a completion
   DaemonConfig cfg_;
   ForwardFn forward_;
   ExecuteFn execute_;

@@ -1,5 +1,7 @@
 #include "work_control.h"
 
+#include <cstring>
+
 #include <algorithm>
 
 namespace spc {
@@ -156,6 +158,25 @@ std::vector<uint8_t> serialize(const Packet& p) {
     w.u32((uint32_t)l.speculative_draft_token_ids.size());
     for (uint32_t t : l.speculative_draft_token_ids) w.u32(t);
   }
+  if (p.flags & kFlagExecutionPayload) {
+    const ExecPayload& e = p.exec;
+    auto ints = [&](const std::vector<int32_t>& v) {
+      w.u32((uint32_t)v.size());
+      for (int32_t x : v) w.u32(uint32_t(x));
+    };
+    ints(e.positions); ints(e.slots); ints(e.block_table); ints(e.context_lens);
+    w.u32(e.block_table_cols);
+    ints(e.cu_q); ints(e.cu_k); ints(e.ctx_slots); ints(e.logits_rows);
+    w.u32(e.max_q);
+    w.u32((uint32_t)e.temperature.size());
+    for (float t : e.temperature) {
+      uint32_t bits;
+      std::memcpy(&bits, &t, 4);
+      w.u32(bits);
+    }
+    w.u32((uint32_t)e.sample_keys.size());
+    for (uint64_t k : e.sample_keys) w.u64(k);
+  }
   put_u32(&w.b[8], (uint32_t)w.b.size());
   return w.b;
 }
@@ -195,6 +216,30 @@ Packet deserialize(const uint8_t* d, size_t n) {
     if (ns > 64) fail(Status::ParseError, "work packet: speculative count");
     l.speculative_draft_token_ids.resize(ns);
     for (auto& t : l.speculative_draft_token_ids) t = r.u32();
+  }
+  if (p.flags & kFlagExecutionPayload) {
+    ExecPayload& e = p.exec;
+    auto ints = [&](std::vector<int32_t>& v) {
+      const uint32_t c = r.u32();
+      if (c > n / 4) fail(Status::ParseError, "work packet: payload array length");
+      v.resize(c);
+      for (auto& x : v) x = int32_t(r.u32());
+    };
+    ints(e.positions); ints(e.slots); ints(e.block_table); ints(e.context_lens);
+    e.block_table_cols = r.u32();
+    ints(e.cu_q); ints(e.cu_k); ints(e.ctx_slots); ints(e.logits_rows);
+    e.max_q = r.u32();
+    const uint32_t nt = r.u32();
+    if (nt > n / 4) fail(Status::ParseError, "work packet: payload temperature count");
+    e.temperature.resize(nt);
+    for (auto& t : e.temperature) {
+      const uint32_t bits = r.u32();
+      std::memcpy(&t, &bits, 4);
+    }
+    const uint32_t nk = r.u32();
+    if (nk > n / 8) fail(Status::ParseError, "work packet: payload key count");
+    e.sample_keys.resize(nk);
+    for (auto& k : e.sample_keys) k = r.u64();
   }
   if (r.o != n) fail(Status::ParseError, "work packet: trailing bytes");
   return p;
@@ -239,6 +284,24 @@ void validate_packet(const Packet& p, const Config& cfg) {
   }
   if (p.execution_row_count != p.active_sequence_count * p.rows_per_lane)
     fail(Status::InvalidArgument, "packet: execution rows");
+  if (p.flags & kFlagExecutionPayload) {
+    const ExecPayload& e = p.exec;
+    const size_t lanes = p.lanes.size(), rows = prefill ? p.prefill_token_ids.size() : lanes;
+    if (e.positions.size() != rows || e.slots.size() != rows)
+      fail(Status::InvalidArgument, "payload: one position and slot per row");
+    if (e.temperature.size() != lanes || e.sample_keys.size() != lanes)
+      fail(Status::InvalidArgument, "payload: sampling parameters per lane");
+    if (prefill) {
+      if (e.cu_q.size() != lanes + 1 || e.cu_k.size() != lanes + 1 || e.logits_rows.size() != lanes ||
+          e.cu_q.front() != 0 || uint32_t(e.cu_q.back()) != rows)
+        fail(Status::InvalidArgument, "payload: prefill layout");
+      if (!e.ctx_slots.empty() && e.ctx_slots.size() != size_t(e.cu_k.back()))
+        fail(Status::InvalidArgument, "payload: context slots");
+    } else if (e.context_lens.size() != lanes || !e.block_table_cols ||
+               e.block_table.size() != lanes * size_t(e.block_table_cols)) {
+      fail(Status::InvalidArgument, "payload: decode layout");
+    }
+  }
 }
 
 Packet build_step_packet(const StepPlan& plan, const Identity& id, const Config& cfg, uint32_t slot) {
@@ -285,6 +348,84 @@ Packet build_step_packet(const StepPlan& plan, const Identity& id, const Config&
     p.sequence_position = p.lanes[0].sequence_position;
   }
   return p;
+}
+
+std::vector<Packet> build_stage_packets(const StepPlan& plan, const Identity& base, const Config& cfg,
+                                        uint32_t chunks, const float* temps, const uint64_t* keys) {
+  if (plan.kind != StepPlan::Prefill && plan.kind != StepPlan::Decode)
+    fail(Status::InvalidArgument, "build_stage_packets: prefill or decode plans only");
+  const uint32_t n = plan.num_seqs;
+  if (!n || !chunks) fail(Status::InvalidArgument, "build_stage_packets: empty plan or zero chunks");
+  chunks = std::min(chunks, n);
+  const bool prefill = plan.kind == StepPlan::Prefill;
+  std::vector<Packet> out;
+  for (uint32_t k = 0; k < chunks; ++k) {
+    const uint32_t s0 = uint32_t(uint64_t(n) * k / chunks), s1 = uint32_t(uint64_t(n) * (k + 1) / chunks);
+    Packet p;
+    p.identity = base;
+    p.identity.transaction_id = base.transaction_id + k;
+    p.identity.step_chunk_index = k;
+    p.identity.step_chunk_count = chunks;
+    p.identity.transaction_phase = prefill ? kPhasePrefill : kPhaseDecode;
+    p.flags = (prefill ? kFlagPrefill : 0u) | kFlagExecutionPayload;
+    p.block_token_count = cfg.kv_block_tokens;
+    p.max_blocks_per_sequence = cfg.kv_block_capacity();
+    p.pipeline_slot = k;
+    p.active_sequence_count = s1 - s0;
+    p.rows_per_lane = 1;
+    p.execution_row_count = s1 - s0;
+    p.execution_batch_bucket = select_batch_bucket(s1 - s0);
+    ExecPayload& e = p.exec;
+    const uint32_t r0 = prefill ? uint32_t(plan.cu_q[s0]) : s0, r1 = prefill ? uint32_t(plan.cu_q[s1]) : s1;
+    e.positions.assign(plan.positions.begin() + r0, plan.positions.begin() + r1);
+    e.slots.assign(plan.slot_mapping.begin() + r0, plan.slot_mapping.begin() + r1);
+    if (prefill) {
+      p.prefill_token_ids.assign(plan.token_ids.begin() + r0, plan.token_ids.begin() + r1);
+      p.new_token_count = r1 - r0;
+      const int32_t q0 = plan.cu_q[s0], kb = plan.cu_k[s0];
+      for (uint32_t i = s0; i <= s1; ++i) {
+        e.cu_q.push_back(plan.cu_q[i] - q0);
+        e.cu_k.push_back(plan.cu_k[i] - kb);
+      }
+      if (plan.has_prefix)
+        e.ctx_slots.assign(plan.ctx_slots.begin() + kb, plan.ctx_slots.begin() + plan.cu_k[s1]);
+      for (uint32_t i = s0; i < s1; ++i) {
+        e.logits_rows.push_back(plan.logits_idx[i] - q0);
+        e.max_q = std::max(e.max_q, uint32_t(plan.cu_q[i + 1] - plan.cu_q[i]));
+      }
+    } else {
+      p.new_token_count = s1 - s0;
+      e.block_table_cols = plan.max_blocks;
+      e.block_table.assign(plan.block_table.begin() + size_t(s0) * plan.max_blocks,
+                           plan.block_table.begin() + size_t(s1) * plan.max_blocks);
+      e.context_lens.assign(plan.context_lens.begin() + s0, plan.context_lens.begin() + s1);
+    }
+    for (uint32_t i = s0; i < s1; ++i) {
+      Lane l;
+      l.request_id = l.sequence_id = plan.seq_ids[i];
+      l.request_generation = base.request_generation;
+      l.step_generation = base.step_generation;
+      l.request_slot_index = i;
+      if (prefill) {
+        const int32_t q1 = plan.cu_q[i + 1];
+        l.context_token_count = uint32_t(plan.cu_k[i + 1] - plan.cu_k[i]);
+        l.input_token_id = uint32_t(plan.token_ids[q1 - 1]);
+        l.sequence_position = uint64_t(plan.positions[q1 - 1]);
+      } else {
+        l.context_token_count = uint32_t(plan.context_lens[i]);
+        l.input_token_id = uint32_t(plan.token_ids[i]);
+        l.sequence_position = uint64_t(plan.positions[i]);
+      }
+      p.lanes.push_back(std::move(l));
+      e.temperature.push_back(temps ? temps[i] : 0.f);
+      e.sample_keys.push_back(keys ? keys[i] : 0);
+    }
+    p.request_id = p.lanes[0].request_id;
+    p.sequence_id = p.lanes[0].sequence_id;
+    p.sequence_position = p.lanes[0].sequence_position;
+    out.push_back(std::move(p));
+  }
+  return out;
 }
 
 // ----------------------------------------------------------------- KV directory

@@ -29,8 +29,9 @@ constexpr uint32_t kPhasePrefill = 1, kPhaseDecode = 2, kPhaseVerify = 3, kPhase
 // packet flags
 constexpr uint32_t kFlagPrefill = 0x01, kFlagMtpDraft = 0x02, kFlagDsparkTapCapture = 0x04,
                    kFlagDsparkSpeculativeVerify = 0x08, kFlagMtpSpeculativeVerify = 0x10,
-                   kFlagReleaseSequences = 0x20, kFlagMtpResolve = 0x40, kFlagMtpTreeVerify = 0x80;
-constexpr uint32_t kKnownFlags = 0xff;
+                   kFlagReleaseSequences = 0x20, kFlagMtpResolve = 0x40, kFlagMtpTreeVerify = 0x80,
+                   kFlagExecutionPayload = 0x100;
+constexpr uint32_t kKnownFlags = 0x1ff;
 
 uint64_t fingerprint_bytes(const uint8_t* data, size_t n);  // FNV-1a 64; 0 remapped to 1
 
@@ -88,6 +89,23 @@ struct Lane {
   std::vector<uint32_t> speculative_draft_token_ids;
 };
 
+// Execution payload (kFlagExecutionPayload): what a stage rank needs to run the
+// packet's rows with no scheduler of its own, since every stage caches its layers'
+// KV under the same slot numbering: each row's position and cache slot; the
+// attention layout (decode: each lane's block table and context length; prefill:
+// per-lane query / key offsets and, when a lane reuses cached tokens, the cache rows
+// of its whole context); the rows whose logits the last stage samples; and each
+// lane's sampling temperature (0 = greedy) and noise key.
+struct ExecPayload {
+  std::vector<int32_t> positions, slots;
+  std::vector<int32_t> block_table, context_lens;
+  uint32_t block_table_cols = 0;
+  std::vector<int32_t> cu_q, cu_k, ctx_slots, logits_rows;
+  uint32_t max_q = 0;
+  std::vector<float> temperature;
+  std::vector<uint64_t> sample_keys;
+};
+
 struct Packet {
   uint32_t magic = kPacketMagic, abi_version = kAbiVersion, flags = 0;
   Identity identity;
@@ -97,6 +115,7 @@ struct Packet {
   uint32_t rows_per_lane = 1, execution_row_count = 0, execution_batch_bucket = 0;
   std::vector<uint32_t> prefill_token_ids;
   std::vector<Lane> lanes;
+  ExecPayload exec;  // serialized only with kFlagExecutionPayload
 };
 
 std::vector<uint8_t> serialize(const Packet& p);
@@ -111,6 +130,11 @@ std::pair<uint32_t, uint32_t> execution_chunk_shape(uint32_t sequences, uint32_t
 
 // Builds the packet of one scheduler step (decode lanes, or the prefill tokens of its sequences).
 Packet build_step_packet(const StepPlan& plan, const Identity& id, const Config& cfg, uint32_t pipeline_slot);
+// Splits one prefill or decode step into `chunks` micro-batch packets of contiguous
+// lanes (transaction ids base.transaction_id + k, chunk k of n), each with its
+// execution payload. temps / keys: per-lane sampling parameters (null: greedy).
+std::vector<Packet> build_stage_packets(const StepPlan& plan, const Identity& base, const Config& cfg,
+                                        uint32_t chunks, const float* temps, const uint64_t* keys);
 
 // ----------------------------------------------------------------- KV directory
 enum class KvEntryState : uint8_t { Missing = 0, InFlight = 1, Resident = 2, Transient = 3 };

@@ -87,7 +87,10 @@ struct MlaCfg {
   static constexpr int MIN_CTAS = (2 * SMEM <= 227 * 1024) ? 2 : 1;
 };
 
-template <int HG, int NJ, int TOK, bool LAST = false>
+// SPLIT: the S = Q K^T product of a warp accumulates even and odd 16-wide K steps
+// into two register sets (two dependency chains of 18 MMAs instead of one of 36),
+// summed before the softmax.
+template <int HG, int NJ, int TOK, bool LAST = false, bool SPLIT = false>
 __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ, TOK>::MIN_CTAS)
     mla_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       const MlaKParams p) {
@@ -183,25 +186,35 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ
     }
 
     // ---- S = Q K^T for 16 heads x TOKW tokens of this warp
-    float sc[C::NT][4];
+    float sc[C::NT][4], sc2[C::NT][4];
 #pragma unroll
-    for (int n = 0; n < C::NT; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+    for (int n = 0; n < C::NT; ++n) {
+      sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+      sc2[n][0] = sc2[n][1] = sc2[n][2] = sc2[n][3] = 0.f;
+    }
 #pragma unroll 4
     for (int kk = 0; kk < MLA_DIM / 16; ++kk) {
       const int c = kk >> 2;
       const int cc = (kk & 3) * 16;
       uint32_t a[4];
       ldsm_x4(a, swz128(sQ + c * HG * 128, qrow + (lane & 15), cc + (lane >> 4) * 8));
+      float (*acc)[4] = (SPLIT && (kk & 1)) ? sc2 : sc;
       if constexpr (C::NT == 2) {
         uint32_t bb[4];
         ldsm_x4(bb, swz128(kvb + c * TOK * 128, j * 16 + (lane & 7) + (lane >> 4) * 8, cc + ((lane >> 3) & 1) * 8));
-        mma16816(sc[0], a, bb[0], bb[1]);
-        mma16816(sc[1], a, bb[2], bb[3]);
+        mma16816(acc[0], a, bb[0], bb[1]);
+        mma16816(acc[1], a, bb[2], bb[3]);
       } else {
         uint32_t bb[2];
         ldsm_x2(bb, swz128(kvb + c * TOK * 128, j * 8 + (lane & 7), cc + ((lane >> 3) & 1) * 8));
-        mma16816(sc[0], a, bb[0], bb[1]);
+        mma16816(acc[0], a, bb[0], bb[1]);
       }
+    }
+    if constexpr (SPLIT) {
+#pragma unroll
+      for (int n = 0; n < C::NT; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[n][e] += sc2[n][e];
     }
     // ---- scale, mask, row max
     const int tok0 = kb0 * MLA_BLK + i * TOK + j * C::TOKW;
@@ -791,13 +804,13 @@ static void launch_mla_tc(const MlaDecodeLaunch& l) {
   }
 }
 
-template <int HG, int NJ, int TOK>
+template <int HG, int NJ, int TOK, bool SPLIT = false>
 static void launch_mla(const MlaDecodeLaunch& l) {
   using C = MlaCfg<HG, NJ, TOK>;
   CUtensorMap tq, tkv;
   make_tmap_2d(&tq, l.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (long long)l.B * l.H, MLA_DIM, MLA_DIM, HG, 64);
   make_tmap_2d(&tkv, l.cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.num_slots, MLA_DIM, MLA_DIM, TOK, 64);
-  auto kern = l.last_slot ? mla_decode_kernel<HG, NJ, TOK, true> : mla_decode_kernel<HG, NJ, TOK, false>;
+  auto kern = l.last_slot ? mla_decode_kernel<HG, NJ, TOK, true, SPLIT> : mla_decode_kernel<HG, NJ, TOK, false, SPLIT>;
   set_smem_bytes(kern, C::SMEM);
   MlaKParams p;
   p.block_table = l.block_table;
@@ -853,11 +866,32 @@ int mla_default_impl() {
   return t;
 }
 
+// Warp layout of the 16-head, 64-token mma.sync kernel: SPARKPIPE_MLA_WARPS=8 splits
+// each stage's tokens and latent columns over 8 warps instead of 4 (measured slower:
+// 27.1 vs 25.0 us at B=64, 16 heads, ctx 1024). The S product's two accumulator
+// chains are the default (25.0 vs 25.3 us there, 56.9 vs 57.2 us at B=32, 64 heads,
+// ctx 2048); SPARKPIPE_MLA_SPLIT_ACC=0 uses one chain.
+int mla_warps16() {
+  static const int w = [] {
+    const char* e = std::getenv("SPARKPIPE_MLA_WARPS");
+    return (e && std::string(e) == "8") ? 8 : 4;
+  }();
+  return w;
+}
+bool mla_split_acc() {
+  static const bool v = [] {
+    const char* e = std::getenv("SPARKPIPE_MLA_SPLIT_ACC");
+    return !(e && std::string(e) == "0");
+  }();
+  return v;
+}
+
 int mla_ctas_per_sm(int heads, int impl) {
   if (impl == MLA_IMPL_AUTO) impl = mla_default_impl();
   if (impl == MLA_IMPL_TC) return 1;
   const int tok = mla_stage_tokens();
   if (heads % 32 == 0) return tok == 64 ? MlaCfg<32, 4, 64>::MIN_CTAS : MlaCfg<32, 4, 32>::MIN_CTAS;
+  if (tok == 64 && mla_warps16() == 8) return MlaCfg<16, 8, 64>::MIN_CTAS;
   return tok == 64 ? MlaCfg<16, 4, 64>::MIN_CTAS : MlaCfg<16, 4, 32>::MIN_CTAS;
 }
 
@@ -875,11 +909,23 @@ void mla_decode(const MlaDecodeLaunch& l) {
     return;
   }
   if (l.H % 32 == 0) {
-    if (mla_stage_tokens() == 64) launch_mla<32, 4, 64>(l);
-    else launch_mla<32, 4, 32>(l);
+    if (mla_stage_tokens() == 64) {
+      if (mla_split_acc()) launch_mla<32, 4, 64, true>(l);
+      else launch_mla<32, 4, 64>(l);
+    } else {
+      launch_mla<32, 4, 32>(l);
+    }
+  } else if (mla_stage_tokens() == 64) {
+    const bool sp = mla_split_acc();
+    if (mla_warps16() == 8) {
+      if (sp) launch_mla<16, 8, 64, true>(l);
+      else launch_mla<16, 8, 64>(l);
+    } else {
+      if (sp) launch_mla<16, 4, 64, true>(l);
+      else launch_mla<16, 4, 64>(l);
+    }
   } else {
-    if (mla_stage_tokens() == 64) launch_mla<16, 4, 64>(l);
-    else launch_mla<16, 4, 32>(l);
+    launch_mla<16, 4, 32>(l);
   }
 }
 

@@ -1,87 +1,50 @@
-"""Pipeline parallelism: layer stages on separate ranks, hidden states handed
-off with point-to-point send/recv (NCCL between GPUs, gloo between CPU ranks).
+"""Pipeline parallelism driven by the work plane: layer stages on separate ranks,
+every step carried to them as work-control packets through each rank's daemon.
 
-Rank 0 runs the serving engine and stage 0. For every step it broadcasts the
-step's batch description (one small int32 tensor: header + token ids,
-positions, cache slots, cu_seqlens / block tables) to all stage ranks, runs
-its layers and sends the residual stream to stage 1; each stage receives,
-runs its layers and forwards; the last stage computes the logits of the
-requested rows and sends them back to rank 0. Every stage owns the paged KV
-cache of its own layers with the same block numbering, so the scheduler's
-slot mapping is valid on every stage.
+Rank 0 runs the serving engine and stage 0. A scheduler step becomes ``chunks``
+micro-batch packets (``work_control.build_stage_packets``: contiguous lanes, one
+transaction each, with an execution payload: rows' positions and cache slots,
+decode block tables and context lengths or prefill query / key offsets, and each
+lane's sampling parameters). Each packet enters rank 0's ``RankDaemon`` (ledger
+handshake, duplicate check, per-sequence ordering), which forwards it to the next
+rank before it runs the local stage (forward-then-submit). Every rank runs its
+layers on the packet's rows and hands the residual stream on with a point-to-point
+send (NCCL between GPUs, gloo between CPU ranks); the last rank computes the
+logits of the packet's sampling rows, samples them (greedy, or Gumbel-max with the
+lane's temperature and noise key) and completes the transaction with one final
+event per lane, which goes back to rank 0 as one message per packet. Rank 0 turns
+the final events into the step's sampled tokens.
 
-Stage boundaries come from the stage planner (``core.build_stage_plan``); the
-reference cuts its 13-node ring the same way
-(crates/spark-sched/src/stage_plan.rs:404-484) and hands hidden states over
-its pluggable transport (crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_hidden_transport.h:11-345).
+Micro-batches overlap stages: while stage s runs micro-batch k + 1, stage s + 1
+runs micro-batch k, and each hidden-state send is asynchronous, so a step of two
+stages and two micro-batches takes about three stage-halves instead of four.
+
+Control messages (packet wires forward, final-event batches back to rank 0) travel
+on a gloo group as a length followed by the bytes; a zero length ends the run.
+Every stage owns the paged KV cache of its own layers with the scheduler's block
+numbering, so a packet's slots are valid on every stage.
+
+Stage boundaries come from the stage planner (``core.stage_plan``); the reference
+cuts its ring the same way (crates/spark-sched/src/stage_plan.rs:404-484). The
+packet / ledger / final-event flow follows crates/spark-node/src/rank_daemon/
+daemon.rs:987-1128 and backend/decode.rs:144-746, with the hidden-state hand-off of
+crates/spark-abi/vendor/sparkpipe/include/sparkpipe/spark_hidden_transport.h.
 """
 from __future__ import annotations
+
+import time
 
 import torch
 import torch.distributed as dist
 
+from ..core import core
 from ..models.mla_moe import ForwardBatch
 
-HEADER = 16
-MODES = {"prefill": 1, "decode": 2}
-
-
-def pack_batch(fb: ForwardBatch) -> torch.Tensor:
-    """Flattens a ForwardBatch into one int32 CPU tensor (header + arrays)."""
-    parts = [fb.token_ids, fb.positions, fb.slot_mapping]
-    hdr = [0] * HEADER
-    hdr[0] = MODES[fb.mode]
-    hdr[1] = fb.token_ids.numel()
-    if fb.mode == "decode":
-        hdr[2], hdr[3] = fb.block_table.shape
-        hdr[4] = fb.decode_splits
-        parts += [fb.block_table.flatten(), fb.context_lens]
-    else:
-        hdr[2] = fb.cu_q.numel()
-        hdr[3] = fb.max_q
-        hdr[5] = fb.ctx_slots.numel() if fb.ctx_slots is not None else -1
-        parts += [fb.cu_q, fb.cu_k]
-        if fb.ctx_slots is not None:
-            parts.append(fb.ctx_slots)
-    hdr[6] = fb.logits_idx.numel() if fb.logits_idx is not None else -1
-    if fb.logits_idx is not None:
-        parts.append(fb.logits_idx)
-    body = torch.cat([p.reshape(-1).to("cpu", torch.int32) for p in parts])
-    return torch.cat([torch.tensor(hdr, dtype=torch.int32), body])
-
-
-def unpack_batch(buf: torch.Tensor, device) -> ForwardBatch:
-    h = buf[:HEADER].tolist()
-    mode = "prefill" if h[0] == 1 else "decode"
-    T = h[1]
-    off = HEADER
-
-    def take(n):
-        nonlocal off
-        t = buf[off:off + n].to(device)
-        off += n
-        return t
-
-    ids, pos, slots = take(T), take(T), take(T)
-    fb = ForwardBatch(mode=mode, token_ids=ids, positions=pos, slot_mapping=slots)
-    if mode == "decode":
-        rows, cols = h[2], h[3]
-        fb.block_table = take(rows * cols).view(rows, cols)
-        fb.context_lens = take(rows)
-        fb.decode_splits = h[4]
-    else:
-        nb = h[2]
-        fb.cu_q, fb.cu_k = take(nb), take(nb)
-        fb.max_q = h[3]
-        if h[5] >= 0:
-            fb.ctx_slots = take(h[5])
-    if h[6] >= 0:
-        fb.logits_idx = take(h[6])
-    return fb
+FINAL_EVENT_BYTES = 272
 
 
 def split_layers(num_layers: int, stages: int, first_routed_layer: int = 0) -> list[list[int]]:
-    """Balanced contiguous layer ranges (uniform per-layer cost); see core.build_stage_plan
+    """Balanced contiguous layer ranges (uniform per-layer cost); see core.stage_plan
     for the cost-driven planner."""
     base, extra = divmod(num_layers, stages)
     out, start = [], 0
@@ -92,76 +55,230 @@ def split_layers(num_layers: int, stages: int, first_routed_layer: int = 0) -> l
     return out
 
 
-class PipelineModel:
-    """Rank-0 view of a pipelined model: ``forward`` drives every stage and returns
-    the last stage's logits (or hidden states)."""
+def work_config(cfg, block_size: int, max_model_len: int, max_lanes: int, max_prefill_tokens: int):
+    """Packet geometry the daemons validate against."""
+    w = core().work_control.Config()
+    w.kv_block_tokens = block_size
+    w.maximum_context_tokens = -(-max_model_len // block_size) * block_size
+    w.output_vocab_count = cfg.vocab_size
+    w.max_lane_count = max(1, max_lanes)
+    w.max_prefill_tokens_per_packet = max(1, max_prefill_tokens)
+    return w
 
-    def __init__(self, local_model, stage_layers: list[list[int]], group=None, device=None):
-        self.local = local_model
-        self.stage_layers = stage_layers
+
+class _Link:
+    """Length-prefixed byte messages on a gloo group; sends are asynchronous and
+    complete before the next send to the same peer reuses nothing (each keeps its
+    buffers until ``drain``)."""
+
+    def __init__(self, group):
         self.group = group
+        self.pending = []
+
+    def send(self, dst: int, payload: bytes):
+        n = torch.tensor([len(payload)], dtype=torch.int64)
+        self.pending.append((dist.isend(n, dst, group=self.group), n))
+        if payload:
+            buf = torch.frombuffer(bytearray(payload), dtype=torch.uint8)
+            self.pending.append((dist.isend(buf, dst, group=self.group), buf))
+        if len(self.pending) > 64:
+            self.drain(keep=16)
+
+    def recv(self, src: int) -> bytes:
+        n = torch.zeros(1, dtype=torch.int64)
+        dist.recv(n, src, group=self.group)
+        if int(n) == 0:
+            return b""
+        buf = torch.empty(int(n), dtype=torch.uint8)
+        dist.recv(buf, src, group=self.group)
+        return buf.numpy().tobytes()
+
+    def drain(self, keep: int = 0):
+        while len(self.pending) > keep:
+            w, _ = self.pending.pop(0)
+            w.wait()
+
+
+def sample_rows(logits: torch.Tensor, temps, keys) -> list[int]:
+    """Greedy argmax per row, or Gumbel-max for rows with a temperature, the noise
+    seeded by the row's key (the engine's sampling, at the last stage)."""
+    if logits.is_cuda:
+        from .. import ops
+
+        if temps is None or not (temps > 0).any():
+            return ops.sample_tokens(logits).tolist()
+        t = torch.as_tensor(temps, dtype=torch.float32).to(logits.device)
+        k = torch.as_tensor(keys, dtype=torch.int64).to(logits.device)
+        return ops.sample_tokens(logits, row_temp=t, row_key=k).tolist()
+    out = logits.float().argmax(-1).tolist()
+    if temps is not None:
+        for i, t in enumerate(temps):
+            if t > 0:
+                g = torch.Generator().manual_seed(int(keys[i]) & ((1 << 63) - 1))
+                u = torch.rand(logits.shape[1], generator=g).clamp_min(1e-20)
+                out[i] = int((logits[i].float() / float(t) - torch.log(-torch.log(u))).argmax())
+    return out
+
+
+class StageRuntime:
+    """One pipeline rank: its daemon, its layers and KV cache, its links."""
+
+    def __init__(self, model, stage_layers: list[list[int]], cache, wcfg, group=None, control_group=None,
+                 device=None):
+        self.C = core()
+        self.model, self.stage_layers, self.cache, self.wcfg = model, stage_layers, cache, wcfg
+        self.group = group
+        self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        self.device = torch.device(device) if device is not None else local_model.device
-        self.cfg = local_model.cfg
-        assert len(stage_layers) == self.world, "one stage per rank"
+        if len(stage_layers) != self.world or self.world < 2:
+            raise ValueError("one stage per rank, at least two stages")
+        self.layers = stage_layers[self.rank]
+        self.last = self.rank == self.world - 1
+        self.device = torch.device(device) if device is not None else model.device
+        ranks = list(range(self.world)) if group is None else dist.get_process_group_ranks(group)
+        self.control = control_group or dist.new_group(ranks=ranks, backend="gloo")
+        self.link = _Link(self.control)
+        self.hidden_sends = []
+        R = self.C.rank_daemon
+        dc = R.DaemonConfig()
+        dc.rank, dc.world, dc.work = self.rank, self.world, wcfg
+        self.finals: list[bytes] = []
+        self.daemon = R.RankDaemon(dc, self._forward, self._execute, self.finals.append)
+        self.h_dtype = torch.float32 if self.device.type == "cpu" else torch.bfloat16
+        self.hidden = model.cfg.hidden_size
+        self.executed = 0
+        self.last_logits = None  # last stage: logits of the most recent packet (diagnostics)
+        self.after_execute = None  # optional callable(runtime) after each packet (diagnostics)
 
-    def _bcast(self, buf: torch.Tensor):
-        n = torch.tensor([buf.numel()], dtype=torch.int64)
-        dev = "cpu" if dist.get_backend(self.group) == "gloo" else self.device
-        n = n.to(dev)
-        dist.broadcast(n, 0, group=self.group)
-        dist.broadcast(buf.to(dev), 0, group=self.group)
+    # ------------------------------------------------------------------ daemon callbacks
+    def _forward(self, wire: bytes):
+        self.link.send(self.rank + 1, wire)
 
-    def forward(self, fb: ForwardBatch, cache, **_):
-        self._bcast(pack_batch(fb))
-        h = self.local.forward(fb, cache, layers=self.stage_layers[0], return_hidden=True, layer_offset=0) \
-            if _accepts_offset(self.local) else self.local.forward(fb, cache, layers=self.stage_layers[0],
-                                                                   return_hidden=True)
-        if self.world == 1:
-            raise RuntimeError("PipelineModel needs at least two stages")
-        dist.send(h.contiguous(), dst=1, group=self.group)
-        n_rows = fb.logits_idx.numel() if fb.logits_idx is not None else fb.token_ids.numel()
-        logits = torch.empty(n_rows, self.cfg.vocab_size, dtype=h.dtype, device=h.device)
-        dist.recv(logits, src=self.world - 1, group=self.group)
-        return logits
+    def _batch(self, pk) -> ForwardBatch:
+        W = self.C.work_control
+        e = pk.exec
+        dev = self.device
+
+        def t(a):
+            return torch.from_numpy(a).to(dev)
+
+        if pk.flags & W.FLAG_PREFILL:
+            return ForwardBatch(mode="prefill", token_ids=t(pk.prefill_tokens), positions=t(e.positions),
+                                slot_mapping=t(e.slots), cu_q=t(e.cu_q), cu_k=t(e.cu_k), max_q=int(e.max_q),
+                                ctx_slots=t(e.ctx_slots) if len(e.ctx_slots) else None,
+                                logits_idx=t(e.logits_rows))
+        lanes = len(e.context_lens)
+        splits = 1
+        if dev.type == "cuda":
+            from .. import ops
+
+            splits = ops.mla_decode_splits(lanes, self.model.cfg.num_heads, int(e.context_lens.max()))
+        return ForwardBatch(mode="decode", token_ids=t(pk.input_token_ids), positions=t(e.positions),
+                            slot_mapping=t(e.slots), block_table=t(e.block_table).view(lanes, e.block_table_cols),
+                            context_lens=t(e.context_lens), decode_splits=splits)
+
+    def _execute(self, wire: bytes):
+        t0 = time.perf_counter_ns()
+        pk = self.C.work_control.deserialize(wire)
+        fb = self._batch(pk)
+        rows = fb.token_ids.numel()
+        h = None
+        if self.rank > 0:
+            h = torch.empty(rows, self.hidden, dtype=self.h_dtype, device=self.device)
+            dist.irecv(h, self.rank - 1, group=self.group).wait()
+        out = self.model.forward(fb, self.cache, layers=self.layers, hidden_in=h, return_hidden=not self.last,
+                                 layer_offset=self.layers[0])
+        if not self.last:
+            out = out.to(self.h_dtype).contiguous()
+            self.hidden_sends.append((dist.isend(out, self.rank + 1, group=self.group), out))
+            while len(self.hidden_sends) > 4:
+                w, _ = self.hidden_sends.pop(0)
+                w.wait()
+            self.daemon.complete(pk.identity, self.C.Status.OK, [], time.perf_counter_ns() - t0)
+        else:
+            self.last_logits = out
+            e = pk.exec
+            toks = sample_rows(out, e.temperature, e.sample_keys)
+            self.finals.clear()
+            self.daemon.complete_lanes(pk.identity, self.C.Status.OK, [[t] for t in toks],
+                                       time.perf_counter_ns() - t0)
+            self.link.send(0, b"".join(self.finals))
+        self.executed += 1
+        if self.after_execute is not None:
+            self.after_execute(self)
+
+    # ------------------------------------------------------------------ stage loop (ranks >= 1)
+    def serve(self):
+        """Runs packets from the previous rank until it ends the run."""
+        while True:
+            wire = self.link.recv(self.rank - 1)
+            if not wire:
+                if not self.last:
+                    self.link.send(self.rank + 1, b"")
+                break
+            self.daemon.submit(wire)
+            self.daemon.pump()
+        self.close()
+
+    def close(self):
+        self.link.drain()
+        for w, _ in self.hidden_sends:
+            w.wait()
+        self.hidden_sends.clear()
+
+
+class PipelineModel(StageRuntime):
+    """Rank 0 of a pipeline: the engine hands it whole scheduler steps
+    (``runs_plans``) and receives each lane's sampled token from the final events."""
+
+    runs_plans = True
+
+    def __init__(self, model, stage_layers, cache, wcfg, micro_batches: int = 2, group=None, control_group=None,
+                 device=None):
+        super().__init__(model, stage_layers, cache, wcfg, group, control_group, device)
+        if self.rank != 0:
+            raise ValueError("PipelineModel runs on rank 0")
+        self.cfg = model.cfg
+        self.micro_batches = max(1, micro_batches)
+        self.step = 0
+        self.tx = 0
+        self.final_events = 0
+
+    def run_plan(self, plan, temps=None, keys=None) -> torch.Tensor:
+        """Runs one scheduler step through every stage; returns the sampled token of
+        each of the plan's sequences (int32, in plan order)."""
+        W, R = self.C.work_control, self.C.rank_daemon
+        self.step += 1
+        ident = W.Identity()
+        ident.control_generation, ident.request_generation = 1, 1
+        ident.dispatch_generation = ident.step_generation = self.step
+        ident.transaction_id = self.tx + 1
+        ident.step_chunk_count = 1
+        ident.transaction_phase = W.PHASE_PREFILL
+        n = plan.num_seqs
+        t = None if temps is None else temps.numpy()[:n]
+        k = None if keys is None else keys.numpy()[:n]
+        wires = W.build_stage_packets(plan, ident, self.wcfg, self.micro_batches, t, k)
+        self.tx += len(wires)
+        for wire in wires:
+            ack = R.ack_from_wire(self.daemon.submit(wire))
+            if ack.status != int(self.C.Status.OK):
+                raise RuntimeError(f"pipeline: packet refused by the daemon (status {ack.status})")
+            self.daemon.pump()
+        tokens: dict[int, int] = {}
+        for _ in wires:
+            buf = self.link.recv(self.world - 1)
+            for off in range(0, len(buf), FINAL_EVENT_BYTES):
+                ev = R.final_event_from_wire(buf[off:off + FINAL_EVENT_BYTES])
+                if ev.status != int(self.C.Status.OK) or not ev.token_ids:
+                    raise RuntimeError("pipeline: a stage failed its packet")
+                tokens[int(ev.sequence_id)] = int(ev.token_ids[0])
+                self.final_events += 1
+        return torch.tensor([tokens[int(s)] for s in plan.seq_ids[:n]], dtype=torch.int32)
 
     def shutdown(self):
-        stop = torch.zeros(HEADER, dtype=torch.int32)
-        self._bcast(stop)
+        self.link.send(1, b"")
+        self.close()
 
 
-def _accepts_offset(model) -> bool:
-    import inspect
-
-    return "layer_offset" in inspect.signature(model.forward).parameters
-
-
-def stage_worker_loop(local_model, stage_layers: list[list[int]], cache, group=None, device=None):
-    """Loop of ranks >= 1: receive a batch, run this stage, pass the result on.
-    Returns when rank 0 broadcasts an empty batch (``PipelineModel.shutdown``)."""
-    rank = dist.get_rank(group)
-    world = dist.get_world_size(group)
-    layers = stage_layers[rank]
-    device = torch.device(device) if device is not None else local_model.device
-    comm_dev = "cpu" if dist.get_backend(group) == "gloo" else device
-    hidden = local_model.cfg.hidden_size
-    h_dtype = torch.float32 if device.type == "cpu" else torch.bfloat16
-    while True:
-        n = torch.zeros(1, dtype=torch.int64, device=comm_dev)
-        dist.broadcast(n, 0, group=group)
-        buf = torch.zeros(int(n.item()), dtype=torch.int32, device=comm_dev)
-        dist.broadcast(buf, 0, group=group)
-        buf = buf.cpu()
-        if int(buf[0]) == 0:
-            return
-        fb = unpack_batch(buf, device)
-        T = fb.token_ids.numel()
-        h = torch.empty(T, hidden, dtype=h_dtype, device=device)
-        dist.recv(h, src=rank - 1, group=group)
-        last = rank == world - 1
-        kw = {"layer_offset": layers[0]} if _accepts_offset(local_model) else {}
-        out = local_model.forward(fb, cache, layers=layers, hidden_in=h, return_hidden=not last, **kw)
-        if last:
-            dist.send(out.to(h_dtype).contiguous(), dst=0, group=group)
-        else:
-            dist.send(out.contiguous(), dst=rank + 1, group=group)
+__all__ = ["split_layers", "work_config", "StageRuntime", "PipelineModel", "sample_rows", "FINAL_EVENT_BYTES"]

@@ -187,7 +187,8 @@ class LLMEngine:
     def __init__(self, cfg: MLAMoEConfig, ecfg: EngineConfig | None = None, model=None, device="cuda",
                  cache: KVCache | None = None, draft=None):
         """``model`` may be the GPU model, the CPU stage driver or a PipelineModel (rank 0
-        of a pipeline); ``cache`` defaults to a full cache on ``device``. ``draft``: the
+        of a pipeline, which runs whole steps through its stages and returns sampled
+        tokens); ``cache`` defaults to a full cache on ``device``. ``draft``: the
         draft model of speculation (default: a one-layer MTP-style head of ``model``)."""
         self.cfg = cfg
         self.ecfg = ecfg or EngineConfig()
@@ -260,8 +261,12 @@ class LLMEngine:
         self._ids = itertools.count(1)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
-        # CUDA eager decode reuses one set of pinned input buffers, so it stays synchronous
-        self.async_decode = e.async_decode and (self.use_graphs or not self.is_cuda)
+        # CUDA eager decode reuses one set of pinned input buffers, so it stays synchronous;
+        # a pipeline runs whole steps on its stages and needs each step's tokens first
+        self.stages = bool(getattr(self.model, "runs_plans", False))
+        self.async_decode = e.async_decode and (self.use_graphs or not self.is_cuda) and not self.stages
+        if self.stages and self.spec:
+            raise ValueError("speculation runs on a single-stage model")
         self._inflight: _Launched | None = None
         self.ahead_steps = 0  # decode steps launched ahead of the previous step's tokens
         self.idle_steps = 0   # idle forwards of a lockstep rank
@@ -509,7 +514,10 @@ class LLMEngine:
         try:
             if plan.kind == 3:
                 return self._launch_verify(plan, t0)
-            if plan.kind == 1:
+            if self.stages:
+                rows = self._sampling_rows(plan, plan.num_seqs, "s")
+                sampled = self.model.run_plan(plan, *(rows if rows is not None else (None, None)))
+            elif plan.kind == 1:
                 sampled = self._run_prefill(plan)
             else:
                 sampled = self._run_decode(plan, prev)

@@ -95,6 +95,8 @@ def test_swapped_sequences_resume_from_the_host_tier():
     assert same >= 3, [(a.token_ids[:8], b.token_ids[:8]) for a, b in zip(res.outputs, ref.outputs)]
     from test_spec_engine_gpu import _check_near_argmax
 
-    _check_near_argmax(model, prompts, [o.token_ids for o in res.outputs])
+    # a preempted sequence decodes in other batches than the teacher-forced prefill, so a
+    # near-tie may go either way: allow two bf16 ulps of logits of magnitude 16-32
+    _check_near_argmax(model, prompts, [o.token_ids for o in res.outputs], tol=0.25)
     tight.shutdown()
     roomy.shutdown()
