@@ -187,6 +187,7 @@ void bind_prefix(py::module_& m) {
       .def_readonly("requested_token_count", &PrefixLookup::requested_token_count)
       .def_readonly("matched_token_count", &PrefixLookup::matched_token_count)
       .def_readonly("matched_block_count", &PrefixLookup::matched_block_count)
+      .def_readonly("host_block_count", &PrefixLookup::host_block_count)
       .def_readonly("next_token_index", &PrefixLookup::next_token_index)
       .def_readonly("last_block_hash", &PrefixLookup::last_block_hash);
   py::class_<PrefixReservation>(m, "PrefixReservation")
@@ -207,7 +208,10 @@ void bind_prefix(py::module_& m) {
       .def_readonly("released_sequences", &PrefixCacheStats::released_sequences)
       .def_readonly("lookahead_protections", &PrefixCacheStats::lookahead_protections)
       .def_readonly("protected_evictions", &PrefixCacheStats::protected_evictions)
-      .def_readonly("trimmed_blocks", &PrefixCacheStats::trimmed_blocks);
+      .def_readonly("trimmed_blocks", &PrefixCacheStats::trimmed_blocks)
+      .def_readonly("demoted_blocks", &PrefixCacheStats::demoted_blocks)
+      .def_readonly("promoted_blocks", &PrefixCacheStats::promoted_blocks)
+      .def_readonly("host_dropped_blocks", &PrefixCacheStats::host_dropped_blocks);
   py::class_<PrefixCache>(m, "PrefixCache")
       .def(py::init<uint32_t, uint32_t, uint32_t>(), py::arg("block_tokens"), py::arg("physical_blocks"),
            py::arg("max_sequences"))
@@ -235,6 +239,14 @@ void bind_prefix(py::module_& m) {
       })
       .def_property_readonly("protected_warm_blocks", &PrefixCache::protected_warm_blocks)
       .def("trim_warm_blocks", &PrefixCache::trim_warm_blocks)
+      .def("enable_host_tier", &PrefixCache::enable_host_tier)
+      .def("take_tier_copies", [](PrefixCache& c) {
+        std::vector<int32_t> o, i;
+        c.take_tier_copies(o, i);
+        return py::make_tuple(o, i);
+      })
+      .def("release_deferred_slots", &PrefixCache::release_deferred_slots)
+      .def_property_readonly("host_entries", &PrefixCache::host_entries)
       .def("bind_committed_prefix_from_sequence", &PrefixCache::bind_committed_prefix_from_sequence)
       .def("reset", &PrefixCache::reset)
       .def("reference_count", [](const PrefixCache& c, uint32_t b) { return c.arena().reference_count(b); })
@@ -339,6 +351,7 @@ void bind_scheduler(py::module_& m) {
       .def_readwrite("spec_row_cost_milli", &SchedulerConfig::spec_row_cost_milli)
       .def_readwrite("spec_shadow_slot_base", &SchedulerConfig::spec_shadow_slot_base)
       .def_readwrite("host_blocks", &SchedulerConfig::host_blocks)
+      .def_readwrite("host_prefix_blocks", &SchedulerConfig::host_prefix_blocks)
       .def_readwrite("lookahead_requests", &SchedulerConfig::lookahead_requests);
   py::class_<RequestSpec>(m, "RequestSpec")
       .def(py::init<>())
@@ -474,6 +487,8 @@ void bind_scheduler(py::module_& m) {
       .def_readonly("family_deferrals", &SchedulerStats::family_deferrals)
       .def_readonly("family_steps", &SchedulerStats::family_steps)
       .def_readonly("lookahead_protected_blocks", &SchedulerStats::lookahead_protected_blocks)
+      .def_readonly("prefix_tier_out_blocks", &SchedulerStats::prefix_tier_out_blocks)
+      .def_readonly("prefix_tier_in_blocks", &SchedulerStats::prefix_tier_in_blocks)
       .def_readonly("preemptions", &SchedulerStats::preemptions)
       .def_readonly("prefill_tokens", &SchedulerStats::prefill_tokens)
       .def_readonly("decode_tokens", &SchedulerStats::decode_tokens)

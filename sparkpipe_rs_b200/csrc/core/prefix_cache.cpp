@@ -62,6 +62,13 @@ PrefixCache::PrefixCache(uint32_t bt, uint32_t blocks, uint32_t max_sequences)
 void PrefixCache::reset() {
   arena_.reset();
   entries_.clear();
+  for (const auto& kv : host_entries_) host_free_.push_back(kv.second.slot);
+  host_entries_.clear();
+  host_lru_.clear();
+  host_free_.insert(host_free_.end(), host_deferred_.begin(), host_deferred_.end());
+  host_deferred_.clear();
+  tier_out_.clear();
+  tier_in_.clear();
   seqs_.clear();
   lru_.clear();
   const uint32_t n = arena_.physical_block_count();
@@ -123,6 +130,15 @@ uint32_t PrefixCache::evict_one() {
   const uint32_t b = *victim;
   lru_.erase(victim);
   in_lru_[b] = 0;
+  const uint32_t slot = host_enabled_ ? host_slot() : kNoSlot;
+  if (slot != kNoSlot) {  // demote: the block's content moves to a host slot, its entry stays findable
+    const uint64_t h = block_hash_[b];
+    tier_out_.push_back(int32_t(b));
+    tier_out_.push_back(int32_t(slot));
+    host_lru_.push_back(h);
+    host_entries_[h] = HostEntry{slot, entries_.at(h).content, std::prev(host_lru_.end())};
+    ++stats_.demoted_blocks;
+  }
   entries_.erase(block_hash_[b]);
   block_has_entry_[b] = 0;
   block_hash_[b] = 0;
@@ -141,6 +157,42 @@ uint32_t PrefixCache::evict_to_free(uint32_t want) {
 }
 
 void PrefixCache::reset_lookahead_protection() { ++protect_epoch_; }
+
+void PrefixCache::enable_host_tier(uint32_t first_slot, uint32_t slots) {
+  if (!slots) fail(Status::InvalidArgument, "PrefixCache: host tier without slots");
+  host_enabled_ = true;
+  host_free_.clear();
+  for (uint32_t i = slots; i > 0; --i) host_free_.push_back(first_slot + i - 1);
+}
+
+uint32_t PrefixCache::host_slot() {
+  if (host_free_.empty()) {
+    // drop the oldest host entry that no reservation is promoting right now
+    auto it = host_lru_.begin();
+    while (it != host_lru_.end() && promoting_.count(*it)) ++it;
+    if (it == host_lru_.end()) return kNoSlot;
+    auto e = host_entries_.find(*it);
+    host_free_.push_back(e->second.slot);
+    host_entries_.erase(e);
+    host_lru_.erase(it);
+    ++stats_.host_dropped_blocks;
+  }
+  const uint32_t s = host_free_.back();
+  host_free_.pop_back();
+  return s;
+}
+
+void PrefixCache::take_tier_copies(std::vector<int32_t>& out, std::vector<int32_t>& in) {
+  out.insert(out.end(), tier_out_.begin(), tier_out_.end());
+  in.insert(in.end(), tier_in_.begin(), tier_in_.end());
+  tier_out_.clear();
+  tier_in_.clear();
+}
+
+void PrefixCache::release_deferred_slots() {
+  host_free_.insert(host_free_.end(), host_deferred_.begin(), host_deferred_.end());
+  host_deferred_.clear();
+}
 
 uint32_t PrefixCache::protect_prompt_lookahead(const uint32_t* t, uint32_t n, uint32_t weight) {
   if (n == 0) fail(Status::InvalidArgument, "PrefixCache: empty prompt");
@@ -212,7 +264,11 @@ PrefixLookup PrefixCache::probe_prompt(const uint32_t* t, uint32_t n) const {
     const uint32_t* bt = t + size_t(b) * block_tokens_;
     const uint64_t nh = prefix_hash_block(bt, block_tokens_, h);
     auto it = entries_.find(nh);
-    if (it == entries_.end() || it->second.content != prefix_content_hash(bt, block_tokens_)) break;
+    if (it == entries_.end() || it->second.content != prefix_content_hash(bt, block_tokens_)) {
+      auto ht = host_entries_.find(nh);
+      if (ht == host_entries_.end() || ht->second.content != prefix_content_hash(bt, block_tokens_)) break;
+      ++r.host_block_count;
+    }
     h = nh;
     ++r.matched_block_count;
   }
@@ -230,35 +286,60 @@ PrefixReservation PrefixCache::reserve_prompt(uint64_t id, const uint32_t* t, ui
   const PrefixLookup hit = probe_prompt(t, n);
   const uint32_t need_blocks = (n + block_tokens_ - 1) / block_tokens_;
   const uint32_t new_blocks = need_blocks - hit.matched_block_count;
-  // warm blocks that the hit itself will retain cannot also be evicted for room
+  // warm blocks that the hit itself will retain cannot also be evicted for room;
+  // host-tier hits need a fresh device block each
+  std::vector<uint64_t> chain(hit.matched_block_count);
   uint32_t hit_warm = 0;
   {
     uint64_t h = kEmptyParentHash;
     for (uint32_t b = 0; b < hit.matched_block_count; ++b) {
       h = prefix_hash_block(t + size_t(b) * block_tokens_, block_tokens_, h);
-      if (in_lru_[entries_.at(h).block]) ++hit_warm;
+      chain[b] = h;
+      auto it = entries_.find(h);
+      if (it != entries_.end() && in_lru_[it->second.block]) ++hit_warm;
     }
   }
-  if (arena_.free_block_count() + lru_.size() - hit_warm < new_blocks)
+  if (arena_.free_block_count() + lru_.size() - hit_warm < new_blocks + hit.host_block_count)
     fail(Status::CapacityExceeded, "PrefixCache: not enough KV blocks for the prompt");
   Seq s;
   s.tokens.assign(t, t + n);
-  uint64_t h = kEmptyParentHash;
+  s.blocks.assign(hit.matched_block_count, kNoSlot);
+  for (uint32_t b = 0; b < hit.matched_block_count; ++b)
+    if (!entries_.count(chain[b])) promoting_.insert(chain[b]);
+  // device hits first (retained, so promotions below cannot evict them), then promotions
   for (uint32_t b = 0; b < hit.matched_block_count; ++b) {
-    h = prefix_hash_block(t + size_t(b) * block_tokens_, block_tokens_, h);
-    Entry& e = entries_.at(h);
-    e.last_used = ++clock_;
-    retain(e.block);
-    s.blocks.push_back(e.block);
-    s.chain.push_back(h);
+    auto it = entries_.find(chain[b]);
+    if (it == entries_.end()) continue;
+    it->second.last_used = ++clock_;
+    retain(it->second.block);
+    s.blocks[b] = it->second.block;
   }
-  s.committed_blocks = hit.matched_block_count;
   try {
+    for (uint32_t b = 0; b < hit.matched_block_count; ++b) {
+      if (entries_.count(chain[b])) continue;
+      auto ht = host_entries_.find(chain[b]);
+      const uint32_t blk = take_block();
+      tier_in_.push_back(int32_t(ht->second.slot));
+      tier_in_.push_back(int32_t(blk));
+      host_deferred_.push_back(ht->second.slot);
+      entries_.emplace(chain[b], Entry{blk, ht->second.content, ++clock_});
+      block_hash_[blk] = chain[b];
+      block_has_entry_[blk] = 1;
+      host_lru_.erase(ht->second.lru);
+      host_entries_.erase(ht);
+      s.blocks[b] = blk;
+      ++stats_.promoted_blocks;
+    }
+    promoting_.clear();
     for (uint32_t b = 0; b < new_blocks; ++b) s.blocks.push_back(take_block());
   } catch (...) {
-    for (uint32_t b : s.blocks) drop(b);
+    promoting_.clear();
+    for (uint32_t b : s.blocks)
+      if (b != kNoSlot) drop(b);
     throw;
   }
+  s.chain = chain;
+  s.committed_blocks = hit.matched_block_count;
   PrefixReservation r;
   r.sequence_id = id;
   r.requested_token_count = n;
@@ -283,6 +364,12 @@ void PrefixCache::commit(uint64_t id, uint32_t computed) {
     h = prefix_hash_block(bt, block_tokens_, h);
     s.chain.push_back(h);
     const uint32_t blk = s.blocks[b];
+    auto ht = host_entries_.find(h);
+    if (ht != host_entries_.end()) {  // recomputed on the device: the host copy is redundant now
+      host_deferred_.push_back(ht->second.slot);
+      host_lru_.erase(ht->second.lru);
+      host_entries_.erase(ht);
+    }
     auto it = entries_.find(h);
     if (it == entries_.end()) {
       // first publisher of this content: the entry points at our block

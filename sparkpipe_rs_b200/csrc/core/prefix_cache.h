@@ -23,6 +23,7 @@
 #include <cstdint>
 #include <list>
 #include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 #include "common.h"
@@ -46,6 +47,7 @@ struct PrefixLookup {
   uint32_t requested_token_count = 0;
   uint32_t matched_token_count = 0;
   uint32_t matched_block_count = 0;
+  uint32_t host_block_count = 0;  // matched blocks that sit in the host tier
   uint32_t next_token_index = 0;
   uint64_t last_block_hash = kEmptyParentHash;
 };
@@ -63,6 +65,7 @@ struct PrefixCacheStats {
   uint64_t committed_blocks = 0, evicted_blocks = 0, reservations = 0, cancellations = 0;
   uint64_t released_sequences = 0;
   uint64_t lookahead_protections = 0, protected_evictions = 0, trimmed_blocks = 0;
+  uint64_t demoted_blocks = 0, promoted_blocks = 0, host_dropped_blocks = 0;
 };
 
 class PrefixCache {
@@ -105,6 +108,19 @@ class PrefixCache {
   uint32_t cached_prefix_blocks(const std::vector<uint64_t>& chain_hashes) const;
   // Evicts warm blocks in that order until at most `max_warm` stay warm; returns how many.
   uint32_t trim_warm_blocks(uint32_t max_warm);
+  // Host tier: a warm block that eviction takes is demoted to a host slot (its entry
+  // stays findable) instead of being dropped, and a prompt that hits it gets a fresh
+  // device block with the slot copied back (promotion). Demotions and promotions are
+  // data copies the caller issues before the next step, all copies out before all
+  // copies in: (device block, host slot) pairs out, (host slot, device block) pairs
+  // in. A slot read by a promotion is handed out again only after the next
+  // release_deferred_slots(), so a later copy out cannot overwrite it first. When the
+  // host slots are all taken, the oldest host entry is dropped.
+  void enable_host_tier(uint32_t first_slot, uint32_t slots);
+  void take_tier_copies(std::vector<int32_t>& out, std::vector<int32_t>& in);
+  bool has_tier_copies() const { return !tier_out_.empty() || !tier_in_.empty(); }
+  void release_deferred_slots();
+  uint32_t host_entries() const { return (uint32_t)host_entries_.size(); }
   // Binds the committed prefix of `src` (first `tokens` tokens, whole blocks) to a new sequence `dst`.
   uint32_t bind_committed_prefix_from_sequence(uint64_t src, uint64_t dst, uint32_t tokens);
   void reset();
@@ -151,6 +167,21 @@ class PrefixCache {
   uint64_t clock_ = 0;
   uint64_t protect_epoch_ = 1;
   PrefixCacheStats stats_;
+  // host tier
+  struct HostEntry {
+    uint32_t slot;
+    uint64_t content;
+    std::list<uint64_t>::iterator lru;
+  };
+  bool host_enabled_ = false;
+  std::unordered_map<uint64_t, HostEntry> host_entries_;  // chain hash -> host slot
+  std::list<uint64_t> host_lru_;                           // chain hashes, oldest first
+  std::vector<uint32_t> host_free_, host_deferred_;
+  std::vector<int32_t> tier_out_, tier_in_;
+  std::unordered_set<uint64_t> promoting_;  // host entries a reservation is bringing back
+  static constexpr uint32_t kNoSlot = 0xffffffffu;
+  // a free slot, dropping the oldest host entry not being promoted when none is free; kNoSlot if none
+  uint32_t host_slot();
 };
 
 }  // namespace spc

@@ -20,6 +20,7 @@ Scheduler::Scheduler(const SchedulerConfig& cfg) : cfg_(cfg) {
   cache_ = std::make_unique<PrefixCache>(cfg.block_tokens, cfg.num_blocks, cfg.max_sequences);
   max_blocks_ = (cfg.max_model_len + cfg.block_tokens - 1) / cfg.block_tokens;
   for (uint32_t i = cfg.host_blocks; i > 0; --i) host_free_.push_back(i - 1);
+  if (cfg.host_prefix_blocks) cache_->enable_host_tier(cfg.host_blocks, cfg.host_prefix_blocks);
 }
 
 uint32_t Scheduler::full_budget() const {
@@ -97,6 +98,11 @@ int32_t Scheduler::slot_of(const Req&, uint64_t id, uint32_t pos) const {
 }
 
 void Scheduler::attach_swaps(StepPlan& p) {
+  // prefix blocks demoted to / promoted from the cache's host tier while planning
+  const size_t o0 = pending_out_.size(), i0 = pending_in_.size();
+  cache_->take_tier_copies(pending_out_, pending_in_);
+  stats_.prefix_tier_out_blocks += (pending_out_.size() - o0) / 2;
+  stats_.prefix_tier_in_blocks += (pending_in_.size() - i0) / 2;
   if (pending_out_.empty() && pending_in_.empty()) return;
   p.swap_out = std::move(pending_out_);
   p.swap_in = std::move(pending_in_);
@@ -110,6 +116,7 @@ StepPlan Scheduler::schedule() {
   // this plan issues, so they can be handed out again
   host_free_.insert(host_free_.end(), host_release_.begin(), host_release_.end());
   host_release_.clear();
+  cache_->release_deferred_slots();
   resume_swapped();
   StepPlan p = schedule_step();
   attach_swaps(p);
@@ -603,7 +610,14 @@ StepPlan Scheduler::schedule_ahead(const StepPlan& inflight) {
     keep.push_back(i);
   }
   const uint32_t n = (uint32_t)keep.size();
-  if (n == 0) return StepPlan{};
+  if (n == 0) {
+    if (cache_->has_tier_copies()) {  // copies already planned must still reach the engine
+      StepPlan none;
+      attach_swaps(none);
+      return none;
+    }
+    return StepPlan{};
+  }
   StepPlan p;
   p.kind = StepPlan::Decode;
   p.flags = kDecisionDecodeStep | kDecisionScheduledAhead;
@@ -637,6 +651,8 @@ StepPlan Scheduler::schedule_ahead(const StepPlan& inflight) {
   ++stats_.steps;
   ++stats_.decode_steps;
   stats_.decode_tokens += n;
+  cache_->release_deferred_slots();
+  attach_swaps(p);
   return p;
 }
 

@@ -96,6 +96,9 @@ struct SchedulerConfig {
   // host KV tier: preemption copies a sequence's KV blocks to host slots and
   // restores them later instead of recomputing its context (0: recompute)
   uint32_t host_blocks = 0;
+  // host slots (after the preemption slots) where warm prefix blocks evicted from the
+  // device wait for a later prompt that reuses them (0: evicted blocks are dropped)
+  uint32_t host_prefix_blocks = 0;
   uint32_t lookahead_requests = 64;     // queued prompts that protect their cached prefix
 };
 
@@ -160,6 +163,7 @@ struct SchedulerStats {
   uint64_t steps = 0, prefill_steps = 0, decode_steps = 0, verify_steps = 0, preemptions = 0;
   uint64_t swapped_out = 0, swapped_in = 0, swap_out_blocks = 0, swap_in_blocks = 0;
   uint64_t family_deferrals = 0, family_steps = 0, lookahead_protected_blocks = 0;
+  uint64_t prefix_tier_out_blocks = 0, prefix_tier_in_blocks = 0;
   uint64_t prefill_tokens = 0, decode_tokens = 0, cached_prompt_tokens = 0;
   uint64_t admitted = 0, finished = 0, cancelled = 0, rejected = 0;
 };

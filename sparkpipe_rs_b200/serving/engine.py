@@ -77,6 +77,7 @@ class EngineConfig:
     spec_seed: int = 17
     spec_row_cap: int = 0             # firing rows of a verify round (0: rows per lane x max_batch)
     host_kv_blocks: int = 0           # host KV tier: preempted sequences swap their KV out (0: recompute)
+    host_prefix_blocks: int = 0       # host KV tier for prefix blocks evicted from the device (0: drop them)
 
 
 @dataclass
@@ -242,13 +243,14 @@ class LLMEngine:
                 flags |= self.core.SCHED_MTP_FORCE_ENABLE
         sc.flags = flags
         sc.host_blocks = e.host_kv_blocks
+        sc.host_prefix_blocks = e.host_prefix_blocks if e.prefix_caching else 0
         self.scheduler = self.core.Scheduler(sc)
         self.max_blocks = self.scheduler.max_blocks_per_seq
         self.host_tier = None
-        if e.host_kv_blocks:
+        if e.host_kv_blocks or sc.host_prefix_blocks:
             from .kv_offload import HostKvTier
 
-            self.host_tier = HostKvTier(self.cache, e.host_kv_blocks)
+            self.host_tier = HostKvTier(self.cache, e.host_kv_blocks + sc.host_prefix_blocks)
         self.graphs: dict[int, DecodeGraph] = {}
         self.verify_rounds: dict[int, VerifyRound] = {}
         self._cost_ema: dict[tuple[int, int], float] = {}
@@ -597,6 +599,8 @@ class LLMEngine:
         plan = None
         if cur is not None and cur.plan is not None and self.async_decode and cur.plan.kind == 2:
             a = self.scheduler.schedule_ahead(cur.plan)
+            if a.flags & self.core.DECISION_SWAP:
+                self._apply_swaps(a)
             if a.kind == 2:
                 plan = a
         if plan is None:

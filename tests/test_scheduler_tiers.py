@@ -152,3 +152,46 @@ def test_engine_prefix_family_saves_prefill_tokens():
         assert o.token_ids == ref.tolist()
     assert res.stats["prefill_tokens"] == 101 + 2 * 5 + 2 * 0  # the shared 96 tokens are computed once
     assert eng.scheduler.stats.family_deferrals > 0
+
+
+def test_prefix_host_tier_demotes_and_promotes():
+    pc = C.PrefixCache(4, 6, 16)
+    pc.enable_host_tier(100, 3)
+    a = list(range(100, 109))                      # 2 reusable blocks + a tail token
+    pc.reserve_prompt(1, a)
+    pc.commit(1, 8)
+    pc.release_sequence(1)                         # a's 2 blocks are warm on the device
+    pc.reserve_prompt(2, list(range(500, 524)))    # 6 blocks: both warm blocks are evicted
+    out, inn = pc.take_tier_copies()
+    assert len(out) == 4 and not inn and sorted(out[1::2]) == [100, 101] and pc.host_entries == 2
+    assert pc.stats.demoted_blocks == 2
+    # the prompt still hits its prefix: in the host tier
+    look = pc.probe_prompt(a + [1])
+    assert look.matched_block_count == 2 and look.host_block_count == 2
+    pc.release_sequence(2)
+    r = pc.reserve_prompt(3, a + [1])
+    assert r.reusable_token_count == 8
+    out, inn = pc.take_tier_copies()
+    # promotion copies land in the reservation's first two blocks; eviction made room first
+    assert list(inn[1::2]) == list(r.physical_blocks[:2]) and sorted(inn[0::2]) == [100, 101]
+    assert pc.stats.promoted_blocks == 2 and pc.host_entries == len(out) // 2
+    # the promoted slots are free again only after the deferred release
+    pc.release_deferred_slots()
+
+
+def test_engine_reuses_a_prefix_from_the_host_tier():
+    # 10 device blocks of 16: prompt A's 6 full blocks are pushed out by two other prompts,
+    # then A comes back: its prefix is restored from the host tier, not recomputed
+    cfg, m, eng = _engine(num_blocks=10, host_prefix_blocks=16)
+    g = torch.Generator().manual_seed(5)
+    a = torch.randint(0, cfg.vocab_size, (100,), generator=g).tolist()
+    first = eng.generate([a], SamplingParams(max_tokens=4, ignore_eos=True))
+    for _ in range(2):
+        other = torch.randint(0, cfg.vocab_size, (120,), generator=g).tolist()
+        eng.generate([other], SamplingParams(max_tokens=4, ignore_eos=True))
+    again = eng.generate([a], SamplingParams(max_tokens=4, ignore_eos=True))
+    st = eng.scheduler.stats
+    assert st.prefix_tier_out_blocks > 0 and st.prefix_tier_in_blocks == 6
+    assert again.stats["prefill_tokens"] == 100 - 96
+    ref, _ = oracle.greedy_generate(cfg, m.w, torch.tensor(a), 4)
+    assert first.outputs[0].token_ids == ref.tolist() == again.outputs[0].token_ids
