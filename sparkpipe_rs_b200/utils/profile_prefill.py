@@ -13,6 +13,9 @@ tokens, the V2-Lite shape) runs eagerly through the kernel-backed model:
     (``--peak-tflops``, default the driver-measured 1,385.6).
 
     python -m sparkpipe_rs_b200.utils.profile_prefill --seqs 8 --len 1024
+
+(the model in the profiled process is the only one on the device; ``--layers 2`` keeps
+an ncu capture small: one dense and one MoE layer)
 """
 from __future__ import annotations
 
@@ -54,6 +57,7 @@ def main():
     ap.add_argument("--seqs", type=int, default=8)
     ap.add_argument("--len", type=int, default=1024)
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu cases)")
     ap.add_argument("--peak-tflops", type=float, default=1385.6)
     ap.add_argument("--no-trace", action="store_true", help="skip the profiler pass (for ncu)")
     args = ap.parse_args()
@@ -61,6 +65,8 @@ def main():
     from sparkpipe_rs_b200.models.mla_moe import ForwardBatch, KVCache, MLAMoEModel, PhaseClock
 
     cfg = get_config(args.model)
+    if args.layers:
+        cfg = cfg.replace(num_layers=args.layers)
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
     S, L = args.seqs, args.len
