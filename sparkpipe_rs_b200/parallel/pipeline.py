@@ -55,6 +55,40 @@ def split_layers(num_layers: int, stages: int, first_routed_layer: int = 0) -> l
     return out
 
 
+def layer_costs(cfg, phase: str = "decode") -> tuple[list[int], int]:
+    """Relative per-layer costs and the last stage's extra (final norm + LM head):
+    decode steps are bound by the weight bytes a layer reads (every routed expert of
+    a batch), prefill chunks by the weights each token multiplies (its top-k experts)."""
+    H, nh = cfg.hidden_size, cfg.num_heads
+    qa = cfg.q_lora_rank or nh * (cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
+    attn = H * (qa + cfg.kv_lora_rank + cfg.qk_rope_head_dim) + cfg.kv_lora_rank * nh * (
+        cfg.qk_nope_head_dim + cfg.v_head_dim) + nh * cfg.v_head_dim * H
+    if cfg.q_lora_rank:
+        attn += cfg.q_lora_rank * nh * (cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
+    expert = 3 * H * cfg.moe_intermediate_size
+    routed = cfg.n_routed_experts if phase == "decode" else cfg.num_experts_per_tok
+    costs = []
+    for i in range(cfg.num_layers):
+        ffn = (routed + cfg.n_shared_experts) * expert if cfg.is_moe_layer(i) else 3 * H * cfg.intermediate_size
+        costs.append(max(1, (attn + ffn) // 1000))
+    return costs, max(1, cfg.vocab_size * H // 1000)
+
+
+def plan_stages(cfg, stages: int, costs: list[int] | None = None, final_extra: int | None = None,
+                phase: str = "decode") -> list[list[int]]:
+    """Contiguous layer ranges per stage from the stage planner: the cuts that minimise
+    the slowest stage under per-layer costs (measured, or ``layer_costs``), the last
+    stage also paying the LM head."""
+    if costs is None:
+        costs, est_extra = layer_costs(cfg, phase)
+        final_extra = est_extra if final_extra is None else final_extra
+    sp = core().stage_plan
+    first_routed = cfg.first_k_dense_replace if cfg.n_routed_experts else cfg.num_layers
+    geo = sp.Geometry(cfg.num_layers, min(first_routed, cfg.num_layers), cfg.num_layers)
+    plan = sp.build_balanced(geo, [int(c) for c in costs], int(final_extra or 0), stages)
+    return [list(range(st.first_layer, st.first_layer + st.layer_count)) for st in plan.stages]
+
+
 def work_config(cfg, block_size: int, max_model_len: int, max_lanes: int, max_prefill_tokens: int):
     """Packet geometry the daemons validate against."""
     w = core().work_control.Config()
@@ -281,4 +315,4 @@ class PipelineModel(StageRuntime):
         self.close()
 
 
-__all__ = ["split_layers", "work_config", "StageRuntime", "PipelineModel", "sample_rows", "FINAL_EVENT_BYTES"]
+__all__ = ["split_layers", "layer_costs", "plan_stages", "work_config", "StageRuntime", "PipelineModel", "sample_rows", "FINAL_EVENT_BYTES"]

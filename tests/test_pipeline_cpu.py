@@ -114,3 +114,23 @@ def test_pipeline_through_packets_ledger_and_final_events(world, micro):
     logits = last[1]   # first packet: the prefill of its lanes (micro-batch 0)
     for i in range(logits.shape[0]):
         assert (logits[i] - refs[i][1][0]).abs().max().item() < 1e-4
+
+
+def test_cost_driven_stage_cuts():
+    from sparkpipe_rs_b200.models.config import k2, v2_lite
+    from sparkpipe_rs_b200.parallel.pipeline import layer_costs, plan_stages
+
+    cfg = v2_lite()
+    costs, head = layer_costs(cfg)
+    assert costs[0] < costs[1] and head > 0          # the dense first layer reads far fewer bytes
+    cuts = plan_stages(cfg, 2)
+    assert [len(c) for c in cuts] == [14, 13] and sum(cuts, []) == list(range(27))
+    # the slowest stage is no slower than under the uniform split
+    uni = [list(range(14)), list(range(14, 27))]
+    worst = lambda st: max(sum(costs[i] for i in s) + (head if k == len(st) - 1 else 0) for k, s in enumerate(st))
+    assert worst(cuts) <= worst(uni)
+    # measured costs move the cut: an expensive last layer pulls the boundary forward
+    costs2 = list(costs)
+    costs2[-1] *= 6
+    assert len(plan_stages(cfg, 2, costs2, head)[1]) < 13
+    assert [len(c) for c in plan_stages(k2(), 4)] == [16, 15, 15, 15]
