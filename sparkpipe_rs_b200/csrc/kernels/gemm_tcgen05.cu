@@ -45,7 +45,14 @@
 
 namespace sp {
 
-enum { MODE_DENSE = 0, MODE_SPLITK = 1, MODE_GROUPED = 2 };
+// MODE_GROUPED_TM: token-major grouped GEMM for expert groups of prefill size: A is
+// the expert-sorted tokens (M = a group's rows, 128 per tile), B the expert's weight
+// rows (N), D row-major [rows, N] (or [rows, N / 2] with the fused SwiGLU: a tile's
+// columns hold [64 gate | 64 up] features twice over, so each thread's token row
+// pairs them from its own TMEM columns and writes 16 features with two 16-byte
+// stores). The weight-major grouped mode keeps decode's swap-AB shape, whose
+// transposed output is written two bytes at a time.
+enum { MODE_DENSE = 0, MODE_SPLITK = 1, MODE_GROUPED = 2, MODE_GROUPED_TM = 3 };
 
 struct GemmKParams {
   int M, N, K;
@@ -115,6 +122,30 @@ struct TileInfo {
 
 template <int BN, int MODE>
 SP_DEVI bool get_tile(const GemmKParams& p, int t, TileInfo& ti) {
+  if (MODE == MODE_GROUPED_TM) {
+    // n fastest: consecutive tiles reuse one token tile against the expert's weight tiles
+    const int nt = t % p.n_tiles;
+    const int q = t / p.n_tiles;  // global 128-row token tile
+    int lo = 0, hi = p.num_groups;
+    while (hi - lo > 1) {
+      int mid = (lo + hi) >> 1;
+      if (__ldg(p.grp_tiles + mid) <= q) lo = mid; else hi = mid;
+    }
+    const int g = lo;
+    const int mt = q - __ldg(p.grp_tiles + g);
+    const int r0 = __ldg(p.grp_rows + g);
+    const int r1 = __ldg(p.grp_rows + g + 1);
+    ti.a_row = r0 + mt * BM;
+    ti.a_k = p.a_k0;
+    ti.b_row = p.b_row0 + g * p.b_batch_rows + nt * BN;
+    ti.b_k = p.b_k0;
+    ti.m_base = ti.a_row;
+    ti.n_base = p.swiglu ? nt * (BN / 2) : nt * BN;
+    ti.m_valid = min(BM, r1 - ti.a_row);
+    ti.n_valid = min(BN, p.N - nt * BN);
+    ti.d_off = 0;
+    return ti.m_valid > 0;
+  }
   if (MODE == MODE_GROUPED) {
     const int mt = t % p.m_tiles;
     const int q = t / p.m_tiles;
@@ -335,12 +366,13 @@ __global__ void __launch_bounds__(192, 1)
   // first stages of A before the previous kernel has finished; everything else
   // (B activations, outputs, device-side tile counts) waits for it.
   // (the all-gather operand's warp-wide flag wait needs the whole producer warp past the PDL wait)
-  const bool prefetch_a = (MODE != MODE_GROUPED) && p.a_evict_first && !p.tp_ag_flags;
+  const bool prefetch_a = (MODE != MODE_GROUPED && MODE != MODE_GROUPED_TM) && p.a_evict_first && !p.tp_ag_flags;
   const bool is_producer = (warp == 0 && lane == 0);
-  if (MODE == MODE_GROUPED) griddep_wait();  // the tile count lives in device memory
+  if (MODE == MODE_GROUPED || MODE == MODE_GROUPED_TM) griddep_wait();  // the tile count lives in device memory
   if (threadIdx.x == 0) {
     int nt = p.num_tiles;
     if (MODE == MODE_GROUPED) nt = p.m_tiles * __ldg(p.grp_tiles + p.num_groups);
+    if (MODE == MODE_GROUPED_TM) nt = p.n_tiles * __ldg(p.grp_tiles + p.num_groups);
     *s_ntiles = nt;
   }
   __syncthreads();
@@ -456,7 +488,27 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t tph = (tc >> 1) & 1;
         if (!mbar_wait(&tfull[buf], tph, s_err, p.err, kErrWaitTimeoutEpilogue)) break;
         tc_fence_after();
-        if (MODE == MODE_GROUPED && p.swiglu) {
+        if (MODE == MODE_GROUPED_TM && p.swiglu) {
+          // this thread's token row: columns [128 h, 128 h + 64) gate, the next 64 up.
+          // tcgen05.ld is warp-collective, so every lane loads; only valid rows store.
+          __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(p.D) +
+                                (long long)(ti.m_base + min(m, ti.m_valid - 1)) * p.ldd + ti.n_base;
+          for (int half = 0; half < BN / 128; ++half) {
+            if (half * 128 >= ti.n_valid) break;
+#pragma unroll 1
+            for (int c0 = 0; c0 < 64; c0 += 16) {
+              float g[16], u[16];
+              tmem_ld16(lane_addr + buf * BN + half * 128 + c0, g);
+              tmem_ld16(lane_addr + buf * BN + half * 128 + 64 + c0, u);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) g[j] = g[j] / (1.f + __expf(-g[j])) * u[j];
+              if (m < ti.m_valid) {
+                st_bf16x8(drow + half * 64 + c0, g);
+                st_bf16x8(drow + half * 64 + c0 + 8, g + 8);
+              }
+            }
+          }
+        } else if (MODE == MODE_GROUPED && p.swiglu) {
           // rows [0, 64) of the tile are gate features, rows [64, 128) the matching
           // up features: exchange through shared memory, write silu(g) * u.
           __nv_bfloat16* D = reinterpret_cast<__nv_bfloat16*>(p.D);
@@ -644,7 +696,7 @@ static void launch_gemm(const GemmLaunch& g, GemmKParams& p) {
     cfg.attrs = attrs;
     cfg.numAttrs = 0;
   } else {
-    int grid = MODE == MODE_GROUPED ? g.num_sms : std::min(p.num_tiles, g.num_sms);
+    int grid = (MODE == MODE_GROUPED || MODE == MODE_GROUPED_TM) ? g.num_sms : std::min(p.num_tiles, g.num_sms);
     if (grid < 1) grid = 1;
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.attrs = attrs;
@@ -704,7 +756,7 @@ int gemm_bf16(const GemmLaunch& g) {
   p.err = g.err;
   p.a_evict_first = g.a_evict_first;
   p.swiglu = g.swiglu;
-  if (g.swiglu && (!g.grouped || !g.trans_out || g.out_f32 || g.M % 128 != 0))
+  if (g.swiglu && g.grouped != 2 && (!g.grouped || !g.trans_out || g.out_f32 || g.M % 128 != 0))
     throw std::runtime_error("gemm: fused SwiGLU needs a grouped, transposed bf16 GEMM with M % 128 == 0");
   p.m_tiles = (g.M + BM - 1) / BM;
   if (g.tp) {
@@ -731,6 +783,21 @@ int gemm_bf16(const GemmLaunch& g) {
     for (int r = 0; r < 8; ++r) p.ep.base[r] = e.base[r];
     p.ep.comb_off = e.comb_off; p.ep.cap = e.cap; p.ep.kk = e.kk; p.ep.H = e.H;
     p.ep.layers_per_step = e.layers_per_step; p.ep.comb_dst = e.comb_dst; p.ep.epoch = e.epoch; p.ep.layer = e.layer;
+  }
+  if (g.grouped == 2) {  // token-major: tokens as A (M), weights as B (N), row-major output
+    const int bn = g.block_n > 0 ? g.block_n : 256;
+    if (g.trans_out || g.out_f32 || g.tp || g.ep || (bn != 128 && bn != 256))
+      throw std::runtime_error("gemm: the token-major grouped GEMM writes bf16 rows with BLOCK_N 128 or 256");
+    if (g.swiglu && (g.N % bn != 0 || g.ldd % 8 != 0 || (reinterpret_cast<uintptr_t>(g.D) & 15)))
+      throw std::runtime_error("gemm: token-major SwiGLU needs N % BLOCK_N == 0 and 16-byte output rows");
+    p.n_tiles = (g.N + bn - 1) / bn;
+    p.num_tiles = 0;
+    p.grp_rows = g.grp_rows;
+    p.grp_tiles = g.grp_tiles;
+    p.num_groups = g.num_groups;
+    if (bn == 256) launch_gemm<256, MODE_GROUPED_TM>(g, p);
+    else launch_gemm<128, MODE_GROUPED_TM>(g, p);
+    return 1;
   }
   if (g.grouped) {
     const int bn = g.block_n > 0 ? g.block_n : 32;

@@ -150,6 +150,38 @@ int64_t gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, 
   return sp::gemm_bf16(g);
 }
 
+// Token-major grouped expert GEMM for prefill-size groups: out[r] = W[g(r)] x[r] for
+// rows sorted by group (grp_tiles counts 128-row token tiles), W as [groups x n, K];
+// with swiglu (W interleaved [64 gate | 64 up] per 128 rows) out[r] = silu(gate) * up.
+int64_t grouped_gemm_tm(const Tensor& x, const Tensor& w, const Tensor& out, const Tensor& grp_rows,
+                        const Tensor& grp_tiles, int64_t num_groups, int64_t n, int64_t block_n, int64_t swiglu) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_BF16(out); CHECK_I32(grp_rows); CHECK_I32(grp_tiles);
+  CHECK_ON(x, w); CHECK_ON(x, out); CHECK_ON(x, grp_rows); CHECK_ON(x, grp_tiles);
+  CHECK_CONTIG(x); CHECK_CONTIG(w); CHECK_CONTIG(out);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "grouped_gemm_tm: 2-D operands");
+  const int64_t K = x.size(1);
+  TORCH_CHECK(w.size(1) == K && w.size(0) == num_groups * n, "grouped_gemm_tm: W is [groups x n, K]");
+  TORCH_CHECK(out.size(0) >= x.size(0) && out.size(1) >= (swiglu ? n / 2 : n), "grouped_gemm_tm: output too small");
+  TORCH_CHECK(grp_rows.numel() > num_groups && grp_tiles.numel() > num_groups, "grouped_gemm_tm: group tables");
+  const c10::cuda::CUDAGuard guard(x.device());
+  sp::GemmLaunch g;
+  g.A = x.data_ptr(); g.a_rows = x.size(0); g.a_cols = K; g.lda = x.stride(0);
+  g.B = w.data_ptr(); g.b_rows = w.size(0); g.b_cols = K; g.ldb = w.stride(0);
+  g.D = out.data_ptr(); g.ldd = out.stride(0);
+  g.M = (int)x.size(0); g.N = (int)n; g.K = (int)K;
+  g.b_batch_rows = (int)n;
+  g.grouped = 2;
+  g.grp_rows = grp_rows.data_ptr<int>();
+  g.grp_tiles = grp_tiles.data_ptr<int>();
+  g.num_groups = (int)num_groups;
+  g.block_n = (int)block_n;
+  g.swiglu = (int)swiglu;
+  g.err = err_word();
+  g.num_sms = num_sms();
+  g.stream = stream();
+  return sp::gemm_bf16(g);
+}
+
 // ---- tensor parallelism (tp.cu, gemm_tcgen05.cu)
 constexpr int kTpArgsWords = 8 + 3 + 5;
 
@@ -1014,6 +1046,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("spec_verify", &spec_verify);
   m.def("decode_advance", &decode_advance);
   m.def("spec_finish", &spec_finish);
+  m.def("grouped_gemm_tm", &grouped_gemm_tm);
   m.def("spec_chain_commit", &spec_chain_commit);
   m.def("mtp_tree_commit", &mtp_tree_commit);
   m.def("top2_rows", &top2_rows);

@@ -109,6 +109,10 @@ class KVCache:
 # the V2-Lite shape (64 tokens, 64 x 2048 gate) it measured 7.33 ms per step against
 # 7.28 ms with the split-K gate GEMM feeding the top-k kernel.
 ROUTER_FUSED_MAX_TOKENS = 256 if os.environ.get("SPARKPIPE_FUSED_ROUTER", "0") == "1" else 0
+# Expert groups averaging at least this many rows (prefill chunks) run the token-major
+# grouped GEMM (tokens as M, row-major output, SwiGLU paired in registers);
+# SPARKPIPE_MOE_TOKEN_MAJOR=0 keeps the weight-major (swap-AB) one everywhere.
+MOE_TOKEN_MAJOR_MIN_ROWS = 256 if os.environ.get("SPARKPIPE_MOE_TOKEN_MAJOR", "1") != "0" else 1 << 62
 ROUTER_FUSED_MAX_WEIGHTS = 1 << 20
 
 
@@ -271,6 +275,15 @@ class MLAMoEModel:
             if isinstance(w[p + "e_w13"], ops.Fp8Weight):
                 bn = max(32, min(bn, 128))
             return self.ep.moe(i, xn, ids, wts, w[p + "e_w13"], w[p + "e_w2"], bn, self.fused_swiglu)
+        if (T * kk >= MOE_TOKEN_MAJOR_MIN_ROWS * (E + S) and self.fused_swiglu
+                and not isinstance(w[p + "e_w13"], ops.Fp8Weight)):
+            grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E + S, 128)
+            xs = ops.gather_rows(xn, sorted_tok)
+            act = torch.empty(T * kk, F, dtype=torch.bfloat16, device=self.device)
+            ops.grouped_gemm_tm(w[p + "e_w13"], xs, act, grp_rows, grp_tiles, E + S, swiglu=True)
+            y = torch.empty(T * kk, c.hidden_size, dtype=torch.bfloat16, device=self.device)
+            ops.grouped_gemm_tm(w[p + "e_w2"], act, y, grp_rows, grp_tiles, E + S)
+            return ("combine", y, inv_pos, wts, kk)
         bn = _moe_block_n(T * kk, E + S)
         if isinstance(w[p + "e_w13"], ops.Fp8Weight):
             bn = max(32, min(bn, 128))

@@ -195,6 +195,22 @@ def grouped_gemm(w: torch.Tensor, x_sorted: torch.Tensor, out: torch.Tensor, grp
     return out
 
 
+def grouped_gemm_tm(w: torch.Tensor, x_sorted: torch.Tensor, out: torch.Tensor, grp_rows: torch.Tensor,
+                    grp_tiles: torch.Tensor, num_groups: int, swiglu: bool = False, block_n: int = 0) -> torch.Tensor:
+    """Token-major MoE expert GEMM for prefill-size groups: out[r] = W[g(r)] @ x_sorted[r]
+    with the tokens as the 128-row M tiles and the expert's weight rows as N, written as
+    rows (``grp_tiles`` counts 128-row token tiles: ``moe_align(ids, groups, 128)``).
+    ``w`` [G, N, K] (or [G*N, K]); with ``swiglu`` the weights are interleaved as for
+    ``grouped_gemm`` and out [R, N/2] receives silu(gate) * up."""
+    n = w.shape[1] if w.dim() == 3 else w.shape[0] // num_groups
+    w2 = w.reshape(-1, w.shape[-1])
+    if not block_n:
+        block_n = 256 if n % 256 == 0 or not swiglu else 128
+    _count(kernels().grouped_gemm_tm(x_sorted, w2, out, grp_rows, grp_tiles, int(num_groups), int(n), int(block_n),
+                                     int(swiglu)))
+    return out
+
+
 def interleave_gate_up(w13: torch.Tensor) -> torch.Tensor:
     """[..., 2F, K] stacked [gate; up] -> per 128-row tile [64 gate rows; 64 up rows] (F % 64 == 0)."""
     *lead, two_f, K = w13.shape

@@ -170,6 +170,36 @@ def test_grouped_gemm_fused_swiglu(T, E, k, bn):
     _status_ok()
 
 
+@pytest.mark.parametrize("T,E,k,F,swiglu", [(3000, 66, 8, 1408, True), (3000, 66, 8, 1408, False),
+                                             (700, 18, 5, 192, True), (257, 9, 3, 256, False)])
+def test_grouped_gemm_token_major(T, E, k, F, swiglu):
+    """Prefill-shaped expert GEMM with the tokens as M tiles: against an fp32 loop over
+    the groups (empty and one-row groups included by the routing), SwiGLU paired in
+    registers from the interleaved weights."""
+    ops = _ops()
+    H = 512
+    g = torch.Generator(device=DEV).manual_seed(T + 7 * E + F)
+    x = torch.randn(T, H, device=DEV, generator=g).bfloat16()
+    # skewed routing: a few hot experts, some experts idle
+    logits = torch.randn(T, E, device=DEV, generator=g) + torch.linspace(3, -3, E, device=DEV)
+    ids = logits.topk(k, dim=-1).indices.int()
+    N = 2 * F if swiglu else F
+    w = (torch.randn(E, N, H, device=DEV, generator=g) * 0.05).bfloat16()
+    grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E, 128)
+    xs = ops.gather_rows(x, sorted_tok)
+    out = torch.empty(T * k, F if swiglu else N, device=DEV, dtype=torch.bfloat16)
+    ops.grouped_gemm_tm(ops.interleave_gate_up(w) if swiglu else w, xs, out, grp_rows, grp_tiles, E, swiglu=swiglu)
+    rows = grp_rows.cpu().tolist()
+    ref = torch.empty(T * k, out.shape[1], device=DEV)
+    for e in range(E):
+        r0, r1 = rows[e], rows[e + 1]
+        if r1 > r0:
+            h = xs[r0:r1].float() @ w[e].float().t()
+            ref[r0:r1] = torch.nn.functional.silu(h[:, :F]) * h[:, F:] if swiglu else h
+    _close(out, ref)
+    _status_ok()
+
+
 # ------------------------------------------------------------------ norms / rope
 @pytest.mark.parametrize("rows,H", [(1, 2048), (64, 2048), (300, 7168), (17, 512)])
 def test_add_rmsnorm(rows, H):
