@@ -44,6 +44,123 @@ constexpr int TOPK_MAX_E = 32 * TOPK_MAX_PER_LANE;
 // groups (group score: the group's best expert, or the sum of its best two as in
 // the bias-corrected sigmoid routers), and picks the top k by k rounds of a warp
 // argmax (ties to the lower expert id).
+// Scores one token's router logits (s_logit: E values in shared memory, read by
+// lane e + 32 i), restricts to the best expert groups, picks the top k by k rounds
+// of a warp argmax (ties to the lower expert id) and writes ids / weights (the
+// shared experts follow as E, E + 1, ... with weight 1). One warp; s_scratch holds
+// E floats for the group scores.
+SP_DEVI void route_token_warp(const float* s_logit, float* s_scratch, int t, int lane, const float* __restrict__ bias,
+                              int* __restrict__ ids, float* __restrict__ wts, int E, int k, int n_shared, int scoring,
+                              int renorm, float scaling, int n_group, int topk_group, int group_top2) {
+  float score[TOPK_MAX_PER_LANE], sel[TOPK_MAX_PER_LANE];
+  const int per = (E + 31) / 32;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+    const int e = lane + i * 32;
+    score[i] = (i < per && e < E) ? s_logit[e] : -INFINITY;
+    mx = fmaxf(mx, score[i]);
+  }
+  if (scoring == 0) {
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      score[i] = (score[i] == -INFINITY) ? 0.f : __expf(score[i] - mx);
+      sum += score[i];
+    }
+    sum = warp_sum(sum);
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      const int e = lane + i * 32;
+      score[i] *= inv;
+      sel[i] = (i < per && e < E) ? score[i] : -INFINITY;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      const int e = lane + i * 32;
+      const bool valid = i < per && e < E;
+      score[i] = valid ? 1.f / (1.f + __expf(-score[i])) : 0.f;
+      sel[i] = valid ? score[i] + (bias ? bias[e] : 0.f) : -INFINITY;
+    }
+  }
+  if (n_group > 1 && topk_group < n_group) {
+    // group-limited routing: lane g scores group g from the selection values
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      const int e = lane + i * 32;
+      if (i < per && e < E) s_scratch[e] = sel[i];
+    }
+    __syncwarp();
+    const int gs = E / n_group;
+    float gscore = -INFINITY;
+    if (lane < n_group) {
+      float b1 = -INFINITY, b2 = -INFINITY;
+      for (int e = lane * gs; e < (lane + 1) * gs; ++e) {
+        const float x = s_scratch[e];
+        if (x > b1) { b2 = b1; b1 = x; } else if (x > b2) { b2 = x; }
+      }
+      gscore = group_top2 ? b1 + b2 : b1;
+    }
+    unsigned keep = 0;
+    for (int j = 0; j < topk_group; ++j) {
+      float best = gscore;
+      int bi = lane < n_group ? lane : 0x7fffffff;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+      }
+      keep |= 1u << bi;
+      if (lane == bi) gscore = -INFINITY;
+    }
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      const int e = lane + i * 32;
+      if (i < per && e < E && !((keep >> (e / gs)) & 1u)) sel[i] = -INFINITY;
+    }
+  }
+  float wsum = 0.f;
+  float my_w = 0.f;
+  int my_id = 0;
+  for (int j = 0; j < k; ++j) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      const int e = lane + i * 32;
+      if (sel[i] > best) { best = sel[i]; bi = e; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    float w = 0.f;
+#pragma unroll
+    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
+      if (lane + i * 32 == bi) { w = score[i]; sel[i] = -INFINITY; }
+    }
+    w = warp_sum(w);  // only the owner lane contributed
+    wsum += w;
+    if (lane == j) { my_w = w; my_id = bi; }
+  }
+  const float norm = (renorm && wsum > 0.f) ? 1.f / wsum : 1.f;
+  const int kk = k + n_shared;
+  if (lane < k) {
+    ids[(long long)t * kk + lane] = my_id;
+    wts[(long long)t * kk + lane] = my_w * norm * scaling;
+  } else if (lane < kk) {
+    ids[(long long)t * kk + lane] = E + (lane - k);
+    wts[(long long)t * kk + lane] = 1.f;
+  }
+}
+
 template <int VEC>
 __global__ void __launch_bounds__(TOPK_THREADS)
     moe_topk_kernel(const float* __restrict__ logits, long long slab_stride, int splits,
@@ -144,114 +261,34 @@ __global__ void __launch_bounds__(TOPK_THREADS)
   }
   __syncthreads();
   if (tid >= 32) return;
+  route_token_warp(s_logit, s_part, t, lane, bias, ids, wts, E, k, n_shared, scoring, renorm, scaling, n_group,
+                   topk_group, group_top2);
+}
 
-  float score[TOPK_MAX_PER_LANE], sel[TOPK_MAX_PER_LANE];
-  const int per = (E + 31) / 32;
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
-    const int e = lane + i * 32;
-    score[i] = (i < per && e < E) ? s_logit[e] : -INFINITY;
-    mx = fmaxf(mx, score[i]);
+// Prefill-sized batches: one warp per token (8 tokens per CTA), each warp loading its
+// token's logits straight into its own shared-memory row (E <= 128).
+constexpr int TOPK_WARP_MAX_E = 128;
+__global__ void __launch_bounds__(TOPK_THREADS)
+    moe_topk_warp_kernel(const float* __restrict__ logits, long long slab_stride, int splits,
+                         const float* __restrict__ bias, int* __restrict__ ids, float* __restrict__ wts, int T, int E,
+                         int k, int n_shared, int scoring, int renorm, float scaling, int n_group, int topk_group,
+                         int group_top2) {
+  __shared__ float s_logit[TOPK_THREADS / 32][TOPK_WARP_MAX_E];
+  __shared__ float s_scratch[TOPK_THREADS / 32][TOPK_WARP_MAX_E];
+  griddep_wait();
+  griddep_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (TOPK_THREADS / 32) + warp;
+  if (t >= T) return;
+  const float* row = logits + (long long)t * E;
+  for (int e = lane; e < E; e += 32) {
+    float x = 0.f;
+    for (int s2 = 0; s2 < splits; ++s2) x += __ldcg(row + s2 * slab_stride + e);
+    s_logit[warp][e] = x;
   }
-  if (scoring == 0) {
-    mx = warp_max(mx);
-    float sum = 0.f;
-#pragma unroll
-    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
-      score[i] = (score[i] == -INFINITY) ? 0.f : __expf(score[i] - mx);
-      sum += score[i];
-    }
-    sum = warp_sum(sum);
-    const float inv = 1.f / sum;
-#pragma unroll
-    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
-      const int e = lane + i * 32;
-      score[i] *= inv;
-      sel[i] = (i < per && e < E) ? score[i] : -INFINITY;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
-      const int e = lane + i * 32;
-      const bool valid = i < per && e < E;
-      score[i] = valid ? 1.f / (1.f + __expf(-score[i])) : 0.f;
-      sel[i] = valid ? score[i] + (bias ? bias[e] : 0.f) : -INFINITY;
-    }
-  }
-  if (n_group > 1 && topk_group < n_group) {
-    // group-limited routing: lane g scores group g from the selection values
-    __syncwarp();
-#pragma unroll
-    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
-      const int e = lane + i * 32;
-      if (i < per && e < E) s_part[e] = sel[i];
-    }
-    __syncwarp();
-    const int gs = E / n_group;
-    float gscore = -INFINITY;
-    if (lane < n_group) {
-      float b1 = -INFINITY, b2 = -INFINITY;
-      for (int e = lane * gs; e < (lane + 1) * gs; ++e) {
-        const float x = s_part[e];
-        if (x > b1) { b2 = b1; b1 = x; } else if (x > b2) { b2 = x; }
-      }
-      gscore = group_top2 ? b1 + b2 : b1;
-    }
-    unsigned keep = 0;
-    for (int j = 0; j < topk_group; ++j) {
-      float best = gscore;
-      int bi = lane < n_group ? lane : 0x7fffffff;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-      }
-      keep |= 1u << bi;
-      if (lane == bi) gscore = -INFINITY;
-    }
-#pragma unroll
-    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
-      const int e = lane + i * 32;
-      if (i < per && e < E && !((keep >> (e / gs)) & 1u)) sel[i] = -INFINITY;
-    }
-  }
-  float wsum = 0.f;
-  float my_w = 0.f;
-  int my_id = 0;
-  for (int j = 0; j < k; ++j) {
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
-      const int e = lane + i * 32;
-      if (sel[i] > best) { best = sel[i]; bi = e; }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-    }
-    float w = 0.f;
-#pragma unroll
-    for (int i = 0; i < TOPK_MAX_PER_LANE; ++i) {
-      if (lane + i * 32 == bi) { w = score[i]; sel[i] = -INFINITY; }
-    }
-    w = warp_sum(w);  // only the owner lane contributed
-    wsum += w;
-    if (lane == j) { my_w = w; my_id = bi; }
-  }
-  const float norm = (renorm && wsum > 0.f) ? 1.f / wsum : 1.f;
-  const int kk = k + n_shared;
-  if (lane < k) {
-    ids[(long long)t * kk + lane] = my_id;
-    wts[(long long)t * kk + lane] = my_w * norm * scaling;
-  } else if (lane < kk) {
-    ids[(long long)t * kk + lane] = E + (lane - k);
-    wts[(long long)t * kk + lane] = 1.f;
-  }
+  __syncwarp();
+  route_token_warp(s_logit[warp], s_scratch[warp], t, lane, bias, ids, wts, E, k, n_shared, scoring, renorm, scaling,
+                   n_group, topk_group, group_top2);
 }
 
 void moe_topk(const float* logits, long long slab_stride, int splits, const float* bias, int* topk_ids, float* topk_w,
@@ -275,6 +312,13 @@ void moe_topk(const float* logits, long long slab_stride, int splits, const floa
     launch_k(moe_topk_kernel<1>, dim3(T), dim3(TOPK_THREADS), 0, s, (const float*)nullptr, 0ll, 1, bias, topk_ids,
              topk_w, E, k, n_shared, scoring, renorm, scaling, n_group, topk_group, group_top2, (const bf16*)gate_x,
              ldx, (const bf16*)gate_w, H);
+    return;
+  }
+  if (T >= 512 && E <= TOPK_WARP_MAX_E) {  // many tokens: a warp each instead of a CTA each
+    const int per_cta = TOPK_THREADS / 32;
+    launch_k(moe_topk_warp_kernel, dim3((T + per_cta - 1) / per_cta), dim3(TOPK_THREADS), 0, s, logits, slab_stride,
+             splits, bias, topk_ids, topk_w, T, E, k, n_shared, scoring, renorm, scaling, n_group, topk_group,
+             group_top2);
     return;
   }
   const bool vec4 = E % 4 == 0 && (splits == 1 || slab_stride % 4 == 0) && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;

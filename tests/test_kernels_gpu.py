@@ -375,12 +375,13 @@ def test_prefill_attention(qlens, klens, impl):
 @pytest.mark.parametrize("scoring,renorm,E,k,groups", [(0, False, 64, 6, None), (1, True, 384, 8, None),
                                                         (0, True, 8, 2, None), (1, True, 256, 8, (8, 4, "noaux_tc")),
                                                         (0, False, 160, 6, (8, 3, "group_limited_greedy")),
-                                                        (0, False, 66, 4, None)])
-def test_moe_topk(scoring, renorm, E, k, groups):
+                                                        (0, False, 66, 4, None),
+                                                        (1, True, 128, 8, (8, 4, "noaux_tc"))])
+@pytest.mark.parametrize("T", [77, 2048])  # a CTA per token / a warp per token (E <= 128)
+def test_moe_topk(scoring, renorm, E, k, groups, T):
     ops = _ops()
     from sparkpipe_rs_b200.models import oracle
     from sparkpipe_rs_b200.models.config import MLAMoEConfig
-    T = 77
     g = torch.Generator(device=DEV).manual_seed(E)
     logits = torch.randn(T, E, device=DEV, generator=g)
     bias = torch.randn(E, device=DEV, generator=g) * 0.1 if scoring == 1 else None
