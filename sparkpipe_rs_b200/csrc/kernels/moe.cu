@@ -553,7 +553,19 @@ __global__ void __launch_bounds__(256) combine_add_rmsnorm_kernel(
     const int c = (threadIdx.x + i * 256) * 8;
     if (c < H) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int j = 0; j < k; ++j) {
+      // four rows' loads in flight before their sums (the rows are scattered in y);
+      // the sum keeps the j order, so results do not change with the grouping
+      int j = 0;
+      for (; j + 4 <= k; j += 4) {
+        float yv[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) ld_bf16x8(y + (long long)s_pos[j + u] * ldy + c, yv[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += s_w[j + u] * yv[u][e];
+      }
+      for (; j < k; ++j) {
         float yv[8];
         ld_bf16x8(y + (long long)s_pos[j] * ldy + c, yv);
 #pragma unroll
