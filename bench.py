@@ -238,7 +238,10 @@ def main():
                "h2d_bytes_per_step": stats["h2d_bytes_per_step"], "d2h_bytes_per_step": stats["d2h_bytes_per_step"],
                "ttft_p50_ms": float(vals[2]), "tpot_p50_ms": float(vals[3]),
                "requests": B * world, "prompt_len": P, "output_len": args.output,
-               "api": "LLMEngine.generate"}
+               "api": "LLMEngine.generate",
+               "prefill_steps": stats["prefill_steps"], "prefill_ms_per_step":
+                   1000.0 * stats["prefill_seconds"] / max(1, stats["prefill_steps"]),
+               "prefill_tokens_per_s": stats["prefill_tokens"] / max(1e-9, stats["prefill_seconds"])}
         engine.shutdown()
 
     if rank == 0:
