@@ -206,10 +206,12 @@ class VerifyRound:
             self.paths.copy_(p)
 
     def capture(self):
-        """Warm-up round (sets kernel attributes outside capture), then the graph."""
-        self._round()
+        """Warm-up round (sets kernel attributes outside capture), then the graph. Without
+        a graph there is nothing to prepare, and no round runs: on a lockstep
+        (expert-parallel) rank each target forward is a collective its peers must join."""
         if not self.use_graph:
             return
+        self._round()
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()

@@ -26,6 +26,7 @@ class _CollectiveModel:
 
     def __init__(self, inner, world):
         self.inner = inner
+        self.cfg, self.device = inner.cfg, inner.device
         self.ep = SimpleNamespace(group=dist.group.WORLD, world=world)
         self.forwards = 0
         self.idle = 0
@@ -46,7 +47,7 @@ class _CollectiveModel:
         return torch.zeros(1, dtype=torch.int32)
 
 
-def _worker(rank, world, port, out_q):
+def _worker(rank, world, port, out_q, spec=""):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
@@ -59,8 +60,14 @@ def _worker(rank, world, port, out_q):
         cfg = tiny()
         inner = CpuMLAMoEModel(cfg, seed=0)
         model = _CollectiveModel(inner, world)
-        eng = LLMEngine(cfg, EngineConfig(max_batch=4, block_size=16, max_model_len=128, max_prefill_tokens=48),
-                        model=model, device="cpu")
+        draft = None
+        if spec:  # verify rounds are one collective target forward each; the draft is local
+            from sparkpipe_rs_b200.models.config import mtp_head
+
+            draft = CpuMLAMoEModel(mtp_head(cfg), seed=3)
+        eng = LLMEngine(cfg, EngineConfig(max_batch=4, block_size=16, max_model_len=128, max_prefill_tokens=48,
+                                          speculation=spec, spec_force=bool(spec)),
+                        model=model, device="cpu", draft=draft)
         assert eng.lockstep
         g = torch.Generator().manual_seed(10 + rank)
         results = []
@@ -83,11 +90,15 @@ def _worker(rank, world, port, out_q):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_engines_step_in_lockstep():
+import pytest
+
+
+@pytest.mark.parametrize("spec", ["", "mtp_tree"])
+def test_expert_parallel_engines_step_in_lockstep(spec):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, spec)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
