@@ -68,8 +68,9 @@ constexpr int MLA_LAT = 512;
 constexpr int MLA_CHUNKS = 9;    // 64-element (128-byte) column chunks
 constexpr int MLA_BLK = 64;      // tokens per cache block
 
-template <int HG, int NJ, int TOK>
+template <int HG, int NJ, int TOK, int NST = 2>
 struct MlaCfg {
+  static constexpr int STAGES = NST;  // KV stages in flight
   static constexpr int WARPS = NJ * (HG / 16);
   static constexpr int STAGE_BYTES = MLA_CHUNKS * TOK * 128;
   static constexpr int PER_BLOCK = MLA_BLK / TOK;  // stages per cache block
@@ -80,7 +81,7 @@ struct MlaCfg {
   static constexpr int Q_BYTES = MLA_CHUNKS * HG * 128;
   static constexpr int P_PITCH = TOK + 8;     // bf16 elements per P row (padded)
   static constexpr int OFF_KV = (Q_BYTES + 1023) / 1024 * 1024;
-  static constexpr int OFF_P = OFF_KV + 2 * STAGE_BYTES;
+  static constexpr int OFF_P = OFF_KV + NST * STAGE_BYTES;
   static constexpr int OFF_STAT = OFF_P + HG * P_PITCH * 2;
   static constexpr int OFF_BAR = OFF_STAT + 2 * NJ * HG * 4;
   static constexpr int SMEM = OFF_BAR + 64 + 1024;
@@ -90,13 +91,13 @@ struct MlaCfg {
 // SPLIT: the S = Q K^T product of a warp accumulates even and odd 16-wide K steps
 // into two register sets (two dependency chains of 18 MMAs instead of one of 36),
 // summed before the softmax.
-template <int HG, int NJ, int TOK, bool LAST = false, bool SPLIT = false>
-__global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ, TOK>::MIN_CTAS)
+template <int HG, int NJ, int TOK, bool LAST = false, bool SPLIT = false, int NST = 2>
+__global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK, NST>::WARPS * 32, MlaCfg<HG, NJ, TOK, NST>::MIN_CTAS)
     mla_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       const MlaKParams p) {
   griddep_wait();
   griddep_launch();
-  using C = MlaCfg<HG, NJ, TOK>;
+  using C = MlaCfg<HG, NJ, TOK, NST>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sQ = smem_u32(smem);
@@ -105,7 +106,7 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ
   float* sMax = reinterpret_cast<float*>(smem + C::OFF_STAT);  // [NJ][HG]
   float* sSum = sMax + NJ * HG;                                 // [NJ][HG]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* qbar = full + 2;
+  uint64_t* qbar = full + NST;
   volatile int* s_err = reinterpret_cast<volatile int*>(qbar + 1);
 
   const int hg = blockIdx.x;
@@ -124,8 +125,7 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ
   const int* bt = p.block_table + (long long)b * p.max_blocks;
 
   if (threadIdx.x == 0) {
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
+    for (int i = 0; i < NST; ++i) mbar_init(&full[i], 1);
     mbar_init(qbar, 1);
     *s_err = 0;
     fence_mbarrier_init();
@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ
   __syncthreads();
 
   auto issue_block = [&](int i) {  // thread 0 only; stage i = part (i % PER_BLOCK) of block kb0 + i / PER_BLOCK
-    const int s = i & 1;
+    const int s = i % NST;
     const int pb = bt[kb0 + i / C::PER_BLOCK];
     const int row = pb * MLA_BLK + (i % C::PER_BLOCK) * TOK;
     uint64_t* bar = &full[s];
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ
     prefetch_tmap(&tmKV);
     mbar_arrive_expect_tx(qbar, C::Q_BYTES);
     for (int c = 0; c < MLA_CHUNKS; ++c) tma_load_2d(smem + c * HG * 128, &tmQ, qbar, c * 64, b * p.H + hg * HG);
-    for (; issued < 2 && issued < nb; ++issued) issue_block(issued);
+    for (; issued < NST && issued < nb; ++issued) issue_block(issued);
   }
 
   float o[2 * C::NP][4];
@@ -163,8 +163,8 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ
   bool ok = mbar_wait(qbar, 0, s_err, p.err, kErrWaitTimeoutMma);
   ok = __syncthreads_and(ok);
   for (int i = 0; ok && i < nb; ++i) {
-    const int s = i & 1;
-    bool got = mbar_wait(&full[s], (i >> 1) & 1, s_err, p.err, kErrWaitTimeoutMma);
+    const int s = i % NST;
+    bool got = mbar_wait(&full[s], (i / NST) & 1, s_err, p.err, kErrWaitTimeoutMma);
     if (!__syncthreads_and(got)) { ok = false; break; }
     const uint32_t kvb = sKV + s * C::STAGE_BYTES;
     if constexpr (LAST) {
@@ -293,7 +293,8 @@ __global__ void __launch_bounds__(MlaCfg<HG, NJ, TOK>::WARPS * 32, MlaCfg<HG, NJ
   if (!ok) {
     // Drain loads still in flight before the CTA's shared memory is released.
     if (threadIdx.x == 0) {
-      for (int i2 = max(0, issued - 2); i2 < issued; ++i2) mbar_wait(&full[i2 & 1], (i2 >> 1) & 1, s_err, nullptr, 0);
+      for (int i2 = max(0, issued - NST); i2 < issued; ++i2)
+        mbar_wait(&full[i2 % NST], (i2 / NST) & 1, s_err, nullptr, 0);
     }
     return;
   }
@@ -804,13 +805,14 @@ static void launch_mla_tc(const MlaDecodeLaunch& l) {
   }
 }
 
-template <int HG, int NJ, int TOK, bool SPLIT = false>
+template <int HG, int NJ, int TOK, bool SPLIT = false, int NST = 2>
 static void launch_mla(const MlaDecodeLaunch& l) {
-  using C = MlaCfg<HG, NJ, TOK>;
+  using C = MlaCfg<HG, NJ, TOK, NST>;
   CUtensorMap tq, tkv;
   make_tmap_2d(&tq, l.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (long long)l.B * l.H, MLA_DIM, MLA_DIM, HG, 64);
   make_tmap_2d(&tkv, l.cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, l.num_slots, MLA_DIM, MLA_DIM, TOK, 64);
-  auto kern = l.last_slot ? mla_decode_kernel<HG, NJ, TOK, true, SPLIT> : mla_decode_kernel<HG, NJ, TOK, false, SPLIT>;
+  auto kern = l.last_slot ? mla_decode_kernel<HG, NJ, TOK, true, SPLIT, NST>
+                          : mla_decode_kernel<HG, NJ, TOK, false, SPLIT, NST>;
   set_smem_bytes(kern, C::SMEM);
   MlaKParams p;
   p.block_table = l.block_table;
@@ -878,6 +880,15 @@ int mla_warps16() {
   }();
   return w;
 }
+// KV stages in flight for 32-token stages: SPARKPIPE_MLA_STAGES=4 keeps four 32-token
+// stages (the shared memory of two 64-token ones) in flight instead of two.
+int mla_stages32() {
+  static const int v = [] {
+    const char* e = std::getenv("SPARKPIPE_MLA_STAGES");
+    return (e && std::string(e) == "4") ? 4 : 2;
+  }();
+  return v;
+}
 bool mla_split_acc() {
   static const bool v = [] {
     const char* e = std::getenv("SPARKPIPE_MLA_SPLIT_ACC");
@@ -890,9 +901,14 @@ int mla_ctas_per_sm(int heads, int impl) {
   if (impl == MLA_IMPL_AUTO) impl = mla_default_impl();
   if (impl == MLA_IMPL_TC) return 1;
   const int tok = mla_stage_tokens();
-  if (heads % 32 == 0) return tok == 64 ? MlaCfg<32, 4, 64>::MIN_CTAS : MlaCfg<32, 4, 32>::MIN_CTAS;
+  const bool deep = mla_stages32() == 4;
+  if (heads % 32 == 0) {
+    if (tok == 64) return MlaCfg<32, 4, 64>::MIN_CTAS;
+    return deep ? MlaCfg<32, 4, 32, 4>::MIN_CTAS : MlaCfg<32, 4, 32>::MIN_CTAS;
+  }
   if (tok == 64 && mla_warps16() == 8) return MlaCfg<16, 8, 64>::MIN_CTAS;
-  return tok == 64 ? MlaCfg<16, 4, 64>::MIN_CTAS : MlaCfg<16, 4, 32>::MIN_CTAS;
+  if (tok == 64) return MlaCfg<16, 4, 64>::MIN_CTAS;
+  return deep ? MlaCfg<16, 4, 32, 4>::MIN_CTAS : MlaCfg<16, 4, 32>::MIN_CTAS;
 }
 
 void mla_decode(const MlaDecodeLaunch& l) {
@@ -912,6 +928,8 @@ void mla_decode(const MlaDecodeLaunch& l) {
     if (mla_stage_tokens() == 64) {
       if (mla_split_acc()) launch_mla<32, 4, 64, true>(l);
       else launch_mla<32, 4, 64>(l);
+    } else if (mla_stages32() == 4) {
+      launch_mla<32, 4, 32, true, 4>(l);
     } else {
       launch_mla<32, 4, 32>(l);
     }
@@ -924,6 +942,8 @@ void mla_decode(const MlaDecodeLaunch& l) {
       if (sp) launch_mla<16, 4, 64, true>(l);
       else launch_mla<16, 4, 64>(l);
     }
+  } else if (mla_stages32() == 4) {
+    launch_mla<16, 4, 32, true, 4>(l);
   } else {
     launch_mla<16, 4, 32>(l);
   }
