@@ -665,6 +665,11 @@ static PFN_encodeTiled get_encode_fn() {
 // (box_cols x box_rows), 128-byte swizzle, zero fill outside the tensor.
 void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, long long rows,
                   long long cols, long long ld, int box_rows, int box_cols) {
+  make_tmap_2d_swizzle(map, ptr, dt, elem_bytes, rows, cols, ld, box_rows, box_cols, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+void make_tmap_2d_swizzle(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, long long rows,
+                          long long cols, long long ld, int box_rows, int box_cols, CUtensorMapSwizzle swizzle) {
   if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) throw std::runtime_error("tensor map base not 16B aligned");
   if ((ld * elem_bytes) % 16 != 0) throw std::runtime_error("tensor map row pitch not a multiple of 16 bytes");
   cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -672,8 +677,8 @@ void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estride[2] = {1, 1};
   CUresult r = get_encode_fn()(map, dt, 2, const_cast<void*>(ptr), gdim, gstride, box, estride,
-                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
 }
 

@@ -71,6 +71,8 @@ struct GemmLaunch {
 int gemm_bf16(const GemmLaunch& g);
 void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, long long rows,
                   long long cols, long long ld, int box_rows, int box_cols);
+void make_tmap_2d_swizzle(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, long long rows,
+                          long long cols, long long ld, int box_rows, int box_cols, CUtensorMapSwizzle swizzle);
 // out[r, c] = sum_s ws[s][r][c] for `splits` dense fp32 slabs [rows, cols] `stride` apart (cols % 4 == 0).
 void split_reduce(const float* ws, long long stride, int splits, int rows, int cols, void* out, long long ldo,
                   int out_f32, cudaStream_t s);
@@ -145,14 +147,16 @@ void slab_add_rmsnorm(const float* slab, long long stride, int splits, void* res
 // q_lat[t, h, kv_lora:] <- rope(q_pe).
 void mla_decode_prep(const float* slab, long long stride, int splits, const void* src, long long lds,
                      const void* norm_w, const int* positions, const float* cos_sin, const int* slot_mapping,
-                     void* cache, void* q_nope_out, void* q_lat, int T, int H, int dn, int dr, int kv_lora,
-                     int q_off, int kv_off, int row_len, float eps, cudaStream_t s);
+                     void* cache, float* kv_scales, void* q_nope_out, void* q_lat, int T, int H, int dn, int dr,
+                     int kv_lora, int q_off, int kv_off, int row_len, float eps, cudaStream_t s);
 // kv: [T, kv_lora + rope] rows (pitch ldkv). Writes norm(latent)|rope(k_pe) into
 // cache rows slot_mapping[t] (pitch kv_lora+rope) and, if latent_out != null,
 // the same row into latent_out (pitch ldl).
 void mla_kv_write(const void* kv, long long ldkv, const void* norm_w, const int* positions, const float* cos_sin,
-                  const int* slot_mapping, void* cache, void* latent_out, long long ldl, int T, int kv_lora, int rope,
-                  float eps, cudaStream_t s);
+                  const int* slot_mapping, void* cache, float* kv_scales, void* latent_out, long long ldl, int T,
+                  int kv_lora, int rope, float eps, cudaStream_t s);
+// With kv_scales set, `cache` is the fp8 cache [slots, 576] e4m3 and kv_scales its [slots, 5]
+// fp32 block scales (amax / 448 per 128 elements; block 4 = the rope dims).
 // In-place-capable RoPE on q: src[t, h, rope_off : rope_off+rope] -> dst[t, h, dst_off : dst_off+rope]
 void rope_q(const void* src, long long src_tok, long long src_head, int src_off, void* dst, long long dst_tok,
             long long dst_head, int dst_off, const int* positions, const float* cos_sin, int T, int H, int rope,
@@ -180,6 +184,7 @@ struct MlaDecodeLaunch {
   int* counters = nullptr;        // stream-K kernel: per-row arrival counters, zero between launches
   int early = 0;                  // stream-K kernel: earlier-position KV may load before the PDL wait
   const int* last_slot = nullptr; // mma.sync kernel: [B] cache row of each row's last context token (-1: its block)
+  const float* kv_scales = nullptr;  // fp8 cache: [num_slots, 5] block scales (cache is [num_slots, 576] e4m3)
   cudaStream_t stream = 0;
 };
 enum { MLA_IMPL_AUTO = 0, MLA_IMPL_TC = 1, MLA_IMPL_MMA = 2 };
@@ -188,6 +193,13 @@ enum { MLA_IMPL_AUTO = 0, MLA_IMPL_TC = 1, MLA_IMPL_MMA = 2 };
 int mla_stage_tokens();
 int mla_ctas_per_sm(int heads, int impl = MLA_IMPL_AUTO);
 void mla_decode(const MlaDecodeLaunch& l);
+// fp8 (e4m3) cache with per-128 block scales (mla_decode_fp8.cu); same scratch and combine.
+void mla_decode_fp8(const MlaDecodeLaunch& l);
+int mla_fp8_ctas_per_sm(int heads);
+// Split-KV merge of [B, splits, H, 512] partials and their log-sum-exps into out [B, H, 512] bf16.
+void mla_combine(const float* o_part, const float* lse_part, void* out, int B, int H, int splits, cudaStream_t s);
+// out[r, :] = dequantised fp8 cache row idx[r] (bf16 [n, 576]).
+void kv8_gather(const void* cache8, const float* scales, const int* idx, void* out, int n, cudaStream_t s);
 // Stream-K decode kernel (mla_decode_sk.cu): one CTA per SM over the flattened KV units.
 // Scratch: o_part [segments][heads per CTA][512] fp32, lse_part [segments][heads per CTA],
 // counters [(H / heads per CTA) * B] int32 zeroed once (the kernel leaves them zero).
@@ -221,6 +233,7 @@ inline void push_kernel_attr(std::vector<KernelAttr>& out, const std::string& na
 void kernel_attrs_gemm(std::vector<KernelAttr>& out);
 void kernel_attrs_fp8(std::vector<KernelAttr>& out);
 void kernel_attrs_mla(std::vector<KernelAttr>& out);
+void kernel_attrs_mla8(std::vector<KernelAttr>& out);
 void kernel_attrs_mla_sk(std::vector<KernelAttr>& out);
 void kernel_attrs_prefill(std::vector<KernelAttr>& out);
 void kernel_attrs_moe(std::vector<KernelAttr>& out);
@@ -297,7 +310,7 @@ void spec_chain_commit(const int* tok, const int* tgt, const int* ctx, const int
                        int* committed, int* counts, cudaStream_t s);
 void mtp_tree_commit(const int* tok, const int* tgt, const int* ctx, const int* slots, int B, void* cache,
                      long long layer_stride, int layers, int row_elems, int* committed, int* counts, int* paths,
-                     cudaStream_t s);
+                     cudaStream_t s, float* aux = nullptr, long long aux_layer_stride = 0, int aux_row = 0);
 void top2_rows(const void* logits, long long ldl, int T, int V, int* out0, int* out1, cudaStream_t s);
 void spec_finish(int* tok_rows, const int* tgt_rows, int B, int L, float p_accept, unsigned long long seed,
                  int* pos_rows, int* ctx_rows, int* slot_rows, const int* block_table, int max_blocks,

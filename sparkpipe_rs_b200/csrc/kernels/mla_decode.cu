@@ -367,6 +367,10 @@ __global__ void mla_combine_kernel(const float* __restrict__ o_part, const float
   *reinterpret_cast<uint32_t*>(orow + 2) = pack_bf16(acc[2] * inv, acc[3] * inv);
 }
 
+void mla_combine(const float* o_part, const float* lse_part, void* out, int B, int H, int splits, cudaStream_t s) {
+  launch_k(mla_combine_kernel, dim3(B * H), dim3(MLA_LAT / 4), 0, s, o_part, lse_part, (bf16*)out, H, splits);
+}
+
 // ============================================================================
 // tcgen05 version. One CTA per (head group of HG heads, sequence, KV split), as
 // above, but the two products run on the 5th-generation tensor cores with the
@@ -880,15 +884,23 @@ int mla_warps16() {
   }();
   return w;
 }
-// KV stages in flight for 32-token stages: SPARKPIPE_MLA_STAGES=4 keeps four 32-token
-// stages (the shared memory of two 64-token ones) in flight instead of two.
-int mla_stages32() {
+// KV stages in flight (SPARKPIPE_MLA_STAGES): 2 by default. With 32-token stages, 4
+// keeps four in flight (the shared memory of two 64-token ones): measured slower, 33.1
+// vs 25.2 us (B=64, 16 heads, ctx 1024, best split each), so the stage pipeline is not
+// starved by load latency. With 64-token stages and 16 heads, 1 leaves each CTA one
+// stage buffer and fits two CTAs per SM, each SM sub-partition then running two warps
+// whose loads and math interleave.
+int mla_stages() {
   static const int v = [] {
     const char* e = std::getenv("SPARKPIPE_MLA_STAGES");
-    return (e && std::string(e) == "4") ? 4 : 2;
+    if (e && std::string(e) == "4") return 4;
+    if (e && std::string(e) == "1") return 1;
+    return 2;
   }();
   return v;
 }
+int mla_stages32() { return mla_stages() == 4 ? 4 : 2; }
+bool mla_single_stage16() { return mla_stages() == 1; }
 bool mla_split_acc() {
   static const bool v = [] {
     const char* e = std::getenv("SPARKPIPE_MLA_SPLIT_ACC");
@@ -907,6 +919,7 @@ int mla_ctas_per_sm(int heads, int impl) {
     return deep ? MlaCfg<32, 4, 32, 4>::MIN_CTAS : MlaCfg<32, 4, 32>::MIN_CTAS;
   }
   if (tok == 64 && mla_warps16() == 8) return MlaCfg<16, 8, 64>::MIN_CTAS;
+  if (tok == 64 && mla_single_stage16()) return MlaCfg<16, 4, 64, 1>::MIN_CTAS;
   if (tok == 64) return MlaCfg<16, 4, 64>::MIN_CTAS;
   return deep ? MlaCfg<16, 4, 32, 4>::MIN_CTAS : MlaCfg<16, 4, 32>::MIN_CTAS;
 }
@@ -938,6 +951,8 @@ void mla_decode(const MlaDecodeLaunch& l) {
     if (mla_warps16() == 8) {
       if (sp) launch_mla<16, 8, 64, true>(l);
       else launch_mla<16, 8, 64>(l);
+    } else if (mla_single_stage16()) {
+      launch_mla<16, 4, 64, true, 1>(l);
     } else {
       if (sp) launch_mla<16, 4, 64, true>(l);
       else launch_mla<16, 4, 64>(l);

@@ -196,10 +196,24 @@ SP_DEVI void rope_store4(const float4& x, const float* cp, int half, int i0, bf1
   reinterpret_cast<__nv_bfloat162*>(dst)[1] = b;
 }
 
+SP_DEVI float4 rope4(const float4& x, const float* cp, int half, int i0) {
+  const float c0 = cp[i0], s0 = cp[half + i0], c1 = cp[i0 + 1], s1 = cp[half + i0 + 1];
+  return make_float4(x.x * c0 - x.y * s0, x.x * s0 + x.y * c0, x.z * c1 - x.w * s1, x.z * s1 + x.w * c1);
+}
+
+// fp8 KV rows: e4m3 values and one fp32 scale (amax / 448) per 128-element block.
+SP_DEVI uint32_t quant4_e4m3(float a, float b, float c, float d, float inv) {
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a * inv, b * inv), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c * inv, d * inv), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
+}
+SP_DEVI float kv8_inv(float amax) { return amax > 0.f ? 448.f / amax : 0.f; }
+
 __global__ void __launch_bounds__(128) mla_decode_prep_kernel(
     PrepSrc src, const bf16* __restrict__ nw, const int* __restrict__ pos, const float* __restrict__ cs,
-    const int* __restrict__ slots, bf16* __restrict__ cache, bf16* __restrict__ q_nope_out,
-    bf16* __restrict__ q_lat, int H, int dn, int dr, int L, int qoff, int kvoff, float eps) {
+    const int* __restrict__ slots, bf16* __restrict__ cache, uint8_t* __restrict__ cache8,
+    float* __restrict__ scales8, bf16* __restrict__ q_nope_out, bf16* __restrict__ q_lat, int H, int dn, int dr,
+    int L, int qoff, int kvoff, float eps) {
   griddep_wait();
   griddep_launch();
   const int t = blockIdx.x;
@@ -225,6 +239,23 @@ __global__ void __launch_bounds__(128) mla_decode_prep_kernel(
     const float inv = rsqrtf((part[0] + part[1] + part[2] + part[3]) / L + eps);
     const int slot = slots[t];
     if (slot < 0) return;
+    if (cache8) {  // fp8 row (L == 512, dr == 64): warp w holds latent block w, warp 0 also the rope block
+      const int c = tid * 4;
+      const float4 x = make_float4(v[0].x * inv * __bfloat162float(nw[c]), v[0].y * inv * __bfloat162float(nw[c + 1]),
+                                   v[0].z * inv * __bfloat162float(nw[c + 2]), v[0].w * inv * __bfloat162float(nw[c + 3]));
+      const float am = warp_max(fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+      uint8_t* row8 = cache8 + (long long)slot * W;
+      *reinterpret_cast<uint32_t*>(row8 + c) = quant4_e4m3(x.x, x.y, x.z, x.w, kv8_inv(am));
+      if ((tid & 31) == 0) scales8[(long long)slot * 5 + (tid >> 5)] = am / 448.f;
+      if (tid < 32) {
+        const float4 r = tid < dr / 4 ? rope4(prep_load4(src, t, kvoff + L + tid * 4), cp, dr / 2, tid * 2)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float ar = warp_max(fmaxf(fmaxf(fabsf(r.x), fabsf(r.y)), fmaxf(fabsf(r.z), fabsf(r.w))));
+        if (tid < dr / 4) *reinterpret_cast<uint32_t*>(row8 + L + tid * 4) = quant4_e4m3(r.x, r.y, r.z, r.w, kv8_inv(ar));
+        if (tid == 0) scales8[(long long)slot * 5 + 4] = ar / 448.f;
+      }
+      return;
+    }
     bf16* crow = cache + (long long)slot * W;
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -261,9 +292,11 @@ __global__ void __launch_bounds__(128) mla_decode_prep_kernel(
 
 void mla_decode_prep(const float* slab, long long stride, int splits, const void* src, long long lds,
                      const void* norm_w, const int* positions, const float* cos_sin, const int* slot_mapping,
-                     void* cache, void* q_nope_out, void* q_lat, int T, int H, int dn, int dr, int kv_lora,
-                     int q_off, int kv_off, int row_len, float eps, cudaStream_t s) {
+                     void* cache, float* kv_scales, void* q_nope_out, void* q_lat, int T, int H, int dn, int dr,
+                     int kv_lora, int q_off, int kv_off, int row_len, float eps, cudaStream_t s) {
   if (T <= 0) return;
+  if (kv_scales && (kv_lora != 512 || dr != 64))
+    throw std::runtime_error("mla_decode_prep: the fp8 cache needs kv_lora 512 and rope 64");
   if (kv_lora % 4 || kv_lora > 1024 || dn % 4 || dr % 4 || dr > 512 || q_off % 4 || kv_off % 4 || row_len % 4)
     throw std::runtime_error("mla_decode_prep: 4-aligned dims, kv_lora <= 1024 required");
   if (!slab && (lds % 4 || (reinterpret_cast<uintptr_t>(src) & 7)))
@@ -272,13 +305,14 @@ void mla_decode_prep(const float* slab, long long stride, int splits, const void
     throw std::runtime_error("mla_decode_prep: without a q_nope output the nope width must equal kv_lora");
   PrepSrc ps{slab, stride, splits < 1 ? 1 : splits, (const bf16*)src, lds, row_len};
   launch_k(mla_decode_prep_kernel, dim3(T, 1 + (H + 3) / 4), dim3(128), 0, s, ps, (const bf16*)norm_w, positions,
-           cos_sin, slot_mapping, (bf16*)cache, (bf16*)q_nope_out, (bf16*)q_lat, H, dn, dr, kv_lora, q_off, kv_off,
-           eps);
+           cos_sin, slot_mapping, kv_scales ? nullptr : (bf16*)cache, kv_scales ? (uint8_t*)cache : nullptr,
+           kv_scales, (bf16*)q_nope_out, (bf16*)q_lat, H, dn, dr, kv_lora, q_off, kv_off, eps);
 }
 
 __global__ void mla_kv_write_kernel(const bf16* __restrict__ kv, long long ldkv, const bf16* __restrict__ nw,
                                     const int* __restrict__ pos, const float* __restrict__ cs,
-                                    const int* __restrict__ slots, bf16* __restrict__ cache, bf16* __restrict__ lat,
+                                    const int* __restrict__ slots, bf16* __restrict__ cache,
+                                    uint8_t* __restrict__ cache8, float* __restrict__ scales8, bf16* __restrict__ lat,
                                     long long ldl, int T, int L, int R, float eps) {
   griddep_wait();
   griddep_launch();
@@ -304,7 +338,8 @@ __global__ void mla_kv_write_kernel(const bf16* __restrict__ kv, long long ldkv,
   const float inv = rsqrtf(ss / L + eps);
   const int slot = slots ? slots[t] : -1;
   const int W = L + R;
-  bf16* crow = slot >= 0 ? cache + (long long)slot * W : nullptr;
+  bf16* crow = (slot >= 0 && cache) ? cache + (long long)slot * W : nullptr;
+  uint8_t* row8 = (slot >= 0 && cache8) ? cache8 + (long long)slot * W : nullptr;
   bf16* lrow = lat ? lat + (long long)t * ldl : nullptr;
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
@@ -316,6 +351,17 @@ __global__ void mla_kv_write_kernel(const bf16* __restrict__ kv, long long ldkv,
       for (int j = 0; j < 8; ++j) v[i][j] = v[i][j] * inv * g[j];
       if (crow) st_bf16x8(crow + c, v[i]);
       if (lrow) st_bf16x8(lrow + c, v[i]);
+      if (row8) {  // 16 lanes hold one 128-element block
+        float am = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(v[i][j]));
+#pragma unroll
+        for (int d = 8; d >= 1; d >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, d));
+        const float iv = kv8_inv(am);
+        *reinterpret_cast<uint2*>(row8 + c) = make_uint2(quant4_e4m3(v[i][0], v[i][1], v[i][2], v[i][3], iv),
+                                                         quant4_e4m3(v[i][4], v[i][5], v[i][6], v[i][7], iv));
+        if ((lane & 15) == 0) scales8[(long long)slot * 5 + c / 128] = am / 448.f;
+      }
     }
   }
   const int p = pos[t];
@@ -329,17 +375,29 @@ __global__ void mla_kv_write_kernel(const bf16* __restrict__ kv, long long ldkv,
     if (crow) { crow[L + 2 * i] = y0; crow[L + 2 * i + 1] = y1; }
     if (lrow) { lrow[L + 2 * i] = y0; lrow[L + 2 * i + 1] = y1; }
   }
+  if (row8) {  // rope block (R == 64): lane i holds pair i
+    const float x0 = __bfloat162float(src[L + 2 * lane]), x1 = __bfloat162float(src[L + 2 * lane + 1]);
+    const float c = cp[lane], sn = cp[R / 2 + lane];
+    const float y0 = x0 * c - x1 * sn, y1 = x0 * sn + x1 * c;
+    const float am = warp_max(fmaxf(fabsf(y0), fabsf(y1)));
+    const float iv = kv8_inv(am);
+    *reinterpret_cast<__nv_fp8x2_storage_t*>(row8 + L + 2 * lane) =
+        __nv_cvt_float2_to_fp8x2(make_float2(y0 * iv, y1 * iv), __NV_SATFINITE, __NV_E4M3);
+    if (lane == 0) scales8[(long long)slot * 5 + 4] = am / 448.f;
+  }
 }
 
 void mla_kv_write(const void* kv, long long ldkv, const void* norm_w, const int* positions, const float* cos_sin,
-                  const int* slot_mapping, void* cache, void* latent_out, long long ldl, int T, int kv_lora, int rope,
-                  float eps, cudaStream_t s) {
+                  const int* slot_mapping, void* cache, float* kv_scales, void* latent_out, long long ldl, int T,
+                  int kv_lora, int rope, float eps, cudaStream_t s) {
   if (T <= 0) return;
   if (kv_lora % 256 != 0 || kv_lora > 1024) throw std::runtime_error("mla_kv_write: kv_lora must be 256..1024");
+  if (kv_scales && (kv_lora != 512 || rope != 64))
+    throw std::runtime_error("mla_kv_write: the fp8 cache needs kv_lora 512 and rope 64");
   const int warps = 8;
   launch_k(mla_kv_write_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, s, (const bf16*)kv, ldkv,
-           (const bf16*)norm_w, positions, cos_sin, slot_mapping, (bf16*)cache, (bf16*)latent_out, ldl, T, kv_lora,
-           rope, eps);
+           (const bf16*)norm_w, positions, cos_sin, slot_mapping, kv_scales ? nullptr : (bf16*)cache,
+           kv_scales ? (uint8_t*)cache : nullptr, kv_scales, (bf16*)latent_out, ldl, T, kv_lora, rope, eps);
 }
 
 __global__ void rope_q_kernel(const bf16* src, long long st, long long sh, int so, bf16* dst, long long dt,

@@ -278,10 +278,30 @@ void add_rmsnorm(const Tensor& x, const c10::optional<Tensor>& residual, const T
                   (int)x.size(1), (float)eps, stream());
 }
 
+// The latent KV cache is bf16 [.., slots, 576], or e4m3 [.., slots, 576] (uint8 or float8_e4m3fn)
+// with its fp32 block scales [.., slots, 5]; returns the scales pointer (null for bf16).
+static float* kv8_scales(const Tensor& cache, const c10::optional<Tensor>& scales, const char* who) {
+  const bool fp8 = cache.scalar_type() == at::kByte || cache.scalar_type() == at::kFloat8_e4m3fn;
+  if (!fp8) {
+    TORCH_CHECK(cache.scalar_type() == at::kBFloat16, who, ": cache must be bf16 or fp8 e4m3");
+    TORCH_CHECK(!scales.has_value(), who, ": scales given for a bf16 cache");
+    return nullptr;
+  }
+  TORCH_CHECK(scales.has_value(), who, ": an fp8 cache needs its block scales");
+  TORCH_CHECK(scales->scalar_type() == at::kFloat && scales->is_contiguous() && scales->size(-1) == 5,
+              who, ": scales must be contiguous fp32 [.., slots, 5]");
+  TORCH_CHECK(cache.size(-1) == 576 && cache.is_contiguous(), who, ": fp8 cache rows of 576, contiguous");
+  TORCH_CHECK(scales->numel() / 5 == cache.numel() / 576, who, ": one scale row per cache row");
+  TORCH_CHECK(scales->device() == cache.device(), who, ": scales on another device");
+  return scales->data_ptr<float>();
+}
+
 void mla_kv_write(const Tensor& kv, const Tensor& norm_w, const Tensor& positions, const Tensor& cos_sin,
                   const c10::optional<Tensor>& slot_mapping, const Tensor& cache,
-                  const c10::optional<Tensor>& latent_out, int64_t kv_lora, int64_t rope, double eps) {
+                  const c10::optional<Tensor>& latent_out, int64_t kv_lora, int64_t rope, double eps,
+                  const c10::optional<Tensor>& kv_scales) {
   CHECK_CUDA(kv); CHECK_BF16(kv); CHECK_BF16(norm_w); CHECK_I32(positions); CHECK_F32(cos_sin);
+  float* ks = kv8_scales(cache, kv_scales, "mla_kv_write");
   TORCH_CHECK(kv.stride(1) == 1, "kv rows must be contiguous");
   const c10::cuda::CUDAGuard guard(kv.device());
   const int* slots = nullptr;
@@ -290,7 +310,7 @@ void mla_kv_write(const Tensor& kv, const Tensor& norm_w, const Tensor& position
   long long ldl = 0;
   if (latent_out.has_value()) { CHECK_BF16(*latent_out); lat = latent_out->data_ptr(); ldl = latent_out->stride(0); }
   sp::mla_kv_write(kv.data_ptr(), kv.stride(0), norm_w.data_ptr(), positions.data_ptr<int>(),
-                   cos_sin.data_ptr<float>(), slots, cache.data_ptr(), lat, ldl, (int)kv.size(0), (int)kv_lora,
+                   cos_sin.data_ptr<float>(), slots, cache.data_ptr(), ks, lat, ldl, (int)kv.size(0), (int)kv_lora,
                    (int)rope, (float)eps, stream());
 }
 
@@ -416,8 +436,9 @@ void quant_weight_fp8(const c10::optional<Tensor>& src, int64_t seed, int64_t fl
 void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table, const Tensor& context_lens,
                 const Tensor& out, const c10::optional<Tensor>& o_part, const c10::optional<Tensor>& lse_part,
                 int64_t splits, double scale, int64_t impl, const c10::optional<Tensor>& trace,
-                const c10::optional<Tensor>& last_slot) {
-  CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(cache); CHECK_I32(block_table); CHECK_I32(context_lens); CHECK_BF16(out);
+                const c10::optional<Tensor>& last_slot, const c10::optional<Tensor>& kv_scales) {
+  CHECK_CUDA(q); CHECK_BF16(q); CHECK_I32(block_table); CHECK_I32(context_lens); CHECK_BF16(out);
+  const float* ks = kv8_scales(cache, kv_scales, "mla_decode");
   CHECK_ON(q, cache); CHECK_ON(q, block_table); CHECK_ON(q, context_lens); CHECK_ON(q, out);
   CHECK_CONTIG(q); CHECK_CONTIG(block_table); CHECK_CONTIG(out);
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 576, "q: [B, H, 576]");
@@ -461,7 +482,23 @@ void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table,
   l.scale = (float)scale;
   l.err = err_word();
   l.stream = stream();
-  sp::mla_decode(l);
+  if (ks) {
+    TORCH_CHECK(!trace.has_value(), "mla_decode: no trace for the fp8 cache kernel");
+    l.kv_scales = ks;
+    sp::mla_decode_fp8(l);
+  } else {
+    sp::mla_decode(l);
+  }
+}
+
+void kv8_gather(const Tensor& cache8, const Tensor& scales, const Tensor& idx, const Tensor& out) {
+  CHECK_CUDA(cache8); CHECK_I32(idx); CHECK_BF16(out); CHECK_CONTIG(idx); CHECK_CONTIG(out);
+  CHECK_ON(cache8, idx); CHECK_ON(cache8, out);
+  const float* ks = kv8_scales(cache8, scales, "kv8_gather");
+  TORCH_CHECK(ks, "kv8_gather: the cache must be fp8");
+  TORCH_CHECK(out.dim() == 2 && out.size(1) == 576 && out.size(0) >= idx.numel(), "kv8_gather: out [n, 576]");
+  const c10::cuda::CUDAGuard guard(cache8.device());
+  sp::kv8_gather(cache8.data_ptr(), ks, idx.data_ptr<int>(), out.data_ptr(), (int)idx.numel(), stream());
 }
 
 // Stream-K MLA decode (mla_decode_sk.cu); scratch sizes from mla_sk_segments / mla_sk_heads_per_cta.
@@ -585,8 +622,10 @@ void mla_decode_prep(const c10::optional<Tensor>& slabs, int64_t stride, int64_t
                      const c10::optional<Tensor>& src, const Tensor& norm_w, const Tensor& positions,
                      const Tensor& cos_sin, const Tensor& slot_mapping, const Tensor& cache,
                      const c10::optional<Tensor>& q_nope_out, const Tensor& q_lat, int64_t T, int64_t dn,
-                     int64_t q_off, int64_t kv_off, int64_t row_len, double eps) {
-  CHECK_I32(positions); CHECK_F32(cos_sin); CHECK_I32(slot_mapping); CHECK_BF16(cache);
+                     int64_t q_off, int64_t kv_off, int64_t row_len, double eps,
+                     const c10::optional<Tensor>& kv_scales) {
+  CHECK_I32(positions); CHECK_F32(cos_sin); CHECK_I32(slot_mapping);
+  float* ks = kv8_scales(cache, kv_scales, "mla_decode_prep");
   CHECK_BF16(q_lat); CHECK_CONTIG(q_lat);
   void* qn = nullptr;
   if (q_nope_out.has_value()) {
@@ -603,7 +642,7 @@ void mla_decode_prep(const c10::optional<Tensor>& slabs, int64_t stride, int64_t
   const int H = (int)q_lat.size(1), W = (int)q_lat.size(2);
   const int kvl = (int)norm_w.size(0);
   sp::mla_decode_prep(sl, stride, (int)splits, sr, lds, norm_w.data_ptr(), positions.data_ptr<int>(),
-                      cos_sin.data_ptr<float>(), slot_mapping.data_ptr<int>(), cache.data_ptr(), qn,
+                      cos_sin.data_ptr<float>(), slot_mapping.data_ptr<int>(), cache.data_ptr(), ks, qn,
                       q_lat.data_ptr(), (int)T, H, (int)dn, W - kvl, kvl, (int)q_off, (int)kv_off, (int)row_len,
                       (float)eps, stream());
 }
@@ -769,8 +808,10 @@ void spec_chain_commit(const Tensor& tok, const Tensor& tgt, const Tensor& ctx, 
 // Verify round of the serving engine: the MTP tree (6 rows per lane) and the KV move
 // of an accepted alternate leaf in `cache` [layers, slots, row].
 void mtp_tree_commit(const Tensor& tok, const Tensor& tgt, const Tensor& ctx, const Tensor& slots,
-                     const Tensor& cache, const Tensor& committed, const Tensor& counts, const Tensor& paths) {
-  CHECK_CUDA(tok); CHECK_I32(tok); CHECK_I32(tgt); CHECK_I32(ctx); CHECK_I32(slots); CHECK_BF16(cache);
+                     const Tensor& cache, const Tensor& committed, const Tensor& counts, const Tensor& paths,
+                     const c10::optional<Tensor>& aux) {
+  CHECK_CUDA(tok); CHECK_I32(tok); CHECK_I32(tgt); CHECK_I32(ctx); CHECK_I32(slots);
+  TORCH_CHECK(cache.element_size() == 2 || cache.element_size() == 1, "mtp_tree_commit: bf16 or fp8 cache");
   CHECK_I32(committed); CHECK_I32(counts); CHECK_I32(paths); CHECK_CONTIG(cache);
   for (const Tensor* t : {&tgt, &ctx, &slots, &cache, &committed, &counts, &paths}) CHECK_ON(tok, *t);
   for (const Tensor* t : {&tok, &tgt, &ctx, &slots, &committed, &counts, &paths}) CHECK_CONTIG(*t);
@@ -780,9 +821,24 @@ void mtp_tree_commit(const Tensor& tok, const Tensor& tgt, const Tensor& ctx, co
                   committed.numel() >= 6 * B && paths.numel() >= B,
               "mtp_tree_commit: row arrays must hold 6 x B entries");
   const c10::cuda::CUDAGuard guard(tok.device());
+  // rows move as 2-byte units (an fp8 row of 576 bytes is 288 of them)
+  const int es = (int)cache.element_size();
+  TORCH_CHECK((cache.size(2) * es) % 2 == 0 && (cache.stride(0) * es) % 2 == 0, "mtp_tree_commit: row bytes");
+  float* ax = nullptr;
+  long long ax_stride = 0;
+  int ax_row = 0;
+  if (aux.has_value()) {
+    CHECK_F32(*aux); CHECK_CONTIG(*aux); CHECK_ON(tok, *aux);
+    TORCH_CHECK(aux->dim() == 3 && aux->size(0) == cache.size(0) && aux->size(1) == cache.size(1),
+                "mtp_tree_commit: aux [layers, slots, k]");
+    ax = aux->data_ptr<float>();
+    ax_stride = aux->stride(0);
+    ax_row = (int)aux->size(2);
+  }
   sp::mtp_tree_commit(tok.data_ptr<int>(), tgt.data_ptr<int>(), ctx.data_ptr<int>(), slots.data_ptr<int>(), (int)B,
-                      cache.data_ptr(), cache.stride(0), (int)cache.size(0), (int)cache.size(2),
-                      committed.data_ptr<int>(), counts.data_ptr<int>(), paths.data_ptr<int>(), stream());
+                      cache.data_ptr(), cache.stride(0) * es / 2, (int)cache.size(0), (int)(cache.size(2) * es / 2),
+                      committed.data_ptr<int>(), counts.data_ptr<int>(), paths.data_ptr<int>(), stream(), ax,
+                      ax_stride, ax_row);
 }
 
 void top2_rows(const Tensor& logits, const Tensor& out0, const Tensor& out1) {
@@ -1029,6 +1085,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_act_fp8", &quant_act_fp8);
   m.def("quant_weight_fp8", &quant_weight_fp8);
   m.def("mla_decode", &mla_decode);
+  m.def("kv8_gather", &kv8_gather);
+  m.def("mla_fp8_ctas_per_sm", [](int64_t heads) { return sp::mla_fp8_ctas_per_sm((int)heads); });
   m.def("mla_decode_sk", &mla_decode_sk);
   m.def("mla_sk_supported", [](int64_t B, int64_t H) { return sp::mla_sk_supported((int)B, (int)H); });
   m.def("mla_sk_heads_per_cta", [](int64_t H) { return sp::mla_sk_heads_per_cta((int)H); });
@@ -1067,6 +1125,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     sp::kernel_attrs_gemm(v);
     sp::kernel_attrs_fp8(v);
     sp::kernel_attrs_mla(v);
+    sp::kernel_attrs_mla8(v);
     sp::kernel_attrs_mla_sk(v);
     sp::kernel_attrs_prefill(v);
     sp::kernel_attrs_moe(v);

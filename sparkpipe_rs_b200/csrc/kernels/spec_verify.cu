@@ -98,7 +98,9 @@ __global__ void __launch_bounds__(128) mtp_tree_commit_kernel(const int* __restr
                                                               const int* __restrict__ slots, int B,
                                                               bf16* __restrict__ cache, long long layer_stride,
                                                               int layers, int row_elems, int* __restrict__ committed,
-                                                              int* __restrict__ counts, int* __restrict__ paths) {
+                                                              int* __restrict__ counts, int* __restrict__ paths,
+                                                              float* __restrict__ aux, long long aux_layer_stride,
+                                                              int aux_row) {
   griddep_wait();
   griddep_launch();
   const int b = blockIdx.x;
@@ -151,15 +153,20 @@ __global__ void __launch_bounds__(128) mtp_tree_commit_kernel(const int* __restr
     uint4* d4 = reinterpret_cast<uint4*>(cache + l * layer_stride + (long long)dst * row_elems) + c;
     *d4 = *s4;
   }
+  // the row's side array (the fp8 cache's block scales), word by word
+  for (int i = threadIdx.x; aux && i < layers * aux_row; i += blockDim.x) {
+    const int l = i / aux_row, c = i - l * aux_row;
+    aux[l * aux_layer_stride + (long long)dst * aux_row + c] = aux[l * aux_layer_stride + (long long)src * aux_row + c];
+  }
 }
 
 void mtp_tree_commit(const int* tok, const int* tgt, const int* ctx, const int* slots, int B, void* cache,
                      long long layer_stride, int layers, int row_elems, int* committed, int* counts, int* paths,
-                     cudaStream_t s) {
+                     cudaStream_t s, float* aux, long long aux_layer_stride, int aux_row) {
   if (B <= 0) return;
   if (row_elems % 8 || layer_stride % 8) throw std::runtime_error("mtp_tree_commit: 16-byte KV rows required");
   launch_k(mtp_tree_commit_kernel, dim3(B), dim3(128), 0, s, tok, tgt, ctx, slots, B, static_cast<bf16*>(cache),
-           layer_stride, layers, row_elems, committed, counts, paths);
+           layer_stride, layers, row_elems, committed, counts, paths, aux, aux_layer_stride, aux_row);
 }
 
 namespace {

@@ -84,24 +84,56 @@ class PhaseClock:
 
 
 class KVCache:
-    """Paged latent KV cache: [layers, num_blocks * block_size, kv_lora + rope] bf16."""
+    """Paged latent KV cache: [layers, num_blocks * block_size, kv_lora + rope] bf16, or
+    with ``kv_dtype="fp8"`` e4m3 rows (uint8) plus fp32 block scales [layers, slots, 5]
+    (amax / 448 of each 128-element block of the row; block 4 is the 64 rope dims),
+    written by the KV-write kernels and read by the fp8 decode kernel and ``kv8_gather``."""
 
     def __init__(self, cfg: MLAMoEConfig, num_blocks: int, block_size: int = 64, device="cuda",
-                 layers: int | None = None, dtype: torch.dtype | None = None):
+                 layers: int | None = None, dtype: torch.dtype | None = None, kv_dtype: str = "bf16"):
         self.block_size = block_size
         self.num_blocks = num_blocks
         self.num_layers = layers if layers is not None else cfg.num_layers
         dev = torch.device(device)
+        self.fp8 = kv_dtype == "fp8"
+        slots = num_blocks * block_size
+        self.scales = None
+        if self.fp8:
+            if dev.type != "cuda" or cfg.kv_cache_dim != 576 or block_size != 64:
+                raise ValueError("the fp8 KV cache needs a CUDA device, 576-wide rows and 64-token blocks")
+            self.data = torch.zeros(self.num_layers, slots, cfg.kv_cache_dim, dtype=torch.uint8, device=dev)
+            self.scales = torch.zeros(self.num_layers, slots, 5, dtype=torch.float32, device=dev)
+            return
+        if kv_dtype not in ("bf16", "auto"):
+            raise ValueError(f"kv_dtype must be bf16 or fp8, not {kv_dtype!r}")
         if dtype is None:
             dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
-        self.data = torch.zeros(self.num_layers, num_blocks * block_size, cfg.kv_cache_dim, dtype=dtype, device=dev)
+        self.data = torch.zeros(self.num_layers, slots, cfg.kv_cache_dim, dtype=dtype, device=dev)
 
     def layer(self, i: int) -> torch.Tensor:
         return self.data[i]
 
+    def layer_scales(self, i: int) -> torch.Tensor | None:
+        return None if self.scales is None else self.scales[i]
+
+    def planes(self) -> list[torch.Tensor]:
+        """The cache's arrays as [layers, slots, row] tensors of 2-byte units (bf16 views
+        of the fp8 rows and their scales) for block copies; the CPU cache as it is."""
+        if self.fp8:
+            return [self.data.view(torch.bfloat16), self.scales.view(torch.bfloat16)]
+        return [self.data]
+
+    def dequantized(self, i: int) -> torch.Tensor:
+        """Layer i's rows as fp32 (the stored values; fp8 rows times their block scales)."""
+        if not self.fp8:
+            return self.data[i].float()
+        v = self.data[i].view(torch.float8_e4m3fn).float()
+        return v * self.scales[i].repeat_interleave(128, dim=1)[:, :576]
+
     @property
     def bytes(self) -> int:
-        return self.data.numel() * self.data.element_size()
+        b = self.data.numel() * self.data.element_size()
+        return b + (self.scales.numel() * 4 if self.scales is not None else 0)
 
 
 # SPARKPIPE_FUSED_ROUTER=1 computes a small router's logits inside the top-k kernel
@@ -190,11 +222,12 @@ class MLAMoEModel:
         T = xn.shape[0]
         nh, dn, dv, kvl = c.num_heads, c.qk_nope_head_dim, c.v_head_dim, c.kv_lora_rank
         layer_cache = cache.layer(i - self._layer_offset)
+        kv_scales = cache.layer_scales(i - self._layer_offset)
         q_lat = torch.empty(T, nh, c.kv_cache_dim, dtype=torch.bfloat16, device=self.device)
         if c.q_lora_rank:
             q, kv_a = self._project(i, xn)
             ops.mla_kv_write(kv_a, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache,
-                             None, kvl, c.qk_rope_head_dim, c.rms_norm_eps)
+                             None, kvl, c.qk_rope_head_dim, c.rms_norm_eps, kv_scales)
             ops.rope_q(self._q_view(q, T), dn, q_lat, kvl, fb.positions, self.cos_sin, c.qk_rope_head_dim)
             q_src, q_batch_k = q, c.qk_head_dim
         elif self.absorbed:
@@ -203,10 +236,10 @@ class MLAMoEModel:
             # normalises / ropes / caches the latent KV
             qkv = self._lin(xn, w[p + "w_qkv_abs"], slab=True)
             ops.mla_decode_prep(qkv, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache,
-                                None, q_lat, kvl, 0, nh * c.kv_cache_dim, c.rms_norm_eps)
+                                None, q_lat, kvl, 0, nh * c.kv_cache_dim, c.rms_norm_eps, kv_scales)
             o_lat = torch.empty(T, nh, kvl, dtype=torch.bfloat16, device=self.device)
             ops.mla_decode(q_lat, layer_cache, fb.block_table, fb.context_lens, o_lat, fb.decode_splits, self.scale,
-                           last_slot=fb.self_slots)
+                           last_slot=fb.self_slots, kv_scales=kv_scales)
             return self._lin(o_lat.view(T, nh * kvl), w[p + "w_ov"], slab=True)
         else:
             # one kernel: split-K reduction of the q/kv projection, latent norm + RoPE
@@ -214,7 +247,7 @@ class MLAMoEModel:
             qkv = self._lin(xn, w[p + "w_qkv_a"], slab=True)
             q_src = torch.empty(T, nh * dn, dtype=torch.bfloat16, device=self.device)
             ops.mla_decode_prep(qkv, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache,
-                                q_src, q_lat, dn, 0, self.qa_dim, c.rms_norm_eps)
+                                q_src, q_lat, dn, 0, self.qa_dim, c.rms_norm_eps, kv_scales)
             q_batch_k = dn
         # q_lat[t, h, :kvl] = q_nope[t, h] @ W_UK[h]
         ops.batched_gemm(w[p + "w_uk_t"], q_src, q_lat.view(T, nh * c.kv_cache_dim), M=kvl, N=T, K=dn, batch=nh,
@@ -222,7 +255,7 @@ class MLAMoEModel:
                          d_batch_stride=c.kv_cache_dim)
         o_lat = torch.empty(T, nh, kvl, dtype=torch.bfloat16, device=self.device)
         ops.mla_decode(q_lat, layer_cache, fb.block_table, fb.context_lens, o_lat, fb.decode_splits, self.scale,
-                           last_slot=fb.self_slots)
+                       last_slot=fb.self_slots, kv_scales=kv_scales)
         attn = torch.empty(T, nh * dv, dtype=torch.bfloat16, device=self.device)
         # attn[t, h*dv + v] = o_lat[t, h] @ W_UV[h]^T
         ops.batched_gemm(w[p + "w_kv_b"], o_lat.view(T, nh * kvl), attn, M=dv, N=T, K=kvl, batch=nh, a_row0=dn,
@@ -236,10 +269,16 @@ class MLAMoEModel:
         nh, dn, dv, kvl, dr = c.num_heads, c.qk_nope_head_dim, c.v_head_dim, c.kv_lora_rank, c.qk_rope_head_dim
         q, kv_a = self._project(i, xn)
         layer_cache = cache.layer(i - self._layer_offset)
+        kv_scales = cache.layer_scales(i - self._layer_offset)
         lat = torch.empty(T, c.kv_cache_dim, dtype=torch.bfloat16, device=self.device)
         ops.mla_kv_write(kv_a, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache, lat,
-                         kvl, dr, c.rms_norm_eps)
-        lat_ctx = lat if fb.ctx_slots is None else ops.gather_rows(layer_cache, fb.ctx_slots)
+                         kvl, dr, c.rms_norm_eps, kv_scales)
+        if fb.ctx_slots is None:
+            lat_ctx = lat
+        elif kv_scales is not None:  # earlier chunks / cached prefix: dequantised fp8 rows
+            lat_ctx = ops.kv8_gather(layer_cache, kv_scales, fb.ctx_slots)
+        else:
+            lat_ctx = ops.gather_rows(layer_cache, fb.ctx_slots)
         Tk = lat_ctx.shape[0]
         kv = ops.linear(lat_ctx[:, :kvl], w[p + "w_kv_b"])              # [Tk, nh*(dn+dv)]
         q3 = self._q_view(q, T)
@@ -337,7 +376,7 @@ class MLAMoEModel:
         ops.add_rmsnorm(x, None, w["l0.in_norm"], xn, c.rms_norm_eps)
         kv_a = ops.linear(xn, wt[self.qa_dim:])
         ops.mla_kv_write(kv_a, w["l0.kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, cache.layer(0), None,
-                         c.kv_lora_rank, c.qk_rope_head_dim, c.rms_norm_eps)
+                         c.kv_lora_rank, c.qk_rope_head_dim, c.rms_norm_eps, cache.layer_scales(0))
 
     # ------------------------------------------------------------------ forward
     def forward(self, fb: ForwardBatch, cache: KVCache, layers: range | None = None,
@@ -423,7 +462,8 @@ class DecodeGraph:
         heads = model.cfg.num_heads
         self.fb = ForwardBatch(mode="decode", token_ids=self.ids, positions=self.pos, slot_mapping=self.slots,
                                block_table=self.block_table, context_lens=self.ctx,
-                               decode_splits=ops.mla_decode_splits(batch, heads, max_context, ops.kernels().num_sms()))
+                               decode_splits=ops.mla_decode_splits(batch, heads, max_context, ops.kernels().num_sms(),
+                                                                   kv_fp8=cache.fp8))
         self.graph = None
         self.use_graph = use_graph
         self._run_eager()  # warm-up (also sets kernel attributes outside capture)

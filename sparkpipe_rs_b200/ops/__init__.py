@@ -33,6 +33,7 @@ __all__ = [
     "interleave_gate_up_fp8",
     "mla_decode",
     "mla_decode_splits",
+    "kv8_gather",
     "prefill_attention",
     "moe_topk",
     "moe_align",
@@ -241,8 +242,12 @@ def add_rmsnorm(x, residual, w, out, eps):
     return out
 
 
-def mla_kv_write(kv, norm_w, positions, cos_sin, slot_mapping, cache, latent_out, kv_lora, rope, eps):
-    kernels().mla_kv_write(kv, norm_w, positions, cos_sin, slot_mapping, cache, latent_out, kv_lora, rope, float(eps))
+def mla_kv_write(kv, norm_w, positions, cos_sin, slot_mapping, cache, latent_out, kv_lora, rope, eps, kv_scales=None):
+    """Latent RMSNorm + rope-key RoPE of kv rows into the paged cache (bf16, or fp8 e4m3
+    with ``kv_scales`` [slots, 5]: one amax / 448 scale per 128 elements, block 4 the
+    rope dims) and optionally into ``latent_out`` (bf16)."""
+    kernels().mla_kv_write(kv, norm_w, positions, cos_sin, slot_mapping, cache, latent_out, kv_lora, rope, float(eps),
+                           kv_scales)
     _count(1)
 
 
@@ -365,15 +370,20 @@ _MLA_DEFAULT = os.environ.get("SPARKPIPE_MLA_KERNEL", "mma")
 _MLA_SK_EARLY = os.environ.get("SPARKPIPE_MLA_SK_EARLY", "1") != "0"
 
 
-def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 148, impl: str = "auto") -> int:
-    """Split-KV factor of the split-KV kernels ("mma", "tc"): the most CTAs that still fit
+def mla_decode_splits(batch: int, heads: int, max_context: int, num_sms: int = 148, impl: str = "auto",
+                      kv_fp8: bool = False) -> int:
+    """Split-KV factor of the split-KV kernels ("mma", "tc", the fp8-cache kernel with
+    ``kv_fp8``): the most CTAs that still fit
     one wave on the SMs, without splits of under two blocks (a second partial wave costs
     more than it hides: B=64, 16 heads, ctx 1024 measured 27 us at 2 splits, 34 us at 3).
     The stream-K kernel ignores it."""
     groups = heads // (32 if heads % 32 == 0 else 16)
     ctas = max(1, batch * groups)
     k_impl = impl if impl in ("tc", "mma") else ("tc" if _MLA_DEFAULT == "tc" else "mma")
-    slots = num_sms * int(kernels().mla_ctas_per_sm(heads, MLA_IMPL[k_impl]))  # CTAs resident at once
+    if kv_fp8:
+        slots = num_sms * int(kernels().mla_fp8_ctas_per_sm(heads))
+    else:
+        slots = num_sms * int(kernels().mla_ctas_per_sm(heads, MLA_IMPL[k_impl]))  # CTAs resident at once
     want = max(1, slots // ctas)
     blocks = max(1, math.ceil(max_context / 64))
     # few long sequences need many splits to use the SMs (one 131K-token sequence:
@@ -427,11 +437,13 @@ def _sk_workspace(device) -> _SkWorkspace:
 
 
 def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=None, lse_part=None, impl="auto",
-               trace=None, last_slot=None):
-    """Absorbed-MLA paged decode attention. ``impl``: "sk" (stream-K kernel: all SMs
-    over the flattened 32-token KV units, the default), "mma" (split-KV mma.sync
-    kernel), "tc" (split-KV tcgen05 kernel) or "auto" (the default, which the
-    SPARKPIPE_MLA_KERNEL environment variable can switch). ``splits`` applies to the
+               trace=None, last_slot=None, kv_scales=None):
+    """Absorbed-MLA paged decode attention. ``impl``: "mma" (split-KV mma.sync kernel,
+    the default), "sk" (stream-K kernel: all SMs over the flattened 32-token KV units),
+    "tc" (split-KV tcgen05 kernel) or "auto" (the default, which the
+    SPARKPIPE_MLA_KERNEL environment variable can switch). With ``kv_scales`` the cache
+    is fp8 e4m3 [slots, 576] with [slots, 5] block scales and the fp8 split-KV kernel
+    runs (``impl`` is ignored). ``splits`` applies to the
     split-KV kernels only. ``trace`` (diagnostics, int64 CUDA tensor): for "sk", 4 x 64
     global-timer stamps (ns) of four CTAs (first, second, middle, last): start,
     schedule ready, dependency wait passed, per piece queries landed / finished, per
@@ -440,6 +452,14 @@ def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=N
     reads its last context token from cache row last_slot[b] (-1: from its block
     table), as a tree verify's alternate leaves need."""
     B, H, _ = q.shape
+    if kv_scales is not None:
+        if splits > 1 and o_part is None:
+            o_part = torch.empty(B, splits, H, 512, dtype=torch.float32, device=q.device)
+            lse_part = torch.empty(B, splits, H, dtype=torch.float32, device=q.device)
+        kernels().mla_decode(q, cache, block_table, context_lens, out, o_part, lse_part, splits, float(scale),
+                             MLA_IMPL["mma"], None, last_slot, kv_scales)
+        _count(1 + (1 if splits > 1 else 0))
+        return out
     if impl == "auto":
         impl = _MLA_DEFAULT
     if last_slot is not None:
@@ -456,8 +476,17 @@ def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=N
         o_part = torch.empty(B, splits, H, 512, dtype=torch.float32, device=q.device)
         lse_part = torch.empty(B, splits, H, dtype=torch.float32, device=q.device)
     kernels().mla_decode(q, cache, block_table, context_lens, out, o_part, lse_part, splits, float(scale),
-                         MLA_IMPL[impl], trace, last_slot)
+                         MLA_IMPL[impl], trace, last_slot, None)
     _count(1 + (1 if splits > 1 else 0))
+    return out
+
+
+def kv8_gather(cache8, scales, idx, out=None):
+    """Dequantised bf16 rows [n, 576] of an fp8 latent cache at row ids ``idx``."""
+    if out is None:
+        out = torch.empty(idx.shape[0], 576, dtype=torch.bfloat16, device=cache8.device)
+    kernels().kv8_gather(cache8, scales, idx, out)
+    _count(1)
     return out
 
 
@@ -581,11 +610,12 @@ def spec_chain_commit(tok, tgt, ctx, pos, budget, keys, L, committed, counts, p_
     _count(1)
 
 
-def mtp_tree_commit(tok, tgt, ctx, slots, cache_data, committed, counts, paths):
+def mtp_tree_commit(tok, tgt, ctx, slots, cache_data, committed, counts, paths, cache_scales=None):
     """Verify round, the fixed MTP tree (rows r * B + b, r = 0..5): resolved path per
     lane, committed [B, 6] / counts [B], and the KV move of an accepted alternate leaf
-    from its shadow slot in ``cache_data`` [layers, slots, row]."""
-    kernels().mtp_tree_commit(tok, tgt, ctx, slots, cache_data, committed, counts, paths)
+    from its shadow slot in ``cache_data`` [layers, slots, row] (and in its fp8 block
+    scales [layers, slots, 5])."""
+    kernels().mtp_tree_commit(tok, tgt, ctx, slots, cache_data, committed, counts, paths, cache_scales)
     _count(1)
 
 
@@ -610,14 +640,16 @@ def slab_add_rmsnorm(x, residual, w, out, eps):
 
 
 def mla_decode_prep(qkv, norm_w, positions, cos_sin, slot_mapping, cache, q_nope_out, q_lat, dn, q_off, kv_off,
-                    eps):
-    """Decode prologue of MLA attention from the fused q/kv projection (``Slabs`` or bf16 [T, Qa + kv])."""
+                    eps, kv_scales=None):
+    """Decode prologue of MLA attention from the fused q/kv projection (``Slabs`` or bf16
+    [T, Qa + kv]); the latent row goes to the bf16 cache, or the fp8 one with ``kv_scales``."""
     if isinstance(qkv, Slabs):
         kernels().mla_decode_prep(qkv.ws, qkv.stride, qkv.splits, None, norm_w, positions, cos_sin, slot_mapping,
-                                  cache, q_nope_out, q_lat, qkv.rows, dn, q_off, kv_off, qkv.cols, float(eps))
+                                  cache, q_nope_out, q_lat, qkv.rows, dn, q_off, kv_off, qkv.cols, float(eps),
+                                  kv_scales)
     else:
         kernels().mla_decode_prep(None, 0, 1, qkv, norm_w, positions, cos_sin, slot_mapping, cache, q_nope_out,
-                                  q_lat, qkv.shape[0], dn, q_off, kv_off, qkv.shape[1], float(eps))
+                                  q_lat, qkv.shape[0], dn, q_off, kv_off, qkv.shape[1], float(eps), kv_scales)
     _count(1)
 
 

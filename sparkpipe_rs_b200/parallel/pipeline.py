@@ -206,7 +206,8 @@ class StageRuntime:
         if dev.type == "cuda":
             from .. import ops
 
-            splits = ops.mla_decode_splits(lanes, self.model.cfg.num_heads, int(e.context_lens.max()))
+            splits = ops.mla_decode_splits(lanes, self.model.cfg.num_heads, int(e.context_lens.max()),
+                                           kv_fp8=getattr(self.cache, "fp8", False))
         return ForwardBatch(mode="decode", token_ids=t(pk.input_token_ids), positions=t(e.positions),
                             slot_mapping=t(e.slots), block_table=t(e.block_table).view(lanes, e.block_table_cols),
                             context_lens=t(e.context_lens), decode_splits=splits)

@@ -78,6 +78,8 @@ class EngineConfig:
     spec_row_cap: int = 0             # firing rows of a verify round (0: rows per lane x max_batch)
     host_kv_blocks: int = 0           # host KV tier: preempted sequences swap their KV out (0: recompute)
     host_prefix_blocks: int = 0       # host KV tier for prefix blocks evicted from the device (0: drop them)
+    kv_cache_dtype: str = "bf16"      # "fp8": e4m3 latent rows with per-128 block scales (CUDA, 576-wide rows)
+    warm_prefill: bool = True         # one throwaway prefill of the largest chunk at start (allocator warm-up)
 
 
 @dataclass
@@ -214,7 +216,7 @@ class LLMEngine:
         if cache is not None and shadow_blocks and cache.num_blocks < num_blocks + shadow_blocks:
             raise ValueError("tree speculation needs a cache with room for the shadow blocks")
         self.cache = cache or KVCache(cfg, num_blocks=num_blocks + shadow_blocks, block_size=e.block_size,
-                                      device=self.device)
+                                      device=self.device, kv_dtype=e.kv_cache_dtype if self.is_cuda else "bf16")
         self.use_graphs = self.is_cuda and e.use_cuda_graph and isinstance(self.model, MLAMoEModel)
         self.draft = self.dcache = None
         if self.spec:
@@ -287,6 +289,8 @@ class LLMEngine:
                     self._verify_round(b)
         if self.spec and self.use_graphs and not e.spec_force:
             self._prime_step_costs()
+        if e.warm_prefill and self.is_cuda and isinstance(self.model, MLAMoEModel):
+            self._warm_prefill()
         self.step_log: list[tuple[str, int, float, int]] = []  # (kind, seqs, seconds, tokens)
 
     # ------------------------------------------------------------------ requests
@@ -403,6 +407,24 @@ class LLMEngine:
                 e1.synchronize()
                 self._record_cost(kind, b, e0.elapsed_time(e1))
 
+    def _warm_prefill(self):
+        """One prefill forward of the largest chunk on throwaway inputs (token 0, every
+        KV slot -1 so nothing is written): the first real chunk then finds its activation
+        and workspace memory in the caching allocator's pool instead of paying for fresh
+        device allocations inside its time to first token. Lockstep ranks all run it."""
+        e = self.ecfg
+        T = max(1, e.max_prefill_tokens)
+        L = max(1, min(T, e.max_model_len))
+        lens = [L] * (T // L) + ([T % L] if T % L else [])
+        dev = self.device
+        cu = torch.tensor([0] + list(itertools.accumulate(lens)), dtype=torch.int32, device=dev)
+        pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in lens]).to(dev)
+        fb = ForwardBatch(mode="prefill", token_ids=torch.zeros(T, dtype=torch.int32, device=dev), positions=pos,
+                          slot_mapping=torch.full((T,), -1, dtype=torch.int32, device=dev), cu_q=cu, cu_k=cu, max_q=L,
+                          logits_idx=(cu[1:] - 1).contiguous())
+        self.model.forward(fb, self.cache)
+        torch.cuda.synchronize(dev)
+
     def _run_prefill(self, plan) -> torch.Tensor:
         fb = ForwardBatch(
             mode="prefill",
@@ -467,7 +489,8 @@ class LLMEngine:
                               slot_mapping=self._h2d("d_slots", plan.slot_mapping),
                               block_table=self._h2d("d_bt", plan.block_table).view(B, plan.max_blocks),
                               context_lens=self._h2d("d_ctx", plan.context_lens),
-                              decode_splits=ops.mla_decode_splits(B, self.cfg.num_heads, plan.max_context)
+                              decode_splits=ops.mla_decode_splits(B, self.cfg.num_heads, plan.max_context,
+                                                                  kv_fp8=getattr(self.cache, "fp8", False))
                               if self.is_cuda else 1)
             logits = self.model.forward(fb, self.cache)
             if self.spec:

@@ -34,31 +34,42 @@ from .. import ops
 
 
 class HostKvTier:
+    """The cache's arrays move together: one plane for a bf16 (or CPU fp32) cache, two
+    for the fp8 cache (its e4m3 rows and their block scales, both as 2-byte units)."""
+
     def __init__(self, cache, host_blocks: int, max_batch_blocks: int = 64):
         self.cache = cache
-        data = cache.data
-        self.layers, _, self.row = data.shape
+        self.planes = cache.planes() if hasattr(cache, "planes") else [cache.data]
+        data = self.planes[0]
+        self.layers = data.shape[0]
         self.bs = cache.block_size
-        self.block_elems = self.layers * self.bs * self.row
+        self.rows = [p.shape[2] for p in self.planes]
+        self.row = self.rows[0]
+        self.plane_elems = [self.layers * self.bs * r for r in self.rows]
+        self.block_elems = sum(self.plane_elems)
         self.max_batch = max_batch_blocks
         self.is_cuda = data.device.type == "cuda"
         self.evicted_blocks = 0
         self.restored_blocks = 0
         if not self.is_cuda:
-            self.host = torch.empty(host_blocks, self.layers, self.bs, self.row, dtype=data.dtype)
+            self.host = [torch.empty(host_blocks, self.layers, self.bs, r, dtype=p.dtype)
+                         for p, r in zip(self.planes, self.rows)]
             self.free, self.pending = list(range(host_blocks))[::-1], []
             return
-        self.host = torch.empty(host_blocks, self.block_elems, dtype=data.dtype, pin_memory=True)
+        self.host = [torch.empty(host_blocks, e, dtype=p.dtype, pin_memory=True)
+                     for p, e in zip(self.planes, self.plane_elems)]
         self.free = list(range(host_blocks))[::-1]
         self.pending = []  # (event, host slots) of restores still reading their slots
-        # one staging buffer per direction: evictions run on the compute stream,
-        # restores on the copy stream
-        self.staging_out = torch.empty(max_batch_blocks * self.block_elems, dtype=data.dtype, device=data.device)
-        self.staging_in = torch.empty(max_batch_blocks * self.block_elems, dtype=data.dtype, device=data.device)
+        # one staging buffer per direction and plane: evictions run on the compute
+        # stream, restores on the copy stream
+        self.staging_out = [torch.empty(max_batch_blocks * e, dtype=p.dtype, device=p.device)
+                            for p, e in zip(self.planes, self.plane_elems)]
+        self.staging_in = [torch.empty(max_batch_blocks * e, dtype=p.dtype, device=p.device)
+                           for p, e in zip(self.planes, self.plane_elems)]
         self.stream = torch.cuda.Stream(device=data.device)
 
     def _ids(self, blocks):
-        return torch.as_tensor(blocks, dtype=torch.int32).to(self.cache.data.device, non_blocking=True)
+        return torch.as_tensor(blocks, dtype=torch.int32).to(self.planes[0].device, non_blocking=True)
 
     def _reclaim(self, block: bool = False):
         keep = []
@@ -81,42 +92,44 @@ class HostKvTier:
         self.evict_to(blocks, slots)
         return slots
 
-    def _cpu_view(self):
-        return self.cache.data.view(self.layers, -1, self.bs, self.row)
+    def _cpu_views(self):
+        return [p.view(self.layers, -1, self.bs, r) for p, r in zip(self.planes, self.rows)]
 
     def evict_to(self, blocks: list[int], slots: list[int]):
         """Copies device blocks into the given host slots; returns when the copy is done
         (earlier restores reading any host slot are waited for first)."""
         assert len(slots) == len(blocks)
         if not self.is_cuda:
-            v = self._cpu_view()
-            for b, s in zip(blocks, slots):
-                self.host[s].copy_(v[:, b])
+            for v, h in zip(self._cpu_views(), self.host):
+                for b, s in zip(blocks, slots):
+                    h[s].copy_(v[:, b])
             self.evicted_blocks += len(blocks)
             return
         self._reclaim(block=True)
         for i in range(0, len(blocks), self.max_batch):
             chunk, sl = blocks[i:i + self.max_batch], slots[i:i + self.max_batch]
             n = len(chunk)
-            ops.kernels().kv_blocks_copy(self.cache.data, self._ids(chunk), self.staging_out, self.bs, True)
-            st = self.staging_out[:n * self.block_elems].view(n, self.block_elems)
-            # host slots of one batch are copied one contiguous run at a time
-            j = 0
-            while j < n:
-                k = j
-                while k + 1 < n and sl[k + 1] == sl[k] + 1:
-                    k += 1
-                self.host[sl[j]:sl[k] + 1].copy_(st[j:k + 1], non_blocking=True)
-                j = k + 1
+            ids = self._ids(chunk)
+            for plane, stage, host, e in zip(self.planes, self.staging_out, self.host, self.plane_elems):
+                ops.kernels().kv_blocks_copy(plane, ids, stage, self.bs, True)
+                st = stage[:n * e].view(n, e)
+                # host slots of one batch are copied one contiguous run at a time
+                j = 0
+                while j < n:
+                    k = j
+                    while k + 1 < n and sl[k + 1] == sl[k] + 1:
+                        k += 1
+                    host[sl[j]:sl[k] + 1].copy_(st[j:k + 1], non_blocking=True)
+                    j = k + 1
         torch.cuda.current_stream().synchronize()
         self.evicted_blocks += len(blocks)
 
     def restore(self, slots: list[int], blocks: list[int]):
         """Copies host slots into device blocks; the compute stream waits for the copy."""
         if not self.is_cuda:
-            v = self._cpu_view()
-            for s, b in zip(slots, blocks):
-                v[:, b].copy_(self.host[s])
+            for v, h in zip(self._cpu_views(), self.host):
+                for s, b in zip(slots, blocks):
+                    v[:, b].copy_(h[s])
             self.restored_blocks += len(blocks)
             return
         self.wait(self.prefetch(slots, blocks, owned=False))
@@ -133,10 +146,12 @@ class HostKvTier:
             for i in range(0, len(blocks), self.max_batch):
                 chunk, sl = blocks[i:i + self.max_batch], slots[i:i + self.max_batch]
                 n = len(chunk)
-                st = self.staging_in[:n * self.block_elems].view(n, self.block_elems)
-                for j, s in enumerate(sl):
-                    st[j].copy_(self.host[s], non_blocking=True)
-                ops.kernels().kv_blocks_copy(self.cache.data, self._ids(chunk), self.staging_in, self.bs, False)
+                ids = self._ids(chunk)
+                for plane, stage, host, e in zip(self.planes, self.staging_in, self.host, self.plane_elems):
+                    st = stage[:n * e].view(n, e)
+                    for j, s in enumerate(sl):
+                        st[j].copy_(host[s], non_blocking=True)
+                    ops.kernels().kv_blocks_copy(plane, ids, stage, self.bs, False)
             done.record(self.stream)
         # slots this tier handed out return to its free list once read; caller-owned
         # slots are only waited for before the next eviction

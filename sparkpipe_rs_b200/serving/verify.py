@@ -137,14 +137,16 @@ class VerifyRound:
         self.paths = torch.zeros(B, **i32)
         nsm = ops.kernels().num_sms() if self.is_cuda else 1
 
-        def splits(rows, heads):
-            return ops.mla_decode_splits(rows, heads, max_context, nsm) if self.is_cuda else 1
+        def splits(rows, heads, cache):
+            if not self.is_cuda:
+                return 1
+            return ops.mla_decode_splits(rows, heads, max_context, nsm, kv_fp8=getattr(cache, "fp8", False))
 
         def rows_fb(j0, j1, model):
             s = slice(j0 * B, j1 * B)
             return ForwardBatch(mode="decode", token_ids=self.tok[s], positions=self.pos[s], slot_mapping=self.slot[s],
                                 block_table=self.bt if j1 - j0 == 1 else self.bt_rows[s], context_lens=self.ctx[s],
-                                decode_splits=splits((j1 - j0) * B, model.cfg.num_heads))
+                                decode_splits=splits((j1 - j0) * B, model.cfg.num_heads, self.dcache))
 
         steps = 3 if mode == "mtp_tree" else draft_len + 1
         self.dfb = [rows_fb(j, j + 1, draft) for j in range(steps)]
@@ -152,7 +154,7 @@ class VerifyRound:
                                     slot_mapping=self.sync[2])
         self.vfb = ForwardBatch(mode="decode", token_ids=self.tok, positions=self.pos, slot_mapping=self.slot,
                                 block_table=self.bt_rows, context_lens=self.ctx,
-                                decode_splits=splits(R, target.cfg.num_heads),
+                                decode_splits=splits(R, target.cfg.num_heads, self.tcache),
                                 self_slots=self.slot if mode == "mtp_tree" else None)
         self.use_graph = use_graph and self.is_cuda
         self.graph = None
@@ -193,7 +195,7 @@ class VerifyRound:
                                       self.counts, self.p_accept, self.seed)
             else:
                 ops.mtp_tree_commit(t, self.tgt, self.ctx, self.slot, self.tcache.data, self.committed, self.counts,
-                                    self.paths)
+                                    self.paths, self.tcache.scales)
         elif self.mode == "chain":
             c, n = chain_commit_reference(t, self.tgt, self.ctx, self.pos, self.budget, self.keys, B, self.L,
                                           self.p_accept, self.seed)

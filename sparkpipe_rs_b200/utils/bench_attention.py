@@ -27,7 +27,8 @@ def main():
     ap.add_argument("--trace", action="store_true",
                     help="sk only: print the kernel's device event trace of four CTAs (one eager launch)")
     ap.add_argument("--impl", default="sk,mma", help="kernels to time: sk (stream-K), tc (tcgen05 split-KV), "
-                                                      "mma (mma.sync split-KV)")
+                                                      "mma (mma.sync split-KV), fp8 (split-KV over the fp8 e4m3 "
+                                                      "cache with per-128 block scales)")
     args = ap.parse_args()
     from sparkpipe_rs_b200 import ops
 
@@ -43,7 +44,29 @@ def main():
     out = torch.empty(B, H, 512, device=dev, dtype=torch.bfloat16)
     nbytes = B * L * 576 * 2
     scale = 1 / math.sqrt(192)
-    for impl in args.impl.split(","):
+    impls = args.impl.split(",")
+    if "fp8" in impls:  # the same rows quantised: e4m3 values, amax / 448 per 128-element block
+        caches8 = []
+        for c in caches:
+            xp = torch.zeros(c.shape[0], 640, device=dev)
+            xp[:, :576] = c.float()
+            amax = xp.view(-1, 5, 128).abs().amax(-1)
+            inv = torch.where(amax > 0, 448.0 / amax, torch.zeros_like(amax))
+            q8 = (xp.view(-1, 5, 128) * inv[..., None]).view(-1, 640)[:, :576].to(torch.float8_e4m3fn)
+            caches8.append((q8.view(torch.uint8).contiguous(), (amax / 448.0).contiguous()))
+            del xp
+    for impl in impls:
+        if impl == "fp8":
+            nb8 = B * L * (576 + 20)
+            for sp in [int(s) for s in args.splits.split(",")]:
+                splits = sp or ops.mla_decode_splits(B, H, L, ops.kernels().num_sms(), kv_fp8=True)
+                o_part = torch.empty(B, splits, H, 512, device=dev, dtype=torch.float32)
+                lse = torch.empty(B, splits, H, device=dev, dtype=torch.float32)
+                us = time_fn(lambda i: ops.mla_decode(q, caches8[i % n_caches][0], bt, ctx, out, splits, scale, o_part,
+                                                      lse, kv_scales=caches8[i % n_caches][1]), args.iters)
+                print(f"mla_decode[fp8] B={B} H={H} ctx={L} splits={splits}{' (auto)' if sp == 0 else ''}: "
+                      f"{us:8.2f} us  {nb8 / us / 1e6:6.2f} TB/s of KV ({nbytes / us / 1e6:6.2f} bf16-equivalent)")
+            continue
         if impl == "sk":  # one schedule over all SMs: no split factor
             ops.mla_decode(q, caches[0], bt, ctx, out, 1, scale, impl="sk")  # sizes the scratch outside capture
             us = time_fn(lambda i: ops.mla_decode(q, caches[i % n_caches], bt, ctx, out, 1, scale, impl="sk"),
