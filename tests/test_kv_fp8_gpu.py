@@ -93,7 +93,8 @@ def test_fp8_mla_decode_last_slot_override():
     B, H, nblocks, maxb = 4, 16, 32, 6
     q8, sc = quant_rows(torch.randn(nblocks * 64, 576, device=DEV, generator=g))
     ctx = torch.tensor([70, 128, 5, 300], device=DEV, dtype=torch.int32)
-    bt = torch.stack([torch.randperm(nblocks - 2, device=DEV, generator=g)[:maxb] for _ in range(B)]).int()
+    # disjoint block tables: a substituted row belongs to one sequence only
+    bt = torch.randperm(nblocks - 2, device=DEV, generator=g)[:B * maxb].int().view(B, maxb)
     shadow = torch.tensor([(nblocks - 1) * 64 + b for b in range(B)], device=DEV, dtype=torch.int32)
     shadow[2] = -1  # this row keeps its own last token
     qv = torch.randn(B, H, 576, device=DEV, generator=g).bfloat16()
