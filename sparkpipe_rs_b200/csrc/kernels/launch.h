@@ -278,6 +278,12 @@ void combine_add_rmsnorm(const void* y, long long ldy, const int* inv_pos, const
 // Returns the number of kernels launched.
 int moe_align(const int* topk_ids, int T, int k, int E, int block_n, int* grp_rows, int* grp_tiles,
                int* sorted_tok, int* inv_pos, int* work, cudaStream_t s);
+// moe_topk + moe_align in one single-CTA launch for decode-sized batches (T <= 256);
+// false (nothing launched) when the shape does not qualify.
+bool moe_route_align(const float* logits, long long slab_stride, int splits, const float* bias, int* topk_ids,
+                     float* topk_w, int T, int E, int k, int n_shared, int scoring, int renorm, float scaling,
+                     int n_group, int topk_group, int group_top2, int block_n, int* grp_rows, int* grp_tiles,
+                     int* sorted_tok, int* inv_pos, cudaStream_t s);
 void gather_rows(const void* x, long long ldx, const int* idx, void* out, long long ldo, int rows, int cols,
                  cudaStream_t s);
 void silu_mul(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s);

@@ -306,6 +306,15 @@ class MLAMoEModel:
                                      c.routed_scaling_factor, **route)
         else:
             logits = ops.linear_slabs(xn, gate, out_dtype=torch.float32)
+            if (self.ep is None and not isinstance(w[p + "e_w13"], ops.Fp8Weight)
+                    and T * (k + S) < MOE_TOKEN_MAJOR_MIN_ROWS * (E + S)):
+                # decode-sized local MoE: routing and the expert-sorted layout in one launch
+                ra = ops.moe_route_align(logits, bias, k, 1 if sigmoid else 0, c.norm_topk_prob,
+                                         c.routed_scaling_factor, S, c.n_group, c.topk_group,
+                                         c.topk_method == "noaux_tc", _moe_block_n(T * (k + S), E + S))
+                if ra is not None:
+                    ids, wts, grp_rows, grp_tiles, sorted_tok, inv_pos = ra
+                    return self._moe_grouped(i, xn, wts, grp_rows, grp_tiles, sorted_tok, inv_pos)
             ids, wts = ops.moe_topk(logits, bias, k, 1 if sigmoid else 0, c.norm_topk_prob, c.routed_scaling_factor,
                                     **route)
         kk = k + S
@@ -334,6 +343,17 @@ class MLAMoEModel:
             ops.grouped_gemm_fp8(w[p + "e_w2"], ops.quant_act_fp8(act), y, grp_rows, grp_tiles, E + S, bn)
             return ("combine", y, inv_pos, wts, kk)
         grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E + S, bn)
+        return self._moe_grouped(i, xn, wts, grp_rows, grp_tiles, sorted_tok, inv_pos)
+
+    def _moe_grouped(self, i, xn, wts, grp_rows, grp_tiles, sorted_tok, inv_pos):
+        """Weight-major grouped expert GEMMs over the expert-sorted rows; returns the
+        deferred weighted combine."""
+        c, w = self.cfg, self.w
+        p = f"l{i}."
+        T = xn.shape[0]
+        E, k, F, S = c.n_routed_experts, c.num_experts_per_tok, c.moe_intermediate_size, c.n_shared_experts
+        kk = k + S
+        bn = _moe_block_n(T * kk, E + S)
         xs = ops.gather_rows(xn, sorted_tok)
         if self.fused_swiglu:
             act = torch.empty(T * kk, F, dtype=torch.bfloat16, device=self.device)

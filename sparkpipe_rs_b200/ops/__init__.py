@@ -37,6 +37,7 @@ __all__ = [
     "prefill_attention",
     "moe_topk",
     "moe_align",
+    "moe_route_align",
     "gather_rows",
     "silu_mul",
     "moe_combine",
@@ -530,6 +531,37 @@ def moe_topk(logits, bias, k, scoring, renorm, scaling, n_shared=0, n_group=1, t
                        splits, int(n_group), int(topk_group), bool(group_top2))
     _count(1)
     return ids, w
+
+
+# SPARKPIPE_MOE_ROUTE_ALIGN=0 keeps decode routing as two launches (top-k, then align).
+_ROUTE_ALIGN = os.environ.get("SPARKPIPE_MOE_ROUTE_ALIGN", "1") != "0"
+
+
+def moe_route_align(logits, bias, k, scoring, renorm, scaling, n_shared, n_group, topk_group, group_top2, block_n):
+    """``moe_topk`` then ``moe_align`` over all E + n_shared experts, in one launch for
+    decode-sized batches (T <= 256); returns (ids, w, grp_rows, grp_tiles, sorted_tok,
+    inv_pos), or None when the shape does not qualify."""
+    if not _ROUTE_ALIGN:
+        return None
+    if isinstance(logits, Slabs):
+        T, E, dev = logits.rows, logits.cols, logits.ws.device
+        src, stride, splits = logits.ws, logits.stride, logits.splits
+    else:
+        T, E, dev = logits.shape[0], logits.shape[1], logits.device
+        src, stride, splits = logits, 0, 1
+    kk = k + n_shared
+    ids = torch.empty(T, kk, dtype=torch.int32, device=dev)
+    w = torch.empty(T, kk, dtype=torch.float32, device=dev)
+    grp_rows = torch.empty(E + n_shared + 1, dtype=torch.int32, device=dev)
+    grp_tiles = torch.empty(E + n_shared + 1, dtype=torch.int32, device=dev)
+    sorted_tok = torch.empty(T * kk, dtype=torch.int32, device=dev)
+    inv_pos = torch.empty(T * kk, dtype=torch.int32, device=dev)
+    if not kernels().moe_route_align(src, bias, ids, w, int(n_shared), int(scoring), bool(renorm), float(scaling), T,
+                                     E, stride, splits, int(n_group), int(topk_group), bool(group_top2), int(block_n),
+                                     grp_rows, grp_tiles, sorted_tok, inv_pos):
+        return None
+    _count(1)
+    return ids, w, grp_rows, grp_tiles, sorted_tok, inv_pos
 
 
 def moe_align(topk_ids, num_experts, block_n):

@@ -154,11 +154,70 @@ def sample_rows(logits: torch.Tensor, temps, keys) -> list[int]:
     return out
 
 
+class _StageGraph:
+    """CUDA graph of one stage's decode forward for a padded lane count: static input
+    buffers (token ids, positions, slots, block table, context lengths and, past stage
+    0, the received hidden rows), captured once after an eager warm-up over idle rows
+    (context 0, slot -1: nothing read, no KV written). Rows past a packet's lanes stay
+    idle."""
+
+    def __init__(self, rt, lanes: int, cols: int):
+        from .. import ops
+
+        dev, m = rt.device, rt.model
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.lanes = lanes
+        self.ids = torch.zeros(lanes, **i32)
+        self.pos = torch.zeros(lanes, **i32)
+        self.slots = torch.full((lanes,), -1, **i32)
+        self.bt = torch.zeros(lanes, cols, **i32)
+        self.ctx = torch.zeros(lanes, **i32)
+        self.h = torch.zeros(lanes, rt.hidden, dtype=rt.h_dtype, device=dev) if rt.rank > 0 else None
+        splits = ops.mla_decode_splits(lanes, m.cfg.num_heads, cols * rt.wcfg.kv_block_tokens,
+                                       kv_fp8=getattr(rt.cache, "fp8", False))
+        self.fb = ForwardBatch(mode="decode", token_ids=self.ids, positions=self.pos, slot_mapping=self.slots,
+                               block_table=self.bt, context_lens=self.ctx, decode_splits=splits)
+
+        def run():
+            return m.forward(self.fb, rt.cache, layers=rt.layers, hidden_in=self.h, return_hidden=not rt.last,
+                             layer_offset=rt.layers[0])
+
+        run()  # sets kernel attributes and sizes workspaces outside capture
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        cur = torch.cuda.current_stream(dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side), torch.cuda.graph(self.graph, stream=side):
+            self.out = run()
+        cur.wait_stream(side)
+
+    def load(self, pk, dev):
+        """Copies a decode packet's rows into the static inputs; the rest go idle."""
+        e = pk.exec
+        n = len(e.context_lens)
+
+        def put(dst, a):
+            dst[:n].copy_(torch.from_numpy(a).to(dev, non_blocking=True).view(dst[:n].shape))
+
+        put(self.ids, pk.input_token_ids)
+        put(self.pos, e.positions)
+        put(self.slots, e.slots)
+        put(self.ctx, e.context_lens)
+        put(self.bt, e.block_table)
+        if n < self.lanes:
+            self.slots[n:].fill_(-1)
+            self.ctx[n:].zero_()
+        return n
+
+
 class StageRuntime:
-    """One pipeline rank: its daemon, its layers and KV cache, its links."""
+    """One pipeline rank: its daemon, its layers and KV cache, its links. Decode
+    packets replay a per-stage CUDA graph of the padded lane count on GPUs
+    (``use_graphs``); prefill packets run eagerly."""
 
     def __init__(self, model, stage_layers: list[list[int]], cache, wcfg, group=None, control_group=None,
-                 device=None):
+                 device=None, use_graphs: bool = True):
         self.C = core()
         self.model, self.stage_layers, self.cache, self.wcfg = model, stage_layers, cache, wcfg
         self.group = group
@@ -181,6 +240,9 @@ class StageRuntime:
         self.h_dtype = torch.float32 if self.device.type == "cpu" else torch.bfloat16
         self.hidden = model.cfg.hidden_size
         self.executed = 0
+        self.use_graphs = use_graphs and self.device.type == "cuda"
+        self.graphs: dict[tuple[int, int], _StageGraph] = {}
+        self.graph_replays = 0
         self.last_logits = None  # last stage: logits of the most recent packet (diagnostics)
         self.after_execute = None  # optional callable(runtime) after each packet (diagnostics)
 
@@ -212,19 +274,42 @@ class StageRuntime:
                             slot_mapping=t(e.slots), block_table=t(e.block_table).view(lanes, e.block_table_cols),
                             context_lens=t(e.context_lens), decode_splits=splits)
 
+    def _graph_for(self, pk):
+        """The stage graph for a decode packet (lanes rounded up to a power of two),
+        captured on first use; None for prefill packets or without graphs."""
+        W = self.C.work_control
+        if not self.use_graphs or pk.flags & W.FLAG_PREFILL:
+            return None
+        lanes = len(pk.exec.context_lens)
+        bucket = 1 << max(0, (lanes - 1).bit_length())
+        key = (bucket, int(pk.exec.block_table_cols))
+        g = self.graphs.get(key)
+        if g is None:
+            g = self.graphs[key] = _StageGraph(self, bucket, key[1])
+        return g
+
     def _execute(self, wire: bytes):
         t0 = time.perf_counter_ns()
         pk = self.C.work_control.deserialize(wire)
-        fb = self._batch(pk)
-        rows = fb.token_ids.numel()
-        h = None
-        if self.rank > 0:
-            h = torch.empty(rows, self.hidden, dtype=self.h_dtype, device=self.device)
-            dist.irecv(h, self.rank - 1, group=self.group).wait()
-        out = self.model.forward(fb, self.cache, layers=self.layers, hidden_in=h, return_hidden=not self.last,
-                                 layer_offset=self.layers[0])
+        g = self._graph_for(pk)
+        if g is not None:
+            rows = g.load(pk, self.device)
+            if self.rank > 0:
+                dist.irecv(g.h[:rows], self.rank - 1, group=self.group).wait()
+            g.graph.replay()
+            self.graph_replays += 1
+            out = g.out[:rows]
+        else:
+            fb = self._batch(pk)
+            rows = fb.token_ids.numel()
+            h = None
+            if self.rank > 0:
+                h = torch.empty(rows, self.hidden, dtype=self.h_dtype, device=self.device)
+                dist.irecv(h, self.rank - 1, group=self.group).wait()
+            out = self.model.forward(fb, self.cache, layers=self.layers, hidden_in=h, return_hidden=not self.last,
+                                     layer_offset=self.layers[0])
         if not self.last:
-            out = out.to(self.h_dtype).contiguous()
+            out = out.to(self.h_dtype).clone() if g is not None else out.to(self.h_dtype).contiguous()
             self.hidden_sends.append((dist.isend(out, self.rank + 1, group=self.group), out))
             while len(self.hidden_sends) > 4:
                 w, _ = self.hidden_sends.pop(0)
@@ -260,6 +345,7 @@ class StageRuntime:
         for w, _ in self.hidden_sends:
             w.wait()
         self.hidden_sends.clear()
+        self.graphs.clear()  # graphs release their pools before the process group goes
 
 
 class PipelineModel(StageRuntime):
@@ -269,8 +355,8 @@ class PipelineModel(StageRuntime):
     runs_plans = True
 
     def __init__(self, model, stage_layers, cache, wcfg, micro_batches: int = 2, group=None, control_group=None,
-                 device=None):
-        super().__init__(model, stage_layers, cache, wcfg, group, control_group, device)
+                 device=None, use_graphs: bool = True):
+        super().__init__(model, stage_layers, cache, wcfg, group, control_group, device, use_graphs)
         if self.rank != 0:
             raise ValueError("PipelineModel runs on rank 0")
         self.cfg = model.cfg

@@ -112,7 +112,17 @@ def main():
             dg.run()
         torch.cuda.synchronize()
         print("ran", args.steps, "decode steps")
-        return
+    else:
+        _trace(args, dg, rank, world, cfg, B)
+    if world > 1:  # every path: graphs holding collectives go before the process group
+        dg.release()
+        torch.distributed.barrier()
+        ep.close()
+        torch.distributed.destroy_process_group()
+
+
+def _trace(args, dg, rank, world, cfg, B):
+    """Per-kernel device time of ``args.steps`` decode steps from torch.profiler."""
     from torch.profiler import ProfilerActivity, profile
 
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
@@ -135,11 +145,6 @@ def main():
     for name, us in sorted(tot.items(), key=lambda kv: -kv[1]):
         print(f"{name:80s} {us / args.steps:10.1f} {100 * us / args.steps / all_us:6.1f}% "
               f"{cnt[name] / args.steps:14.1f}")
-    if world > 1:
-        dg.release()
-        torch.distributed.barrier()
-        ep.close()
-        torch.distributed.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -2,7 +2,9 @@
 gloo for packets and final events): a 4-layer MLA-MoE split 2 / 2. With one
 micro-batch per step the greedy tokens equal a single-GPU engine's; with one or two
 micro-batches the last stage's prefill logits are bitwise equal to a single-GPU
-forward of the same batch (the hand-off between stages is exact)."""
+forward of the same batch (the hand-off between stages is exact). With two
+micro-batches the decode packets replay per-stage CUDA graphs (padded lane buckets,
+their own split-KV factor), so tokens match the single-GPU engine's up to near-ties."""
 import os
 import socket
 
@@ -42,7 +44,7 @@ def _engine_cfg(**kw):
                         decode_buckets=(1, 2, 4), use_cuda_graph=False, async_decode=False, **kw)
 
 
-def _worker(rank, port, micro, out_q):
+def _worker(rank, port, micro, graphs, out_q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -62,30 +64,30 @@ def _worker(rank, port, micro, out_q):
         cache = KVCache(cfg, num_blocks=nblocks, block_size=64, device=dev, layers=2)
         wcfg = work_config(cfg, 64, 256, 4, 512)
         if rank == 0:
-            pm = PipelineModel(model, stages, cache, wcfg, micro_batches=micro)
+            pm = PipelineModel(model, stages, cache, wcfg, micro_batches=micro, use_graphs=graphs)
             eng = LLMEngine(cfg, _engine_cfg(num_blocks=nblocks), model=pm, device=dev, cache=cache)
             res = eng.generate(_prompts(cfg), SamplingParams(max_tokens=24, ignore_eos=True))
             eng.shutdown()
-            out_q.put(("rank0", [o.token_ids for o in res.outputs], pm.final_events))
+            out_q.put(("rank0", [o.token_ids for o in res.outputs], pm.final_events, pm.graph_replays))
         else:
-            rt = StageRuntime(model, stages, cache, wcfg)
+            rt = StageRuntime(model, stages, cache, wcfg, use_graphs=graphs)
             first = []
             rt.after_execute = lambda r: first.append(r.last_logits.float().cpu()) if not first else None
             rt.serve()
-            out_q.put(("rank1", first[0]))
+            out_q.put(("rank1", first[0], rt.graph_replays))
         torch.cuda.synchronize()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("micro", [1, 2])
-def test_two_gpu_pipeline_matches_single_gpu(micro):
+@pytest.mark.parametrize("micro,graphs", [(1, False), (2, True)])
+def test_two_gpu_pipeline_matches_single_gpu(micro, graphs):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, micro, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, port, micro, graphs, q)) for r in range(2)]
     for p in procs:
         p.start()
     got = {}
@@ -95,8 +97,10 @@ def test_two_gpu_pipeline_matches_single_gpu(micro):
     for p in procs:
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    tokens, finals = got["rank0"]
-    pp_logits = got["rank1"][0]
+    tokens, finals, replays0 = got["rank0"]
+    pp_logits, replays1 = got["rank1"]
+    # every decode packet (23 steps x micro-batches) replayed a graph on both stages
+    assert (replays0, replays1) == ((23 * micro, 23 * micro) if graphs else (0, 0))
 
     # single-GPU reference: the same model and the same batches in one process
     from sparkpipe_rs_b200.models.mla_moe import ForwardBatch, KVCache, MLAMoEModel
