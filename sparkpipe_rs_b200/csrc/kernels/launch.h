@@ -200,6 +200,8 @@ int mla_fp8_ctas_per_sm(int heads);
 void mla_combine(const float* o_part, const float* lse_part, void* out, int B, int H, int splits, cudaStream_t s);
 // out[r, :] = dequantised fp8 cache row idx[r] (bf16 [n, 576]).
 void kv8_gather(const void* cache8, const float* scales, const int* idx, void* out, int n, cudaStream_t s);
+// Background L2 prefetch of [p, p + bytes) (16-byte aligned start; the tail under 16 bytes is skipped).
+void l2_prefetch(const void* p, long long bytes, cudaStream_t s);
 // Stream-K decode kernel (mla_decode_sk.cu): one CTA per SM over the flattened KV units.
 // Scratch: o_part [segments][heads per CTA][512] fp32, lse_part [segments][heads per CTA],
 // counters [(H / heads per CTA) * B] int32 zeroed once (the kernel leaves them zero).
@@ -278,12 +280,6 @@ void combine_add_rmsnorm(const void* y, long long ldy, const int* inv_pos, const
 // Returns the number of kernels launched.
 int moe_align(const int* topk_ids, int T, int k, int E, int block_n, int* grp_rows, int* grp_tiles,
                int* sorted_tok, int* inv_pos, int* work, cudaStream_t s);
-// moe_topk + moe_align in one single-CTA launch for decode-sized batches (T <= 256);
-// false (nothing launched) when the shape does not qualify.
-bool moe_route_align(const float* logits, long long slab_stride, int splits, const float* bias, int* topk_ids,
-                     float* topk_w, int T, int E, int k, int n_shared, int scoring, int renorm, float scaling,
-                     int n_group, int topk_group, int group_top2, int block_n, int* grp_rows, int* grp_tiles,
-                     int* sorted_tok, int* inv_pos, cudaStream_t s);
 void gather_rows(const void* x, long long ldx, const int* idx, void* out, long long ldo, int rows, int cols,
                  cudaStream_t s);
 void silu_mul(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s);

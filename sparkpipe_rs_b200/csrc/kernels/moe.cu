@@ -390,69 +390,6 @@ __global__ void __launch_bounds__(1024) moe_align_small_kernel(const int* __rest
   }
 }
 
-// Decode-sized routing in one launch: the CTA's 32 warps route the tokens (warp w takes
-// tokens w, w + 32, ..., each summing its token's split-K logit slabs into its own
-// shared-memory row), then the same CTA builds the expert-sorted layout as
-// moe_align_small_kernel does. Dynamic shared memory: 32 warps x 2 x E floats.
-constexpr int ROUTE_ALIGN_THREADS = 1024;
-__global__ void __launch_bounds__(ROUTE_ALIGN_THREADS)
-    moe_route_align_kernel(const float* __restrict__ logits, long long slab_stride, int splits,
-                           const float* __restrict__ bias, int* __restrict__ ids, float* __restrict__ wts, int T,
-                           int E, int k, int n_shared, int scoring, int renorm, float scaling, int n_group,
-                           int topk_group, int group_top2, int bn, int* __restrict__ grp_rows,
-                           int* __restrict__ grp_tiles, int* __restrict__ sorted_tok, int* __restrict__ inv_pos) {
-  extern __shared__ float s_route[];  // [32][2][E]
-  __shared__ int cnt[ALIGN_MAX_E];
-  __shared__ int cur[ALIGN_MAX_E];
-  griddep_wait();
-  griddep_launch();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* s_logit = s_route + warp * 2 * E;
-  float* s_scratch = s_logit + E;
-  for (int t = warp; t < T; t += ROUTE_ALIGN_THREADS / 32) {
-    const float* row = logits + (long long)t * E;
-    for (int e = lane; e < E; e += 32) {
-      float x = 0.f;
-      for (int s2 = 0; s2 < splits; ++s2) x += __ldcg(row + s2 * slab_stride + e);
-      s_logit[e] = x;
-    }
-    __syncwarp();
-    route_token_warp(s_logit, s_scratch, t, lane, bias, ids, wts, E, k, n_shared, scoring, renorm, scaling, n_group,
-                     topk_group, group_top2);
-    __syncwarp();
-  }
-  const int kk = k + n_shared, Et = E + n_shared, n = T * kk;
-  for (int e = threadIdx.x; e < Et; e += blockDim.x) cnt[e] = 0;
-  __syncthreads();  // the ids written above are visible to the whole CTA from here
-  for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&cnt[ids[i]], 1);
-  __syncthreads();
-  if (threadIdx.x < 32) scan_counts_warp(cnt, Et, bn, grp_rows, grp_tiles, cur);
-  __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int pos = atomicAdd(&cur[ids[i]], 1);
-    sorted_tok[pos] = i / kk;
-    inv_pos[i] = pos;
-  }
-}
-
-bool moe_route_align(const float* logits, long long slab_stride, int splits, const float* bias, int* topk_ids,
-                     float* topk_w, int T, int E, int k, int n_shared, int scoring, int renorm, float scaling,
-                     int n_group, int topk_group, int group_top2, int block_n, int* grp_rows, int* grp_tiles,
-                     int* sorted_tok, int* inv_pos, cudaStream_t s) {
-  const int kk = k + n_shared;
-  if (T <= 0 || T > 256 || E > TOPK_MAX_E || E + n_shared > ALIGN_MAX_E || kk > 32 || T * kk > 16384) return false;
-  if (n_group < 1) n_group = 1;
-  if (n_group > 1 && (n_group > 32 || E % n_group || topk_group < 1 || topk_group > n_group ||
-                      topk_group * (E / n_group) < k))
-    return false;
-  const int smem = 32 * 2 * E * (int)sizeof(float);
-  set_smem_bytes(moe_route_align_kernel, smem);
-  launch_k(moe_route_align_kernel, dim3(1), dim3(ROUTE_ALIGN_THREADS), smem, s, logits, slab_stride,
-           splits < 1 ? 1 : splits, bias, topk_ids, topk_w, T, E, k, n_shared, scoring, renorm, scaling, n_group,
-           topk_group, group_top2, block_n, grp_rows, grp_tiles, sorted_tok, inv_pos);
-  return true;
-}
-
 __global__ void moe_zero_kernel(int* __restrict__ p, int n) {
   griddep_wait();
   griddep_launch();

@@ -491,6 +491,12 @@ void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table,
   }
 }
 
+void l2_prefetch(const Tensor& t) {
+  CHECK_CUDA(t); CHECK_CONTIG(t);
+  const c10::cuda::CUDAGuard guard(t.device());
+  sp::l2_prefetch(t.data_ptr(), (long long)(t.numel() * t.element_size()), stream());
+}
+
 void kv8_gather(const Tensor& cache8, const Tensor& scales, const Tensor& idx, const Tensor& out) {
   CHECK_CUDA(cache8); CHECK_I32(idx); CHECK_BF16(out); CHECK_CONTIG(idx); CHECK_CONTIG(out);
   CHECK_ON(cache8, idx); CHECK_ON(cache8, out);
@@ -661,29 +667,6 @@ Tensor split_workspace() {
   float* w = split_ws();
   auto opts = torch::TensorOptions().dtype(torch::kFloat32).device(torch::kCUDA, c10::cuda::current_device());
   return torch::from_blob(w, {kSplitWsFloats}, opts);
-}
-
-// Routing and expert-sorted layout of a decode-sized batch in one launch; false when the
-// shape does not qualify (the caller then runs moe_topk and moe_align).
-bool moe_route_align(const Tensor& logits, const c10::optional<Tensor>& bias, const Tensor& ids, const Tensor& w,
-                     int64_t n_shared, int64_t scoring, bool renorm, double scaling, int64_t T, int64_t E,
-                     int64_t slab_stride, int64_t splits, int64_t n_group, int64_t topk_group, bool group_top2,
-                     int64_t block_n, const Tensor& grp_rows, const Tensor& grp_tiles, const Tensor& sorted_tok,
-                     const Tensor& inv_pos) {
-  CHECK_CUDA(logits); CHECK_F32(logits); CHECK_CONTIG(logits); CHECK_I32(ids); CHECK_F32(w); CHECK_CONTIG(ids);
-  CHECK_I32(grp_rows); CHECK_I32(grp_tiles); CHECK_I32(sorted_tok); CHECK_I32(inv_pos);
-  const int64_t kk = ids.size(1);
-  TORCH_CHECK(ids.size(0) >= T && grp_rows.numel() >= E + n_shared + 1 && grp_tiles.numel() >= E + n_shared + 1 &&
-                  sorted_tok.numel() >= T * kk && inv_pos.numel() >= T * kk,
-              "moe_route_align: outputs too small");
-  const c10::cuda::CUDAGuard guard(logits.device());
-  const float* b = nullptr;
-  if (bias.has_value()) { CHECK_F32(*bias); b = bias->data_ptr<float>(); }
-  return sp::moe_route_align(logits.data_ptr<float>(), slab_stride, (int)splits, b, ids.data_ptr<int>(),
-                             w.data_ptr<float>(), (int)T, (int)E, (int)(kk - n_shared), (int)n_shared, (int)scoring,
-                             renorm ? 1 : 0, (float)scaling, (int)n_group, (int)topk_group, group_top2 ? 1 : 0,
-                             (int)block_n, grp_rows.data_ptr<int>(), grp_tiles.data_ptr<int>(),
-                             sorted_tok.data_ptr<int>(), inv_pos.data_ptr<int>(), stream());
 }
 
 int64_t moe_align(const Tensor& topk_ids, int64_t num_experts, int64_t block_n, const Tensor& grp_rows,
@@ -1108,8 +1091,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_act_fp8", &quant_act_fp8);
   m.def("quant_weight_fp8", &quant_weight_fp8);
   m.def("mla_decode", &mla_decode);
-  m.def("moe_route_align", &moe_route_align);
   m.def("kv8_gather", &kv8_gather);
+  m.def("l2_prefetch", &l2_prefetch);
   m.def("mla_fp8_ctas_per_sm", [](int64_t heads) { return sp::mla_fp8_ctas_per_sm((int)heads); });
   m.def("mla_decode_sk", &mla_decode_sk);
   m.def("mla_sk_supported", [](int64_t B, int64_t H) { return sp::mla_sk_supported((int)B, (int)H); });

@@ -37,7 +37,6 @@ __all__ = [
     "prefill_attention",
     "moe_topk",
     "moe_align",
-    "moe_route_align",
     "gather_rows",
     "silu_mul",
     "moe_combine",
@@ -482,6 +481,12 @@ def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=N
     return out
 
 
+def l2_prefetch(t):
+    """Starts background L2 fetches of a contiguous CUDA tensor (a weight read soon)."""
+    kernels().l2_prefetch(t)
+    _count(1)
+
+
 def kv8_gather(cache8, scales, idx, out=None):
     """Dequantised bf16 rows [n, 576] of an fp8 latent cache at row ids ``idx``."""
     if out is None:
@@ -531,37 +536,6 @@ def moe_topk(logits, bias, k, scoring, renorm, scaling, n_shared=0, n_group=1, t
                        splits, int(n_group), int(topk_group), bool(group_top2))
     _count(1)
     return ids, w
-
-
-# SPARKPIPE_MOE_ROUTE_ALIGN=0 keeps decode routing as two launches (top-k, then align).
-_ROUTE_ALIGN = os.environ.get("SPARKPIPE_MOE_ROUTE_ALIGN", "1") != "0"
-
-
-def moe_route_align(logits, bias, k, scoring, renorm, scaling, n_shared, n_group, topk_group, group_top2, block_n):
-    """``moe_topk`` then ``moe_align`` over all E + n_shared experts, in one launch for
-    decode-sized batches (T <= 256); returns (ids, w, grp_rows, grp_tiles, sorted_tok,
-    inv_pos), or None when the shape does not qualify."""
-    if not _ROUTE_ALIGN:
-        return None
-    if isinstance(logits, Slabs):
-        T, E, dev = logits.rows, logits.cols, logits.ws.device
-        src, stride, splits = logits.ws, logits.stride, logits.splits
-    else:
-        T, E, dev = logits.shape[0], logits.shape[1], logits.device
-        src, stride, splits = logits, 0, 1
-    kk = k + n_shared
-    ids = torch.empty(T, kk, dtype=torch.int32, device=dev)
-    w = torch.empty(T, kk, dtype=torch.float32, device=dev)
-    grp_rows = torch.empty(E + n_shared + 1, dtype=torch.int32, device=dev)
-    grp_tiles = torch.empty(E + n_shared + 1, dtype=torch.int32, device=dev)
-    sorted_tok = torch.empty(T * kk, dtype=torch.int32, device=dev)
-    inv_pos = torch.empty(T * kk, dtype=torch.int32, device=dev)
-    if not kernels().moe_route_align(src, bias, ids, w, int(n_shared), int(scoring), bool(renorm), float(scaling), T,
-                                     E, stride, splits, int(n_group), int(topk_group), bool(group_top2), int(block_n),
-                                     grp_rows, grp_tiles, sorted_tok, inv_pos):
-        return None
-    _count(1)
-    return ids, w, grp_rows, grp_tiles, sorted_tok, inv_pos
 
 
 def moe_align(topk_ids, num_experts, block_n):

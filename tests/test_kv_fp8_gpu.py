@@ -202,7 +202,7 @@ def test_fp8_cache_model_decode_tracks_bf16_cache():
                               max_q=n, ctx_slots=ctx_slots, logits_idx=(cu_q[1:] - 1).contiguous())
             outs.append(model.forward(fb, cache).float())
         bt = (torch.arange(S, dtype=torch.int32)[:, None] * 4 + torch.arange(4, dtype=torch.int32)).to(dev)
-        nxt = outs[-1].argmax(-1).int()
+        nxt = ids[:, L - 1].to(dev)  # the same decode inputs for both caches (no argmax near-ties)
         for step in range(3):
             p = L + step
             fb = ForwardBatch(mode="decode", token_ids=nxt, positions=torch.full((S,), p, dtype=torch.int32, device=dev),
