@@ -70,6 +70,7 @@ struct GemmKParams {
   const int* grp_tiles;  // [G+1]
   int num_groups;
   int a_evict_first;  // A is a weight operand: stream it with evict_first and prefetch it before the PDL wait
+  int sched_early;    // MODE_GROUPED: the tile schedule may be read before the PDL wait
   int swiglu;         // grouped: A rows are [64 gate | 64 up] per tile; write silu(gate) * up
   float* ws;          // split-K partial slabs: [splits][N][M] (trans_out) or [splits][M][N], fp32
   long long split_stride;
@@ -369,9 +370,13 @@ __global__ void __launch_bounds__(192, 1)
   // first stages of A before the previous kernel has finished; everything else
   // (B activations, outputs, device-side tile counts) waits for it.
   // (the all-gather operand's warp-wide flag wait needs the whole producer warp past the PDL wait)
-  const bool prefetch_a = (MODE != MODE_GROUPED && MODE != MODE_GROUPED_TM) && p.a_evict_first && !p.tp_ag_flags;
+  // Grouped: the tile count lives in device memory; with sched_early its writer is known
+  // to have finished, so the weight-major grouped producer prefetches too.
+  const bool sched_ready = MODE == MODE_GROUPED && p.sched_early && !p.ep_on;
+  const bool prefetch_a = ((MODE != MODE_GROUPED && MODE != MODE_GROUPED_TM) || sched_ready) && p.a_evict_first &&
+                          !p.tp_ag_flags;
   const bool is_producer = (warp == 0 && lane == 0);
-  if (MODE == MODE_GROUPED || MODE == MODE_GROUPED_TM) griddep_wait();  // the tile count lives in device memory
+  if ((MODE == MODE_GROUPED || MODE == MODE_GROUPED_TM) && !sched_ready) griddep_wait();
   if (threadIdx.x == 0) {
     int nt = p.num_tiles;
     if (MODE == MODE_GROUPED) nt = p.m_tiles * __ldg(p.grp_tiles + p.num_groups);
@@ -763,6 +768,7 @@ int gemm_bf16(const GemmLaunch& g) {
   p.trans_out = g.trans_out; p.out_f32 = g.out_f32;
   p.err = g.err;
   p.a_evict_first = g.a_evict_first;
+  p.sched_early = g.sched_early;
   p.swiglu = g.swiglu;
   if (g.swiglu && g.grouped != 2 && (!g.grouped || !g.trans_out || g.out_f32 || g.M % 128 != 0))
     throw std::runtime_error("gemm: fused SwiGLU needs a grouped, transposed bf16 GEMM with M % 128 == 0");

@@ -56,6 +56,10 @@ struct GemmLaunch {
   const int* grp_tiles = nullptr;  // [num_groups + 1] n-tile prefix counts (for block_n)
   int num_groups = 0;
   int a_evict_first = 0;
+  // grouped (weight-major) only: grp_rows / grp_tiles were written at least two launches
+  // back, so the producer may read the tile schedule and stream the first weight tiles
+  // before the PDL wait (the launch right before it has itself waited for their writer)
+  int sched_early = 0;
   int swiglu = 0;  // grouped only: fused silu(gate) * up epilogue, output [rows, M / 2]
   float* ws = nullptr;        // split-K partial workspace (fp32 slabs)
   long long ws_floats = 0;

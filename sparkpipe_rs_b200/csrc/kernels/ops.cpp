@@ -111,7 +111,7 @@ int64_t gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, 
           int64_t block_n, const c10::optional<Tensor>& grp_rows, const c10::optional<Tensor>& grp_tiles,
           int64_t num_groups, int64_t a_evict_first, int64_t swiglu, int64_t slab_out,
           const std::vector<int64_t>& ep, const c10::optional<Tensor>& comb_dst, const c10::optional<Tensor>& epoch,
-          int64_t ep_layer) {
+          int64_t ep_layer, int64_t sched_early) {
   CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D);
   CHECK_BF16(A); CHECK_BF16(B);
   TORCH_CHECK(D.scalar_type() == at::kBFloat16 || D.scalar_type() == at::kFloat, "D must be bf16 or fp32");
@@ -136,6 +136,7 @@ int64_t gemm(const Tensor& A, const Tensor& B, const Tensor& D, int64_t a_rows, 
     g.num_groups = (int)num_groups;
   }
   g.a_evict_first = (int)a_evict_first;
+  g.sched_early = (int)sched_early;
   g.swiglu = (int)swiglu;
   if (!grp_rows.has_value() && splits != 1) {
     g.ws = split_ws();

@@ -351,16 +351,18 @@ class MLAMoEModel:
         E, k, F, S = c.n_routed_experts, c.num_experts_per_tok, c.moe_intermediate_size, c.n_shared_experts
         kk = k + S
         bn = _moe_block_n(T * kk, E + S)
+        # align -> gather -> w13 -> w2: the schedule is two or more launches old at each
+        # expert GEMM, which may then stream weights before its dependency wait
         xs = ops.gather_rows(xn, sorted_tok)
         if self.fused_swiglu:
             act = torch.empty(T * kk, F, dtype=torch.bfloat16, device=self.device)
-            ops.grouped_gemm(w[p + "e_w13"], xs, act, grp_rows, grp_tiles, E + S, bn, swiglu=True)
+            ops.grouped_gemm(w[p + "e_w13"], xs, act, grp_rows, grp_tiles, E + S, bn, swiglu=True, sched_early=True)
         else:
             h13 = torch.empty(T * kk, 2 * F, dtype=torch.bfloat16, device=self.device)
-            ops.grouped_gemm(w[p + "e_w13"], xs, h13, grp_rows, grp_tiles, E + S, bn)
+            ops.grouped_gemm(w[p + "e_w13"], xs, h13, grp_rows, grp_tiles, E + S, bn, sched_early=True)
             act = ops.silu_mul(h13)
         y = torch.empty(T * kk, c.hidden_size, dtype=torch.bfloat16, device=self.device)
-        ops.grouped_gemm(w[p + "e_w2"], act, y, grp_rows, grp_tiles, E + S, bn)
+        ops.grouped_gemm(w[p + "e_w2"], act, y, grp_rows, grp_tiles, E + S, bn, sched_early=True)
         # the weighted combine is fused into the next residual add + RMSNorm
         return ("combine", y, inv_pos, wts, kk)
 

@@ -91,7 +91,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, d: torch.Tensor, *, M: int, N: int, K
          b_row0: int = 0, b_batch_rows: int = 0, b_k0: int = 0, b_batch_k: int = 0, ldd: int | None = None,
          d_batch_stride: int = 0, splits: int = 0, block_n: int = 0, grp_rows=None, grp_tiles=None,
          num_groups: int = 0, a_evict_first: bool = False, swiglu: bool = False, slab_out: bool = False,
-         ep_combine=None):
+         ep_combine=None, sched_early: bool = False):
     """Raw tcgen05 GEMM: D[m, n] = sum_k A[m, k] B[n, k] (see gemm_tcgen05.cu).
     ``ep_combine`` = (EP argument vector, comb_dst, epoch, MoE layer) sends a grouped
     GEMM's output rows straight to their source ranks' combine slots (D unused).
@@ -107,7 +107,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, d: torch.Tensor, *, M: int, N: int, K
     r = kernels().gemm(a, b, d, ar, ac, lda, br, bc, ldb, ldd, d_batch_stride, M, N, K, batch, a_row0,
                        a_batch_rows, a_k0, a_batch_k, b_row0, b_batch_rows, b_k0, b_batch_k, int(trans_out),
                        splits, block_n, grp_rows, grp_tiles, num_groups, int(a_evict_first), int(swiglu),
-                       int(slab_out), ep_args, comb_dst, epoch, ep_layer)
+                       int(slab_out), ep_args, comb_dst, epoch, ep_layer, int(sched_early))
     if r < 0:
         _count(1)
         return r
@@ -176,12 +176,14 @@ def batched_gemm(a, b, d, *, M, N, K, batch, a_row0=0, a_batch_rows=0, a_k0=0, a
 
 def grouped_gemm(w: torch.Tensor, x_sorted: torch.Tensor, out: torch.Tensor, grp_rows: torch.Tensor,
                  grp_tiles: torch.Tensor, num_groups: int, block_n: int, swiglu: bool = False,
-                 ep_combine=None) -> torch.Tensor:
+                 ep_combine=None, sched_early: bool = False) -> torch.Tensor:
     """MoE expert GEMM: out[r] = W[g(r)] @ x_sorted[r] for rows r sorted by group.
 
     w is [G, M, K] (or its [G*M, K] view), x_sorted [R, K], out [R, M]. With
     swiglu, w holds per 128-row tile 64 gate rows then the 64 matching up rows
     (see ``interleave_gate_up``) and out [R, M/2] receives silu(gate) * up.
+    ``sched_early``: grp_rows / grp_tiles were written at least two launches before
+    this one, so the kernel streams its first weight tiles before its dependency wait.
     """
     if w.dim() == 3:
         G, M, K = w.shape
@@ -192,8 +194,12 @@ def grouped_gemm(w: torch.Tensor, x_sorted: torch.Tensor, out: torch.Tensor, grp
         K = w.shape[1]
     gemm(w2, x_sorted, out, M=M, N=x_sorted.shape[0], K=K, trans_out=True, a_batch_rows=M, block_n=block_n,
          grp_rows=grp_rows, grp_tiles=grp_tiles, num_groups=num_groups, a_evict_first=True, swiglu=swiglu,
-         ep_combine=ep_combine)
+         ep_combine=ep_combine, sched_early=sched_early and ep_combine is None and _SCHED_EARLY)
     return out
+
+
+# SPARKPIPE_GROUPED_EARLY=0: grouped GEMMs read their tile schedule after the PDL wait only.
+_SCHED_EARLY = os.environ.get("SPARKPIPE_GROUPED_EARLY", "1") != "0"
 
 
 def grouped_gemm_tm(w: torch.Tensor, x_sorted: torch.Tensor, out: torch.Tensor, grp_rows: torch.Tensor,

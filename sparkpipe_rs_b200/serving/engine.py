@@ -78,6 +78,8 @@ class EngineConfig:
     spec_row_cap: int = 0             # firing rows of a verify round (0: rows per lane x max_batch)
     host_kv_blocks: int = 0           # host KV tier: preempted sequences swap their KV out (0: recompute)
     host_prefix_blocks: int = 0       # host KV tier for prefix blocks evicted from the device (0: drop them)
+    host_resident_blocks: int = 0     # pinned buffers behind the host tier's slots (0: one per slot)
+    host_drive_path: str = ""         # with fewer resident buffers than slots: the drive file the rest spill to
     kv_cache_dtype: str = "bf16"      # "fp8": e4m3 latent rows with per-128 block scales (CUDA, 576-wide rows)
     warm_prefill: bool = True         # one throwaway prefill of the largest chunk at start (allocator warm-up)
 
@@ -252,7 +254,15 @@ class LLMEngine:
         if e.host_kv_blocks or sc.host_prefix_blocks:
             from .kv_offload import HostKvTier
 
-            self.host_tier = HostKvTier(self.cache, e.host_kv_blocks + sc.host_prefix_blocks)
+            slots = e.host_kv_blocks + sc.host_prefix_blocks
+            drive = None
+            if e.host_resident_blocks and e.host_resident_blocks < slots:
+                from .kv_offload import DriveSpill
+
+                probe = HostKvTier(self.cache, 1)
+                drive = DriveSpill(probe.block_bytes, slots, path=e.host_drive_path or None)
+                del probe
+            self.host_tier = HostKvTier(self.cache, slots, resident_blocks=e.host_resident_blocks, drive=drive)
         self.graphs: dict[int, DecodeGraph] = {}
         self.verify_rounds: dict[int, VerifyRound] = {}
         self._cost_ema: dict[tuple[int, int], float] = {}

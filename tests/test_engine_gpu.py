@@ -100,3 +100,31 @@ def test_swapped_sequences_resume_from_the_host_tier():
     _check_near_argmax(model, prompts, [o.token_ids for o in res.outputs], tol=0.25)
     tight.shutdown()
     roomy.shutdown()
+
+
+@pytest.mark.parametrize("kv_dtype", ["bf16", "fp8"])
+def test_drive_backed_host_tier_round_trip_on_the_gpu_cache(tmp_path, kv_dtype):
+    """Host slots over 2 pinned buffers and a drive file: device blocks evicted in
+    pieces spill through the NVMe tier and come back bit-exact into other blocks (the
+    fp8 cache moves its block scales with its rows)."""
+    from sparkpipe_rs_b200.models.mla_moe import KVCache
+    from sparkpipe_rs_b200.serving.kv_offload import DriveSpill, HostKvTier
+
+    cfg = _cfg()
+    cache = KVCache(cfg, num_blocks=12, block_size=64, device="cuda", kv_dtype=kv_dtype)
+    for t in cache.planes():
+        t.view(torch.uint8).copy_(torch.randint(0, 120, t.view(torch.uint8).shape, dtype=torch.uint8))
+    probe = HostKvTier(cache, 1)
+    drive = DriveSpill(probe.block_bytes, 8, path=str(tmp_path / "spill.bin"))
+    tier = HostKvTier(cache, 8, max_batch_blocks=2, resident_blocks=2, drive=drive)
+    src, dst = [1, 4, 7, 9, 10], [8, 2, 11, 0, 3]
+    before = [[t[:, b * 64:(b + 1) * 64].clone() for t in cache.planes()] for b in src]
+    tier.evict_to(src, [5, 0, 3, 6, 1])
+    for t in cache.planes():
+        t.zero_()
+    tier.restore([5, 0, 3, 6, 1], dst)
+    torch.cuda.synchronize()
+    for want, b in zip(before, dst):
+        for w, t in zip(want, cache.planes()):
+            assert torch.equal(t[:, b * 64:(b + 1) * 64], w)
+    assert tier.spilled_blocks >= 3 and tier.fetched_blocks >= 3
