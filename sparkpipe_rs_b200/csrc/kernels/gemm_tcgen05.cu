@@ -106,12 +106,11 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // Split-K CTAs with wide token tiles keep a short pipeline (two CTAs per SM, so under
-  // PDL the next kernel's CTAs can become resident beside them). Decode-width split-K
-  // (BN <= 64: a stream-K CTA streams ~16 weight K-blocks) keeps 8 stages in flight:
-  // with 4 (96 KB) a CTA's weight stream ran at ~35 GB/s, 28 % of HBM over the SMs
-  // (ncu, 64 tokens x 9792 x 2048), bounded by bytes in flight per SM.
-  static constexpr int STAGES = MODE == MODE_SPLITK ? (BN <= 64 ? 8 : 4) : (BN >= 256 ? 4 : (BN >= 128 ? 6 : 8));
+  // split-K CTAs own only a few K blocks: a short pipeline keeps two CTAs per SM, so
+  // under PDL the next kernel's CTAs can become resident beside them. (Eight stages for
+  // decode-width split-K measured no faster: 16.6 vs 16.4 us at 64 x 9792 x 2048, so
+  // bytes in flight do not bound it.)
+  static constexpr int STAGES = MODE == MODE_SPLITK ? 4 : (BN >= 256 ? 4 : (BN >= 128 ? 6 : 8));
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int XBUF_BYTES = 64 * 17 * 4;  // SwiGLU exchange buffer (64 rows x 16 cols, padded)
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + XBUF_BYTES;

@@ -204,8 +204,6 @@ int mla_fp8_ctas_per_sm(int heads);
 void mla_combine(const float* o_part, const float* lse_part, void* out, int B, int H, int splits, cudaStream_t s);
 // out[r, :] = dequantised fp8 cache row idx[r] (bf16 [n, 576]).
 void kv8_gather(const void* cache8, const float* scales, const int* idx, void* out, int n, cudaStream_t s);
-// Background L2 prefetch of [p, p + bytes) (16-byte aligned start; the tail under 16 bytes is skipped).
-void l2_prefetch(const void* p, long long bytes, cudaStream_t s);
 // Stream-K decode kernel (mla_decode_sk.cu): one CTA per SM over the flattened KV units.
 // Scratch: o_part [segments][heads per CTA][512] fp32, lse_part [segments][heads per CTA],
 // counters [(H / heads per CTA) * B] int32 zeroed once (the kernel leaves them zero).

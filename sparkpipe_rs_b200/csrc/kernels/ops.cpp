@@ -492,12 +492,6 @@ void mla_decode(const Tensor& q, const Tensor& cache, const Tensor& block_table,
   }
 }
 
-void l2_prefetch(const Tensor& t) {
-  CHECK_CUDA(t); CHECK_CONTIG(t);
-  const c10::cuda::CUDAGuard guard(t.device());
-  sp::l2_prefetch(t.data_ptr(), (long long)(t.numel() * t.element_size()), stream());
-}
-
 void kv8_gather(const Tensor& cache8, const Tensor& scales, const Tensor& idx, const Tensor& out) {
   CHECK_CUDA(cache8); CHECK_I32(idx); CHECK_BF16(out); CHECK_CONTIG(idx); CHECK_CONTIG(out);
   CHECK_ON(cache8, idx); CHECK_ON(cache8, out);
@@ -1093,7 +1087,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_weight_fp8", &quant_weight_fp8);
   m.def("mla_decode", &mla_decode);
   m.def("kv8_gather", &kv8_gather);
-  m.def("l2_prefetch", &l2_prefetch);
   m.def("mla_fp8_ctas_per_sm", [](int64_t heads) { return sp::mla_fp8_ctas_per_sm((int)heads); });
   m.def("mla_decode_sk", &mla_decode_sk);
   m.def("mla_sk_supported", [](int64_t B, int64_t H) { return sp::mla_sk_supported((int)B, (int)H); });

@@ -270,35 +270,6 @@ void kv_blocks_copy(void* cache, long long layer_stride, const int* blocks, int 
            layer_stride, blocks, static_cast<bf16*>(staging), layers, block_size, row, to_staging);
 }
 
-// Warms L2 with a weight the step will read soon: each thread issues bulk L2
-// prefetches (cp.async.bulk.prefetch.L2) for its 64 KB pieces of the range and
-// exits; the fetches complete in the background while the next kernels run. Used
-// ahead of a latency-bound kernel that leaves HBM bandwidth idle (MLA decode), for
-// the weight of the GEMM after it. Stream order only: nothing waits for the fetches.
-__global__ void l2_prefetch_kernel(const char* __restrict__ p, long long bytes) {
-  // The fetches go out before the dependency wait (the weight does not depend on the
-  // previous kernel); the wait stays, so this grid completes only after its
-  // predecessor and the kernel after it still sees every earlier result.
-  griddep_launch();
-  constexpr long long PIECE = 64 * 1024;
-  const long long n = (bytes + PIECE - 1) / PIECE;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const long long off = i * PIECE;
-    const unsigned len = (unsigned)((bytes - off < PIECE ? bytes - off : PIECE) & ~15ll);
-    if (len) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + off), "r"(len) : "memory");
-  }
-  griddep_wait();
-}
-
-void l2_prefetch(const void* p, long long bytes, cudaStream_t s) {
-  if (bytes < 16) return;
-  if (reinterpret_cast<uintptr_t>(p) & 15) throw std::runtime_error("l2_prefetch: 16-byte aligned ranges only");
-  const long long pieces = (bytes + 65535) / 65536;
-  const int threads = (int)std::min<long long>(256, pieces);
-  const int blocks = (int)std::min<long long>(16, (pieces + threads - 1) / threads);
-  launch_k(l2_prefetch_kernel, dim3(blocks), dim3(threads), 0, s, static_cast<const char*>(p), bytes);
-}
-
 // Phase clock: one thread stamps the device's global timer (ns) into slot `slot`
 // of a step's clock array and adds the time since slot `prev`'s stamp to the
 // phase's running total. Stream-ordered with the kernels around it (it waits for

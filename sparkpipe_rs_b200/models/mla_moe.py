@@ -146,10 +146,6 @@ ROUTER_FUSED_MAX_TOKENS = 256 if os.environ.get("SPARKPIPE_FUSED_ROUTER", "0") =
 # SPARKPIPE_MOE_TOKEN_MAJOR=0 keeps the weight-major (swap-AB) one everywhere.
 MOE_TOKEN_MAJOR_MIN_ROWS = 256 if os.environ.get("SPARKPIPE_MOE_TOKEN_MAJOR", "1") != "0" else 1 << 62
 ROUTER_FUSED_MAX_WEIGHTS = 1 << 20
-# Decode: start L2 fetches of the absorbed output projection's weight (33.5 MB on the
-# V2-Lite shape) before the MLA attention kernel, which leaves HBM bandwidth idle;
-# SPARKPIPE_L2_PREFETCH=0 turns it off.
-L2_PREFETCH_OPROJ = os.environ.get("SPARKPIPE_L2_PREFETCH", "1") != "0"
 
 
 def _moe_block_n(rows: int, experts: int) -> int:
@@ -242,8 +238,6 @@ class MLAMoEModel:
             ops.mla_decode_prep(qkv, w[p + "kv_a_norm"], fb.positions, self.cos_sin, fb.slot_mapping, layer_cache,
                                 None, q_lat, kvl, 0, nh * c.kv_cache_dim, c.rms_norm_eps, kv_scales)
             o_lat = torch.empty(T, nh, kvl, dtype=torch.bfloat16, device=self.device)
-            if L2_PREFETCH_OPROJ and isinstance(w[p + "w_ov"], torch.Tensor):
-                ops.l2_prefetch(w[p + "w_ov"])  # fetched while the latency-bound attention runs
             ops.mla_decode(q_lat, layer_cache, fb.block_table, fb.context_lens, o_lat, fb.decode_splits, self.scale,
                            last_slot=fb.self_slots, kv_scales=kv_scales)
             return self._lin(o_lat.view(T, nh * kvl), w[p + "w_ov"], slab=True)

@@ -487,12 +487,6 @@ def mla_decode(q, cache, block_table, context_lens, out, splits, scale, o_part=N
     return out
 
 
-def l2_prefetch(t):
-    """Starts background L2 fetches of a contiguous CUDA tensor (a weight read soon)."""
-    kernels().l2_prefetch(t)
-    _count(1)
-
-
 def kv8_gather(cache8, scales, idx, out=None):
     """Dequantised bf16 rows [n, 576] of an fp8 latent cache at row ids ``idx``."""
     if out is None:

@@ -69,6 +69,9 @@ def main():
             us = time_fn(lambda i: ops.linear(x, ws[i % n_pool], out=out, splits=sp), args.iters)
             print(f"linear T={T:5d} O={O:6d} K={K:6d} splits={sp}: {us:8.2f} us  "
                   f"{wbytes / us / 1e6:6.2f} TB/s  {flops / us / 1e6:8.1f} TFLOP/s")
+        # the model's form at decode: partial slabs left for the consuming kernel (one launch)
+        us = time_fn(lambda i: ops.linear_slabs(x, ws[i % n_pool], out_dtype=torch.float32), args.iters)
+        print(f"linear_slabs T={T:5d} O={O:6d} K={K:6d}: {us:8.2f} us  {wbytes / us / 1e6:6.2f} TB/s")
         us = time_fn(lambda i: torch.matmul(x, ws[i % n_pool].t(), out=out), args.iters)
         print(f"torch.matmul (cuBLAS) T={T:5d} O={O:6d} K={K:6d}: {us:8.2f} us  {wbytes / us / 1e6:6.2f} TB/s  "
               f"{flops / us / 1e6:8.1f} TFLOP/s")

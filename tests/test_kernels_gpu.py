@@ -563,20 +563,3 @@ def test_moe_route_fused_matches_gemm_router(scoring, E, k, groups):
     _close(w[:, :k].gather(1, order), w2[:, :k].gather(1, order2), atol=1e-4, rtol=1e-3)
     _status_ok()
 
-
-def test_l2_prefetch_leaves_data_and_order_intact():
-    """Bulk L2 prefetches of a weight-sized range (not a multiple of the 64 KB piece nor
-    of 16 bytes at the tail) are hints: the tensor is unchanged, a kernel launched after
-    them still sees the previous kernel's result, and the status word stays clean."""
-    ops = _ops()
-    g = torch.Generator(device=DEV).manual_seed(3)
-    w = torch.randn(40 * 1024 * 1024 // 2 + 37, device=DEV, generator=g).bfloat16()
-    before = w.clone()
-    x = torch.randn(64, 2048, device=DEV, generator=g).bfloat16()
-    y = torch.empty_like(x)
-    ops.add_rmsnorm(x, None, torch.ones(2048, device=DEV, dtype=torch.bfloat16), y, 1e-6)
-    ops.l2_prefetch(w)
-    z = ops.gather_rows(y, torch.arange(64, device=DEV, dtype=torch.int32))
-    torch.cuda.synchronize()
-    assert torch.equal(w, before) and torch.equal(z, y)
-    _status_ok()
