@@ -275,7 +275,8 @@ void moe_topk(const float* logits, long long slab_stride, int splits, const floa
               const void* gate_w = nullptr, int H = 0);
 // res[t] += sum_j w[t, j] * y[inv_pos[t*k + j]]; out[t] = rmsnorm(res[t]) * gamma
 void combine_add_rmsnorm(const void* y, long long ldy, const int* inv_pos, const float* topk_w, void* residual,
-                         const void* gamma, void* out, long long ldo, int T, int k, int H, float eps, cudaStream_t s);
+                         const void* gamma, void* out, long long ldo, int T, int k, int H, float eps, cudaStream_t s,
+                         const void* shared = nullptr, long long ld_shared = 0, int n_shared = 0);
 // Builds the expert-sorted row layout: counts -> grp_rows [E+1], grp_tiles [E+1]
 // (n-tiles of width block_n), sorted_tok [T*k] (source token of each sorted row),
 // inv_pos [T*k] (sorted row of pair (t, j)). `work` is E ints of scratch.

@@ -533,7 +533,7 @@ void moe_combine(const void* y, long long ldy, const int* inv_pos, const float* 
 __global__ void __launch_bounds__(256) combine_add_rmsnorm_kernel(
     const bf16* __restrict__ y, long long ldy, const int* __restrict__ inv_pos, const float* __restrict__ w,
     bf16* __restrict__ res, const bf16* __restrict__ gamma, bf16* __restrict__ out, long long ldo, int k, int H,
-    float eps) {
+    float eps, const bf16* __restrict__ sh, long long ldsh, int n_sh, int T) {
   griddep_wait();
   griddep_launch();
   const int t = blockIdx.x;
@@ -571,6 +571,13 @@ __global__ void __launch_bounds__(256) combine_add_rmsnorm_kernel(
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] += s_w[j] * yv[e];
       }
+      // shared experts computed apart (rows s * T + t of sh, weight 1), after the routed ones
+      for (int q = 0; q < n_sh; ++q) {
+        float yv[8];
+        ld_bf16x8(sh + ((long long)q * T + t) * ldsh + c, yv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += yv[e];
+      }
       float r[8];
       ld_bf16x8(rr + c, r);
 #pragma unroll
@@ -603,12 +610,14 @@ __global__ void __launch_bounds__(256) combine_add_rmsnorm_kernel(
 }
 
 void combine_add_rmsnorm(const void* y, long long ldy, const int* inv_pos, const float* topk_w, void* residual,
-                         const void* gamma, void* out, long long ldo, int T, int k, int H, float eps, cudaStream_t s) {
+                         const void* gamma, void* out, long long ldo, int T, int k, int H, float eps, cudaStream_t s,
+                         const void* shared, long long ld_shared, int n_shared) {
   if (T <= 0) return;
   if (k > COMBINE_MAXK) throw std::runtime_error("combine_add_rmsnorm: k <= 32");
   if (H % 8 || H > 8192) throw std::runtime_error("combine_add_rmsnorm: hidden % 8, <= 8192");
   launch_k(combine_add_rmsnorm_kernel, dim3(T), dim3(256), 0, s, (const bf16*)y, ldy, inv_pos, topk_w,
-           (bf16*)residual, (const bf16*)gamma, (bf16*)out, ldo, k, H, eps);
+           (bf16*)residual, (const bf16*)gamma, (bf16*)out, ldo, k, H, eps, (const bf16*)shared, ld_shared,
+           shared ? n_shared : 0, T);
 }
 
 void kernel_attrs_moe(std::vector<KernelAttr>& out) {

@@ -649,13 +649,27 @@ void mla_decode_prep(const c10::optional<Tensor>& slabs, int64_t stride, int64_t
 }
 
 void combine_add_rmsnorm(const Tensor& y, const Tensor& inv_pos, const Tensor& w, const Tensor& residual,
-                         const Tensor& gamma, const Tensor& out, int64_t k, double eps) {
+                         const Tensor& gamma, const Tensor& out, int64_t k, double eps,
+                         const c10::optional<Tensor>& shared) {
   CHECK_CUDA(y); CHECK_BF16(y); CHECK_I32(inv_pos); CHECK_F32(w); CHECK_BF16(residual); CHECK_CONTIG(residual);
   CHECK_BF16(gamma); CHECK_BF16(out);
+  const int64_t T = residual.size(0);
+  const void* sh = nullptr;
+  long long ldsh = 0;
+  int nsh = 0;
+  if (shared.has_value()) {  // [S * T, H] rows s * T + t: the shared experts' outputs, weight 1
+    CHECK_BF16(*shared); CHECK_ON(y, *shared);
+    TORCH_CHECK(shared->dim() == 2 && shared->stride(1) == 1 && shared->size(1) == residual.size(1) && T > 0 &&
+                    shared->size(0) % T == 0,
+                "combine_add_rmsnorm: shared rows [S * T, H]");
+    sh = shared->data_ptr();
+    ldsh = shared->stride(0);
+    nsh = (int)(shared->size(0) / T);
+  }
   const c10::cuda::CUDAGuard guard(y.device());
   sp::combine_add_rmsnorm(y.data_ptr(), y.stride(0), inv_pos.data_ptr<int>(), w.data_ptr<float>(), residual.data_ptr(),
-                          gamma.data_ptr(), out.data_ptr(), out.stride(0), (int)residual.size(0), (int)k,
-                          (int)residual.size(1), (float)eps, stream());
+                          gamma.data_ptr(), out.data_ptr(), out.stride(0), (int)T, (int)k,
+                          (int)residual.size(1), (float)eps, stream(), sh, ldsh, nsh);
 }
 
 Tensor split_workspace() {

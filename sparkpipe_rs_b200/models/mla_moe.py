@@ -145,6 +145,10 @@ ROUTER_FUSED_MAX_TOKENS = 256 if os.environ.get("SPARKPIPE_FUSED_ROUTER", "0") =
 # grouped GEMM (tokens as M, row-major output, SwiGLU paired in registers);
 # SPARKPIPE_MOE_TOKEN_MAJOR=0 keeps the weight-major (swap-AB) one everywhere.
 MOE_TOKEN_MAJOR_MIN_ROWS = 256 if os.environ.get("SPARKPIPE_MOE_TOKEN_MAJOR", "1") != "0" else 1 << 62
+# Decode-sized local MoE runs the shared experts on a forked stream, overlapping the
+# routing kernels; SPARKPIPE_SHARED_SIDE_STREAM=0 keeps them as extra groups of the
+# routed grouped GEMMs.
+SHARED_SIDE_STREAM = os.environ.get("SPARKPIPE_SHARED_SIDE_STREAM", "1") != "0"
 ROUTER_FUSED_MAX_WEIGHTS = 1 << 20
 
 
@@ -173,6 +177,8 @@ class MLAMoEModel:
         derive_decode_weights(cfg, self.w)
         # latent up-projections folded into the decode projections (SPARKPIPE_ABSORB=0: the four-GEMM form)
         self.absorbed = os.environ.get("SPARKPIPE_ABSORB", "1") != "0" and absorb_decode_weights(cfg, self.w)
+        self._side = None           # forked stream of the shared experts (decode MoE)
+        self._shared_tables = {}    # (T, bn) -> shared experts' row / tile prefix tables
         # routed + shared expert gate/up weights in the fused-SwiGLU tile order
         self.fused_swiglu = cfg.moe_intermediate_size % 64 == 0
         for i in range(cfg.num_layers):
@@ -306,6 +312,10 @@ class MLAMoEModel:
                                      c.routed_scaling_factor, **route)
         else:
             logits = ops.linear_slabs(xn, gate, out_dtype=torch.float32)
+            if (SHARED_SIDE_STREAM and S and self.ep is None and self.fused_swiglu
+                    and not isinstance(w[p + "e_w13"], ops.Fp8Weight)
+                    and T * (k + S) < MOE_TOKEN_MAJOR_MIN_ROWS * (E + S)):
+                return self._moe_shared_apart(i, xn, logits, bias, sigmoid, route)
             ids, wts = ops.moe_topk(logits, bias, k, 1 if sigmoid else 0, c.norm_topk_prob, c.routed_scaling_factor,
                                     **route)
         kk = k + S
@@ -335,6 +345,63 @@ class MLAMoEModel:
             return ("combine", y, inv_pos, wts, kk)
         grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E + S, bn)
         return self._moe_grouped(i, xn, wts, grp_rows, grp_tiles, sorted_tok, inv_pos)
+
+    def _shared_layout(self, T: int, bn: int):
+        """Row / tile prefix tables of the shared experts taking all T tokens each
+        (cached per (T, bn); first built in a step's eager warm-up, outside capture)."""
+        key = (T, bn)
+        if key not in self._shared_tables:
+            S = self.cfg.n_shared_experts
+            nt = -(-T // bn)
+            rows = torch.tensor([s * T for s in range(S + 1)], dtype=torch.int32, device=self.device)
+            tiles = torch.tensor([s * nt for s in range(S + 1)], dtype=torch.int32, device=self.device)
+            self._shared_tables[key] = (rows, tiles)
+        return self._shared_tables[key]
+
+    def _moe_shared_apart(self, i, xn, logits, bias, sigmoid, route):
+        """Decode-sized local MoE with the shared experts on a forked stream: their two
+        GEMMs (which need only xn) stream their weights while the main stream routes the
+        tokens and builds the expert-sorted layout; the routed grouped GEMMs cover the E
+        routed experts and the combine adds the shared rows."""
+        c, w = self.cfg, self.w
+        p = f"l{i}."
+        T = xn.shape[0]
+        E, k, F, S = c.n_routed_experts, c.num_experts_per_tok, c.moe_intermediate_size, c.n_shared_experts
+        main = torch.cuda.current_stream(self.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        side = self._side
+        fork = torch.cuda.Event()
+        fork.record(main)
+        side.wait_event(fork)
+        bn_s = _moe_block_n(T * S, S)
+        rows_s, tiles_s = self._shared_layout(T, bn_s)  # static tables, built in the eager warm-up
+        # buffers come from the main stream's pool: the main stream waits for the fork's
+        # end before any of them is used or freed there
+        xs_s = xn if S == 1 else torch.empty(S * T, xn.shape[1], dtype=xn.dtype, device=self.device)
+        act_s = torch.empty(S * T, F, dtype=torch.bfloat16, device=self.device)
+        y_s = torch.empty(S * T, c.hidden_size, dtype=torch.bfloat16, device=self.device)
+        w13, w2 = w[p + "e_w13"], w[p + "e_w2"]
+        w13_s = w13[E:E + S] if w13.dim() == 3 else w13[E * (w13.shape[0] // (E + S)):]
+        w2_s = w2[E:E + S] if w2.dim() == 3 else w2[E * (w2.shape[0] // (E + S)):]
+        with torch.cuda.stream(side):
+            for q in range(S if S > 1 else 0):
+                xs_s[q * T:(q + 1) * T].copy_(xn)
+            ops.grouped_gemm(w13_s, xs_s, act_s, rows_s, tiles_s, S, bn_s, swiglu=True, sched_early=True)
+            ops.grouped_gemm(w2_s, act_s, y_s, rows_s, tiles_s, S, bn_s, sched_early=True)
+            join = torch.cuda.Event()
+            join.record(side)
+        route = dict(route, n_shared=0)
+        ids, wts = ops.moe_topk(logits, bias, k, 1 if sigmoid else 0, c.norm_topk_prob, c.routed_scaling_factor,
+                                **route)
+        bn = _moe_block_n(T * k, E)
+        grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E, bn)
+        xs = ops.gather_rows(xn, sorted_tok)
+        act = torch.empty(T * k, F, dtype=torch.bfloat16, device=self.device)
+        ops.grouped_gemm(w[p + "e_w13"], xs, act, grp_rows, grp_tiles, E, bn, swiglu=True, sched_early=True)
+        y = torch.empty(T * k, c.hidden_size, dtype=torch.bfloat16, device=self.device)
+        ops.grouped_gemm(w[p + "e_w2"], act, y, grp_rows, grp_tiles, E, bn, sched_early=True)
+        return ("combine", y, inv_pos, wts, k, y_s, join)
 
     def _moe_grouped(self, i, xn, wts, grp_rows, grp_tiles, sorted_tok, inv_pos):
         """Weight-major grouped expert GEMMs over the expert-sorted rows; returns the
@@ -368,6 +435,10 @@ class MLAMoEModel:
             ops.add_rmsnorm(res, None, gamma, xn, eps)
         elif isinstance(pending, tuple) and pending[0] == "ep_combine":
             pending[1].combine_add_rmsnorm(pending[2], pending[3], res, gamma, xn, eps)
+        elif isinstance(pending, tuple) and len(pending) == 7:  # shared experts from the forked stream
+            _, y, inv_pos, wts, kk, y_s, join = pending
+            torch.cuda.current_stream(self.device).wait_event(join)
+            ops.combine_add_rmsnorm(y, inv_pos, wts, res, gamma, xn, kk, eps, shared=y_s)
         elif isinstance(pending, tuple):
             _, y, inv_pos, wts, kk = pending
             ops.combine_add_rmsnorm(y, inv_pos, wts, res, gamma, xn, kk, eps)

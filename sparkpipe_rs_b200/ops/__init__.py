@@ -659,8 +659,10 @@ def mla_decode_prep(qkv, norm_w, positions, cos_sin, slot_mapping, cache, q_nope
     _count(1)
 
 
-def combine_add_rmsnorm(y, inv_pos, w, residual, gamma, out, k, eps):
-    kernels().combine_add_rmsnorm(y, inv_pos, w, residual, gamma, out, int(k), float(eps))
+def combine_add_rmsnorm(y, inv_pos, w, residual, gamma, out, k, eps, shared=None):
+    """residual[t] += sum_j w[t, j] * y[inv_pos[t, j]] (+ the shared experts' rows
+    shared[s * T + t], weight 1); out[t] = rmsnorm(residual[t]) * gamma."""
+    kernels().combine_add_rmsnorm(y, inv_pos, w, residual, gamma, out, int(k), float(eps), shared)
     _count(1)
     return out
 
