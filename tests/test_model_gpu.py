@@ -143,3 +143,35 @@ def test_fp8_block_model_matches_oracle():
         cur = out.clone()
     dg.release()
     assert ops.status_word() == 0
+
+
+@pytest.mark.parametrize("shared", [1, 2])
+def test_shared_experts_on_a_forked_stream_match_grouped(shared, monkeypatch):
+    """Decode steps with the shared experts on the forked stream (their own grouped GEMMs,
+    joined before the combine) equal the steps that run them as extra groups of the
+    routed GEMMs, eagerly and replayed from a CUDA graph (fork / join captured)."""
+    from sparkpipe_rs_b200.models import mla_moe
+    from sparkpipe_rs_b200.models.mla_moe import DecodeGraph, KVCache
+
+    cfg = small_cfg().replace(n_shared_experts=shared)
+    model, _, _ = _setup(cfg)
+    B, ctx = 24, 130
+    outs = {}
+    for side in (False, True):
+        monkeypatch.setattr(mla_moe, "SHARED_SIDE_STREAM", side)
+        cache = KVCache(cfg, num_blocks=64, block_size=64, device=DEV)
+        g = torch.Generator(device=DEV).manual_seed(1)
+        cache.data.copy_(torch.randn(cache.data.shape, device=DEV, generator=g).bfloat16())
+        res = []
+        for use_graph in (False, True):
+            dg = DecodeGraph(model, cache, B, 4, 256, use_graph=use_graph)
+            dg.ids.copy_(torch.randint(0, cfg.vocab_size, (B,), device=DEV, generator=g, dtype=torch.int32))
+            dg.block_table.copy_(torch.arange(B * 4, device=DEV, dtype=torch.int32).view(B, 4) % 64)
+            dg.pos.fill_(ctx)
+            dg.ctx.fill_(ctx + 1)
+            dg.slots.fill_(-1)
+            res.append(dg.run().clone())
+            dg.release()
+        outs[side] = res
+    assert torch.equal(outs[True][0], outs[False][0]) and torch.equal(outs[True][1], outs[False][1])
+    assert torch.equal(outs[True][0], outs[True][1])
