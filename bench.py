@@ -148,7 +148,9 @@ def main():
     parallelism = f"dp{world}-ep{world}" if ep is not None else f"dp{world}"
 
     # ------------------------------------------------------------ device-timed decode
-    total_ctx = P + args.warmup + args.steps + 2
+    # the timed steps start at context P; a second timed window runs at mid-output context
+    mid_start = max(P + args.warmup + args.steps, P + args.output // 2)
+    total_ctx = mid_start + args.steps + 2
     bps = math.ceil(total_ctx / bs)
     cache = KVCache(cfg, num_blocks=B * bps, block_size=bs, device=dev)
     block_table = torch.arange(B * bps, dtype=torch.int32, device=dev).view(B, bps)
@@ -208,6 +210,25 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     value = B * world * args.steps / (ms_max / 1000.0)
+    # the same steps at mid-output context (untimed advance, then one more timed window)
+    for _ in range(mid_start - (P + args.warmup + args.steps)):
+        graph.run()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    m0.record()
+    for _ in range(args.steps):
+        graph.run()
+    m1.record()
+    torch.cuda.synchronize()
+    tm = torch.tensor([m0.elapsed_time(m1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    ms_mid = float(tm.item())
+    mid = {"context": mid_start + 1, "ms_per_step": ms_mid / args.steps,
+           "value": B * world * args.steps / (ms_mid / 1000.0)}
     graph.release()
     del graph, cache
     torch.cuda.empty_cache()
@@ -276,6 +297,7 @@ def main():
         }
         if e2e is not None:
             line["e2e"] = e2e
+        line["mid_output"] = mid
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
