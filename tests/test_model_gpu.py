@@ -162,10 +162,11 @@ def test_shared_experts_on_a_forked_stream_match_grouped(shared, monkeypatch):
         cache = KVCache(cfg, num_blocks=64, block_size=64, device=DEV)
         g = torch.Generator(device=DEV).manual_seed(1)
         cache.data.copy_(torch.randn(cache.data.shape, device=DEV, generator=g).bfloat16())
+        ids = torch.randint(0, cfg.vocab_size, (B,), device=DEV, generator=g, dtype=torch.int32)
         res = []
         for use_graph in (False, True):
             dg = DecodeGraph(model, cache, B, 4, 256, use_graph=use_graph)
-            dg.ids.copy_(torch.randint(0, cfg.vocab_size, (B,), device=DEV, generator=g, dtype=torch.int32))
+            dg.ids.copy_(ids)
             dg.block_table.copy_(torch.arange(B * 4, device=DEV, dtype=torch.int32).view(B, 4) % 64)
             dg.pos.fill_(ctx)
             dg.ctx.fill_(ctx + 1)
