@@ -188,7 +188,9 @@ class _StageGraph:
         cur = torch.cuda.current_stream(dev)
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(cur)
-        with torch.cuda.stream(side), torch.cuda.graph(self.graph, stream=side):
+        # thread-local capture: the process group's own threads (NCCL watchdog, gloo
+        # workers) keep making CUDA calls while this thread captures
+        with torch.cuda.stream(side), torch.cuda.graph(self.graph, stream=side, capture_error_mode="thread_local"):
             self.out = run()
         cur.wait_stream(side)
 
