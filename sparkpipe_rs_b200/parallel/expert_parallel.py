@@ -25,6 +25,8 @@ on a concurrently running one.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from .. import _ext, ops
@@ -100,7 +102,13 @@ class ExpertParallel:
         self.layers_per_step = len(self.moe_layers) + (len(self.moe_layers) & 1)
         self.fp8 = (cfg.weight_dtype == "fp8_block") if fp8_transport is None else bool(fp8_transport)
         self.S = cfg.n_shared_experts
+        # SPARKPIPE_EP_SHARED_LOCAL=1 turns it on where the caller leaves the default
+        shared_local = shared_local or os.environ.get("SPARKPIPE_EP_SHARED_LOCAL", "0") == "1"
         self.shared_local = bool(shared_local) and self.S > 0
+        # SPARKPIPE_EP_SHARED_SIDE=1: local shared experts on a forked stream
+        self.shared_side = os.environ.get("SPARKPIPE_EP_SHARED_SIDE", "0") == "1"
+        self._side = None
+        self._join = None
         self.row_words = row_words(self.H, self.fp8)
         self.layout = ep_layout(world, cap_tokens, self.H, self.kk, self.fp8)
         K = _ext.kernels()
@@ -259,6 +267,9 @@ class ExpertParallel:
     def combine_add_rmsnorm(self, layer: int, wts: torch.Tensor, res: torch.Tensor, gamma: torch.Tensor,
                             out: torch.Tensor, eps: float):
         ys = self.y_sh if self.shared_local and res.shape[0] > 0 else None
+        if self.shared_local and self.shared_side and self._join is not None:
+            torch.cuda.current_stream(self.device).wait_event(self._join)
+            self._join = None
         self.K.ep_combine_add_rmsnorm(self.args(), self.epoch, self.moe_index[layer], wts, res, gamma, out, eps,
                                       self.budget, ys)
         ops._count(1)
@@ -274,7 +285,21 @@ class ExpertParallel:
         if xn.shape[0] > self.cap:
             raise ValueError(f"expert parallel: {xn.shape[0]} tokens exceed the buffer capacity {self.cap}")
         self.dispatch(layer, xn, ids)
-        if self.shared_local:
+        if self.shared_local and self.shared_side:
+            # forked stream: the shared experts' GEMMs stream their weights while the main
+            # stream waits for the routed rows, runs the routed experts and sends them back
+            # (the warm-up keeps its tables built outside capture); joined before the combine
+            main = torch.cuda.current_stream(self.device)
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=self.device)
+            fork = torch.cuda.Event()
+            fork.record(main)
+            self._side.wait_event(fork)
+            with torch.cuda.stream(self._side):
+                self.shared(xn, w13, w2, fused_swiglu)
+                self._join = torch.cuda.Event()
+                self._join.record(self._side)
+        elif self.shared_local:
             self.shared(xn, w13, w2, fused_swiglu)  # runs while the routed rows cross NVLink
         self.receive(layer, bn)
         self.experts(w13, w2, bn, fused_swiglu, layer=layer)  # down projection sends to the source ranks
