@@ -63,6 +63,11 @@ class EngineConfig:
     num_blocks: int = 0               # 0: enough for max_batch full-length sequences
     max_prefill_tokens: int = 16384
     max_consecutive_prefills: int = 4
+    # prefill and decode at equal priority: False = a waiting prompt's prefill goes first
+    # while KV blocks allow it (the reference's rule: prefill wins at equal priority with
+    # resident KV headroom); True = at most max_consecutive_prefills prefill steps while
+    # decodes wait (protects TPOT during a burst of arrivals)
+    prefill_decode_interleave: bool = False
     use_cuda_graph: bool = True
     decode_buckets: tuple = (1, 2, 4, 8, 16, 32, 64, 128, 256)
     prefix_caching: bool = True
@@ -238,6 +243,10 @@ class LLMEngine:
             flags &= ~self.core.SCHED_PREFIX_CACHE
         if not e.chunked_prefill:
             flags &= ~self.core.SCHED_CHUNKED_PREFILL
+        if e.prefill_decode_interleave:
+            flags |= self.core.SCHED_PREFILL_DECODE_INTERLEAVE
+        else:
+            flags &= ~self.core.SCHED_PREFILL_DECODE_INTERLEAVE
         if self.spec:
             sc.spec_mode = self.core.SPEC_CHAIN if self.spec == "chain" else self.core.SPEC_MTP_TREE
             sc.spec_draft_len = e.draft_len
