@@ -421,10 +421,49 @@ __global__ void rope_q_kernel(const bf16* src, long long st, long long sh, int s
   }
 }
 
+// Vector form: one thread rotates 8 consecutive elements (4 pairs) with 16-byte loads and
+// stores and float4 reads of the cos / sin rows (rope % 8 == 0, 16-byte aligned rows).
+// The scalar one above moved 2-byte elements and measured 0.23 of the HBM copy bandwidth
+// on 8,192 tokens x 16 heads x 64 rope dims.
+__global__ void rope_q_vec_kernel(const bf16* src, long long st, long long sh, int so, bf16* dst, long long dt,
+                                  long long dh, int doff, const int* __restrict__ pos, const float* __restrict__ cs,
+                                  int T, int H, int R) {
+  griddep_wait();
+  griddep_launch();
+  const int per = R / 8;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)T * H * per) return;
+  const int c = int(i % per);
+  const long long th = i / per;
+  const int t = int(th / H), h = int(th % H);
+  const float* cp = cs + (long long)pos[t] * R;
+  const uint4 v = *reinterpret_cast<const uint4*>(src + t * st + h * sh + so + c * 8);
+  const float4 cc = *reinterpret_cast<const float4*>(cp + c * 4);
+  const float4 ss = *reinterpret_cast<const float4*>(cp + R / 2 + c * 4);
+  const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+  const float cv[4] = {cc.x, cc.y, cc.z, cc.w}, sv[4] = {ss.x, ss.y, ss.z, ss.w};
+  uint32_t out[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&in[k]));
+    const __nv_bfloat162 y = __floats2bfloat162_rn(x.x * cv[k] - x.y * sv[k], x.x * sv[k] + x.y * cv[k]);
+    out[k] = *reinterpret_cast<const uint32_t*>(&y);
+  }
+  *reinterpret_cast<uint4*>(dst + t * dt + h * dh + doff + c * 8) = make_uint4(out[0], out[1], out[2], out[3]);
+}
+
 void rope_q(const void* src, long long src_tok, long long src_head, int src_off, void* dst, long long dst_tok,
             long long dst_head, int dst_off, const int* positions, const float* cos_sin, int T, int H, int rope,
             cudaStream_t s) {
   if (T <= 0) return;
+  const auto a16 = [](const void* p, long long off) { return ((reinterpret_cast<uintptr_t>(p) + off * 2) & 15) == 0; };
+  if (rope % 8 == 0 && src_tok % 8 == 0 && src_head % 8 == 0 && dst_tok % 8 == 0 && dst_head % 8 == 0 &&
+      a16(src, src_off) && a16(dst, dst_off) && (reinterpret_cast<uintptr_t>(cos_sin) & 15) == 0) {
+    const long long n = (long long)T * H * (rope / 8);
+    launch_k(rope_q_vec_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, (const bf16*)src, src_tok,
+             src_head, src_off, (bf16*)dst, dst_tok, dst_head, dst_off, positions, cos_sin, T, H, rope);
+    return;
+  }
   const int warps = 8;
   const int n = T * H;
   launch_k(rope_q_kernel, dim3((n + warps - 1) / warps), dim3(warps * 32), 0, s, (const bf16*)src, src_tok, src_head,
