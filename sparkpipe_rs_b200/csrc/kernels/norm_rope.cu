@@ -470,36 +470,52 @@ void rope_q(const void* src, long long src_tok, long long src_head, int src_off,
            src_off, (bf16*)dst, dst_tok, dst_head, dst_off, positions, cos_sin, T, H, rope);
 }
 
+// Half a warp per 128-element block: each lane loads 8 elements (16 bytes), the block's
+// amax reduces over its 16 lanes, and each lane stores its 8 e4m3 bytes at once. (One
+// warp per block with 4 elements and 1-byte stores per lane measured 0.39 of the HBM copy
+// bandwidth on 8,192 x 7,168.)
 __global__ void quant_fp8_block_kernel(const bf16* __restrict__ x, long long ldx, __nv_fp8_e4m3* __restrict__ q,
                                        float* __restrict__ scales, int rows, int cols) {
   griddep_wait();
   griddep_launch();
   const int nb = cols / 128;
-  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (w >= rows * nb) return;
-  const int r = w / nb, b = w % nb;
-  const bf16* src = x + (long long)r * ldx + b * 128 + lane * 4;
-  float v[4];
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(src);
-  float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
-  v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
-  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-  amax = warp_max(amax);
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long blk = i >> 4;
+  const int l = int(i & 15);
+  const bool ok = blk < (long long)rows * nb;  // whole half-warps share it: shuffles stay uniform
+  const int r = ok ? int(blk / nb) : 0, b = ok ? int(blk % nb) : 0;
+  float v[8];
+  float amax = 0.f;
+  if (ok) {
+    ld_bf16x8(x + (long long)r * ldx + b * 128 + l * 8, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+  }
+#pragma unroll
+  for (int d = 8; d >= 1; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+  if (!ok) return;
   const float scale = amax > 0.f ? amax / 448.f : 1.f;
   const float inv = 1.f / scale;
-  __nv_fp8_e4m3* dst = q + (long long)r * cols + b * 128 + lane * 4;
+  uint32_t w[2];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) dst[j] = __nv_fp8_e4m3(v[j] * inv);
-  if (lane == 0) scales[(long long)r * nb + b] = scale;
+  for (int k = 0; k < 2; ++k) {
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * k] * inv, v[4 * k + 1] * inv), __NV_SATFINITE,
+                                                 __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * k + 2] * inv, v[4 * k + 3] * inv),
+                                                 __NV_SATFINITE, __NV_E4M3);
+    w[k] = lo | (hi << 16);
+  }
+  *reinterpret_cast<uint2*>(q + (long long)r * cols + b * 128 + l * 8) = make_uint2(w[0], w[1]);
+  if (l == 0) scales[(long long)r * nb + b] = scale;
 }
 
 void quant_fp8_block(const void* x, long long ldx, void* q, float* scales, int rows, int cols, cudaStream_t s) {
   if (rows <= 0) return;
   if (cols % 128 != 0) throw std::runtime_error("quant_fp8_block: cols % 128");
-  const int n = rows * (cols / 128);
-  const int warps = 8;
-  launch_k(quant_fp8_block_kernel, dim3((n + warps - 1) / warps), dim3(warps * 32), 0, s, (const bf16*)x, ldx,
+  if (ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 7))
+    throw std::runtime_error("quant_fp8_block: 16-byte aligned rows required");
+  const long long n = (long long)rows * (cols / 128) * 16;
+  launch_k(quant_fp8_block_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, (const bf16*)x, ldx,
            (__nv_fp8_e4m3*)q, scales, rows, cols);
 }
 
