@@ -80,11 +80,12 @@ class ExpertParallel:
         gathers them straight into the fp8 expert GEMM's operand layout.
 
         ``shared_local``: the shared experts are not dispatched; every rank runs them
-        on its own tokens right after the dispatch, while the routed rows are still
-        crossing NVLink, and the combine reads their rows locally. Off by default: on
-        the V2-Lite shape (2 GPUs, 64 tokens per rank) the shared experts' own grouped
-        GEMMs (44 tiles) took 32.8 us against 12.7 us saved in the routed GEMM, and the
-        step slowed from 5.96 to 6.46 ms."""
+        on its own tokens while the routed rows cross NVLink, and the combine reads their
+        rows locally. On the main stream this was slower (V2-Lite, 2 GPUs: the shared
+        experts' own grouped GEMMs took 32.8 us against 12.7 us saved in the routed GEMM,
+        5.96 -> 6.46 ms per step); on a forked stream they overlap the dispatch, receive
+        and routed experts and the step is faster (5.75 -> 5.67 ms), so ranks in
+        separate processes use it by default."""
         assert cfg.n_routed_experts % world == 0, "routed experts must split evenly over the ranks"
         assert 1 <= world <= 8
         cap_tokens = -(-cap_tokens // CHUNK_TOKENS) * CHUNK_TOKENS
@@ -102,11 +103,14 @@ class ExpertParallel:
         self.layers_per_step = len(self.moe_layers) + (len(self.moe_layers) & 1)
         self.fp8 = (cfg.weight_dtype == "fp8_block") if fp8_transport is None else bool(fp8_transport)
         self.S = cfg.n_shared_experts
-        # SPARKPIPE_EP_SHARED_LOCAL=1 turns it on where the caller leaves the default
-        shared_local = shared_local or os.environ.get("SPARKPIPE_EP_SHARED_LOCAL", "0") == "1"
+        # Multi-process ranks default to local shared experts on a forked stream, which
+        # measured faster than dispatching them (V2-Lite, 2 GPUs: 5.67 vs 5.75 ms per
+        # step); SPARKPIPE_EP_SHARED_LOCAL=0 dispatches them, SPARKPIPE_EP_SHARED_SIDE=0
+        # runs them on the main stream after the dispatch.
+        if group is not None and os.environ.get("SPARKPIPE_EP_SHARED_LOCAL", "1") == "1":
+            shared_local = True
         self.shared_local = bool(shared_local) and self.S > 0
-        # SPARKPIPE_EP_SHARED_SIDE=1: local shared experts on a forked stream
-        self.shared_side = os.environ.get("SPARKPIPE_EP_SHARED_SIDE", "0") == "1"
+        self.shared_side = os.environ.get("SPARKPIPE_EP_SHARED_SIDE", "1") == "1"
         self._side = None
         self._join = None
         self.row_words = row_words(self.H, self.fp8)
@@ -223,18 +227,20 @@ class ExpertParallel:
         T, S, F = xn.shape[0], self.S, self.act.shape[1]
         if T == 0:
             return
-        key = T
-        if key not in self._sh:
-            bn = max(32, min(128, 1 << max(0, (T - 1).bit_length()))) if self.fp8 else \
-                 max(16, min(256, 1 << max(0, (T - 1).bit_length())))
-            dev = self.device
-            rows = torch.arange(0, (S + 1) * T, T, dtype=torch.int32, device=dev)
-            tiles = torch.arange(0, S + 1, dtype=torch.int32, device=dev) * ((T + bn - 1) // bn)
-            src = (torch.arange(S * T, device=dev) % T).to(torch.int32)
-            self._sh[key] = dict(bn=bn, rows=rows, tiles=tiles, src=src,
-                                 act=torch.empty(S * T, F, dtype=torch.bfloat16, device=dev),
-                                 y=torch.empty(S, T, self.H, dtype=torch.bfloat16, device=dev))
-        b = self._sh[key]
+        # buffers per power-of-two bucket of T (bounded, and alive for any graph captured
+        # with them); the small row / tile / source tables are rebuilt for every call (in
+        # a captured step they are kernels of the graph)
+        bucket = 1 << max(0, (T - 1).bit_length())
+        dev = self.device
+        if bucket not in self._sh:
+            self._sh[bucket] = dict(act=torch.empty(S * bucket * F, dtype=torch.bfloat16, device=dev),
+                                    y=torch.empty(S * bucket * self.H, dtype=torch.bfloat16, device=dev))
+        bn = max(32, min(128, bucket)) if self.fp8 else max(16, min(256, bucket))
+        cb = self._sh[bucket]
+        b = dict(bn=bn, rows=torch.arange(0, (S + 1) * T, T, dtype=torch.int32, device=dev),
+                 tiles=torch.arange(0, S + 1, dtype=torch.int32, device=dev) * ((T + bn - 1) // bn),
+                 src=(torch.arange(S * T, device=dev) % T).to(torch.int32),
+                 act=cb["act"][:S * T * F].view(S * T, F), y=cb["y"][:S * T * self.H].view(S, T, self.H))
         El = self.El
         if isinstance(w13, ops.Fp8Weight):
             w13s = ops.Fp8Weight(w13.q[El:], w13.s[El:], w13.sa_rows)
