@@ -148,7 +148,8 @@ class ExpertParallel:
             self.xs = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
             self.xq = self.aq = None
         self.act = torch.zeros(max_pairs, F, dtype=torch.bfloat16, device=dev)
-        self._sh = {}  # shared-expert buffers per token count
+        self._sh = {}  # shared-expert buffers per power-of-two token bucket
+        self._sh_tables = {}  # shared-expert row / tile / source tables per token count
         self.y = torch.zeros(max_pairs, self.H, dtype=torch.bfloat16, device=dev)
 
     @classmethod
@@ -228,8 +229,8 @@ class ExpertParallel:
         if T == 0:
             return
         # buffers per power-of-two bucket of T (bounded, and alive for any graph captured
-        # with them); the small row / tile / source tables are rebuilt for every call (in
-        # a captured step they are kernels of the graph)
+        # with them); the small row / tile / source tables are cached per T up to 4,096
+        # tokens and rebuilt per call above that
         bucket = 1 << max(0, (T - 1).bit_length())
         dev = self.device
         if bucket not in self._sh:
@@ -237,9 +238,14 @@ class ExpertParallel:
                                     y=torch.empty(S * bucket * self.H, dtype=torch.bfloat16, device=dev))
         bn = max(32, min(128, bucket)) if self.fp8 else max(16, min(256, bucket))
         cb = self._sh[bucket]
-        b = dict(bn=bn, rows=torch.arange(0, (S + 1) * T, T, dtype=torch.int32, device=dev),
-                 tiles=torch.arange(0, S + 1, dtype=torch.int32, device=dev) * ((T + bn - 1) // bn),
-                 src=(torch.arange(S * T, device=dev) % T).to(torch.int32),
+        tab = self._sh_tables.get(T)
+        if tab is None:  # decode-sized T: built once (in the eager warm-up), replayed from then on
+            tab = (torch.arange(0, (S + 1) * T, T, dtype=torch.int32, device=dev),
+                   torch.arange(0, S + 1, dtype=torch.int32, device=dev) * ((T + bn - 1) // bn),
+                   (torch.arange(S * T, device=dev) % T).to(torch.int32))
+            if T <= 4096:
+                self._sh_tables[T] = tab
+        b = dict(bn=bn, rows=tab[0], tiles=tab[1], src=tab[2],
                  act=cb["act"][:S * T * F].view(S * T, F), y=cb["y"][:S * T * self.H].view(S, T, self.H))
         El = self.El
         if isinstance(w13, ops.Fp8Weight):
