@@ -21,6 +21,8 @@
 // and the fused top-k reduce of the FP8 MoE entry point (:321-342, :1053).
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include <stdexcept>
 #include <string>
 
@@ -390,36 +392,72 @@ __global__ void __launch_bounds__(1024) moe_align_small_kernel(const int* __rest
   }
 }
 
-__global__ void moe_zero_kernel(int* __restrict__ p, int n) {
+
+
+
+
+// Prefill-sized layouts in three launches without contended global atomics: each CTA
+// histograms its contiguous slice of the (token, slot) pairs in shared memory, one CTA
+// turns the per-CTA counts into the expert offsets and each CTA's base per expert, and
+// each CTA scatters its slice from those bases with shared-memory cursors. (Grid-wide
+// global atomics on ~E counters measured 0.8 ms per 8,192-token chunk for count and
+// scatter together.)
+constexpr int ALIGN_MAX_CTAS = 128;
+__global__ void __launch_bounds__(1024) moe_hist_kernel(const int* __restrict__ ids, int n, int chunk, int E,
+                                                        int* __restrict__ cta_counts) {
   griddep_wait();
   griddep_launch();
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = 0;
+  __shared__ int cnt[ALIGN_MAX_E];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  const int i0 = blockIdx.x * chunk, i1 = min(n, i0 + chunk);
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) atomicAdd(&cnt[ids[i]], 1);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cta_counts[blockIdx.x * E + e] = cnt[e];
 }
 
-__global__ void moe_count_kernel(const int* __restrict__ ids, int n, int* __restrict__ counts) {
+__global__ void __launch_bounds__(1024) moe_bases_kernel(int* __restrict__ cta_counts, int G, int E, int bn,
+                                                         int* __restrict__ grp_rows, int* __restrict__ grp_tiles) {
   griddep_wait();
   griddep_launch();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) atomicAdd(&counts[ids[i]], 1);
+  __shared__ int tot[ALIGN_MAX_E];
+  __shared__ int cur[ALIGN_MAX_E];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int t = 0;
+    for (int c = 0; c < G; ++c) t += cta_counts[c * E + e];
+    tot[e] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) scan_counts_warp(tot, E, bn, grp_rows, grp_tiles, cur);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {  // counts -> each CTA's first row per expert
+    int base = cur[e];
+    for (int c = 0; c < G; ++c) {
+      const int v = cta_counts[c * E + e];
+      cta_counts[c * E + e] = base;
+      base += v;
+    }
+  }
 }
 
-__global__ void moe_scan_kernel(int* __restrict__ counts, int E, int bn, int* __restrict__ grp_rows,
-                                int* __restrict__ grp_tiles) {
+__global__ void __launch_bounds__(1024) moe_scatter_slices_kernel(const int* __restrict__ ids, int n, int chunk, int k,
+                                                                  int E, const int* __restrict__ cta_bases,
+                                                                  int* __restrict__ sorted_tok,
+                                                                  int* __restrict__ inv_pos) {
   griddep_wait();
   griddep_launch();
-  scan_counts_warp(counts, E, bn, grp_rows, grp_tiles, counts);
+  __shared__ int cur[ALIGN_MAX_E];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cur[e] = cta_bases[blockIdx.x * E + e];
+  __syncthreads();
+  const int i0 = blockIdx.x * chunk, i1 = min(n, i0 + chunk);
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const int pos = atomicAdd(&cur[ids[i]], 1);
+    sorted_tok[pos] = i / k;
+    inv_pos[i] = pos;
+  }
 }
 
-__global__ void moe_scatter_kernel(const int* __restrict__ ids, int n, int k, int* __restrict__ cursor,
-                                   int* __restrict__ sorted_tok, int* __restrict__ inv_pos) {
-  griddep_wait();
-  griddep_launch();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const int pos = atomicAdd(&cursor[ids[i]], 1);
-  sorted_tok[pos] = i / k;
-  inv_pos[i] = pos;
-}
+int moe_align_work_ints(int E) { return (ALIGN_MAX_CTAS + 1) * E; }
 
 int moe_align(const int* topk_ids, int T, int k, int E, int block_n, int* grp_rows, int* grp_tiles, int* sorted_tok,
               int* inv_pos, int* work, cudaStream_t s) {
@@ -430,12 +468,13 @@ int moe_align(const int* topk_ids, int T, int k, int E, int block_n, int* grp_ro
              sorted_tok, inv_pos);
     return 1;
   }
-  launch_k(moe_zero_kernel, dim3(1), dim3(1024), 0, s, work, E);
-  launch_k(moe_count_kernel, dim3((n + 255) / 256), dim3(256), 0, s, (const int*)topk_ids, n, work);
-  launch_k(moe_scan_kernel, dim3(1), dim3(32), 0, s, work, E, block_n, grp_rows, grp_tiles);
-  launch_k(moe_scatter_kernel, dim3((n + 255) / 256), dim3(256), 0, s, (const int*)topk_ids, n, k, work, sorted_tok,
-           inv_pos);
-  return 4;
+  const int G = std::min(ALIGN_MAX_CTAS, (n + 4095) / 4096);
+  const int chunk = (n + G - 1) / G;
+  launch_k(moe_hist_kernel, dim3(G), dim3(1024), 0, s, topk_ids, n, chunk, E, work);
+  launch_k(moe_bases_kernel, dim3(1), dim3(1024), 0, s, work, G, E, block_n, grp_rows, grp_tiles);
+  launch_k(moe_scatter_slices_kernel, dim3(G), dim3(1024), 0, s, topk_ids, n, chunk, k, E, (const int*)work,
+           sorted_tok, inv_pos);
+  return 3;
 }
 
 // ---------------------------------------------------------------- data movement

@@ -682,6 +682,7 @@ int64_t moe_align(const Tensor& topk_ids, int64_t num_experts, int64_t block_n, 
                const Tensor& grp_tiles, const Tensor& sorted_tok, const Tensor& inv_pos, const Tensor& work) {
   CHECK_CUDA(topk_ids); CHECK_I32(topk_ids); CHECK_CONTIG(topk_ids);
   CHECK_I32(grp_rows); CHECK_I32(grp_tiles); CHECK_I32(sorted_tok); CHECK_I32(inv_pos); CHECK_I32(work);
+  TORCH_CHECK(work.numel() >= 129 * num_experts, "moe_align: work holds 129 x experts ints");
   const c10::cuda::CUDAGuard guard(topk_ids.device());
   return sp::moe_align(topk_ids.data_ptr<int>(), (int)topk_ids.size(0), (int)topk_ids.size(1), (int)num_experts,
                 (int)block_n, grp_rows.data_ptr<int>(), grp_tiles.data_ptr<int>(), sorted_tok.data_ptr<int>(),

@@ -545,7 +545,7 @@ def moe_align(topk_ids, num_experts, block_n):
     grp_tiles = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
     sorted_tok = torch.empty(n, dtype=torch.int32, device=dev)
     inv_pos = torch.empty(n, dtype=torch.int32, device=dev)
-    work = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    work = torch.empty(129 * num_experts, dtype=torch.int32, device=dev)  # per-CTA counts of large layouts
     _count(kernels().moe_align(topk_ids, num_experts, block_n, grp_rows, grp_tiles, sorted_tok, inv_pos, work))
     return grp_rows, grp_tiles, sorted_tok, inv_pos
 

@@ -563,3 +563,31 @@ def test_moe_route_fused_matches_gemm_router(scoring, E, k, groups):
     _close(w[:, :k].gather(1, order), w2[:, :k].gather(1, order2), atol=1e-4, rtol=1e-3)
     _status_ok()
 
+
+
+@pytest.mark.parametrize("T,E,k", [(64, 66, 8), (8192, 66, 8), (3000, 384, 9)])
+def test_moe_align_layout(T, E, k):
+    """Expert-sorted layout (one-CTA path for decode sizes, sliced histogram path above
+    16,384 pairs): rows grouped by expert in grp_rows order, inv_pos its inverse, tile
+    prefix counts from the row counts."""
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(T + E)
+    logits = torch.randn(T, E, device=DEV, generator=g) + torch.linspace(2, -2, E, device=DEV)
+    ids = logits.topk(k, dim=-1).indices.int().contiguous()
+    bn = 64
+    grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E, bn)
+    torch.cuda.synchronize()
+    counts = torch.bincount(ids.flatten().long(), minlength=E).cpu()
+    rows = grp_rows.cpu()
+    assert rows[0] == 0 and torch.equal(rows[1:] - rows[:-1], counts.int())
+    tiles = grp_tiles.cpu()
+    assert torch.equal(tiles[1:] - tiles[:-1], ((counts + bn - 1) // bn).int())
+    inv = inv_pos.cpu().long()
+    assert torch.equal(torch.sort(inv).values, torch.arange(T * k))
+    flat = ids.flatten().cpu().long()
+    st = sorted_tok.cpu().long()
+    for i in torch.randint(0, T * k, (500,), generator=torch.Generator().manual_seed(1)).tolist():
+        p = int(inv[i])
+        e = int(flat[i])
+        assert int(rows[e]) <= p < int(rows[e + 1]) and int(st[p]) == i // k
+    _status_ok()
