@@ -107,7 +107,9 @@ class ExpertParallel:
         # measured faster than dispatching them (V2-Lite, 2 GPUs: 5.67 vs 5.75 ms per
         # step); SPARKPIPE_EP_SHARED_LOCAL=0 dispatches them, SPARKPIPE_EP_SHARED_SIDE=0
         # runs them on the main stream after the dispatch.
-        if group is not None and os.environ.get("SPARKPIPE_EP_SHARED_LOCAL", "1") == "1":
+        # (bf16 experts: the fp8 shared-expert path is verified with dispatched shared
+        # experts only, so fp8 models keep dispatching them unless asked)
+        if group is not None and os.environ.get("SPARKPIPE_EP_SHARED_LOCAL", "0" if self.fp8 else "1") == "1":
             shared_local = True
         self.shared_local = bool(shared_local) and self.S > 0
         self.shared_side = os.environ.get("SPARKPIPE_EP_SHARED_SIDE", "1") == "1"
