@@ -13,6 +13,14 @@ context, and the per-step host<->device bytes. Wall-clock timing of the engine
 (host loop included), as a serving user sees it.
 
     python -m sparkpipe_rs_b200.utils.bench_long_context [--model v2_lite] [--prompt 131072]
+
+Under torchrun (one process per GPU) the model runs expert-parallel (attention
+data-parallel, routed experts split over the ranks): rank 0 serves both requests and
+the other ranks step in lockstep with idle forwards, supplying their experts. The
+1T Kimi-K2-shape config runs this way on 8 GPUs:
+
+    python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \
+        -m sparkpipe_rs_b200.utils.bench_long_context --model k2
 """
 from __future__ import annotations
 
@@ -36,13 +44,25 @@ def main():
     from sparkpipe_rs_b200.serving.engine import EngineConfig, LLMEngine, SamplingParams
     from sparkpipe_rs_b200.utils.clocks import ClockSampler
 
-    dev = torch.device("cuda", 0)
+    import datetime
+    import os
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
     cfg = get_config(args.model)
     P, S, out = args.prompt, args.shared, args.output
     max_len = P + out + 64
     bs = 64
-    model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=max_len + 64)
+    ep = None
+    if world > 1:
+        import torch.distributed as dist
+        from sparkpipe_rs_b200.parallel.expert_parallel import ExpertParallel
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+        ep = ExpertParallel(cfg, rank, world, args.chunk, dev, group=dist.group.WORLD)
+    model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=max_len + 64, ep=ep)
     blocks = 2 * math.ceil(max_len / bs) + 64
     engine = LLMEngine(cfg, EngineConfig(max_batch=2, block_size=bs, max_model_len=max_len, num_blocks=blocks,
                                          max_prefill_tokens=args.chunk, use_cuda_graph=True, prefix_caching=True),
@@ -51,9 +71,14 @@ def main():
     a = torch.randint(0, cfg.vocab_size, (P,), generator=g, dtype=torch.int32).tolist()
     b = a[:S] + torch.randint(0, cfg.vocab_size, (P - S,), generator=g, dtype=torch.int32).tolist()
     params = SamplingParams(max_tokens=out, temperature=0.0, ignore_eos=True)
-    with ClockSampler(0) as clk:
-        ra = engine.generate([a], params)
-        rb = engine.generate([b], params)
+    mine = rank == 0  # rank 0 serves the requests; the others run idle lockstep forwards
+    with ClockSampler(dev.index or 0) as clk:
+        ra = engine.generate([a] if mine else [], params)
+        rb = engine.generate([b] if mine else [], params)
+    if not mine:
+        engine.shutdown()
+        _finish(world, ep)
+        return
     sa, sb = ra.stats, rb.stats
     print(json.dumps({
         "metric": "long-context serving (TTFT ms, prefill tokens/s, TPOT ms)",
@@ -71,8 +96,19 @@ def main():
         "data": "synthetic: seeded uniform-random prompt ids, random-init N(0,0.02) weights",
         "timing": "wall clock around LLMEngine.generate (host scheduling included)",
         "clocks": clk.summary(),
+        "n_gpus": world, "parallelism": f"dp{world}-ep{world}" if world > 1 else "1 GPU",
     }), flush=True)
     engine.shutdown()
+    _finish(world, ep)
+
+
+def _finish(world, ep):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        ep.close()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
