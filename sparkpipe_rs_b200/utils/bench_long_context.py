@@ -63,7 +63,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
         ep = ExpertParallel(cfg, rank, world, args.chunk, dev, group=dist.group.WORLD)
     model = MLAMoEModel(cfg, seed=0, device=dev, max_positions=max_len + 64, ep=ep)
-    blocks = 2 * math.ceil(max_len / bs) + 64
+    # request A's whole context plus request B's new part: B reuses A's prefix blocks
+    # from the prefix cache, and A's other cached blocks are evicted as B needs room
+    blocks = math.ceil(max_len / bs) + math.ceil((P - S + out) / bs) + 64
     engine = LLMEngine(cfg, EngineConfig(max_batch=2, block_size=bs, max_model_len=max_len, num_blocks=blocks,
                                          max_prefill_tokens=args.chunk, use_cuda_graph=True, prefix_caching=True),
                        model=model, device=dev)
