@@ -87,6 +87,7 @@ class EngineConfig:
     host_drive_path: str = ""         # with fewer resident buffers than slots: the drive file the rest spill to
     kv_cache_dtype: str = "bf16"      # "fp8": e4m3 latent rows with per-128 block scales (CUDA, 576-wide rows)
     warm_prefill: bool = True         # one throwaway prefill of the largest chunk at start (allocator warm-up)
+    prefill_graphs: bool = True       # replay repeated prefill chunk shapes (no cached prefix) from CUDA graphs
 
 
 @dataclass
@@ -193,6 +194,33 @@ class _Launched:
     timing: tuple | None = None  # CUDA events around the step's device work (cost model)
 
 
+class _PrefillGraph:
+    """One prefill chunk shape without a cached prefix (tokens, sequences, longest
+    query) as a CUDA graph: static device inputs, captured the second time the shape
+    comes up (its first run was eager, so every kernel's attributes and workspaces are
+    set), replayed from then on. A serving burst of equal prompts repeats one shape, and
+    the chunk's ~430 launches then cost one graph launch instead of one host round trip
+    each."""
+
+    def __init__(self, model, cache, T: int, nseq: int, max_q: int, dev):
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.model, self.cache = model, cache
+        self.ids = torch.zeros(T, **i32)
+        self.pos = torch.zeros(T, **i32)
+        self.slots = torch.full((T,), -1, **i32)
+        self.cu = torch.zeros(nseq + 1, **i32)
+        self.lidx = torch.zeros(nseq, **i32)
+        self.fb = ForwardBatch(mode="prefill", token_ids=self.ids, positions=self.pos, slot_mapping=self.slots,
+                               cu_q=self.cu, cu_k=self.cu, max_q=max_q, logits_idx=self.lidx)
+        cur = torch.cuda.current_stream(dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(cur)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side), torch.cuda.graph(self.graph, stream=side, capture_error_mode="thread_local"):
+            self.out = model.forward(self.fb, cache)
+        cur.wait_stream(side)
+
+
 class LLMEngine:
     def __init__(self, cfg: MLAMoEConfig, ecfg: EngineConfig | None = None, model=None, device="cuda",
                  cache: KVCache | None = None, draft=None):
@@ -225,6 +253,8 @@ class LLMEngine:
         self.cache = cache or KVCache(cfg, num_blocks=num_blocks + shadow_blocks, block_size=e.block_size,
                                       device=self.device, kv_dtype=e.kv_cache_dtype if self.is_cuda else "bf16")
         self.use_graphs = self.is_cuda and e.use_cuda_graph and isinstance(self.model, MLAMoEModel)
+        self._pgraphs: dict[tuple, _PrefillGraph] = {}
+        self._pseen: dict[tuple, int] = {}
         self.draft = self.dcache = None
         if self.spec:
             self.draft = draft or _default_draft(self.model, e)
@@ -444,7 +474,37 @@ class LLMEngine:
         self.model.forward(fb, self.cache)
         torch.cuda.synchronize(dev)
 
+    def _prefill_graph(self, plan):
+        """The captured graph of this plan's chunk shape, if it has one (or gets one now:
+        second sighting of the shape); None runs the chunk eagerly."""
+        if not (self.use_graphs and self.ecfg.prefill_graphs) or plan.has_prefix or self._lockstep is not None:
+            return None
+        if not np.array_equal(plan.cu_q, plan.cu_k):  # keys beyond the chunk: not this graph's shape
+            return None
+        sig = (len(plan.token_ids), len(plan.cu_q) - 1, int(plan.max_q))
+        g = self._pgraphs.get(sig)
+        if g is None:
+            seen = self._pseen.get(sig, 0)
+            self._pseen[sig] = seen + 1
+            if seen == 0 or len(self._pgraphs) >= 4:
+                return None
+            g = self._pgraphs[sig] = _PrefillGraph(self.model, self.cache, sig[0], sig[1], sig[2], self.device)
+        return g
+
     def _run_prefill(self, plan) -> torch.Tensor:
+        g = self._prefill_graph(plan)
+        if g is not None:
+            for name, buf, arr in (("p_ids", g.ids, plan.token_ids), ("p_pos", g.pos, plan.positions),
+                                   ("p_slots", g.slots, plan.slot_mapping), ("p_cuq", g.cu, plan.cu_q),
+                                   ("p_lidx", g.lidx, plan.logits_idx)):
+                host = self.pinned.get(name, len(arr))
+                host.numpy()[:] = arr
+                self.h2d_bytes += host.numel() * host.element_size()
+                buf.copy_(host, non_blocking=True)
+            g.graph.replay()
+            if self.spec:
+                self._draft_kv(g.fb)
+            return self._sample(g.out, plan)
         fb = ForwardBatch(
             mode="prefill",
             token_ids=self._h2d("p_ids", plan.token_ids),
@@ -797,6 +857,7 @@ class LLMEngine:
         for v in self.verify_rounds.values():
             v.release()
         self.verify_rounds.clear()
+        self._pgraphs.clear()
         if hasattr(self.model, "shutdown"):
             self.model.shutdown()
         if self.is_cuda:

@@ -128,3 +128,26 @@ def test_drive_backed_host_tier_round_trip_on_the_gpu_cache(tmp_path, kv_dtype):
         for w, t in zip(want, cache.planes()):
             assert torch.equal(t[:, b * 64:(b + 1) * 64], w)
     assert tier.spilled_blocks >= 3 and tier.fetched_blocks >= 3
+
+
+def test_prefill_graphs_replay_repeated_chunk_shapes():
+    """Six 100-token prompts in 200-token chunks: the chunk shape repeats, so the second
+    chunk captures a prefill graph and the third replays it; tokens equal an engine that
+    runs every chunk eagerly."""
+    from sparkpipe_rs_b200.models.mla_moe import MLAMoEModel
+    from sparkpipe_rs_b200.serving.engine import SamplingParams
+
+    cfg = _cfg()
+    model = MLAMoEModel(cfg, seed=0, device="cuda", max_positions=1024)
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, cfg.vocab_size, (100,), generator=g).tolist() for _ in range(6)]
+    params = SamplingParams(max_tokens=8, ignore_eos=True)
+    outs = {}
+    for graphs in (False, True):
+        eng = _engine(model, cfg, max_prefill_tokens=200, prefill_graphs=graphs, prefix_caching=False)
+        res = eng.generate(prompts, params)
+        outs[graphs] = [o.token_ids for o in res.outputs]
+        if graphs:
+            assert len(eng._pgraphs) == 1 and list(eng._pgraphs) == [(200, 2, 100)]
+        eng.shutdown()
+    assert outs[True] == outs[False]
