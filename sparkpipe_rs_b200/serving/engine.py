@@ -196,9 +196,9 @@ class _Launched:
 
 class _PrefillGraph:
     """One prefill chunk shape without a cached prefix (tokens, sequences, longest
-    query) as a CUDA graph: static device inputs, captured the second time the shape
-    comes up (its first run was eager, so every kernel's attributes and workspaces are
-    set), replayed from then on. A serving burst of equal prompts repeats one shape, and
+    query) as a CUDA graph: static device inputs, captured the first time the shape comes
+    up after the engine's warm-up prefill (else the second time, after an eager run has
+    set every kernel's attributes), replayed from then on. A serving burst of equal prompts repeats one shape, and
     the chunk's ~430 launches then cost one graph launch instead of one host round trip
     each."""
 
@@ -255,6 +255,7 @@ class LLMEngine:
         self.use_graphs = self.is_cuda and e.use_cuda_graph and isinstance(self.model, MLAMoEModel)
         self._pgraphs: dict[tuple, _PrefillGraph] = {}
         self._pseen: dict[tuple, int] = {}
+        self._prefill_warmed = False
         self.draft = self.dcache = None
         if self.spec:
             self.draft = draft or _default_draft(self.model, e)
@@ -473,6 +474,7 @@ class LLMEngine:
                           logits_idx=(cu[1:] - 1).contiguous())
         self.model.forward(fb, self.cache)
         torch.cuda.synchronize(dev)
+        self._prefill_warmed = True
 
     def _prefill_graph(self, plan):
         """The captured graph of this plan's chunk shape, if it has one (or gets one now:
@@ -486,7 +488,9 @@ class LLMEngine:
         if g is None:
             seen = self._pseen.get(sig, 0)
             self._pseen[sig] = seen + 1
-            if seen == 0 or len(self._pgraphs) >= 4:
+            # after the warm-up prefill every prefill kernel's attributes are set, so a
+            # shape can be captured the first time it comes up
+            if (seen == 0 and not self._prefill_warmed) or len(self._pgraphs) >= 4:
                 return None
             g = self._pgraphs[sig] = _PrefillGraph(self.model, self.cache, sig[0], sig[1], sig[2], self.device)
         return g

@@ -131,9 +131,9 @@ def test_drive_backed_host_tier_round_trip_on_the_gpu_cache(tmp_path, kv_dtype):
 
 
 def test_prefill_graphs_replay_repeated_chunk_shapes():
-    """Six 100-token prompts in 200-token chunks: the chunk shape repeats, so the second
-    chunk captures a prefill graph and the third replays it; tokens equal an engine that
-    runs every chunk eagerly."""
+    """Six 100-token prompts in 200-token chunks: the chunk shape repeats, so one prefill
+    graph is captured (at the first chunk after the engine's warm-up prefill) and replayed
+    for the others; tokens equal an engine that runs every chunk eagerly."""
     from sparkpipe_rs_b200.models.mla_moe import MLAMoEModel
     from sparkpipe_rs_b200.serving.engine import SamplingParams
 
