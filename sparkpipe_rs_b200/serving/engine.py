@@ -87,7 +87,7 @@ class EngineConfig:
     host_drive_path: str = ""         # with fewer resident buffers than slots: the drive file the rest spill to
     kv_cache_dtype: str = "bf16"      # "fp8": e4m3 latent rows with per-128 block scales (CUDA, 576-wide rows)
     warm_prefill: bool = True         # one throwaway prefill of the largest chunk at start (allocator warm-up)
-    prefill_graphs: bool = True       # replay repeated prefill chunk shapes (no cached prefix) from CUDA graphs
+    prefill_graphs: bool = False      # replay repeated prefill chunk shapes (no cached prefix) from CUDA graphs
 
 
 @dataclass

@@ -17,8 +17,9 @@ def _cfg():
 def _engine(model, cfg, **kw):
     from sparkpipe_rs_b200.serving.engine import EngineConfig, LLMEngine
 
-    ec = EngineConfig(max_batch=8, block_size=64, max_model_len=512, max_prefill_tokens=256,
-                      decode_buckets=(1, 2, 4, 8), **kw)
+    kw = {"max_batch": 8, "block_size": 64, "max_model_len": 512, "max_prefill_tokens": 256,
+          "decode_buckets": (1, 2, 4, 8), **kw}
+    ec = EngineConfig(**kw)
     return LLMEngine(cfg, ec, model=model, device="cuda")
 
 
