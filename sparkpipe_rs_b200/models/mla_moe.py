@@ -323,7 +323,10 @@ class MLAMoEModel:
             bn = _moe_block_n(T * kk, self.ep.n_local)
             if isinstance(w[p + "e_w13"], ops.Fp8Weight):
                 bn = max(32, min(bn, 128))
-            return self.ep.moe(i, xn, ids, wts, w[p + "e_w13"], w[p + "e_w2"], bn, self.fused_swiglu)
+            # prefill-sized groups (a rank receives ~T * k / n_local rows per local expert)
+            tm = (self.fused_swiglu and not isinstance(w[p + "e_w13"], ops.Fp8Weight)
+                  and T * k >= MOE_TOKEN_MAJOR_MIN_ROWS * self.ep.n_local)
+            return self.ep.moe(i, xn, ids, wts, w[p + "e_w13"], w[p + "e_w2"], bn, self.fused_swiglu, token_major=tm)
         if (T * kk >= MOE_TOKEN_MAJOR_MIN_ROWS * (E + S) and self.fused_swiglu
                 and not isinstance(w[p + "e_w13"], ops.Fp8Weight)):
             grp_rows, grp_tiles, sorted_tok, inv_pos = ops.moe_align(ids, E + S, 128)

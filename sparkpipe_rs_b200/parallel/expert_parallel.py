@@ -200,10 +200,13 @@ class ExpertParallel:
         """Combine epilogue arguments of the down-projection GEMM for MoE layer `layer`."""
         return (self.args(), self.comb_dst, self.epoch, self.moe_index[layer])
 
-    def experts(self, w13, w2, bn: int, fused_swiglu: bool = True, layer: int | None = None):
+    def experts(self, w13, w2, bn: int, fused_swiglu: bool = True, layer: int | None = None,
+                token_major: bool = False):
         """Expert GEMMs of the received rows. With `layer` the down projection's epilogue
         sends every output row straight into its source rank's combine slot (the
-        combine-send kernel is not needed); without it the rows land in ``self.y``."""
+        combine-send kernel is not needed); without it the rows land in ``self.y``.
+        ``token_major`` (prefill-sized groups, bf16, fused SwiGLU; the rows were laid out
+        in 128-row tiles, bn = 128) runs the gate/up GEMM with the tokens as the M tiles."""
         comb = self._comb(layer) if layer is not None else None
         if isinstance(w13, ops.Fp8Weight):
             # block-scaled fp8 experts; the live row count stays on the device
@@ -216,7 +219,10 @@ class ExpertParallel:
             return
         if self.fp8:
             raise ValueError("expert parallel: the fp8 transport needs fp8 expert weights")
-        if fused_swiglu:
+        if fused_swiglu and token_major:
+            ops.grouped_gemm_tm(w13[:self.n_local], self.xs, self.act, self.grp_rows, self.grp_tiles, self.n_local,
+                                swiglu=True)
+        elif fused_swiglu:
             ops.grouped_gemm(w13, self.xs, self.act, self.grp_rows, self.grp_tiles, self.n_local, bn, swiglu=True)
         else:
             h13 = torch.empty(self.xs.shape[0], 2 * self.act.shape[1], dtype=torch.bfloat16, device=self.device)
@@ -224,9 +230,10 @@ class ExpertParallel:
             ops.silu_mul(h13, out=self.act)
         ops.grouped_gemm(w2, self.act, self.y, self.grp_rows, self.grp_tiles, self.n_local, bn, ep_combine=comb)
 
-    def shared(self, xn: torch.Tensor, w13, w2, fused_swiglu: bool = True):
+    def shared(self, xn: torch.Tensor, w13, w2, fused_swiglu: bool = True, token_major: bool = False):
         """The shared experts on this rank's tokens (S groups of T rows, the same grouped
-        kernels as the routed experts); rows land in ``self.y_sh`` [S, T, H]."""
+        kernels as the routed experts; token-major 128-row tiles with ``token_major``);
+        rows land in ``self.y_sh`` [S, T, H]."""
         T, S, F = xn.shape[0], self.S, self.act.shape[1]
         if T == 0:
             return
@@ -238,15 +245,16 @@ class ExpertParallel:
         if bucket not in self._sh:
             self._sh[bucket] = dict(act=torch.empty(S * bucket * F, dtype=torch.bfloat16, device=dev),
                                     y=torch.empty(S * bucket * self.H, dtype=torch.bfloat16, device=dev))
-        bn = max(32, min(128, bucket)) if self.fp8 else max(16, min(256, bucket))
+        tm = token_major and fused_swiglu and not isinstance(w13, ops.Fp8Weight)
+        bn = 128 if tm else max(32, min(128, bucket)) if self.fp8 else max(16, min(256, bucket))
         cb = self._sh[bucket]
-        tab = self._sh_tables.get(T)
+        tab = self._sh_tables.get((T, bn))
         if tab is None:  # decode-sized T: built once (in the eager warm-up), replayed from then on
             tab = (torch.arange(0, (S + 1) * T, T, dtype=torch.int32, device=dev),
                    torch.arange(0, S + 1, dtype=torch.int32, device=dev) * ((T + bn - 1) // bn),
                    (torch.arange(S * T, device=dev) % T).to(torch.int32))
             if T <= 4096:
-                self._sh_tables[T] = tab
+                self._sh_tables[(T, bn)] = tab
         b = dict(bn=bn, rows=tab[0], tiles=tab[1], src=tab[2],
                  act=cb["act"][:S * T * F].view(S * T, F), y=cb["y"][:S * T * self.H].view(S, T, self.H))
         El = self.El
@@ -259,6 +267,11 @@ class ExpertParallel:
                                  S, b["bn"])
         else:
             xs = ops.gather_rows(xn, b["src"])
+            if tm:
+                ops.grouped_gemm_tm(w13[El:], xs, b["act"], b["rows"], b["tiles"], S, swiglu=True)
+                ops.grouped_gemm_tm(w2[El:], b["act"], b["y"].view(S * T, self.H), b["rows"], b["tiles"], S)
+                self.y_sh = b["y"]
+                return
             if fused_swiglu:
                 ops.grouped_gemm(w13[El:], xs, b["act"], b["rows"], b["tiles"], S, b["bn"], swiglu=True)
             else:
@@ -294,8 +307,12 @@ class ExpertParallel:
 
     # ------------------------------------------------------------------ one layer
     def moe(self, layer: int, xn: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, w13: torch.Tensor,
-            w2: torch.Tensor, bn: int, fused_swiglu: bool = True):
-        """Runs one MoE layer for this rank's tokens; returns the deferred combine."""
+            w2: torch.Tensor, bn: int, fused_swiglu: bool = True, token_major: bool = False):
+        """Runs one MoE layer for this rank's tokens; returns the deferred combine.
+        ``token_major`` (prefill-sized groups) lays the received rows out in 128-row
+        tiles and runs the gate/up GEMMs (and the shared experts') token-major."""
+        if token_major:
+            bn = 128
         if xn.shape[0] > self.cap:
             raise ValueError(f"expert parallel: {xn.shape[0]} tokens exceed the buffer capacity {self.cap}")
         self.dispatch(layer, xn, ids)
@@ -310,13 +327,14 @@ class ExpertParallel:
             fork.record(main)
             self._side.wait_event(fork)
             with torch.cuda.stream(self._side):
-                self.shared(xn, w13, w2, fused_swiglu)
+                self.shared(xn, w13, w2, fused_swiglu, token_major)
                 self._join = torch.cuda.Event()
                 self._join.record(self._side)
         elif self.shared_local:
-            self.shared(xn, w13, w2, fused_swiglu)  # runs while the routed rows cross NVLink
+            self.shared(xn, w13, w2, fused_swiglu, token_major)  # runs while the routed rows cross NVLink
         self.receive(layer, bn)
-        self.experts(w13, w2, bn, fused_swiglu, layer=layer)  # down projection sends to the source ranks
+        # down projection sends to the source ranks
+        self.experts(w13, w2, bn, fused_swiglu, layer=layer, token_major=token_major)
         return self.combine(layer, wts)
 
 
